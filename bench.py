@@ -1,0 +1,453 @@
+"""Decode hot-path benchmark: KV append + GQA decode attention on B200.
+
+Workload (the one the headline metric is quoted on, one GPU): batch 32,
+per-sequence context lengths uniform in [256, 4096] (seed 1), fp16 KV cache
+with values N(0,1), Q [32,12,128] / new K,V [32,2,128] per step, one layer,
+Qwen2-1.5B head shapes (12 query heads share 2 KV heads, head_dim 128),
+softmax scale 1/sqrt(128).  A step appends one token to every sequence and
+attends over its whole context.  Synthetic seeded data; the 72 MB working
+set fits in the 126 MB L2, so L2 is flushed (256 MiB write) before every
+timed step and the flush is kept out of the step's events.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 is launched by torchrun, one process per GPU; every rank owns its own
+32 sequences (placement by request, no collective on the data path: weak
+scaling); timing is the max over ranks of device-event time.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "rk3588-npu_b200")
+
+METRIC = "decode attention tokens/s and achieved HBM GB/s vs B200 peak at 1/2/4/8 GPUs"
+B, NQ, NKV, HD = 32, 12, 2, 128
+KVD = NKV * HD
+HID = NQ * HD
+FLUSH_BYTES = 256 << 20
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    return ap.parse_args()
+
+
+def load_pkg():
+    name = "rk3588_npu_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, os.path.join(PKG_DIR, "__init__.py"),
+                                                  submodule_search_locations=[PKG_DIR])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def context_lengths() -> list[int]:
+    return [int(x) for x in np.random.default_rng(1).integers(256, 4097, B)]
+
+
+def step_bytes(kv_lens) -> float:
+    """Algorithmic HBM bytes of one decode launch.  Per sequence attending T
+    tokens: the K and V rows of the T-1 cached tokens (2 KV heads x 128 dims
+    x 2 B x 2 = 1024 B per token), the appended 1024 B row, fp32 q/k/v in and
+    fp32 out (4 x (1536 + 256 + 256 + 1536) B), and 4 B per block-table entry."""
+    tot = 0.0
+    for T in kv_lens:
+        tot += 1024.0 * (T - 1) + 1024.0 + 4.0 * -(-T // 16) + 4.0 * (HID + 2 * KVD + HID)
+    return tot
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_indices):
+        self.gpus = set(gpu_indices)
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        import tempfile
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                idx = int(parts[0])
+            except ValueError:
+                continue
+            if idx not in self.gpus:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        busy = [s for s, p in zip(sm, power) if p > 0] or sm
+        return {"sm_mhz": statistics.median(busy) if busy else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(power) if power else None}
+
+
+def encode_device(x, dtype: int):
+    """fp32 -> 16-bit codes with the reference's truncating encoders
+    (half.h:17-20 bf16, half.h:24-32 fp16), on the device: input preparation."""
+    import torch
+    u = x.contiguous().view(torch.int32)
+    if dtype == 1:
+        return (u >> 16).to(torch.int16)
+    sign = (u >> 16) & 0x8000
+    e = ((u >> 23) & 0xFF) - 112
+    mant = u & 0x7FFFFF
+    h = sign | (e.clamp(0, 31) << 10) | (mant >> 13)
+    h = torch.where(e <= 0, sign, h)
+    h = torch.where(e >= 31, sign | 0x7C00, h)
+    return torch.where(h >= 32768, h - 65536, h).to(torch.int16)
+
+def peak_hbm():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def ncu_traffic():
+    """Per-launch DRAM bytes of the decode kernel from the committed ncu
+    summary (profiles/decode_kernel_b32_ncu.txt, line `traffic_bytes_per_launch:`)."""
+    path = os.path.join(ROOT, "profiles", "decode_kernel_b32_ncu.txt")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+def setup_pool(kv, torch, dev, lens, steps_total, seed):
+    nb = sum(-(-(L + steps_total + 1) // 16) for L in lens) + 64
+    P = kv.Pool(dev, 1, nb, num_q_heads=NQ, num_kv_heads=NKV, dtype=kv.KV_F16, max_seqs=B,
+                max_seq_len=max(lens) + steps_total + 32)
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    ids = []
+    for L in lens:
+        s = P.seq_alloc()
+        P.reserve(s, L)
+        k = encode_device(torch.randn((L, KVD), generator=g, device="cuda"), 0)
+        v = encode_device(torch.randn((L, KVD), generator=g, device="cuda"), 0)
+        P.import_rows(0, s, 0, k, v)
+        P.set_cur_pos(s, L)
+        ids.append(s)
+    torch.cuda.synchronize()
+    return P, ids
+
+
+def run_ours(args, rank, world, local):
+    import torch
+    kv = load_pkg()
+    kv.load()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    lens = context_lengths()
+    K, W = args.steps, args.warmup
+    P, ids = setup_pool(kv, torch, local, lens, K + W + 2, seed=1 + rank)
+    g = torch.Generator(device="cuda").manual_seed(100 + rank)
+    nsteps = W + K
+    q = torch.randn((nsteps, B, HID), generator=g, device="cuda")
+    kn = torch.randn((nsteps, B, KVD), generator=g, device="cuda")
+    vn = torch.randn((nsteps, B, KVD), generator=g, device="cuda")
+    out = torch.empty((B, HID), device="cuda")
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.int32, device="cuda")
+
+    def step(i):
+        P.plan(ids)
+        P.decode_layer(0, q[i], kn[i], vn[i], out)
+        P.commit()
+
+    def reset_lens():
+        torch.cuda.synchronize()
+        for s, L in zip(ids, lens):
+            P.set_cur_pos(s, L)
+
+    sampler = ClockSampler(range(local, local + 1)) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    for i in range(W):
+        flush.zero_()
+        step(i)
+    # Keep the GPU loaded ~1 s so the clock samples reflect load; lengths
+    # are put back afterwards so the timed steps see the stated contexts.
+    t_end = time.time() + 1.0
+    while time.time() < t_end:
+        for i in range(8):
+            flush.zero_()
+            step(i)
+        reset_lens()
+        torch.cuda.synchronize()
+    reset_lens()
+
+    # ---- value: inputs resident in HBM ----
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    kv_lens_per_step = []
+    for i in range(K):
+        kv_lens_per_step.append([L + 1 + i for L in lens])
+        flush.zero_()
+        e0, e1, e2, e3 = ev[i]
+        e0.record()
+        P.plan(ids)
+        e1.record()
+        P.decode_layer(0, q[W + i], kn[W + i], vn[W + i], out)
+        e2.record()
+        P.commit()
+        e3.record()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    step_ms = sum(e[0].elapsed_time(e[3]) for e in ev)
+    kern_ms = sum(e[1].elapsed_time(e[2]) for e in ev)
+    clocks = sampler.stop() if sampler else None
+    assert P.device_status() == 0, "device-side wait gave up"
+
+    # ---- e2e: host buffers, copies inside the timed region ----
+    reset_lens()
+    qh = q[W:].cpu().pin_memory()
+    kh = kn[W:].cpu().pin_memory()
+    vh = vn[W:].cpu().pin_memory()
+    oh = torch.empty((K, B, HID)).pin_memory()
+    qd = torch.empty((B, HID), device="cuda")
+    kd = torch.empty((B, KVD), device="cuda")
+    vd = torch.empty((B, KVD), device="cuda")
+    e2e_ms = 0.0
+    if dist:
+        dist.barrier()
+    for i in range(K):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        qd.copy_(qh[i], non_blocking=True)
+        kd.copy_(kh[i], non_blocking=True)
+        vd.copy_(vh[i], non_blocking=True)
+        P.plan(ids)
+        P.decode_layer(0, qd, kd, vd, out)
+        P.commit()
+        oh[i].copy_(out, non_blocking=True)
+        b.record()
+        b.synchronize()  # the caller waits for its result
+        e2e_ms += a.elapsed_time(b)
+    if dist:
+        dist.barrier()
+
+    times = torch.tensor([step_ms, kern_ms, e2e_ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    step_ms, kern_ms, e2e_ms = times.tolist()
+    launches = K  # one fused decode kernel per step (table patches ride in it)
+    if rank == 0:
+        alg = sum(step_bytes(kl) for kl in kv_lens_per_step) / K
+        peak, peak_kind = peak_hbm()
+        achieved = alg / (kern_ms / K * 1e-3) / 1e9
+        line = {
+            "metric": METRIC,
+            "value": round(world * B * K / (step_ms * 1e-3), 1),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": K,
+            "warmup": W,
+            "ms_per_step": round(step_ms / K, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f16",
+            "data": "synthetic (seeded N(0,1) K/V/q; context lengths U[256,4096] seed 1)",
+            "config": {"workload": "decode step: KV append + GQA decode attention, batch 32 per GPU, "
+                                   "context U[256,4096], 12 q / 2 kv heads x 128, fp16 KV, 1 layer",
+                       "batch_per_gpu": B, "layers": 1, "kv_dtype": "f16", "block_tokens": 16,
+                       "parallelism": f"request placement x{world} (no data-path collective)",
+                       "l2": "flushed before every timed step (256 MiB write), flush outside events"},
+            "hbm_gbs_step": round(alg / (step_ms / K * 1e-3) / 1e9, 1),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": ncu_traffic(), "peak_source": peak_kind,
+                         "kernel_ms": round(kern_ms / K, 5), "algorithmic_bytes": round(alg)},
+            "e2e": {"value": round(world * B * K / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 4 * B * (HID + 2 * KVD), "d2h_bytes_per_step": 4 * B * HID},
+            "gpu_launches": launches,
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(lens, args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    P.close()
+    if dist:
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------------- CPU (reference) path
+def _oracle():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    return oracle
+
+
+def cpu_workload(orc, lens, extra, seed=1):
+    rng = np.random.default_rng(seed)
+    kcs, vcs = [], []
+    for L in lens:
+        kc = np.zeros((L + extra, KVD), np.uint16)
+        vc = np.zeros((L + extra, KVD), np.uint16)
+        kc[:L] = orc.encode(rng.standard_normal((L, KVD), dtype=np.float32))
+        vc[:L] = orc.encode(rng.standard_normal((L, KVD), dtype=np.float32))
+        kcs.append(kc)
+        vcs.append(vc)
+    return kcs, vcs, rng
+
+
+def cpu_step_fn(orc, threads):
+    """One decode step of all sequences on the host: the reference's own
+    functions (oracle/_ref) when built, else the C restatement."""
+    if orc.have_ref():
+        return "reference", lambda q, k, v, kc, vc, pos: orc.ref_batch_step(q, k, v, kc, vc, pos, threads)
+    from concurrent.futures import ThreadPoolExecutor
+    ex = ThreadPoolExecutor(threads)
+
+    def port(q, k, v, kc, vc, pos):
+        def one(i):
+            o, _, _ = orc.layer_step(q[i:i + 1], k[i:i + 1], v[i:i + 1], kc[i], vc[i], int(pos[i]))
+            return o[0]
+        return np.stack(list(ex.map(one, range(len(kc)))))
+    return "port", port
+
+
+def cpu_baseline(lens, seconds):
+    """Single-thread CPU sample of the same workload (rank 0, N=1 only)."""
+    orc = _oracle()
+    kind, fn = cpu_step_fn(orc, 1)
+    max_steps = 64
+    kcs, vcs, rng = cpu_workload(orc, lens, max_steps + 1)
+    pos = list(lens)
+    t0 = time.perf_counter()
+    steps = 0
+    while steps < max_steps and (steps == 0 or time.perf_counter() - t0 < seconds):
+        q = rng.standard_normal((B, HID), dtype=np.float32)
+        k = rng.standard_normal((B, KVD), dtype=np.float32)
+        v = rng.standard_normal((B, KVD), dtype=np.float32)
+        fn(q, k, v, kcs, vcs, pos)
+        pos = [p + 1 for p in pos]
+        steps += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(B * steps / dt, 2), "unit": "tokens/s", "cores": 1, "kind": kind,
+            "sample": f"{steps} full decode steps of the 32-sequence workload on 1 host thread "
+                      f"({dt:.1f} s)"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    orc = _oracle()
+    threads = max(1, min(os.cpu_count() or 1, B))
+    kind, fn = cpu_step_fn(orc, threads)
+    lens = context_lengths()
+    K, W = args.steps, args.warmup
+    kcs, vcs, rng = cpu_workload(orc, lens, K + W + 1)
+    pos = list(lens)
+    total = 0.0
+    for i in range(W + K):
+        q = rng.standard_normal((B, HID), dtype=np.float32)
+        k = rng.standard_normal((B, KVD), dtype=np.float32)
+        v = rng.standard_normal((B, KVD), dtype=np.float32)
+        t0 = time.perf_counter()
+        fn(q, k, v, kcs, vcs, pos)
+        dt = time.perf_counter() - t0
+        if i >= W:
+            total += dt
+        pos = [p + 1 for p in pos]
+    value = round(B * K / total, 2)
+    sample = (f"{K} timed decode steps of the 32-sequence workload, {threads} host threads taking "
+              f"whole sequences, {'reference functions compiled from source' if kind == 'reference' else 'C restatement'}")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(total / K * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded N(0,1); context lengths U[256,4096] seed 1)",
+            "config": {"workload": "decode step: KV append + GQA decode attention, batch 32, "
+                                   "context U[256,4096], 12 q / 2 kv heads x 128, fp16 KV, 1 layer",
+                       "batch_per_gpu": B, "layers": 1, "kv_dtype": "f16"},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": kind,
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_ours(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,200 @@
+/*
+ * kvattn.h -- C ABI of the B200 decode hot path: a paged KV-cache block pool
+ * with on-device RoPE'd append, and grouped-query split-KV decode attention.
+ *
+ * It replaces, behind plain C entry points, the Qwen2 worker's
+ *   KVCache                 worker/include/model/kv_cache.h:19-41
+ *                           worker/src/model/kv_cache.cpp:4-16
+ *   op_rope                 worker/include/ops/op_rope.h:17-19
+ *   the KV append loop      worker/src/model/qwen2_model.cpp:188-200
+ *   op_attention            worker/include/ops/op_attention.h:19-26
+ *                           (with op_softmax, worker/src/ops/op_softmax.cpp:6-16)
+ * and the call-site contract around them (qwen2_model.cpp:140-141,203-206,268:
+ * the position is read before the layers and advanced once after the last).
+ *
+ * Conventions
+ *  - Every function returns an int status (KV_OK == 0).  kv_last_error()
+ *    gives the message of the calling thread's last failure.
+ *  - Tensors are DEVICE pointers on the pool's device; host pointers are used
+ *    only for control arguments (sequence ids, block ids, counts).
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *    Device work is stream-ordered; a decode step's plan, layer calls and any
+ *    gather of its results must be issued on one stream.
+ *  - One pool per GPU.  Host calls on one pool are serialised internally.
+ *  - Numerics (the reference's, kept bit-exact where they are integer work):
+ *    appended K is RoPE'd in fp32 with non-fused multiply/add, using cos/sin
+ *    values computed on the host with the same float libm calls as
+ *    op_rope.cpp:11-14, then stored with half.h's TRUNCATING encoders
+ *    (f32_to_f16 half.h:24-32, or f32_to_bf16 half.h:17-20); V is stored the
+ *    same way without rotation.  Attention reads fp32 q, decodes the cache to
+ *    fp32 and accumulates in fp32; outputs are fp32.
+ */
+#ifndef KVATTN_H
+#define KVATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct kvp_pool kvp_pool; /* opaque: one paged KV pool on one GPU */
+
+enum kv_status {
+    KV_OK = 0,
+    KV_ERR_INVAL = 1,   /* bad argument or unsupported shape */
+    KV_ERR_OOM = 2,     /* the pool has too few free blocks (nothing was changed) */
+    KV_ERR_BADSEQ = 3,  /* sequence id unknown or not live */
+    KV_ERR_CUDA = 4,    /* a CUDA runtime call failed */
+    KV_ERR_RANGE = 5,   /* position beyond max_seq_len or beyond reserved blocks */
+    KV_ERR_STATE = 6,   /* call order violated (e.g. layer call without a plan) */
+    KV_ERR_TIMEOUT = 7  /* a device-side bounded wait gave up (see kvp_device_status) */
+};
+
+enum kv_dtype { KV_F16 = 0, KV_BF16 = 1 };
+
+/* Pass as `device` to kvp_create for a bookkeeping-only pool: allocator,
+ * block tables and decode planning run on the host with no device memory
+ * (plans are sized for a nominal 148-SM part).  Data-movement and attention
+ * calls on it return KV_ERR_STATE.  Used to test host logic without a GPU. */
+#define KVP_HOST_ONLY (-1)
+
+/* Message for the calling thread's last non-OK status ("" if none). */
+const char* kv_last_error(void);
+/* Static name of a status code. */
+const char* kv_status_str(int status);
+/* Library version, "major.minor.patch". */
+const char* kv_version(void);
+
+/* ------------------------------------------------------------------ pool */
+
+/* Create a pool on `device`.  Replaces KVCache::init (kv_cache.h:21,
+ * kv_cache.cpp:4-10): the contiguous per-layer [capacity][kv_dim] arrays
+ * become `num_blocks` blocks of `block_tokens` token rows shared by all
+ * sequences, zero-filled like init's assign(..., 0).
+ * Supported shapes: head_dim 128, block_tokens 16, num_q_heads a multiple of
+ * num_kv_heads with num_q_heads/num_kv_heads <= 8.  max_seq_len bounds any
+ * position (it sizes the RoPE table and the per-sequence block table). */
+int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, int head_dim,
+               int block_tokens, int num_blocks, int dtype, int max_seqs, int max_seq_len,
+               float rope_theta, kvp_pool** out);
+int kvp_destroy(kvp_pool* pool);
+
+/* Free every sequence and zero the pool's K/V memory (KVCache::reset,
+ * kv_cache.cpp:12-16).  Stream-ordered. */
+int kvp_reset(kvp_pool* pool, void* stream);
+
+/* Pool facts: number of free blocks / total blocks. */
+int kvp_free_blocks(const kvp_pool* pool, int* n_free);
+int kvp_num_blocks(const kvp_pool* pool, int* n_blocks);
+
+/* Device pointers of the raw storage, for callers that manage layout
+ * themselves (tests, zero-copy consumers).  Layout of one layer:
+ * [num_blocks][num_kv_heads][4096-byte tile]; a tile holds 16 token rows of
+ * 128 dims in the swizzled order documented in the design notes. */
+int kvp_storage(const kvp_pool* pool, void** k_base, void** v_base, size_t* layer_bytes);
+
+/* ------------------------------------------------------------- sequences */
+
+/* A new empty sequence (length 0).  KVCache has exactly one implicit
+ * sequence; the pool holds up to max_seqs. */
+int kvp_seq_alloc(kvp_pool* pool, int* seq_id);
+/* Return the sequence's blocks to the free list and retire the id. */
+int kvp_seq_free(kvp_pool* pool, int seq_id);
+/* Grow the sequence's block table to hold n_tokens positions, taking blocks
+ * from the free list (all or nothing: KV_ERR_OOM leaves it unchanged). */
+int kvp_seq_reserve(kvp_pool* pool, int seq_id, int n_tokens);
+/* Append explicit block ids (each must be free) to the sequence's table,
+ * e.g. a random permutation of the pool.  All or nothing. */
+int kvp_seq_set_blocks(kvp_pool* pool, int seq_id, const int* block_ids, int n);
+/* Current length: KVCache::cur_pos / set_cur_pos (kv_cache.h:24-25).  A new
+ * length may not exceed the reserved capacity. */
+int kvp_seq_len(const kvp_pool* pool, int seq_id, int* len);
+int kvp_seq_set_len(kvp_pool* pool, int seq_id, int len);
+/* Copy the host block table of a sequence (n_out receives its length). */
+int kvp_seq_blocks(const kvp_pool* pool, int seq_id, int* block_ids, int cap, int* n_out);
+
+/* --------------------------------------------------------- data movement */
+
+/* Write n already-encoded rows [n][num_kv_heads*128] (the reference layout
+ * of k_ptr(layer)/v_ptr(layer), kv_cache.h:30-33) at positions pos0.. of a
+ * sequence.  Blocks must be reserved.  Does not change the length. */
+int kvp_import(kvp_pool* pool, int layer, int seq_id, int pos0, int n, const void* k_rows,
+               const void* v_rows, void* stream);
+/* Read positions [0, len) of a sequence back into the reference layout
+ * [len][num_kv_heads*128] (what k_ptr(layer)/v_ptr(layer) would hold). */
+int kvp_gather(kvp_pool* pool, int layer, int seq_id, void* k_rows, void* v_rows,
+               void* stream);
+
+/* Prefill append: RoPE (positions pos0..pos0+n-1) and encode n new tokens'
+ * k/v [n][num_kv_heads*128] fp32 into the sequence's blocks, as
+ * qwen2_model.cpp:180-200 does for seq=n.  Blocks must be reserved; the
+ * length is not changed (set it after the last layer, as qwen2_model.cpp:268). */
+int kv_append_chunk(kvp_pool* pool, int layer, int seq_id, int pos0, int n, const float* k,
+                    const float* v, void* stream);
+
+/* ---------------------------------------------------------------- decode */
+
+/* Plan one decode step for nseq sequences (host ids).  For each sequence:
+ * position p = its length; one block is reserved for p+1 if needed (all or
+ * nothing); the split-KV work list is built and uploaded on `stream`.
+ * The plan stays valid for every layer until the next plan or commit. */
+int attn_decode_plan(kvp_pool* pool, int nseq, const int* seq_ids, void* stream);
+
+/* The same with per-sequence control, for a sequence whose positions are
+ * split across GPUs: rope_pos[i] is the GLOBAL position of the new token
+ * (used for q and k rotation); append[i] = 1 writes the new token at local
+ * slot `length` and attends [0, length]; append[i] = 0 attends [0, length)
+ * only and writes nothing.  NULL arrays mean rope_pos = length, append = 1. */
+int attn_decode_plan_ex(kvp_pool* pool, int nseq, const int* seq_ids, const int* rope_pos,
+                        const int* append, void* stream);
+
+/* One layer of the planned step, fused in one launch: RoPE q and the new k,
+ * append the encoded k/v row, grouped-query attention over the sequence's
+ * blocks with an online softmax, split-KV partials merged on device.
+ *   q     [nseq][num_q_heads*128]  fp32 (pre-RoPE, bias added)
+ *   k_new [nseq][num_kv_heads*128] fp32 (pre-RoPE, bias added)
+ *   v_new [nseq][num_kv_heads*128] fp32
+ *   out   [nseq][num_q_heads*128]  fp32
+ * Row i belongs to seq_ids[i] of the plan.  Replaces op_rope + the append
+ * loop + op_attention for seq=1 (qwen2_model.cpp:180-206). */
+int attn_decode_append(kvp_pool* pool, int layer, const float* q, const float* k_new,
+                       const float* v_new, float* out, void* stream);
+
+/* The same, also writing each row's softmax state for a cross-GPU merge:
+ * m [nseq][num_q_heads] = max of the scaled scores, l = sum of exp(s - m);
+ * out holds the normalised partial output.  Rows with nothing to attend get
+ * m = -inf, l = 0, out = 0. */
+int attn_decode_append_partial(kvp_pool* pool, int layer, const float* q, const float* k_new,
+                               const float* v_new, float* out, float* m, float* l,
+                               void* stream);
+
+/* Advance the planned sequences by one position (set_cur_pos(total_len),
+ * qwen2_model.cpp:268) and retire the plan. */
+int attn_decode_commit(kvp_pool* pool);
+
+/* Log-sum-exp merge of G partial states per row (split-KV across GPUs):
+ *   m, l [G][rows], o [G][rows][dim] (normalised partial outputs) ->
+ *   out [rows][dim] = sum_g l_g e^(m_g-M) o_g / sum_g l_g e^(m_g-M).
+ * No reference counterpart (the reference has no split-KV). */
+int attn_combine_lse(int G, int rows, int dim, const float* m, const float* l, const float* o,
+                     float* out, void* stream);
+
+/* Device status word of the pool: 0, or KV_ERR_TIMEOUT if a kernel's
+ * bounded wait gave up.  Synchronises `stream`; clears the word. */
+int kvp_device_status(kvp_pool* pool, void* stream, int* status);
+
+/* The active plan's work list (host copy): item count, chunk size in tokens,
+ * number of new block-table entries, and up to `cap` items' (slot, kv head,
+ * chunk).  Any output pointer may be NULL. */
+int kvp_plan_info(const kvp_pool* pool, int* nitems, int* chunk_tokens, int* npatch, int* item_slot,
+                  int* item_head, int* item_chunk, int cap);
+
+/* Number of SMs and of resident decode CTAs per SM used for grid sizing. */
+int kvp_launch_info(const kvp_pool* pool, int* num_sms, int* ctas_per_sm);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KVATTN_H */

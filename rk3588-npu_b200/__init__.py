@@ -1,0 +1,278 @@
+"""Python host binding of the B200 decode hot path (ctypes over include/kvattn.h).
+
+The product is the C ABI in ``lib/libkvattn.so`` (CUDA kernels for sm_100a +
+C++ host runtime).  This module only marshals arguments: device tensors are
+torch tensors (used for device memory and streams), everything else is plain
+Python.  There is no fallback: if the library is missing, ``load()`` raises.
+
+Reference interfaces mirrored (Bobchasm/rk3588-npu):
+  KVCache        worker/include/model/kv_cache.h:19-41  -> Pool + sequences
+  op_rope + append loop + op_attention
+                 worker/src/model/qwen2_model.cpp:180-206 -> Pool.decode_step
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libkvattn.so")
+
+KV_OK, KV_ERR_INVAL, KV_ERR_OOM, KV_ERR_BADSEQ, KV_ERR_CUDA, KV_ERR_RANGE, KV_ERR_STATE, \
+    KV_ERR_TIMEOUT = range(8)
+KV_F16, KV_BF16 = 0, 1
+KVP_HOST_ONLY = -1
+HEAD_DIM = 128
+BLOCK_TOKENS = 16
+
+_vp = C.c_void_p
+_ip = C.POINTER(C.c_int)
+
+# name -> argtypes (all return int status unless listed in _RESTYPE)
+_SIGS = {
+    "kv_last_error": [],
+    "kv_status_str": [C.c_int],
+    "kv_version": [],
+    "kvp_create": [C.c_int] * 10 + [C.c_float, C.POINTER(_vp)],
+    "kvp_destroy": [_vp],
+    "kvp_reset": [_vp, _vp],
+    "kvp_free_blocks": [_vp, _ip],
+    "kvp_num_blocks": [_vp, _ip],
+    "kvp_storage": [_vp, C.POINTER(_vp), C.POINTER(_vp), C.POINTER(C.c_size_t)],
+    "kvp_seq_alloc": [_vp, _ip],
+    "kvp_seq_free": [_vp, C.c_int],
+    "kvp_seq_reserve": [_vp, C.c_int, C.c_int],
+    "kvp_seq_set_blocks": [_vp, C.c_int, _ip, C.c_int],
+    "kvp_seq_len": [_vp, C.c_int, _ip],
+    "kvp_seq_set_len": [_vp, C.c_int, C.c_int],
+    "kvp_seq_blocks": [_vp, C.c_int, _ip, C.c_int, _ip],
+    "kvp_import": [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp],
+    "kvp_gather": [_vp, C.c_int, C.c_int, _vp, _vp, _vp],
+    "kv_append_chunk": [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp],
+    "attn_decode_plan": [_vp, C.c_int, _ip, _vp],
+    "attn_decode_plan_ex": [_vp, C.c_int, _ip, _ip, _ip, _vp],
+    "attn_decode_append": [_vp, C.c_int, _vp, _vp, _vp, _vp, _vp],
+    "attn_decode_append_partial": [_vp, C.c_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
+    "attn_decode_commit": [_vp],
+    "attn_combine_lse": [C.c_int, C.c_int, C.c_int, _vp, _vp, _vp, _vp, _vp],
+    "kvp_device_status": [_vp, _vp, _ip],
+    "kvp_plan_info": [_vp, _ip, _ip, _ip, _ip, _ip, _ip, C.c_int],
+    "kvp_launch_info": [_vp, _ip, _ip],
+}
+_RESTYPE = {"kv_last_error": C.c_char_p, "kv_status_str": C.c_char_p, "kv_version": C.c_char_p}
+
+_lib = None
+
+
+class KVError(RuntimeError):
+    def __init__(self, status: int, fn: str, msg: str):
+        self.status = status
+        super().__init__(f"{fn}: {_lib.kv_status_str(status).decode()} ({msg})")
+
+
+def load() -> C.CDLL:
+    """Load libkvattn.so (build it with rk3588-npu_b200/build.py).  Raises
+    FileNotFoundError when it is absent: there is no other implementation."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(
+                f"{LIB_PATH} is missing; build it with `python rk3588-npu_b200/build.py`")
+        L = C.CDLL(LIB_PATH)
+        for name, args in _SIGS.items():
+            f = getattr(L, name)
+            f.argtypes = args
+            f.restype = _RESTYPE.get(name, C.c_int)
+        _lib = L
+    return _lib
+
+
+def _check(rc: int, fn: str) -> None:
+    if rc != KV_OK:
+        raise KVError(rc, fn, _lib.kv_last_error().decode())
+
+
+def call(fn: str, *args) -> None:
+    """Call a status-returning C entry point, raising KVError on failure."""
+    _check(getattr(load(), fn)(*args), fn)
+
+
+def _ptr(t) -> int | None:
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    if not t.is_contiguous():
+        raise ValueError("tensor must be contiguous")
+    return t.data_ptr()
+
+
+def _stream(stream):
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+def _ints(xs):
+    xs = list(int(x) for x in xs)
+    return (C.c_int * max(1, len(xs)))(*xs)
+
+
+class Pool:
+    """A paged KV pool on one GPU (or a host-only bookkeeping pool).
+
+    Method names follow KVCache where one exists (kv_cache.h:19-41):
+    ``reset``, ``cur_pos``/``set_cur_pos`` (per sequence), ``capacity``."""
+
+    def __init__(self, device: int, num_layers: int, num_blocks: int, *, num_q_heads: int = 12,
+                 num_kv_heads: int = 2, dtype: int = KV_F16, max_seqs: int = 256,
+                 max_seq_len: int = 32768, rope_theta: float = 1e6):
+        L = load()
+        h = _vp()
+        _check(L.kvp_create(device, num_layers, num_q_heads, num_kv_heads, HEAD_DIM, BLOCK_TOKENS,
+                            num_blocks, dtype, max_seqs, max_seq_len, rope_theta, C.byref(h)),
+               "kvp_create")
+        self.h = h
+        self.device = device
+        self.num_layers = num_layers
+        self.num_blocks = num_blocks
+        self.q_heads = num_q_heads
+        self.kv_heads = num_kv_heads
+        self.kv_dim = num_kv_heads * HEAD_DIM
+        self.hidden = num_q_heads * HEAD_DIM
+        self.dtype = dtype
+        self.max_seqs = max_seqs
+        self.max_seq_len = max_seq_len
+        self._plan_n = 0
+
+    def close(self) -> None:
+        if self.h:
+            _check(_lib.kvp_destroy(self.h), "kvp_destroy")
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- pool ----
+    def reset(self, stream=None) -> None:
+        call("kvp_reset", self.h, None if self.device < 0 else _stream(stream))
+
+    def free_blocks(self) -> int:
+        n = C.c_int()
+        call("kvp_free_blocks", self.h, C.byref(n))
+        return n.value
+
+    def storage(self):
+        k, v, lb = _vp(), _vp(), C.c_size_t()
+        call("kvp_storage", self.h, C.byref(k), C.byref(v), C.byref(lb))
+        return k.value, v.value, lb.value
+
+    def launch_info(self):
+        a, b = C.c_int(), C.c_int()
+        call("kvp_launch_info", self.h, C.byref(a), C.byref(b))
+        return a.value, b.value
+
+    # ---- sequences ----
+    def seq_alloc(self) -> int:
+        s = C.c_int()
+        call("kvp_seq_alloc", self.h, C.byref(s))
+        return s.value
+
+    def seq_free(self, seq: int) -> None:
+        call("kvp_seq_free", self.h, seq)
+
+    def reserve(self, seq: int, n_tokens: int) -> None:
+        call("kvp_seq_reserve", self.h, seq, n_tokens)
+
+    def set_blocks(self, seq: int, block_ids) -> None:
+        ids = list(block_ids)
+        call("kvp_seq_set_blocks", self.h, seq, _ints(ids), len(ids))
+
+    def cur_pos(self, seq: int) -> int:
+        n = C.c_int()
+        call("kvp_seq_len", self.h, seq, C.byref(n))
+        return n.value
+
+    def set_cur_pos(self, seq: int, pos: int) -> None:
+        call("kvp_seq_set_len", self.h, seq, pos)
+
+    def blocks(self, seq: int) -> list[int]:
+        n = C.c_int()
+        call("kvp_seq_blocks", self.h, seq, None, 0, C.byref(n))
+        buf = (C.c_int * max(1, n.value))()
+        call("kvp_seq_blocks", self.h, seq, buf, n.value, C.byref(n))
+        return list(buf[:n.value])
+
+    def capacity(self, seq: int) -> int:
+        return len(self.blocks(seq)) * BLOCK_TOKENS
+
+    # ---- data movement (device tensors) ----
+    def import_rows(self, layer, seq, pos0, k_rows, v_rows, stream=None) -> None:
+        n = k_rows.shape[0]
+        assert k_rows.shape == (n, self.kv_dim) and v_rows.shape == (n, self.kv_dim)
+        call("kvp_import", self.h, layer, seq, pos0, n, _ptr(k_rows), _ptr(v_rows), _stream(stream))
+
+    def gather(self, layer, seq, stream=None):
+        import torch
+        n = self.cur_pos(seq)
+        dev = torch.device("cuda", self.device)
+        k = torch.empty((n, self.kv_dim), dtype=torch.int16, device=dev)
+        v = torch.empty((n, self.kv_dim), dtype=torch.int16, device=dev)
+        call("kvp_gather", self.h, layer, seq, _ptr(k), _ptr(v), _stream(stream))
+        return k, v
+
+    def append_chunk(self, layer, seq, pos0, k, v, stream=None) -> None:
+        n = k.shape[0]
+        assert k.shape == (n, self.kv_dim) and v.shape == (n, self.kv_dim)
+        call("kv_append_chunk", self.h, layer, seq, pos0, n, _ptr(k), _ptr(v), _stream(stream))
+
+    # ---- decode ----
+    def plan(self, seq_ids, rope_pos=None, append=None, stream=None) -> None:
+        ids = list(seq_ids)
+        st = None if self.device < 0 else _stream(stream)
+        if rope_pos is None and append is None:
+            call("attn_decode_plan", self.h, len(ids), _ints(ids), st)
+        else:
+            rp = _ints(rope_pos) if rope_pos is not None else None
+            ap = _ints(append) if append is not None else None
+            call("attn_decode_plan_ex", self.h, len(ids), _ints(ids), rp, ap, st)
+        self._plan_n = len(ids)
+
+    def plan_info(self):
+        n, ch, npatch = C.c_int(), C.c_int(), C.c_int()
+        call("kvp_plan_info", self.h, C.byref(n), C.byref(ch), C.byref(npatch), None, None, None, 0)
+        cap = n.value
+        a, b, c = (C.c_int * max(1, cap))(), (C.c_int * max(1, cap))(), (C.c_int * max(1, cap))()
+        call("kvp_plan_info", self.h, C.byref(n), C.byref(ch), C.byref(npatch), a, b, c, cap)
+        return {"nitems": n.value, "chunk_tokens": ch.value, "npatch": npatch.value,
+                "items": list(zip(a[:cap], b[:cap], c[:cap]))}
+
+    def decode_layer(self, layer, q, k_new, v_new, out, m=None, l=None, stream=None) -> None:
+        n = self._plan_n
+        assert q.shape[0] >= n and out.shape[0] >= n
+        if m is None:
+            call("attn_decode_append", self.h, layer, _ptr(q), _ptr(k_new), _ptr(v_new), _ptr(out),
+                 _stream(stream))
+        else:
+            call("attn_decode_append_partial", self.h, layer, _ptr(q), _ptr(k_new), _ptr(v_new),
+                 _ptr(out), _ptr(m), _ptr(l), _stream(stream))
+
+    def commit(self) -> None:
+        call("attn_decode_commit", self.h)
+
+    def device_status(self, stream=None) -> int:
+        s = C.c_int()
+        call("kvp_device_status", self.h, _stream(stream), C.byref(s))
+        return s.value
+
+
+def combine_lse(m, l, o, out, stream=None) -> None:
+    """out[rows, dim] = LSE merge of G partial states m, l [G, rows], o [G, rows, dim]."""
+    G, rows, dim = o.shape
+    call("attn_combine_lse", G, rows, dim, _ptr(m), _ptr(l), _ptr(o), _ptr(out), _stream(stream))

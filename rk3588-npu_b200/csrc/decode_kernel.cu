@@ -1,0 +1,468 @@
+// decode_kernel.cu -- fused RoPE + KV append + grouped-query split-KV decode
+// attention over the paged pool, one launch per layer.
+//
+// Replaces, for seq = 1, steps 3-5 of Qwen2Model::forward
+// (worker/src/model/qwen2_model.cpp:180-206): op_rope (op_rope.cpp:8-30),
+// the append loop (qwen2_model.cpp:188-200) and op_attention with op_softmax
+// (op_attention.cpp:9-56, op_softmax.cpp:6-16).
+//
+// Work unit: (batch slot, KV head, chunk of `chunk_tokens` positions).  A
+// persistent grid walks the item list with a static stride.  Per CTA:
+//   warp 4     producer: one lane issues 1-D bulk async copies (TMA engine,
+//              no multicast) of each 16-token block's K and V tiles (4 KiB
+//              each, contiguous in HBM) into a 6-stage shared-memory ring;
+//   warps 0-3  consumers: stage k goes to warp k % 4.  Per block: S^T =
+//              K * Q^T with mma.sync m16n8k16 (16 tokens x 8 query heads,
+//              fp32 q split into hi + lo 16-bit halves so the products keep
+//              ~22 bits), online softmax in fp32 (base 2), P^T transposed in
+//              registers with movmatrix, O^T += V^T * P^T (P split hi + lo).
+// At the end of an item the four warps' states are merged in shared memory.
+// A sequence split into several chunks writes per-chunk partial (m, l, o);
+// the CTA that finishes last for a (slot, head) -- found with a per-(slot,
+// head) arrival counter, no waiting -- merges them and writes the output.
+//
+// The new token: the consumer that owns the block holding position kv_len-1
+// rotates k (non-fused fp32, cos/sin from the host-built table), encodes k
+// and v with the truncating encoders, stores the row to HBM (the append) and
+// into the staged tile, so attention sees exactly what the cache holds.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "device_common.cuh"
+#include "kvattn_internal.h"
+
+namespace kvattn {
+
+namespace {
+
+constexpr int kStages = 6;
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kStageBytes = 2 * kTileBytes;  // K tile then V tile
+constexpr int kMergeStride = 132;            // floats per (warp, head) row, padded
+constexpr long long kWaitLimit = 4000000000LL;  // SM clocks (~2 s) before a wait gives up
+
+struct Smem {
+    alignas(1024) uint8_t stage[kStages][kStageBytes];
+    float merge_o[kConsumerWarps][kMaxGroup][kMergeStride];
+    float merge_m[kConsumerWarps][kMaxGroup];
+    float merge_l[kConsumerWarps][kMaxGroup];
+    uint64_t full[kStages];
+    uint64_t empty[kStages];
+    int last_flag;
+    int failed;
+};
+
+__device__ __forceinline__ void flag_timeout(const PoolView& pv, Smem& sm) {
+    atomicExch(pv.status, 7 /* KV_ERR_TIMEOUT */);
+    sm.failed = 1;
+}
+
+// Rotated, pre-scaled q of query head (head*group + g) as mma B fragments.
+// Thread (g = lane/4, c = lane%4) holds, for k-step kk, dims kk*16 + 2c + {0,1}
+// (reg 0) and kk*16 + 8 + 2c + {0,1} (reg 1).  Dims i < 64 pair with i + 64
+// in NeoX RoPE, and kk + 4 covers exactly the partners of kk, so each thread
+// rotates its own 16 pairs.
+template <int DT>
+__device__ __forceinline__ void load_q_frags(const PoolView& pv, const float* q, int row,
+                                             int head, int rope_pos, float qscale, int lane,
+                                             uint32_t (&qh)[8][2], uint32_t (&ql)[8][2]) {
+    const int g = lane >> 2, c = lane & 3;
+    if (g >= pv.group) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) qh[kk][0] = qh[kk][1] = ql[kk][0] = ql[kk][1] = 0u;
+        return;
+    }
+    const float* qr = q + (size_t)row * (pv.q_heads * kHeadDim) + (size_t)(head * pv.group + g) * kHeadDim;
+    const float* cs = reinterpret_cast<const float*>(pv.rope + (size_t)rope_pos * (kHeadDim / 2));
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int i = kk * 16 + r * 8 + 2 * c;  // even, < 64
+            float2 a = *reinterpret_cast<const float2*>(qr + i);
+            float2 b = *reinterpret_cast<const float2*>(qr + i + 64);
+            float4 t = *reinterpret_cast<const float4*>(cs + 2 * i);  // c_i, s_i, c_i+1, s_i+1
+            float lo0, hi0, lo1, hi1;
+            rope_pair(a.x, b.x, t.x, t.y, lo0, hi0);
+            rope_pair(a.y, b.y, t.z, t.w, lo1, hi1);
+            split_pair<DT>(lo0 * qscale, lo1 * qscale, qh[kk][r], ql[kk][r]);
+            split_pair<DT>(hi0 * qscale, hi1 * qscale, qh[kk + 4][r], ql[kk + 4][r]);
+        }
+    }
+}
+
+// Write the new token's encoded K and V rows for `head` into the staged tiles
+// (row `t`) and into the pool block `blk` of `layer` (the append).
+template <int DT>
+__device__ __forceinline__ void write_new_row(const PoolView& pv, int layer, int blk, int head,
+                                              int t, const float* k_new, const float* v_new,
+                                              int row, int rope_pos, uint8_t* sK, uint8_t* sV,
+                                              int lane) {
+    const size_t kvw = (size_t)pv.kv_heads * kHeadDim;
+    const float* kr = k_new + (size_t)row * kvw + (size_t)head * kHeadDim;
+    const float* vr = v_new + (size_t)row * kvw + (size_t)head * kHeadDim;
+    const float* cs = reinterpret_cast<const float*>(pv.rope + (size_t)rope_pos * (kHeadDim / 2));
+    const int i = 2 * lane;  // dims i, i+1 and their partners i+64, i+65
+    float2 a = *reinterpret_cast<const float2*>(kr + i);
+    float2 b = *reinterpret_cast<const float2*>(kr + i + 64);
+    float4 cc = *reinterpret_cast<const float4*>(cs + 2 * i);
+    float lo0, hi0, lo1, hi1;
+    rope_pair(a.x, b.x, cc.x, cc.y, lo0, hi0);
+    rope_pair(a.y, b.y, cc.z, cc.w, lo1, hi1);
+    const uint32_t klo = (uint32_t)enc_trunc<DT>(lo0) | ((uint32_t)enc_trunc<DT>(lo1) << 16);
+    const uint32_t khi = (uint32_t)enc_trunc<DT>(hi0) | ((uint32_t)enc_trunc<DT>(hi1) << 16);
+    float2 va = *reinterpret_cast<const float2*>(vr + i);
+    float2 vb = *reinterpret_cast<const float2*>(vr + i + 64);
+    const uint32_t vlo = (uint32_t)enc_trunc<DT>(va.x) | ((uint32_t)enc_trunc<DT>(va.y) << 16);
+    const uint32_t vhi = (uint32_t)enc_trunc<DT>(vb.x) | ((uint32_t)enc_trunc<DT>(vb.y) << 16);
+    const uint32_t o_lo = tile_offset(t, i), o_hi = tile_offset(t, i + 64);
+    const size_t tile = (size_t)layer * pv.layer_bytes + ((size_t)blk * pv.kv_heads + head) * kTileBytes;
+    *reinterpret_cast<uint32_t*>(pv.k + tile + o_lo) = klo;
+    *reinterpret_cast<uint32_t*>(pv.k + tile + o_hi) = khi;
+    *reinterpret_cast<uint32_t*>(pv.v + tile + o_lo) = vlo;
+    *reinterpret_cast<uint32_t*>(pv.v + tile + o_hi) = vhi;
+    *reinterpret_cast<uint32_t*>(sK + o_lo) = klo;
+    *reinterpret_cast<uint32_t*>(sK + o_hi) = khi;
+    *reinterpret_cast<uint32_t*>(sV + o_lo) = vlo;
+    *reinterpret_cast<uint32_t*>(sV + o_hi) = vhi;
+}
+
+// One 16-token block: scores, online softmax update, P*V accumulate.
+// `valid` tokens (rows 0..valid-1) take part; the rest are masked.
+template <int DT>
+__device__ __forceinline__ void consume_block(uint32_t sK, uint32_t sV, int valid, int lane,
+                                              const uint32_t (&qh)[8][2],
+                                              const uint32_t (&ql)[8][2], float (&m2)[2],
+                                              float (&lsum)[2], float (&o)[8][4]) {
+    const int g = lane >> 2;
+    const int mi = lane >> 3, r = lane & 7;
+    // ---- S^T[16 tokens][8 heads] = K[16][128] * Qs^T ----
+    float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+    {
+        const int t = (mi & 1) * 8 + r;
+        const uint32_t rowb = sK + (uint32_t)t * 128u;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+            const int cidx = 2 * kk + (mi >> 1);
+            const uint32_t addr = rowb + (uint32_t)(cidx >> 3) * 2048u + (uint32_t)(((cidx & 7) ^ r) << 4);
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4(addr, a0, a1, a2, a3);
+            mma16816<DT>(sa, a0, a1, a2, a3, qh[kk][0], qh[kk][1]);
+            mma16816<DT>(sb, a0, a1, a2, a3, ql[kk][0], ql[kk][1]);
+        }
+    }
+    float s[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) s[e] = sa[e] + sb[e];
+    if (g >= valid) s[0] = s[1] = -INFINITY;
+    if (g + 8 >= valid) s[2] = s[3] = -INFINITY;
+    // ---- online softmax, per head column (2c, 2c+1) ----
+    float bm0 = fmaxf(s[0], s[2]), bm1 = fmaxf(s[1], s[3]);
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+        bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, off));
+        bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, off));
+    }
+    const float mn0 = fmaxf(m2[0], bm0), mn1 = fmaxf(m2[1], bm1);
+    const float mu0 = (mn0 == -INFINITY) ? 0.f : mn0;
+    const float mu1 = (mn1 == -INFINITY) ? 0.f : mn1;
+    const float al0 = fast_exp2(m2[0] - mu0), al1 = fast_exp2(m2[1] - mu1);
+    m2[0] = mn0;
+    m2[1] = mn1;
+    const float p0 = fast_exp2(s[0] - mu0), p1 = fast_exp2(s[1] - mu1);
+    const float p2 = fast_exp2(s[2] - mu0), p3 = fast_exp2(s[3] - mu1);
+    lsum[0] = lsum[0] * al0 + p0 + p2;
+    lsum[1] = lsum[1] * al1 + p1 + p3;
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+        o[mt][0] *= al0;
+        o[mt][1] *= al1;
+        o[mt][2] *= al0;
+        o[mt][3] *= al1;
+    }
+    // ---- P^T as B fragments (k = tokens, n = heads) ----
+    uint32_t h01, l01, h23, l23;
+    split_pair<DT>(p0, p1, h01, l01);
+    split_pair<DT>(p2, p3, h23, l23);
+    const uint32_t bh0 = movmatrix_t(h01), bh1 = movmatrix_t(h23);
+    const uint32_t bl0 = movmatrix_t(l01), bl1 = movmatrix_t(l23);
+    // ---- O^T[128 dims][8 heads] += V^T * P^T ----
+    {
+        const int t = (mi >> 1) * 8 + r;
+        const uint32_t rowb = sV + (uint32_t)t * 128u;
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+            const int cidx = 2 * mt + (mi & 1);
+            const uint32_t addr = rowb + (uint32_t)(cidx >> 3) * 2048u + (uint32_t)(((cidx & 7) ^ r) << 4);
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4_t(addr, a0, a1, a2, a3);
+            mma16816<DT>(o[mt], a0, a1, a2, a3, bh0, bh1);
+            mma16816<DT>(o[mt], a0, a1, a2, a3, bl0, bl1);
+        }
+    }
+}
+
+}  // namespace
+
+template <int DT>
+__global__ void __launch_bounds__(kThreads, 3)
+    decode_kernel(PoolView pv, PlanView plan, int layer, const float* __restrict__ q,
+                  const float* __restrict__ k_new, const float* __restrict__ v_new,
+                  float* __restrict__ out, float* __restrict__ m_out, float* __restrict__ l_out) {
+    extern __shared__ uint8_t smem_raw[];
+    Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const PlanHeader hdr = *plan.hdr;
+    const int CH = hdr.chunk_tokens;
+
+    // Block-table entries allocated by this step's plan.  No launch reads an
+    // entry it patches: the block of the new token is taken from the slot.
+    for (int i = blockIdx.x * kThreads + tid; i < hdr.npatch; i += gridDim.x * kThreads) {
+        const TablePatch p = plan.patches[i];
+        pv.table[(size_t)p.seq * pv.max_blocks_per_seq + p.idx] = p.block;
+    }
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&sm.full[s], 1);
+            mbar_init(&sm.empty[s], 1);
+        }
+        sm.failed = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        // ------------------------------------------------------ producer
+        // The whole warp fetches up to 32 block-table entries at once (one
+        // per lane); lane 0 waits on the ring and issues the copies.
+        const uint64_t policy = policy_evict_first();
+        uint32_t seqno = 0;
+        int ok = 1;
+        for (int it = blockIdx.x; it < hdr.nitems && ok; it += gridDim.x) {
+            const WorkItem wi = plan.items[it];
+            const DecodeSlot sl = plan.slots[wi.slot];
+            const int t0 = wi.chunk * CH;
+            const int t1 = min(sl.kv_len, t0 + CH);
+            const int nb = t1 > t0 ? (t1 - t0 + kBlockTokens - 1) / kBlockTokens : 0;
+            const int last_blk = (sl.kv_len - 1) / kBlockTokens;
+            const int* trow = pv.table + (size_t)sl.seq * pv.max_blocks_per_seq;
+            for (int b0 = 0; b0 < nb && ok; b0 += 32) {
+                const int jl = t0 / kBlockTokens + b0 + lane;
+                const int myblk = (b0 + lane < nb) ? trow[jl] : 0;
+                const int cnt = min(32, nb - b0);
+                for (int bb = 0; bb < cnt; ++bb) {
+                    const int tblk = __shfl_sync(0xffffffffu, myblk, bb);
+                    if (lane == 0) {
+                        const uint32_t k = seqno + b0 + bb;
+                        const int s = k % kStages;
+                        if (!mbar_wait_bounded(&sm.empty[s], ((k / kStages) & 1) ^ 1, kWaitLimit)) {
+                            flag_timeout(pv, sm);
+                            ok = 0;
+                        } else {
+                            const int j = t0 / kBlockTokens + b0 + bb;
+                            const int valid = min(kBlockTokens, sl.kv_len - j * kBlockTokens);
+                            const bool newblk = sl.append && j == last_blk;
+                            const int blk = newblk ? sl.new_block : tblk;
+                            if (newblk && valid == 1) {
+                                mbar_arrive(&sm.full[s]);  // only the new token: nothing to load
+                            } else if ((unsigned)blk >= (unsigned)pv.num_blocks) {
+                                atomicExch(pv.status, 5 /* KV_ERR_RANGE */);  // never read outside the pool
+                                mbar_arrive(&sm.full[s]);
+                            } else {
+                                const size_t off = (size_t)layer * pv.layer_bytes +
+                                                   ((size_t)blk * pv.kv_heads + wi.head) * kTileBytes;
+                                mbar_arrive_expect_tx(&sm.full[s], kStageBytes);
+                                bulk_g2s_hint(sm.stage[s], pv.k + off, kTileBytes, &sm.full[s], policy);
+                                bulk_g2s_hint(sm.stage[s] + kTileBytes, pv.v + off, kTileBytes,
+                                              &sm.full[s], policy);
+                            }
+                        }
+                    }
+                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                    if (!ok) break;
+                }
+            }
+            seqno += nb;
+        }
+        // Drain: copies into this CTA's shared memory must land before exit.
+        if (lane == 0 && ok) {
+            const uint32_t first = seqno > (uint32_t)kStages ? seqno - kStages : 0u;
+            for (uint32_t k = first; k < seqno; ++k)
+                if (!mbar_wait_bounded(&sm.full[k % kStages], (k / kStages) & 1, kWaitLimit)) {
+                    atomicExch(pv.status, 7);
+                    break;
+                }
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------- consumers
+    const float qscale = 0.08838834764831845f * 1.4426950408889634f;  // 1/sqrt(128) * log2(e)
+    const int g = lane >> 2, c = lane & 3;
+    uint32_t seqno = 0;
+    bool dead = false;
+    for (int it = blockIdx.x; it < hdr.nitems; it += gridDim.x) {
+        const WorkItem wi = plan.items[it];
+        const DecodeSlot sl = plan.slots[wi.slot];
+        const int t0 = wi.chunk * CH;
+        const int t1 = min(sl.kv_len, t0 + CH);
+        const int nb = t1 > t0 ? (t1 - t0 + kBlockTokens - 1) / kBlockTokens : 0;
+        const int last_blk = (sl.kv_len - 1) / kBlockTokens;
+
+        uint32_t qh[8][2], ql[8][2];
+        load_q_frags<DT>(pv, q, wi.slot, wi.head, sl.rope_pos, qscale, lane, qh, ql);
+        float m2[2] = {-INFINITY, -INFINITY}, lsum[2] = {0.f, 0.f};
+        float o[8][4];
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+
+        for (int b = 0; b < nb; ++b) {
+            const uint32_t k = seqno + b;
+            if ((int)(k % kConsumerWarps) != warp) continue;
+            const int s = k % kStages;
+            if (!dead && !mbar_wait_bounded(&sm.full[s], (k / kStages) & 1, kWaitLimit)) {
+                flag_timeout(pv, sm);
+                dead = true;
+            }
+            if (dead) continue;
+            uint8_t* sK = sm.stage[s];
+            uint8_t* sV = sm.stage[s] + kTileBytes;
+            const int j = t0 / kBlockTokens + b;
+            const int valid = min(kBlockTokens, sl.kv_len - j * kBlockTokens);
+            if (sl.append && j == last_blk)
+                write_new_row<DT>(pv, layer, sl.new_block, wi.head, valid - 1, k_new, v_new,
+                                  wi.slot, sl.rope_pos, sK, sV, lane);
+            if (valid < kBlockTokens) {
+                // Rows past the end may hold anything (stale tiles, inf):
+                // zero them in V so masked weights (exactly 0) stay 0.
+                for (int x = lane; x < (kBlockTokens - valid) * 16; x += 32) {
+                    const int t = valid + (x >> 4), ch = x & 15;
+                    *reinterpret_cast<uint4*>(sV + ((ch >> 3) * 16 + t) * 128 + (ch & 7) * 16) =
+                        make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+            __syncwarp();
+            consume_block<DT>(smem_u32(sK), smem_u32(sV), valid, lane, qh, ql, m2, lsum, o);
+            // Generic-proxy writes to the tile must be ordered before the
+            // next bulk copy (async proxy) overwrites it.
+            if (valid < kBlockTokens || (sl.append && j == last_blk))
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.empty[s]);
+        }
+        seqno += nb;
+
+        // ---- merge the four warps' states for this item ----
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+            lsum[0] += __shfl_xor_sync(0xffffffffu, lsum[0], off);
+            lsum[1] += __shfl_xor_sync(0xffffffffu, lsum[1], off);
+        }
+        named_bar_sync(1, kConsumerWarps * 32);  // previous item's readers are done
+        if (g == 0) {
+            sm.merge_m[warp][2 * c] = m2[0];
+            sm.merge_m[warp][2 * c + 1] = m2[1];
+            sm.merge_l[warp][2 * c] = lsum[0];
+            sm.merge_l[warp][2 * c + 1] = lsum[1];
+        }
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+            sm.merge_o[warp][2 * c][mt * 16 + g] = o[mt][0];
+            sm.merge_o[warp][2 * c + 1][mt * 16 + g] = o[mt][1];
+            sm.merge_o[warp][2 * c][mt * 16 + g + 8] = o[mt][2];
+            sm.merge_o[warp][2 * c + 1][mt * 16 + g + 8] = o[mt][3];
+        }
+        named_bar_sync(1, kConsumerWarps * 32);
+
+        const int d = tid;  // 0..127: one output dim per thread
+        const int qrow = wi.slot * pv.q_heads + wi.head * pv.group;
+        float* part = pv.partials + (size_t)(sl.item_base + wi.head * sl.nchunks + wi.chunk) * kPartialFloats;
+        for (int h = 0; h < pv.group; ++h) {
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm.merge_m[w][h]);
+            const float Mu = (M == -INFINITY) ? 0.f : M;
+            float L = 0.f, O = 0.f;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) {
+                const float e = fast_exp2(sm.merge_m[w][h] - Mu);
+                L += sm.merge_l[w][h] * e;
+                O += sm.merge_o[w][h][d] * e;
+            }
+            const float on = L > 0.f ? O / L : 0.f;
+            if (sl.nchunks == 1) {
+                out[(size_t)(qrow + h) * kHeadDim + d] = on;
+                if (m_out != nullptr && d == 0) {
+                    m_out[qrow + h] = M * 0.6931471805599453f;
+                    l_out[qrow + h] = L;
+                }
+            } else {
+                part[2 * kMaxGroup + h * kHeadDim + d] = on;
+                if (d == 0) {
+                    part[h] = M;
+                    part[kMaxGroup + h] = L;
+                }
+            }
+        }
+        if (sl.nchunks == 1) continue;
+
+        // ---- split sequence: the last CTA to finish a (slot, head) merges ----
+        __threadfence();
+        named_bar_sync(1, kConsumerWarps * 32);
+        if (tid == 0) {
+            const int prev = atomicAdd(&pv.counters[wi.slot * pv.kv_heads + wi.head], 1);
+            sm.last_flag = (prev == sl.nchunks - 1);
+        }
+        named_bar_sync(1, kConsumerWarps * 32);
+        if (!sm.last_flag) continue;
+        __threadfence();
+        const float* p0 = pv.partials + (size_t)(sl.item_base + wi.head * sl.nchunks) * kPartialFloats;
+        for (int h = 0; h < pv.group; ++h) {
+            float M = -INFINITY;
+            for (int ci = 0; ci < sl.nchunks; ++ci)
+                M = fmaxf(M, __ldcg(p0 + (size_t)ci * kPartialFloats + h));
+            const float Mu = (M == -INFINITY) ? 0.f : M;
+            float L = 0.f, O = 0.f;
+            for (int ci = 0; ci < sl.nchunks; ++ci) {
+                const float* pc = p0 + (size_t)ci * kPartialFloats;
+                const float w = __ldcg(pc + kMaxGroup + h) * fast_exp2(__ldcg(pc + h) - Mu);
+                L += w;
+                O += w * __ldcg(pc + 2 * kMaxGroup + h * kHeadDim + d);
+            }
+            out[(size_t)(qrow + h) * kHeadDim + d] = L > 0.f ? O / L : 0.f;
+            if (m_out != nullptr && d == 0) {
+                m_out[qrow + h] = M * 0.6931471805599453f;
+                l_out[qrow + h] = L;
+            }
+        }
+        if (tid == 0) pv.counters[wi.slot * pv.kv_heads + wi.head] = 0;
+    }
+}
+
+cudaError_t decode_occupancy(int* ctas_per_sm) {
+    const int smem = (int)sizeof(Smem) + 1024;
+    cudaError_t e = cudaFuncSetAttribute(decode_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, decode_kernel<0>, kThreads, smem);
+}
+
+cudaError_t launch_decode(const PoolView& pv, const PlanView& plan, int nitems, int npatch,
+                          int layer, const float* q, const float* k_new, const float* v_new,
+                          float* out, float* m_out, float* l_out, int grid, cudaStream_t st) {
+    (void)nitems;
+    (void)npatch;
+    const int smem = (int)sizeof(Smem) + 1024;
+    if (grid < 1) grid = 1;
+    if (pv.dtype == 0)
+        decode_kernel<0><<<grid, kThreads, smem, st>>>(pv, plan, layer, q, k_new, v_new, out, m_out, l_out);
+    else
+        decode_kernel<1><<<grid, kThreads, smem, st>>>(pv, plan, layer, q, k_new, v_new, out, m_out, l_out);
+    return cudaGetLastError();
+}
+
+}  // namespace kvattn

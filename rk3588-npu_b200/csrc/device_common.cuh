@@ -1,0 +1,191 @@
+// device_common.cuh -- encoders and sm_100a PTX wrappers used by the kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "kvattn_internal.h"
+
+namespace kvattn {
+
+// ---------------------------------------------------------------- encoders
+// f32 -> fp16 exactly as worker/include/core/half.h:24-32: mantissa truncated,
+// exp <= 0 -> signed zero, exp >= 31 (incl. NaN) -> signed inf.
+__device__ __forceinline__ uint16_t enc_f16_trunc(float f) {
+    uint32_t x = __float_as_uint(f);
+    uint32_t sign = (x >> 16) & 0x8000u;
+    int e = (int)((x >> 23) & 0xFFu) - 112;
+    uint32_t mant = x & 0x7FFFFFu;
+    if (e <= 0) return (uint16_t)sign;
+    if (e >= 31) return (uint16_t)(sign | 0x7C00u);
+    return (uint16_t)(sign | ((uint32_t)e << 10) | (mant >> 13));
+}
+
+// f32 -> bf16 exactly as half.h:17-20 (upper 16 bits, truncation).
+__device__ __forceinline__ uint16_t enc_bf16_trunc(float f) {
+    return (uint16_t)(__float_as_uint(f) >> 16);
+}
+
+template <int DT>
+__device__ __forceinline__ uint16_t enc_trunc(float f) {
+    return DT == 0 ? enc_f16_trunc(f) : enc_bf16_trunc(f);
+}
+
+// Decoders for the gather-free paths (prefill checks etc.).
+__device__ __forceinline__ float dec_bf16(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+
+// RoPE of one pair with separate rounding of every product (no FMA), the
+// arithmetic of op_rope.cpp:17-18 compiled without contraction.
+__device__ __forceinline__ void rope_pair(float v0, float v1, float c, float s, float& r0,
+                                          float& r1) {
+    r0 = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, s));
+    r1 = __fadd_rn(__fmul_rn(v0, s), __fmul_rn(v1, c));
+}
+
+// Split an fp32 pair into hi + lo 16-bit pairs of the MMA operand type.
+template <int DT>
+__device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint32_t& lo) {
+    if (DT == 0) {
+        __half2 h = __floats2half2_rn(a, b);
+        float2 hf = __half22float2(h);
+        __half2 l = __floats2half2_rn(a - hf.x, b - hf.y);
+        hi = *reinterpret_cast<uint32_t*>(&h);
+        lo = *reinterpret_cast<uint32_t*>(&l);
+    } else {
+        __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        float2 hf = __bfloat1622float2(h);
+        __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+        hi = *reinterpret_cast<uint32_t*>(&h);
+        lo = *reinterpret_cast<uint32_t*>(&l);
+    }
+}
+
+// ------------------------------------------------------------------- PTX
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile(
+        "{\n .reg .b64 st;\n mbarrier.arrive.shared::cta.b64 st, [%0];\n}" ::"r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile(
+        "{\n .reg .b64 st;\n mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n}" ::"r"(
+            smem_u32(bar)),
+        "r"(bytes)
+        : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: gives up after ~`limit_cycles` SM clocks and returns false.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  long long limit_cycles) {
+    if (mbar_try_wait(bar, parity)) return true;
+    long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > limit_cycles) return false;
+    }
+    return true;
+}
+
+// One-dimensional bulk copy global -> this CTA's shared memory, completing
+// on `bar` (no multicast).  Addresses 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes,
+                                         uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(smem_u32(smem_dst)),
+        "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// The same with an L2 eviction-priority hint (streamed data read once).
+__device__ __forceinline__ void bulk_g2s_hint(void* smem_dst, const void* gmem_src,
+                                              uint32_t bytes, uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], "
+        "[%1], %2, [%3], %4;" ::"r"(smem_u32(smem_dst)),
+        "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                          uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t a) {
+    uint32_t d;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+    return d;
+}
+
+// D += A(16x16, row) * B(16x8, col), fp32 accumulate; DT 0 = f16, 1 = bf16.
+template <int DT>
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+    if (DT == 0) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+            "{%8,%9}, {%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    } else {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+            "{%8,%9}, {%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    }
+}
+
+// 2^x on the SFU (ex2.approx, flush-to-zero).
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+}  // namespace kvattn

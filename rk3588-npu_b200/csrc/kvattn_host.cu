@@ -1,0 +1,843 @@
+// kvattn_host.cu -- host runtime behind include/kvattn.h: the paged pool,
+// its block allocator and block tables, the decode planner, and the C ABI.
+//
+// Replaces KVCache (worker/include/model/kv_cache.h:19-41,
+// worker/src/model/kv_cache.cpp:4-16) with a pool of fixed-size blocks shared
+// by many sequences, and the inline KV write + op_attention call of
+// Qwen2Model::forward (worker/src/model/qwen2_model.cpp:180-206) with a
+// planned, batched device step.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/kvattn.h"
+#include "kvattn_internal.h"
+
+using namespace kvattn;
+
+// ------------------------------------------------------------------ errors
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int status, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(KV_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define KV_CUDA(call)                                   \
+    do {                                                \
+        cudaError_t e_ = (call);                        \
+        if (e_ != cudaSuccess) return cuda_fail(e_, #call); \
+    } while (0)
+
+// Sets the pool's device for the scope of a call and restores the caller's.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int dev) {
+        if (dev < 0) return;  // host-only pool: no device calls
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+constexpr int kRing = 4;  // plan upload buffers in flight
+
+struct Seq {
+    bool live = false;
+    int len = 0;
+    std::vector<int> blocks;
+};
+
+}  // namespace
+
+// ------------------------------------------------------------------- pool
+struct kvp_pool {
+    std::mutex mu;
+    int device = 0;
+    bool host_only = false;  // device == KVP_HOST_ONLY: allocator/planner only
+    int layers = 0, q_heads = 0, kv_heads = 0, head_dim = 0, block_tokens = 0;
+    int num_blocks = 0, dtype = 0, max_seqs = 0, max_seq_len = 0, mbps = 0;
+    float theta = 0.f;
+    int num_sms = 0, occupancy = 0;
+    long max_items = 0;
+    PoolView pv{};
+
+    // device allocations
+    void* d_k = nullptr;
+    void* d_v = nullptr;
+    float2* d_rope = nullptr;
+    int* d_table = nullptr;
+    int* d_counters = nullptr;
+    float* d_partials = nullptr;
+    int* d_status = nullptr;
+
+    // allocator: LIFO stack of free block ids + position index
+    std::vector<int> free_;
+    std::vector<int> where_;
+    std::vector<Seq> seqs;
+
+    // block-table entries not yet on the device
+    std::vector<TablePatch> pending;
+    TablePatch* h_pending = nullptr;  // pinned
+    TablePatch* d_pending = nullptr;
+    size_t pending_cap = 0;
+    cudaEvent_t pending_evt = nullptr;
+
+    // plan ring
+    size_t plan_bytes = 0;
+    uint8_t* h_plan[kRing] = {};
+    uint8_t* d_plan[kRing] = {};
+    cudaEvent_t plan_evt[kRing] = {};
+    int ring_next = 0;
+
+    // active plan
+    bool plan_active = false;
+    bool plan_patched = false;
+    int plan_slot_ring = 0;
+    int plan_nslots = 0, plan_nitems = 0, plan_npatch = 0;
+    PlanView plan_view{};
+    std::vector<int> plan_seqs;
+    std::vector<int> plan_append;
+    cudaStream_t plan_stream = nullptr;
+
+    void reset_free_list() {
+        free_.resize(num_blocks);
+        where_.assign(num_blocks, -1);
+        for (int i = 0; i < num_blocks; ++i) {
+            free_[i] = num_blocks - 1 - i;  // back() == 0: blocks are handed out 0, 1, 2, ...
+            where_[num_blocks - 1 - i] = i;
+        }
+    }
+    int pop_block() {
+        int b = free_.back();
+        free_.pop_back();
+        where_[b] = -1;
+        return b;
+    }
+    void push_block(int b) {
+        where_[b] = (int)free_.size();
+        free_.push_back(b);
+    }
+    void remove_block(int b) {  // b must be free
+        int i = where_[b];
+        int last = free_.back();
+        free_[i] = last;
+        where_[last] = i;
+        free_.pop_back();
+        where_[b] = -1;
+    }
+};
+
+namespace {
+
+// cos/sin for every (position, pair) with the float libm calls and operation
+// order of rope_one_head (worker/src/ops/op_rope.cpp:11-14): freq =
+// 1/powf(theta, 2i/head_dim), angle = (float)pos * freq.  Built once on the
+// host so the device rotation uses bit-identical factors.
+void build_rope_table(std::vector<float2>& tab, int max_pos, int head_dim, float theta) {
+    const int half = head_dim / 2;
+    std::vector<float> freq(half);
+    for (int i = 0; i < half; ++i)
+        freq[i] = 1.0f / std::pow(theta, (float)(2 * i) / (float)head_dim);
+    tab.resize((size_t)max_pos * half);
+    for (int p = 0; p < max_pos; ++p)
+        for (int i = 0; i < half; ++i) {
+            const float angle = (float)p * freq[i];
+            tab[(size_t)p * half + i] = make_float2(std::cos(angle), std::sin(angle));
+        }
+}
+
+// Upload and apply block-table entries queued by reserve/set_blocks.
+int flush_pending(kvp_pool* p, cudaStream_t st) {
+    if (p->pending.empty()) return KV_OK;
+    if (p->host_only) {
+        p->pending.clear();
+        return KV_OK;
+    }
+    const size_t n = p->pending.size();
+    if (n > p->pending_cap) {
+        if (p->h_pending) {
+            cudaEventSynchronize(p->pending_evt);
+            cudaFreeHost(p->h_pending);
+            cudaFree(p->d_pending);
+            p->h_pending = nullptr;
+            p->d_pending = nullptr;
+        }
+        size_t cap = std::max<size_t>(n, 1024);
+        KV_CUDA(cudaMallocHost((void**)&p->h_pending, cap * sizeof(TablePatch)));
+        KV_CUDA(cudaMalloc((void**)&p->d_pending, cap * sizeof(TablePatch)));
+        p->pending_cap = cap;
+    } else {
+        KV_CUDA(cudaEventSynchronize(p->pending_evt));  // previous upload has read the buffer
+    }
+    memcpy(p->h_pending, p->pending.data(), n * sizeof(TablePatch));
+    KV_CUDA(cudaMemcpyAsync(p->d_pending, p->h_pending, n * sizeof(TablePatch), cudaMemcpyHostToDevice, st));
+    KV_CUDA(cudaEventRecord(p->pending_evt, st));
+    KV_CUDA(launch_patch(p->pv, p->d_pending, (int)n, st));
+    p->pending.clear();
+    return KV_OK;
+}
+
+// Make the device block table current: queued patches and, if no layer call
+// applied them yet, the active plan's new-block patches.
+int sync_table(kvp_pool* p, cudaStream_t st) {
+    int rc = flush_pending(p, st);
+    if (rc != KV_OK) return rc;
+    if (p->plan_active && !p->plan_patched && p->plan_npatch > 0) {
+        KV_CUDA(launch_patch(p->pv, p->plan_view.patches, p->plan_npatch, st));
+        p->plan_patched = true;
+    }
+    return KV_OK;
+}
+
+int require_device(const kvp_pool* p) {
+    if (p->host_only) return fail(KV_ERR_STATE, "host-only pool has no device storage");
+    return KV_OK;
+}
+
+int check_seq(const kvp_pool* p, int seq) {
+    if (seq < 0 || seq >= p->max_seqs || !p->seqs[seq].live)
+        return fail(KV_ERR_BADSEQ, "sequence %d is not live", seq);
+    return KV_OK;
+}
+
+void free_device(kvp_pool* p) {
+    cudaFree(p->d_k);
+    cudaFree(p->d_v);
+    cudaFree(p->d_rope);
+    cudaFree(p->d_table);
+    cudaFree(p->d_counters);
+    cudaFree(p->d_partials);
+    cudaFree(p->d_status);
+    cudaFree(p->d_pending);
+    cudaFreeHost(p->h_pending);
+    if (p->pending_evt) cudaEventDestroy(p->pending_evt);
+    for (int i = 0; i < kRing; ++i) {
+        cudaFree(p->d_plan[i]);
+        cudaFreeHost(p->h_plan[i]);
+        if (p->plan_evt[i]) cudaEventDestroy(p->plan_evt[i]);
+    }
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ C ABI
+extern "C" {
+
+const char* kv_last_error(void) { return g_err.c_str(); }
+
+const char* kv_status_str(int s) {
+    switch (s) {
+        case KV_OK: return "KV_OK";
+        case KV_ERR_INVAL: return "KV_ERR_INVAL";
+        case KV_ERR_OOM: return "KV_ERR_OOM";
+        case KV_ERR_BADSEQ: return "KV_ERR_BADSEQ";
+        case KV_ERR_CUDA: return "KV_ERR_CUDA";
+        case KV_ERR_RANGE: return "KV_ERR_RANGE";
+        case KV_ERR_STATE: return "KV_ERR_STATE";
+        case KV_ERR_TIMEOUT: return "KV_ERR_TIMEOUT";
+        default: return "KV_ERR_UNKNOWN";
+    }
+}
+
+const char* kv_version(void) { return "0.1.0"; }
+
+int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, int head_dim,
+               int block_tokens, int num_blocks, int dtype, int max_seqs, int max_seq_len,
+               float rope_theta, kvp_pool** out) {
+    if (!out) return fail(KV_ERR_INVAL, "out is NULL");
+    *out = nullptr;
+    if (head_dim != kHeadDim) return fail(KV_ERR_INVAL, "head_dim must be %d (got %d)", kHeadDim, head_dim);
+    if (block_tokens != kBlockTokens)
+        return fail(KV_ERR_INVAL, "block_tokens must be %d (got %d)", kBlockTokens, block_tokens);
+    if (num_layers < 1 || num_kv_heads < 1 || num_q_heads < 1 || num_blocks < 1 || max_seqs < 1 ||
+        max_seq_len < 1)
+        return fail(KV_ERR_INVAL, "sizes must be positive");
+    if (num_q_heads % num_kv_heads != 0 || num_q_heads / num_kv_heads > kMaxGroup)
+        return fail(KV_ERR_INVAL, "num_q_heads/num_kv_heads must be an integer <= %d", kMaxGroup);
+    if (dtype != KV_F16 && dtype != KV_BF16) return fail(KV_ERR_INVAL, "dtype must be KV_F16 or KV_BF16");
+    if (!(rope_theta > 0.f)) return fail(KV_ERR_INVAL, "rope_theta must be > 0");
+    const bool host_only = (device == KVP_HOST_ONLY);
+    if (!host_only) {
+        int ndev = 0;
+        KV_CUDA(cudaGetDeviceCount(&ndev));
+        if (device < 0 || device >= ndev)
+            return fail(KV_ERR_INVAL, "device %d out of range (%d devices)", device, ndev);
+    }
+    DeviceGuard dg(host_only ? -1 : device);
+    if (!dg.ok) return fail(KV_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+
+    kvp_pool* p = new kvp_pool();
+    p->device = device;
+    p->host_only = host_only;
+    p->layers = num_layers;
+    p->q_heads = num_q_heads;
+    p->kv_heads = num_kv_heads;
+    p->head_dim = head_dim;
+    p->block_tokens = block_tokens;
+    p->num_blocks = num_blocks;
+    p->dtype = dtype;
+    p->max_seqs = max_seqs;
+    p->max_seq_len = max_seq_len;
+    p->mbps = (max_seq_len + kBlockTokens - 1) / kBlockTokens;
+    p->theta = rope_theta;
+    p->seqs.resize(max_seqs);
+    p->reset_free_list();
+    p->max_items = (long)num_kv_heads * ((long)num_blocks / 8 + 1 + max_seqs);
+
+    auto bail = [&](cudaError_t e, const char* what) {
+        free_device(p);
+        delete p;
+        return cuda_fail(e, what);
+    };
+#define KV_CUDA_B(call)                         \
+    do {                                        \
+        cudaError_t e_ = (call);                \
+        if (e_ != cudaSuccess) return bail(e_, #call); \
+    } while (0)
+
+    if (host_only) {
+        // Bookkeeping only: plans are built for a nominal 148-SM part and kept on the host.
+        p->num_sms = 148;
+        p->occupancy = 3;
+        p->plan_bytes = sizeof(PlanHeader) + (size_t)max_seqs * sizeof(DecodeSlot) +
+                        (size_t)p->max_items * sizeof(WorkItem) + (size_t)max_seqs * sizeof(TablePatch);
+        p->h_plan[0] = (uint8_t*)malloc(p->plan_bytes);
+        if (!p->h_plan[0]) {
+            delete p;
+            return fail(KV_ERR_INVAL, "host allocation of %zu bytes failed", p->plan_bytes);
+        }
+        p->pv.num_blocks = num_blocks;
+        p->pv.kv_heads = num_kv_heads;
+        p->pv.q_heads = num_q_heads;
+        p->pv.group = num_q_heads / num_kv_heads;
+        p->pv.max_blocks_per_seq = p->mbps;
+        p->pv.max_seq_len = max_seq_len;
+        p->pv.dtype = dtype;
+        *out = p;
+        return KV_OK;
+    }
+    KV_CUDA_B(cudaDeviceGetAttribute(&p->num_sms, cudaDevAttrMultiProcessorCount, device));
+    KV_CUDA_B(decode_occupancy(&p->occupancy));
+    if (p->occupancy < 1) p->occupancy = 1;
+
+    const size_t layer_bytes = (size_t)num_blocks * num_kv_heads * kTileBytes;
+    KV_CUDA_B(cudaMalloc(&p->d_k, layer_bytes * num_layers));
+    KV_CUDA_B(cudaMalloc(&p->d_v, layer_bytes * num_layers));
+    KV_CUDA_B(cudaMemset(p->d_k, 0, layer_bytes * num_layers));
+    KV_CUDA_B(cudaMemset(p->d_v, 0, layer_bytes * num_layers));
+
+    std::vector<float2> tab;
+    build_rope_table(tab, max_seq_len, head_dim, rope_theta);
+    KV_CUDA_B(cudaMalloc((void**)&p->d_rope, tab.size() * sizeof(float2)));
+    KV_CUDA_B(cudaMemcpy(p->d_rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+
+    KV_CUDA_B(cudaMalloc((void**)&p->d_table, (size_t)max_seqs * p->mbps * sizeof(int)));
+    KV_CUDA_B(cudaMemset(p->d_table, 0, (size_t)max_seqs * p->mbps * sizeof(int)));
+    KV_CUDA_B(cudaMalloc((void**)&p->d_counters, (size_t)max_seqs * num_kv_heads * sizeof(int)));
+    KV_CUDA_B(cudaMemset(p->d_counters, 0, (size_t)max_seqs * num_kv_heads * sizeof(int)));
+    KV_CUDA_B(cudaMalloc((void**)&p->d_partials, (size_t)p->max_items * kPartialFloats * sizeof(float)));
+    KV_CUDA_B(cudaMalloc((void**)&p->d_status, sizeof(int)));
+    KV_CUDA_B(cudaMemset(p->d_status, 0, sizeof(int)));
+    KV_CUDA_B(cudaEventCreateWithFlags(&p->pending_evt, cudaEventDisableTiming));
+
+    p->plan_bytes = sizeof(PlanHeader) + (size_t)max_seqs * sizeof(DecodeSlot) +
+                    (size_t)p->max_items * sizeof(WorkItem) + (size_t)max_seqs * sizeof(TablePatch);
+    for (int i = 0; i < kRing; ++i) {
+        KV_CUDA_B(cudaMallocHost((void**)&p->h_plan[i], p->plan_bytes));
+        KV_CUDA_B(cudaMalloc((void**)&p->d_plan[i], p->plan_bytes));
+        KV_CUDA_B(cudaEventCreateWithFlags(&p->plan_evt[i], cudaEventDisableTiming));
+    }
+#undef KV_CUDA_B
+
+    PoolView& pv = p->pv;
+    pv.k = (uint8_t*)p->d_k;
+    pv.v = (uint8_t*)p->d_v;
+    pv.rope = p->d_rope;
+    pv.table = p->d_table;
+    pv.counters = p->d_counters;
+    pv.partials = p->d_partials;
+    pv.status = p->d_status;
+    pv.num_blocks = num_blocks;
+    pv.kv_heads = num_kv_heads;
+    pv.q_heads = num_q_heads;
+    pv.group = num_q_heads / num_kv_heads;
+    pv.max_blocks_per_seq = p->mbps;
+    pv.max_seq_len = max_seq_len;
+    pv.dtype = dtype;
+    pv.layer_bytes = layer_bytes;
+    *out = p;
+    return KV_OK;
+}
+
+int kvp_destroy(kvp_pool* p) {
+    if (!p) return KV_OK;
+    if (p->host_only) {
+        free(p->h_plan[0]);
+        delete p;
+        return KV_OK;
+    }
+    {
+        DeviceGuard dg(p->device);
+        cudaDeviceSynchronize();
+        free_device(p);
+    }
+    delete p;
+    return KV_OK;
+}
+
+int kvp_reset(kvp_pool* p, void* stream) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    std::lock_guard<std::mutex> lk(p->mu);
+    DeviceGuard dg(p->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (!p->host_only) {
+        const size_t bytes = p->pv.layer_bytes * p->layers;
+        KV_CUDA(cudaMemsetAsync(p->d_k, 0, bytes, st));
+        KV_CUDA(cudaMemsetAsync(p->d_v, 0, bytes, st));
+    }
+    for (auto& s : p->seqs) s = Seq();
+    p->reset_free_list();
+    p->pending.clear();
+    p->plan_active = false;
+    return KV_OK;
+}
+
+int kvp_free_blocks(const kvp_pool* p, int* n) {
+    if (!p || !n) return fail(KV_ERR_INVAL, "NULL argument");
+    *n = (int)p->free_.size();
+    return KV_OK;
+}
+
+int kvp_num_blocks(const kvp_pool* p, int* n) {
+    if (!p || !n) return fail(KV_ERR_INVAL, "NULL argument");
+    *n = p->num_blocks;
+    return KV_OK;
+}
+
+int kvp_storage(const kvp_pool* p, void** k, void** v, size_t* layer_bytes) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    if (k) *k = p->d_k;
+    if (v) *v = p->d_v;
+    if (layer_bytes) *layer_bytes = p->pv.layer_bytes;
+    return KV_OK;
+}
+
+int kvp_launch_info(const kvp_pool* p, int* num_sms, int* ctas_per_sm) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    if (num_sms) *num_sms = p->num_sms;
+    if (ctas_per_sm) *ctas_per_sm = p->occupancy;
+    return KV_OK;
+}
+
+int kvp_seq_alloc(kvp_pool* p, int* seq_id) {
+    if (!p || !seq_id) return fail(KV_ERR_INVAL, "NULL argument");
+    std::lock_guard<std::mutex> lk(p->mu);
+    for (int i = 0; i < p->max_seqs; ++i)
+        if (!p->seqs[i].live) {
+            p->seqs[i] = Seq();
+            p->seqs[i].live = true;
+            *seq_id = i;
+            return KV_OK;
+        }
+    return fail(KV_ERR_OOM, "all %d sequence slots are live", p->max_seqs);
+}
+
+int kvp_seq_free(kvp_pool* p, int seq) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    std::lock_guard<std::mutex> lk(p->mu);
+    int rc = check_seq(p, seq);
+    if (rc) return rc;
+    if (p->plan_active && std::find(p->plan_seqs.begin(), p->plan_seqs.end(), seq) != p->plan_seqs.end())
+        return fail(KV_ERR_STATE, "sequence %d is part of the active decode plan", seq);
+    Seq& s = p->seqs[seq];
+    for (int j = (int)s.blocks.size() - 1; j >= 0; --j) p->push_block(s.blocks[j]);
+    // Drop queued table writes for this sequence: its row is dead.
+    p->pending.erase(std::remove_if(p->pending.begin(), p->pending.end(),
+                                    [seq](const TablePatch& t) { return t.seq == seq; }),
+                     p->pending.end());
+    s = Seq();
+    return KV_OK;
+}
+
+int kvp_seq_reserve(kvp_pool* p, int seq, int n_tokens) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    std::lock_guard<std::mutex> lk(p->mu);
+    int rc = check_seq(p, seq);
+    if (rc) return rc;
+    if (n_tokens < 0) return fail(KV_ERR_INVAL, "n_tokens < 0");
+    if (n_tokens > p->max_seq_len)
+        return fail(KV_ERR_RANGE, "n_tokens %d > max_seq_len %d", n_tokens, p->max_seq_len);
+    Seq& s = p->seqs[seq];
+    const int need = (n_tokens + kBlockTokens - 1) / kBlockTokens - (int)s.blocks.size();
+    if (need <= 0) return KV_OK;
+    if (need > (int)p->free_.size())
+        return fail(KV_ERR_OOM, "need %d blocks, %zu free", need, p->free_.size());
+    for (int i = 0; i < need; ++i) {
+        const int b = p->pop_block();
+        p->pending.push_back(TablePatch{seq, (int)s.blocks.size(), b, 0});
+        s.blocks.push_back(b);
+    }
+    return KV_OK;
+}
+
+int kvp_seq_set_blocks(kvp_pool* p, int seq, const int* ids, int n) {
+    if (!p || (n > 0 && !ids)) return fail(KV_ERR_INVAL, "NULL argument");
+    std::lock_guard<std::mutex> lk(p->mu);
+    int rc = check_seq(p, seq);
+    if (rc) return rc;
+    if (n < 0) return fail(KV_ERR_INVAL, "n < 0");
+    Seq& s = p->seqs[seq];
+    if ((long)s.blocks.size() + n > p->mbps)
+        return fail(KV_ERR_RANGE, "table would hold %ld blocks > %d", (long)s.blocks.size() + n, p->mbps);
+    std::vector<char> seen;
+    for (int i = 0; i < n; ++i) {
+        if (ids[i] < 0 || ids[i] >= p->num_blocks) return fail(KV_ERR_INVAL, "block id %d out of range", ids[i]);
+        if (p->where_[ids[i]] < 0) return fail(KV_ERR_INVAL, "block %d is not free", ids[i]);
+    }
+    seen.assign(p->num_blocks, 0);
+    for (int i = 0; i < n; ++i) {
+        if (seen[ids[i]]) return fail(KV_ERR_INVAL, "block %d listed twice", ids[i]);
+        seen[ids[i]] = 1;
+    }
+    for (int i = 0; i < n; ++i) {
+        p->remove_block(ids[i]);
+        p->pending.push_back(TablePatch{seq, (int)s.blocks.size(), ids[i], 0});
+        s.blocks.push_back(ids[i]);
+    }
+    return KV_OK;
+}
+
+int kvp_seq_len(const kvp_pool* p, int seq, int* len) {
+    if (!p || !len) return fail(KV_ERR_INVAL, "NULL argument");
+    int rc = check_seq(p, seq);
+    if (rc) return rc;
+    *len = p->seqs[seq].len;
+    return KV_OK;
+}
+
+int kvp_seq_set_len(kvp_pool* p, int seq, int len) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    std::lock_guard<std::mutex> lk(p->mu);
+    int rc = check_seq(p, seq);
+    if (rc) return rc;
+    Seq& s = p->seqs[seq];
+    if (len < 0 || len > (int)s.blocks.size() * kBlockTokens)
+        return fail(KV_ERR_RANGE, "length %d outside [0, %zu] reserved", len, s.blocks.size() * kBlockTokens);
+    s.len = len;
+    return KV_OK;
+}
+
+int kvp_seq_blocks(const kvp_pool* p, int seq, int* ids, int cap, int* n_out) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    int rc = check_seq(p, seq);
+    if (rc) return rc;
+    const Seq& s = p->seqs[seq];
+    if (n_out) *n_out = (int)s.blocks.size();
+    if (ids) {
+        const int n = std::min(cap, (int)s.blocks.size());
+        for (int i = 0; i < n; ++i) ids[i] = s.blocks[i];
+    }
+    return KV_OK;
+}
+
+int kvp_import(kvp_pool* p, int layer, int seq, int pos0, int n, const void* k_rows,
+               const void* v_rows, void* stream) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    std::lock_guard<std::mutex> lk(p->mu);
+    int rc = check_seq(p, seq);
+    if (rc) return rc;
+    rc = require_device(p);
+    if (rc) return rc;
+    if (layer < 0 || layer >= p->layers) return fail(KV_ERR_INVAL, "layer %d out of range", layer);
+    if (n < 0 || pos0 < 0) return fail(KV_ERR_INVAL, "negative position/count");
+    if ((long)pos0 + n > (long)p->seqs[seq].blocks.size() * kBlockTokens)
+        return fail(KV_ERR_RANGE, "positions [%d, %d) exceed reserved blocks", pos0, pos0 + n);
+    if (n == 0) return KV_OK;
+    if (!k_rows || !v_rows || ((uintptr_t)k_rows & 15) || ((uintptr_t)v_rows & 15))
+        return fail(KV_ERR_INVAL, "row pointers must be non-NULL and 16-byte aligned");
+    DeviceGuard dg(p->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    rc = sync_table(p, st);
+    if (rc) return rc;
+    KV_CUDA(launch_import(p->pv, layer, seq, pos0, n, (const uint16_t*)k_rows, (const uint16_t*)v_rows, st));
+    return KV_OK;
+}
+
+int kvp_gather(kvp_pool* p, int layer, int seq, void* k_rows, void* v_rows, void* stream) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    std::lock_guard<std::mutex> lk(p->mu);
+    int rc = check_seq(p, seq);
+    if (rc) return rc;
+    rc = require_device(p);
+    if (rc) return rc;
+    if (layer < 0 || layer >= p->layers) return fail(KV_ERR_INVAL, "layer %d out of range", layer);
+    const int len = p->seqs[seq].len;
+    if (len == 0) return KV_OK;
+    if (!k_rows || !v_rows || ((uintptr_t)k_rows & 15) || ((uintptr_t)v_rows & 15))
+        return fail(KV_ERR_INVAL, "row pointers must be non-NULL and 16-byte aligned");
+    DeviceGuard dg(p->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    rc = sync_table(p, st);
+    if (rc) return rc;
+    KV_CUDA(launch_gather(p->pv, layer, seq, len, (uint16_t*)k_rows, (uint16_t*)v_rows, st));
+    return KV_OK;
+}
+
+int kv_append_chunk(kvp_pool* p, int layer, int seq, int pos0, int n, const float* k,
+                    const float* v, void* stream) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    std::lock_guard<std::mutex> lk(p->mu);
+    int rc = check_seq(p, seq);
+    if (rc) return rc;
+    rc = require_device(p);
+    if (rc) return rc;
+    if (layer < 0 || layer >= p->layers) return fail(KV_ERR_INVAL, "layer %d out of range", layer);
+    if (n < 0 || pos0 < 0) return fail(KV_ERR_INVAL, "negative position/count");
+    if ((long)pos0 + n > p->max_seq_len)
+        return fail(KV_ERR_RANGE, "position %ld beyond max_seq_len %d", (long)pos0 + n - 1, p->max_seq_len);
+    if ((long)pos0 + n > (long)p->seqs[seq].blocks.size() * kBlockTokens)
+        return fail(KV_ERR_RANGE, "positions [%d, %d) exceed reserved blocks", pos0, pos0 + n);
+    if (n == 0) return KV_OK;
+    if (!k || !v || ((uintptr_t)k & 7) || ((uintptr_t)v & 7))
+        return fail(KV_ERR_INVAL, "k/v must be non-NULL and 8-byte aligned");
+    DeviceGuard dg(p->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    rc = sync_table(p, st);
+    if (rc) return rc;
+    KV_CUDA(launch_append_chunk(p->pv, layer, seq, pos0, n, k, v, st));
+    return KV_OK;
+}
+
+int attn_decode_plan_ex(kvp_pool* p, int nseq, const int* seq_ids, const int* rope_pos,
+                        const int* append, void* stream) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    std::lock_guard<std::mutex> lk(p->mu);
+    if (nseq < 1 || nseq > p->max_seqs) return fail(KV_ERR_INVAL, "nseq %d outside [1, %d]", nseq, p->max_seqs);
+    if (!seq_ids) return fail(KV_ERR_INVAL, "seq_ids is NULL");
+    DeviceGuard dg(p->device);
+    cudaStream_t st = (cudaStream_t)stream;
+
+    // ---- validate everything before changing anything ----
+    std::vector<char> seen(p->max_seqs, 0);
+    int new_blocks = 0;
+    long total = 0;
+    int maxlen = 0;
+    for (int i = 0; i < nseq; ++i) {
+        const int sid = seq_ids[i];
+        int rc = check_seq(p, sid);
+        if (rc) return rc;
+        if (seen[sid]) return fail(KV_ERR_INVAL, "sequence %d listed twice", sid);
+        seen[sid] = 1;
+        const Seq& s = p->seqs[sid];
+        const int app = append ? (append[i] != 0) : 1;
+        const int rp = rope_pos ? rope_pos[i] : s.len;
+        if (rp < 0 || rp >= p->max_seq_len)
+            return fail(KV_ERR_RANGE, "rope position %d outside [0, %d)", rp, p->max_seq_len);
+        const int kv_len = s.len + app;
+        if (kv_len > p->mbps * kBlockTokens || kv_len > p->max_seq_len)
+            return fail(KV_ERR_RANGE, "sequence %d would reach %d tokens > max_seq_len %d", sid, kv_len, p->max_seq_len);
+        if (app && s.len / kBlockTokens >= (int)s.blocks.size()) ++new_blocks;
+        total += kv_len;
+        maxlen = std::max(maxlen, kv_len);
+    }
+    if (new_blocks > (int)p->free_.size())
+        return fail(KV_ERR_OOM, "decode step needs %d new blocks, %zu free", new_blocks, p->free_.size());
+
+    // A plan that never reached a layer call still owes its table entries.
+    if (p->plan_active && !p->plan_patched && p->plan_npatch > 0 && !p->host_only) {
+        KV_CUDA(launch_patch(p->pv, p->plan_view.patches, p->plan_npatch, st));
+        p->plan_patched = true;
+    }
+    int rc = flush_pending(p, st);
+    if (rc) return rc;
+
+    // ---- chunk size: ~2 items per resident CTA, >= 128 tokens, <= 256 chunks per row ----
+    const long grid = (long)p->num_sms * p->occupancy;
+    long ch = (total * p->kv_heads + 2 * grid - 1) / (2 * grid);
+    ch = std::max(ch, (long)(maxlen + 255) / 256);
+    ch = std::max<long>(ch, 128);
+    ch = (ch + kBlockTokens - 1) / kBlockTokens * kBlockTokens;
+
+    // ---- build into the next ring buffer ----
+    const int r = p->host_only ? 0 : p->ring_next;
+    p->ring_next = (r + 1) % kRing;
+    if (!p->host_only) KV_CUDA(cudaEventSynchronize(p->plan_evt[r]));  // its previous upload has read it
+    uint8_t* h = p->h_plan[r];
+    PlanHeader* hdr = (PlanHeader*)h;
+    DecodeSlot* slots = (DecodeSlot*)(h + sizeof(PlanHeader));
+    WorkItem* items = (WorkItem*)(slots + p->max_seqs);
+    TablePatch* patches = (TablePatch*)(items + p->max_items);
+    int nitems = 0, npatch = 0;
+    p->plan_seqs.assign(seq_ids, seq_ids + nseq);
+    p->plan_append.resize(nseq);
+    for (int i = 0; i < nseq; ++i) {
+        const int sid = seq_ids[i];
+        Seq& s = p->seqs[sid];
+        const int app = append ? (append[i] != 0) : 1;
+        DecodeSlot& sl = slots[i];
+        sl.seq = sid;
+        sl.kv_len = s.len + app;
+        sl.rope_pos = rope_pos ? rope_pos[i] : s.len;
+        sl.append = app;
+        sl.new_block = -1;
+        if (app) {
+            const int idx = s.len / kBlockTokens;
+            if (idx >= (int)s.blocks.size()) {
+                const int b = p->pop_block();
+                s.blocks.push_back(b);
+                patches[npatch++] = TablePatch{sid, idx, b, 0};
+            }
+            sl.new_block = s.blocks[idx];
+        }
+        sl.nchunks = std::max(1, (int)((sl.kv_len + ch - 1) / ch));
+        sl.item_base = nitems;
+        sl.pad = 0;
+        if (nitems + (long)p->kv_heads * sl.nchunks > p->max_items)
+            return fail(KV_ERR_STATE, "work list overflow (%ld items)", p->max_items);
+        for (int hd = 0; hd < p->kv_heads; ++hd)
+            for (int c = 0; c < sl.nchunks; ++c) items[nitems++] = WorkItem{i, hd, c, 0};
+        p->plan_append[i] = app;
+    }
+    hdr->nslots = nseq;
+    hdr->nitems = nitems;
+    hdr->npatch = npatch;
+    hdr->chunk_tokens = (int)ch;
+    // Upload the used parts (header + slots contiguous; items; patches).
+    const size_t off_items = (uint8_t*)items - h, off_patch = (uint8_t*)patches - h;
+    p->plan_active = true;
+    p->plan_patched = (npatch == 0);
+    p->plan_slot_ring = r;
+    p->plan_nslots = nseq;
+    p->plan_nitems = nitems;
+    p->plan_npatch = npatch;
+    if (p->host_only) {
+        p->plan_view = PlanView{(const PlanHeader*)h, slots, items, patches};
+        p->plan_patched = true;
+        return KV_OK;
+    }
+    uint8_t* d = p->d_plan[r];
+    KV_CUDA(cudaMemcpyAsync(d, h, sizeof(PlanHeader) + nseq * sizeof(DecodeSlot), cudaMemcpyHostToDevice, st));
+    KV_CUDA(cudaMemcpyAsync(d + off_items, h + off_items, nitems * sizeof(WorkItem), cudaMemcpyHostToDevice, st));
+    if (npatch)
+        KV_CUDA(cudaMemcpyAsync(d + off_patch, h + off_patch, npatch * sizeof(TablePatch), cudaMemcpyHostToDevice, st));
+    KV_CUDA(cudaEventRecord(p->plan_evt[r], st));
+
+    p->plan_view.hdr = (const PlanHeader*)d;
+    p->plan_view.slots = (const DecodeSlot*)(d + sizeof(PlanHeader));
+    p->plan_view.items = (const WorkItem*)(d + off_items);
+    p->plan_view.patches = (const TablePatch*)(d + off_patch);
+    p->plan_stream = st;
+    return KV_OK;
+}
+
+int kvp_plan_info(const kvp_pool* p, int* nitems, int* chunk_tokens, int* npatch, int* item_slot,
+                  int* item_head, int* item_chunk, int cap) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    if (!p->plan_active) return fail(KV_ERR_STATE, "no active decode plan");
+    const uint8_t* h = p->h_plan[p->plan_slot_ring];
+    const PlanHeader* hdr = (const PlanHeader*)h;
+    const WorkItem* items = (const WorkItem*)(h + sizeof(PlanHeader) + (size_t)p->max_seqs * sizeof(DecodeSlot));
+    if (nitems) *nitems = hdr->nitems;
+    if (chunk_tokens) *chunk_tokens = hdr->chunk_tokens;
+    if (npatch) *npatch = hdr->npatch;
+    const int n = std::min(cap, hdr->nitems);
+    for (int i = 0; i < n; ++i) {
+        if (item_slot) item_slot[i] = items[i].slot;
+        if (item_head) item_head[i] = items[i].head;
+        if (item_chunk) item_chunk[i] = items[i].chunk;
+    }
+    return KV_OK;
+}
+
+int attn_decode_plan(kvp_pool* p, int nseq, const int* seq_ids, void* stream) {
+    return attn_decode_plan_ex(p, nseq, seq_ids, nullptr, nullptr, stream);
+}
+
+static int decode_call(kvp_pool* p, int layer, const float* q, const float* k_new, const float* v_new,
+                       float* out, float* m, float* l, void* stream) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    std::lock_guard<std::mutex> lk(p->mu);
+    if (!p->plan_active) return fail(KV_ERR_STATE, "no active decode plan");
+    if (int rc = require_device(p)) return rc;
+    if (layer < 0 || layer >= p->layers) return fail(KV_ERR_INVAL, "layer %d out of range", layer);
+    if (!q || !k_new || !v_new || !out) return fail(KV_ERR_INVAL, "NULL tensor");
+    if (((uintptr_t)q | (uintptr_t)k_new | (uintptr_t)v_new) & 7)
+        return fail(KV_ERR_INVAL, "q/k_new/v_new must be 8-byte aligned");
+    DeviceGuard dg(p->device);
+    const long grid = std::min<long>(p->plan_nitems, (long)p->num_sms * p->occupancy);
+    KV_CUDA(launch_decode(p->pv, p->plan_view, p->plan_nitems, p->plan_npatch, layer, q, k_new, v_new, out,
+                          m, l, (int)grid, (cudaStream_t)stream));
+    p->plan_patched = true;
+    return KV_OK;
+}
+
+int attn_decode_append(kvp_pool* p, int layer, const float* q, const float* k_new,
+                       const float* v_new, float* out, void* stream) {
+    return decode_call(p, layer, q, k_new, v_new, out, nullptr, nullptr, stream);
+}
+
+int attn_decode_append_partial(kvp_pool* p, int layer, const float* q, const float* k_new,
+                               const float* v_new, float* out, float* m, float* l, void* stream) {
+    if (!m || !l) return fail(KV_ERR_INVAL, "m and l are required");
+    return decode_call(p, layer, q, k_new, v_new, out, m, l, stream);
+}
+
+int attn_decode_commit(kvp_pool* p) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    std::lock_guard<std::mutex> lk(p->mu);
+    if (!p->plan_active) return fail(KV_ERR_STATE, "no active decode plan");
+    if (!p->plan_patched && p->plan_npatch > 0 && !p->host_only) {
+        DeviceGuard dg(p->device);
+        KV_CUDA(launch_patch(p->pv, p->plan_view.patches, p->plan_npatch, p->plan_stream));
+    }
+    for (size_t i = 0; i < p->plan_seqs.size(); ++i)
+        if (p->plan_append[i]) p->seqs[p->plan_seqs[i]].len += 1;
+    p->plan_active = false;
+    return KV_OK;
+}
+
+int attn_combine_lse(int G, int rows, int dim, const float* m, const float* l, const float* o,
+                     float* out, void* stream) {
+    if (G < 1 || rows < 0 || dim < 1) return fail(KV_ERR_INVAL, "bad sizes");
+    if (rows == 0) return KV_OK;
+    if (!m || !l || !o || !out) return fail(KV_ERR_INVAL, "NULL tensor");
+    KV_CUDA(launch_combine(G, rows, dim, m, l, o, out, (cudaStream_t)stream));
+    return KV_OK;
+}
+
+int kvp_device_status(kvp_pool* p, void* stream, int* status) {
+    if (!p || !status) return fail(KV_ERR_INVAL, "NULL argument");
+    if (int rc = require_device(p)) return rc;
+    DeviceGuard dg(p->device);
+    int v = 0;
+    KV_CUDA(cudaMemcpyAsync(&v, p->d_status, sizeof(int), cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+    KV_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+    KV_CUDA(cudaMemsetAsync(p->d_status, 0, sizeof(int), (cudaStream_t)stream));
+    *status = v;
+    return KV_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,102 @@
+// kvattn_internal.h -- structures shared by the host runtime and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace kvattn {
+
+constexpr int kHeadDim = 128;          // dims per head (the only supported value)
+constexpr int kBlockTokens = 16;       // token rows per block
+constexpr int kTileBytes = kBlockTokens * kHeadDim * 2;  // one (block, kv head) tile: 4 KiB
+constexpr int kMaxGroup = 8;           // query heads per KV head handled by one MMA tile
+constexpr int kPartialFloats = kMaxGroup * (kHeadDim + 2);  // m[8], l[8], o[8][128]
+
+// Byte offset of element (token t, dim d) inside a 4 KiB tile.
+// Two 2 KiB halves (dims 0-63, 64-127); each half has 16 rows of 128 bytes;
+// the 16-byte chunk index inside a row is XORed with (t & 7).  This is the
+// 128-byte-swizzle K-major layout, so ldmatrix rows of 8 consecutive tokens at
+// one logical chunk land in 8 different bank groups.
+__host__ __device__ inline uint32_t tile_offset(int t, int d) {
+    return (uint32_t)(((d >> 6) * 16 + t) * 128 + ((((d >> 3) & 7) ^ (t & 7)) << 4) + (d & 7) * 2);
+}
+
+// One batch row of a decode plan.
+struct DecodeSlot {
+    int seq;        // row of the block table
+    int kv_len;     // tokens attended (including the new one when append)
+    int rope_pos;   // position used to rotate q and the new k
+    int append;     // 1: write the new token at local slot kv_len-1
+    int new_block;  // block id holding slot kv_len-1 when append (else -1)
+    int nchunks;    // split-KV chunks per KV head (>= 1)
+    int item_base;  // index of this slot's first work item
+    int pad;
+};
+
+// One unit of work: (slot, kv head, chunk).
+struct WorkItem {
+    int slot;
+    int head;
+    int chunk;
+    int pad;
+};
+
+// A block-table entry to write before use: table[seq][idx] = block.
+struct TablePatch {
+    int seq;
+    int idx;
+    int block;
+    int pad;
+};
+
+struct PlanHeader {
+    int nslots;
+    int nitems;
+    int npatch;
+    int chunk_tokens;  // multiple of kBlockTokens
+};
+
+// Device view of the pool handed to kernels by value.
+struct PoolView {
+    uint8_t* k;              // [layers][num_blocks][kv_heads][kTileBytes]
+    uint8_t* v;
+    const float2* rope;      // [max_seq_len][kHeadDim/2] (cos, sin)
+    int* table;              // [max_seqs][max_blocks_per_seq]
+    int* counters;           // [max_seqs][kv_heads] arrival counters (kept at 0 between launches)
+    float* partials;         // [max_items][kPartialFloats]
+    int* status;             // device status word
+    int num_blocks;
+    int kv_heads;
+    int q_heads;
+    int group;               // q_heads / kv_heads
+    int max_blocks_per_seq;
+    int max_seq_len;
+    int dtype;               // 0 f16, 1 bf16
+    size_t layer_bytes;      // num_blocks * kv_heads * kTileBytes
+};
+
+// Plan as the decode kernel sees it (device pointers into one upload).
+struct PlanView {
+    const PlanHeader* hdr;
+    const DecodeSlot* slots;
+    const WorkItem* items;
+    const TablePatch* patches;
+};
+
+// ---- launchers (kernels.cu) ----
+cudaError_t launch_decode(const PoolView& pv, const PlanView& plan, int nitems, int npatch,
+                          int layer, const float* q, const float* k_new, const float* v_new,
+                          float* out, float* m_out, float* l_out, int grid, cudaStream_t st);
+cudaError_t decode_occupancy(int* ctas_per_sm);
+cudaError_t launch_import(const PoolView& pv, int layer, int seq, int pos0, int n,
+                          const uint16_t* k_rows, const uint16_t* v_rows, cudaStream_t st);
+cudaError_t launch_gather(const PoolView& pv, int layer, int seq, int len, uint16_t* k_rows,
+                          uint16_t* v_rows, cudaStream_t st);
+cudaError_t launch_append_chunk(const PoolView& pv, int layer, int seq, int pos0, int n,
+                                const float* k, const float* v, cudaStream_t st);
+cudaError_t launch_patch(const PoolView& pv, const TablePatch* patches, int npatch,
+                         cudaStream_t st);
+cudaError_t launch_combine(int G, int rows, int dim, const float* m, const float* l,
+                           const float* o, float* out, cudaStream_t st);
+
+}  // namespace kvattn

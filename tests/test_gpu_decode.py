@@ -1,0 +1,282 @@
+"""GPU parity: the CUDA decode path through the C ABI against the oracle.
+
+Bars (from the task's stated tolerances):
+  * appended cache contents and block bookkeeping: bit-exact (kvp_gather
+    returns the reference's contiguous row layout);
+  * attention outputs: relative error <= 1e-3 per (sequence, query head)
+    row, measured as max|gpu - ref| / max|ref| over the row's 128 dims.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3
+HD = 128
+
+
+def need_gpu():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def to_dev(a: np.ndarray):
+    if a.dtype == np.uint16:
+        a = a.view(np.int16)
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def rel_err(gpu: np.ndarray, ref: np.ndarray) -> float:
+    g = gpu.reshape(-1, HD).astype(np.float64)
+    r = ref.reshape(-1, HD).astype(np.float64)
+    den = np.maximum(np.abs(r).max(axis=1), 1e-30)
+    return float((np.abs(g - r).max(axis=1) / den).max())
+
+
+class Harness:
+    """One pool plus the oracle's contiguous per-sequence caches."""
+
+    def __init__(self, kv, orc, lens, dtype, layers=1, q_heads=12, kv_heads=2, extra=8, seed=0,
+                 perm=False, num_blocks=None):
+        self.kv, self.orc = kv, orc
+        self.rng = np.random.default_rng(seed)
+        self.dtype, self.layers = dtype, layers
+        self.qh, self.kvh = q_heads, kv_heads
+        self.kvd = kv_heads * HD
+        need = sum(-(-(L + extra) // 16) for L in lens)
+        nb = num_blocks or need + 8
+        maxlen = max(lens) + extra + 16
+        self.P = kv.Pool(0, layers, nb, num_q_heads=q_heads, num_kv_heads=kv_heads, dtype=dtype,
+                         max_seqs=max(len(lens), 1), max_seq_len=maxlen)
+        self.ids, self.kc, self.vc = [], [], []
+        order = self.rng.permutation(nb) if perm else None
+        used = 0
+        for L in lens:
+            s = self.P.seq_alloc()
+            cap = L + extra
+            if perm:
+                nblk = -(-cap // 16)
+                self.P.set_blocks(s, order[used:used + nblk])
+                used += nblk
+            else:
+                self.P.reserve(s, cap)
+            kcs, vcs = [], []
+            for layer in range(layers):
+                kc = np.zeros((cap, self.kvd), np.uint16)
+                vc = np.zeros((cap, self.kvd), np.uint16)
+                if L:
+                    kc[:L] = orc.encode(self.rng.standard_normal((L, self.kvd)).astype(np.float32), dtype)
+                    vc[:L] = orc.encode(self.rng.standard_normal((L, self.kvd)).astype(np.float32), dtype)
+                    self.P.import_rows(layer, s, 0, to_dev(kc[:L]), to_dev(vc[:L]))
+                kcs.append(kc)
+                vcs.append(vc)
+            self.P.set_cur_pos(s, L)
+            self.ids.append(s)
+            self.kc.append(kcs)
+            self.vc.append(vcs)
+        self.len = list(lens)
+
+    def step(self, check_gather=True):
+        B = len(self.ids)
+        self.P.plan(self.ids)
+        worst = 0.0
+        for layer in range(self.layers):
+            q = self.rng.standard_normal((B, self.qh * HD)).astype(np.float32)
+            k = self.rng.standard_normal((B, self.kvd)).astype(np.float32)
+            v = self.rng.standard_normal((B, self.kvd)).astype(np.float32)
+            out = torch.empty((B, self.qh * HD), dtype=torch.float32, device="cuda")
+            self.P.decode_layer(layer, to_dev(q), to_dev(k), to_dev(v), out)
+            got = out.cpu().numpy()
+            for i in range(B):
+                ref, _, _ = self.orc.layer_step(q[i:i + 1], k[i:i + 1], v[i:i + 1],
+                                                self.kc[i][layer], self.vc[i][layer], self.len[i],
+                                                self.qh, self.kvh, HD, 1e6, self.dtype)
+                worst = max(worst, rel_err(got[i], ref[0]))
+        self.P.commit()
+        for i in range(B):
+            self.len[i] += 1
+            assert self.P.cur_pos(self.ids[i]) == self.len[i]
+        if check_gather:
+            self.check_cache()
+        return worst
+
+    def check_cache(self):
+        torch.cuda.synchronize()
+        for i, s in enumerate(self.ids):
+            for layer in range(self.layers):
+                kd, vd = self.P.gather(layer, s)
+                kg = kd.cpu().numpy().view(np.uint16)
+                vg = vd.cpu().numpy().view(np.uint16)
+                L = self.len[i]
+                assert np.array_equal(kg, self.kc[i][layer][:L]), (i, layer)
+                assert np.array_equal(vg, self.vc[i][layer][:L]), (i, layer)
+
+
+EDGE_LENS = [0, 1, 14, 15, 16, 17, 31, 127, 128, 129, 255, 256, 257, 1000, 3001]
+
+
+@pytest.mark.parametrize("dtype", [0, 1], ids=["f16", "bf16"])
+def test_decode_ragged_edges(kv, orc, dtype):
+    need_gpu()
+    H = Harness(kv, orc, EDGE_LENS, dtype, extra=20, seed=dtype)
+    for _ in range(3):  # crosses block boundaries for 14/15/16/31/127/...
+        assert H.step() <= TOL
+    assert H.P.device_status() == 0
+
+
+def test_decode_random_permutation_tables_multi_layer(kv, orc):
+    need_gpu()
+    H = Harness(kv, orc, [5, 40, 300, 777], 1, layers=3, perm=True, seed=3, extra=18)
+    for _ in range(2):
+        assert H.step() <= TOL
+
+
+@pytest.mark.parametrize("qh,kvh", [(16, 2), (4, 4), (8, 1)])
+def test_decode_group_sizes(kv, orc, qh, kvh):
+    need_gpu()
+    H = Harness(kv, orc, [3, 100, 513], 0, q_heads=qh, kv_heads=kvh, seed=qh)
+    assert H.step() <= TOL
+
+
+def test_decode_long_sequence_many_chunks(kv, orc):
+    need_gpu()
+    H = Harness(kv, orc, [20000, 37], 1, seed=9, extra=4)
+    info_lens = list(H.len)
+    assert H.step(check_gather=False) <= TOL
+    H.P.plan(H.ids)
+    assert H.P.plan_info()["nitems"] > 2 * 8
+    H.P.commit()  # advances without a layer call: table entries still applied
+    H.len = [L + 1 for L in H.len]
+    assert H.P.cur_pos(H.ids[0]) == info_lens[0] + 2
+
+
+def test_decode_config2_shape(kv, orc):
+    """Batch 32, lengths U[256,4096] (seed 1), fp16: 4 steps, every row checked."""
+    need_gpu()
+    rng = np.random.default_rng(1)
+    lens = [int(x) for x in rng.integers(256, 4097, 32)]
+    H = Harness(kv, orc, lens, 0, seed=1, extra=8)
+    for _ in range(4):
+        assert H.step(check_gather=False) <= TOL
+    H.check_cache()
+    assert H.P.device_status() == 0
+
+
+@pytest.mark.parametrize("dtype", [0, 1], ids=["f16", "bf16"])
+def test_prefill_append_chunk_bit_exact(kv, orc, dtype):
+    need_gpu()
+    rng = np.random.default_rng(21)
+    P = kv.Pool(0, 2, 64, dtype=dtype, max_seqs=2, max_seq_len=1024)
+    s = P.seq_alloc()
+    pos0, n = 13, 150
+    P.reserve(s, pos0 + n)
+    kc = [np.zeros((pos0 + n, 256), np.uint16) for _ in range(2)]
+    vc = [np.zeros((pos0 + n, 256), np.uint16) for _ in range(2)]
+    for layer in range(2):
+        k0 = orc.encode(rng.standard_normal((pos0, 256)).astype(np.float32), dtype)
+        v0 = orc.encode(rng.standard_normal((pos0, 256)).astype(np.float32), dtype)
+        kc[layer][:pos0], vc[layer][:pos0] = k0, v0
+        P.import_rows(layer, s, 0, to_dev(k0), to_dev(v0))
+        k = (rng.standard_normal((n, 256)) * 40).astype(np.float32)
+        v = (rng.standard_normal((n, 256)) * 40).astype(np.float32)
+        k[0, :3] = [1e6, -1e-9, np.nan]  # inf and flush-to-zero paths of the encoder
+        P.append_chunk(layer, s, pos0, to_dev(k), to_dev(v))
+        q = np.zeros((n, 12 * HD), np.float32)
+        orc.lib().orc_rope_append(q.reshape(-1), k.copy().reshape(-1), v.reshape(-1),
+                                  kc[layer].reshape(-1), vc[layer].reshape(-1), n, pos0, 12, 2, HD,
+                                  1e6, dtype)
+    P.set_cur_pos(s, pos0 + n)
+    for layer in range(2):
+        kd, vd = P.gather(layer, s)
+        assert np.array_equal(kd.cpu().numpy().view(np.uint16), kc[layer])
+        assert np.array_equal(vd.cpu().numpy().view(np.uint16), vc[layer])
+
+
+def test_import_gather_roundtrip_any_bits(kv):
+    need_gpu()
+    rng = np.random.default_rng(4)
+    P = kv.Pool(0, 1, 40, max_seqs=3, max_seq_len=640)
+    ids = []
+    rows = []
+    for L in (1, 200, 333):
+        s = P.seq_alloc()
+        P.reserve(s, L)
+        r = rng.integers(0, 65536, (L, 256), dtype=np.uint16)
+        P.import_rows(0, s, 0, to_dev(r), to_dev(r[::-1].copy()))
+        P.set_cur_pos(s, L)
+        ids.append(s)
+        rows.append(r)
+    for s, r in zip(ids, rows):
+        kd, vd = P.gather(0, s)
+        assert np.array_equal(kd.cpu().numpy().view(np.uint16), r)
+        assert np.array_equal(vd.cpu().numpy().view(np.uint16), r[::-1])
+
+
+def test_split_kv_partials_and_lse_combine(kv, orc):
+    """One sequence of T tokens split over two pools (the per-GPU shards of a
+    long context): shard 0 holds [0, A), shard 1 holds [A, T) and appends the
+    new token at global position T.  Partials merged by attn_combine_lse must
+    equal the unsplit attention."""
+    need_gpu()
+    rng = np.random.default_rng(8)
+    T, A, dtype = 2500, 1111, 1
+    full_k = np.zeros((T + 1, 256), np.uint16)
+    full_v = np.zeros((T + 1, 256), np.uint16)
+    full_k[:T] = orc.encode(rng.standard_normal((T, 256)).astype(np.float32), dtype)
+    full_v[:T] = orc.encode(rng.standard_normal((T, 256)).astype(np.float32), dtype)
+    shards = []
+    for lo, hi in ((0, A), (A, T)):
+        P = kv.Pool(0, 1, 200, dtype=dtype, max_seqs=1, max_seq_len=T + 16)
+        s = P.seq_alloc()
+        P.reserve(s, hi - lo + 1)
+        P.import_rows(0, s, 0, to_dev(full_k[lo:hi]), to_dev(full_v[lo:hi]))
+        P.set_cur_pos(s, hi - lo)
+        shards.append((P, s))
+    q = rng.standard_normal((1, 1536)).astype(np.float32)
+    k = rng.standard_normal((1, 256)).astype(np.float32)
+    v = rng.standard_normal((1, 256)).astype(np.float32)
+    ms = torch.empty((2, 12), device="cuda")
+    ls = torch.empty((2, 12), device="cuda")
+    os_ = torch.empty((2, 12, HD), device="cuda")
+    for g, (P, s) in enumerate(shards):
+        P.plan([s], rope_pos=[T], append=[g == 1])
+        P.decode_layer(0, to_dev(q), to_dev(k), to_dev(v), os_[g].view(1, -1), ms[g], ls[g])
+        P.commit()
+    out = torch.empty((12, HD), device="cuda")
+    kv.combine_lse(ms, ls, os_, out)
+    ref, _, _ = orc.layer_step(q, k, v, full_k, full_v, T, dtype=dtype)
+    assert rel_err(out.cpu().numpy(), ref[0]) <= TOL
+    P1, s1 = shards[1]
+    kd, vd = P1.gather(0, s1)
+    assert np.array_equal(kd.cpu().numpy().view(np.uint16), full_k[A:T + 1])
+    assert np.array_equal(vd.cpu().numpy().view(np.uint16), full_v[A:T + 1])
+    assert shards[0][0].cur_pos(shards[0][1]) == A  # no append on shard 0
+
+
+def test_partial_state_of_empty_shard(kv):
+    need_gpu()
+    P = kv.Pool(0, 1, 4, max_seqs=1, max_seq_len=64)
+    s = P.seq_alloc()
+    P.plan([s], rope_pos=[5], append=[0])
+    z = torch.zeros((1, 256), device="cuda")
+    out = torch.full((1, 1536), 7.0, device="cuda")
+    m = torch.zeros(12, device="cuda")
+    l = torch.ones(12, device="cuda")
+    P.decode_layer(0, torch.zeros((1, 1536), device="cuda"), z, z, out, m, l)
+    P.commit()
+    assert torch.all(out == 0) and torch.all(l == 0) and torch.all(torch.isinf(m))
+
+
+def test_reset_zeroes_pool(kv, orc):
+    need_gpu()
+    H = Harness(kv, orc, [40], 0, seed=2)
+    H.step()
+    H.P.reset()
+    s = H.P.seq_alloc()
+    H.P.reserve(s, 48)
+    H.P.set_cur_pos(s, 48)
+    kd, vd = H.P.gather(0, s)
+    assert int(kd.abs().sum()) == 0 and int(vd.abs().sum()) == 0

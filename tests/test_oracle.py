@@ -1,0 +1,128 @@
+"""Pin the checker: the C restatement (oracle/kvattn_oracle.c) must reproduce
+the reference's golden vectors bit-for-bit, and match the reference's own
+compiled functions live where they were built."""
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+import pytest
+
+NH, NKV, HD, THETA = 12, 2, 128, 1e6
+KVD = NKV * HD
+
+
+def bits(a):
+    return np.ascontiguousarray(a).view(np.uint32 if a.dtype == np.float32 else np.uint16)
+
+
+def test_conversions_match_golden(orc, golden):
+    x = golden["conv_x"]
+    assert np.array_equal(orc.encode(x, orc.F16), golden["conv_f16"])
+    assert np.array_equal(orc.encode(x, orc.BF16), golden["conv_bf16"])
+    codes = np.arange(65536, dtype=np.uint16)
+    for dt, key in ((orc.F16, "dec_f16_sha256"), (orc.BF16, "dec_bf16_sha256")):
+        dig = hashlib.sha256(orc.decode(codes, dt).view(np.uint32).tobytes()).digest()
+        assert dig == golden[key].tobytes()
+
+
+def test_f16_encoder_truncates_and_flushes(orc):
+    # half.h:24-32: no rounding, exp<=0 -> signed zero, exp>=31 (and NaN) -> inf.
+    f = orc.lib().orc_f32_to_f16
+    assert f(1.0009765625) == 0x3C01          # exactly representable
+    assert f(1.00146484375) == 0x3C01         # 1.5 ulp: truncated, not rounded up
+    assert f(6.0e-05) == 0x0000               # below 2^-14: flushed
+    assert f(-6.0e-05) == 0x8000
+    assert f(65536.0) == 0x7C00
+    assert f(float("nan")) == 0x7C00
+    assert f(float("-inf")) == 0xFC00
+
+
+def test_rope_matches_golden(orc, golden):
+    L = orc.lib()
+    for i, p in enumerate(golden["rope_pos"]):
+        q = golden["rope_q"][i].copy()
+        k = golden["rope_k"][i].copy()
+        L.orc_rope(q, k, NH, NKV, HD, int(p), THETA)
+        assert np.array_equal(bits(q), bits(golden["rope_q_out"][i]))
+        assert np.array_equal(bits(k), bits(golden["rope_k_out"][i]))
+
+
+@pytest.mark.parametrize("ci", range(8))
+def test_layer_step_matches_golden(orc, golden, ci):
+    g = {k[len(f"step{ci}_"):]: v for k, v in golden.items() if k.startswith(f"step{ci}_")}
+    pos = int(g["pos"])
+    seq = g["q"].shape[0]
+    kc = np.zeros((pos + seq, KVD), np.uint16)
+    vc = np.zeros((pos + seq, KVD), np.uint16)
+    kc[:pos], vc[:pos] = g["k0"], g["v0"]
+    out, q_rot, _ = orc.layer_step(g["q"], g["k"], g["v"], kc, vc, pos)
+    assert np.array_equal(kc[pos:], g["k_app"])
+    assert np.array_equal(vc[pos:], g["v_app"])
+    assert np.array_equal(bits(q_rot), bits(g["q_rot"]))
+    assert np.array_equal(bits(out), bits(g["out"]))
+
+
+def test_rope_table_matches_rotation(orc):
+    # The table the product builds uses the same three libm calls; spot-check
+    # that rotating with table values equals the oracle's rotation.
+    c, s = orc.rope_table(THETA, HD, 4090, 8)
+    rng = np.random.default_rng(3)
+    k = rng.standard_normal(KVD).astype(np.float32)
+    for j in range(8):
+        q = np.zeros(NH * HD, np.float32)
+        kk = k.copy()
+        orc.lib().orc_rope(q, kk, NH, NKV, HD, 4090 + j, THETA)
+        a, b = k[:64], k[64:128]
+        with np.errstate(all="ignore"):
+            r0 = (a * c[j]).astype(np.float32) - (b * s[j]).astype(np.float32)
+            r1 = (a * s[j]).astype(np.float32) + (b * c[j]).astype(np.float32)
+        assert np.array_equal(bits(r0.astype(np.float32)), bits(kk[:64]))
+        assert np.array_equal(bits(r1.astype(np.float32)), bits(kk[64:128]))
+
+
+def test_lse_combine_equals_unsplit_attention(orc):
+    rng = np.random.default_rng(5)
+    T = 70
+    kc = orc.encode(rng.standard_normal((T, KVD)).astype(np.float32))
+    vc = orc.encode(rng.standard_normal((T, KVD)).astype(np.float32))
+    q = rng.standard_normal((1, NH * HD)).astype(np.float32)
+    full = orc.attention(q, kc, vc, 1, T, NH, NKV, HD, T - 1)
+    # Split positions [0,30) and [30,70): compute each part's (m, l, o) by hand.
+    ms, ls, os_ = [], [], []
+    kd = orc.decode(kc)
+    vd = orc.decode(vc)
+    for lo, hi in ((0, 30), (30, 70)):
+        m = np.empty(NH, np.float32)
+        l = np.empty(NH, np.float32)
+        o = np.empty((NH, HD), np.float32)
+        for h in range(NH):
+            kh = h // (NH // NKV)
+            sc = (kd[lo:hi, kh * HD:(kh + 1) * HD] @ q[0, h * HD:(h + 1) * HD]) / np.sqrt(HD)
+            m[h] = sc.max()
+            w = np.exp(sc - m[h])
+            l[h] = w.sum()
+            o[h] = (w @ vd[lo:hi, kh * HD:(kh + 1) * HD]) / l[h]
+        ms.append(m)
+        ls.append(l)
+        os_.append(o)
+    comb = orc.lse_combine(np.stack(ms), np.stack(ls), np.stack(os_))
+    np.testing.assert_allclose(comb.reshape(-1), full.reshape(-1), rtol=0, atol=1e-5)
+
+
+@pytest.mark.skipif("not __import__('oracle').have_ref()")
+def test_restatement_equals_reference_live(orc):
+    rng = np.random.default_rng(99)
+    for pos, seq in ((0, 1), (63, 1), (64, 3), (200, 1)):
+        cap = pos + seq
+        kc = orc.encode(rng.standard_normal((cap, KVD)).astype(np.float32))
+        vc = orc.encode(rng.standard_normal((cap, KVD)).astype(np.float32))
+        kc2, vc2 = kc.copy(), vc.copy()
+        q = rng.standard_normal((seq, NH * HD)).astype(np.float32)
+        k = (rng.standard_normal((seq, KVD)) * 30000).astype(np.float32)  # some encode to inf
+        v = rng.standard_normal((seq, KVD)).astype(np.float32)
+        o1, q1, _ = orc.layer_step(q, k, v, kc, vc, pos)
+        o2, q2, _ = orc.ref_layer_step(q, k, v, kc2, vc2, pos)
+        assert np.array_equal(kc, kc2) and np.array_equal(vc, vc2)
+        assert np.array_equal(bits(q1), bits(q2))
+        assert np.array_equal(bits(o1), bits(o2))
