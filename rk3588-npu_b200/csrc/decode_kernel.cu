@@ -10,8 +10,8 @@
 // persistent grid walks the item list with a static stride.  Per CTA:
 //   warp 4     producer: one lane issues 1-D bulk async copies (TMA engine,
 //              no multicast) of each 16-token block's K and V tiles (4 KiB
-//              each, contiguous in HBM) into a 6-stage shared-memory ring;
-//   warps 0-3  consumers: stage k goes to warp k % 4.  Per block: S^T =
+//              each, contiguous in HBM) into an 8-stage shared-memory ring;
+//   warps 0-3  consumers: stage k goes to warp k % 4 (two stages per warp).  Per block: S^T =
 //              K * Q^T with mma.sync m16n8k16 (16 tokens x 8 query heads,
 //              fp32 q split into hi + lo 16-bit halves so the products keep
 //              ~22 bits), online softmax in fp32 (base 2), P^T transposed in
@@ -36,8 +36,15 @@ namespace kvattn {
 
 namespace {
 
-constexpr int kStages = 6;
+constexpr int kStages = 8;
 constexpr int kConsumerWarps = 4;
+// Stage k of the ring is consumed by warp k % kConsumerWarps.  With kStages a
+// multiple of kConsumerWarps every stage belongs to ONE warp, which consumes
+// its rounds in order; so no waiter is ever more than one phase ahead of a
+// barrier, the condition under which a parity wait is unambiguous.  (With 6
+// stages and 4 warps a warp could wait on round r+1 of a stage whose round r,
+// owned by another warp, had not landed; the parity test then passed early.)
+static_assert(kStages % kConsumerWarps == 0, "each ring stage must belong to one consumer warp");
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kStageBytes = 2 * kTileBytes;  // K tile then V tile
 constexpr int kMergeStride = 132;            // floats per (warp, head) row, padded
@@ -52,11 +59,56 @@ struct Smem {
     uint64_t empty[kStages];
     int last_flag;
     int failed;
+    int prod_issued;                  // stages issued by the producer (progress record)
+    int cons_done[kConsumerWarps];    // stages released by each consumer warp
 };
 
-__device__ __forceinline__ void flag_timeout(const PoolView& pv, Smem& sm) {
-    atomicExch(pv.status, 7 /* KV_ERR_TIMEOUT */);
+// Record the first device-side error: status[0] = code, [1] = item, [2] = detail.
+__device__ __forceinline__ void report(const PoolView& pv, int code, int item, int detail) {
+    if (atomicCAS(pv.status, 0, code) == 0) {
+        pv.status[1] = item;
+        pv.status[2] = detail;
+    }
+}
+
+// A bounded wait gave up: record where (status[3..16]) for the host to read.
+__device__ __forceinline__ void flag_timeout(const PoolView& pv, Smem& sm, int item, int role,
+                                             uint32_t k) {
+    if (atomicCAS(pv.status, 0, 7 /* KV_ERR_TIMEOUT */) == 0) {
+        const int s = k % kStages;
+        const uint64_t f = *reinterpret_cast<volatile uint64_t*>(&sm.full[s]);
+        const uint64_t e = *reinterpret_cast<volatile uint64_t*>(&sm.empty[s]);
+        pv.status[1] = item;
+        pv.status[2] = role;
+        pv.status[3] = blockIdx.x;
+        pv.status[4] = threadIdx.x >> 5;
+        pv.status[5] = (int)k;
+        pv.status[6] = (int)(k / kStages);
+        pv.status[7] = (int)(uint32_t)f;
+        pv.status[8] = (int)(uint32_t)(f >> 32);
+        pv.status[9] = (int)(uint32_t)e;
+        pv.status[10] = (int)(uint32_t)(e >> 32);
+        pv.status[11] = *reinterpret_cast<volatile int*>(&sm.prod_issued);
+        for (int w = 0; w < kConsumerWarps; ++w)
+            pv.status[12 + w] = *reinterpret_cast<volatile int*>(&sm.cons_done[w]);
+    }
     sm.failed = 1;
+}
+
+// Every index an item leads to, checked before any access; producer and
+// consumers evaluate the same predicate on the same plan data, so a bad item
+// is skipped by all of them alike (and reported once, by the producer).
+__device__ __forceinline__ int item_check(const PoolView& pv, const PlanHeader& hdr,
+                                          const WorkItem& wi, const DecodeSlot& sl) {
+    if (wi.head < 0 || wi.head >= pv.kv_heads) return 1;
+    if (sl.seq < 0 || sl.seq >= pv.max_seqs) return 2;
+    if (sl.kv_len < 0 || sl.kv_len > pv.max_blocks_per_seq * kBlockTokens) return 3;
+    if (sl.rope_pos < 0 || sl.rope_pos >= pv.max_seq_len) return 4;
+    if (sl.append && (sl.kv_len < 1 || sl.new_block < 0 || sl.new_block >= pv.num_blocks)) return 5;
+    if (wi.chunk < 0 || wi.chunk >= sl.nchunks) return 6;
+    if (sl.item_base < 0 || sl.item_base + (wi.head + 1) * sl.nchunks > pv.max_items) return 7;
+    if (hdr.chunk_tokens <= 0 || (hdr.chunk_tokens % kBlockTokens) != 0) return 8;
+    return 0;
 }
 
 // Rotated, pre-scaled q of query head (head*group + g) as mma B fragments.
@@ -207,7 +259,7 @@ __device__ __forceinline__ void consume_block(uint32_t sK, uint32_t sV, int vali
 }  // namespace
 
 template <int DT>
-__global__ void __launch_bounds__(kThreads, 3)
+__global__ void __launch_bounds__(kThreads, 2)
     decode_kernel(PoolView pv, PlanView plan, int layer, const float* __restrict__ q,
                   const float* __restrict__ k_new, const float* __restrict__ v_new,
                   float* __restrict__ out, float* __restrict__ m_out, float* __restrict__ l_out) {
@@ -221,6 +273,11 @@ __global__ void __launch_bounds__(kThreads, 3)
     // entry it patches: the block of the new token is taken from the slot.
     for (int i = blockIdx.x * kThreads + tid; i < hdr.npatch; i += gridDim.x * kThreads) {
         const TablePatch p = plan.patches[i];
+        if (p.seq < 0 || p.seq >= pv.max_seqs || p.idx < 0 || p.idx >= pv.max_blocks_per_seq ||
+            p.block < 0 || p.block >= pv.num_blocks) {
+            report(pv, 5, -1, i);
+            continue;
+        }
         pv.table[(size_t)p.seq * pv.max_blocks_per_seq + p.idx] = p.block;
     }
 
@@ -230,6 +287,8 @@ __global__ void __launch_bounds__(kThreads, 3)
             mbar_init(&sm.empty[s], 1);
         }
         sm.failed = 0;
+        sm.prod_issued = 0;
+        for (int w = 0; w < kConsumerWarps; ++w) sm.cons_done[w] = 0;
         fence_mbar_init();
     }
     __syncthreads();
@@ -243,7 +302,15 @@ __global__ void __launch_bounds__(kThreads, 3)
         int ok = 1;
         for (int it = blockIdx.x; it < hdr.nitems && ok; it += gridDim.x) {
             const WorkItem wi = plan.items[it];
+            if (wi.slot < 0 || wi.slot >= hdr.nslots) {
+                if (lane == 0) report(pv, 5, it, 100);
+                continue;
+            }
             const DecodeSlot sl = plan.slots[wi.slot];
+            if (const int bad = item_check(pv, hdr, wi, sl)) {
+                if (lane == 0) report(pv, 5, it, bad);
+                continue;
+            }
             const int t0 = wi.chunk * CH;
             const int t1 = min(sl.kv_len, t0 + CH);
             const int nb = t1 > t0 ? (t1 - t0 + kBlockTokens - 1) / kBlockTokens : 0;
@@ -259,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 3)
                         const uint32_t k = seqno + b0 + bb;
                         const int s = k % kStages;
                         if (!mbar_wait_bounded(&sm.empty[s], ((k / kStages) & 1) ^ 1, kWaitLimit)) {
-                            flag_timeout(pv, sm);
+                            flag_timeout(pv, sm, it, 0, k);
                             ok = 0;
                         } else {
                             const int j = t0 / kBlockTokens + b0 + bb;
@@ -269,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 3)
                             if (newblk && valid == 1) {
                                 mbar_arrive(&sm.full[s]);  // only the new token: nothing to load
                             } else if ((unsigned)blk >= (unsigned)pv.num_blocks) {
-                                atomicExch(pv.status, 5 /* KV_ERR_RANGE */);  // never read outside the pool
+                                report(pv, 5 /* KV_ERR_RANGE */, it, 200 + j);  // never read outside the pool
                                 mbar_arrive(&sm.full[s]);
                             } else {
                                 const size_t off = (size_t)layer * pv.layer_bytes +
@@ -279,6 +346,7 @@ __global__ void __launch_bounds__(kThreads, 3)
                                 bulk_g2s_hint(sm.stage[s] + kTileBytes, pv.v + off, kTileBytes,
                                               &sm.full[s], policy);
                             }
+                            *reinterpret_cast<volatile int*>(&sm.prod_issued) = (int)k + 1;
                         }
                     }
                     ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -287,12 +355,15 @@ __global__ void __launch_bounds__(kThreads, 3)
             }
             seqno += nb;
         }
-        // Drain: copies into this CTA's shared memory must land before exit.
-        if (lane == 0 && ok) {
-            const uint32_t first = seqno > (uint32_t)kStages ? seqno - kStages : 0u;
-            for (uint32_t k = first; k < seqno; ++k)
+        // Drain, on every path (also after a timeout): copies into this CTA's
+        // shared memory must land before it exits.  At most the last kStages
+        // issued stages can still be in flight.
+        if (lane == 0) {
+            const uint32_t issued = (uint32_t)*reinterpret_cast<volatile int*>(&sm.prod_issued);
+            const uint32_t first = issued > (uint32_t)kStages ? issued - kStages : 0u;
+            for (uint32_t k = first; k < issued; ++k)
                 if (!mbar_wait_bounded(&sm.full[k % kStages], (k / kStages) & 1, kWaitLimit)) {
-                    atomicExch(pv.status, 7);
+                    flag_timeout(pv, sm, -2, 2, k);
                     break;
                 }
         }
@@ -306,7 +377,9 @@ __global__ void __launch_bounds__(kThreads, 3)
     bool dead = false;
     for (int it = blockIdx.x; it < hdr.nitems; it += gridDim.x) {
         const WorkItem wi = plan.items[it];
+        if (wi.slot < 0 || wi.slot >= hdr.nslots) continue;
         const DecodeSlot sl = plan.slots[wi.slot];
+        if (item_check(pv, hdr, wi, sl)) continue;
         const int t0 = wi.chunk * CH;
         const int t1 = min(sl.kv_len, t0 + CH);
         const int nb = t1 > t0 ? (t1 - t0 + kBlockTokens - 1) / kBlockTokens : 0;
@@ -324,7 +397,7 @@ __global__ void __launch_bounds__(kThreads, 3)
             if ((int)(k % kConsumerWarps) != warp) continue;
             const int s = k % kStages;
             if (!dead && !mbar_wait_bounded(&sm.full[s], (k / kStages) & 1, kWaitLimit)) {
-                flag_timeout(pv, sm);
+                flag_timeout(pv, sm, it, 1, k);
                 dead = true;
             }
             if (dead) continue;
@@ -351,7 +424,10 @@ __global__ void __launch_bounds__(kThreads, 3)
             if (valid < kBlockTokens || (sl.append && j == last_blk))
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.empty[s]);
+            if (lane == 0) {
+                mbar_arrive(&sm.empty[s]);
+                *reinterpret_cast<volatile int*>(&sm.cons_done[warp]) = (int)k + 1;
+            }
         }
         seqno += nb;
 

@@ -359,8 +359,8 @@ int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, in
     KV_CUDA_B(cudaMalloc((void**)&p->d_counters, (size_t)max_seqs * num_kv_heads * sizeof(int)));
     KV_CUDA_B(cudaMemset(p->d_counters, 0, (size_t)max_seqs * num_kv_heads * sizeof(int)));
     KV_CUDA_B(cudaMalloc((void**)&p->d_partials, (size_t)p->max_items * kPartialFloats * sizeof(float)));
-    KV_CUDA_B(cudaMalloc((void**)&p->d_status, sizeof(int)));
-    KV_CUDA_B(cudaMemset(p->d_status, 0, sizeof(int)));
+    KV_CUDA_B(cudaMalloc((void**)&p->d_status, 32 * sizeof(int)));
+    KV_CUDA_B(cudaMemset(p->d_status, 0, 32 * sizeof(int)));
     KV_CUDA_B(cudaEventCreateWithFlags(&p->pending_evt, cudaEventDisableTiming));
 
     p->plan_bytes = sizeof(PlanHeader) + (size_t)max_seqs * sizeof(DecodeSlot) +
@@ -386,6 +386,8 @@ int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, in
     pv.group = num_q_heads / num_kv_heads;
     pv.max_blocks_per_seq = p->mbps;
     pv.max_seq_len = max_seq_len;
+    pv.max_seqs = max_seqs;
+    pv.max_items = (int)p->max_items;
     pv.dtype = dtype;
     pv.layer_bytes = layer_bytes;
     *out = p;
@@ -832,11 +834,18 @@ int kvp_device_status(kvp_pool* p, void* stream, int* status) {
     if (!p || !status) return fail(KV_ERR_INVAL, "NULL argument");
     if (int rc = require_device(p)) return rc;
     DeviceGuard dg(p->device);
-    int v = 0;
-    KV_CUDA(cudaMemcpyAsync(&v, p->d_status, sizeof(int), cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+    int v[32] = {0};
+    KV_CUDA(cudaMemcpyAsync(v, p->d_status, sizeof v, cudaMemcpyDeviceToHost, (cudaStream_t)stream));
     KV_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
-    KV_CUDA(cudaMemsetAsync(p->d_status, 0, sizeof(int), (cudaStream_t)stream));
-    *status = v;
+    KV_CUDA(cudaMemsetAsync(p->d_status, 0, sizeof v, (cudaStream_t)stream));
+    *status = v[0];
+    if (v[0] == KV_ERR_TIMEOUT)
+        fail(v[0], "device wait gave up: item %d role %d block %d warp %d stage %d round %d "
+                   "full=%08x%08x empty=%08x%08x issued=%d released=%d,%d,%d,%d",
+             v[1], v[2], v[3], v[4], v[5], v[6], v[8], v[7], v[10], v[9], v[11], v[12], v[13],
+             v[14], v[15]);
+    else if (v[0] != 0)
+        fail(v[0], "device status %d at item %d (detail %d)", v[0], v[1], v[2]);
     return KV_OK;
 }
 

@@ -64,13 +64,15 @@ struct PoolView {
     int* table;              // [max_seqs][max_blocks_per_seq]
     int* counters;           // [max_seqs][kv_heads] arrival counters (kept at 0 between launches)
     float* partials;         // [max_items][kPartialFloats]
-    int* status;             // device status word
+    int* status;             // device status: [0] code, [1] item index, [2] detail
     int num_blocks;
     int kv_heads;
     int q_heads;
     int group;               // q_heads / kv_heads
     int max_blocks_per_seq;
     int max_seq_len;
+    int max_seqs;
+    int max_items;
     int dtype;               // 0 f16, 1 bf16
     size_t layer_bytes;      // num_blocks * kv_heads * kTileBytes
 };
