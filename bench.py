@@ -46,6 +46,8 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--settle", type=float, default=1.0,
+                    help="seconds of untimed load before the timed steps (clock samples)")
     return ap.parse_args()
 
 
@@ -237,7 +239,7 @@ def run_ours(args, rank, world, local):
         step(i)
     # Keep the GPU loaded ~1 s so the clock samples reflect load; lengths
     # are put back afterwards so the timed steps see the stated contexts.
-    t_end = time.time() + 1.0
+    t_end = time.time() + args.settle
     while time.time() < t_end:
         for i in range(8):
             flush.zero_()
