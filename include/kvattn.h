@@ -185,11 +185,14 @@ int attn_combine_lse(int G, int rows, int dim, const float* m, const float* l, c
  * bounded wait gave up.  Synchronises `stream`; clears the word. */
 int kvp_device_status(kvp_pool* pool, void* stream, int* status);
 
-/* The active plan's work list (host copy): item count, chunk size in tokens,
- * number of new block-table entries, and up to `cap` items' (slot, kv head,
- * chunk).  Any output pointer may be NULL. */
-int kvp_plan_info(const kvp_pool* pool, int* nitems, int* chunk_tokens, int* npatch, int* item_slot,
-                  int* item_head, int* item_chunk, int cap);
+/* The active plan's work list (host copy): number of pieces, CTAs the
+ * layer calls launch, new block-table entries, and up to `cap` pieces'
+ * (slot, kv head, first block, end block).  Any output pointer may be NULL. */
+int kvp_plan_info(const kvp_pool* pool, int* nitems, int* grid, int* npatch, int* item_slot,
+                  int* item_head, int* item_b0, int* item_b1, int cap);
+/* cta_start[0..grid] of the active plan: CTA g runs pieces
+ * [cta_start[g], cta_start[g+1]). */
+int kvp_plan_cta_start(const kvp_pool* pool, int* cta_start, int cap);
 
 /* Number of SMs and of resident decode CTAs per SM used for grid sizing. */
 int kvp_launch_info(const kvp_pool* pool, int* num_sms, int* ctas_per_sm);

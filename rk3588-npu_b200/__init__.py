@@ -56,7 +56,8 @@ _SIGS = {
     "attn_decode_commit": [_vp],
     "attn_combine_lse": [C.c_int, C.c_int, C.c_int, _vp, _vp, _vp, _vp, _vp],
     "kvp_device_status": [_vp, _vp, _ip],
-    "kvp_plan_info": [_vp, _ip, _ip, _ip, _ip, _ip, _ip, C.c_int],
+    "kvp_plan_info": [_vp, _ip, _ip, _ip, _ip, _ip, _ip, _ip, C.c_int],
+    "kvp_plan_cta_start": [_vp, _ip, C.c_int],
     "kvp_launch_info": [_vp, _ip, _ip],
 }
 _RESTYPE = {"kv_last_error": C.c_char_p, "kv_status_str": C.c_char_p, "kv_version": C.c_char_p}
@@ -245,13 +246,18 @@ class Pool:
         self._plan_n = len(ids)
 
     def plan_info(self):
-        n, ch, npatch = C.c_int(), C.c_int(), C.c_int()
-        call("kvp_plan_info", self.h, C.byref(n), C.byref(ch), C.byref(npatch), None, None, None, 0)
-        cap = n.value
-        a, b, c = (C.c_int * max(1, cap))(), (C.c_int * max(1, cap))(), (C.c_int * max(1, cap))()
-        call("kvp_plan_info", self.h, C.byref(n), C.byref(ch), C.byref(npatch), a, b, c, cap)
-        return {"nitems": n.value, "chunk_tokens": ch.value, "npatch": npatch.value,
-                "items": list(zip(a[:cap], b[:cap], c[:cap]))}
+        """The active plan: pieces (slot, kv head, b0, b1), CTA ranges, patches."""
+        n, grid, npatch = C.c_int(), C.c_int(), C.c_int()
+        call("kvp_plan_info", self.h, C.byref(n), C.byref(grid), C.byref(npatch), None, None, None,
+             None, 0)
+        cap = max(1, n.value)
+        a, b, c, d = [(C.c_int * cap)() for _ in range(4)]
+        call("kvp_plan_info", self.h, C.byref(n), C.byref(grid), C.byref(npatch), a, b, c, d, cap)
+        cs = (C.c_int * (grid.value + 1))()
+        call("kvp_plan_cta_start", self.h, cs, grid.value + 1)
+        return {"nitems": n.value, "grid": grid.value, "npatch": npatch.value,
+                "items": list(zip(a[:n.value], b[:n.value], c[:n.value], d[:n.value])),
+                "cta_start": list(cs)}
 
     def decode_layer(self, layer, q, k_new, v_new, out, m=None, l=None, stream=None) -> None:
         n = self._plan_n

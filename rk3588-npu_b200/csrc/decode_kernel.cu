@@ -6,20 +6,24 @@
 // the append loop (qwen2_model.cpp:188-200) and op_attention with op_softmax
 // (op_attention.cpp:9-56, op_softmax.cpp:6-16).
 //
-// Work unit: (batch slot, KV head, chunk of `chunk_tokens` positions).  A
-// persistent grid walks the item list with a static stride.  Per CTA:
-//   warp 4     producer: one lane issues 1-D bulk async copies (TMA engine,
-//              no multicast) of each 16-token block's K and V tiles (4 KiB
-//              each, contiguous in HBM) into an 8-stage shared-memory ring;
-//   warps 0-3  consumers: stage k goes to warp k % 4 (two stages per warp).  Per block: S^T =
-//              K * Q^T with mma.sync m16n8k16 (16 tokens x 8 query heads,
-//              fp32 q split into hi + lo 16-bit halves so the products keep
-//              ~22 bits), online softmax in fp32 (base 2), P^T transposed in
-//              registers with movmatrix, O^T += V^T * P^T (P split hi + lo).
-// At the end of an item the four warps' states are merged in shared memory.
-// A sequence split into several chunks writes per-chunk partial (m, l, o);
-// the CTA that finishes last for a (slot, head) -- found with a per-(slot,
-// head) arrival counter, no waiting -- merges them and writes the output.
+// Work: the host planner flattens the step into segments (one per batch slot
+// and KV head, all its 16-token blocks) and gives every CTA one contiguous,
+// equal run of that flat block sequence; a segment crossing a CTA boundary
+// becomes several pieces.  Per CTA:
+//   warp 4     producer: the warp fetches block-table entries one 32-block
+//              batch ahead; one lane issues 1-D bulk async copies (TMA engine,
+//              no multicast) of each block's K and V tiles (4 KiB each,
+//              contiguous in HBM) into an 8-stage shared-memory ring;
+//   warps 0-3  consumers: flat block f goes to warp f % 4 (two ring stages
+//              per warp).  Per block: S^T = K * Q^T with mma.sync m16n8k16
+//              (16 tokens x 8 query heads, fp32 q split into hi + lo 16-bit
+//              halves so the products keep ~22 bits), online softmax in fp32
+//              (base 2), P^T transposed in registers with movmatrix,
+//              O^T += V^T * P^T (P split hi + lo).
+// At the end of a piece the four warps' states are merged in shared memory.
+// A segment cut into pieces writes per-piece partial (m, l, o); the CTA that
+// finishes last for a segment -- found with a per-segment arrival counter,
+// no waiting -- merges them and writes the output.
 //
 // The new token: the consumer that owns the block holding position kv_len-1
 // rotates k (non-fused fp32, cos/sin from the host-built table), encodes k
@@ -55,8 +59,11 @@ struct Smem {
     float merge_o[kConsumerWarps][kMaxGroup][kMergeStride];
     float merge_m[kConsumerWarps][kMaxGroup];
     float merge_l[kConsumerWarps][kMaxGroup];
+    WorkItem items[kMaxCtaItems];     // this CTA's pieces
+    int cum[kMaxCtaItems + 1];        // flat block offset of each piece
     uint64_t full[kStages];
     uint64_t empty[kStages];
+    int nitems;
     int last_flag;
     int failed;
     int prod_issued;                  // stages issued by the producer (progress record)
@@ -95,19 +102,19 @@ __device__ __forceinline__ void flag_timeout(const PoolView& pv, Smem& sm, int i
     sm.failed = 1;
 }
 
-// Every index an item leads to, checked before any access; producer and
-// consumers evaluate the same predicate on the same plan data, so a bad item
-// is skipped by all of them alike (and reported once, by the producer).
+// Every index a piece leads to, checked before any access (the plan comes
+// from the host planner; a bad one is reported and its piece skipped).
 __device__ __forceinline__ int item_check(const PoolView& pv, const PlanHeader& hdr,
-                                          const WorkItem& wi, const DecodeSlot& sl) {
-    if (wi.head < 0 || wi.head >= pv.kv_heads) return 1;
-    if (sl.seq < 0 || sl.seq >= pv.max_seqs) return 2;
-    if (sl.kv_len < 0 || sl.kv_len > pv.max_blocks_per_seq * kBlockTokens) return 3;
-    if (sl.rope_pos < 0 || sl.rope_pos >= pv.max_seq_len) return 4;
-    if (sl.append && (sl.kv_len < 1 || sl.new_block < 0 || sl.new_block >= pv.num_blocks)) return 5;
-    if (wi.chunk < 0 || wi.chunk >= sl.nchunks) return 6;
-    if (sl.item_base < 0 || sl.item_base + (wi.head + 1) * sl.nchunks > pv.max_items) return 7;
-    if (hdr.chunk_tokens <= 0 || (hdr.chunk_tokens % kBlockTokens) != 0) return 8;
+                                          const WorkItem& wi, const PlanView& plan) {
+    if (wi.slot < 0 || wi.slot >= hdr.nslots) return 1;
+    if (wi.head < 0 || wi.head >= pv.kv_heads) return 2;
+    const DecodeSlot sl = plan.slots[wi.slot];
+    if (sl.seq < 0 || sl.seq >= pv.max_seqs) return 3;
+    if (sl.kv_len < 0 || sl.kv_len > pv.max_blocks_per_seq * kBlockTokens) return 4;
+    if (sl.rope_pos < 0 || sl.rope_pos >= pv.max_seq_len) return 5;
+    if (sl.append && (sl.kv_len < 1 || sl.new_block < 0 || sl.new_block >= pv.num_blocks)) return 6;
+    if (wi.b0 < 0 || wi.b1 < wi.b0 || wi.b1 > (sl.kv_len + kBlockTokens - 1) / kBlockTokens) return 7;
+    if (wi.seg_first < 0 || wi.seg_n < 1 || wi.seg_first + wi.seg_n > pv.max_items) return 8;
     return 0;
 }
 
@@ -267,10 +274,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const PlanHeader hdr = *plan.hdr;
-    const int CH = hdr.chunk_tokens;
 
     // Block-table entries allocated by this step's plan.  No launch reads an
-    // entry it patches: the block of the new token is taken from the slot.
+    // entry it patches: the block of a new token is taken from its slot.
     for (int i = blockIdx.x * kThreads + tid; i < hdr.npatch; i += gridDim.x * kThreads) {
         const TablePatch p = plan.patches[i];
         if (p.seq < 0 || p.seq >= pv.max_seqs || p.idx < 0 || p.idx >= pv.max_blocks_per_seq ||
@@ -281,6 +287,14 @@ __global__ void __launch_bounds__(kThreads, 2)
         pv.table[(size_t)p.seq * pv.max_blocks_per_seq + p.idx] = p.block;
     }
 
+    // This CTA's pieces into shared memory.
+    const int i0 = plan.cta_start[blockIdx.x];
+    int n = plan.cta_start[blockIdx.x + 1] - i0;
+    if (n < 0 || n > kMaxCtaItems || i0 < 0 || i0 + n > hdr.nitems) {
+        if (tid == 0) report(pv, 5, i0, 300);
+        n = 0;
+    }
+    for (int j = tid; j < n; j += kThreads) sm.items[j] = plan.items[i0 + j];
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&sm.full[s], 1);
@@ -292,68 +306,77 @@ __global__ void __launch_bounds__(kThreads, 2)
         fence_mbar_init();
     }
     __syncthreads();
+    if (tid == 0) {
+        sm.cum[0] = 0;
+        for (int j = 0; j < n; ++j) {
+            WorkItem& w = sm.items[j];
+            if (const int bad = item_check(pv, hdr, w, plan)) {
+                report(pv, 5, i0 + j, bad);
+                w.b0 = w.b1 = 0;
+                w.seg_n = 0;  // skipped by everyone
+            }
+            sm.cum[j + 1] = sm.cum[j] + (w.b1 - w.b0);
+        }
+        sm.nitems = n;
+    }
+    __syncthreads();
+    const int total = sm.cum[n];
 
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------ producer
-        // The whole warp fetches up to 32 block-table entries at once (one
-        // per lane); lane 0 waits on the ring and issues the copies.
+        // Flat walk over this CTA's blocks.  Lanes fetch the block ids of the
+        // next 32 flat positions one batch ahead of lane 0's issue loop.
         const uint64_t policy = policy_evict_first();
-        uint32_t seqno = 0;
-        int ok = 1;
-        for (int it = blockIdx.x; it < hdr.nitems && ok; it += gridDim.x) {
-            const WorkItem wi = plan.items[it];
-            if (wi.slot < 0 || wi.slot >= hdr.nslots) {
-                if (lane == 0) report(pv, 5, it, 100);
-                continue;
-            }
-            const DecodeSlot sl = plan.slots[wi.slot];
-            if (const int bad = item_check(pv, hdr, wi, sl)) {
-                if (lane == 0) report(pv, 5, it, bad);
-                continue;
-            }
-            const int t0 = wi.chunk * CH;
-            const int t1 = min(sl.kv_len, t0 + CH);
-            const int nb = t1 > t0 ? (t1 - t0 + kBlockTokens - 1) / kBlockTokens : 0;
-            const int last_blk = (sl.kv_len - 1) / kBlockTokens;
-            const int* trow = pv.table + (size_t)sl.seq * pv.max_blocks_per_seq;
-            for (int b0 = 0; b0 < nb && ok; b0 += 32) {
-                const int jl = t0 / kBlockTokens + b0 + lane;
-                const int myblk = (b0 + lane < nb) ? trow[jl] : 0;
-                const int cnt = min(32, nb - b0);
-                for (int bb = 0; bb < cnt; ++bb) {
-                    const int tblk = __shfl_sync(0xffffffffu, myblk, bb);
-                    if (lane == 0) {
-                        const uint32_t k = seqno + b0 + bb;
-                        const int s = k % kStages;
-                        if (!mbar_wait_bounded(&sm.empty[s], ((k / kStages) & 1) ^ 1, kWaitLimit)) {
-                            flag_timeout(pv, sm, it, 0, k);
-                            ok = 0;
+        auto fetch = [&](int f) -> int {
+            if (f >= total) return 0;
+            int j = 0;
+            while (sm.cum[j + 1] <= f) ++j;
+            const WorkItem& w = sm.items[j];
+            const DecodeSlot sl = plan.slots[w.slot];
+            const int idx = w.b0 + (f - sm.cum[j]);
+            if (sl.append && idx == (sl.kv_len - 1) / kBlockTokens) return sl.new_block;
+            return pv.table[(size_t)sl.seq * pv.max_blocks_per_seq + idx];
+        };
+        int cur = fetch(lane), nxt = fetch(32 + lane);
+        int ok = 1, j = 0;
+        for (int f0 = 0; f0 < total && ok; f0 += 32) {
+            const int cnt = min(32, total - f0);
+            for (int bb = 0; bb < cnt; ++bb) {
+                const int f = f0 + bb;
+                const int blk = __shfl_sync(0xffffffffu, cur, bb);
+                while (sm.cum[j + 1] <= f) ++j;
+                if (lane == 0) {
+                    const int s = f % kStages;
+                    if (!mbar_wait_bounded(&sm.empty[s], ((f / kStages) & 1) ^ 1, kWaitLimit)) {
+                        flag_timeout(pv, sm, i0 + j, 0, (uint32_t)f);
+                        ok = 0;
+                    } else {
+                        const WorkItem& w = sm.items[j];
+                        const DecodeSlot sl = plan.slots[w.slot];
+                        const int idx = w.b0 + (f - sm.cum[j]);
+                        const int valid = min(kBlockTokens, sl.kv_len - idx * kBlockTokens);
+                        const bool newblk = sl.append && idx == (sl.kv_len - 1) / kBlockTokens;
+                        if (newblk && valid == 1) {
+                            mbar_arrive(&sm.full[s]);  // only the new token: nothing to load
+                        } else if ((unsigned)blk >= (unsigned)pv.num_blocks) {
+                            report(pv, 5, i0 + j, 200 + idx);  // never read outside the pool
+                            mbar_arrive(&sm.full[s]);
                         } else {
-                            const int j = t0 / kBlockTokens + b0 + bb;
-                            const int valid = min(kBlockTokens, sl.kv_len - j * kBlockTokens);
-                            const bool newblk = sl.append && j == last_blk;
-                            const int blk = newblk ? sl.new_block : tblk;
-                            if (newblk && valid == 1) {
-                                mbar_arrive(&sm.full[s]);  // only the new token: nothing to load
-                            } else if ((unsigned)blk >= (unsigned)pv.num_blocks) {
-                                report(pv, 5 /* KV_ERR_RANGE */, it, 200 + j);  // never read outside the pool
-                                mbar_arrive(&sm.full[s]);
-                            } else {
-                                const size_t off = (size_t)layer * pv.layer_bytes +
-                                                   ((size_t)blk * pv.kv_heads + wi.head) * kTileBytes;
-                                mbar_arrive_expect_tx(&sm.full[s], kStageBytes);
-                                bulk_g2s_hint(sm.stage[s], pv.k + off, kTileBytes, &sm.full[s], policy);
-                                bulk_g2s_hint(sm.stage[s] + kTileBytes, pv.v + off, kTileBytes,
-                                              &sm.full[s], policy);
-                            }
-                            *reinterpret_cast<volatile int*>(&sm.prod_issued) = (int)k + 1;
+                            const size_t off = (size_t)layer * pv.layer_bytes +
+                                               ((size_t)blk * pv.kv_heads + w.head) * kTileBytes;
+                            mbar_arrive_expect_tx(&sm.full[s], kStageBytes);
+                            bulk_g2s_hint(sm.stage[s], pv.k + off, kTileBytes, &sm.full[s], policy);
+                            bulk_g2s_hint(sm.stage[s] + kTileBytes, pv.v + off, kTileBytes, &sm.full[s],
+                                          policy);
                         }
+                        *reinterpret_cast<volatile int*>(&sm.prod_issued) = f + 1;
                     }
-                    ok = __shfl_sync(0xffffffffu, ok, 0);
-                    if (!ok) break;
                 }
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
             }
-            seqno += nb;
+            cur = nxt;
+            nxt = fetch(f0 + 64 + lane);
         }
         // Drain, on every path (also after a timeout): copies into this CTA's
         // shared memory must land before it exits.  At most the last kStages
@@ -373,16 +396,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ---------------------------------------------------------- consumers
     const float qscale = 0.08838834764831845f * 1.4426950408889634f;  // 1/sqrt(128) * log2(e)
     const int g = lane >> 2, c = lane & 3;
-    uint32_t seqno = 0;
     bool dead = false;
-    for (int it = blockIdx.x; it < hdr.nitems; it += gridDim.x) {
-        const WorkItem wi = plan.items[it];
-        if (wi.slot < 0 || wi.slot >= hdr.nslots) continue;
+    for (int j = 0; j < n; ++j) {
+        const WorkItem wi = sm.items[j];
+        if (wi.seg_n == 0) continue;  // rejected by the checks above
         const DecodeSlot sl = plan.slots[wi.slot];
-        if (item_check(pv, hdr, wi, sl)) continue;
-        const int t0 = wi.chunk * CH;
-        const int t1 = min(sl.kv_len, t0 + CH);
-        const int nb = t1 > t0 ? (t1 - t0 + kBlockTokens - 1) / kBlockTokens : 0;
+        const int nb = wi.b1 - wi.b0;
+        const int fbase = sm.cum[j];
         const int last_blk = (sl.kv_len - 1) / kBlockTokens;
 
         uint32_t qh[8][2], ql[8][2];
@@ -392,22 +412,23 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
 
-        for (int b = 0; b < nb; ++b) {
-            const uint32_t k = seqno + b;
-            if ((int)(k % kConsumerWarps) != warp) continue;
+        for (int b = (warp - fbase % kConsumerWarps + kConsumerWarps) % kConsumerWarps; b < nb;
+             b += kConsumerWarps) {
+            const uint32_t k = (uint32_t)(fbase + b);  // k % kConsumerWarps == warp
             const int s = k % kStages;
             if (!dead && !mbar_wait_bounded(&sm.full[s], (k / kStages) & 1, kWaitLimit)) {
-                flag_timeout(pv, sm, it, 1, k);
+                flag_timeout(pv, sm, i0 + j, 1, k);
                 dead = true;
             }
             if (dead) continue;
             uint8_t* sK = sm.stage[s];
             uint8_t* sV = sm.stage[s] + kTileBytes;
-            const int j = t0 / kBlockTokens + b;
-            const int valid = min(kBlockTokens, sl.kv_len - j * kBlockTokens);
-            if (sl.append && j == last_blk)
-                write_new_row<DT>(pv, layer, sl.new_block, wi.head, valid - 1, k_new, v_new,
-                                  wi.slot, sl.rope_pos, sK, sV, lane);
+            const int idx = wi.b0 + b;
+            const int valid = min(kBlockTokens, sl.kv_len - idx * kBlockTokens);
+            const bool newblk = sl.append && idx == last_blk;
+            if (newblk)
+                write_new_row<DT>(pv, layer, sl.new_block, wi.head, valid - 1, k_new, v_new, wi.slot,
+                                  sl.rope_pos, sK, sV, lane);
             if (valid < kBlockTokens) {
                 // Rows past the end may hold anything (stale tiles, inf):
                 // zero them in V so masked weights (exactly 0) stay 0.
@@ -421,23 +442,21 @@ __global__ void __launch_bounds__(kThreads, 2)
             consume_block<DT>(smem_u32(sK), smem_u32(sV), valid, lane, qh, ql, m2, lsum, o);
             // Generic-proxy writes to the tile must be ordered before the
             // next bulk copy (async proxy) overwrites it.
-            if (valid < kBlockTokens || (sl.append && j == last_blk))
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            if (valid < kBlockTokens || newblk) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&sm.empty[s]);
                 *reinterpret_cast<volatile int*>(&sm.cons_done[warp]) = (int)k + 1;
             }
         }
-        seqno += nb;
 
-        // ---- merge the four warps' states for this item ----
+        // ---- merge the four warps' states for this piece ----
 #pragma unroll
         for (int off = 4; off < 32; off <<= 1) {
             lsum[0] += __shfl_xor_sync(0xffffffffu, lsum[0], off);
             lsum[1] += __shfl_xor_sync(0xffffffffu, lsum[1], off);
         }
-        named_bar_sync(1, kConsumerWarps * 32);  // previous item's readers are done
+        named_bar_sync(1, kConsumerWarps * 32);  // previous piece's readers are done
         if (g == 0) {
             sm.merge_m[warp][2 * c] = m2[0];
             sm.merge_m[warp][2 * c + 1] = m2[1];
@@ -455,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
         const int d = tid;  // 0..127: one output dim per thread
         const int qrow = wi.slot * pv.q_heads + wi.head * pv.group;
-        float* part = pv.partials + (size_t)(sl.item_base + wi.head * sl.nchunks + wi.chunk) * kPartialFloats;
+        float* part = pv.partials + (size_t)(i0 + j) * kPartialFloats;
         for (int h = 0; h < pv.group; ++h) {
             float M = -INFINITY;
 #pragma unroll
@@ -469,7 +488,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                 O += sm.merge_o[w][h][d] * e;
             }
             const float on = L > 0.f ? O / L : 0.f;
-            if (sl.nchunks == 1) {
+            if (wi.seg_n == 1) {
                 out[(size_t)(qrow + h) * kHeadDim + d] = on;
                 if (m_out != nullptr && d == 0) {
                     m_out[qrow + h] = M * 0.6931471805599453f;
@@ -483,30 +502,38 @@ __global__ void __launch_bounds__(kThreads, 2)
                 }
             }
         }
-        if (sl.nchunks == 1) continue;
+        if (wi.seg_n == 1) continue;
 
-        // ---- split sequence: the last CTA to finish a (slot, head) merges ----
-        __threadfence();
+        // ---- split segment: the last CTA to finish one merges its pieces.
+        // Release: the barrier orders every thread's partial stores before
+        // thread 0's fence + counter increment; acquire: thread 0 fences
+        // after seeing the final count, and the barrier passes it on.
         named_bar_sync(1, kConsumerWarps * 32);
         if (tid == 0) {
+            __threadfence();
             const int prev = atomicAdd(&pv.counters[wi.slot * pv.kv_heads + wi.head], 1);
-            sm.last_flag = (prev == sl.nchunks - 1);
+            const int last = (prev == wi.seg_n - 1);
+            if (last) __threadfence();
+            sm.last_flag = last;
         }
         named_bar_sync(1, kConsumerWarps * 32);
         if (!sm.last_flag) continue;
-        __threadfence();
-        const float* p0 = pv.partials + (size_t)(sl.item_base + wi.head * sl.nchunks) * kPartialFloats;
+        const float* p0 = pv.partials + (size_t)wi.seg_first * kPartialFloats;
         for (int h = 0; h < pv.group; ++h) {
             float M = -INFINITY;
-            for (int ci = 0; ci < sl.nchunks; ++ci)
-                M = fmaxf(M, __ldcg(p0 + (size_t)ci * kPartialFloats + h));
+            for (int ci = 0; ci < wi.seg_n; ++ci)
+                if (__ldcg(p0 + (size_t)ci * kPartialFloats + kMaxGroup + h) > 0.f)
+                    M = fmaxf(M, __ldcg(p0 + (size_t)ci * kPartialFloats + h));
             const float Mu = (M == -INFINITY) ? 0.f : M;
             float L = 0.f, O = 0.f;
-            for (int ci = 0; ci < sl.nchunks; ++ci) {
+            for (int ci = 0; ci < wi.seg_n; ++ci) {
                 const float* pc = p0 + (size_t)ci * kPartialFloats;
-                const float w = __ldcg(pc + kMaxGroup + h) * fast_exp2(__ldcg(pc + h) - Mu);
-                L += w;
-                O += w * __ldcg(pc + 2 * kMaxGroup + h * kHeadDim + d);
+                const float lc = __ldcg(pc + kMaxGroup + h);
+                if (lc > 0.f) {
+                    const float w = lc * fast_exp2(__ldcg(pc + h) - Mu);
+                    L += w;
+                    O += w * __ldcg(pc + 2 * kMaxGroup + h * kHeadDim + d);
+                }
             }
             out[(size_t)(qrow + h) * kHeadDim + d] = L > 0.f ? O / L : 0.f;
             if (m_out != nullptr && d == 0) {
@@ -517,6 +544,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (tid == 0) pv.counters[wi.slot * pv.kv_heads + wi.head] = 0;
     }
 }
+
 
 cudaError_t decode_occupancy(int* ctas_per_sm) {
     const int smem = (int)sizeof(Smem) + 1024;

@@ -109,14 +109,16 @@ struct kvp_pool {
     size_t plan_bytes = 0;
     uint8_t* h_plan[kRing] = {};
     uint8_t* d_plan[kRing] = {};
-    cudaEvent_t plan_evt[kRing] = {};
+    cudaEvent_t copy_done[kRing] = {};  // upload of ring slot r finished (copy stream)
+    cudaEvent_t slot_free[kRing] = {};  // last launch reading ring slot r finished
+    cudaStream_t copy_stream = nullptr; // non-blocking: plan uploads overlap running kernels
     int ring_next = 0;
 
     // active plan
     bool plan_active = false;
     bool plan_patched = false;
     int plan_slot_ring = 0;
-    int plan_nslots = 0, plan_nitems = 0, plan_npatch = 0;
+    int plan_nslots = 0, plan_nitems = 0, plan_npatch = 0, plan_grid = 0;
     PlanView plan_view{};
     std::vector<int> plan_seqs;
     std::vector<int> plan_append;
@@ -206,7 +208,10 @@ int sync_table(kvp_pool* p, cudaStream_t st) {
     int rc = flush_pending(p, st);
     if (rc != KV_OK) return rc;
     if (p->plan_active && !p->plan_patched && p->plan_npatch > 0) {
+        const int r = p->plan_slot_ring;
+        KV_CUDA(cudaStreamWaitEvent(st, p->copy_done[r], 0));
         KV_CUDA(launch_patch(p->pv, p->plan_view.patches, p->plan_npatch, st));
+        KV_CUDA(cudaEventRecord(p->slot_free[r], st));
         p->plan_patched = true;
     }
     return KV_OK;
@@ -223,6 +228,23 @@ int check_seq(const kvp_pool* p, int seq) {
     return KV_OK;
 }
 
+// Byte layout of one packed plan: header, slots, items, patches, cta_start.
+struct PlanLayout {
+    size_t slots, items, patches, cta, bytes;
+};
+
+size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
+
+PlanLayout plan_layout(int nslots, long nitems, int npatch, long grid) {
+    PlanLayout L;
+    L.slots = align16(sizeof(PlanHeader));
+    L.items = align16(L.slots + (size_t)nslots * sizeof(DecodeSlot));
+    L.patches = align16(L.items + (size_t)nitems * sizeof(WorkItem));
+    L.cta = align16(L.patches + (size_t)npatch * sizeof(TablePatch));
+    L.bytes = align16(L.cta + (size_t)(grid + 1) * sizeof(int));
+    return L;
+}
+
 void free_device(kvp_pool* p) {
     cudaFree(p->d_k);
     cudaFree(p->d_v);
@@ -237,8 +259,10 @@ void free_device(kvp_pool* p) {
     for (int i = 0; i < kRing; ++i) {
         cudaFree(p->d_plan[i]);
         cudaFreeHost(p->h_plan[i]);
-        if (p->plan_evt[i]) cudaEventDestroy(p->plan_evt[i]);
+        if (p->copy_done[i]) cudaEventDestroy(p->copy_done[i]);
+        if (p->slot_free[i]) cudaEventDestroy(p->slot_free[i]);
     }
+    if (p->copy_stream) cudaStreamDestroy(p->copy_stream);
 }
 
 }  // namespace
@@ -305,7 +329,9 @@ int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, in
     p->theta = rope_theta;
     p->seqs.resize(max_seqs);
     p->reset_free_list();
-    p->max_items = (long)num_kv_heads * ((long)num_blocks / 8 + 1 + max_seqs);
+    // Pieces: every CTA boundary splits at most one segment, so items <=
+    // segments + CTAs; CTAs <= grid + segments / kMaxCtaItems (item cap).
+    p->max_items = 2L * max_seqs * num_kv_heads + 148L * 4 + 64;
 
     auto bail = [&](cudaError_t e, const char* what) {
         free_device(p);
@@ -322,8 +348,7 @@ int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, in
         // Bookkeeping only: plans are built for a nominal 148-SM part and kept on the host.
         p->num_sms = 148;
         p->occupancy = 3;
-        p->plan_bytes = sizeof(PlanHeader) + (size_t)max_seqs * sizeof(DecodeSlot) +
-                        (size_t)p->max_items * sizeof(WorkItem) + (size_t)max_seqs * sizeof(TablePatch);
+        p->plan_bytes = plan_layout(max_seqs, p->max_items, max_seqs, p->max_items).bytes;
         p->h_plan[0] = (uint8_t*)malloc(p->plan_bytes);
         if (!p->h_plan[0]) {
             delete p;
@@ -342,6 +367,7 @@ int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, in
     KV_CUDA_B(cudaDeviceGetAttribute(&p->num_sms, cudaDevAttrMultiProcessorCount, device));
     KV_CUDA_B(decode_occupancy(&p->occupancy));
     if (p->occupancy < 1) p->occupancy = 1;
+    p->max_items = 2L * max_seqs * num_kv_heads + (long)p->num_sms * p->occupancy + 64;
 
     const size_t layer_bytes = (size_t)num_blocks * num_kv_heads * kTileBytes;
     KV_CUDA_B(cudaMalloc(&p->d_k, layer_bytes * num_layers));
@@ -363,12 +389,13 @@ int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, in
     KV_CUDA_B(cudaMemset(p->d_status, 0, 32 * sizeof(int)));
     KV_CUDA_B(cudaEventCreateWithFlags(&p->pending_evt, cudaEventDisableTiming));
 
-    p->plan_bytes = sizeof(PlanHeader) + (size_t)max_seqs * sizeof(DecodeSlot) +
-                    (size_t)p->max_items * sizeof(WorkItem) + (size_t)max_seqs * sizeof(TablePatch);
+    p->plan_bytes = plan_layout(max_seqs, p->max_items, max_seqs, p->max_items).bytes;
+    KV_CUDA_B(cudaStreamCreateWithFlags(&p->copy_stream, cudaStreamNonBlocking));
     for (int i = 0; i < kRing; ++i) {
         KV_CUDA_B(cudaMallocHost((void**)&p->h_plan[i], p->plan_bytes));
         KV_CUDA_B(cudaMalloc((void**)&p->d_plan[i], p->plan_bytes));
-        KV_CUDA_B(cudaEventCreateWithFlags(&p->plan_evt[i], cudaEventDisableTiming));
+        KV_CUDA_B(cudaEventCreateWithFlags(&p->copy_done[i], cudaEventDisableTiming));
+        KV_CUDA_B(cudaEventCreateWithFlags(&p->slot_free[i], cudaEventDisableTiming));
     }
 #undef KV_CUDA_B
 
@@ -645,8 +672,6 @@ int attn_decode_plan_ex(kvp_pool* p, int nseq, const int* seq_ids, const int* ro
     // ---- validate everything before changing anything ----
     std::vector<char> seen(p->max_seqs, 0);
     int new_blocks = 0;
-    long total = 0;
-    int maxlen = 0;
     for (int i = 0; i < nseq; ++i) {
         const int sid = seq_ids[i];
         int rc = check_seq(p, sid);
@@ -662,44 +687,38 @@ int attn_decode_plan_ex(kvp_pool* p, int nseq, const int* seq_ids, const int* ro
         if (kv_len > p->mbps * kBlockTokens || kv_len > p->max_seq_len)
             return fail(KV_ERR_RANGE, "sequence %d would reach %d tokens > max_seq_len %d", sid, kv_len, p->max_seq_len);
         if (app && s.len / kBlockTokens >= (int)s.blocks.size()) ++new_blocks;
-        total += kv_len;
-        maxlen = std::max(maxlen, kv_len);
     }
     if (new_blocks > (int)p->free_.size())
         return fail(KV_ERR_OOM, "decode step needs %d new blocks, %zu free", new_blocks, p->free_.size());
 
     // A plan that never reached a layer call still owes its table entries.
     if (p->plan_active && !p->plan_patched && p->plan_npatch > 0 && !p->host_only) {
+        const int r0 = p->plan_slot_ring;
+        KV_CUDA(cudaStreamWaitEvent(st, p->copy_done[r0], 0));
         KV_CUDA(launch_patch(p->pv, p->plan_view.patches, p->plan_npatch, st));
+        KV_CUDA(cudaEventRecord(p->slot_free[r0], st));
         p->plan_patched = true;
     }
     int rc = flush_pending(p, st);
     if (rc) return rc;
 
-    // ---- chunk size: ~2 items per resident CTA, >= 128 tokens, <= 256 chunks per row ----
-    const long grid = (long)p->num_sms * p->occupancy;
-    long ch = (total * p->kv_heads + 2 * grid - 1) / (2 * grid);
-    ch = std::max(ch, (long)(maxlen + 255) / 256);
-    ch = std::max<long>(ch, 128);
-    ch = (ch + kBlockTokens - 1) / kBlockTokens * kBlockTokens;
-
-    // ---- build into the next ring buffer ----
+    // ---- slots (and the blocks new tokens start) ----
     const int r = p->host_only ? 0 : p->ring_next;
     p->ring_next = (r + 1) % kRing;
-    if (!p->host_only) KV_CUDA(cudaEventSynchronize(p->plan_evt[r]));  // its previous upload has read it
+    if (!p->host_only) KV_CUDA(cudaEventSynchronize(p->copy_done[r]));  // host buffer reusable
     uint8_t* h = p->h_plan[r];
-    PlanHeader* hdr = (PlanHeader*)h;
-    DecodeSlot* slots = (DecodeSlot*)(h + sizeof(PlanHeader));
-    WorkItem* items = (WorkItem*)(slots + p->max_seqs);
-    TablePatch* patches = (TablePatch*)(items + p->max_items);
-    int nitems = 0, npatch = 0;
+    std::vector<DecodeSlot> slots(nseq);
+    std::vector<TablePatch> patches;
     p->plan_seqs.assign(seq_ids, seq_ids + nseq);
     p->plan_append.resize(nseq);
+    long total_blocks = 0;
+    int nsegments = 0;
     for (int i = 0; i < nseq; ++i) {
         const int sid = seq_ids[i];
         Seq& s = p->seqs[sid];
         const int app = append ? (append[i] != 0) : 1;
         DecodeSlot& sl = slots[i];
+        sl = DecodeSlot{};
         sl.seq = sid;
         sl.kv_len = s.len + app;
         sl.rope_pos = rope_pos ? rope_pos[i] : s.len;
@@ -710,67 +729,128 @@ int attn_decode_plan_ex(kvp_pool* p, int nseq, const int* seq_ids, const int* ro
             if (idx >= (int)s.blocks.size()) {
                 const int b = p->pop_block();
                 s.blocks.push_back(b);
-                patches[npatch++] = TablePatch{sid, idx, b, 0};
+                patches.push_back(TablePatch{sid, idx, b, 0});
             }
             sl.new_block = s.blocks[idx];
         }
-        sl.nchunks = std::max(1, (int)((sl.kv_len + ch - 1) / ch));
-        sl.item_base = nitems;
-        sl.pad = 0;
-        if (nitems + (long)p->kv_heads * sl.nchunks > p->max_items)
-            return fail(KV_ERR_STATE, "work list overflow (%ld items)", p->max_items);
-        for (int hd = 0; hd < p->kv_heads; ++hd)
-            for (int c = 0; c < sl.nchunks; ++c) items[nitems++] = WorkItem{i, hd, c, 0};
         p->plan_append[i] = app;
+        total_blocks += (long)p->kv_heads * ((sl.kv_len + kBlockTokens - 1) / kBlockTokens);
+        nsegments += p->kv_heads;
     }
+
+    // ---- pieces: each CTA gets one contiguous, equal run of the flattened
+    // (slot, kv head, block) sequence; a segment crossing a CTA boundary is
+    // cut into pieces whose partial results are merged on the device ----
+    const long gmax = std::max(1L, (long)p->num_sms * p->occupancy);
+    const long G = std::min(gmax, std::max(1L, (total_blocks + 7) / 8));
+    const long per = std::max(1L, (total_blocks + G - 1) / G);
+    std::vector<WorkItem> items;
+    std::vector<int> cta_start(1, 0);
+    long fill = 0;
+    int cta_items = 0;
+    auto close_cta = [&]() {
+        cta_start.push_back((int)items.size());
+        fill = 0;
+        cta_items = 0;
+    };
+    for (int i = 0; i < nseq; ++i) {
+        const int nblk = (slots[i].kv_len + kBlockTokens - 1) / kBlockTokens;
+        for (int hd = 0; hd < p->kv_heads; ++hd) {
+            const int seg_first = (int)items.size();
+            if (nblk == 0) {  // nothing to attend: one empty piece still writes the (zero) result
+                if (cta_items == kMaxCtaItems) close_cta();
+                items.push_back(WorkItem{i, hd, 0, 0, seg_first, 1, {0, 0}});
+                ++cta_items;
+                continue;
+            }
+            int b = 0;
+            while (b < nblk) {
+                if (fill >= per || cta_items == kMaxCtaItems) close_cta();
+                const int take = (int)std::min<long>(nblk - b, per - fill);
+                items.push_back(WorkItem{i, hd, b, b + take, seg_first, 0, {0, 0}});
+                b += take;
+                fill += take;
+                ++cta_items;
+            }
+            const int seg_n = (int)items.size() - seg_first;
+            for (int x = seg_first; x < (int)items.size(); ++x) items[x].seg_n = seg_n;
+        }
+    }
+    close_cta();
+    const int grid = (int)cta_start.size() - 1;
+    if ((long)items.size() > p->max_items || grid > p->max_items)
+        return fail(KV_ERR_STATE, "work list overflow (%zu items, %d CTAs)", items.size(), grid);
+
+    // ---- pack and upload once, on the copy stream ----
+    const PlanLayout L = plan_layout(nseq, (long)items.size(), (int)patches.size(), grid);
+    PlanHeader* hdr = (PlanHeader*)h;
     hdr->nslots = nseq;
-    hdr->nitems = nitems;
-    hdr->npatch = npatch;
-    hdr->chunk_tokens = (int)ch;
-    // Upload the used parts (header + slots contiguous; items; patches).
-    const size_t off_items = (uint8_t*)items - h, off_patch = (uint8_t*)patches - h;
+    hdr->nitems = (int)items.size();
+    hdr->npatch = (int)patches.size();
+    hdr->grid = grid;
+    hdr->off_slots = (int)L.slots;
+    hdr->off_items = (int)L.items;
+    hdr->off_patches = (int)L.patches;
+    hdr->off_cta = (int)L.cta;
+    memcpy(h + L.slots, slots.data(), slots.size() * sizeof(DecodeSlot));
+    memcpy(h + L.items, items.data(), items.size() * sizeof(WorkItem));
+    if (!patches.empty()) memcpy(h + L.patches, patches.data(), patches.size() * sizeof(TablePatch));
+    memcpy(h + L.cta, cta_start.data(), cta_start.size() * sizeof(int));
+
     p->plan_active = true;
-    p->plan_patched = (npatch == 0);
+    p->plan_patched = patches.empty();
     p->plan_slot_ring = r;
     p->plan_nslots = nseq;
-    p->plan_nitems = nitems;
-    p->plan_npatch = npatch;
+    p->plan_nitems = (int)items.size();
+    p->plan_npatch = (int)patches.size();
+    p->plan_grid = grid;
+    const uint8_t* base = p->host_only ? h : p->d_plan[r];
+    p->plan_view.hdr = (const PlanHeader*)base;
+    p->plan_view.slots = (const DecodeSlot*)(base + L.slots);
+    p->plan_view.items = (const WorkItem*)(base + L.items);
+    p->plan_view.patches = (const TablePatch*)(base + L.patches);
+    p->plan_view.cta_start = (const int*)(base + L.cta);
+    p->plan_stream = st;
     if (p->host_only) {
-        p->plan_view = PlanView{(const PlanHeader*)h, slots, items, patches};
         p->plan_patched = true;
         return KV_OK;
     }
-    uint8_t* d = p->d_plan[r];
-    KV_CUDA(cudaMemcpyAsync(d, h, sizeof(PlanHeader) + nseq * sizeof(DecodeSlot), cudaMemcpyHostToDevice, st));
-    KV_CUDA(cudaMemcpyAsync(d + off_items, h + off_items, nitems * sizeof(WorkItem), cudaMemcpyHostToDevice, st));
-    if (npatch)
-        KV_CUDA(cudaMemcpyAsync(d + off_patch, h + off_patch, npatch * sizeof(TablePatch), cudaMemcpyHostToDevice, st));
-    KV_CUDA(cudaEventRecord(p->plan_evt[r], st));
-
-    p->plan_view.hdr = (const PlanHeader*)d;
-    p->plan_view.slots = (const DecodeSlot*)(d + sizeof(PlanHeader));
-    p->plan_view.items = (const WorkItem*)(d + off_items);
-    p->plan_view.patches = (const TablePatch*)(d + off_patch);
-    p->plan_stream = st;
+    // The previous launches that read ring slot r must be done before the
+    // copy overwrites it; the copy itself overlaps whatever runs now.
+    KV_CUDA(cudaStreamWaitEvent(p->copy_stream, p->slot_free[r], 0));
+    KV_CUDA(cudaMemcpyAsync(p->d_plan[r], h, L.bytes, cudaMemcpyHostToDevice, p->copy_stream));
+    KV_CUDA(cudaEventRecord(p->copy_done[r], p->copy_stream));
     return KV_OK;
 }
 
-int kvp_plan_info(const kvp_pool* p, int* nitems, int* chunk_tokens, int* npatch, int* item_slot,
-                  int* item_head, int* item_chunk, int cap) {
+int kvp_plan_info(const kvp_pool* p, int* nitems, int* grid, int* npatch, int* item_slot,
+                  int* item_head, int* item_b0, int* item_b1, int cap) {
     if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
     if (!p->plan_active) return fail(KV_ERR_STATE, "no active decode plan");
     const uint8_t* h = p->h_plan[p->plan_slot_ring];
     const PlanHeader* hdr = (const PlanHeader*)h;
-    const WorkItem* items = (const WorkItem*)(h + sizeof(PlanHeader) + (size_t)p->max_seqs * sizeof(DecodeSlot));
+    const WorkItem* items = (const WorkItem*)(h + hdr->off_items);
     if (nitems) *nitems = hdr->nitems;
-    if (chunk_tokens) *chunk_tokens = hdr->chunk_tokens;
+    if (grid) *grid = hdr->grid;
     if (npatch) *npatch = hdr->npatch;
     const int n = std::min(cap, hdr->nitems);
     for (int i = 0; i < n; ++i) {
         if (item_slot) item_slot[i] = items[i].slot;
         if (item_head) item_head[i] = items[i].head;
-        if (item_chunk) item_chunk[i] = items[i].chunk;
+        if (item_b0) item_b0[i] = items[i].b0;
+        if (item_b1) item_b1[i] = items[i].b1;
     }
+    return KV_OK;
+}
+
+int kvp_plan_cta_start(const kvp_pool* p, int* cta_start, int cap) {
+    if (!p || !cta_start) return fail(KV_ERR_INVAL, "NULL argument");
+    if (!p->plan_active) return fail(KV_ERR_STATE, "no active decode plan");
+    const uint8_t* h = p->h_plan[p->plan_slot_ring];
+    const PlanHeader* hdr = (const PlanHeader*)h;
+    const int* cs = (const int*)(h + hdr->off_cta);
+    const int n = std::min(cap, hdr->grid + 1);
+    for (int i = 0; i < n; ++i) cta_start[i] = cs[i];
     return KV_OK;
 }
 
@@ -789,9 +869,12 @@ static int decode_call(kvp_pool* p, int layer, const float* q, const float* k_ne
     if (((uintptr_t)q | (uintptr_t)k_new | (uintptr_t)v_new) & 7)
         return fail(KV_ERR_INVAL, "q/k_new/v_new must be 8-byte aligned");
     DeviceGuard dg(p->device);
-    const long grid = std::min<long>(p->plan_nitems, (long)p->num_sms * p->occupancy);
+    cudaStream_t st = (cudaStream_t)stream;
+    const int r = p->plan_slot_ring;
+    KV_CUDA(cudaStreamWaitEvent(st, p->copy_done[r], 0));
     KV_CUDA(launch_decode(p->pv, p->plan_view, p->plan_nitems, p->plan_npatch, layer, q, k_new, v_new, out,
-                          m, l, (int)grid, (cudaStream_t)stream));
+                          m, l, p->plan_grid, st));
+    KV_CUDA(cudaEventRecord(p->slot_free[r], st));
     p->plan_patched = true;
     return KV_OK;
 }
@@ -813,13 +896,17 @@ int attn_decode_commit(kvp_pool* p) {
     if (!p->plan_active) return fail(KV_ERR_STATE, "no active decode plan");
     if (!p->plan_patched && p->plan_npatch > 0 && !p->host_only) {
         DeviceGuard dg(p->device);
+        const int r = p->plan_slot_ring;
+        KV_CUDA(cudaStreamWaitEvent(p->plan_stream, p->copy_done[r], 0));
         KV_CUDA(launch_patch(p->pv, p->plan_view.patches, p->plan_npatch, p->plan_stream));
+        KV_CUDA(cudaEventRecord(p->slot_free[r], p->plan_stream));
     }
     for (size_t i = 0; i < p->plan_seqs.size(); ++i)
         if (p->plan_append[i]) p->seqs[p->plan_seqs[i]].len += 1;
     p->plan_active = false;
     return KV_OK;
 }
+
 
 int attn_combine_lse(int G, int rows, int dim, const float* m, const float* l, const float* o,
                      float* out, void* stream) {

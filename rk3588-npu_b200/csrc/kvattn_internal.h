@@ -11,6 +11,7 @@ constexpr int kBlockTokens = 16;       // token rows per block
 constexpr int kTileBytes = kBlockTokens * kHeadDim * 2;  // one (block, kv head) tile: 4 KiB
 constexpr int kMaxGroup = 8;           // query heads per KV head handled by one MMA tile
 constexpr int kPartialFloats = kMaxGroup * (kHeadDim + 2);  // m[8], l[8], o[8][128]
+constexpr int kMaxCtaItems = 64;       // pieces per decode CTA (the planner never assigns more)
 
 // Byte offset of element (token t, dim d) inside a 4 KiB tile.
 // Two 2 KiB halves (dims 0-63, 64-127); each half has 16 rows of 128 bytes;
@@ -28,17 +29,21 @@ struct DecodeSlot {
     int rope_pos;   // position used to rotate q and the new k
     int append;     // 1: write the new token at local slot kv_len-1
     int new_block;  // block id holding slot kv_len-1 when append (else -1)
-    int nchunks;    // split-KV chunks per KV head (>= 1)
-    int item_base;  // index of this slot's first work item
-    int pad;
+    int pad[3];
 };
 
-// One unit of work: (slot, kv head, chunk).
+// One piece of work: blocks [b0, b1) of the segment (slot, kv head).  A
+// segment (all blocks of one sequence for one KV head) is cut into seg_n
+// consecutive pieces starting at item index seg_first; each CTA owns a
+// contiguous run of items, so pieces of one segment sit in different CTAs.
 struct WorkItem {
     int slot;
     int head;
-    int chunk;
-    int pad;
+    int b0;
+    int b1;
+    int seg_first;
+    int seg_n;
+    int pad[2];
 };
 
 // A block-table entry to write before use: table[seq][idx] = block.
@@ -49,11 +54,17 @@ struct TablePatch {
     int pad;
 };
 
+// The plan is one contiguous upload: header, slots, items, patches, and
+// cta_start[grid + 1] (CTA g owns items [cta_start[g], cta_start[g+1])).
 struct PlanHeader {
     int nslots;
     int nitems;
     int npatch;
-    int chunk_tokens;  // multiple of kBlockTokens
+    int grid;
+    int off_slots;    // byte offsets from the header
+    int off_items;
+    int off_patches;
+    int off_cta;
 };
 
 // Device view of the pool handed to kernels by value.
@@ -83,6 +94,7 @@ struct PlanView {
     const DecodeSlot* slots;
     const WorkItem* items;
     const TablePatch* patches;
+    const int* cta_start;
 };
 
 // ---- launchers (kernels.cu) ----

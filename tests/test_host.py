@@ -197,7 +197,7 @@ def test_lengths_and_errors(kv):
     assert e.value.status == kv.KV_ERR_STATE
 
 
-def test_plan_work_list_covers_every_chunk_once(kv):
+def test_plan_pieces_cover_every_block_once_balanced(kv):
     P = host_pool(kv, nblocks=40000, max_seqs=40, max_seq_len=32768)
     rng = np.random.default_rng(1)
     lens = [0, 1, 15, 16, 17, 255, 256, 257] + list(rng.integers(1, 20000, 24))
@@ -209,22 +209,36 @@ def test_plan_work_list_covers_every_chunk_once(kv):
         ids.append(s)
     P.plan(ids)
     info = P.plan_info()
-    ch = info["chunk_tokens"]
-    assert ch % 16 == 0 and ch >= 128
-    want = set()
-    for i, L in enumerate(lens):
-        kvl = L + 1
-        assert -(-kvl // ch) <= 256
-        for h in range(2):
-            for c in range(max(1, -(-kvl // ch))):
-                want.add((i, h, c))
-    got = info["items"]
-    assert len(got) == len(set(got)) == info["nitems"]
-    assert set(got) == want
+    items, cs = info["items"], info["cta_start"]
+    assert cs[0] == 0 and cs[-1] == info["nitems"] == len(items)
+    assert info["grid"] == len(cs) - 1 <= 148 * 3
+    # every (slot, head, block) covered exactly once, pieces in flat order
+    cover = {}
+    for (slot, h, b0, b1) in items:
+        assert 0 <= b0 <= b1
+        for b in range(b0, b1):
+            assert (slot, h, b) not in cover
+            cover[(slot, h, b)] = 1
+    want = {(i, h, b) for i, L in enumerate(lens) for h in range(2) for b in range(-(-(L + 1) // 16))}
+    assert set(cover) == want
+    # balance: CTA loads differ by at most one piece boundary's worth
+    loads = [sum(b1 - b0 for (_, _, b0, b1) in items[cs[g]:cs[g + 1]]) for g in range(info["grid"])]
+    total = len(want)
+    per = -(-total // info["grid"])
+    assert max(loads) <= per and min(loads[:-1]) == per
+    assert all(cs[g + 1] - cs[g] <= 64 for g in range(info["grid"]))
     # one new block for every sequence whose next position starts a block
     assert info["npatch"] == sum(1 for L in lens if L % 16 == 0)
     P.commit()
     assert [P.cur_pos(s) for s in ids] == [L + 1 for L in lens]
+
+
+def test_plan_small_workload_uses_few_ctas(kv):
+    P = host_pool(kv, nblocks=64)
+    a = P.seq_alloc()
+    P.plan([a])
+    info = P.plan_info()
+    assert info["grid"] == 1 and info["items"] == [(0, 0, 0, 1), (0, 1, 0, 1)]
 
 
 def test_plan_ex_no_append_reserves_nothing(kv):
