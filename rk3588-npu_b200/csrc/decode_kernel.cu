@@ -61,6 +61,9 @@ struct Smem {
     float merge_l[kConsumerWarps][kMaxGroup];
     WorkItem items[kMaxCtaItems];     // this CTA's pieces
     int cum[kMaxCtaItems + 1];        // flat block offset of each piece
+    int ok[kMaxCtaItems];             // piece passed the checks
+    int last[kMaxCtaItems];           // this CTA merges the piece's segment
+    float segM[kMaxGroup];            // final merge: per-head max
     uint64_t full[kStages];
     uint64_t empty[kStages];
     int nitems;
@@ -103,18 +106,17 @@ __device__ __forceinline__ void flag_timeout(const PoolView& pv, Smem& sm, int i
 }
 
 // Every index a piece leads to, checked before any access (the plan comes
-// from the host planner; a bad one is reported and its piece skipped).
+// from the host planner; a bad piece is reported and skipped).
 __device__ __forceinline__ int item_check(const PoolView& pv, const PlanHeader& hdr,
-                                          const WorkItem& wi, const PlanView& plan) {
-    if (wi.slot < 0 || wi.slot >= hdr.nslots) return 1;
-    if (wi.head < 0 || wi.head >= pv.kv_heads) return 2;
-    const DecodeSlot sl = plan.slots[wi.slot];
-    if (sl.seq < 0 || sl.seq >= pv.max_seqs) return 3;
-    if (sl.kv_len < 0 || sl.kv_len > pv.max_blocks_per_seq * kBlockTokens) return 4;
-    if (sl.rope_pos < 0 || sl.rope_pos >= pv.max_seq_len) return 5;
-    if (sl.append && (sl.kv_len < 1 || sl.new_block < 0 || sl.new_block >= pv.num_blocks)) return 6;
-    if (wi.b0 < 0 || wi.b1 < wi.b0 || wi.b1 > (sl.kv_len + kBlockTokens - 1) / kBlockTokens) return 7;
-    if (wi.seg_first < 0 || wi.seg_n < 1 || wi.seg_first + wi.seg_n > pv.max_items) return 8;
+                                          const WorkItem& w) {
+    if (w.slot < 0 || w.slot >= hdr.nslots) return 1;
+    if (w.head < 0 || w.head >= pv.kv_heads) return 2;
+    if (w.seq < 0 || w.seq >= pv.max_seqs) return 3;
+    if (w.kv_len < 0 || w.kv_len > pv.max_blocks_per_seq * kBlockTokens) return 4;
+    if (w.rope_pos < 0 || w.rope_pos >= pv.max_seq_len) return 5;
+    if (w.append && (w.kv_len < 1 || w.new_block < 0 || w.new_block >= pv.num_blocks)) return 6;
+    if (w.b0 < 0 || w.b1 < w.b0 || w.b1 > (w.kv_len + kBlockTokens - 1) / kBlockTokens) return 7;
+    if (w.seg_first < 0 || w.seg_n < 1 || w.seg_first + w.seg_n > pv.max_items) return 8;
     return 0;
 }
 
@@ -265,6 +267,79 @@ __device__ __forceinline__ void consume_block(uint32_t sK, uint32_t sV, int vali
 
 }  // namespace
 
+// Final merge of a split segment, run by the CTA that finished it last.
+// Per-head maxima first (16 threads per head), then rounds of up to 512
+// pieces: weights l_c * 2^(m_c - M) staged in shared memory, and every output
+// dim sums its pieces with independent loads (no load waits on another).
+__device__ __forceinline__ void merge_segment(const PoolView& pv, Smem& sm, const WorkItem& wi,
+                                              float* out, float* m_out, float* l_out, int tid) {
+    const int G = pv.group;
+    const int n = wi.seg_n;
+    const float* p0 = pv.partials + (size_t)wi.seg_first * kPartialFloats;
+    {
+        const int h = tid >> 4, sub = tid & 15;
+        float M = -INFINITY;
+        if (h < G)
+            for (int ci = sub; ci < n; ci += 16) {
+                const float* pc = p0 + (size_t)ci * kPartialFloats;
+                const float l = __ldcg(pc + kMaxGroup + h);
+                const float m = __ldcg(pc + h);
+                if (l > 0.f) M = fmaxf(M, m);
+            }
+#pragma unroll
+        for (int off = 8; off; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+        if (sub == 0) sm.segM[h] = M;
+    }
+    named_bar_sync(1, kConsumerWarps * 32);
+    constexpr int R = 512;  // R * kMaxGroup floats fit in merge_o
+    static_assert(R * kMaxGroup <= kConsumerWarps * kMaxGroup * kMergeStride, "merge scratch");
+    float* W = &sm.merge_o[0][0][0];
+    const int d = tid;
+    float acc[kMaxGroup], L[kMaxGroup];
+#pragma unroll
+    for (int h = 0; h < kMaxGroup; ++h) acc[h] = L[h] = 0.f;
+    for (int c0 = 0; c0 < n; c0 += R) {
+        const int cn = min(R, n - c0);
+        for (int x = tid; x < cn * kMaxGroup; x += kConsumerWarps * 32) {
+            const int ci = x >> 3, h = x & 7;
+            float w = 0.f;
+            if (h < G) {
+                const float* pc = p0 + (size_t)(c0 + ci) * kPartialFloats;
+                const float l = __ldcg(pc + kMaxGroup + h);
+                const float Mu = sm.segM[h] == -INFINITY ? 0.f : sm.segM[h];
+                if (l > 0.f) w = l * fast_exp2(__ldcg(pc + h) - Mu);
+            }
+            W[x] = w;
+        }
+        named_bar_sync(1, kConsumerWarps * 32);
+#pragma unroll
+        for (int h = 0; h < kMaxGroup; ++h) {
+            if (h >= G) break;
+            float a = 0.f, ls = 0.f;
+            const float* po = p0 + (size_t)c0 * kPartialFloats + 2 * kMaxGroup + h * kHeadDim + d;
+#pragma unroll 4
+            for (int ci = 0; ci < cn; ++ci) {
+                const float w = W[ci * kMaxGroup + h];
+                ls += w;
+                a += w * __ldcg(po + (size_t)ci * kPartialFloats);
+            }
+            acc[h] += a;
+            L[h] += ls;
+        }
+        named_bar_sync(1, kConsumerWarps * 32);
+    }
+    const int qrow = wi.slot * pv.q_heads + wi.head * G;
+#pragma unroll
+    for (int h = 0; h < kMaxGroup; ++h) {
+        if (h >= G) break;
+        out[(size_t)(qrow + h) * kHeadDim + d] = L[h] > 0.f ? acc[h] / L[h] : 0.f;
+        if (m_out != nullptr && d == 0) {
+            m_out[qrow + h] = sm.segM[h] * 0.6931471805599453f;
+            l_out[qrow + h] = L[h];
+        }
+    }
+}
+
 template <int DT>
 __global__ void __launch_bounds__(kThreads, 2)
     decode_kernel(PoolView pv, PlanView plan, int layer, const float* __restrict__ q,
@@ -276,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     const PlanHeader hdr = *plan.hdr;
 
     // Block-table entries allocated by this step's plan.  No launch reads an
-    // entry it patches: the block of a new token is taken from its slot.
+    // entry it patches: the block of a new token is taken from its piece.
     for (int i = blockIdx.x * kThreads + tid; i < hdr.npatch; i += gridDim.x * kThreads) {
         const TablePatch p = plan.patches[i];
         if (p.seq < 0 || p.seq >= pv.max_seqs || p.idx < 0 || p.idx >= pv.max_blocks_per_seq ||
@@ -287,14 +362,24 @@ __global__ void __launch_bounds__(kThreads, 2)
         pv.table[(size_t)p.seq * pv.max_blocks_per_seq + p.idx] = p.block;
     }
 
-    // This CTA's pieces into shared memory.
+    // This CTA's pieces into shared memory, each checked by its own thread.
     const int i0 = plan.cta_start[blockIdx.x];
     int n = plan.cta_start[blockIdx.x + 1] - i0;
     if (n < 0 || n > kMaxCtaItems || i0 < 0 || i0 + n > hdr.nitems) {
         if (tid == 0) report(pv, 5, i0, 300);
         n = 0;
     }
-    for (int j = tid; j < n; j += kThreads) sm.items[j] = plan.items[i0 + j];
+    for (int j = tid; j < n; j += kThreads) {
+        WorkItem w = plan.items[i0 + j];
+        const int bad = item_check(pv, hdr, w);
+        if (bad) {
+            report(pv, 5, i0 + j, bad);
+            w.b0 = w.b1 = 0;
+        }
+        sm.items[j] = w;
+        sm.ok[j] = !bad;
+        sm.last[j] = 0;
+    }
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&sm.full[s], 1);
@@ -308,15 +393,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncthreads();
     if (tid == 0) {
         sm.cum[0] = 0;
-        for (int j = 0; j < n; ++j) {
-            WorkItem& w = sm.items[j];
-            if (const int bad = item_check(pv, hdr, w, plan)) {
-                report(pv, 5, i0 + j, bad);
-                w.b0 = w.b1 = 0;
-                w.seg_n = 0;  // skipped by everyone
-            }
-            sm.cum[j + 1] = sm.cum[j] + (w.b1 - w.b0);
-        }
+        for (int j = 0; j < n; ++j) sm.cum[j + 1] = sm.cum[j] + (sm.items[j].b1 - sm.items[j].b0);
         sm.nitems = n;
     }
     __syncthreads();
@@ -325,17 +402,17 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------ producer
         // Flat walk over this CTA's blocks.  Lanes fetch the block ids of the
-        // next 32 flat positions one batch ahead of lane 0's issue loop.
+        // next 32 flat positions one batch ahead of lane 0's issue loop;
+        // everything else comes from shared memory.
         const uint64_t policy = policy_evict_first();
         auto fetch = [&](int f) -> int {
             if (f >= total) return 0;
             int j = 0;
             while (sm.cum[j + 1] <= f) ++j;
             const WorkItem& w = sm.items[j];
-            const DecodeSlot sl = plan.slots[w.slot];
             const int idx = w.b0 + (f - sm.cum[j]);
-            if (sl.append && idx == (sl.kv_len - 1) / kBlockTokens) return sl.new_block;
-            return pv.table[(size_t)sl.seq * pv.max_blocks_per_seq + idx];
+            if (w.append && idx == (w.kv_len - 1) / kBlockTokens) return w.new_block;
+            return pv.table[(size_t)w.seq * pv.max_blocks_per_seq + idx];
         };
         int cur = fetch(lane), nxt = fetch(32 + lane);
         int ok = 1, j = 0;
@@ -352,10 +429,9 @@ __global__ void __launch_bounds__(kThreads, 2)
                         ok = 0;
                     } else {
                         const WorkItem& w = sm.items[j];
-                        const DecodeSlot sl = plan.slots[w.slot];
                         const int idx = w.b0 + (f - sm.cum[j]);
-                        const int valid = min(kBlockTokens, sl.kv_len - idx * kBlockTokens);
-                        const bool newblk = sl.append && idx == (sl.kv_len - 1) / kBlockTokens;
+                        const int valid = min(kBlockTokens, w.kv_len - idx * kBlockTokens);
+                        const bool newblk = w.append && idx == (w.kv_len - 1) / kBlockTokens;
                         if (newblk && valid == 1) {
                             mbar_arrive(&sm.full[s]);  // only the new token: nothing to load
                         } else if ((unsigned)blk >= (unsigned)pv.num_blocks) {
@@ -398,15 +474,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int g = lane >> 2, c = lane & 3;
     bool dead = false;
     for (int j = 0; j < n; ++j) {
+        if (!sm.ok[j]) continue;  // rejected by the checks above
         const WorkItem wi = sm.items[j];
-        if (wi.seg_n == 0) continue;  // rejected by the checks above
-        const DecodeSlot sl = plan.slots[wi.slot];
         const int nb = wi.b1 - wi.b0;
         const int fbase = sm.cum[j];
-        const int last_blk = (sl.kv_len - 1) / kBlockTokens;
+        const int last_blk = (wi.kv_len - 1) / kBlockTokens;
 
         uint32_t qh[8][2], ql[8][2];
-        load_q_frags<DT>(pv, q, wi.slot, wi.head, sl.rope_pos, qscale, lane, qh, ql);
+        load_q_frags<DT>(pv, q, wi.slot, wi.head, wi.rope_pos, qscale, lane, qh, ql);
         float m2[2] = {-INFINITY, -INFINITY}, lsum[2] = {0.f, 0.f};
         float o[8][4];
 #pragma unroll
@@ -424,11 +499,11 @@ __global__ void __launch_bounds__(kThreads, 2)
             uint8_t* sK = sm.stage[s];
             uint8_t* sV = sm.stage[s] + kTileBytes;
             const int idx = wi.b0 + b;
-            const int valid = min(kBlockTokens, sl.kv_len - idx * kBlockTokens);
-            const bool newblk = sl.append && idx == last_blk;
+            const int valid = min(kBlockTokens, wi.kv_len - idx * kBlockTokens);
+            const bool newblk = wi.append && idx == last_blk;
             if (newblk)
-                write_new_row<DT>(pv, layer, sl.new_block, wi.head, valid - 1, k_new, v_new, wi.slot,
-                                  sl.rope_pos, sK, sV, lane);
+                write_new_row<DT>(pv, layer, wi.new_block, wi.head, valid - 1, k_new, v_new, wi.slot,
+                                  wi.rope_pos, sK, sV, lane);
             if (valid < kBlockTokens) {
                 // Rows past the end may hold anything (stale tiles, inf):
                 // zero them in V so masked weights (exactly 0) stay 0.
@@ -502,45 +577,31 @@ __global__ void __launch_bounds__(kThreads, 2)
                 }
             }
         }
-        if (wi.seg_n == 1) continue;
+    }
 
-        // ---- split segment: the last CTA to finish one merges its pieces.
-        // Release: the barrier orders every thread's partial stores before
-        // thread 0's fence + counter increment; acquire: thread 0 fences
-        // after seeing the final count, and the barrier passes it on.
-        named_bar_sync(1, kConsumerWarps * 32);
-        if (tid == 0) {
-            __threadfence();
-            const int prev = atomicAdd(&pv.counters[wi.slot * pv.kv_heads + wi.head], 1);
-            const int last = (prev == wi.seg_n - 1);
-            if (last) __threadfence();
-            sm.last_flag = last;
+    // ---- split segments: counted once, after all of this CTA's pieces.
+    // Release: the barrier orders every thread's partial stores before
+    // thread 0's fence and counter increments; acquire: thread 0 fences after
+    // seeing a final count, and the barrier passes it on.  The CTA that
+    // completes a segment's count merges that segment.
+    named_bar_sync(1, kConsumerWarps * 32);
+    if (tid == 0) {
+        bool any = false;
+        __threadfence();
+        for (int j = 0; j < n; ++j) {
+            const WorkItem& w = sm.items[j];
+            if (!sm.ok[j] || w.seg_n == 1) continue;
+            const int prev = atomicAdd(&pv.counters[w.slot * pv.kv_heads + w.head], 1);
+            sm.last[j] = (prev == w.seg_n - 1);
+            any |= (prev == w.seg_n - 1);
         }
-        named_bar_sync(1, kConsumerWarps * 32);
-        if (!sm.last_flag) continue;
-        const float* p0 = pv.partials + (size_t)wi.seg_first * kPartialFloats;
-        for (int h = 0; h < pv.group; ++h) {
-            float M = -INFINITY;
-            for (int ci = 0; ci < wi.seg_n; ++ci)
-                if (__ldcg(p0 + (size_t)ci * kPartialFloats + kMaxGroup + h) > 0.f)
-                    M = fmaxf(M, __ldcg(p0 + (size_t)ci * kPartialFloats + h));
-            const float Mu = (M == -INFINITY) ? 0.f : M;
-            float L = 0.f, O = 0.f;
-            for (int ci = 0; ci < wi.seg_n; ++ci) {
-                const float* pc = p0 + (size_t)ci * kPartialFloats;
-                const float lc = __ldcg(pc + kMaxGroup + h);
-                if (lc > 0.f) {
-                    const float w = lc * fast_exp2(__ldcg(pc + h) - Mu);
-                    L += w;
-                    O += w * __ldcg(pc + 2 * kMaxGroup + h * kHeadDim + d);
-                }
-            }
-            out[(size_t)(qrow + h) * kHeadDim + d] = L > 0.f ? O / L : 0.f;
-            if (m_out != nullptr && d == 0) {
-                m_out[qrow + h] = M * 0.6931471805599453f;
-                l_out[qrow + h] = L;
-            }
-        }
+        if (any) __threadfence();
+    }
+    named_bar_sync(1, kConsumerWarps * 32);
+    for (int j = 0; j < n; ++j) {
+        if (!sm.last[j]) continue;
+        const WorkItem wi = sm.items[j];
+        merge_segment(pv, sm, wi, out, m_out, l_out, tid);
         if (tid == 0) pv.counters[wi.slot * pv.kv_heads + wi.head] = 0;
     }
 }

@@ -18,7 +18,7 @@
 #include <string>
 #include <vector>
 
-#include "../../include/kvattn.h"
+#include "kvattn.h"
 #include "kvattn_internal.h"
 
 using namespace kvattn;
@@ -741,13 +741,23 @@ int attn_decode_plan_ex(kvp_pool* p, int nseq, const int* seq_ids, const int* ro
     // ---- pieces: each CTA gets one contiguous, equal run of the flattened
     // (slot, kv head, block) sequence; a segment crossing a CTA boundary is
     // cut into pieces whose partial results are merged on the device ----
+    // Cost model: a piece costs its blocks plus kPieceCost block-equivalents
+    // (warp merge, q reload, partial write), so CTAs holding two pieces take
+    // fewer blocks and every CTA finishes at about the same time.
+    constexpr long kPieceCost = 4;
     const long gmax = std::max(1L, (long)p->num_sms * p->occupancy);
     const long G = std::min(gmax, std::max(1L, (total_blocks + 7) / 8));
-    const long per = std::max(1L, (total_blocks + G - 1) / G);
+    const long per = std::max(kPieceCost + 1,
+                              (total_blocks + kPieceCost * (nsegments + G - 1) + G - 1) / G);
     std::vector<WorkItem> items;
     std::vector<int> cta_start(1, 0);
     long fill = 0;
     int cta_items = 0;
+    auto piece = [&](int i, int hd, int b0, int b1, int seg_first) {
+        const DecodeSlot& sl = slots[i];
+        return WorkItem{i, hd, b0, b1, seg_first, 1, sl.seq, sl.kv_len, sl.rope_pos, sl.append,
+                        sl.new_block, 0};
+    };
     auto close_cta = [&]() {
         cta_start.push_back((int)items.size());
         fill = 0;
@@ -758,16 +768,18 @@ int attn_decode_plan_ex(kvp_pool* p, int nseq, const int* seq_ids, const int* ro
         for (int hd = 0; hd < p->kv_heads; ++hd) {
             const int seg_first = (int)items.size();
             if (nblk == 0) {  // nothing to attend: one empty piece still writes the (zero) result
-                if (cta_items == kMaxCtaItems) close_cta();
-                items.push_back(WorkItem{i, hd, 0, 0, seg_first, 1, {0, 0}});
+                if (fill + kPieceCost > per || cta_items == kMaxCtaItems) close_cta();
+                items.push_back(piece(i, hd, 0, 0, seg_first));
+                fill += kPieceCost;
                 ++cta_items;
                 continue;
             }
             int b = 0;
             while (b < nblk) {
-                if (fill >= per || cta_items == kMaxCtaItems) close_cta();
+                if (fill + kPieceCost >= per || cta_items == kMaxCtaItems) close_cta();
+                fill += kPieceCost;
                 const int take = (int)std::min<long>(nblk - b, per - fill);
-                items.push_back(WorkItem{i, hd, b, b + take, seg_first, 0, {0, 0}});
+                items.push_back(piece(i, hd, b, b + take, seg_first));
                 b += take;
                 fill += take;
                 ++cta_items;

@@ -36,6 +36,7 @@ struct DecodeSlot {
 // segment (all blocks of one sequence for one KV head) is cut into seg_n
 // consecutive pieces starting at item index seg_first; each CTA owns a
 // contiguous run of items, so pieces of one segment sit in different CTAs.
+// The slot's fields are repeated here so a CTA needs one load per piece.
 struct WorkItem {
     int slot;
     int head;
@@ -43,7 +44,12 @@ struct WorkItem {
     int b1;
     int seg_first;
     int seg_n;
-    int pad[2];
+    int seq;        // = slots[slot].seq
+    int kv_len;     // = slots[slot].kv_len
+    int rope_pos;   // = slots[slot].rope_pos
+    int append;     // = slots[slot].append
+    int new_block;  // = slots[slot].new_block
+    int pad;
 };
 
 // A block-table entry to write before use: table[seq][idx] = block.
