@@ -10,10 +10,11 @@
 // and KV head, all its 16-token blocks) and gives every CTA one contiguous,
 // equal run of that flat block sequence; a segment crossing a CTA boundary
 // becomes several pieces.  Per CTA:
-//   warp 4     producer: the warp fetches block-table entries one 32-block
-//              batch ahead; one lane issues 1-D bulk async copies (TMA engine,
-//              no multicast) of each block's K and V tiles (4 KiB each,
-//              contiguous in HBM) into an 8-stage shared-memory ring;
+//   warp 4     producer: lane l < 8 owns ring stage l and issues 1-D bulk
+//              async copies (TMA engine, no multicast) of the K and V tiles
+//              (4 KiB each, contiguous in HBM) of flat blocks l, l+8, ...; the
+//              eight lanes run in step, so one instruction issues up to eight
+//              stages, and each lane fetches its next block id a round ahead;
 //   warps 0-3  consumers: flat block f goes to warp f % 4 (two ring stages
 //              per warp).  Per block: S^T = K * Q^T with mma.sync m16n8k16
 //              (16 tokens x 8 query heads, fp32 q split into hi + lo 16-bit
@@ -312,19 +313,25 @@ __device__ __forceinline__ void merge_segment(const PoolView& pv, Smem& sm, cons
             W[x] = w;
         }
         named_bar_sync(1, kConsumerWarps * 32);
+        // Pieces in groups of 4: the 4 x kMaxGroup loads of a group are all
+        // issued before any is used.
+        const float* po = p0 + (size_t)c0 * kPartialFloats + 2 * kMaxGroup + d;
+        for (int c4 = 0; c4 < cn; c4 += 4) {
+            float v[4][kMaxGroup];
 #pragma unroll
-        for (int h = 0; h < kMaxGroup; ++h) {
-            if (h >= G) break;
-            float a = 0.f, ls = 0.f;
-            const float* po = p0 + (size_t)c0 * kPartialFloats + 2 * kMaxGroup + h * kHeadDim + d;
-#pragma unroll 4
-            for (int ci = 0; ci < cn; ++ci) {
-                const float w = W[ci * kMaxGroup + h];
-                ls += w;
-                a += w * __ldcg(po + (size_t)ci * kPartialFloats);
-            }
-            acc[h] += a;
-            L[h] += ls;
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+                for (int h = 0; h < kMaxGroup; ++h)
+                    v[u][h] = (c4 + u < cn && h < G) ? __ldcg(po + (size_t)(c4 + u) * kPartialFloats + h * kHeadDim)
+                                                      : 0.f;
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+                for (int h = 0; h < kMaxGroup; ++h) {
+                    const float w = (c4 + u < cn) ? W[(c4 + u) * kMaxGroup + h] : 0.f;
+                    L[h] += w;
+                    acc[h] += w * v[u][h];
+                }
         }
         named_bar_sync(1, kConsumerWarps * 32);
     }
@@ -401,70 +408,54 @@ __global__ void __launch_bounds__(kThreads, 2)
 
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------ producer
-        // Flat walk over this CTA's blocks.  Lanes fetch the block ids of the
-        // next 32 flat positions one batch ahead of lane 0's issue loop;
-        // everything else comes from shared memory.
-        const uint64_t policy = policy_evict_first();
-        auto fetch = [&](int f) -> int {
-            if (f >= total) return 0;
-            int j = 0;
-            while (sm.cum[j + 1] <= f) ++j;
-            const WorkItem& w = sm.items[j];
-            const int idx = w.b0 + (f - sm.cum[j]);
-            if (w.append && idx == (w.kv_len - 1) / kBlockTokens) return w.new_block;
-            return pv.table[(size_t)w.seq * pv.max_blocks_per_seq + idx];
-        };
-        int cur = fetch(lane), nxt = fetch(32 + lane);
-        int ok = 1, j = 0;
-        for (int f0 = 0; f0 < total && ok; f0 += 32) {
-            const int cnt = min(32, total - f0);
-            for (int bb = 0; bb < cnt; ++bb) {
-                const int f = f0 + bb;
-                const int blk = __shfl_sync(0xffffffffu, cur, bb);
+        // Lane l < kStages owns ring stage l and issues flat blocks l, l +
+        // kStages, ...; the lanes run the same loop in step, so one warp
+        // instruction issues up to kStages stages.  Each lane fetches the
+        // block id of its next round one round ahead.
+        if (lane < kStages) {
+            const uint64_t policy = policy_evict_first();
+            const int s = lane;
+            auto blk_of = [&](int f, int& jj) -> int {
+                while (sm.cum[jj + 1] <= f) ++jj;
+                const WorkItem& w = sm.items[jj];
+                const int idx = w.b0 + (f - sm.cum[jj]);
+                if (w.append && idx == (w.kv_len - 1) / kBlockTokens) return w.new_block;
+                return pv.table[(size_t)w.seq * pv.max_blocks_per_seq + idx];
+            };
+            int j = 0, jn = 0;
+            int blk = lane < total ? blk_of(lane, jn) : 0;
+            uint32_t rounds = 0;
+            for (int f = lane; f < total; f += kStages) {
+                const int cur = blk;
+                if (f + kStages < total) blk = blk_of(f + kStages, jn);  // next round, in flight
                 while (sm.cum[j + 1] <= f) ++j;
-                if (lane == 0) {
-                    const int s = f % kStages;
-                    if (!mbar_wait_bounded(&sm.empty[s], ((f / kStages) & 1) ^ 1, kWaitLimit)) {
-                        flag_timeout(pv, sm, i0 + j, 0, (uint32_t)f);
-                        ok = 0;
-                    } else {
-                        const WorkItem& w = sm.items[j];
-                        const int idx = w.b0 + (f - sm.cum[j]);
-                        const int valid = min(kBlockTokens, w.kv_len - idx * kBlockTokens);
-                        const bool newblk = w.append && idx == (w.kv_len - 1) / kBlockTokens;
-                        if (newblk && valid == 1) {
-                            mbar_arrive(&sm.full[s]);  // only the new token: nothing to load
-                        } else if ((unsigned)blk >= (unsigned)pv.num_blocks) {
-                            report(pv, 5, i0 + j, 200 + idx);  // never read outside the pool
-                            mbar_arrive(&sm.full[s]);
-                        } else {
-                            const size_t off = (size_t)layer * pv.layer_bytes +
-                                               ((size_t)blk * pv.kv_heads + w.head) * kTileBytes;
-                            mbar_arrive_expect_tx(&sm.full[s], kStageBytes);
-                            bulk_g2s_hint(sm.stage[s], pv.k + off, kTileBytes, &sm.full[s], policy);
-                            bulk_g2s_hint(sm.stage[s] + kTileBytes, pv.v + off, kTileBytes, &sm.full[s],
-                                          policy);
-                        }
-                        *reinterpret_cast<volatile int*>(&sm.prod_issued) = f + 1;
-                    }
-                }
-                ok = __shfl_sync(0xffffffffu, ok, 0);
-                if (!ok) break;
-            }
-            cur = nxt;
-            nxt = fetch(f0 + 64 + lane);
-        }
-        // Drain, on every path (also after a timeout): copies into this CTA's
-        // shared memory must land before it exits.  At most the last kStages
-        // issued stages can still be in flight.
-        if (lane == 0) {
-            const uint32_t issued = (uint32_t)*reinterpret_cast<volatile int*>(&sm.prod_issued);
-            const uint32_t first = issued > (uint32_t)kStages ? issued - kStages : 0u;
-            for (uint32_t k = first; k < issued; ++k)
-                if (!mbar_wait_bounded(&sm.full[k % kStages], (k / kStages) & 1, kWaitLimit)) {
-                    flag_timeout(pv, sm, -2, 2, k);
+                if (!mbar_wait_bounded(&sm.empty[s], (rounds & 1) ^ 1, kWaitLimit)) {
+                    flag_timeout(pv, sm, i0 + j, 0, (uint32_t)f);
                     break;
                 }
+                const WorkItem& w = sm.items[j];
+                const int idx = w.b0 + (f - sm.cum[j]);
+                const int valid = min(kBlockTokens, w.kv_len - idx * kBlockTokens);
+                const bool newblk = w.append && idx == (w.kv_len - 1) / kBlockTokens;
+                if (newblk && valid == 1) {
+                    mbar_arrive(&sm.full[s]);  // only the new token: nothing to load
+                } else if ((unsigned)cur >= (unsigned)pv.num_blocks) {
+                    report(pv, 5, i0 + j, 200 + idx);  // never read outside the pool
+                    mbar_arrive(&sm.full[s]);
+                } else {
+                    const size_t off = (size_t)layer * pv.layer_bytes +
+                                       ((size_t)cur * pv.kv_heads + w.head) * kTileBytes;
+                    mbar_arrive_expect_tx(&sm.full[s], kStageBytes);
+                    bulk_g2s_hint(sm.stage[s], pv.k + off, kTileBytes, &sm.full[s], policy);
+                    bulk_g2s_hint(sm.stage[s] + kTileBytes, pv.v + off, kTileBytes, &sm.full[s], policy);
+                }
+                ++rounds;
+                atomicMax(&sm.prod_issued, f + 1);
+            }
+            // Drain, on every path (also after a timeout): this lane's last
+            // issued stage must land before the CTA exits.
+            if (rounds > 0 && !mbar_wait_bounded(&sm.full[s], (rounds - 1) & 1, kWaitLimit))
+                flag_timeout(pv, sm, -2, 2, (uint32_t)(lane + (rounds - 1) * kStages));
         }
         return;
     }
