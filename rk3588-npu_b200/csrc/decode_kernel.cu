@@ -64,7 +64,6 @@ struct Smem {
     int cum[kMaxCtaItems + 1];        // flat block offset of each piece
     int ok[kMaxCtaItems];             // piece passed the checks
     int last[kMaxCtaItems];           // this CTA merges the piece's segment
-    float segM[kMaxGroup];            // final merge: per-head max
     uint64_t full[kStages];
     uint64_t empty[kStages];
     int nitems;
@@ -268,80 +267,53 @@ __device__ __forceinline__ void consume_block(uint32_t sK, uint32_t sV, int vali
 
 }  // namespace
 
-// Final merge of a split segment, run by the CTA that finished it last.
-// Per-head maxima first (16 threads per head), then rounds of up to 512
-// pieces: weights l_c * 2^(m_c - M) staged in shared memory, and every output
-// dim sums its pieces with independent loads (no load waits on another).
-__device__ __forceinline__ void merge_segment(const PoolView& pv, Smem& sm, const WorkItem& wi,
-                                              float* out, float* m_out, float* l_out, int tid) {
+// Final merge of a split segment, run by the CTA that finished it last: one
+// online log-sum-exp pass per output dim over the segment's pieces, two
+// pieces' loads (all heads, m, l and o) issued together per step.
+__device__ __forceinline__ void merge_segment(const PoolView& pv, const WorkItem& wi, float* out,
+                                              float* m_out, float* l_out, int tid) {
     const int G = pv.group;
     const int n = wi.seg_n;
     const float* p0 = pv.partials + (size_t)wi.seg_first * kPartialFloats;
-    {
-        const int h = tid >> 4, sub = tid & 15;
-        float M = -INFINITY;
-        if (h < G)
-            for (int ci = sub; ci < n; ci += 16) {
-                const float* pc = p0 + (size_t)ci * kPartialFloats;
-                const float l = __ldcg(pc + kMaxGroup + h);
-                const float m = __ldcg(pc + h);
-                if (l > 0.f) M = fmaxf(M, m);
-            }
-#pragma unroll
-        for (int off = 8; off; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-        if (sub == 0) sm.segM[h] = M;
-    }
-    named_bar_sync(1, kConsumerWarps * 32);
-    constexpr int R = 512;  // R * kMaxGroup floats fit in merge_o
-    static_assert(R * kMaxGroup <= kConsumerWarps * kMaxGroup * kMergeStride, "merge scratch");
-    float* W = &sm.merge_o[0][0][0];
     const int d = tid;
-    float acc[kMaxGroup], L[kMaxGroup];
+    float M[kMaxGroup], L[kMaxGroup], A[kMaxGroup];
 #pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h) acc[h] = L[h] = 0.f;
-    for (int c0 = 0; c0 < n; c0 += R) {
-        const int cn = min(R, n - c0);
-        for (int x = tid; x < cn * kMaxGroup; x += kConsumerWarps * 32) {
-            const int ci = x >> 3, h = x & 7;
-            float w = 0.f;
-            if (h < G) {
-                const float* pc = p0 + (size_t)(c0 + ci) * kPartialFloats;
-                const float l = __ldcg(pc + kMaxGroup + h);
-                const float Mu = sm.segM[h] == -INFINITY ? 0.f : sm.segM[h];
-                if (l > 0.f) w = l * fast_exp2(__ldcg(pc + h) - Mu);
+    for (int h = 0; h < kMaxGroup; ++h) {
+        M[h] = -INFINITY;
+        L[h] = A[h] = 0.f;
+    }
+    for (int c = 0; c < n; c += 2) {
+        float mm[2][kMaxGroup], ll[2][kMaxGroup], oo[2][kMaxGroup];
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+            for (int h = 0; h < kMaxGroup; ++h) {
+                const bool live = (c + u < n) && h < G;
+                const float* pc = p0 + (size_t)(c + u) * kPartialFloats;
+                mm[u][h] = live ? __ldcg(pc + h) : 0.f;
+                ll[u][h] = live ? __ldcg(pc + kMaxGroup + h) : 0.f;
+                oo[u][h] = live ? __ldcg(pc + 2 * kMaxGroup + h * kHeadDim + d) : 0.f;
             }
-            W[x] = w;
-        }
-        named_bar_sync(1, kConsumerWarps * 32);
-        // Pieces in groups of 4: the 4 x kMaxGroup loads of a group are all
-        // issued before any is used.
-        const float* po = p0 + (size_t)c0 * kPartialFloats + 2 * kMaxGroup + d;
-        for (int c4 = 0; c4 < cn; c4 += 4) {
-            float v[4][kMaxGroup];
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
+        for (int u = 0; u < 2; ++u)
 #pragma unroll
-                for (int h = 0; h < kMaxGroup; ++h)
-                    v[u][h] = (c4 + u < cn && h < G) ? __ldcg(po + (size_t)(c4 + u) * kPartialFloats + h * kHeadDim)
-                                                      : 0.f;
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-#pragma unroll
-                for (int h = 0; h < kMaxGroup; ++h) {
-                    const float w = (c4 + u < cn) ? W[(c4 + u) * kMaxGroup + h] : 0.f;
-                    L[h] += w;
-                    acc[h] += w * v[u][h];
-                }
-        }
-        named_bar_sync(1, kConsumerWarps * 32);
+            for (int h = 0; h < kMaxGroup; ++h) {
+                if (!(ll[u][h] > 0.f)) continue;  // empty piece: no weight
+                const float Mn = fmaxf(M[h], mm[u][h]);
+                const float a = fast_exp2(M[h] - Mn);   // 0 while M is -inf
+                const float e = ll[u][h] * fast_exp2(mm[u][h] - Mn);
+                A[h] = A[h] * a + e * oo[u][h];
+                L[h] = L[h] * a + e;
+                M[h] = Mn;
+            }
     }
     const int qrow = wi.slot * pv.q_heads + wi.head * G;
 #pragma unroll
     for (int h = 0; h < kMaxGroup; ++h) {
         if (h >= G) break;
-        out[(size_t)(qrow + h) * kHeadDim + d] = L[h] > 0.f ? acc[h] / L[h] : 0.f;
+        out[(size_t)(qrow + h) * kHeadDim + d] = L[h] > 0.f ? A[h] / L[h] : 0.f;
         if (m_out != nullptr && d == 0) {
-            m_out[qrow + h] = sm.segM[h] * 0.6931471805599453f;
+            m_out[qrow + h] = M[h] * 0.6931471805599453f;
             l_out[qrow + h] = L[h];
         }
     }
@@ -369,13 +341,19 @@ __global__ void __launch_bounds__(kThreads, 2)
         pv.table[(size_t)p.seq * pv.max_blocks_per_seq + p.idx] = p.block;
     }
 
-    // This CTA's pieces into shared memory, each checked by its own thread.
-    const int i0 = plan.cta_start[blockIdx.x];
-    int n = plan.cta_start[blockIdx.x + 1] - i0;
-    if (n < 0 || n > kMaxCtaItems || i0 < 0 || i0 + n > hdr.nitems) {
-        if (tid == 0) report(pv, 5, i0, 300);
+    // This CTA's descriptor; producer lanes fetch their first tile ids while
+    // the other threads load and check the pieces.
+    const CtaDesc cd = plan.cta[blockIdx.x];
+    int n = cd.n, nf = cd.nf;
+    if (n < 0 || n > kMaxCtaItems || cd.i0 < 0 || cd.i0 + n > hdr.nitems || nf < 0 || cd.f0 < 0 ||
+        cd.f0 + nf > hdr.ntiles) {
+        if (tid == 0) report(pv, 5, cd.i0, 300);
         n = 0;
+        nf = 0;
     }
+    const int i0 = cd.i0;
+    const bool prod_lane = warp == kConsumerWarps && lane < kStages;
+    int tile_next = (prod_lane && lane < nf) ? plan.tiles[cd.f0 + lane] : -1;
     for (int j = tid; j < n; j += kThreads) {
         WorkItem w = plan.items[i0 + j];
         const int bad = item_check(pv, hdr, w);
@@ -401,9 +379,17 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (tid == 0) {
         sm.cum[0] = 0;
         for (int j = 0; j < n; ++j) sm.cum[j + 1] = sm.cum[j] + (sm.items[j].b1 - sm.items[j].b0);
+        // The tile list and the pieces must describe the same blocks; if not,
+        // nothing of this CTA runs (producer and consumers would disagree).
+        if (sm.cum[n] != nf) {
+            report(pv, 5, i0, 301);
+            n = 0;
+            sm.cum[0] = 0;
+        }
         sm.nitems = n;
     }
     __syncthreads();
+    n = sm.nitems;
     const int total = sm.cum[n];
 
     if (warp == kConsumerWarps) {
@@ -411,40 +397,26 @@ __global__ void __launch_bounds__(kThreads, 2)
         // Lane l < kStages owns ring stage l and issues flat blocks l, l +
         // kStages, ...; the lanes run the same loop in step, so one warp
         // instruction issues up to kStages stages.  Each lane fetches the
-        // block id of its next round one round ahead.
+        // tile id of its next round one round ahead.
         if (lane < kStages) {
             const uint64_t policy = policy_evict_first();
             const int s = lane;
-            auto blk_of = [&](int f, int& jj) -> int {
-                while (sm.cum[jj + 1] <= f) ++jj;
-                const WorkItem& w = sm.items[jj];
-                const int idx = w.b0 + (f - sm.cum[jj]);
-                if (w.append && idx == (w.kv_len - 1) / kBlockTokens) return w.new_block;
-                return pv.table[(size_t)w.seq * pv.max_blocks_per_seq + idx];
-            };
-            int j = 0, jn = 0;
-            int blk = lane < total ? blk_of(lane, jn) : 0;
+            const long ntile_ids = (long)pv.num_blocks * pv.kv_heads;
             uint32_t rounds = 0;
             for (int f = lane; f < total; f += kStages) {
-                const int cur = blk;
-                if (f + kStages < total) blk = blk_of(f + kStages, jn);  // next round, in flight
-                while (sm.cum[j + 1] <= f) ++j;
+                const int cur = tile_next;
+                if (f + kStages < total) tile_next = plan.tiles[cd.f0 + f + kStages];  // in flight
                 if (!mbar_wait_bounded(&sm.empty[s], (rounds & 1) ^ 1, kWaitLimit)) {
-                    flag_timeout(pv, sm, i0 + j, 0, (uint32_t)f);
+                    flag_timeout(pv, sm, i0, 0, (uint32_t)f);
                     break;
                 }
-                const WorkItem& w = sm.items[j];
-                const int idx = w.b0 + (f - sm.cum[j]);
-                const int valid = min(kBlockTokens, w.kv_len - idx * kBlockTokens);
-                const bool newblk = w.append && idx == (w.kv_len - 1) / kBlockTokens;
-                if (newblk && valid == 1) {
+                if (cur == -1) {
                     mbar_arrive(&sm.full[s]);  // only the new token: nothing to load
-                } else if ((unsigned)cur >= (unsigned)pv.num_blocks) {
-                    report(pv, 5, i0 + j, 200 + idx);  // never read outside the pool
+                } else if (cur < 0 || cur >= ntile_ids) {
+                    report(pv, 5, i0, 200 + f);  // never read outside the pool
                     mbar_arrive(&sm.full[s]);
                 } else {
-                    const size_t off = (size_t)layer * pv.layer_bytes +
-                                       ((size_t)cur * pv.kv_heads + w.head) * kTileBytes;
+                    const size_t off = (size_t)layer * pv.layer_bytes + (size_t)cur * kTileBytes;
                     mbar_arrive_expect_tx(&sm.full[s], kStageBytes);
                     bulk_g2s_hint(sm.stage[s], pv.k + off, kTileBytes, &sm.full[s], policy);
                     bulk_g2s_hint(sm.stage[s] + kTileBytes, pv.v + off, kTileBytes, &sm.full[s], policy);
@@ -570,33 +542,31 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
     }
 
-    // ---- split segments: counted once, after all of this CTA's pieces.
-    // Release: the barrier orders every thread's partial stores before
-    // thread 0's fence and counter increments; acquire: thread 0 fences after
-    // seeing a final count, and the barrier passes it on.  The CTA that
-    // completes a segment's count merges that segment.
+    // ---- split segments: counted once, after all of this CTA's pieces, one
+    // thread per piece.  Release: the barrier orders every thread's partial
+    // stores before the counting thread's fence and increment; acquire: that
+    // thread fences after seeing the final count, and the barrier passes it
+    // on.  The CTA that completes a segment's count merges that segment.
     named_bar_sync(1, kConsumerWarps * 32);
-    if (tid == 0) {
-        bool any = false;
-        __threadfence();
-        for (int j = 0; j < n; ++j) {
-            const WorkItem& w = sm.items[j];
-            if (!sm.ok[j] || w.seg_n == 1) continue;
+    if (tid < n) {
+        const WorkItem& w = sm.items[tid];
+        int last = 0;
+        if (sm.ok[tid] && w.seg_n > 1) {
+            __threadfence();
             const int prev = atomicAdd(&pv.counters[w.slot * pv.kv_heads + w.head], 1);
-            sm.last[j] = (prev == w.seg_n - 1);
-            any |= (prev == w.seg_n - 1);
+            last = (prev == w.seg_n - 1);
+            if (last) __threadfence();
         }
-        if (any) __threadfence();
+        sm.last[tid] = last;
     }
     named_bar_sync(1, kConsumerWarps * 32);
     for (int j = 0; j < n; ++j) {
         if (!sm.last[j]) continue;
         const WorkItem wi = sm.items[j];
-        merge_segment(pv, sm, wi, out, m_out, l_out, tid);
+        merge_segment(pv, wi, out, m_out, l_out, tid);
         if (tid == 0) pv.counters[wi.slot * pv.kv_heads + wi.head] = 0;
     }
 }
-
 
 cudaError_t decode_occupancy(int* ctas_per_sm) {
     const int smem = (int)sizeof(Smem) + 1024;

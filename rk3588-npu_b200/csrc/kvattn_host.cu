@@ -82,6 +82,7 @@ struct kvp_pool {
     float theta = 0.f;
     int num_sms = 0, occupancy = 0;
     long max_items = 0;
+    long max_tiles = 0;  // bound on flat blocks in one plan
     PoolView pv{};
 
     // device allocations
@@ -228,20 +229,22 @@ int check_seq(const kvp_pool* p, int seq) {
     return KV_OK;
 }
 
-// Byte layout of one packed plan: header, slots, items, patches, cta_start.
+// Byte layout of one packed plan: header, slots, items, patches, CTA
+// descriptors, tile list.
 struct PlanLayout {
-    size_t slots, items, patches, cta, bytes;
+    size_t slots, items, patches, cta, tiles, bytes;
 };
 
 size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
 
-PlanLayout plan_layout(int nslots, long nitems, int npatch, long grid) {
+PlanLayout plan_layout(int nslots, long nitems, int npatch, long grid, long ntiles) {
     PlanLayout L;
     L.slots = align16(sizeof(PlanHeader));
     L.items = align16(L.slots + (size_t)nslots * sizeof(DecodeSlot));
     L.patches = align16(L.items + (size_t)nitems * sizeof(WorkItem));
     L.cta = align16(L.patches + (size_t)npatch * sizeof(TablePatch));
-    L.bytes = align16(L.cta + (size_t)(grid + 1) * sizeof(int));
+    L.tiles = align16(L.cta + (size_t)grid * sizeof(CtaDesc));
+    L.bytes = align16(L.tiles + (size_t)ntiles * sizeof(int));
     return L;
 }
 
@@ -348,7 +351,8 @@ int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, in
         // Bookkeeping only: plans are built for a nominal 148-SM part and kept on the host.
         p->num_sms = 148;
         p->occupancy = 3;
-        p->plan_bytes = plan_layout(max_seqs, p->max_items, max_seqs, p->max_items).bytes;
+        p->max_tiles = ((long)num_blocks + max_seqs) * num_kv_heads;
+        p->plan_bytes = plan_layout(max_seqs, p->max_items, max_seqs, p->max_items, p->max_tiles).bytes;
         p->h_plan[0] = (uint8_t*)malloc(p->plan_bytes);
         if (!p->h_plan[0]) {
             delete p;
@@ -389,7 +393,8 @@ int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, in
     KV_CUDA_B(cudaMemset(p->d_status, 0, 32 * sizeof(int)));
     KV_CUDA_B(cudaEventCreateWithFlags(&p->pending_evt, cudaEventDisableTiming));
 
-    p->plan_bytes = plan_layout(max_seqs, p->max_items, max_seqs, p->max_items).bytes;
+    p->max_tiles = ((long)num_blocks + max_seqs) * num_kv_heads;
+    p->plan_bytes = plan_layout(max_seqs, p->max_items, max_seqs, p->max_items, p->max_tiles).bytes;
     KV_CUDA_B(cudaStreamCreateWithFlags(&p->copy_stream, cudaStreamNonBlocking));
     for (int i = 0; i < kRing; ++i) {
         KV_CUDA_B(cudaMallocHost((void**)&p->h_plan[i], p->plan_bytes));
@@ -793,8 +798,31 @@ int attn_decode_plan_ex(kvp_pool* p, int nseq, const int* seq_ids, const int* ro
     if ((long)items.size() > p->max_items || grid > p->max_items)
         return fail(KV_ERR_STATE, "work list overflow (%zu items, %d CTAs)", items.size(), grid);
 
+    // ---- per-CTA descriptors and the flat tile list (the host owns the
+    // block tables, so the kernel needs no table reads to start copying) ----
+    std::vector<CtaDesc> ctas(grid);
+    std::vector<int> tiles;
+    tiles.reserve((size_t)total_blocks);
+    for (int gi = 0; gi < grid; ++gi) {
+        ctas[gi] = CtaDesc{cta_start[gi], cta_start[gi + 1] - cta_start[gi], (int)tiles.size(), 0};
+        for (int x = cta_start[gi]; x < cta_start[gi + 1]; ++x) {
+            const WorkItem& w = items[x];
+            const Seq& sq = p->seqs[w.seq];
+            const int last = (w.kv_len - 1) / kBlockTokens;
+            for (int b = w.b0; b < w.b1; ++b) {
+                const bool newblk = w.append && b == last;
+                const int valid = std::min(kBlockTokens, w.kv_len - b * kBlockTokens);
+                const int blk = newblk ? w.new_block : sq.blocks[b];
+                tiles.push_back(newblk && valid == 1 ? -1 : blk * p->kv_heads + w.head);
+            }
+        }
+        ctas[gi].nf = (int)tiles.size() - ctas[gi].f0;
+    }
+    if ((long)tiles.size() > p->max_tiles)
+        return fail(KV_ERR_STATE, "tile list overflow (%zu > %ld)", tiles.size(), p->max_tiles);
+
     // ---- pack and upload once, on the copy stream ----
-    const PlanLayout L = plan_layout(nseq, (long)items.size(), (int)patches.size(), grid);
+    const PlanLayout L = plan_layout(nseq, (long)items.size(), (int)patches.size(), grid, (long)tiles.size());
     PlanHeader* hdr = (PlanHeader*)h;
     hdr->nslots = nseq;
     hdr->nitems = (int)items.size();
@@ -804,10 +832,13 @@ int attn_decode_plan_ex(kvp_pool* p, int nseq, const int* seq_ids, const int* ro
     hdr->off_items = (int)L.items;
     hdr->off_patches = (int)L.patches;
     hdr->off_cta = (int)L.cta;
+    hdr->off_tiles = (int)L.tiles;
+    hdr->ntiles = (int)tiles.size();
     memcpy(h + L.slots, slots.data(), slots.size() * sizeof(DecodeSlot));
     memcpy(h + L.items, items.data(), items.size() * sizeof(WorkItem));
     if (!patches.empty()) memcpy(h + L.patches, patches.data(), patches.size() * sizeof(TablePatch));
-    memcpy(h + L.cta, cta_start.data(), cta_start.size() * sizeof(int));
+    memcpy(h + L.cta, ctas.data(), ctas.size() * sizeof(CtaDesc));
+    if (!tiles.empty()) memcpy(h + L.tiles, tiles.data(), tiles.size() * sizeof(int));
 
     p->plan_active = true;
     p->plan_patched = patches.empty();
@@ -821,7 +852,8 @@ int attn_decode_plan_ex(kvp_pool* p, int nseq, const int* seq_ids, const int* ro
     p->plan_view.slots = (const DecodeSlot*)(base + L.slots);
     p->plan_view.items = (const WorkItem*)(base + L.items);
     p->plan_view.patches = (const TablePatch*)(base + L.patches);
-    p->plan_view.cta_start = (const int*)(base + L.cta);
+    p->plan_view.cta = (const CtaDesc*)(base + L.cta);
+    p->plan_view.tiles = (const int*)(base + L.tiles);
     p->plan_stream = st;
     if (p->host_only) {
         p->plan_patched = true;
@@ -860,9 +892,9 @@ int kvp_plan_cta_start(const kvp_pool* p, int* cta_start, int cap) {
     if (!p->plan_active) return fail(KV_ERR_STATE, "no active decode plan");
     const uint8_t* h = p->h_plan[p->plan_slot_ring];
     const PlanHeader* hdr = (const PlanHeader*)h;
-    const int* cs = (const int*)(h + hdr->off_cta);
+    const CtaDesc* cs = (const CtaDesc*)(h + hdr->off_cta);
     const int n = std::min(cap, hdr->grid + 1);
-    for (int i = 0; i < n; ++i) cta_start[i] = cs[i];
+    for (int i = 0; i < n; ++i) cta_start[i] = i < hdr->grid ? cs[i].i0 : hdr->nitems;
     return KV_OK;
 }
 

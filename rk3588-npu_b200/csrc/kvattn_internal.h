@@ -60,8 +60,19 @@ struct TablePatch {
     int pad;
 };
 
-// The plan is one contiguous upload: header, slots, items, patches, and
-// cta_start[grid + 1] (CTA g owns items [cta_start[g], cta_start[g+1])).
+// Per-CTA descriptor: pieces [i0, i0 + n) and flat blocks [f0, f0 + nf) of
+// the plan's tile list.
+struct CtaDesc {
+    int i0;
+    int n;
+    int f0;
+    int nf;
+};
+
+// The plan is one contiguous upload: header, slots, items, patches, one
+// CtaDesc per CTA, and the tile list: for every flat block of every CTA (in
+// CTA order) the tile index block * kv_heads + head to copy, or -1 for a
+// block that holds only the new token (nothing to load).
 struct PlanHeader {
     int nslots;
     int nitems;
@@ -71,6 +82,9 @@ struct PlanHeader {
     int off_items;
     int off_patches;
     int off_cta;
+    int off_tiles;
+    int ntiles;
+    int pad[2];
 };
 
 // Device view of the pool handed to kernels by value.
@@ -100,7 +114,8 @@ struct PlanView {
     const DecodeSlot* slots;
     const WorkItem* items;
     const TablePatch* patches;
-    const int* cta_start;
+    const CtaDesc* cta;
+    const int* tiles;
 };
 
 // ---- launchers (kernels.cu) ----
