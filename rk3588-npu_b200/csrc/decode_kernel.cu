@@ -64,6 +64,7 @@ struct Smem {
     int cum[kMaxCtaItems + 1];        // flat block offset of each piece
     int ok[kMaxCtaItems];             // piece passed the checks
     int last[kMaxCtaItems];           // this CTA merges the piece's segment
+    float segM[kMaxGroup];            // final merge: running per-head max
     uint64_t full[kStages];
     uint64_t empty[kStages];
     int nitems;
@@ -267,14 +268,21 @@ __device__ __forceinline__ void consume_block(uint32_t sK, uint32_t sV, int vali
 
 }  // namespace
 
-// Final merge of a split segment, run by the CTA that finished it last: one
-// online log-sum-exp pass per output dim over the segment's pieces, two
-// pieces' loads (all heads, m, l and o) issued together per step.
-__device__ __forceinline__ void merge_segment(const PoolView& pv, const WorkItem& wi, float* out,
-                                              float* m_out, float* l_out, int tid) {
+// Final merge of a split segment, run by the CTA that finished it last, in
+// three phases so the dependent latency stays a few L2 round trips however
+// many pieces there are: (A) every piece's m and l loaded in parallel into
+// shared memory, (B) per-head maxima and weights l_c * 2^(m_c - M) computed
+// there, (C) every output dim sums w * o over the pieces in batches of
+// 8 pieces x all heads of independent loads.  Pieces are taken 128 at a time.
+__device__ __forceinline__ void merge_segment(const PoolView& pv, Smem& sm, const WorkItem& wi,
+                                              float* out, float* m_out, float* l_out, int tid) {
+    constexpr int kChunk = 128;  // pieces per pass: kChunk * 8 * 2 floats fit in merge_o
+    static_assert(kChunk * kMaxGroup * 2 <= kConsumerWarps * kMaxGroup * kMergeStride, "merge scratch");
     const int G = pv.group;
     const int n = wi.seg_n;
     const float* p0 = pv.partials + (size_t)wi.seg_first * kPartialFloats;
+    float* Wm = &sm.merge_o[0][0][0];             // [kChunk][8]: m, then weights
+    float* Wl = Wm + kChunk * kMaxGroup;          // [kChunk][8]: l
     const int d = tid;
     float M[kMaxGroup], L[kMaxGroup], A[kMaxGroup];
 #pragma unroll
@@ -282,30 +290,63 @@ __device__ __forceinline__ void merge_segment(const PoolView& pv, const WorkItem
         M[h] = -INFINITY;
         L[h] = A[h] = 0.f;
     }
-    for (int c = 0; c < n; c += 2) {
-        float mm[2][kMaxGroup], ll[2][kMaxGroup], oo[2][kMaxGroup];
+    for (int c0 = 0; c0 < n; c0 += kChunk) {
+        const int cn = min(kChunk, n - c0);
+        // (A)
+        for (int x = tid; x < cn * kMaxGroup; x += kConsumerWarps * 32) {
+            const int ci = x >> 3, h = x & 7;
+            const float* pc = p0 + (size_t)(c0 + ci) * kPartialFloats;
+            const bool live = h < G;
+            Wm[x] = live ? __ldcg(pc + h) : 0.f;
+            Wl[x] = live ? __ldcg(pc + kMaxGroup + h) : 0.f;
+        }
+        named_bar_sync(1, kConsumerWarps * 32);
+        // (B) running max over chunks (threads 0..7, one head each), weights
+        // relative to it; what earlier chunks accumulated is rescaled if the
+        // max grew.
+        if (tid < kMaxGroup) {
+            float mx = M[0];
 #pragma unroll
-        for (int u = 0; u < 2; ++u)
+            for (int h = 1; h < kMaxGroup; ++h)
+                if (tid == h) mx = M[h];
+            for (int ci = 0; ci < cn; ++ci)
+                if (Wl[ci * kMaxGroup + tid] > 0.f) mx = fmaxf(mx, Wm[ci * kMaxGroup + tid]);
+            sm.segM[tid] = mx;
+        }
+        named_bar_sync(1, kConsumerWarps * 32);
+        for (int x = tid; x < cn * kMaxGroup; x += kConsumerWarps * 32) {
+            const float l = Wl[x];
+            Wm[x] = (l > 0.f) ? l * fast_exp2(Wm[x] - sm.segM[x & 7]) : 0.f;
+        }
+        named_bar_sync(1, kConsumerWarps * 32);
 #pragma unroll
-            for (int h = 0; h < kMaxGroup; ++h) {
-                const bool live = (c + u < n) && h < G;
-                const float* pc = p0 + (size_t)(c + u) * kPartialFloats;
-                mm[u][h] = live ? __ldcg(pc + h) : 0.f;
-                ll[u][h] = live ? __ldcg(pc + kMaxGroup + h) : 0.f;
-                oo[u][h] = live ? __ldcg(pc + 2 * kMaxGroup + h * kHeadDim + d) : 0.f;
-            }
+        for (int h = 0; h < kMaxGroup; ++h) {
+            const float Mc = sm.segM[h];
+            const float r = (M[h] == -INFINITY || Mc == -INFINITY) ? 0.f : fast_exp2(M[h] - Mc);
+            A[h] *= r;
+            L[h] *= r;
+            M[h] = Mc;
+        }
+        // (C)
+        const float* po = p0 + (size_t)c0 * kPartialFloats + 2 * kMaxGroup + d;
+        for (int c8 = 0; c8 < cn; c8 += 8) {
+            float v[8][kMaxGroup];
 #pragma unroll
-        for (int u = 0; u < 2; ++u)
+            for (int u = 0; u < 8; ++u)
 #pragma unroll
-            for (int h = 0; h < kMaxGroup; ++h) {
-                if (!(ll[u][h] > 0.f)) continue;  // empty piece: no weight
-                const float Mn = fmaxf(M[h], mm[u][h]);
-                const float a = fast_exp2(M[h] - Mn);   // 0 while M is -inf
-                const float e = ll[u][h] * fast_exp2(mm[u][h] - Mn);
-                A[h] = A[h] * a + e * oo[u][h];
-                L[h] = L[h] * a + e;
-                M[h] = Mn;
-            }
+                for (int h = 0; h < kMaxGroup; ++h)
+                    v[u][h] = (c8 + u < cn && h < G) ? __ldcg(po + (size_t)(c8 + u) * kPartialFloats + h * kHeadDim)
+                                                      : 0.f;
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+#pragma unroll
+                for (int h = 0; h < kMaxGroup; ++h) {
+                    const float w = (c8 + u < cn) ? Wm[(c8 + u) * kMaxGroup + h] : 0.f;
+                    A[h] += w * v[u][h];
+                    L[h] += w;
+                }
+        }
+        named_bar_sync(1, kConsumerWarps * 32);  // scratch reused by the next chunk
     }
     const int qrow = wi.slot * pv.q_heads + wi.head * G;
 #pragma unroll
@@ -563,7 +604,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int j = 0; j < n; ++j) {
         if (!sm.last[j]) continue;
         const WorkItem wi = sm.items[j];
-        merge_segment(pv, wi, out, m_out, l_out, tid);
+        merge_segment(pv, sm, wi, out, m_out, l_out, tid);
         if (tid == 0) pv.counters[wi.slot * pv.kv_heads + wi.head] = 0;
     }
 }
