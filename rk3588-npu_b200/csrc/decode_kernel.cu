@@ -268,21 +268,19 @@ __device__ __forceinline__ void consume_block(uint32_t sK, uint32_t sV, int vali
 
 }  // namespace
 
-// Final merge of a split segment, run by the CTA that finished it last, in
-// three phases so the dependent latency stays a few L2 round trips however
-// many pieces there are: (A) every piece's m and l loaded in parallel into
-// shared memory, (B) per-head maxima and weights l_c * 2^(m_c - M) computed
-// there, (C) every output dim sums w * o over the pieces in batches of
-// 8 pieces x all heads of independent loads.  Pieces are taken 128 at a time.
+// Final merge of a split segment, run by the CTA that finished it last.
+// Pieces are taken 8 at a time and each group costs one L2 round trip: the
+// group's m and l go to shared memory and every thread's o values (8 pieces
+// x all heads, for its output dim) to registers, all loads issued together;
+// then per-head maxima (threads 0..7) and an online log-sum-exp update.
 __device__ __forceinline__ void merge_segment(const PoolView& pv, Smem& sm, const WorkItem& wi,
                                               float* out, float* m_out, float* l_out, int tid) {
-    constexpr int kChunk = 128;  // pieces per pass: kChunk * 8 * 2 floats fit in merge_o
-    static_assert(kChunk * kMaxGroup * 2 <= kConsumerWarps * kMaxGroup * kMergeStride, "merge scratch");
+    constexpr int kGroupPieces = 8;
     const int G = pv.group;
     const int n = wi.seg_n;
     const float* p0 = pv.partials + (size_t)wi.seg_first * kPartialFloats;
-    float* Wm = &sm.merge_o[0][0][0];             // [kChunk][8]: m, then weights
-    float* Wl = Wm + kChunk * kMaxGroup;          // [kChunk][8]: l
+    float* Wm = &sm.merge_o[0][0][0];          // [8 pieces][8 heads]
+    float* Wl = Wm + kGroupPieces * kMaxGroup;
     const int d = tid;
     float M[kMaxGroup], L[kMaxGroup], A[kMaxGroup];
 #pragma unroll
@@ -290,63 +288,50 @@ __device__ __forceinline__ void merge_segment(const PoolView& pv, Smem& sm, cons
         M[h] = -INFINITY;
         L[h] = A[h] = 0.f;
     }
-    for (int c0 = 0; c0 < n; c0 += kChunk) {
-        const int cn = min(kChunk, n - c0);
-        // (A)
-        for (int x = tid; x < cn * kMaxGroup; x += kConsumerWarps * 32) {
-            const int ci = x >> 3, h = x & 7;
-            const float* pc = p0 + (size_t)(c0 + ci) * kPartialFloats;
-            const bool live = h < G;
-            Wm[x] = live ? __ldcg(pc + h) : 0.f;
-            Wl[x] = live ? __ldcg(pc + kMaxGroup + h) : 0.f;
+    for (int c0 = 0; c0 < n; c0 += kGroupPieces) {
+        const int cn = min(kGroupPieces, n - c0);
+        const float* pg = p0 + (size_t)c0 * kPartialFloats;
+        if (tid < kGroupPieces * kMaxGroup) {
+            const int u = tid >> 3, h = tid & 7;
+            const bool live = u < cn && h < G;
+            Wm[tid] = live ? __ldcg(pg + (size_t)u * kPartialFloats + h) : 0.f;
+            Wl[tid] = live ? __ldcg(pg + (size_t)u * kPartialFloats + kMaxGroup + h) : 0.f;
         }
-        named_bar_sync(1, kConsumerWarps * 32);
-        // (B) running max over chunks (threads 0..7, one head each), weights
-        // relative to it; what earlier chunks accumulated is rescaled if the
-        // max grew.
-        if (tid < kMaxGroup) {
-            float mx = M[0];
+        float v[kGroupPieces][kMaxGroup];
 #pragma unroll
-            for (int h = 1; h < kMaxGroup; ++h)
-                if (tid == h) mx = M[h];
-            for (int ci = 0; ci < cn; ++ci)
-                if (Wl[ci * kMaxGroup + tid] > 0.f) mx = fmaxf(mx, Wm[ci * kMaxGroup + tid]);
-            sm.segM[tid] = mx;
-        }
+        for (int u = 0; u < kGroupPieces; ++u)
+#pragma unroll
+            for (int h = 0; h < kMaxGroup; ++h)
+                v[u][h] = (u < cn && h < G)
+                              ? __ldcg(pg + (size_t)u * kPartialFloats + 2 * kMaxGroup + h * kHeadDim + d)
+                              : 0.f;
         named_bar_sync(1, kConsumerWarps * 32);
-        for (int x = tid; x < cn * kMaxGroup; x += kConsumerWarps * 32) {
-            const float l = Wl[x];
-            Wm[x] = (l > 0.f) ? l * fast_exp2(Wm[x] - sm.segM[x & 7]) : 0.f;
+        if (tid < kMaxGroup) {
+            float mx = -INFINITY;
+            for (int u = 0; u < cn; ++u)
+                if (Wl[u * kMaxGroup + tid] > 0.f) mx = fmaxf(mx, Wm[u * kMaxGroup + tid]);
+            sm.segM[tid] = mx;
         }
         named_bar_sync(1, kConsumerWarps * 32);
 #pragma unroll
         for (int h = 0; h < kMaxGroup; ++h) {
-            const float Mc = sm.segM[h];
-            const float r = (M[h] == -INFINITY || Mc == -INFINITY) ? 0.f : fast_exp2(M[h] - Mc);
-            A[h] *= r;
-            L[h] *= r;
-            M[h] = Mc;
+            const float Mg = sm.segM[h];
+            if (Mg == -INFINITY) continue;  // nothing in this group for head h
+            const float Mn = fmaxf(M[h], Mg);
+            const float r = fast_exp2(M[h] - Mn);  // 0 while M is -inf
+            float a = 0.f, l = 0.f;
+#pragma unroll
+            for (int u = 0; u < kGroupPieces; ++u) {
+                const float lu = Wl[u * kMaxGroup + h];
+                const float w = lu > 0.f ? lu * fast_exp2(Wm[u * kMaxGroup + h] - Mn) : 0.f;
+                a += w * v[u][h];
+                l += w;
+            }
+            A[h] = A[h] * r + a;
+            L[h] = L[h] * r + l;
+            M[h] = Mn;
         }
-        // (C)
-        const float* po = p0 + (size_t)c0 * kPartialFloats + 2 * kMaxGroup + d;
-        for (int c8 = 0; c8 < cn; c8 += 8) {
-            float v[8][kMaxGroup];
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-#pragma unroll
-                for (int h = 0; h < kMaxGroup; ++h)
-                    v[u][h] = (c8 + u < cn && h < G) ? __ldcg(po + (size_t)(c8 + u) * kPartialFloats + h * kHeadDim)
-                                                      : 0.f;
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-#pragma unroll
-                for (int h = 0; h < kMaxGroup; ++h) {
-                    const float w = (c8 + u < cn) ? Wm[(c8 + u) * kMaxGroup + h] : 0.f;
-                    A[h] += w * v[u][h];
-                    L[h] += w;
-                }
-        }
-        named_bar_sync(1, kConsumerWarps * 32);  // scratch reused by the next chunk
+        named_bar_sync(1, kConsumerWarps * 32);  // scratch reused by the next group
     }
     const int qrow = wi.slot * pv.q_heads + wi.head * G;
 #pragma unroll
@@ -382,8 +367,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         pv.table[(size_t)p.seq * pv.max_blocks_per_seq + p.idx] = p.block;
     }
 
-    // This CTA's descriptor; producer lanes fetch their first tile ids while
-    // the other threads load and check the pieces.
+    // This CTA's descriptor.  Producer lanes initialise their own stage's
+    // barriers and issue the first ring round straight from the descriptor,
+    // before the CTA-wide barrier; the other threads load and check pieces.
     const CtaDesc cd = plan.cta[blockIdx.x];
     int n = cd.n, nf = cd.nf;
     if (n < 0 || n > kMaxCtaItems || cd.i0 < 0 || cd.i0 + n > hdr.nitems || nf < 0 || cd.f0 < 0 ||
@@ -394,7 +380,29 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     const int i0 = cd.i0;
     const bool prod_lane = warp == kConsumerWarps && lane < kStages;
-    int tile_next = (prod_lane && lane < nf) ? plan.tiles[cd.f0 + lane] : -1;
+    const uint64_t policy = policy_evict_first();
+    const long ntile_ids = (long)pv.num_blocks * pv.kv_heads;
+    // One ring round of producer lane `s` for flat block f with tile id `tile`.
+    auto issue = [&](int s, int f, int tile) {
+        if (tile == -1) {
+            mbar_arrive(&sm.full[s]);  // only the new token: nothing to load
+        } else if (tile < 0 || tile >= ntile_ids) {
+            report(pv, 5, i0, 200 + f);  // never read outside the pool
+            mbar_arrive(&sm.full[s]);
+        } else {
+            const size_t off = (size_t)layer * pv.layer_bytes + (size_t)tile * kTileBytes;
+            mbar_arrive_expect_tx(&sm.full[s], kStageBytes);
+            bulk_g2s_hint(sm.stage[s], pv.k + off, kTileBytes, &sm.full[s], policy);
+            bulk_g2s_hint(sm.stage[s] + kTileBytes, pv.v + off, kTileBytes, &sm.full[s], policy);
+        }
+    };
+    if (prod_lane) {
+        mbar_init(&sm.full[lane], 1);
+        mbar_init(&sm.empty[lane], 1);
+        fence_mbar_init();
+        if (lane < nf) issue(lane, lane, plan.cta[blockIdx.x].first[lane]);  // round 0: the stage is free
+    }
+    int tile_next = (prod_lane && lane + kStages < nf) ? plan.tiles[cd.f0 + lane + kStages] : -1;
     for (int j = tid; j < n; j += kThreads) {
         WorkItem w = plan.items[i0 + j];
         const int bad = item_check(pv, hdr, w);
@@ -407,27 +415,18 @@ __global__ void __launch_bounds__(kThreads, 2)
         sm.last[j] = 0;
     }
     if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(&sm.full[s], 1);
-            mbar_init(&sm.empty[s], 1);
-        }
         sm.failed = 0;
         sm.prod_issued = 0;
         for (int w = 0; w < kConsumerWarps; ++w) sm.cons_done[w] = 0;
-        fence_mbar_init();
     }
     __syncthreads();
     if (tid == 0) {
         sm.cum[0] = 0;
         for (int j = 0; j < n; ++j) sm.cum[j + 1] = sm.cum[j] + (sm.items[j].b1 - sm.items[j].b0);
         // The tile list and the pieces must describe the same blocks; if not,
-        // nothing of this CTA runs (producer and consumers would disagree).
-        if (sm.cum[n] != nf) {
-            report(pv, 5, i0, 301);
-            n = 0;
-            sm.cum[0] = 0;
-        }
-        sm.nitems = n;
+        // no consumer runs (the producer still drains what it issued).
+        sm.nitems = (sm.cum[n] == nf) ? n : 0;
+        if (sm.cum[n] != nf) report(pv, 5, i0, 301);
     }
     __syncthreads();
     n = sm.nitems;
@@ -440,33 +439,21 @@ __global__ void __launch_bounds__(kThreads, 2)
         // instruction issues up to kStages stages.  Each lane fetches the
         // tile id of its next round one round ahead.
         if (lane < kStages) {
-            const uint64_t policy = policy_evict_first();
             const int s = lane;
-            const long ntile_ids = (long)pv.num_blocks * pv.kv_heads;
-            uint32_t rounds = 0;
-            for (int f = lane; f < total; f += kStages) {
+            uint32_t rounds = lane < nf ? 1u : 0u;  // round 0 went out above
+            for (int f = lane + kStages; f < total; f += kStages) {
                 const int cur = tile_next;
                 if (f + kStages < total) tile_next = plan.tiles[cd.f0 + f + kStages];  // in flight
                 if (!mbar_wait_bounded(&sm.empty[s], (rounds & 1) ^ 1, kWaitLimit)) {
                     flag_timeout(pv, sm, i0, 0, (uint32_t)f);
                     break;
                 }
-                if (cur == -1) {
-                    mbar_arrive(&sm.full[s]);  // only the new token: nothing to load
-                } else if (cur < 0 || cur >= ntile_ids) {
-                    report(pv, 5, i0, 200 + f);  // never read outside the pool
-                    mbar_arrive(&sm.full[s]);
-                } else {
-                    const size_t off = (size_t)layer * pv.layer_bytes + (size_t)cur * kTileBytes;
-                    mbar_arrive_expect_tx(&sm.full[s], kStageBytes);
-                    bulk_g2s_hint(sm.stage[s], pv.k + off, kTileBytes, &sm.full[s], policy);
-                    bulk_g2s_hint(sm.stage[s] + kTileBytes, pv.v + off, kTileBytes, &sm.full[s], policy);
-                }
+                issue(s, f, cur);
                 ++rounds;
                 atomicMax(&sm.prod_issued, f + 1);
             }
-            // Drain, on every path (also after a timeout): this lane's last
-            // issued stage must land before the CTA exits.
+            // Drain, on every path (also after a timeout or a rejected plan):
+            // this lane's last issued stage must land before the CTA exits.
             if (rounds > 0 && !mbar_wait_bounded(&sm.full[s], (rounds - 1) & 1, kWaitLimit))
                 flag_timeout(pv, sm, -2, 2, (uint32_t)(lane + (rounds - 1) * kStages));
         }
@@ -584,20 +571,17 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
 
     // ---- split segments: counted once, after all of this CTA's pieces, one
-    // thread per piece.  Release: the barrier orders every thread's partial
-    // stores before the counting thread's fence and increment; acquire: that
-    // thread fences after seeing the final count, and the barrier passes it
-    // on.  The CTA that completes a segment's count merges that segment.
+    // thread per piece.  The barrier orders every thread's partial stores
+    // before the counting thread's acquire-release increment (release); the
+    // thread that completes a count has acquired all earlier increments'
+    // partials, and the barrier passes that on.  The CTA that completes a
+    // segment's count merges that segment.
     named_bar_sync(1, kConsumerWarps * 32);
     if (tid < n) {
         const WorkItem& w = sm.items[tid];
         int last = 0;
-        if (sm.ok[tid] && w.seg_n > 1) {
-            __threadfence();
-            const int prev = atomicAdd(&pv.counters[w.slot * pv.kv_heads + w.head], 1);
-            last = (prev == w.seg_n - 1);
-            if (last) __threadfence();
-        }
+        if (sm.ok[tid] && w.seg_n > 1)
+            last = atomic_add_acq_rel_gpu(&pv.counters[w.slot * pv.kv_heads + w.head], 1) == w.seg_n - 1;
         sm.last[tid] = last;
     }
     named_bar_sync(1, kConsumerWarps * 32);

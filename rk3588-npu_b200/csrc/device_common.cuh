@@ -196,6 +196,15 @@ __device__ __forceinline__ float fast_exp2(float x) {
     return y;
 }
 
+// Counter increment with acquire-release semantics at GPU scope: publishes
+// everything that happens-before it and sees everything published before
+// the values it reads.
+__device__ __forceinline__ int atomic_add_acq_rel_gpu(int* p, int v) {
+    int old;
+    asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }

@@ -804,7 +804,8 @@ int attn_decode_plan_ex(kvp_pool* p, int nseq, const int* seq_ids, const int* ro
     std::vector<int> tiles;
     tiles.reserve((size_t)total_blocks);
     for (int gi = 0; gi < grid; ++gi) {
-        ctas[gi] = CtaDesc{cta_start[gi], cta_start[gi + 1] - cta_start[gi], (int)tiles.size(), 0};
+        ctas[gi] = CtaDesc{cta_start[gi], cta_start[gi + 1] - cta_start[gi], (int)tiles.size(), 0,
+                           {-2, -2, -2, -2, -2, -2, -2, -2}};
         for (int x = cta_start[gi]; x < cta_start[gi + 1]; ++x) {
             const WorkItem& w = items[x];
             const Seq& sq = p->seqs[w.seq];
@@ -817,6 +818,7 @@ int attn_decode_plan_ex(kvp_pool* p, int nseq, const int* seq_ids, const int* ro
             }
         }
         ctas[gi].nf = (int)tiles.size() - ctas[gi].f0;
+        for (int x = 0; x < 8 && x < ctas[gi].nf; ++x) ctas[gi].first[x] = tiles[ctas[gi].f0 + x];
     }
     if ((long)tiles.size() > p->max_tiles)
         return fail(KV_ERR_STATE, "tile list overflow (%zu > %ld)", tiles.size(), p->max_tiles);

@@ -67,6 +67,7 @@ struct CtaDesc {
     int n;
     int f0;
     int nf;
+    int first[8];  // tiles[f0 .. f0+7] (or -2 past nf): the first ring round needs no second load
 };
 
 // The plan is one contiguous upload: header, slots, items, patches, one
