@@ -54,6 +54,7 @@ constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kStageBytes = 2 * kTileBytes;  // K tile then V tile
 constexpr int kMergeStride = 132;            // floats per (warp, head) row, padded
 constexpr long long kWaitLimit = 4000000000LL;  // SM clocks (~2 s) before a wait gives up
+constexpr int kQPre = 4;                     // pieces whose q fragments are prepared up front
 
 struct Smem {
     alignas(1024) uint8_t stage[kStages][kStageBytes];
@@ -65,6 +66,8 @@ struct Smem {
     int ok[kMaxCtaItems];             // piece passed the checks
     int last[kMaxCtaItems];           // this CTA merges the piece's segment
     float segM[kMaxGroup];            // final merge: running per-head max
+    // q fragments (hi, lo) of the first kQPre pieces, as each lane holds them
+    uint32_t qfrag[kQPre][2][8][2][32];
     uint64_t full[kStages];
     uint64_t empty[kStages];
     int nitems;
@@ -463,6 +466,21 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ---------------------------------------------------------- consumers
     const float qscale = 0.08838834764831845f * 1.4426950408889634f;  // 1/sqrt(128) * log2(e)
     const int g = lane >> 2, c = lane & 3;
+    // Warp w prepares the q fragments of piece w (w < kQPre) while the first
+    // copies are in flight, so piece switches read them from shared memory.
+    if (warp < n && warp < kQPre && sm.ok[warp]) {
+        const WorkItem& w = sm.items[warp];
+        uint32_t qh[8][2], ql[8][2];
+        load_q_frags<DT>(pv, q, w.slot, w.head, w.rope_pos, qscale, lane, qh, ql);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                sm.qfrag[warp][0][kk][r][lane] = qh[kk][r];
+                sm.qfrag[warp][1][kk][r][lane] = ql[kk][r];
+            }
+    }
+    named_bar_sync(1, kConsumerWarps * 32);
     bool dead = false;
     for (int j = 0; j < n; ++j) {
         if (!sm.ok[j]) continue;  // rejected by the checks above
@@ -472,7 +490,17 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int last_blk = (wi.kv_len - 1) / kBlockTokens;
 
         uint32_t qh[8][2], ql[8][2];
-        load_q_frags<DT>(pv, q, wi.slot, wi.head, wi.rope_pos, qscale, lane, qh, ql);
+        if (j < kQPre) {
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+#pragma unroll
+                for (int r = 0; r < 2; ++r) {
+                    qh[kk][r] = sm.qfrag[j][0][kk][r][lane];
+                    ql[kk][r] = sm.qfrag[j][1][kk][r][lane];
+                }
+        } else {
+            load_q_frags<DT>(pv, q, wi.slot, wi.head, wi.rope_pos, qscale, lane, qh, ql);
+        }
         float m2[2] = {-INFINITY, -INFINITY}, lsum[2] = {0.f, 0.f};
         float o[8][4];
 #pragma unroll

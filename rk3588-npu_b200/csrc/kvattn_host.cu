@@ -749,7 +749,7 @@ int attn_decode_plan_ex(kvp_pool* p, int nseq, const int* seq_ids, const int* ro
     // Cost model: a piece costs its blocks plus kPieceCost block-equivalents
     // (warp merge, q reload, partial write), so CTAs holding two pieces take
     // fewer blocks and every CTA finishes at about the same time.
-    constexpr long kPieceCost = 4;
+    constexpr long kPieceCost = 6;
     const long gmax = std::max(1L, (long)p->num_sms * p->occupancy);
     const long G = std::min(gmax, std::max(1L, (total_blocks + 7) / 8));
     const long per = std::max(kPieceCost + 1,
