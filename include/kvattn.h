@@ -194,6 +194,13 @@ int kvp_plan_info(const kvp_pool* pool, int* nitems, int* grid, int* npatch, int
  * [cta_start[g], cta_start[g+1]). */
 int kvp_plan_cta_start(const kvp_pool* pool, int* cta_start, int cap);
 
+/* Launch timing: when enabled, CUDA events are recorded on the launching
+ * stream immediately before and after every decode launch of this pool.
+ * kvp_timing_read synchronises on the last event and returns the summed
+ * launch durations (ms) and the launch count since enabling, then resets. */
+int kvp_timing_enable(kvp_pool* pool, int enable);
+int kvp_timing_read(kvp_pool* pool, double* total_ms, int* launches);
+
 /* Number of SMs and of resident decode CTAs per SM used for grid sizing. */
 int kvp_launch_info(const kvp_pool* pool, int* num_sms, int* ctas_per_sm);
 

@@ -59,6 +59,8 @@ _SIGS = {
     "kvp_plan_info": [_vp, _ip, _ip, _ip, _ip, _ip, _ip, _ip, C.c_int],
     "kvp_plan_cta_start": [_vp, _ip, C.c_int],
     "kvp_launch_info": [_vp, _ip, _ip],
+    "kvp_timing_enable": [_vp, C.c_int],
+    "kvp_timing_read": [_vp, C.POINTER(C.c_double), _ip],
 }
 _RESTYPE = {"kv_last_error": C.c_char_p, "kv_status_str": C.c_char_p, "kv_version": C.c_char_p}
 
@@ -271,6 +273,15 @@ class Pool:
 
     def commit(self) -> None:
         call("attn_decode_commit", self.h)
+
+    def timing(self, enable: bool) -> None:
+        call("kvp_timing_enable", self.h, int(enable))
+
+    def timing_read(self):
+        """(summed decode-launch milliseconds, launches) since timing(True)."""
+        ms, n = C.c_double(), C.c_int()
+        call("kvp_timing_read", self.h, C.byref(ms), C.byref(n))
+        return ms.value, n.value
 
     def device_status(self, stream=None) -> int:
         s = C.c_int()

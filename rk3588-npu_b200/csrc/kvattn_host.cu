@@ -125,6 +125,11 @@ struct kvp_pool {
     std::vector<int> plan_append;
     cudaStream_t plan_stream = nullptr;
 
+    // launch timing (kvp_timing_enable)
+    bool timing = false;
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> tev;
+    size_t tev_used = 0;
+
     void reset_free_list() {
         free_.resize(num_blocks);
         where_.assign(num_blocks, -1);
@@ -266,6 +271,10 @@ void free_device(kvp_pool* p) {
         if (p->slot_free[i]) cudaEventDestroy(p->slot_free[i]);
     }
     if (p->copy_stream) cudaStreamDestroy(p->copy_stream);
+    for (auto& e : p->tev) {
+        cudaEventDestroy(e.first);
+        cudaEventDestroy(e.second);
+    }
 }
 
 }  // namespace
@@ -918,10 +927,49 @@ static int decode_call(kvp_pool* p, int layer, const float* q, const float* k_ne
     cudaStream_t st = (cudaStream_t)stream;
     const int r = p->plan_slot_ring;
     KV_CUDA(cudaStreamWaitEvent(st, p->copy_done[r], 0));
+    std::pair<cudaEvent_t, cudaEvent_t>* te = nullptr;
+    if (p->timing) {
+        if (p->tev_used == p->tev.size()) {
+            cudaEvent_t a, b;
+            KV_CUDA(cudaEventCreate(&a));
+            KV_CUDA(cudaEventCreate(&b));
+            p->tev.emplace_back(a, b);
+        }
+        te = &p->tev[p->tev_used++];
+        KV_CUDA(cudaEventRecord(te->first, st));
+    }
     KV_CUDA(launch_decode(p->pv, p->plan_view, p->plan_nitems, p->plan_npatch, layer, q, k_new, v_new, out,
                           m, l, p->plan_grid, st));
+    if (te) KV_CUDA(cudaEventRecord(te->second, st));
     KV_CUDA(cudaEventRecord(p->slot_free[r], st));
     p->plan_patched = true;
+    return KV_OK;
+}
+
+int kvp_timing_enable(kvp_pool* p, int enable) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    std::lock_guard<std::mutex> lk(p->mu);
+    if (int rc = require_device(p)) return rc;
+    p->timing = enable != 0;
+    p->tev_used = 0;
+    return KV_OK;
+}
+
+int kvp_timing_read(kvp_pool* p, double* total_ms, int* launches) {
+    if (!p || !total_ms || !launches) return fail(KV_ERR_INVAL, "NULL argument");
+    std::lock_guard<std::mutex> lk(p->mu);
+    if (int rc = require_device(p)) return rc;
+    DeviceGuard dg(p->device);
+    double tot = 0.0;
+    for (size_t i = 0; i < p->tev_used; ++i) {
+        KV_CUDA(cudaEventSynchronize(p->tev[i].second));
+        float ms = 0.f;
+        KV_CUDA(cudaEventElapsedTime(&ms, p->tev[i].first, p->tev[i].second));
+        tot += ms;
+    }
+    *total_ms = tot;
+    *launches = (int)p->tev_used;
+    p->tev_used = 0;
     return KV_OK;
 }
 
