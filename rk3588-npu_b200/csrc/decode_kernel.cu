@@ -22,9 +22,10 @@
 //              (base 2), P^T transposed in registers with movmatrix,
 //              O^T += V^T * P^T (P split hi + lo).
 // At the end of a piece the four warps' states are merged in shared memory.
-// A segment cut into pieces writes per-piece partial (m, l, o); the CTA that
-// finishes last for a segment -- found with a per-segment arrival counter,
-// no waiting -- merges them and writes the output.
+// A segment cut into pieces writes per-piece partial (m, l, o); a small
+// combine kernel, launched behind the decode grid with programmatic
+// dependent launch (resident early, released when the grid completes),
+// merges each split segment's pieces with one round of loads.
 //
 // The new token: the consumer that owns the block holding position kv_len-1
 // rotates k (non-fused fp32, cos/sin from the host-built table), encodes k
@@ -64,8 +65,6 @@ struct Smem {
     WorkItem items[kMaxCtaItems];     // this CTA's pieces
     int cum[kMaxCtaItems + 1];        // flat block offset of each piece
     int ok[kMaxCtaItems];             // piece passed the checks
-    int last[kMaxCtaItems];           // this CTA merges the piece's segment
-    float segM[kMaxGroup];            // final merge: running per-head max
     // q fragments (hi, lo) of the first kQPre pieces, as each lane holds them
     uint32_t qfrag[kQPre][2][8][2][32];
     uint64_t full[kStages];
@@ -204,7 +203,8 @@ __device__ __forceinline__ void consume_block(uint32_t sK, uint32_t sV, int vali
     const int g = lane >> 2;
     const int mi = lane >> 3, r = lane & 7;
     // ---- S^T[16 tokens][8 heads] = K[16][128] * Qs^T ----
-    float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+    // Four independent accumulator chains (hi/lo x even/odd k-steps).
+    float sa[2][4] = {}, sb[2][4] = {};
     {
         const int t = (mi & 1) * 8 + r;
         const uint32_t rowb = sK + (uint32_t)t * 128u;
@@ -214,13 +214,13 @@ __device__ __forceinline__ void consume_block(uint32_t sK, uint32_t sV, int vali
             const uint32_t addr = rowb + (uint32_t)(cidx >> 3) * 2048u + (uint32_t)(((cidx & 7) ^ r) << 4);
             uint32_t a0, a1, a2, a3;
             ldsm_x4(addr, a0, a1, a2, a3);
-            mma16816<DT>(sa, a0, a1, a2, a3, qh[kk][0], qh[kk][1]);
-            mma16816<DT>(sb, a0, a1, a2, a3, ql[kk][0], ql[kk][1]);
+            mma16816<DT>(sa[kk & 1], a0, a1, a2, a3, qh[kk][0], qh[kk][1]);
+            mma16816<DT>(sb[kk & 1], a0, a1, a2, a3, ql[kk][0], ql[kk][1]);
         }
     }
     float s[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) s[e] = sa[e] + sb[e];
+    for (int e = 0; e < 4; ++e) s[e] = (sa[0][e] + sa[1][e]) + (sb[0][e] + sb[1][e]);
     if (g >= valid) s[0] = s[1] = -INFINITY;
     if (g + 8 >= valid) s[2] = s[3] = -INFINITY;
     // ---- online softmax, per head column (2c, 2c+1) ----
@@ -271,83 +271,6 @@ __device__ __forceinline__ void consume_block(uint32_t sK, uint32_t sV, int vali
 
 }  // namespace
 
-// Final merge of a split segment, run by the CTA that finished it last.
-// Pieces are taken 8 at a time and each group costs one L2 round trip: the
-// group's m and l go to shared memory and every thread's o values (8 pieces
-// x all heads, for its output dim) to registers, all loads issued together;
-// then per-head maxima (threads 0..7) and an online log-sum-exp update.
-__device__ __forceinline__ void merge_segment(const PoolView& pv, Smem& sm, const WorkItem& wi,
-                                              float* out, float* m_out, float* l_out, int tid) {
-    constexpr int kGroupPieces = 8;
-    const int G = pv.group;
-    const int n = wi.seg_n;
-    const float* p0 = pv.partials + (size_t)wi.seg_first * kPartialFloats;
-    float* Wm = &sm.merge_o[0][0][0];          // [8 pieces][8 heads]
-    float* Wl = Wm + kGroupPieces * kMaxGroup;
-    const int d = tid;
-    float M[kMaxGroup], L[kMaxGroup], A[kMaxGroup];
-#pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h) {
-        M[h] = -INFINITY;
-        L[h] = A[h] = 0.f;
-    }
-    for (int c0 = 0; c0 < n; c0 += kGroupPieces) {
-        const int cn = min(kGroupPieces, n - c0);
-        const float* pg = p0 + (size_t)c0 * kPartialFloats;
-        if (tid < kGroupPieces * kMaxGroup) {
-            const int u = tid >> 3, h = tid & 7;
-            const bool live = u < cn && h < G;
-            Wm[tid] = live ? __ldcg(pg + (size_t)u * kPartialFloats + h) : 0.f;
-            Wl[tid] = live ? __ldcg(pg + (size_t)u * kPartialFloats + kMaxGroup + h) : 0.f;
-        }
-        float v[kGroupPieces][kMaxGroup];
-#pragma unroll
-        for (int u = 0; u < kGroupPieces; ++u)
-#pragma unroll
-            for (int h = 0; h < kMaxGroup; ++h)
-                v[u][h] = (u < cn && h < G)
-                              ? __ldcg(pg + (size_t)u * kPartialFloats + 2 * kMaxGroup + h * kHeadDim + d)
-                              : 0.f;
-        named_bar_sync(1, kConsumerWarps * 32);
-        if (tid < kMaxGroup) {
-            float mx = -INFINITY;
-            for (int u = 0; u < cn; ++u)
-                if (Wl[u * kMaxGroup + tid] > 0.f) mx = fmaxf(mx, Wm[u * kMaxGroup + tid]);
-            sm.segM[tid] = mx;
-        }
-        named_bar_sync(1, kConsumerWarps * 32);
-#pragma unroll
-        for (int h = 0; h < kMaxGroup; ++h) {
-            const float Mg = sm.segM[h];
-            if (Mg == -INFINITY) continue;  // nothing in this group for head h
-            const float Mn = fmaxf(M[h], Mg);
-            const float r = fast_exp2(M[h] - Mn);  // 0 while M is -inf
-            float a = 0.f, l = 0.f;
-#pragma unroll
-            for (int u = 0; u < kGroupPieces; ++u) {
-                const float lu = Wl[u * kMaxGroup + h];
-                const float w = lu > 0.f ? lu * fast_exp2(Wm[u * kMaxGroup + h] - Mn) : 0.f;
-                a += w * v[u][h];
-                l += w;
-            }
-            A[h] = A[h] * r + a;
-            L[h] = L[h] * r + l;
-            M[h] = Mn;
-        }
-        named_bar_sync(1, kConsumerWarps * 32);  // scratch reused by the next group
-    }
-    const int qrow = wi.slot * pv.q_heads + wi.head * G;
-#pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h) {
-        if (h >= G) break;
-        out[(size_t)(qrow + h) * kHeadDim + d] = L[h] > 0.f ? A[h] / L[h] : 0.f;
-        if (m_out != nullptr && d == 0) {
-            m_out[qrow + h] = M[h] * 0.6931471805599453f;
-            l_out[qrow + h] = L[h];
-        }
-    }
-}
-
 template <int DT>
 __global__ void __launch_bounds__(kThreads, 2)
     decode_kernel(PoolView pv, PlanView plan, int layer, const float* __restrict__ q,
@@ -356,6 +279,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     extern __shared__ uint8_t smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // The combine kernel may be scheduled now; it waits for this grid.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const PlanHeader hdr = *plan.hdr;
 
     // Block-table entries allocated by this step's plan.  No launch reads an
@@ -415,7 +340,6 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         sm.items[j] = w;
         sm.ok[j] = !bad;
-        sm.last[j] = 0;
     }
     if (tid == 0) {
         sm.failed = 0;
@@ -597,27 +521,57 @@ __global__ void __launch_bounds__(kThreads, 2)
             }
         }
     }
+}
 
-    // ---- split segments: counted once, after all of this CTA's pieces, one
-    // thread per piece.  The barrier orders every thread's partial stores
-    // before the counting thread's acquire-release increment (release); the
-    // thread that completes a count has acquired all earlier increments'
-    // partials, and the barrier passes that on.  The CTA that completes a
-    // segment's count merges that segment.
-    named_bar_sync(1, kConsumerWarps * 32);
-    if (tid < n) {
-        const WorkItem& w = sm.items[tid];
-        int last = 0;
-        if (sm.ok[tid] && w.seg_n > 1)
-            last = atomic_add_acq_rel_gpu(&pv.counters[w.slot * pv.kv_heads + w.head], 1) == w.seg_n - 1;
-        sm.last[tid] = last;
+// Merge of the pieces of every split segment, one CTA per (segment, query
+// head), one thread per output dim.  Launched right behind the decode grid
+// with programmatic dependent launch: its CTAs become resident early and
+// block in griddepcontrol.wait until the decode grid has completed and its
+// partial stores are visible.  Pieces are taken 8 at a time, each group's
+// loads (m, l, o of 8 pieces) issued together, merged with an online
+// log-sum-exp.
+__global__ void __launch_bounds__(kHeadDim)
+    combine_kernel(PoolView pv, PlanView plan, int nsplits, float* __restrict__ out,
+                   float* __restrict__ m_out, float* __restrict__ l_out) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int G = pv.group;
+    const int si = blockIdx.x / G, h = blockIdx.x % G;
+    if (si >= nsplits) return;
+    const SplitSeg sg = plan.splits[si];
+    if (sg.slot < 0 || sg.slot >= plan.hdr->nslots || sg.head < 0 || sg.head >= pv.kv_heads ||
+        sg.seg_first < 0 || sg.seg_n < 1 || sg.seg_first + sg.seg_n > pv.max_items) {
+        if (threadIdx.x == 0) report(pv, 5, si, 400);
+        return;
     }
-    named_bar_sync(1, kConsumerWarps * 32);
-    for (int j = 0; j < n; ++j) {
-        if (!sm.last[j]) continue;
-        const WorkItem wi = sm.items[j];
-        merge_segment(pv, sm, wi, out, m_out, l_out, tid);
-        if (tid == 0) pv.counters[wi.slot * pv.kv_heads + wi.head] = 0;
+    const int d = threadIdx.x;
+    const float* p0 = pv.partials + (size_t)sg.seg_first * kPartialFloats;
+    float M = -INFINITY, L = 0.f, A = 0.f;
+    for (int c0 = 0; c0 < sg.seg_n; c0 += 8) {
+        float mm[8], ll[8], oo[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const bool live = c0 + u < sg.seg_n;
+            const float* pc = p0 + (size_t)(c0 + u) * kPartialFloats;
+            mm[u] = live ? __ldcg(pc + h) : 0.f;
+            ll[u] = live ? __ldcg(pc + kMaxGroup + h) : 0.f;
+            oo[u] = live ? __ldcg(pc + 2 * kMaxGroup + h * kHeadDim + d) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            if (!(ll[u] > 0.f)) continue;  // empty piece: no weight
+            const float Mn = fmaxf(M, mm[u]);
+            const float a = fast_exp2(M - Mn);  // 0 while M is -inf
+            const float e = ll[u] * fast_exp2(mm[u] - Mn);
+            A = A * a + e * oo[u];
+            L = L * a + e;
+            M = Mn;
+        }
+    }
+    const int row = sg.slot * pv.q_heads + sg.head * G + h;
+    out[(size_t)row * kHeadDim + d] = L > 0.f ? A / L : 0.f;
+    if (m_out != nullptr && d == 0) {
+        m_out[row] = M * 0.6931471805599453f;
+        l_out[row] = L;
     }
 }
 
@@ -630,18 +584,28 @@ cudaError_t decode_occupancy(int* ctas_per_sm) {
     return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, decode_kernel<0>, kThreads, smem);
 }
 
-cudaError_t launch_decode(const PoolView& pv, const PlanView& plan, int nitems, int npatch,
-                          int layer, const float* q, const float* k_new, const float* v_new,
-                          float* out, float* m_out, float* l_out, int grid, cudaStream_t st) {
-    (void)nitems;
-    (void)npatch;
+cudaError_t launch_decode(const PoolView& pv, const PlanView& plan, int nsplits, int layer,
+                          const float* q, const float* k_new, const float* v_new, float* out,
+                          float* m_out, float* l_out, int grid, cudaStream_t st) {
     const int smem = (int)sizeof(Smem) + 1024;
     if (grid < 1) grid = 1;
     if (pv.dtype == 0)
         decode_kernel<0><<<grid, kThreads, smem, st>>>(pv, plan, layer, q, k_new, v_new, out, m_out, l_out);
     else
         decode_kernel<1><<<grid, kThreads, smem, st>>>(pv, plan, layer, q, k_new, v_new, out, m_out, l_out);
-    return cudaGetLastError();
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || nsplits == 0) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(nsplits * pv.group));
+    cfg.blockDim = dim3(kHeadDim);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, combine_kernel, pv, plan, nsplits, out, m_out, l_out);
 }
 
 }  // namespace kvattn

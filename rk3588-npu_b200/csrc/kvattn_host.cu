@@ -119,7 +119,7 @@ struct kvp_pool {
     bool plan_active = false;
     bool plan_patched = false;
     int plan_slot_ring = 0;
-    int plan_nslots = 0, plan_nitems = 0, plan_npatch = 0, plan_grid = 0;
+    int plan_nslots = 0, plan_nitems = 0, plan_npatch = 0, plan_grid = 0, plan_nsplits = 0;
     PlanView plan_view{};
     std::vector<int> plan_seqs;
     std::vector<int> plan_append;
@@ -237,19 +237,20 @@ int check_seq(const kvp_pool* p, int seq) {
 // Byte layout of one packed plan: header, slots, items, patches, CTA
 // descriptors, tile list.
 struct PlanLayout {
-    size_t slots, items, patches, cta, tiles, bytes;
+    size_t slots, items, patches, cta, tiles, splits, bytes;
 };
 
 size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
 
-PlanLayout plan_layout(int nslots, long nitems, int npatch, long grid, long ntiles) {
+PlanLayout plan_layout(int nslots, long nitems, int npatch, long grid, long ntiles, long nsplits) {
     PlanLayout L;
     L.slots = align16(sizeof(PlanHeader));
     L.items = align16(L.slots + (size_t)nslots * sizeof(DecodeSlot));
     L.patches = align16(L.items + (size_t)nitems * sizeof(WorkItem));
     L.cta = align16(L.patches + (size_t)npatch * sizeof(TablePatch));
     L.tiles = align16(L.cta + (size_t)grid * sizeof(CtaDesc));
-    L.bytes = align16(L.tiles + (size_t)ntiles * sizeof(int));
+    L.splits = align16(L.tiles + (size_t)ntiles * sizeof(int));
+    L.bytes = align16(L.splits + (size_t)nsplits * sizeof(SplitSeg));
     return L;
 }
 
@@ -361,7 +362,8 @@ int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, in
         p->num_sms = 148;
         p->occupancy = 3;
         p->max_tiles = ((long)num_blocks + max_seqs) * num_kv_heads;
-        p->plan_bytes = plan_layout(max_seqs, p->max_items, max_seqs, p->max_items, p->max_tiles).bytes;
+        p->plan_bytes = plan_layout(max_seqs, p->max_items, max_seqs, p->max_items, p->max_tiles,
+                                 (long)max_seqs * num_kv_heads).bytes;
         p->h_plan[0] = (uint8_t*)malloc(p->plan_bytes);
         if (!p->h_plan[0]) {
             delete p;
@@ -403,7 +405,8 @@ int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, in
     KV_CUDA_B(cudaEventCreateWithFlags(&p->pending_evt, cudaEventDisableTiming));
 
     p->max_tiles = ((long)num_blocks + max_seqs) * num_kv_heads;
-    p->plan_bytes = plan_layout(max_seqs, p->max_items, max_seqs, p->max_items, p->max_tiles).bytes;
+    p->plan_bytes = plan_layout(max_seqs, p->max_items, max_seqs, p->max_items, p->max_tiles,
+                                 (long)max_seqs * num_kv_heads).bytes;
     KV_CUDA_B(cudaStreamCreateWithFlags(&p->copy_stream, cudaStreamNonBlocking));
     for (int i = 0; i < kRing; ++i) {
         KV_CUDA_B(cudaMallocHost((void**)&p->h_plan[i], p->plan_bytes));
@@ -831,9 +834,14 @@ int attn_decode_plan_ex(kvp_pool* p, int nseq, const int* seq_ids, const int* ro
     }
     if ((long)tiles.size() > p->max_tiles)
         return fail(KV_ERR_STATE, "tile list overflow (%zu > %ld)", tiles.size(), p->max_tiles);
+    std::vector<SplitSeg> splits;
+    for (size_t x = 0; x < items.size(); ++x)
+        if (items[x].seg_n > 1 && (int)x == items[x].seg_first)
+            splits.push_back(SplitSeg{items[x].slot, items[x].head, items[x].seg_first, items[x].seg_n});
 
     // ---- pack and upload once, on the copy stream ----
-    const PlanLayout L = plan_layout(nseq, (long)items.size(), (int)patches.size(), grid, (long)tiles.size());
+    const PlanLayout L = plan_layout(nseq, (long)items.size(), (int)patches.size(), grid, (long)tiles.size(),
+                                     (long)splits.size());
     PlanHeader* hdr = (PlanHeader*)h;
     hdr->nslots = nseq;
     hdr->nitems = (int)items.size();
@@ -845,11 +853,14 @@ int attn_decode_plan_ex(kvp_pool* p, int nseq, const int* seq_ids, const int* ro
     hdr->off_cta = (int)L.cta;
     hdr->off_tiles = (int)L.tiles;
     hdr->ntiles = (int)tiles.size();
+    hdr->off_splits = (int)L.splits;
+    hdr->nsplits = (int)splits.size();
     memcpy(h + L.slots, slots.data(), slots.size() * sizeof(DecodeSlot));
     memcpy(h + L.items, items.data(), items.size() * sizeof(WorkItem));
     if (!patches.empty()) memcpy(h + L.patches, patches.data(), patches.size() * sizeof(TablePatch));
     memcpy(h + L.cta, ctas.data(), ctas.size() * sizeof(CtaDesc));
     if (!tiles.empty()) memcpy(h + L.tiles, tiles.data(), tiles.size() * sizeof(int));
+    if (!splits.empty()) memcpy(h + L.splits, splits.data(), splits.size() * sizeof(SplitSeg));
 
     p->plan_active = true;
     p->plan_patched = patches.empty();
@@ -865,6 +876,8 @@ int attn_decode_plan_ex(kvp_pool* p, int nseq, const int* seq_ids, const int* ro
     p->plan_view.patches = (const TablePatch*)(base + L.patches);
     p->plan_view.cta = (const CtaDesc*)(base + L.cta);
     p->plan_view.tiles = (const int*)(base + L.tiles);
+    p->plan_view.splits = (const SplitSeg*)(base + L.splits);
+    p->plan_nsplits = (int)splits.size();
     p->plan_stream = st;
     if (p->host_only) {
         p->plan_patched = true;
@@ -938,8 +951,8 @@ static int decode_call(kvp_pool* p, int layer, const float* q, const float* k_ne
         te = &p->tev[p->tev_used++];
         KV_CUDA(cudaEventRecord(te->first, st));
     }
-    KV_CUDA(launch_decode(p->pv, p->plan_view, p->plan_nitems, p->plan_npatch, layer, q, k_new, v_new, out,
-                          m, l, p->plan_grid, st));
+    KV_CUDA(launch_decode(p->pv, p->plan_view, p->plan_nsplits, layer, q, k_new, v_new, out, m, l,
+                          p->plan_grid, st));
     if (te) KV_CUDA(cudaEventRecord(te->second, st));
     KV_CUDA(cudaEventRecord(p->slot_free[r], st));
     p->plan_patched = true;

@@ -74,6 +74,15 @@ struct CtaDesc {
 // CtaDesc per CTA, and the tile list: for every flat block of every CTA (in
 // CTA order) the tile index block * kv_heads + head to copy, or -1 for a
 // block that holds only the new token (nothing to load).
+// A segment cut into several pieces: its partial states are merged by the
+// combine kernel into the outputs of (slot, head).
+struct SplitSeg {
+    int slot;
+    int head;
+    int seg_first;
+    int seg_n;
+};
+
 struct PlanHeader {
     int nslots;
     int nitems;
@@ -85,7 +94,8 @@ struct PlanHeader {
     int off_cta;
     int off_tiles;
     int ntiles;
-    int pad[2];
+    int off_splits;
+    int nsplits;
 };
 
 // Device view of the pool handed to kernels by value.
@@ -117,12 +127,13 @@ struct PlanView {
     const TablePatch* patches;
     const CtaDesc* cta;
     const int* tiles;
+    const SplitSeg* splits;
 };
 
 // ---- launchers (kernels.cu) ----
-cudaError_t launch_decode(const PoolView& pv, const PlanView& plan, int nitems, int npatch,
-                          int layer, const float* q, const float* k_new, const float* v_new,
-                          float* out, float* m_out, float* l_out, int grid, cudaStream_t st);
+cudaError_t launch_decode(const PoolView& pv, const PlanView& plan, int nsplits, int layer,
+                          const float* q, const float* k_new, const float* v_new, float* out,
+                          float* m_out, float* l_out, int grid, cudaStream_t st);
 cudaError_t decode_occupancy(int* ctas_per_sm);
 cudaError_t launch_import(const PoolView& pv, int layer, int seq, int pos0, int n,
                           const uint16_t* k_rows, const uint16_t* v_rows, cudaStream_t st);
