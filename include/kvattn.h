@@ -181,6 +181,26 @@ int attn_decode_commit(kvp_pool* pool);
 int attn_combine_lse(int G, int rows, int dim, const float* m, const float* l, const float* o,
                      float* out, void* stream);
 
+/* Attention for callers that cannot allocate device memory (a host that
+ * owns all GPU memory in its own arena and forbids plugin allocations, or a
+ * decode loop that may not call into the allocator).  It creates no pool and
+ * calls no cudaMalloc/cudaFree: split-KV partial states go to a fixed
+ * file-scope device array of 4 MiB that every GPU loading this library holds
+ * until the process exits.  No counterpart in the reference; it has
+ * op_attention's semantics (worker/src/ops/op_attention.cpp:9-56) on device
+ * pointers: q [seq][n_heads*128] fp32 already rotated, contiguous caches
+ * [total_len][n_kv_heads*128] of `dtype`, causal mask from pos_base, out
+ * [seq][n_heads*128] fp32.  Limit: seq * n_kv_heads <= 1008 (else
+ * KV_ERR_RANGE).  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress) with that device current, so make that first
+ * call before any stream capture.  All calls share the array: calls that
+ * overlap on the GPU (concurrent streams) race and must be serialised by the
+ * caller; nothing in it needs clearing, every value read is written first
+ * in the same call. */
+int attn_contig_noalloc(const float* q, const void* k_cache, const void* v_cache, float* out,
+                        int seq, int total_len, int n_heads, int n_kv_heads, int head_dim,
+                        int pos_base, int dtype, void* stream);
+
 /* Device status word of the pool: 0, or KV_ERR_TIMEOUT if a kernel's
  * bounded wait gave up.  Synchronises `stream`; clears the word. */
 int kvp_device_status(kvp_pool* pool, void* stream, int* status);

@@ -60,6 +60,7 @@ _SIGS = {
     "kvp_plan_cta_start": [_vp, _ip, C.c_int],
     "kvp_launch_info": [_vp, _ip, _ip],
     "kvp_timing_enable": [_vp, C.c_int],
+    "attn_contig_noalloc": [_vp, _vp, _vp, _vp] + [C.c_int] * 7 + [_vp],
     "kvp_timing_read": [_vp, C.POINTER(C.c_double), _ip],
 }
 _RESTYPE = {"kv_last_error": C.c_char_p, "kv_status_str": C.c_char_p, "kv_version": C.c_char_p}
