@@ -224,6 +224,31 @@ int kvp_timing_read(kvp_pool* pool, double* total_ms, int* launches);
 /* Number of SMs and of resident decode CTAs per SM used for grid sizing. */
 int kvp_launch_info(const kvp_pool* pool, int* num_sms, int* ctas_per_sm);
 
+/* ---- Placement of requests onto GPUs --------------------------------------
+ * No counterpart in the reference: its engine runs one sequence on one
+ * device (worker/src/engine/llm_engine.cpp:68-98).  A request is placed
+ * whole on the GPU holding the fewest resident KV blocks among those with
+ * room for it (ties: lowest index); its blocks are counted as
+ * ceil(tokens / block_tokens).  The state is plain host data: every process
+ * that makes the same calls in the same order reaches the same placement,
+ * so a scheduler replicated on every rank needs no communication.  Calls on
+ * one scheduler are serialised internally.  Request ids are the caller's.
+ * An OOM (no GPU has room) changes nothing. */
+typedef struct kvs_sched kvs_sched;
+
+int kvs_create(int n_gpus, int block_tokens, const long long* blocks_per_gpu, kvs_sched** out);
+int kvs_destroy(kvs_sched* s);
+/* Place a new request that needs `tokens` tokens of cache; *gpu = its GPU. */
+int kvs_place(kvs_sched* s, long long request, int tokens, int* gpu);
+/* The request now needs `tokens` tokens (growth by decode, or a prefill
+ * chunk); KV_ERR_OOM if its GPU has no room for the extra blocks. */
+int kvs_resize(kvs_sched* s, long long request, int tokens);
+/* The request completed: its blocks leave its GPU's load. */
+int kvs_release(kvs_sched* s, long long request);
+int kvs_gpu_of(const kvs_sched* s, long long request, int* gpu);
+/* Resident blocks and requests of one GPU (either pointer may be NULL). */
+int kvs_load(const kvs_sched* s, int gpu, long long* resident_blocks, int* resident_requests);
+
 #ifdef __cplusplus
 }
 #endif

@@ -8,7 +8,8 @@ Python.  There is no fallback: if the library is missing, ``load()`` raises.
 Reference interfaces mirrored (Bobchasm/rk3588-npu):
   KVCache        worker/include/model/kv_cache.h:19-41  -> Pool + sequences
   op_rope + append loop + op_attention
-                 worker/src/model/qwen2_model.cpp:180-206 -> Pool.decode_step
+                 worker/src/model/qwen2_model.cpp:180-206 -> Pool.plan / decode_layer / commit
+  (no counterpart) placement of requests onto GPUs      -> Scheduler
 """
 from __future__ import annotations
 
@@ -62,6 +63,13 @@ _SIGS = {
     "kvp_timing_enable": [_vp, C.c_int],
     "attn_contig_noalloc": [_vp, _vp, _vp, _vp] + [C.c_int] * 7 + [_vp],
     "kvp_timing_read": [_vp, C.POINTER(C.c_double), _ip],
+    "kvs_create": [C.c_int, C.c_int, C.POINTER(C.c_longlong), C.POINTER(_vp)],
+    "kvs_destroy": [_vp],
+    "kvs_place": [_vp, C.c_longlong, C.c_int, _ip],
+    "kvs_resize": [_vp, C.c_longlong, C.c_int],
+    "kvs_release": [_vp, C.c_longlong],
+    "kvs_gpu_of": [_vp, C.c_longlong, _ip],
+    "kvs_load": [_vp, C.c_int, C.POINTER(C.c_longlong), _ip],
 }
 _RESTYPE = {"kv_last_error": C.c_char_p, "kv_status_str": C.c_char_p, "kv_version": C.c_char_p}
 
@@ -294,3 +302,50 @@ def combine_lse(m, l, o, out, stream=None) -> None:
     """out[rows, dim] = LSE merge of G partial states m, l [G, rows], o [G, rows, dim]."""
     G, rows, dim = o.shape
     call("attn_combine_lse", G, rows, dim, _ptr(m), _ptr(l), _ptr(o), _ptr(out), _stream(stream))
+
+
+class Scheduler:
+    """Placement of requests onto GPUs by resident KV blocks (kvs_* C ABI).
+
+    Deterministic: ranks that make the same calls in the same order agree
+    on every placement without communicating."""
+
+    def __init__(self, blocks_per_gpu, block_tokens: int = BLOCK_TOKENS):
+        L = load()
+        caps = (C.c_longlong * len(blocks_per_gpu))(*[int(b) for b in blocks_per_gpu])
+        h = _vp()
+        _check(L.kvs_create(len(blocks_per_gpu), block_tokens, caps, C.byref(h)), "kvs_create")
+        self.h = h
+        self.n_gpus = len(blocks_per_gpu)
+
+    def close(self) -> None:
+        if self.h:
+            _check(_lib.kvs_destroy(self.h), "kvs_destroy")
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def place(self, request: int, tokens: int) -> int:
+        g = C.c_int()
+        call("kvs_place", self.h, request, tokens, C.byref(g))
+        return g.value
+
+    def resize(self, request: int, tokens: int) -> None:
+        call("kvs_resize", self.h, request, tokens)
+
+    def release(self, request: int) -> None:
+        call("kvs_release", self.h, request)
+
+    def gpu_of(self, request: int) -> int:
+        g = C.c_int()
+        call("kvs_gpu_of", self.h, request, C.byref(g))
+        return g.value
+
+    def load(self, gpu: int) -> tuple[int, int]:
+        b, n = C.c_longlong(), C.c_int()
+        call("kvs_load", self.h, gpu, C.byref(b), C.byref(n))
+        return b.value, n.value

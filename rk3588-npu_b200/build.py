@@ -2,7 +2,8 @@
 
 Usage: python rk3588-npu_b200/build.py [--force]
 
-Sources: csrc/*.cu (kernels + host runtime + C ABI).  Output:
+Sources: csrc/*.cu (kernels + host runtime + C ABI) and csrc/*.cpp (host-only
+C ABI parts, compiled through nvcc's host compiler).  Output:
 lib/libkvattn.so next to this file.  cudart is linked statically, so the
 library needs only the CUDA driver at run time; streams and device pointers
 from any other runtime in the process (e.g. torch's) are interchangeable
@@ -28,7 +29,7 @@ FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O2", "--expt-re
 
 
 def sources() -> list[str]:
-    return sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+    return sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
 
 
 def _deps() -> list[str]:

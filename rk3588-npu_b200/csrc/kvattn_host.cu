@@ -38,6 +38,12 @@ int fail(int status, const char* fmt, ...) {
     return status;
 }
 
+}  // namespace
+
+int kvattn::set_error(int status, const char* msg) { return fail(status, "%s", msg); }
+
+namespace {
+
 int cuda_fail(cudaError_t e, const char* what) {
     return fail(KV_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }

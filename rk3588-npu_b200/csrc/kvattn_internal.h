@@ -146,4 +146,7 @@ cudaError_t launch_patch(const PoolView& pv, const TablePatch* patches, int npat
 cudaError_t launch_combine(int G, int rows, int dim, const float* m, const float* l,
                            const float* o, float* out, cudaStream_t st);
 
+// Sets the calling thread's kv_last_error() message; returns `status`.
+int set_error(int status, const char* msg);
+
 }  // namespace kvattn
