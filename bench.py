@@ -1,18 +1,27 @@
 """Decode hot-path benchmark: KV append + GQA decode attention on B200.
 
-Workload (the one the headline metric is quoted on, one GPU): batch 32,
-per-sequence context lengths uniform in [256, 4096] (seed 1), fp16 KV cache
-with values N(0,1), Q [32,12,128] / new K,V [32,2,128] per step, one layer,
-Qwen2-1.5B head shapes (12 query heads share 2 KV heads, head_dim 128),
-softmax scale 1/sqrt(128).  A step appends one token to every sequence and
-attends over its whole context.  Synthetic seeded data; the 72 MB working
+Default workload (the one the headline metric is quoted on, one GPU): batch
+32, per-sequence context lengths uniform in [256, 4096] (seed 1), fp16 KV
+cache with values N(0,1), Q [32,12,128] / new K,V [32,2,128] per step, one
+layer, Qwen2-1.5B head shapes (12 query heads share 2 KV heads, head_dim
+128), softmax scale 1/sqrt(128).  A step appends one token to every sequence
+and attends over its whole context.  Synthetic seeded data; the 72 MB working
 set fits in the 126 MB L2, so L2 is flushed (256 MiB write) before every
 timed step and the flush is kept out of the step's events.
 
+--workload paged28: 256 sequences, lengths lognormal (median 2048, sigma 0.8)
+capped at 32768 (seed 2), block tables a random permutation (seed 2) of a
+pool sized to 1.1x the blocks the contexts need, bf16 KV N(0,1), all 28
+layers per step (one plan, 28 decode launches, one commit).  The ~20 GB read
+per step is far larger than L2, so no flush is needed.  --workload paged1 is
+the same sequences with one layer (the size of one of those launches), for
+profiling.
+
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload batch32|paged28|paged1]
 
 N > 1 is launched by torchrun, one process per GPU; every rank owns its own
-32 sequences (placement by request, no collective on the data path: weak
+sequences (placement by request, no collective on the data path: weak
 scaling); timing is the max over ranks of device-event time.
 """
 from __future__ import annotations
@@ -32,10 +41,54 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 PKG_DIR = os.path.join(ROOT, "rk3588-npu_b200")
 
 METRIC = "decode attention tokens/s and achieved HBM GB/s vs B200 peak at 1/2/4/8 GPUs"
-B, NQ, NKV, HD = 32, 12, 2, 128
+NQ, NKV, HD = 12, 2, 128
 KVD = NKV * HD
 HID = NQ * HD
 FLUSH_BYTES = 256 << 20
+
+
+class Workload:
+    """One bench workload: the sequences a GPU holds and how a step runs."""
+
+    def __init__(self, name, batch, layers, dtype, lens, perm_seed, flush, desc, data, profile):
+        self.name, self.batch, self.layers, self.dtype = name, batch, layers, dtype
+        self.lens, self.perm_seed, self.flush = lens, perm_seed, flush
+        self.desc, self.data, self.profile = desc, data, profile
+
+    @property
+    def dtype_name(self) -> str:
+        return "f16" if self.dtype == 0 else "bf16"
+
+
+def uniform_lengths(n=32, seed=1) -> list[int]:
+    return [int(x) for x in np.random.default_rng(seed).integers(256, 4097, n)]
+
+
+def lognormal_lengths(n=256, seed=2) -> list[int]:
+    """Lognormal context lengths, median 2048, sigma 0.8, capped at 32768."""
+    x = np.random.default_rng(seed).lognormal(np.log(2048.0), 0.8, n)
+    return [int(min(32768, max(1, round(v)))) for v in x]
+
+
+def make_workload(name: str) -> Workload:
+    if name == "batch32":
+        return Workload(
+            "batch32", 32, 1, 0, uniform_lengths(), None, True,
+            "decode step: KV append + GQA decode attention, batch 32 per GPU, context U[256,4096], "
+            "12 q / 2 kv heads x 128, fp16 KV, 1 layer",
+            "synthetic (seeded N(0,1) K/V/q; context lengths U[256,4096] seed 1)",
+            "decode_kernel_b32_ncu.txt")
+    if name in ("paged28", "paged1"):
+        layers = 28 if name == "paged28" else 1
+        return Workload(
+            name, 256, layers, 1, lognormal_lengths(), 2, False,
+            f"paged decode step: block gather + KV append + GQA decode attention over {layers} "
+            "layer(s), 256 sequences per GPU, context lognormal(median 2048, sigma 0.8) capped at "
+            "32768, block tables a random permutation of a pool of 1.1x the needed blocks, "
+            "12 q / 2 kv heads x 128, bf16 KV",
+            "synthetic (seeded N(0,1) K/V/q; lognormal context lengths and block permutation seed 2)",
+            "decode_kernel_paged256_ncu.txt")
+    raise ValueError(f"unknown workload {name}")
 
 
 def parse_args():
@@ -44,6 +97,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["batch32", "paged28", "paged1"], default="batch32")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--settle", type=float, default=1.0,
@@ -68,10 +122,6 @@ def dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     return rank, world, local
-
-
-def context_lengths() -> list[int]:
-    return [int(x) for x in np.random.default_rng(1).integers(256, 4097, B)]
 
 
 def step_bytes(kv_lens) -> float:
@@ -168,10 +218,10 @@ def peak_hbm():
         return 6650.0, "fallback"
 
 
-def ncu_traffic():
+def ncu_traffic(profile: str):
     """Per-launch DRAM bytes of the decode kernel from the committed ncu
-    summary (profiles/decode_kernel_b32_ncu.txt, line `traffic_bytes_per_launch:`)."""
-    path = os.path.join(ROOT, "profiles", "decode_kernel_b32_ncu.txt")
+    summary of the workload (line `traffic_bytes_per_launch:`)."""
+    path = os.path.join(ROOT, "profiles", profile)
     try:
         for line in open(path):
             if line.startswith("traffic_bytes_per_launch:"):
@@ -181,20 +231,41 @@ def ncu_traffic():
     return None
 
 
-def setup_pool(kv, torch, dev, lens, steps_total, seed):
-    nb = sum(-(-(L + steps_total + 1) // 16) for L in lens) + 64
-    P = kv.Pool(dev, 1, nb, num_q_heads=NQ, num_kv_heads=NKV, dtype=kv.KV_F16, max_seqs=B,
-                max_seq_len=max(lens) + steps_total + 32)
+def setup_pool(kv, torch, dev, wl: Workload, steps_total: int, seed: int):
+    """A pool holding the workload's contexts in every layer.  Permuted
+    workloads take a pool of 1.1x the blocks the contexts need and hand each
+    sequence consecutive runs of a seeded random permutation of its block
+    ids; the rest stay free for the blocks appended tokens open."""
+    need = [-(-L // 16) for L in wl.lens]
+    grow = [-(-(L + steps_total + 1) // 16) - n for L, n in zip(wl.lens, need)]
+    if wl.perm_seed is None:
+        nb = sum(need) + sum(grow) + 64
+    else:
+        nb = max(-(-sum(need) * 11 // 10), sum(need) + sum(grow) + 64)
+    P = kv.Pool(dev, wl.layers, nb, num_q_heads=NQ, num_kv_heads=NKV, dtype=wl.dtype,
+                max_seqs=wl.batch, max_seq_len=max(wl.lens) + steps_total + 32)
+    ids = [P.seq_alloc() for _ in wl.lens]
+    if wl.perm_seed is None:
+        for s, L in zip(ids, wl.lens):
+            P.reserve(s, L)
+    else:
+        perm = np.random.default_rng(wl.perm_seed).permutation(nb)
+        o = 0
+        for s, n in zip(ids, need):
+            P.set_blocks(s, perm[o:o + n].tolist())
+            o += n
     g = torch.Generator(device="cuda").manual_seed(seed)
-    ids = []
-    for L in lens:
-        s = P.seq_alloc()
-        P.reserve(s, L)
-        k = encode_device(torch.randn((L, KVD), generator=g, device="cuda"), 0)
-        v = encode_device(torch.randn((L, KVD), generator=g, device="cuda"), 0)
-        P.import_rows(0, s, 0, k, v)
+    total = sum(wl.lens)
+    for layer in range(wl.layers):
+        k_all = encode_device(torch.randn((total, KVD), generator=g, device="cuda"), wl.dtype)
+        v_all = encode_device(torch.randn((total, KVD), generator=g, device="cuda"), wl.dtype)
+        o = 0
+        for s, L in zip(ids, wl.lens):
+            P.import_rows(layer, s, 0, k_all[o:o + L], v_all[o:o + L])
+            o += L
+        del k_all, v_all
+    for s, L in zip(ids, wl.lens):
         P.set_cur_pos(s, L)
-        ids.append(s)
     torch.cuda.synchronize()
     return P, ids
 
@@ -210,20 +281,22 @@ def run_ours(args, rank, world, local):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
-    lens = context_lengths()
+    wl = make_workload(args.workload)
+    B, NL, lens = wl.batch, wl.layers, wl.lens
     K, W = args.steps, args.warmup
-    P, ids = setup_pool(kv, torch, local, lens, K + W + 2, seed=1 + rank)
+    P, ids = setup_pool(kv, torch, local, wl, K + W + 10, seed=1 + rank)
     g = torch.Generator(device="cuda").manual_seed(100 + rank)
     nsteps = W + K
-    q = torch.randn((nsteps, B, HID), generator=g, device="cuda")
-    kn = torch.randn((nsteps, B, KVD), generator=g, device="cuda")
-    vn = torch.randn((nsteps, B, KVD), generator=g, device="cuda")
-    out = torch.empty((B, HID), device="cuda")
+    q = torch.randn((nsteps, NL, B, HID), generator=g, device="cuda")
+    kn = torch.randn((nsteps, NL, B, KVD), generator=g, device="cuda")
+    vn = torch.randn((nsteps, NL, B, KVD), generator=g, device="cuda")
+    out = torch.empty((NL, B, HID), device="cuda")
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.int32, device="cuda")
 
     def step(i):
         P.plan(ids)
-        P.decode_layer(0, q[i], kn[i], vn[i], out)
+        for layer in range(NL):
+            P.decode_layer(layer, q[i, layer], kn[i, layer], vn[i, layer], out[layer])
         P.commit()
 
     def reset_lens():
@@ -231,19 +304,23 @@ def run_ours(args, rank, world, local):
         for s, L in zip(ids, lens):
             P.set_cur_pos(s, L)
 
+    def maybe_flush():
+        if wl.flush:
+            flush.zero_()
+
     sampler = ClockSampler(range(local, local + 1)) if rank == 0 else None
     if sampler:
         sampler.start()
     for i in range(W):
-        flush.zero_()
+        maybe_flush()
         step(i)
     # Keep the GPU loaded ~1 s so the clock samples reflect load; lengths
     # are put back afterwards so the timed steps see the stated contexts.
     t_end = time.time() + args.settle
     while time.time() < t_end:
         for i in range(8):
-            flush.zero_()
-            step(i)
+            maybe_flush()
+            step(i % nsteps)
         reset_lens()
         torch.cuda.synchronize()
     reset_lens()
@@ -261,21 +338,20 @@ def run_ours(args, rank, world, local):
             raise kv.KVError(rc, fn, L.kv_last_error().decode())
 
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
-    qp = [q[W + i].data_ptr() for i in range(K)]
-    kp = [kn[W + i].data_ptr() for i in range(K)]
-    vp = [vn[W + i].data_ptr() for i in range(K)]
-    outp = out.data_ptr()
+    ptrs = [[(q[W + i, y].data_ptr(), kn[W + i, y].data_ptr(), vn[W + i, y].data_ptr(),
+              out[y].data_ptr()) for y in range(NL)] for i in range(K)]
     kv_lens_per_step = [[Ln + 1 + i for Ln in lens] for i in range(K)]
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
     P.timing(True)
     for i in range(K):
-        flush.zero_()
+        maybe_flush()
         e0, e1 = ev[i]
         e0.record()
         chk(L.attn_decode_plan(h, nseq, ids_c, st), "attn_decode_plan")
-        chk(L.attn_decode_append(h, 0, qp[i], kp[i], vp[i], outp, st), "attn_decode_append")
+        for y, (qa, ka, va, oa) in enumerate(ptrs[i]):
+            chk(L.attn_decode_append(h, y, qa, ka, va, oa, st), "attn_decode_append")
         chk(L.attn_decode_commit(h), "attn_decode_commit")
         e1.record()
     torch.cuda.synchronize()
@@ -285,33 +361,38 @@ def run_ours(args, rank, world, local):
     kern_ms, launches = P.timing_read()
     P.timing(False)
     clocks = sampler.stop() if sampler else None
-    assert launches == K
+    assert launches == K * NL
     assert P.device_status() == 0, "device-side check failed: " + L.kv_last_error().decode()
 
     # ---- e2e: host buffers, copies inside the timed region ----
+    # Every step copies its q / k / v for all layers from pinned host memory
+    # and reads all layers' outputs back; at most 8 distinct host input sets
+    # are kept and cycled.
     reset_lens()
-    qh = q[W:].cpu().pin_memory()
-    kh = kn[W:].cpu().pin_memory()
-    vh = vn[W:].cpu().pin_memory()
-    oh = torch.empty((K, B, HID)).pin_memory()
-    qd = torch.empty((B, HID), device="cuda")
-    kd = torch.empty((B, KVD), device="cuda")
-    vd = torch.empty((B, KVD), device="cuda")
+    R = min(K, 8)
+    qh = q[W:W + R].cpu().pin_memory()
+    kh = kn[W:W + R].cpu().pin_memory()
+    vh = vn[W:W + R].cpu().pin_memory()
+    oh = torch.empty((R, NL, B, HID)).pin_memory()
+    qd = torch.empty((NL, B, HID), device="cuda")
+    kd = torch.empty((NL, B, KVD), device="cuda")
+    vd = torch.empty((NL, B, KVD), device="cuda")
+    dptr = [(qd[y].data_ptr(), kd[y].data_ptr(), vd[y].data_ptr(), out[y].data_ptr()) for y in range(NL)]
     e2e_ms = 0.0
     if dist:
         dist.barrier()
     for i in range(K):
-        flush.zero_()
+        maybe_flush()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        qd.copy_(qh[i], non_blocking=True)
-        kd.copy_(kh[i], non_blocking=True)
-        vd.copy_(vh[i], non_blocking=True)
+        qd.copy_(qh[i % R], non_blocking=True)
+        kd.copy_(kh[i % R], non_blocking=True)
+        vd.copy_(vh[i % R], non_blocking=True)
         chk(L.attn_decode_plan(h, nseq, ids_c, st), "attn_decode_plan")
-        chk(L.attn_decode_append(h, 0, qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), outp, st),
-            "attn_decode_append")
+        for y, (qa, ka, va, oa) in enumerate(dptr):
+            chk(L.attn_decode_append(h, y, qa, ka, va, oa, st), "attn_decode_append")
         chk(L.attn_decode_commit(h), "attn_decode_commit")
-        oh[i].copy_(out, non_blocking=True)
+        oh[i % R].copy_(out, non_blocking=True)
         b.record()
         b.synchronize()  # the caller waits for its result
         e2e_ms += a.elapsed_time(b)
@@ -322,11 +403,11 @@ def run_ours(args, rank, world, local):
     if dist:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
     step_ms, kern_ms, e2e_ms = times.tolist()
-    # one fused decode kernel per step (table patches ride in it), counted by the library
+    # one fused decode kernel per layer (table patches ride in it), counted by the library
     if rank == 0:
-        alg = sum(step_bytes(kl) for kl in kv_lens_per_step) / K
+        alg = sum(step_bytes(kl) for kl in kv_lens_per_step) / K  # per launch
         peak, peak_kind = peak_hbm()
-        achieved = alg / (kern_ms / K * 1e-3) / 1e9
+        achieved = alg / (kern_ms / (K * NL) * 1e-3) / 1e9
         line = {
             "metric": METRIC,
             "value": round(world * B * K / (step_ms * 1e-3), 1),
@@ -338,25 +419,26 @@ def run_ours(args, rank, world, local):
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": "f16",
-            "data": "synthetic (seeded N(0,1) K/V/q; context lengths U[256,4096] seed 1)",
-            "config": {"workload": "decode step: KV append + GQA decode attention, batch 32 per GPU, "
-                                   "context U[256,4096], 12 q / 2 kv heads x 128, fp16 KV, 1 layer",
-                       "batch_per_gpu": B, "layers": 1, "kv_dtype": "f16", "block_tokens": 16,
+            "dtype": wl.dtype_name,
+            "data": wl.data,
+            "config": {"workload": wl.desc, "name": wl.name,
+                       "batch_per_gpu": B, "layers": NL, "kv_dtype": wl.dtype_name, "block_tokens": 16,
                        "parallelism": f"request placement x{world} (no data-path collective)",
-                       "l2": "flushed before every timed step (256 MiB write), flush outside events"},
-            "hbm_gbs_step": round(alg / (step_ms / K * 1e-3) / 1e9, 1),
+                       "l2": ("flushed before every timed step (256 MiB write), flush outside events"
+                              if wl.flush else "inputs larger than L2 (no flush)")},
+            "hbm_gbs_step": round(alg * NL / (step_ms / K * 1e-3) / 1e9, 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": ncu_traffic(), "peak_source": peak_kind,
-                         "kernel_ms": round(kern_ms / K, 5), "algorithmic_bytes": round(alg)},
+                         "traffic": ncu_traffic(wl.profile), "peak_source": peak_kind,
+                         "kernel_ms": round(kern_ms / (K * NL), 5), "algorithmic_bytes": round(alg)},
             "e2e": {"value": round(world * B * K / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
-                    "h2d_bytes_per_step": 4 * B * (HID + 2 * KVD), "d2h_bytes_per_step": 4 * B * HID},
+                    "h2d_bytes_per_step": 4 * NL * B * (HID + 2 * KVD),
+                    "d2h_bytes_per_step": 4 * NL * B * HID},
             "gpu_launches": int(launches),
             "clocks": clocks,
         }
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(lens, args.cpu_seconds)
+            line["cpu_baseline"] = cpu_baseline(wl, args.cpu_seconds)
         print(json.dumps(line), flush=True)
     P.close()
     if dist:
@@ -399,59 +481,81 @@ def cpu_step_fn(orc, threads):
     return "port", port
 
 
-def cpu_baseline(lens, seconds):
+def cpu_sample(wl: Workload, nseq: int):
+    """The first `nseq` sequences of the workload, one layer, and the factor
+    that scales a step over them to a full step of the workload (all its
+    sequences' tokens, all its layers)."""
+    lens = wl.lens[:nseq]
+    return lens, wl.layers * sum(wl.lens) / sum(lens)
+
+
+CPU_DTYPE_NOTE = ("the reference CPU path keeps fp16 caches (its only cache type); "
+                  "bf16 workloads are timed on it at the same sizes in fp16")
+
+
+def cpu_baseline(wl: Workload, seconds):
     """Single-thread CPU sample of the same workload (rank 0, N=1 only)."""
     orc = _oracle()
     kind, fn = cpu_step_fn(orc, 1)
     max_steps = 64
+    lens, scale = cpu_sample(wl, 32)
+    n = len(lens)
     kcs, vcs, rng = cpu_workload(orc, lens, max_steps + 1)
     pos = list(lens)
     t0 = time.perf_counter()
     steps = 0
     while steps < max_steps and (steps == 0 or time.perf_counter() - t0 < seconds):
-        q = rng.standard_normal((B, HID), dtype=np.float32)
-        k = rng.standard_normal((B, KVD), dtype=np.float32)
-        v = rng.standard_normal((B, KVD), dtype=np.float32)
+        q = rng.standard_normal((n, HID), dtype=np.float32)
+        k = rng.standard_normal((n, KVD), dtype=np.float32)
+        v = rng.standard_normal((n, KVD), dtype=np.float32)
         fn(q, k, v, kcs, vcs, pos)
         pos = [p + 1 for p in pos]
         steps += 1
     dt = time.perf_counter() - t0
-    return {"value": round(B * steps / dt, 2), "unit": "tokens/s", "cores": 1, "kind": kind,
-            "sample": f"{steps} full decode steps of the 32-sequence workload on 1 host thread "
-                      f"({dt:.1f} s)"}
+    full_step = dt / steps * scale
+    sample = (f"{steps} decode steps of {n} of the workload's {wl.batch} sequences, 1 layer, "
+              f"1 host thread ({dt:.1f} s), scaled x{scale:.2f} to a full step")
+    if wl.dtype != 0:
+        sample += "; " + CPU_DTYPE_NOTE
+    return {"value": round(wl.batch / full_step, 3), "unit": "tokens/s", "cores": 1, "kind": kind,
+            "sample": sample}
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return
     orc = _oracle()
-    threads = max(1, min(os.cpu_count() or 1, B))
+    wl = make_workload(args.workload)
+    threads = max(1, min(os.cpu_count() or 1, wl.batch))
     kind, fn = cpu_step_fn(orc, threads)
-    lens = context_lengths()
+    lens, scale = cpu_sample(wl, min(wl.batch, max(32, threads)))
+    n = len(lens)
     K, W = args.steps, args.warmup
     kcs, vcs, rng = cpu_workload(orc, lens, K + W + 1)
     pos = list(lens)
     total = 0.0
     for i in range(W + K):
-        q = rng.standard_normal((B, HID), dtype=np.float32)
-        k = rng.standard_normal((B, KVD), dtype=np.float32)
-        v = rng.standard_normal((B, KVD), dtype=np.float32)
+        q = rng.standard_normal((n, HID), dtype=np.float32)
+        k = rng.standard_normal((n, KVD), dtype=np.float32)
+        v = rng.standard_normal((n, KVD), dtype=np.float32)
         t0 = time.perf_counter()
         fn(q, k, v, kcs, vcs, pos)
         dt = time.perf_counter() - t0
         if i >= W:
-            total += dt
+            total += dt * scale
         pos = [p + 1 for p in pos]
-    value = round(B * K / total, 2)
-    sample = (f"{K} timed decode steps of the 32-sequence workload, {threads} host threads taking "
-              f"whole sequences, {'reference functions compiled from source' if kind == 'reference' else 'C restatement'}")
+    value = round(wl.batch * K / total, 3)
+    sample = (f"{K} timed decode steps over {n} of the workload's {wl.batch} sequences, 1 layer, "
+              f"{threads} host threads taking whole sequences, scaled x{scale:.2f} to a full step, "
+              f"{'reference functions compiled from source' if kind == 'reference' else 'C restatement'}")
+    if wl.dtype != 0:
+        sample += "; " + CPU_DTYPE_NOTE
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(total / K * 1e3, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
-            "data": "synthetic (seeded N(0,1); context lengths U[256,4096] seed 1)",
-            "config": {"workload": "decode step: KV append + GQA decode attention, batch 32, "
-                                   "context U[256,4096], 12 q / 2 kv heads x 128, fp16 KV, 1 layer",
-                       "batch_per_gpu": B, "layers": 1, "kv_dtype": "f16"},
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": wl.dtype_name, "data": wl.data,
+            "config": {"workload": wl.desc, "name": wl.name, "batch_per_gpu": wl.batch,
+                       "layers": wl.layers, "kv_dtype": wl.dtype_name},
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": kind,
                              "sample": sample},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
