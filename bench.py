@@ -88,6 +88,15 @@ def make_workload(name: str) -> Workload:
             "12 q / 2 kv heads x 128, bf16 KV",
             "synthetic (seeded N(0,1) K/V/q; lognormal context lengths and block permutation seed 2)",
             "decode_kernel_paged256_ncu.txt")
+    if name in ("long1", "long4"):
+        b = 1 if name == "long1" else 4
+        return Workload(
+            name, b, 28, 1, [131072] * b, None, False,
+            f"long-context decode step: batch {b}, context 131072 per sequence split along the "
+            "sequence across the GPUs (contiguous slices), 28 layers, bf16 KV; per layer partial "
+            "(m, l, o) per GPU, NCCL all-gather, log-sum-exp combine",
+            "synthetic (seeded N(0,1) K/V/q, seed 3)",
+            "decode_kernel_long_ncu.txt")
     raise ValueError(f"unknown workload {name}")
 
 
@@ -97,7 +106,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["batch32", "paged28", "paged1"], default="batch32")
+    ap.add_argument("--workload", choices=["batch32", "paged28", "paged1", "long1", "long4"],
+                    default="batch32")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--settle", type=float, default=1.0,
@@ -345,6 +355,7 @@ def run_ours(args, rank, world, local):
         dist.barrier()
     torch.cuda.synchronize()
     P.timing(True)
+    kc0 = kv.kernel_count()
     for i in range(K):
         maybe_flush()
         e0, e1 = ev[i]
@@ -355,6 +366,7 @@ def run_ours(args, rank, world, local):
         chk(L.attn_decode_commit(h), "attn_decode_commit")
         e1.record()
     torch.cuda.synchronize()
+    kernels = kv.kernel_count() - kc0
     if dist:
         dist.barrier()
     step_ms = sum(a.elapsed_time(b) for a, b in ev)
@@ -403,7 +415,7 @@ def run_ours(args, rank, world, local):
     if dist:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
     step_ms, kern_ms, e2e_ms = times.tolist()
-    # one fused decode kernel per layer (table patches ride in it), counted by the library
+    # decode kernel per layer (+ its split combine), counted by the library
     if rank == 0:
         alg = sum(step_bytes(kl) for kl in kv_lens_per_step) / K  # per launch
         peak, peak_kind = peak_hbm()
@@ -434,7 +446,174 @@ def run_ours(args, rank, world, local):
             "e2e": {"value": round(world * B * K / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": 4 * NL * B * (HID + 2 * KVD),
                     "d2h_bytes_per_step": 4 * NL * B * HID},
-            "gpu_launches": int(launches),
+            "gpu_launches": int(kernels),
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(wl, args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    P.close()
+    if dist:
+        dist.destroy_process_group()
+
+
+def run_long(args, rank, world, local):
+    """A few long sequences split along the sequence across the GPUs: every
+    rank holds a contiguous 1/world of each context in its own pool; per layer
+    partial states, an NCCL all-gather and a log-sum-exp combine (strong
+    scaling: the total work is fixed as the GPU count grows)."""
+    import torch
+    kv = load_pkg()
+    kv.load()
+    from importlib import import_module
+    splitkv = import_module("rk3588_npu_b200.splitkv")
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    wl = make_workload(args.workload)
+    B, NL = wl.batch, wl.layers
+    K, W = args.steps, args.warmup
+    extra = K + W + 16
+    lo, hi = splitkv.slice_bounds(wl.lens[0], rank, world)
+    n_loc = hi - lo
+    nb = B * (-(-(n_loc + extra) // 16)) + 16
+    P = kv.Pool(local, NL, nb, num_q_heads=NQ, num_kv_heads=NKV, dtype=wl.dtype, max_seqs=B,
+                max_seq_len=wl.lens[0] + extra + 32)
+    S = splitkv.SplitKV(P, wl.lens, rank, world)
+    S.reserve(extra)
+    g = torch.Generator(device="cuda").manual_seed(3 + 1000 * rank)
+    for layer in range(NL):
+        for i in range(B):
+            k = encode_device(torch.randn((n_loc, KVD), generator=g, device="cuda"), wl.dtype)
+            v = encode_device(torch.randn((n_loc, KVD), generator=g, device="cuda"), wl.dtype)
+            S.load_slice(layer, i, k, v)
+    torch.cuda.synchronize()
+    # q / k / v of a step are the same on every rank (seeded alike)
+    gq = torch.Generator(device="cuda").manual_seed(103)
+    R = min(K + W, 16)
+    q = torch.randn((R, NL, B, HID), generator=gq, device="cuda")
+    kn = torch.randn((R, NL, B, KVD), generator=gq, device="cuda")
+    vn = torch.randn((R, NL, B, KVD), generator=gq, device="cuda")
+    out = torch.empty((NL, B, HID), device="cuda")
+
+    def step(i, qs=None, ks=None, vs=None):
+        qs = q[i % R] if qs is None else qs
+        ks = kn[i % R] if ks is None else ks
+        vs = vn[i % R] if vs is None else vs
+        S.begin_step()
+        for y in range(NL):
+            S.layer(y, qs[y], ks[y], vs[y], out[y])
+        S.end_step()
+
+    sampler = ClockSampler(range(local, local + 1)) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    for i in range(W):
+        step(i)
+    # ~settle seconds of load (the same number of steps on every rank)
+    torch.cuda.synchronize()
+    t0 = time.time()
+    step(0)
+    torch.cuda.synchronize()
+    n_settle = int(args.settle / max(time.time() - t0, 1e-4))
+    n_settle = torch.tensor([n_settle], device="cuda")
+    if dist:
+        dist.all_reduce(n_settle, op=dist.ReduceOp.MIN)
+    for i in range(int(n_settle.item())):
+        step(i)
+        if (i + 1) % 8 == 0:
+            torch.cuda.synchronize()
+            S.rewind()
+    torch.cuda.synchronize()
+    S.rewind()
+
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    P.timing(True)
+    kc0 = kv.kernel_count()
+    for i in range(K):
+        e0, e1 = ev[i]
+        e0.record()
+        step(W + i)
+        e1.record()
+    torch.cuda.synchronize()
+    kernels = kv.kernel_count() - kc0
+    if dist:
+        dist.barrier()
+    step_ms = sum(a.elapsed_time(b) for a, b in ev)
+    kern_ms, launches = P.timing_read()
+    P.timing(False)
+    clocks = sampler.stop() if sampler else None
+    assert launches == K * NL
+    assert P.device_status() == 0, "device-side check failed: " + kv._lib.kv_last_error().decode()
+
+    # ---- e2e: host inputs per step, outputs read back ----
+    S.rewind()
+    qh = q[:1].cpu().pin_memory()
+    kh = kn[:1].cpu().pin_memory()
+    vh = vn[:1].cpu().pin_memory()
+    oh = torch.empty((NL, B, HID)).pin_memory()
+    qd, kd, vd = torch.empty_like(q[0]), torch.empty_like(kn[0]), torch.empty_like(vn[0])
+    e2e_ms = 0.0
+    if dist:
+        dist.barrier()
+    for i in range(K):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        qd.copy_(qh[0], non_blocking=True)
+        kd.copy_(kh[0], non_blocking=True)
+        vd.copy_(vh[0], non_blocking=True)
+        step(i, qd, kd, vd)
+        oh.copy_(out, non_blocking=True)
+        b.record()
+        b.synchronize()
+        e2e_ms += a.elapsed_time(b)
+    if dist:
+        dist.barrier()
+
+    times = torch.tensor([step_ms, kern_ms, e2e_ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    step_ms, kern_ms, e2e_ms = times.tolist()
+    if rank == 0:
+        # per-GPU bytes of one decode launch (rank 0's slice; the last rank's
+        # differs by one appended token per sequence)
+        alg = step_bytes([n_loc] * B)
+        peak, peak_kind = peak_hbm()
+        achieved = alg / (kern_ms / (K * NL) * 1e-3) / 1e9
+        line = {
+            "metric": METRIC,
+            "value": round(B * K / (step_ms * 1e-3), 2),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": K,
+            "warmup": W,
+            "ms_per_step": round(step_ms / K, 5),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": wl.dtype_name,
+            "data": wl.data,
+            "config": {"workload": wl.desc, "name": wl.name, "batch": B, "context": wl.lens[0],
+                       "layers": NL, "kv_dtype": wl.dtype_name, "block_tokens": 16,
+                       "parallelism": f"sequence split x{world} (NCCL all-gather of partial states)",
+                       "l2": "inputs larger than L2 (no flush)"},
+            "hbm_gbs_step": round(world * alg * NL / (step_ms / K * 1e-3) / 1e9, 1),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": ncu_traffic(wl.profile), "peak_source": peak_kind,
+                         "kernel_ms": round(kern_ms / (K * NL), 5), "algorithmic_bytes": round(alg),
+                         "per": "GPU (its slice)"},
+            "e2e": {"value": round(B * K / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 4 * NL * B * (HID + 2 * KVD),
+                    "d2h_bytes_per_step": 4 * NL * B * HID},
+            "gpu_launches": int(kernels),
             "clocks": clocks,
         }
         if world == 1 and not args.no_cpu_baseline:
@@ -552,7 +731,8 @@ def run_reference(args, rank, world):
         sample += "; " + CPU_DTYPE_NOTE
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(total / K * 1e3, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True,
+            "scaling": "strong" if wl.name.startswith("long") else "weak", "vs_baseline": None,
             "dtype": wl.dtype_name, "data": wl.data,
             "config": {"workload": wl.desc, "name": wl.name, "batch_per_gpu": wl.batch,
                        "layers": wl.layers, "kv_dtype": wl.dtype_name},
@@ -567,6 +747,8 @@ def main():
     rank, world, local = dist_env()
     if args.impl == "reference":
         run_reference(args, rank, world)
+    elif args.workload.startswith("long"):
+        run_long(args, rank, world, local)
     else:
         run_ours(args, rank, world, local)
 

@@ -62,6 +62,9 @@ enum kv_dtype { KV_F16 = 0, KV_BF16 = 1 };
 
 /* Message for the calling thread's last non-OK status ("" if none). */
 const char* kv_last_error(void);
+/* Process-wide number of CUDA kernels this library has launched (every
+ * entry point that launches counts its kernels). */
+int kv_kernel_count(long long* n);
 /* Static name of a status code. */
 const char* kv_status_str(int status);
 /* Library version, "major.minor.patch". */
@@ -180,6 +183,11 @@ int attn_decode_commit(kvp_pool* pool);
  * No reference counterpart (the reference has no split-KV). */
 int attn_combine_lse(int G, int rows, int dim, const float* m, const float* l, const float* o,
                      float* out, void* stream);
+/* The same merge over the packed buffer an all-gather of per-rank states
+ * yields: packed [G][rows*(2+dim)], rank g's part laid out as
+ * [m rows][l rows][o rows x dim].  No reference counterpart. */
+int attn_combine_lse_packed(int G, int rows, int dim, const float* packed, float* out,
+                            void* stream);
 
 /* Attention for callers that cannot allocate device memory (a host that
  * owns all GPU memory in its own arena and forbids plugin allocations, or a

@@ -34,6 +34,7 @@ _SIGS = {
     "kv_last_error": [],
     "kv_status_str": [C.c_int],
     "kv_version": [],
+    "kv_kernel_count": [C.POINTER(C.c_longlong)],
     "kvp_create": [C.c_int] * 10 + [C.c_float, C.POINTER(_vp)],
     "kvp_destroy": [_vp],
     "kvp_reset": [_vp, _vp],
@@ -56,6 +57,7 @@ _SIGS = {
     "attn_decode_append_partial": [_vp, C.c_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
     "attn_decode_commit": [_vp],
     "attn_combine_lse": [C.c_int, C.c_int, C.c_int, _vp, _vp, _vp, _vp, _vp],
+    "attn_combine_lse_packed": [C.c_int, C.c_int, C.c_int, _vp, _vp, _vp],
     "kvp_device_status": [_vp, _vp, _ip],
     "kvp_plan_info": [_vp, _ip, _ip, _ip, _ip, _ip, _ip, _ip, C.c_int],
     "kvp_plan_cta_start": [_vp, _ip, C.c_int],
@@ -298,10 +300,24 @@ class Pool:
         return s.value
 
 
+def kernel_count() -> int:
+    """Kernels the library has launched in this process so far."""
+    n = C.c_longlong()
+    call("kv_kernel_count", C.byref(n))
+    return n.value
+
+
 def combine_lse(m, l, o, out, stream=None) -> None:
     """out[rows, dim] = LSE merge of G partial states m, l [G, rows], o [G, rows, dim]."""
     G, rows, dim = o.shape
     call("attn_combine_lse", G, rows, dim, _ptr(m), _ptr(l), _ptr(o), _ptr(out), _stream(stream))
+
+
+def combine_lse_packed(packed, rows, out, stream=None) -> None:
+    """The same merge over packed [G, rows*(2+dim)] rows of [m | l | o]."""
+    G = packed.shape[0]
+    dim = packed.shape[1] // rows - 2
+    call("attn_combine_lse_packed", G, rows, dim, _ptr(packed), _ptr(out), _stream(stream))
 
 
 class Scheduler:

@@ -11,7 +11,7 @@
 // equal run of that flat block sequence; a segment crossing a CTA boundary
 // becomes several pieces.  Per CTA:
 //   warp 4     producer: lane l < 8 owns ring stage l and issues 1-D bulk
-//              async copies (TMA engine, no multicast) of the K and V tiles
+//              async copies (TMA engine, into this CTA only) of the K and V tiles
 //              (4 KiB each, contiguous in HBM) of flat blocks l, l+8, ...; the
 //              eight lanes run in step, so one instruction issues up to eight
 //              stages, and each lane fetches its next block id a round ahead;
@@ -524,54 +524,93 @@ __global__ void __launch_bounds__(kThreads, 2)
 }
 
 // Merge of the pieces of every split segment, one CTA per (segment, query
-// head), one thread per output dim.  Launched right behind the decode grid
-// with programmatic dependent launch: its CTAs become resident early and
-// block in griddepcontrol.wait until the decode grid has completed and its
-// partial stores are visible.  Pieces are taken 8 at a time, each group's
-// loads (m, l, o of 8 pieces) issued together, merged with an online
-// log-sum-exp.
-__global__ void __launch_bounds__(kHeadDim)
+// head).  Launched right behind the decode grid with programmatic dependent
+// launch: its CTAs become resident early (a 4-warp one fits beside two decode
+// CTAs on an SM), read their segment descriptor -- the plan was uploaded
+// before the decode grid started -- and block in griddepcontrol.wait until
+// the decode grid has completed and its partial stores are visible.  Warp w
+// takes pieces w, w+W, ... eight at a time (all their loads issued together;
+// lane l holds dims 4l..4l+3), merging with an online log-sum-exp; the W
+// warps' states are then merged in shared memory.  A segment of P pieces
+// costs ceil(P / 8W) load rounds: W = 4 normally, 16 when a segment has
+// more than 64 pieces (a few very long contexts over the whole GPU).
+template <int kCombineWarps>
+__global__ void __launch_bounds__(kCombineWarps * 32)
     combine_kernel(PoolView pv, PlanView plan, int nsplits, float* __restrict__ out,
                    float* __restrict__ m_out, float* __restrict__ l_out) {
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    static_assert(kCombineWarps * 32 >= kHeadDim, "the final merge maps one thread to each dim");
+    __shared__ float s_m[kCombineWarps], s_l[kCombineWarps];
+    __shared__ __align__(16) float s_o[kCombineWarps][kHeadDim];
     const int G = pv.group;
     const int si = blockIdx.x / G, h = blockIdx.x % G;
-    if (si >= nsplits) return;
-    const SplitSeg sg = plan.splits[si];
-    if (sg.slot < 0 || sg.slot >= plan.hdr->nslots || sg.head < 0 || sg.head >= pv.kv_heads ||
-        sg.seg_first < 0 || sg.seg_n < 1 || sg.seg_first + sg.seg_n > pv.max_items) {
-        if (threadIdx.x == 0) report(pv, 5, si, 400);
-        return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    SplitSeg sg = {};
+    bool ok = si < nsplits;
+    if (ok) {
+        sg = plan.splits[si];
+        if (sg.slot < 0 || sg.slot >= plan.hdr->nslots || sg.head < 0 || sg.head >= pv.kv_heads ||
+            sg.seg_first < 0 || sg.seg_n < 1 || sg.seg_first + sg.seg_n > pv.max_items) {
+            if (threadIdx.x == 0) report(pv, 5, si, 400);
+            ok = false;
+        }
     }
-    const int d = threadIdx.x;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (!ok) return;
     const float* p0 = pv.partials + (size_t)sg.seg_first * kPartialFloats;
-    float M = -INFINITY, L = 0.f, A = 0.f;
-    for (int c0 = 0; c0 < sg.seg_n; c0 += 8) {
-        float mm[8], ll[8], oo[8];
+    float M = -INFINITY, L = 0.f;
+    float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int c0 = warp; c0 < sg.seg_n; c0 += 8 * kCombineWarps) {
+        float mm[8], ll[8];
+        float4 oo[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-            const bool live = c0 + u < sg.seg_n;
-            const float* pc = p0 + (size_t)(c0 + u) * kPartialFloats;
-            mm[u] = live ? __ldcg(pc + h) : 0.f;
-            ll[u] = live ? __ldcg(pc + kMaxGroup + h) : 0.f;
-            oo[u] = live ? __ldcg(pc + 2 * kMaxGroup + h * kHeadDim + d) : 0.f;
+            const int pc = c0 + u * kCombineWarps;
+            const bool live = pc < sg.seg_n;
+            const float* pp = p0 + (size_t)pc * kPartialFloats;
+            mm[u] = live ? __ldcg(pp + h) : 0.f;
+            ll[u] = live ? __ldcg(pp + kMaxGroup + h) : 0.f;
+            oo[u] = live ? __ldcg(reinterpret_cast<const float4*>(pp + 2 * kMaxGroup + h * kHeadDim) + lane)
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-            if (!(ll[u] > 0.f)) continue;  // empty piece: no weight
+            if (!(ll[u] > 0.f)) continue;  // empty piece (or past the end): no weight
             const float Mn = fmaxf(M, mm[u]);
             const float a = fast_exp2(M - Mn);  // 0 while M is -inf
             const float e = ll[u] * fast_exp2(mm[u] - Mn);
-            A = A * a + e * oo[u];
+            A.x = A.x * a + e * oo[u].x;
+            A.y = A.y * a + e * oo[u].y;
+            A.z = A.z * a + e * oo[u].z;
+            A.w = A.w * a + e * oo[u].w;
             L = L * a + e;
             M = Mn;
         }
     }
+    if (lane == 0) {
+        s_m[warp] = M;
+        s_l[warp] = L;
+    }
+    reinterpret_cast<float4*>(s_o[warp])[lane] = A;
+    __syncthreads();
+    const int d = threadIdx.x;  // 0..127: one output dim per thread
+    if (d >= kHeadDim) return;
+    float Mt = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kCombineWarps; ++w)
+        if (s_l[w] > 0.f) Mt = fmaxf(Mt, s_m[w]);
+    float Lt = 0.f, At = 0.f;
+#pragma unroll
+    for (int w = 0; w < kCombineWarps; ++w) {
+        if (!(s_l[w] > 0.f)) continue;
+        const float f = fast_exp2(s_m[w] - Mt);
+        Lt += s_l[w] * f;
+        At += s_o[w][d] * f;
+    }
     const int row = sg.slot * pv.q_heads + sg.head * G + h;
-    out[(size_t)row * kHeadDim + d] = L > 0.f ? A / L : 0.f;
+    out[(size_t)row * kHeadDim + d] = Lt > 0.f ? At / Lt : 0.f;
     if (m_out != nullptr && d == 0) {
-        m_out[row] = M * 0.6931471805599453f;
-        l_out[row] = L;
+        m_out[row] = Mt * 0.6931471805599453f;
+        l_out[row] = Lt;
     }
 }
 
@@ -584,20 +623,21 @@ cudaError_t decode_occupancy(int* ctas_per_sm) {
     return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, decode_kernel<0>, kThreads, smem);
 }
 
-cudaError_t launch_decode(const PoolView& pv, const PlanView& plan, int nsplits, int layer,
-                          const float* q, const float* k_new, const float* v_new, float* out,
-                          float* m_out, float* l_out, int grid, cudaStream_t st) {
+cudaError_t launch_decode(const PoolView& pv, const PlanView& plan, int nsplits, int max_pieces,
+                          int layer, const float* q, const float* k_new, const float* v_new,
+                          float* out, float* m_out, float* l_out, int grid, cudaStream_t st) {
     const int smem = (int)sizeof(Smem) + 1024;
     if (grid < 1) grid = 1;
     if (pv.dtype == 0)
         decode_kernel<0><<<grid, kThreads, smem, st>>>(pv, plan, layer, q, k_new, v_new, out, m_out, l_out);
     else
         decode_kernel<1><<<grid, kThreads, smem, st>>>(pv, plan, layer, q, k_new, v_new, out, m_out, l_out);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = counted(cudaGetLastError());
     if (e != cudaSuccess || nsplits == 0) return e;
+    const bool wide = max_pieces > 64;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(nsplits * pv.group));
-    cfg.blockDim = dim3(kHeadDim);
+    cfg.blockDim = dim3((wide ? 16 : 4) * 32);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -605,7 +645,8 @@ cudaError_t launch_decode(const PoolView& pv, const PlanView& plan, int nsplits,
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, combine_kernel, pv, plan, nsplits, out, m_out, l_out);
+    if (wide) return counted(cudaLaunchKernelEx(&cfg, combine_kernel<16>, pv, plan, nsplits, out, m_out, l_out));
+    return counted(cudaLaunchKernelEx(&cfg, combine_kernel<4>, pv, plan, nsplits, out, m_out, l_out));
 }
 
 }  // namespace kvattn

@@ -124,7 +124,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 }
 
 // One-dimensional bulk copy global -> this CTA's shared memory, completing
-// on `bar` (no multicast).  Addresses 16-byte aligned, bytes % 16 == 0.
+// on `bar` (this CTA only).  Addresses 16-byte aligned, bytes % 16 == 0.
 __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes,
                                          uint64_t* bar) {
     asm volatile(

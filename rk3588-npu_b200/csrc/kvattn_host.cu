@@ -14,6 +14,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -41,6 +42,18 @@ int fail(int status, const char* fmt, ...) {
 }  // namespace
 
 int kvattn::set_error(int status, const char* msg) { return fail(status, "%s", msg); }
+
+namespace {
+std::atomic<long long> g_kernel_launches{0};
+}  // namespace
+
+void kvattn::count_launch() { g_kernel_launches.fetch_add(1, std::memory_order_relaxed); }
+
+int kv_kernel_count(long long* n) {
+    if (!n) return fail(KV_ERR_INVAL, "NULL argument");
+    *n = g_kernel_launches.load(std::memory_order_relaxed);
+    return KV_OK;
+}
 
 namespace {
 
@@ -126,6 +139,7 @@ struct kvp_pool {
     bool plan_patched = false;
     int plan_slot_ring = 0;
     int plan_nslots = 0, plan_nitems = 0, plan_npatch = 0, plan_grid = 0, plan_nsplits = 0;
+    int plan_max_pieces = 0;  // most pieces of one split segment
     PlanView plan_view{};
     std::vector<int> plan_seqs;
     std::vector<int> plan_append;
@@ -884,6 +898,8 @@ int attn_decode_plan_ex(kvp_pool* p, int nseq, const int* seq_ids, const int* ro
     p->plan_view.tiles = (const int*)(base + L.tiles);
     p->plan_view.splits = (const SplitSeg*)(base + L.splits);
     p->plan_nsplits = (int)splits.size();
+    p->plan_max_pieces = 0;
+    for (const SplitSeg& sg : splits) p->plan_max_pieces = std::max(p->plan_max_pieces, sg.seg_n);
     p->plan_stream = st;
     if (p->host_only) {
         p->plan_patched = true;
@@ -957,8 +973,8 @@ static int decode_call(kvp_pool* p, int layer, const float* q, const float* k_ne
         te = &p->tev[p->tev_used++];
         KV_CUDA(cudaEventRecord(te->first, st));
     }
-    KV_CUDA(launch_decode(p->pv, p->plan_view, p->plan_nsplits, layer, q, k_new, v_new, out, m, l,
-                          p->plan_grid, st));
+    KV_CUDA(launch_decode(p->pv, p->plan_view, p->plan_nsplits, p->plan_max_pieces, layer, q, k_new,
+                          v_new, out, m, l, p->plan_grid, st));
     if (te) KV_CUDA(cudaEventRecord(te->second, st));
     KV_CUDA(cudaEventRecord(p->slot_free[r], st));
     p->plan_patched = true;
@@ -1026,7 +1042,18 @@ int attn_combine_lse(int G, int rows, int dim, const float* m, const float* l, c
     if (G < 1 || rows < 0 || dim < 1) return fail(KV_ERR_INVAL, "bad sizes");
     if (rows == 0) return KV_OK;
     if (!m || !l || !o || !out) return fail(KV_ERR_INVAL, "NULL tensor");
-    KV_CUDA(launch_combine(G, rows, dim, m, l, o, out, (cudaStream_t)stream));
+    KV_CUDA(launch_combine(G, rows, dim, m, l, o, (size_t)rows, (size_t)rows * dim, out,
+                           (cudaStream_t)stream));
+    return KV_OK;
+}
+
+int attn_combine_lse_packed(int G, int rows, int dim, const float* packed, float* out, void* stream) {
+    if (G < 1 || rows < 0 || dim < 1) return fail(KV_ERR_INVAL, "bad sizes");
+    if (rows == 0) return KV_OK;
+    if (!packed || !out) return fail(KV_ERR_INVAL, "NULL tensor");
+    const size_t per = (size_t)rows * (2 + dim);
+    KV_CUDA(launch_combine(G, rows, dim, packed, packed + rows, packed + 2 * (size_t)rows, per, per,
+                           out, (cudaStream_t)stream));
     return KV_OK;
 }
 

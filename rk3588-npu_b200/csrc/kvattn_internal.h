@@ -131,9 +131,9 @@ struct PlanView {
 };
 
 // ---- launchers (kernels.cu) ----
-cudaError_t launch_decode(const PoolView& pv, const PlanView& plan, int nsplits, int layer,
-                          const float* q, const float* k_new, const float* v_new, float* out,
-                          float* m_out, float* l_out, int grid, cudaStream_t st);
+cudaError_t launch_decode(const PoolView& pv, const PlanView& plan, int nsplits, int max_pieces,
+                          int layer, const float* q, const float* k_new, const float* v_new,
+                          float* out, float* m_out, float* l_out, int grid, cudaStream_t st);
 cudaError_t decode_occupancy(int* ctas_per_sm);
 cudaError_t launch_import(const PoolView& pv, int layer, int seq, int pos0, int n,
                           const uint16_t* k_rows, const uint16_t* v_rows, cudaStream_t st);
@@ -144,9 +144,18 @@ cudaError_t launch_append_chunk(const PoolView& pv, int layer, int seq, int pos0
 cudaError_t launch_patch(const PoolView& pv, const TablePatch* patches, int npatch,
                          cudaStream_t st);
 cudaError_t launch_combine(int G, int rows, int dim, const float* m, const float* l,
-                           const float* o, float* out, cudaStream_t st);
+                           const float* o, size_t gstride_ml, size_t gstride_o, float* out,
+                           cudaStream_t st);
 
 // Sets the calling thread's kv_last_error() message; returns `status`.
 int set_error(int status, const char* msg);
+
+// Process-wide count of kernels this library launched (kv_kernel_count):
+// a launcher passes its launch's status through counted().
+void count_launch();
+inline cudaError_t counted(cudaError_t e) {
+    if (e == cudaSuccess) count_launch();
+    return e;
+}
 
 }  // namespace kvattn

@@ -192,8 +192,8 @@ extern "C" int attn_contig_noalloc(const float* q, const void* k_cache, const vo
     contig_partial_kernel<<<dim3(nsplit, n_kv_heads, seq), kWarps * 32, 0, st>>>(
         q, (const uint16_t*)k_cache, (const uint16_t*)v_cache, scratch, seq, total_len, n_heads,
         n_kv_heads, pos_base, nsplit, split_tokens, dtype);
-    if (cudaGetLastError() != cudaSuccess) return KV_ERR_CUDA;
+    if (counted(cudaGetLastError()) != cudaSuccess) return KV_ERR_CUDA;
     contig_merge_kernel<<<dim3(n_heads, seq), kHeadDim, 0, st>>>(scratch, out, n_heads, n_kv_heads, nsplit);
-    if (cudaGetLastError() != cudaSuccess) return KV_ERR_CUDA;
+    if (counted(cudaGetLastError()) != cudaSuccess) return KV_ERR_CUDA;
     return KV_OK;
 }

@@ -110,22 +110,23 @@ __global__ void patch_kernel(PoolView pv, const TablePatch* __restrict__ patches
 
 // out[r][d] = sum_g l_g e^(m_g - M) o_g[r][d] / sum_g l_g e^(m_g - M); states
 // with l == 0 (nothing attended) carry no weight.
+// Rank g's m, l and o start `gstride` floats after rank g-1's.
 __global__ void combine_kernel(int G, int rows, int dim, const float* __restrict__ m,
                                const float* __restrict__ l, const float* __restrict__ o,
-                               float* __restrict__ out) {
+                               size_t gstride_ml, size_t gstride_o, float* __restrict__ out) {
     const long total = (long)rows * dim;
     for (long x = blockIdx.x * (long)blockDim.x + threadIdx.x; x < total; x += (long)gridDim.x * blockDim.x) {
         const int r = (int)(x / dim);
         float M = -INFINITY;
         for (int g = 0; g < G; ++g)
-            if (l[(size_t)g * rows + r] > 0.f) M = fmaxf(M, m[(size_t)g * rows + r]);
+            if (l[(size_t)g * gstride_ml + r] > 0.f) M = fmaxf(M, m[(size_t)g * gstride_ml + r]);
         float L = 0.f, acc = 0.f;
         for (int g = 0; g < G; ++g) {
-            const float lg = l[(size_t)g * rows + r];
+            const float lg = l[(size_t)g * gstride_ml + r];
             if (lg > 0.f) {
-                const float w = lg * expf(m[(size_t)g * rows + r] - M);
+                const float w = lg * expf(m[(size_t)g * gstride_ml + r] - M);
                 L += w;
-                acc += w * o[(size_t)g * total + x];
+                acc += w * o[(size_t)g * gstride_o + x];
             }
         }
         out[x] = L > 0.f ? acc / L : 0.f;
@@ -156,7 +157,7 @@ cudaError_t launch_import(const PoolView& pv, int layer, int seq, int pos0, int 
     import_kernel<<<grid_for(work, 256), 256, 0, st>>>(pv, layer, seq, pos0, n,
                                                        reinterpret_cast<const uint4*>(k_rows),
                                                        reinterpret_cast<const uint4*>(v_rows));
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 cudaError_t launch_gather(const PoolView& pv, int layer, int seq, int len, uint16_t* k_rows,
@@ -165,7 +166,7 @@ cudaError_t launch_gather(const PoolView& pv, int layer, int seq, int len, uint1
     const long work = (long)len * pv.kv_heads * 32;
     gather_kernel<<<grid_for(work, 256), 256, 0, st>>>(pv, layer, seq, len, reinterpret_cast<uint4*>(k_rows),
                                                        reinterpret_cast<uint4*>(v_rows));
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 cudaError_t launch_append_chunk(const PoolView& pv, int layer, int seq, int pos0, int n,
@@ -177,21 +178,21 @@ cudaError_t launch_append_chunk(const PoolView& pv, int layer, int seq, int pos0
         append_chunk_kernel<0><<<grid, 256, 0, st>>>(pv, layer, seq, pos0, n, k, v);
     else
         append_chunk_kernel<1><<<grid, 256, 0, st>>>(pv, layer, seq, pos0, n, k, v);
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 cudaError_t launch_patch(const PoolView& pv, const TablePatch* patches, int npatch, cudaStream_t st) {
     if (npatch <= 0) return cudaSuccess;
     patch_kernel<<<grid_for(npatch, 256), 256, 0, st>>>(pv, patches, npatch);
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 cudaError_t launch_combine(int G, int rows, int dim, const float* m, const float* l, const float* o,
-                           float* out, cudaStream_t st) {
+                           size_t gstride_ml, size_t gstride_o, float* out, cudaStream_t st) {
     const long total = (long)rows * dim;
     if (total <= 0) return cudaSuccess;
-    combine_kernel<<<grid_for(total, 256), 256, 0, st>>>(G, rows, dim, m, l, o, out);
-    return cudaGetLastError();
+    combine_kernel<<<grid_for(total, 256), 256, 0, st>>>(G, rows, dim, m, l, o, gstride_ml, gstride_o, out);
+    return counted(cudaGetLastError());
 }
 
 }  // namespace kvattn

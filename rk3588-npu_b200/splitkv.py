@@ -37,6 +37,7 @@ class SplitKV:
     def __init__(self, pool: Pool, lengths, rank: int, world: int, group=None):
         self.pool, self.rank, self.world, self.group = pool, rank, world, group
         self.lengths = [int(x) for x in lengths]
+        self.initial = list(self.lengths)
         self.ids = []
         self.bounds = []
         for L in self.lengths:
@@ -80,6 +81,9 @@ class SplitKV:
     def layer(self, layer: int, q, k_new, v_new, out, stream=None) -> None:
         """One layer of the step.  q [B, q_heads*128], k/v [B, kv_heads*128]
         fp32 (the same on every rank), out [B, q_heads*128] fp32."""
+        if self.world == 1:  # the whole context is here: no partials
+            self.pool.decode_layer(layer, q, k_new, v_new, out, stream=stream)
+            return
         R = self.rows
         buf = self._buf
         m, l, o = buf[:R], buf[R:2 * R], buf[2 * R:]
@@ -88,12 +92,17 @@ class SplitKV:
             dist.all_gather_into_tensor(self._all, buf, group=self.group)
         else:  # gloo (tests on one GPU): list form
             dist.all_gather(list(self._all.unbind(0)), buf, group=self.group)
-        allm = self._all[:, :R].contiguous()
-        alll = self._all[:, R:2 * R].contiguous()
-        allo = self._all[:, 2 * R:].contiguous()
-        call("attn_combine_lse", self.world, R, HEAD_DIM, _ptr(allm), _ptr(alll), _ptr(allo),
-             _ptr(out), _stream(stream))
+        # rank g's [m | l | o] at row g of the gathered buffer
+        call("attn_combine_lse_packed", self.world, R, HEAD_DIM, _ptr(self._all), _ptr(out),
+             _stream(stream))
 
     def end_step(self) -> None:
         self.pool.commit()
         self.lengths = [L + 1 for L in self.lengths]
+
+    def rewind(self) -> None:
+        """Back to the initial contexts (drops the tokens appended since;
+        their blocks stay reserved)."""
+        self.lengths = list(self.initial)
+        for s, (lo, hi) in zip(self.ids, self.bounds):
+            self.pool.set_cur_pos(s, hi - lo)

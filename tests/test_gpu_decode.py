@@ -148,7 +148,14 @@ def test_decode_long_sequence_many_chunks(kv, orc):
     info_lens = list(H.len)
     assert H.step(check_gather=False) <= TOL
     H.P.plan(H.ids)
-    assert H.P.plan_info()["nitems"] > 2 * 8
+    info = H.P.plan_info()
+    assert info["nitems"] > 2 * 8
+    # a segment in more than 64 pieces: the step above merged it with the
+    # 16-warp combine
+    per_seg = {}
+    for slot, head, _, _ in info["items"]:
+        per_seg[(slot, head)] = per_seg.get((slot, head), 0) + 1
+    assert max(per_seg.values()) > 64
     H.P.commit()  # advances without a layer call: table entries still applied
     H.len = [L + 1 for L in H.len]
     assert H.P.cur_pos(H.ids[0]) == info_lens[0] + 2
@@ -263,6 +270,11 @@ def test_split_kv_partials_and_lse_combine(kv, orc):
     kv.combine_lse(ms, ls, os_, out)
     ref, _, _ = orc.layer_step(q, k, v, full_k, full_v, T, dtype=dtype)
     assert rel_err(out.cpu().numpy(), ref[0]) <= TOL
+    # the packed form an all-gather yields: rank g's [m | l | o] in row g
+    packed = torch.cat([ms, ls, os_.reshape(2, -1)], dim=1).contiguous()
+    out_p = torch.empty_like(out)
+    kv.combine_lse_packed(packed, 12, out_p)
+    assert torch.equal(out_p, out)
     P1, s1 = shards[1]
     kd, vd = P1.gather(0, s1)
     assert np.array_equal(kd.cpu().numpy().view(np.uint16), full_k[A:T + 1])
