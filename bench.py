@@ -70,6 +70,14 @@ def lognormal_lengths(n=256, seed=2) -> list[int]:
     return [int(min(32768, max(1, round(v)))) for v in x]
 
 
+def serve_stream(seed=4, resident=128, new=4096):
+    """Resident (context, budget) pairs, then the stream of new requests
+    (prompt, budget): contexts and prompts U[512,8192], budgets U[16,256]."""
+    rng = np.random.default_rng(seed)
+    pairs = [(int(rng.integers(512, 8193)), int(rng.integers(16, 257))) for _ in range(resident + new)]
+    return pairs[:resident], pairs[resident:]
+
+
 def make_workload(name: str) -> Workload:
     if name == "batch32":
         return Workload(
@@ -97,6 +105,15 @@ def make_workload(name: str) -> Workload:
             "(m, l, o) per GPU, NCCL all-gather, log-sum-exp combine",
             "synthetic (seeded N(0,1) K/V/q, seed 3)",
             "decode_kernel_long_ncu.txt")
+    if name == "serve":
+        return Workload(
+            "serve", 128, 28, 1, [L for L, _ in serve_stream()[0]], None, False,
+            "continuous batching: 128 resident decode sequences (context U[512,8192], generation "
+            "budget U[16,256]) plus 8 requests at a time in chunked prefill (prompt U[512,8192], "
+            "512-token chunks appended into the paged pool), completed sequences free their blocks, "
+            "requests placed by resident KV blocks across the GPUs, 28 layers, bf16 KV",
+            "synthetic (seeded N(0,1) K/V/q; request stream seed 4)",
+            "decode_kernel_paged256_ncu.txt")
     raise ValueError(f"unknown workload {name}")
 
 
@@ -106,7 +123,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["batch32", "paged28", "paged1", "long1", "long4"],
+    ap.add_argument("--workload", choices=["batch32", "paged28", "paged1", "long1", "long4", "serve"],
                     default="batch32")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -624,6 +641,149 @@ def run_long(args, rank, world, local):
         dist.destroy_process_group()
 
 
+def run_serve(args, rank, world, local):
+    """Continuous batching through serving.Server on every rank (placement
+    replicated, each rank executes its own requests; no collective on the
+    data path).  Strong scaling: the request stream is fixed."""
+    import torch
+    kv = load_pkg()
+    kv.load()
+    from importlib import import_module
+    serving = import_module("rk3588_npu_b200.serving")
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    wl = make_workload("serve")
+    NL = wl.layers
+    K, W = args.steps, args.warmup
+    residents, stream = serve_stream()
+    foot = sum(-(-(L + g) // 16) for L, g in residents) + 8 * (-(-(8192 + 256) // 16))
+    nb = int(foot * 1.3 / world) + 2048
+    P = kv.Pool(local, NL, nb, num_q_heads=NQ, num_kv_heads=NKV, dtype=wl.dtype, max_seqs=512,
+                max_seq_len=8192 + 256 + 64)
+    S = kv.Scheduler([nb] * world)
+    srv = serving.Server(P, S, rank, world, chunk=512, prefill_slots=8)
+    g = torch.Generator(device="cuda").manual_seed(4 + 1000 * rank)
+    local_res = []
+    for i, (L, gen) in enumerate(residents):
+        srv.add_resident(serving.Request(i, L, gen))
+        if srv.decoding[-1].gpu == rank:
+            local_res.append(srv.decoding[-1])
+    total = sum(r.prompt for r in local_res)
+    for layer in range(NL):
+        k_all = encode_device(torch.randn((max(total, 1), KVD), generator=g, device="cuda"), wl.dtype)
+        v_all = encode_device(torch.randn((max(total, 1), KVD), generator=g, device="cuda"), wl.dtype)
+        o = 0
+        for r in local_res:
+            P.import_rows(layer, r.seq, 0, k_all[o:o + r.prompt], v_all[o:o + r.prompt])
+            o += r.prompt
+        del k_all, v_all
+    for i, (L, gen) in enumerate(stream):
+        srv.submit(serving.Request(len(residents) + i, L, gen))
+    maxrows = 512
+    gq = torch.Generator(device="cuda").manual_seed(104 + rank)
+    qb = torch.randn((NL, maxrows, HID), generator=gq, device="cuda")
+    kb = torch.randn((NL, maxrows, KVD), generator=gq, device="cuda")
+    vb = torch.randn((NL, maxrows, KVD), generator=gq, device="cuda")
+    ob = torch.empty((NL, maxrows, HID), device="cuda")
+    kp = torch.randn((NL, 512, KVD), generator=gq, device="cuda")
+    vp = torch.randn((NL, 512, KVD), generator=gq, device="cuda")
+
+    def decode_io(layer, reqs):
+        n = len(reqs)
+        return qb[layer, :n], kb[layer, :n], vb[layer, :n], ob[layer, :n]
+
+    def prefill_kv(layer, req, pos0, n):
+        return kp[layer, :n], vp[layer, :n]
+
+    torch.cuda.synchronize()
+    sampler = ClockSampler(range(local, local + 1)) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    for _ in range(W):
+        srv.step(decode_io, prefill_kv)
+    # ~settle seconds more of untimed steps (the same count on every rank)
+    torch.cuda.synchronize()
+    t0 = time.time()
+    srv.step(decode_io, prefill_kv)
+    torch.cuda.synchronize()
+    n_settle = torch.tensor([int(args.settle / max(time.time() - t0, 1e-4))], device="cuda")
+    if dist:
+        dist.all_reduce(n_settle, op=dist.ReduceOp.MIN)
+    for _ in range(int(n_settle.item())):
+        srv.step(decode_io, prefill_kv)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    alg = 0.0
+    dec_tokens = pre_tokens = completed = 0
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    P.timing(True)
+    kc0 = kv.kernel_count()
+    for i in range(K):
+        mine = srv.local_decode()
+        alg += NL * step_bytes([r.length + 1 for r in mine]) if mine else 0.0
+        e0, e1 = ev[i]
+        e0.record()
+        c = srv.step(decode_io, prefill_kv)
+        e1.record()
+        dec_tokens += c["decode_tokens"]
+        pre_tokens += c["prefill_tokens"]
+        completed += c["completed"]
+    torch.cuda.synchronize()
+    kernels = kv.kernel_count() - kc0
+    if dist:
+        dist.barrier()
+    step_ms = sum(a.elapsed_time(b) for a, b in ev)
+    kern_ms, launches = P.timing_read()
+    P.timing(False)
+    clocks = sampler.stop() if sampler else None
+    assert P.device_status() == 0, "device-side check failed: " + kv._lib.kv_last_error().decode()
+    times = torch.tensor([step_ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    step_ms = times.item()
+    if rank == 0:
+        peak, peak_kind = peak_hbm()
+        achieved = alg / (kern_ms * 1e-3) / 1e9 if kern_ms > 0 else 0.0
+        line = {
+            "metric": METRIC,
+            "value": round(dec_tokens / (step_ms * 1e-3), 1),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": K,
+            "warmup": W,
+            "ms_per_step": round(step_ms / K, 5),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": wl.dtype_name,
+            "data": wl.data,
+            "config": {"workload": wl.desc, "name": wl.name, "layers": NL, "kv_dtype": wl.dtype_name,
+                       "block_tokens": 16, "chunk": 512, "prefill_slots": 8,
+                       "parallelism": f"request placement x{world} (no data-path collective)",
+                       "l2": "inputs larger than L2 (no flush)"},
+            "prefill_tokens_per_s": round(pre_tokens / (step_ms * 1e-3), 1),
+            "decode_tokens_per_step": round(dec_tokens / K, 2),
+            "completed": completed,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": None, "peak_source": peak_kind,
+                         "kernel_ms": round(kern_ms / max(launches, 1), 5),
+                         "per": "GPU 0, decode launches (prefill appends excluded)"},
+            "gpu_launches": int(kernels),
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    P.close()
+    if dist:
+        dist.destroy_process_group()
+
+
 # ------------------------------------------------------- CPU (reference) path
 def _oracle():
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -732,7 +892,8 @@ def run_reference(args, rank, world):
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(total / K * 1e3, 3),
             "higher_is_better": True,
-            "scaling": "strong" if wl.name.startswith("long") else "weak", "vs_baseline": None,
+            "scaling": "strong" if wl.name.startswith("long") or wl.name == "serve" else "weak",
+            "vs_baseline": None,
             "dtype": wl.dtype_name, "data": wl.data,
             "config": {"workload": wl.desc, "name": wl.name, "batch_per_gpu": wl.batch,
                        "layers": wl.layers, "kv_dtype": wl.dtype_name},
@@ -749,6 +910,8 @@ def main():
         run_reference(args, rank, world)
     elif args.workload.startswith("long"):
         run_long(args, rank, world, local)
+    elif args.workload == "serve":
+        run_serve(args, rank, world, local)
     else:
         run_ours(args, rank, world, local)
 
