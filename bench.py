@@ -125,6 +125,9 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["batch32", "paged28", "paged1", "long1", "long4", "serve"],
                     default="batch32")
+    ap.add_argument("--transport", choices=["nccl", "p2p"], default="nccl",
+                    help="long workloads: merge of the per-GPU states by NCCL all-gather + combine "
+                         "launch, or by the fused peer-memory exchange kernel")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--settle", type=float, default=1.0,
@@ -500,7 +503,7 @@ def run_long(args, rank, world, local):
     nb = B * (-(-(n_loc + extra) // 16)) + 16
     P = kv.Pool(local, NL, nb, num_q_heads=NQ, num_kv_heads=NKV, dtype=wl.dtype, max_seqs=B,
                 max_seq_len=wl.lens[0] + extra + 32)
-    S = splitkv.SplitKV(P, wl.lens, rank, world)
+    S = splitkv.SplitKV(P, wl.lens, rank, world, transport=args.transport)
     S.reserve(extra)
     g = torch.Generator(device="cuda").manual_seed(3 + 1000 * rank)
     for layer in range(NL):
@@ -619,7 +622,9 @@ def run_long(args, rank, world, local):
             "data": wl.data,
             "config": {"workload": wl.desc, "name": wl.name, "batch": B, "context": wl.lens[0],
                        "layers": NL, "kv_dtype": wl.dtype_name, "block_tokens": 16,
-                       "parallelism": f"sequence split x{world} (NCCL all-gather of partial states)",
+                       "parallelism": f"sequence split x{world} (" + (
+                           "NCCL all-gather of partial states + combine launch" if args.transport == "nccl"
+                           else "fused peer-memory exchange of partial states") + ")",
                        "l2": "inputs larger than L2 (no flush)"},
             "hbm_gbs_step": round(world * alg * NL / (step_ms / K * 1e-3) / 1e9, 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
@@ -636,6 +641,7 @@ def run_long(args, rank, world, local):
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(wl, args.cpu_seconds)
         print(json.dumps(line), flush=True)
+    S.close()
     P.close()
     if dist:
         dist.destroy_process_group()

@@ -183,6 +183,28 @@ int attn_decode_commit(kvp_pool* pool);
  * No reference counterpart (the reference has no split-KV). */
 int attn_combine_lse(int G, int rows, int dim, const float* m, const float* l, const float* o,
                      float* out, void* stream);
+/* ---- Split-KV across GPUs over peer memory ---------------------------------
+ * No counterpart in the reference.  One exchange object per rank (one process
+ * per GPU, all on one node): kvx_create allocates this rank's area on
+ * `device` for up to max_rows (sequence x query head) rows; kvx_handle gives
+ * its CUDA IPC handle (KVX_HANDLE_BYTES bytes) for the caller to pass to the
+ * other ranks (e.g. through torch.distributed); kvx_open maps a peer's area.
+ * attn_decode_append_xgpu then runs one layer of a sequence-split step: the
+ * local decode over this rank's slice (as attn_decode_append_partial), and,
+ * launched right behind it, an exchange kernel that pushes every row's
+ * (m, l, o) to every peer over NVLink, waits (bounded, ~1 s, then
+ * KV_ERR_TIMEOUT in kvp_device_status) for every peer's states of the same
+ * call and writes the merged out [rows][128].  Every rank must make the same
+ * sequence of calls.  Destroy after a barrier, when no rank calls any more. */
+typedef struct kvx_exch kvx_exch;
+#define KVX_HANDLE_BYTES 64
+int kvx_create(int device, int rank, int world, int max_rows, kvx_exch** out);
+int kvx_handle(const kvx_exch* x, void* handle);
+int kvx_open(kvx_exch* x, int peer, const void* handle);
+int kvx_destroy(kvx_exch* x);
+int attn_decode_append_xgpu(kvp_pool* pool, int layer, const float* q, const float* k_new,
+                            const float* v_new, float* out, kvx_exch* x, void* stream);
+
 /* The same merge over the packed buffer an all-gather of per-rank states
  * yields: packed [G][rows*(2+dim)], rank g's part laid out as
  * [m rows][l rows][o rows x dim].  No reference counterpart. */

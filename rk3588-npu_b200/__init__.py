@@ -25,6 +25,7 @@ KV_F16, KV_BF16 = 0, 1
 KVP_HOST_ONLY = -1
 HEAD_DIM = 128
 BLOCK_TOKENS = 16
+KVX_HANDLE_BYTES = 64
 
 _vp = C.c_void_p
 _ip = C.POINTER(C.c_int)
@@ -65,6 +66,11 @@ _SIGS = {
     "kvp_timing_enable": [_vp, C.c_int],
     "attn_contig_noalloc": [_vp, _vp, _vp, _vp] + [C.c_int] * 7 + [_vp],
     "kvp_timing_read": [_vp, C.POINTER(C.c_double), _ip],
+    "kvx_create": [C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)],
+    "kvx_handle": [_vp, _vp],
+    "kvx_open": [_vp, C.c_int, _vp],
+    "kvx_destroy": [_vp],
+    "attn_decode_append_xgpu": [_vp, C.c_int, _vp, _vp, _vp, _vp, _vp, _vp],
     "kvs_create": [C.c_int, C.c_int, C.POINTER(C.c_longlong), C.POINTER(_vp)],
     "kvs_destroy": [_vp],
     "kvs_place": [_vp, C.c_longlong, C.c_int, _ip],

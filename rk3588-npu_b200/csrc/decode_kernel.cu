@@ -539,6 +539,9 @@ __global__ void __launch_bounds__(kCombineWarps * 32)
     combine_kernel(PoolView pv, PlanView plan, int nsplits, float* __restrict__ out,
                    float* __restrict__ m_out, float* __restrict__ l_out) {
     static_assert(kCombineWarps * 32 >= kHeadDim, "the final merge maps one thread to each dim");
+    // A kernel launched behind this one with programmatic dependent launch
+    // (the cross-GPU exchange) may be scheduled now; it waits for this grid.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     __shared__ float s_m[kCombineWarps], s_l[kCombineWarps];
     __shared__ __align__(16) float s_o[kCombineWarps][kHeadDim];
     const int G = pv.group;

@@ -949,7 +949,8 @@ int attn_decode_plan(kvp_pool* p, int nseq, const int* seq_ids, void* stream) {
 }
 
 static int decode_call(kvp_pool* p, int layer, const float* q, const float* k_new, const float* v_new,
-                       float* out, float* m, float* l, void* stream) {
+                       float* out, float* m, float* l, void* stream, kvx_exch* x = nullptr,
+                       float* x_out = nullptr) {
     if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
     std::lock_guard<std::mutex> lk(p->mu);
     if (!p->plan_active) return fail(KV_ERR_STATE, "no active decode plan");
@@ -958,6 +959,13 @@ static int decode_call(kvp_pool* p, int layer, const float* q, const float* k_ne
     if (!q || !k_new || !v_new || !out) return fail(KV_ERR_INVAL, "NULL tensor");
     if (((uintptr_t)q | (uintptr_t)k_new | (uintptr_t)v_new) & 7)
         return fail(KV_ERR_INVAL, "q/k_new/v_new must be 8-byte aligned");
+    XchgArgs xa;
+    if (x) {
+        // the local states go to this rank's slot of the exchange area
+        if (int rc = xchg_prepare(x, p->device, p->plan_nslots * p->q_heads, p->pv.status, x_out, &xa,
+                                  &m, &l, &out))
+            return rc;
+    }
     DeviceGuard dg(p->device);
     cudaStream_t st = (cudaStream_t)stream;
     const int r = p->plan_slot_ring;
@@ -975,6 +983,10 @@ static int decode_call(kvp_pool* p, int layer, const float* q, const float* k_ne
     }
     KV_CUDA(launch_decode(p->pv, p->plan_view, p->plan_nsplits, p->plan_max_pieces, layer, q, k_new,
                           v_new, out, m, l, p->plan_grid, st));
+    if (x) {
+        KV_CUDA(launch_xchg(xa, st));
+        xchg_commit(x);
+    }
     if (te) KV_CUDA(cudaEventRecord(te->second, st));
     KV_CUDA(cudaEventRecord(p->slot_free[r], st));
     p->plan_patched = true;
@@ -1017,6 +1029,13 @@ int attn_decode_append_partial(kvp_pool* p, int layer, const float* q, const flo
                                const float* v_new, float* out, float* m, float* l, void* stream) {
     if (!m || !l) return fail(KV_ERR_INVAL, "m and l are required");
     return decode_call(p, layer, q, k_new, v_new, out, m, l, stream);
+}
+
+int attn_decode_append_xgpu(kvp_pool* p, int layer, const float* q, const float* k_new,
+                            const float* v_new, float* out, kvx_exch* x, void* stream) {
+    if (!x || !out) return fail(KV_ERR_INVAL, "NULL argument");
+    float* dummy = out;  // replaced by the exchange slot inside decode_call
+    return decode_call(p, layer, q, k_new, v_new, dummy, dummy, dummy, stream, x, out);
 }
 
 int attn_decode_commit(kvp_pool* p) {

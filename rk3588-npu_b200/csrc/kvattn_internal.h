@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+struct kvx_exch;  // split-KV exchange object of the C ABI (xgpu_exchange.cu)
+
 namespace kvattn {
 
 constexpr int kHeadDim = 128;          // dims per head (the only supported value)
@@ -146,6 +148,42 @@ cudaError_t launch_patch(const PoolView& pv, const TablePatch* patches, int npat
 cudaError_t launch_combine(int G, int rows, int dim, const float* m, const float* l,
                            const float* o, size_t gstride_ml, size_t gstride_o, float* out,
                            cudaStream_t st);
+
+// ---- split-KV exchange over peer memory (xgpu_exchange.cu) ----
+// Every rank owns one area in its own device memory, mapped by every peer:
+//   local   [m max_rows][l max_rows][o max_rows x 128] floats: this rank's
+//           states, written by its decode (never read by peers);
+//   inbox   [2 buffers][world sources][max_rows][2 + 128] words of 8 bytes,
+//           each {value bits, epoch}: a source writes a word with one 8-byte
+//           store, so a reader that sees the epoch of the current call sees
+//           its value (m, l, then the 128 dims of o).
+// Layer call e uses inbox buffer e & 1.
+constexpr int kMaxRanks = 8;
+
+struct XchgArgs {
+    float* base[kMaxRanks];  // every rank's area (this rank's is local)
+    int world, me, rows, max_rows;
+    unsigned epoch;          // >= 1, one more per layer call
+    float* out;              // [rows][128]
+    int* status;             // the pool's status words
+};
+
+__host__ __device__ inline size_t xchg_local_floats(int max_rows) { return (size_t)max_rows * (2 + kHeadDim); }
+__host__ __device__ inline uint2* xchg_inbox(float* base, int world, int max_rows, int buf, int src) {
+    return reinterpret_cast<uint2*>(base + xchg_local_floats(max_rows)) +
+           ((size_t)buf * world + src) * (size_t)max_rows * (2 + kHeadDim);
+}
+inline size_t xchg_bytes(int world, int max_rows) {
+    return xchg_local_floats(max_rows) * 4 + 2 * (size_t)world * max_rows * (2 + kHeadDim) * 8;
+}
+
+cudaError_t launch_xchg(const XchgArgs& a, cudaStream_t st);
+// Fill the arguments of the next layer call on `x` and point m/l/o at this
+// rank's own slot (where the local decode writes its states); the epoch
+// advances only on xchg_commit, after the launches succeeded.
+int xchg_prepare(::kvx_exch* x, int device, int rows, int* status, float* out, XchgArgs* a,
+                 float** m, float** l, float** o);
+void xchg_commit(::kvx_exch* x);
 
 // Sets the calling thread's kv_last_error() message; returns `status`.
 int set_error(int status, const char* msg);

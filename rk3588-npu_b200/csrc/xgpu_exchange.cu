@@ -1,0 +1,257 @@
+// xgpu_exchange.cu -- split-KV across GPUs, merged over peer memory.
+//
+// A long sequence is split along its positions across the GPUs of a node
+// (one process per GPU).  Per layer every rank attends over its slice; the
+// partial states (m, l, o) of every (sequence, query head) row must then be
+// merged across ranks.  The reference has no split-KV (it runs one sequence
+// on one device); the merge is the log-sum-exp identity
+//   out = sum_g l_g e^(m_g - M) o_g / sum_g l_g e^(m_g - M),  M = max_g m_g.
+//
+// Instead of an all-gather followed by a separate merge launch, the exchange
+// kernel runs right behind the local decode (programmatic dependent launch).
+// Per row, thread d (one per dim) writes this rank's value of dim d into
+// every peer's inbox as one 64-bit word {value, epoch of this layer call}
+// with one store over NVLink (the areas are mapped with CUDA IPC); two
+// more words carry m and l.  Readers poll the words of their own inbox until
+// every word carries the current epoch -- a scalar 64-bit access is seen
+// whole, so the value beside a current epoch is current -- and merge.  No fence, flag
+// or barrier sits on the path (the low-latency protocol NCCL calls LL).  No
+// multicast and no bulk copies touch peer memory.
+//
+// Two inbox buffers alternate by layer call, so a rank that runs ahead never
+// overwrites words a peer has not read yet: it cannot write call e+2's words
+// before it has read every peer's call-(e+1) words, which a peer writes only
+// after its call-e kernel completed.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "kvattn.h"
+#include "kvattn_internal.h"
+
+struct kvx_exch {
+    int device = 0, rank = 0, world = 1, max_rows = 0;
+    float* base[kvattn::kMaxRanks] = {};  // [rank] is the local allocation
+    bool opened[kvattn::kMaxRanks] = {};
+    unsigned epoch = 0;                   // layer calls made
+    std::mutex mu;
+};
+
+namespace kvattn {
+namespace {
+
+constexpr long long kXchgWaitLimit = 2000000000LL;  // SM clocks (~1 s) before a wait gives up
+
+// An inbox word is one scalar 64-bit access (value bits low, epoch high):
+// relaxed at system scope, so a reader observes it whole.
+__device__ __forceinline__ void st_word(uint2* p, float v, unsigned epoch) {
+    const unsigned long long w = ((unsigned long long)epoch << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+__device__ __forceinline__ uint2 ld_word(const uint2* p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return make_uint2((unsigned)w, (unsigned)(w >> 32));
+}
+
+// Poll one inbox word until it carries `epoch` (bounded); false on timeout.
+__device__ __forceinline__ bool wait_word(const uint2* p, unsigned epoch, float& v) {
+    uint2 w = ld_word(p);
+    if (w.y != epoch) {
+        const long long t0 = clock64();
+        do {
+            if (clock64() - t0 > kXchgWaitLimit) return false;
+            w = ld_word(p);
+        } while (w.y != epoch);
+    }
+    v = __uint_as_float(w.x);
+    return true;
+}
+
+// One CTA per (sequence, query head) row, one thread per dim.
+__global__ void __launch_bounds__(kHeadDim) xchg_kernel(const __grid_constant__ XchgArgs a) {
+    // The local states come from the decode grid (and its split merge):
+    // wait until they are complete and visible.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int r = blockIdx.x, d = threadIdx.x;
+    if (r >= a.rows) return;
+    const int buf = (int)(a.epoch & 1u);
+    const int W = a.world, R = a.max_rows;
+    const float* mine = a.base[a.me];
+    const float m0 = __ldcg(mine + r);
+    const float l0 = __ldcg(mine + R + r);
+    const float o0 = __ldcg(mine + 2 * R + (size_t)r * kHeadDim + d);
+    for (int g = 0; g < W; ++g) {
+        if (g == a.me) continue;
+        uint2* w = xchg_inbox(a.base[g], W, R, buf, a.me) + (size_t)r * (2 + kHeadDim);
+        st_word(w + 2 + d, o0, a.epoch);
+        if (d == 0) st_word(w, m0, a.epoch);
+        if (d == 1) st_word(w + 1, l0, a.epoch);
+    }
+    // Merge in rank order (the same arithmetic on every rank), each state
+    // read as it arrives; this rank's own comes from its local area.
+    float M = -INFINITY, L = 0.f, A = 0.f;
+    bool ok = true;
+    for (int g = 0; g < W; ++g) {
+        float mg = m0, lg = l0, og = o0;
+        if (g != a.me) {
+            const uint2* w = xchg_inbox(a.base[a.me], W, R, buf, g) + (size_t)r * (2 + kHeadDim);
+            ok = wait_word(w, a.epoch, mg) && wait_word(w + 1, a.epoch, lg) &&
+                 wait_word(w + 2 + d, a.epoch, og);
+            if (!ok) {
+                if (atomicCAS(a.status, 0, KV_ERR_TIMEOUT) == 0) {
+                    a.status[1] = r;
+                    a.status[2] = 500 + g;
+                    a.status[3] = (int)a.epoch;
+                }
+                break;
+            }
+        }
+        if (!(lg > 0.f)) continue;  // an empty slice: no weight
+        const float Mn = fmaxf(M, mg);
+        const float sa = expf(M - Mn);  // 0 while M is -inf
+        const float e = lg * expf(mg - Mn);
+        A = A * sa + e * og;
+        L = L * sa + e;
+        M = Mn;
+    }
+    a.out[(size_t)r * kHeadDim + d] = (ok && L > 0.f) ? A / L : 0.f;
+}
+
+struct DevGuard {
+    int prev = -1;
+    explicit DevGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        cudaSetDevice(dev);
+    }
+    ~DevGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+int cuda_err(cudaError_t e, const char* what) {
+    char buf[256];
+    snprintf(buf, sizeof buf, "%s: %s", what, cudaGetErrorString(e));
+    return set_error(KV_ERR_CUDA, buf);
+}
+
+}  // namespace
+
+cudaError_t launch_xchg(const XchgArgs& a, cudaStream_t st) {
+    if (a.rows <= 0) return cudaSuccess;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)a.rows);
+    cfg.blockDim = dim3(kHeadDim);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return counted(cudaLaunchKernelEx(&cfg, xchg_kernel, a));
+}
+
+int xchg_prepare(kvx_exch* x, int device, int rows, int* status, float* out, XchgArgs* a,
+                 float** m, float** l, float** o) {
+    if (!x) return set_error(KV_ERR_INVAL, "exchange is NULL");
+    if (x->device != device) return set_error(KV_ERR_INVAL, "exchange and pool are on different devices");
+    if (rows > x->max_rows) return set_error(KV_ERR_RANGE, "more rows than the exchange holds");
+    for (int g = 0; g < x->world; ++g)
+        if (!x->base[g]) return set_error(KV_ERR_STATE, "a peer's area is not open (kvx_open)");
+    *a = XchgArgs{};
+    for (int g = 0; g < x->world; ++g) a->base[g] = x->base[g];
+    a->world = x->world;
+    a->me = x->rank;
+    a->rows = rows;
+    a->max_rows = x->max_rows;
+    a->epoch = x->epoch + 1;
+    a->out = out;
+    a->status = status;
+    float* slot = x->base[x->rank];  // the local states
+    *m = slot;
+    *l = slot + x->max_rows;
+    *o = slot + 2 * (size_t)x->max_rows;
+    return KV_OK;
+}
+
+void xchg_commit(kvx_exch* x) { x->epoch += 1; }
+
+}  // namespace kvattn
+
+using namespace kvattn;
+
+extern "C" {
+
+int kvx_create(int device, int rank, int world, int max_rows, kvx_exch** out) {
+    if (!out) return set_error(KV_ERR_INVAL, "out is NULL");
+    *out = nullptr;
+    if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || max_rows < 1)
+        return set_error(KV_ERR_INVAL, "need 1 <= world <= 8, 0 <= rank < world, max_rows >= 1");
+    DevGuard dg(device);
+    kvx_exch* x = new kvx_exch;
+    x->device = device;
+    x->rank = rank;
+    x->world = world;
+    x->max_rows = (max_rows + 3) & ~3;
+    const size_t bytes = xchg_bytes(world, x->max_rows);
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);  // inbox words start at epoch 0
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        if (p) cudaFree(p);
+        delete x;
+        return cuda_err(e, "kvx_create");
+    }
+    x->base[rank] = static_cast<float*>(p);
+    *out = x;
+    return KV_OK;
+}
+
+int kvx_handle(const kvx_exch* x, void* handle) {
+    if (!x || !handle) return set_error(KV_ERR_INVAL, "NULL argument");
+    DevGuard dg(x->device);
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, x->base[x->rank]);
+    if (e != cudaSuccess) return cuda_err(e, "cudaIpcGetMemHandle");
+    static_assert(sizeof(h) == KVX_HANDLE_BYTES, "IPC handle size");
+    memcpy(handle, &h, sizeof h);
+    return KV_OK;
+}
+
+int kvx_open(kvx_exch* x, int peer, const void* handle) {
+    if (!x || !handle) return set_error(KV_ERR_INVAL, "NULL argument");
+    std::lock_guard<std::mutex> lk(x->mu);
+    if (peer < 0 || peer >= x->world || peer == x->rank) return set_error(KV_ERR_INVAL, "bad peer rank");
+    if (x->opened[peer]) return set_error(KV_ERR_STATE, "peer already open");
+    DevGuard dg(x->device);
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof h);
+    void* p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_err(e, "cudaIpcOpenMemHandle");
+    x->base[peer] = static_cast<float*>(p);
+    x->opened[peer] = true;
+    return KV_OK;
+}
+
+int kvx_destroy(kvx_exch* x) {
+    if (!x) return KV_OK;
+    {
+        DevGuard dg(x->device);
+        cudaDeviceSynchronize();
+        for (int g = 0; g < x->world; ++g)
+            if (x->opened[g]) cudaIpcCloseMemHandle(x->base[g]);
+        if (x->base[x->rank]) cudaFree(x->base[x->rank]);
+    }
+    delete x;
+    return KV_OK;
+}
+
+}  // extern "C"

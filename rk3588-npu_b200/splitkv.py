@@ -9,7 +9,13 @@ step per layer:
      rank also appending the new token: per (sequence, query head) a partial
      state (m, l, o) -- max of the scaled scores, sum of exp, normalised o;
   2. one all-gather of the packed states (NCCL over NVLink on GPUs);
-  3. attn_combine_lse merges the gathered states into the full output.
+  3. attn_combine_lse_packed merges the gathered states into the output.
+
+With transport="p2p" steps 2-3 run inside the library instead
+(attn_decode_append_xgpu): right behind the local decode, an exchange kernel
+pushes the states into every peer's area over NVLink (CUDA IPC mappings set
+up once, the handles passed through torch.distributed), waits for the peers'
+states of the same call and merges -- one host call per layer.
 
 The reference has no split-KV; the merge restates the log-sum-exp identity
 the oracle checks (oracle/kvattn_oracle.c: orc_lse_combine).
@@ -19,7 +25,9 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
-from . import Pool, call, _ptr, _stream, HEAD_DIM
+import ctypes as C
+
+from . import Pool, call, _ptr, _stream, _vp, HEAD_DIM, KVX_HANDLE_BYTES
 
 
 def slice_bounds(length: int, rank: int, world: int) -> tuple[int, int]:
@@ -34,8 +42,12 @@ class SplitKV:
     lengths   initial global context length of each sequence
     """
 
-    def __init__(self, pool: Pool, lengths, rank: int, world: int, group=None):
+    def __init__(self, pool: Pool, lengths, rank: int, world: int, group=None,
+                 transport: str = "nccl"):
+        assert transport in ("nccl", "p2p")
         self.pool, self.rank, self.world, self.group = pool, rank, world, group
+        self.transport = transport
+        self._x = None
         self.lengths = [int(x) for x in lengths]
         self.initial = list(self.lengths)
         self.ids = []
@@ -47,6 +59,29 @@ class SplitKV:
             self.bounds.append((lo, hi))
         self.rows = len(self.ids) * pool.q_heads
         self._buf = None
+        if transport == "p2p" and world > 1 and pool.device >= 0:
+            self._open_exchange()
+
+    def _open_exchange(self) -> None:
+        x = _vp()
+        call("kvx_create", self.pool.device, self.rank, self.world, self.rows, C.byref(x))
+        self._x = x
+        h = (C.c_char * KVX_HANDLE_BYTES)()
+        call("kvx_handle", x, h)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(h), group=self.group)
+        for g, hb in enumerate(handles):
+            if g != self.rank:
+                call("kvx_open", x, g, C.create_string_buffer(hb, KVX_HANDLE_BYTES))
+        dist.barrier(group=self.group)
+
+    def close(self) -> None:
+        """Release the exchange (every rank, after its last layer call)."""
+        if self._x is not None:
+            torch.cuda.synchronize(self.pool.device)
+            dist.barrier(group=self.group)
+            call("kvx_destroy", self._x)
+            self._x = None
 
     @property
     def is_last(self) -> bool:
@@ -72,7 +107,7 @@ class SplitKV:
         rope = list(self.lengths)
         append = [1 if self.is_last else 0] * len(self.ids)
         self.pool.plan(self.ids, rope_pos=rope, append=append, stream=stream)
-        if self._buf is None and self.pool.device >= 0:  # host-only pools plan but never run
+        if self._buf is None and self.pool.device >= 0 and self._x is None:  # host-only pools never run
             dev = torch.device("cuda", self.pool.device)
             n = self.rows * (2 + HEAD_DIM)
             self._buf = torch.empty(n, device=dev)
@@ -83,6 +118,10 @@ class SplitKV:
         fp32 (the same on every rank), out [B, q_heads*128] fp32."""
         if self.world == 1:  # the whole context is here: no partials
             self.pool.decode_layer(layer, q, k_new, v_new, out, stream=stream)
+            return
+        if self._x is not None:
+            call("attn_decode_append_xgpu", self.pool.h, layer, _ptr(q), _ptr(k_new), _ptr(v_new),
+                 _ptr(out), self._x, _stream(stream))
             return
         R = self.rows
         buf = self._buf

@@ -11,6 +11,7 @@ import torch
 import torch.multiprocessing as mp
 
 from conftest import ROOT, load_pkg
+from importlib import import_module
 
 
 def _free_port() -> int:
@@ -135,3 +136,120 @@ def test_splitkv_two_ranks_one_gpu_matches_unsplit():
     for rank, worst, status in out:
         assert status == 0
         assert worst <= 1e-3, (rank, worst)
+
+
+def _p2p_worker(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import sys
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as orc
+        kv = load_pkg()
+        sk_mod = import_module("rk3588_npu_b200.splitkv")
+        rng = np.random.default_rng(6)
+        lens = [900, 3100, 17]
+        dtype = 1
+        full_k = [orc.encode(rng.standard_normal((L + 8, 256)).astype(np.float32), dtype) for L in lens]
+        full_v = [orc.encode(rng.standard_normal((L + 8, 256)).astype(np.float32), dtype) for L in lens]
+        P = kv.Pool(rank, 2, 600, dtype=dtype, max_seqs=4, max_seq_len=4096)
+        S = sk_mod.SplitKV(P, lens, rank, world, transport="p2p")
+        S.reserve(8)
+        for layer in range(2):
+            for i, (lo, hi) in enumerate(S.bounds):
+                k = torch.from_numpy(full_k[i][lo:hi].view(np.int16)).cuda()
+                v = torch.from_numpy(full_v[i][lo:hi].view(np.int16)).cuda()
+                S.load_slice(layer, i, k, v)
+        worst = 0.0
+        caches = [[(full_k[i].copy(), full_v[i].copy()) for i in range(3)] for _ in range(2)]
+        for step in range(3):
+            pos = list(S.lengths)
+            S.begin_step()
+            for layer in range(2):
+                qh = rng.standard_normal((3, 1536)).astype(np.float32)
+                kh = rng.standard_normal((3, 256)).astype(np.float32)
+                vh = rng.standard_normal((3, 256)).astype(np.float32)
+                out = torch.empty((3, 1536), device="cuda")
+                S.layer(layer, torch.from_numpy(qh).cuda(), torch.from_numpy(kh).cuda(),
+                        torch.from_numpy(vh).cuda(), out)
+                got = out.cpu().numpy()
+                for i in range(3):
+                    kc, vc = caches[layer][i]
+                    ref, _, _ = orc.layer_step(qh[i:i + 1], kh[i:i + 1], vh[i:i + 1], kc, vc, pos[i],
+                                               dtype=dtype)
+                    g = got[i].reshape(-1, 128).astype(np.float64)
+                    r = ref[0].reshape(-1, 128).astype(np.float64)
+                    worst = max(worst, float((np.abs(g - r).max(1) / np.abs(r).max(1)).max()))
+            S.end_step()
+        status = P.device_status()
+        S.close()
+        q.put((rank, worst, status))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_splitkv_p2p_exchange_two_gpus_matches_unsplit():
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two CUDA devices")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_p2p_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, worst, status in out:
+        assert status == 0
+        assert worst <= 1e-3, (rank, worst)
+
+
+@pytest.mark.gpu
+def test_xgpu_call_with_one_rank_equals_local_decode():
+    """A one-rank exchange: the decode states go through this rank's slot of
+    the exchange area and the exchange kernel's merge of a single state must
+    reproduce the ordinary decode output exactly."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import ctypes as C
+    import sys
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    kv = load_pkg()
+    rng = np.random.default_rng(7)
+    lens = [5, 700, 4000]
+    P = kv.Pool(0, 1, 400, dtype=0, max_seqs=3, max_seq_len=4200)
+    ids = []
+    for L in lens:
+        s = P.seq_alloc()
+        P.reserve(s, L + 4)
+        kc = orc.encode(rng.standard_normal((L, 256)).astype(np.float32), 0)
+        vc = orc.encode(rng.standard_normal((L, 256)).astype(np.float32), 0)
+        P.import_rows(0, s, 0, torch.from_numpy(kc.view(np.int16)).cuda(),
+                      torch.from_numpy(vc.view(np.int16)).cuda())
+        P.set_cur_pos(s, L)
+        ids.append(s)
+    x = kv._vp()
+    kv.call("kvx_create", 0, 0, 1, 3 * 12, C.byref(x))
+    q = torch.randn((3, 1536), device="cuda")
+    k = torch.randn((3, 256), device="cuda")
+    v = torch.randn((3, 256), device="cuda")
+    ref = torch.empty((3, 1536), device="cuda")
+    got = torch.empty((3, 1536), device="cuda")
+    for s, L in zip(ids, lens):
+        P.set_cur_pos(s, L)
+    P.plan(ids, rope_pos=lens, append=[0, 0, 0])
+    P.decode_layer(0, q, k, v, ref)
+    for _ in range(3):  # both buffers of the exchange area
+        kv.call("attn_decode_append_xgpu", P.h, 0, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                got.data_ptr(), x, None)
+        torch.cuda.synchronize()
+        assert torch.allclose(got, ref, rtol=1e-6, atol=1e-7)
+    P.commit()
+    assert P.device_status() == 0
+    kv.call("kvx_destroy", x)
