@@ -253,3 +253,57 @@ def test_xgpu_call_with_one_rank_equals_local_decode():
     P.commit()
     assert P.device_status() == 0
     kv.call("kvx_destroy", x)
+
+
+def _skip_worker(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        kv = load_pkg()
+        sk_mod = import_module("rk3588_npu_b200.splitkv")
+        P = kv.Pool(rank, 1, 64, dtype=1, max_seqs=1, max_seq_len=1024)
+        S = sk_mod.SplitKV(P, [300], rank, world, transport="p2p")
+        S.reserve(4)
+        lo, hi = S.bounds[0]
+        z = torch.zeros((hi - lo, 256), dtype=torch.int16, device="cuda")
+        S.load_slice(0, 0, z, z)
+        q_ = torch.randn((1, 1536), device="cuda")
+        k_ = torch.randn((1, 256), device="cuda")
+        out = torch.empty((1, 1536), device="cuda")
+        S.begin_step()
+        S.layer(0, q_, k_, k_, out)       # both ranks: a completed exchange
+        torch.cuda.synchronize()
+        ok_status = P.device_status()
+        dist.barrier()
+        if rank == 0:                     # rank 1 skips this call: nothing sets its words
+            S.layer(0, q_, k_, k_, out)
+            torch.cuda.synchronize()
+        status = P.device_status()
+        dist.barrier()
+        q.put((rank, ok_status, status, bool(torch.all(out == 0)) if rank == 0 else None))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_xgpu_timeout_when_peer_skips_call():
+    """A peer that never makes its layer call: the exchange's bounded wait
+    gives up (~1 s) and reports KV_ERR_TIMEOUT; no hang, outputs zeroed."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two CUDA devices")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_skip_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = sorted(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    (_, ok0, st0, zero0), (_, ok1, st1, _) = out
+    assert ok0 == 0 and ok1 == 0
+    assert st0 == 7 and zero0          # KV_ERR_TIMEOUT on the rank that waited
+    assert st1 == 0
