@@ -281,6 +281,41 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // The combine kernel may be scheduled now; it waits for this grid.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // Round 0 first: producer lane l initialises its own stage's barriers and
+    // issues flat block l straight from this CTA's descriptor, which needs no
+    // other load, so the first copies leave after one round trip.  A tile id
+    // is range-checked before any copy; the descriptor itself is validated
+    // below, and a lane that issued round 0 always drains it.
+    const CtaDesc* cdp = plan.cta + blockIdx.x;
+    const bool prod_lane = warp == kConsumerWarps && lane < kStages;
+    const uint64_t policy = policy_evict_first();
+    const long ntile_ids = (long)pv.num_blocks * pv.kv_heads;
+    // One ring round of producer lane `s` for flat block f with tile id `tile`.
+    auto issue = [&](int s, int f, int tile) {
+        if (tile == -1) {
+            mbar_arrive(&sm.full[s]);  // only the new token: nothing to load
+        } else if (tile < 0 || tile >= ntile_ids) {
+            report(pv, 5, blockIdx.x, 200 + f);  // never read outside the pool
+            mbar_arrive(&sm.full[s]);
+        } else {
+            const size_t off = (size_t)layer * pv.layer_bytes + (size_t)tile * kTileBytes;
+            mbar_arrive_expect_tx(&sm.full[s], kStageBytes);
+            bulk_g2s_hint(sm.stage[s], pv.k + off, kTileBytes, &sm.full[s], policy);
+            bulk_g2s_hint(sm.stage[s] + kTileBytes, pv.v + off, kTileBytes, &sm.full[s], policy);
+        }
+    };
+    bool issued0 = false;
+    if (prod_lane) {
+        const int nf0 = cdp->nf;
+        const int tile0 = cdp->first[lane];
+        mbar_init(&sm.full[lane], 1);
+        mbar_init(&sm.empty[lane], 1);
+        fence_mbar_init();
+        if (lane < nf0) {  // round 0: the stage is free
+            issue(lane, lane, tile0);
+            issued0 = true;
+        }
+    }
     const PlanHeader hdr = *plan.hdr;
 
     // Block-table entries allocated by this step's plan.  No launch reads an
@@ -295,10 +330,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         pv.table[(size_t)p.seq * pv.max_blocks_per_seq + p.idx] = p.block;
     }
 
-    // This CTA's descriptor.  Producer lanes initialise their own stage's
-    // barriers and issue the first ring round straight from the descriptor,
-    // before the CTA-wide barrier; the other threads load and check pieces.
-    const CtaDesc cd = plan.cta[blockIdx.x];
+    // This CTA's descriptor, checked against the plan before its pieces and
+    // tiles are used; the other threads load and check the pieces.
+    const CtaDesc cd = *cdp;
     int n = cd.n, nf = cd.nf;
     if (n < 0 || n > kMaxCtaItems || cd.i0 < 0 || cd.i0 + n > hdr.nitems || nf < 0 || cd.f0 < 0 ||
         cd.f0 + nf > hdr.ntiles) {
@@ -307,29 +341,6 @@ __global__ void __launch_bounds__(kThreads, 2)
         nf = 0;
     }
     const int i0 = cd.i0;
-    const bool prod_lane = warp == kConsumerWarps && lane < kStages;
-    const uint64_t policy = policy_evict_first();
-    const long ntile_ids = (long)pv.num_blocks * pv.kv_heads;
-    // One ring round of producer lane `s` for flat block f with tile id `tile`.
-    auto issue = [&](int s, int f, int tile) {
-        if (tile == -1) {
-            mbar_arrive(&sm.full[s]);  // only the new token: nothing to load
-        } else if (tile < 0 || tile >= ntile_ids) {
-            report(pv, 5, i0, 200 + f);  // never read outside the pool
-            mbar_arrive(&sm.full[s]);
-        } else {
-            const size_t off = (size_t)layer * pv.layer_bytes + (size_t)tile * kTileBytes;
-            mbar_arrive_expect_tx(&sm.full[s], kStageBytes);
-            bulk_g2s_hint(sm.stage[s], pv.k + off, kTileBytes, &sm.full[s], policy);
-            bulk_g2s_hint(sm.stage[s] + kTileBytes, pv.v + off, kTileBytes, &sm.full[s], policy);
-        }
-    };
-    if (prod_lane) {
-        mbar_init(&sm.full[lane], 1);
-        mbar_init(&sm.empty[lane], 1);
-        fence_mbar_init();
-        if (lane < nf) issue(lane, lane, plan.cta[blockIdx.x].first[lane]);  // round 0: the stage is free
-    }
     int tile_next = (prod_lane && lane + kStages < nf) ? plan.tiles[cd.f0 + lane + kStages] : -1;
     for (int j = tid; j < n; j += kThreads) {
         WorkItem w = plan.items[i0 + j];
@@ -367,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         // tile id of its next round one round ahead.
         if (lane < kStages) {
             const int s = lane;
-            uint32_t rounds = lane < nf ? 1u : 0u;  // round 0 went out above
+            uint32_t rounds = issued0 ? 1u : 0u;  // round 0 went out above
             for (int f = lane + kStages; f < total; f += kStages) {
                 const int cur = tile_next;
                 if (f + kStages < total) tile_next = plan.tiles[cd.f0 + f + kStages];  // in flight
