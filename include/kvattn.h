@@ -137,6 +137,16 @@ int kvp_gather(kvp_pool* pool, int layer, int seq_id, void* k_rows, void* v_rows
 int kv_append_chunk(kvp_pool* pool, int layer, int seq_id, int pos0, int n, const float* k,
                     const float* v, void* stream);
 
+/* Causal attention of a prompt chunk over the pool: op_attention with
+ * seq = n > 1 (op_attention.cpp:9-56).  Query s sits at position pos0 + s of
+ * the sequence and attends to positions [0, pos0 + s]; the chunk's own K/V
+ * must already be in the pool for `layer` (kv_append_chunk).  q [n][num_q_heads
+ * * 128] fp32 straight from the projections (16-byte aligned): it is rotated
+ * here at pos0 + s with the append's RoPE arithmetic.  out [n][num_q_heads *
+ * 128] fp32.  The length is not changed. */
+int attn_prefill(kvp_pool* pool, int layer, int seq_id, int pos0, int n, const float* q,
+                 float* out, void* stream);
+
 /* ---------------------------------------------------------------- decode */
 
 /* Plan one decode step for nseq sequences (host ids).  For each sequence:

@@ -52,6 +52,7 @@ _SIGS = {
     "kvp_import": [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp],
     "kvp_gather": [_vp, C.c_int, C.c_int, _vp, _vp, _vp],
     "kv_append_chunk": [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp],
+    "attn_prefill": [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp],
     "attn_decode_plan": [_vp, C.c_int, _ip, _vp],
     "attn_decode_plan_ex": [_vp, C.c_int, _ip, _ip, _ip, _vp],
     "attn_decode_append": [_vp, C.c_int, _vp, _vp, _vp, _vp, _vp],
@@ -251,6 +252,12 @@ class Pool:
         n = k.shape[0]
         assert k.shape == (n, self.kv_dim) and v.shape == (n, self.kv_dim)
         call("kv_append_chunk", self.h, layer, seq, pos0, n, _ptr(k), _ptr(v), _stream(stream))
+
+    def prefill(self, layer, seq, pos0, q, out, stream=None) -> None:
+        """Causal attention of q [n, hidden] (unrotated) at positions pos0.. over
+        the pool (the chunk's K/V appended first)."""
+        n = q.shape[0]
+        call("attn_prefill", self.h, layer, seq, pos0, n, _ptr(q), _ptr(out), _stream(stream))
 
     # ---- decode ----
     def plan(self, seq_ids, rope_pos=None, append=None, stream=None) -> None:

@@ -112,6 +112,8 @@ struct kvp_pool {
     int* d_counters = nullptr;
     float* d_partials = nullptr;
     int* d_status = nullptr;
+    float* d_prefill_part = nullptr;  // key-split partials of attn_prefill (grown on demand)
+    size_t prefill_part_floats = 0;
 
     // allocator: LIFO stack of free block ids + position index
     std::vector<int> free_;
@@ -281,6 +283,7 @@ void free_device(kvp_pool* p) {
     cudaFree(p->d_table);
     cudaFree(p->d_counters);
     cudaFree(p->d_partials);
+    cudaFree(p->d_prefill_part);
     cudaFree(p->d_status);
     cudaFree(p->d_pending);
     cudaFreeHost(p->h_pending);
@@ -694,6 +697,51 @@ int kv_append_chunk(kvp_pool* p, int layer, int seq, int pos0, int n, const floa
     rc = sync_table(p, st);
     if (rc) return rc;
     KV_CUDA(launch_append_chunk(p->pv, layer, seq, pos0, n, k, v, st));
+    return KV_OK;
+}
+
+int attn_prefill(kvp_pool* p, int layer, int seq, int pos0, int n, const float* q, float* out,
+                 void* stream) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    std::lock_guard<std::mutex> lk(p->mu);
+    int rc = check_seq(p, seq);
+    if (rc) return rc;
+    rc = require_device(p);
+    if (rc) return rc;
+    if (layer < 0 || layer >= p->layers) return fail(KV_ERR_INVAL, "layer %d out of range", layer);
+    if (n < 0 || pos0 < 0) return fail(KV_ERR_INVAL, "negative position/count");
+    if ((long)pos0 + n > p->max_seq_len)
+        return fail(KV_ERR_RANGE, "position %ld beyond max_seq_len %d", (long)pos0 + n - 1, p->max_seq_len);
+    if ((long)pos0 + n > (long)p->seqs[seq].blocks.size() * kBlockTokens)
+        return fail(KV_ERR_RANGE, "positions [%d, %d) exceed reserved blocks", pos0, pos0 + n);
+    if (n == 0) return KV_OK;
+    if (!q || !out || ((uintptr_t)q & 15) || ((uintptr_t)out & 7))
+        return fail(KV_ERR_INVAL, "q must be 16-byte and out 8-byte aligned");
+    DeviceGuard dg(p->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    rc = sync_table(p, st);
+    if (rc) return rc;
+    // Key splits: enough CTAs for two per SM, at least 16 tiles (256 keys)
+    // per split.
+    const int nqb = (n + 15) / 16;
+    const int max_tiles = (pos0 + n - 1) / kBlockTokens + 1;
+    const long ctas = (long)nqb * p->kv_heads;
+    int nsplit = (int)std::min<long>((2L * p->num_sms + ctas - 1) / ctas, (max_tiles + 15) / 16);
+    nsplit = std::max(nsplit, 1);
+    const int tps = (max_tiles + nsplit - 1) / nsplit;
+    nsplit = (max_tiles + tps - 1) / tps;
+    if (nsplit > 1) {
+        const size_t need = (size_t)p->q_heads * nqb * 16 * nsplit * (2 + kHeadDim);
+        if (need > p->prefill_part_floats) {
+            KV_CUDA(cudaStreamSynchronize(st));
+            cudaFree(p->d_prefill_part);
+            p->d_prefill_part = nullptr;
+            p->prefill_part_floats = 0;
+            KV_CUDA(cudaMalloc((void**)&p->d_prefill_part, need * sizeof(float)));
+            p->prefill_part_floats = need;
+        }
+    }
+    KV_CUDA(launch_prefill(p->pv, layer, seq, pos0, n, q, out, p->d_prefill_part, nsplit, tps, st));
     return KV_OK;
 }
 

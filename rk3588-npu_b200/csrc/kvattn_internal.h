@@ -145,6 +145,8 @@ cudaError_t launch_append_chunk(const PoolView& pv, int layer, int seq, int pos0
                                 const float* k, const float* v, cudaStream_t st);
 cudaError_t launch_patch(const PoolView& pv, const TablePatch* patches, int npatch,
                          cudaStream_t st);
+cudaError_t launch_prefill(const PoolView& pv, int layer, int seq, int pos0, int n, const float* q,
+                           float* out, float* part, int nsplit, int tiles_per_split, cudaStream_t st);
 cudaError_t launch_combine(int G, int rows, int dim, const float* m, const float* l,
                            const float* o, size_t gstride_ml, size_t gstride_o, float* out,
                            cudaStream_t st);
