@@ -56,6 +56,7 @@ constexpr int kStageBytes = 2 * kTileBytes;  // K tile then V tile
 constexpr int kMergeStride = 132;            // floats per (warp, head) row, padded
 constexpr long long kWaitLimit = 4000000000LL;  // SM clocks (~2 s) before a wait gives up
 constexpr int kQPre = 4;                     // pieces whose q fragments are prepared up front
+constexpr int kEarlyLanes = 2;               // ring stages issued before the plan header load
 
 struct Smem {
     alignas(1024) uint8_t stage[kStages][kStageBytes];
@@ -304,14 +305,18 @@ __global__ void __launch_bounds__(kThreads, 2)
             bulk_g2s_hint(sm.stage[s] + kTileBytes, pv.v + off, kTileBytes, &sm.full[s], policy);
         }
     };
+    // Only the first kEarlyLanes stages go out here: their tiles then sit at
+    // the front of the DRAM queue and arrive early; the other lanes issue
+    // their first round from the producer loop a little later.
     bool issued0 = false;
+    int tile0 = -2;
     if (prod_lane) {
         const int nf0 = cdp->nf;
-        const int tile0 = cdp->first[lane];
+        tile0 = cdp->first[lane];
         mbar_init(&sm.full[lane], 1);
         mbar_init(&sm.empty[lane], 1);
         fence_mbar_init();
-        if (lane < nf0) {  // round 0: the stage is free
+        if (lane < kEarlyLanes && lane < nf0) {  // round 0: the stage is free
             issue(lane, lane, tile0);
             issued0 = true;
         }
@@ -373,22 +378,39 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------ producer
         // Lane l < kStages owns ring stage l and issues flat blocks l, l +
-        // kStages, ...; the lanes run the same loop in step, so one warp
-        // instruction issues up to kStages stages.  Each lane fetches the
-        // tile id of its next round one round ahead.
+        // kStages, ...  Each lane refills its stage as soon as that stage is
+        // released -- the lanes poll their own barriers without blocking and
+        // never wait for one another -- so a slow stage does not hold back
+        // the other seven.  Each lane fetches the tile id of its next round
+        // one round ahead.
         if (lane < kStages) {
             const int s = lane;
-            uint32_t rounds = issued0 ? 1u : 0u;  // round 0 went out above
-            for (int f = lane + kStages; f < total; f += kStages) {
-                const int cur = tile_next;
-                if (f + kStages < total) tile_next = plan.tiles[cd.f0 + f + kStages];  // in flight
-                if (!mbar_wait_bounded(&sm.empty[s], (rounds & 1) ^ 1, kWaitLimit)) {
+            // Lanes below kEarlyLanes issued round 0 above; the others start
+            // with it (their stage is free: a fresh barrier passes the
+            // parity-1 test at once).
+            uint32_t rounds = issued0 ? 1u : 0u;
+            int f = issued0 ? lane + kStages : lane;  // this lane's next flat block
+            int cur = issued0 ? tile_next : tile0;    // its tile id
+            int nxt = issued0 ? ((f + kStages < total) ? plan.tiles[cd.f0 + f + kStages] : -1) : tile_next;
+            bool stopped = false;
+            long long since = clock64();
+            for (;;) {
+                const bool has = !stopped && f < total;
+                if (!__any_sync(0xffu, has)) break;
+                bool ready = has && mbar_test_wait(&sm.empty[s], (rounds & 1) ^ 1);
+                if (ready) {
+                    issue(s, f, cur);
+                    ++rounds;
+                    atomicMax(&sm.prod_issued, f + 1);
+                    f += kStages;
+                    cur = nxt;
+                    if (f + kStages < total) nxt = plan.tiles[cd.f0 + f + kStages];  // in flight
+                    since = clock64();
+                } else if (has && clock64() - since > kWaitLimit) {
                     flag_timeout(pv, sm, i0, 0, (uint32_t)f);
-                    break;
+                    stopped = true;
                 }
-                issue(s, f, cur);
-                ++rounds;
-                atomicMax(&sm.prod_issued, f + 1);
+                if (!__any_sync(0xffu, ready)) __nanosleep(32);
             }
             // Drain, on every path (also after a timeout or a rejected plan):
             // this lane's last issued stage must land before the CTA exits.
