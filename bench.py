@@ -406,19 +406,19 @@ def run_ours(args, rank, world, local):
     assert P.device_status() == 0, "device-side check failed: " + L.kv_last_error().decode()
 
     # ---- e2e: host buffers, copies inside the timed region ----
-    # Every step copies its q / k / v for all layers from pinned host memory
-    # and reads all layers' outputs back; at most 8 distinct host input sets
-    # are kept and cycled.
+    # Every step copies its inputs for all layers from pinned host memory in
+    # one copy -- per layer q [B][1536] | k [B][256] | v [B][256], the layout a
+    # fused QKV projection writes -- and reads all layers' outputs back in one
+    # copy; at most 8 distinct host input sets are kept and cycled.
     reset_lens()
     R = min(K, 8)
-    qh = q[W:W + R].cpu().pin_memory()
-    kh = kn[W:W + R].cpu().pin_memory()
-    vh = vn[W:W + R].cpu().pin_memory()
+    per = B * (HID + 2 * KVD)
+    inh = torch.cat([q[W:W + R].reshape(R, NL, -1), kn[W:W + R].reshape(R, NL, -1),
+                     vn[W:W + R].reshape(R, NL, -1)], dim=2).cpu().pin_memory()
     oh = torch.empty((R, NL, B, HID)).pin_memory()
-    qd = torch.empty((NL, B, HID), device="cuda")
-    kd = torch.empty((NL, B, KVD), device="cuda")
-    vd = torch.empty((NL, B, KVD), device="cuda")
-    dptr = [(qd[y].data_ptr(), kd[y].data_ptr(), vd[y].data_ptr(), out[y].data_ptr()) for y in range(NL)]
+    ind = torch.empty((NL, per), device="cuda")
+    dptr = [(ind[y].data_ptr(), ind[y].data_ptr() + 4 * B * HID, ind[y].data_ptr() + 4 * B * (HID + KVD),
+             out[y].data_ptr()) for y in range(NL)]
     e2e_ms = 0.0
     if dist:
         dist.barrier()
@@ -426,9 +426,7 @@ def run_ours(args, rank, world, local):
         maybe_flush()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        qd.copy_(qh[i % R], non_blocking=True)
-        kd.copy_(kh[i % R], non_blocking=True)
-        vd.copy_(vh[i % R], non_blocking=True)
+        ind.copy_(inh[i % R], non_blocking=True)
         chk(L.attn_decode_plan(h, nseq, ids_c, st), "attn_decode_plan")
         for y, (qa, ka, va, oa) in enumerate(dptr):
             chk(L.attn_decode_append(h, y, qa, ka, va, oa, st), "attn_decode_append")
@@ -902,10 +900,43 @@ def run_prefill(args, rank, world, local):
             "gpu_launches": int(kernels),
             "clocks": clocks,
         }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_prefill(pos0, CH, NL, args.cpu_seconds)
         print(json.dumps(line), flush=True)
     P.close()
     if dist:
         dist.destroy_process_group()
+
+
+def cpu_baseline_prefill(pos0, ch, layers, seconds):
+    """The reference's own RoPE + append + op_attention for one 512-token
+    chunk (one request, one layer, 1 thread), scaled by attention FLOPs to
+    the workload's 8 requests x 28 layers."""
+    orc = _oracle()
+    if not orc.have_ref():
+        return {"value": None, "unit": "tokens/s", "cores": 1, "kind": "unavailable",
+                "sample": "the reference functions were not built"}
+    rng = np.random.default_rng(4)
+    p0 = pos0[0]
+    kc = np.zeros((p0 + ch, KVD), np.uint16)
+    vc = np.zeros((p0 + ch, KVD), np.uint16)
+    kc[:p0] = orc.encode(rng.standard_normal((p0, KVD), dtype=np.float32))
+    vc[:p0] = orc.encode(rng.standard_normal((p0, KVD), dtype=np.float32))
+    work = lambda p: sum(p + i + 1 for i in range(ch))
+    t0 = time.perf_counter()
+    reps = 0
+    while reps == 0 or (time.perf_counter() - t0 < seconds and reps < 4):
+        q = rng.standard_normal((ch, HID), dtype=np.float32)
+        k = rng.standard_normal((ch, KVD), dtype=np.float32)
+        v = rng.standard_normal((ch, KVD), dtype=np.float32)
+        orc.ref_layer_step(q, k, v, kc, vc, p0)
+        reps += 1
+    dt = (time.perf_counter() - t0) / reps
+    full = dt * layers * sum(work(p) for p in pos0) / work(p0)
+    return {"value": round(len(pos0) * ch / full, 3), "unit": "tokens/s", "cores": 1, "kind": "reference",
+            "sample": f"{reps} x one 512-token chunk at position {p0}, 1 layer, 1 host thread "
+                      f"({dt:.2f} s each), scaled by attention work to {len(pos0)} chunks x {layers} "
+                      f"layers; fp16 caches (the reference's only cache type)"}
 
 
 # ------------------------------------------------------- CPU (reference) path
@@ -984,10 +1015,62 @@ def cpu_baseline(wl: Workload, seconds):
             "sample": sample}
 
 
+def run_reference_prefill(args, world):
+    """Reference arm of the prefill workload: the reference's RoPE + append +
+    op_attention, one host thread per request; each step a bounded sample
+    (the first 64 queries of every request's chunk, one layer), scaled by
+    attention work to the full step."""
+    from concurrent.futures import ThreadPoolExecutor
+    orc = _oracle()
+    wl = make_workload("prefill")
+    CH, SUB, NL = 512, 64, wl.layers
+    _, stream = serve_stream()
+    pos0 = [max(0, (L // CH // 2) * CH) for L, _ in stream[:wl.batch]]
+    rng = np.random.default_rng(4)
+    caches = []
+    for p0 in pos0:
+        kc = np.zeros((p0 + CH, KVD), np.uint16)
+        vc = np.zeros((p0 + CH, KVD), np.uint16)
+        kc[:p0] = orc.encode(rng.standard_normal((p0, KVD), dtype=np.float32))
+        vc[:p0] = orc.encode(rng.standard_normal((p0, KVD), dtype=np.float32))
+        caches.append((kc, vc))
+    threads = max(1, min(os.cpu_count() or 1, wl.batch))
+    ex = ThreadPoolExecutor(threads)
+    work_full = NL * sum(sum(p + i + 1 for i in range(CH)) for p in pos0)
+    work_sub = sum(sum(p + i + 1 for i in range(SUB)) for p in pos0)
+    K, W = args.steps, args.warmup
+    total = 0.0
+    for it in range(W + K):
+        qs = [rng.standard_normal((SUB, HID), dtype=np.float32) for _ in pos0]
+        ks = [rng.standard_normal((SUB, KVD), dtype=np.float32) for _ in pos0]
+        t0 = time.perf_counter()
+        list(ex.map(lambda j: orc.ref_layer_step(qs[j], ks[j], ks[j], caches[j][0], caches[j][1], pos0[j]),
+                    range(len(pos0))))
+        dt = time.perf_counter() - t0
+        if it >= W:
+            total += dt * work_full / work_sub
+    value = round(wl.batch * CH * K / total, 3)
+    sample = (f"{K} steps of the first {SUB} queries of each of the {wl.batch} chunks, 1 layer, {threads} "
+              f"host threads (one per request), reference functions compiled from source, scaled by "
+              f"attention work to {wl.batch} x {CH}-token chunks x {NL} layers; fp16 caches")
+    line = {"impl": "reference", "metric": "chunked-prefill attention tokens/s and achieved TFLOP/s vs B200 bf16 peak",
+            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": round(total / K * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": wl.dtype_name, "data": wl.data,
+            "config": {"workload": wl.desc, "name": wl.name, "chunk": CH, "layers": NL},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
     orc = _oracle()
+    if args.workload == "prefill":
+        run_reference_prefill(args, world)
+        return
     wl = make_workload(args.workload)
     threads = max(1, min(os.cpu_count() or 1, wl.batch))
     kind, fn = cpu_step_fn(orc, threads)
