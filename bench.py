@@ -137,6 +137,8 @@ def parse_args():
     ap.add_argument("--transport", choices=["nccl", "p2p"], default="nccl",
                     help="long workloads: merge of the per-GPU states by NCCL all-gather + combine "
                          "launch, or by the fused peer-memory exchange kernel")
+    ap.add_argument("--prefill-kernel", choices=["tc", "mma"], default="tc",
+                    help="prefill workload: the tcgen05 kernel (attn_prefill) or the mma.sync baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--settle", type=float, default=1.0,
@@ -840,6 +842,7 @@ def run_prefill(args, rank, world, local):
     ob = torch.empty((CH, HID), device="cuda")
     L = kv._lib
     st = torch.cuda.current_stream().cuda_stream
+    prefill_fn = L.attn_prefill if args.prefill_kernel == "tc" else L.attn_prefill_mma
 
     def chk(rc, fn):
         if rc != 0:
@@ -850,7 +853,7 @@ def run_prefill(args, rank, world, local):
             for s, p0 in zip(ids, pos0):
                 chk(L.kv_append_chunk(P.h, y, s, p0, CH, kb[y].data_ptr(), vb[y].data_ptr(), st),
                     "kv_append_chunk")
-                chk(L.attn_prefill(P.h, y, s, p0, CH, qb[y].data_ptr(), ob.data_ptr(), st), "attn_prefill")
+                chk(prefill_fn(P.h, y, s, p0, CH, qb[y].data_ptr(), ob.data_ptr(), st), "attn_prefill")
 
     # real (not doubled by the hi/lo split) FLOPs: QK^T and PV, 2 * 128 each per (query, key, head)
     flops = NL * sum(sum(4.0 * HD * NQ * (p0 + i + 1) for i in range(CH)) for p0 in pos0)
@@ -891,12 +894,13 @@ def run_prefill(args, rank, world, local):
             "ms_per_step": round(step_ms / K, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": wl.dtype_name, "data": wl.data,
             "config": {"workload": wl.desc, "name": wl.name, "chunk": CH, "layers": NL,
+                       "kernel": "tcgen05" if args.prefill_kernel == "tc" else "mma.sync",
                        "contexts_before_chunk": pos0, "l2": "inputs larger than L2 (no flush)"},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": None,
                          "peak_source": "measured (bf16 sustained)",
-                         "note": "whole step (append + attention launches); mma.sync with hi/lo "
-                                 "operand splits issues 2x these FLOPs"},
+                         "note": "whole step (append + attention launches); the hi/lo operand "
+                                 "splits issue 2x these FLOPs on the tensor cores"},
             "gpu_launches": int(kernels),
             "clocks": clocks,
         }

@@ -143,9 +143,14 @@ int kv_append_chunk(kvp_pool* pool, int layer, int seq_id, int pos0, int n, cons
  * must already be in the pool for `layer` (kv_append_chunk).  q [n][num_q_heads
  * * 128] fp32 straight from the projections (16-byte aligned): it is rotated
  * here at pos0 + s with the append's RoPE arithmetic.  out [n][num_q_heads *
- * 128] fp32.  The length is not changed. */
+ * 128] fp32 (both 16-byte aligned).  The length is not changed.  Runs on the
+ * 5th-generation tensor cores (tcgen05 MMA with accumulators in tensor memory). */
 int attn_prefill(kvp_pool* pool, int layer, int seq_id, int pos0, int n, const float* q,
                  float* out, void* stream);
+/* The same computation on the legacy mma.sync tensor path (the baseline
+ * attn_prefill's tcgen05 kernel is measured against). */
+int attn_prefill_mma(kvp_pool* pool, int layer, int seq_id, int pos0, int n, const float* q,
+                     float* out, void* stream);
 
 /* ---------------------------------------------------------------- decode */
 

@@ -53,6 +53,7 @@ _SIGS = {
     "kvp_gather": [_vp, C.c_int, C.c_int, _vp, _vp, _vp],
     "kv_append_chunk": [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp],
     "attn_prefill": [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp],
+    "attn_prefill_mma": [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp],
     "attn_decode_plan": [_vp, C.c_int, _ip, _vp],
     "attn_decode_plan_ex": [_vp, C.c_int, _ip, _ip, _ip, _vp],
     "attn_decode_append": [_vp, C.c_int, _vp, _vp, _vp, _vp, _vp],
@@ -253,11 +254,13 @@ class Pool:
         assert k.shape == (n, self.kv_dim) and v.shape == (n, self.kv_dim)
         call("kv_append_chunk", self.h, layer, seq, pos0, n, _ptr(k), _ptr(v), _stream(stream))
 
-    def prefill(self, layer, seq, pos0, q, out, stream=None) -> None:
+    def prefill(self, layer, seq, pos0, q, out, stream=None, kernel="tc") -> None:
         """Causal attention of q [n, hidden] (unrotated) at positions pos0.. over
-        the pool (the chunk's K/V appended first)."""
+        the pool (the chunk's K/V appended first); kernel "tc" (tcgen05) or
+        "mma" (the mma.sync baseline)."""
         n = q.shape[0]
-        call("attn_prefill", self.h, layer, seq, pos0, n, _ptr(q), _ptr(out), _stream(stream))
+        fn = "attn_prefill" if kernel == "tc" else "attn_prefill_mma"
+        call(fn, self.h, layer, seq, pos0, n, _ptr(q), _ptr(out), _stream(stream))
 
     # ---- decode ----
     def plan(self, seq_ids, rope_pos=None, append=None, stream=None) -> None:

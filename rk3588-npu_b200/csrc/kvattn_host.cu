@@ -700,10 +700,22 @@ int kv_append_chunk(kvp_pool* p, int layer, int seq, int pos0, int n, const floa
     return KV_OK;
 }
 
-int attn_prefill(kvp_pool* p, int layer, int seq, int pos0, int n, const float* q, float* out,
-                 void* stream) {
-    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
-    std::lock_guard<std::mutex> lk(p->mu);
+namespace {
+
+int prefill_part_reserve(kvp_pool* p, size_t need, cudaStream_t st) {
+    if (need <= p->prefill_part_floats) return KV_OK;
+    KV_CUDA(cudaStreamSynchronize(st));
+    cudaFree(p->d_prefill_part);
+    p->d_prefill_part = nullptr;
+    p->prefill_part_floats = 0;
+    KV_CUDA(cudaMalloc((void**)&p->d_prefill_part, need * sizeof(float)));
+    p->prefill_part_floats = need;
+    return KV_OK;
+}
+
+// Shared checks of the prefill entry points; on success the table is on the device.
+int prefill_checks(kvp_pool* p, int layer, int seq, int pos0, int n, const float* q, float* out,
+                   cudaStream_t st) {
     int rc = check_seq(p, seq);
     if (rc) return rc;
     rc = require_device(p);
@@ -715,12 +727,61 @@ int attn_prefill(kvp_pool* p, int layer, int seq, int pos0, int n, const float* 
     if ((long)pos0 + n > (long)p->seqs[seq].blocks.size() * kBlockTokens)
         return fail(KV_ERR_RANGE, "positions [%d, %d) exceed reserved blocks", pos0, pos0 + n);
     if (n == 0) return KV_OK;
-    if (!q || !out || ((uintptr_t)q & 15) || ((uintptr_t)out & 7))
-        return fail(KV_ERR_INVAL, "q must be 16-byte and out 8-byte aligned");
+    if (!q || !out || ((uintptr_t)q & 15) || ((uintptr_t)out & 15))
+        return fail(KV_ERR_INVAL, "q and out must be 16-byte aligned");
+    return sync_table(p, st);
+}
+
+}  // namespace
+
+// Tensor-core (tcgen05) version: 128 (token, head) rows per CTA, key splits
+// of whole 64-key stages, about one CTA per SM.
+int attn_prefill(kvp_pool* p, int layer, int seq, int pos0, int n, const float* q, float* out,
+                 void* stream) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    std::lock_guard<std::mutex> lk(p->mu);
     DeviceGuard dg(p->device);
     cudaStream_t st = (cudaStream_t)stream;
-    rc = sync_table(p, st);
-    if (rc) return rc;
+    int rc = prefill_checks(p, layer, seq, pos0, n, q, out, st);
+    if (rc || n == 0) return rc;
+    const int tc = prefill_tc_tokens_per_cta(p->q_heads / p->kv_heads);
+    const int nq = (n + tc - 1) / tc;
+    const int max_tiles = (pos0 + n - 1) / kBlockTokens + 1;
+    const long ctas = (long)nq * p->kv_heads;
+    // One CTA per SM is resident: pick the split count that minimises
+    // waves x (tiles per CTA + a fixed cost per CTA of ~8 tiles) + a merge
+    // cost per split, with at least one 64-key stage per split.
+    const int max_split = std::max(1, std::min(64, max_tiles / 4));
+    int nsplit = 1;
+    double best = 1e30;
+    for (int ns = 1; ns <= max_split; ++ns) {
+        const long waves = (ctas * ns + p->num_sms - 1) / p->num_sms;
+        const double cost = (double)waves * ((double)max_tiles / ns + 8.0) + 0.25 * ns;
+        if (cost < best - 1e-9) {
+            best = cost;
+            nsplit = ns;
+        }
+    }
+    int tps = (max_tiles + nsplit - 1) / nsplit;
+    tps = (tps + 3) / 4 * 4;  // whole 64-key stages
+    nsplit = (max_tiles + tps - 1) / tps;
+    if (nsplit > 1) {
+        rc = prefill_part_reserve(p, prefill_tc_part_floats(p->q_heads, n, nsplit), st);
+        if (rc) return rc;
+    }
+    KV_CUDA(launch_prefill_tc(p->pv, layer, seq, pos0, n, q, out, p->d_prefill_part, nsplit, tps, st));
+    return KV_OK;
+}
+
+// The same on mma.sync (the baseline the tensor-core version is measured against).
+int attn_prefill_mma(kvp_pool* p, int layer, int seq, int pos0, int n, const float* q, float* out,
+                     void* stream) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    std::lock_guard<std::mutex> lk(p->mu);
+    DeviceGuard dg(p->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    int rc = prefill_checks(p, layer, seq, pos0, n, q, out, st);
+    if (rc || n == 0) return rc;
     // Key splits: enough CTAs for two per SM, at least 16 tiles (256 keys)
     // per split.
     const int nqb = (n + 15) / 16;
@@ -731,15 +792,8 @@ int attn_prefill(kvp_pool* p, int layer, int seq, int pos0, int n, const float* 
     const int tps = (max_tiles + nsplit - 1) / nsplit;
     nsplit = (max_tiles + tps - 1) / tps;
     if (nsplit > 1) {
-        const size_t need = (size_t)p->q_heads * nqb * 16 * nsplit * (2 + kHeadDim);
-        if (need > p->prefill_part_floats) {
-            KV_CUDA(cudaStreamSynchronize(st));
-            cudaFree(p->d_prefill_part);
-            p->d_prefill_part = nullptr;
-            p->prefill_part_floats = 0;
-            KV_CUDA(cudaMalloc((void**)&p->d_prefill_part, need * sizeof(float)));
-            p->prefill_part_floats = need;
-        }
+        rc = prefill_part_reserve(p, (size_t)p->q_heads * nqb * 16 * nsplit * (2 + kHeadDim), st);
+        if (rc) return rc;
     }
     KV_CUDA(launch_prefill(p->pv, layer, seq, pos0, n, q, out, p->d_prefill_part, nsplit, tps, st));
     return KV_OK;

@@ -1,0 +1,558 @@
+// prefill_tc_kernel.cu -- chunked-prefill attention on the 5th-generation
+// tensor cores (tcgen05 MMA, accumulators in tensor memory).
+//
+// Same semantics as prefill_kernel.cu (op_attention with seq = n > 1,
+// worker/src/ops/op_attention.cpp:9-56, causal, GQA; q rotated here at
+// pos0 + s): query s attends to positions [0, pos0 + s] of the pool.
+//
+// One CTA = one KV head h, Tc = 128 / G query tokens x the G query heads of the
+// group = up to 128 rows (row r = token r / G, head r % G), one key split.
+//   warps 0-3  rows: thread r owns tensor-memory lane r = row r.  They rotate,
+//              scale and split their q row into 16-bit hi + lo halves in shared
+//              memory (K-major, 128-byte swizzle), then per key stage of 64
+//              keys read the row's scores from tensor memory, apply the causal
+//              mask, run the online softmax, rescale the output row in tensor
+//              memory when the row maximum moved, and write P (hi + lo) back to
+//              shared memory as the next MMA's A operand;
+//   warp 4     producer: bulk async copies (TMA engine, into this CTA only) of
+//              the stage's four (block, head) tiles -- each K tile as two
+//              2 KiB halves into two 64-row K-major regions, each V tile whole;
+//   warp 5     allocates 256 tensor-memory columns (two 64-column score
+//              buffers, a 128-column output) and one elected lane issues the
+//              MMAs:  S = Qhi K^T + Qlo K^T  (M 128, N 64, K 16 x 8 x 2),
+//                     O += Phi V + Plo V    (M 128, N 128, K 16 x 4 x 2; the
+//              pool's V tile is an MN-major operand as it lies), committing
+//              each group to an mbarrier.  The next stage's S is computed while
+//              the rows run the softmax of this one (double-buffered S); the
+//              issuing lane polls both conditions and issues whichever group is
+//              ready, so a P*V never waits for the next stage's copies.
+// Every wait is bounded; a timeout is recorded in the pool's status words and
+// the CTA still drains its copies, retires its MMAs and frees its tensor memory.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "device_common.cuh"
+#include "kvattn.h"
+#include "kvattn_internal.h"
+
+namespace kvattn {
+
+namespace {
+
+constexpr int kTcRows = 128;                 // MMA M: rows per CTA
+constexpr int kTcStageKeys = 64;             // keys per stage = 4 tiles
+constexpr int kTcThreads = 6 * 32;
+constexpr int kTcKvStages = 3;               // K/V stages in flight
+constexpr uint32_t kTmemCols = 256;          // S0 [0,64) S1 [64,128) O [128,256)
+constexpr long long kTcWaitLimit = 4000000000LL;
+constexpr int kTcPartFloats = kHeadDim + 4;  // 16-byte aligned rows
+constexpr float kTcRescale = 8.f;            // lazy-rescale threshold (log2 units)
+
+// Shared memory: all regions 1024-byte aligned (128-byte swizzle atoms).
+struct TcSmem {
+    uint8_t q[2][2][kTcRows * 128];         // [hi/lo][dims 0-63 / 64-127][row][128 B]
+    uint8_t k[kTcKvStages][2][kTcStageKeys * 128];  // [stage][dims half][key][128 B]
+    uint8_t v[kTcKvStages][4][kTileBytes];          // [stage][tile] pool tile layout
+    uint8_t p[2][kTcRows * 128];                    // [hi/lo][row][64 keys x 2 B]
+    uint64_t full[kTcKvStages], empty[kTcKvStages], s_full[2], p_ready, o_done, q_ready, mma_done;
+    uint32_t tmem_base;
+    int failed;
+};
+
+// ---- tcgen05 wrappers (PTX ISA, sm_100a) ----
+__device__ __forceinline__ void tmem_alloc(uint32_t* holder, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(holder)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// D[tmem] (+)= A[smem desc] * B[smem desc]
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive once on `bar` when every MMA this thread issued so far has completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 32 consecutive fp32 columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&r)[32]) {
+    uint32_t* u = reinterpret_cast<uint32_t*>(r);
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]),
+          "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]), "=r"(u[14]),
+          "=r"(u[15]), "=r"(u[16]), "=r"(u[17]), "=r"(u[18]), "=r"(u[19]), "=r"(u[20]), "=r"(u[21]),
+          "=r"(u[22]), "=r"(u[23]), "=r"(u[24]), "=r"(u[25]), "=r"(u[26]), "=r"(u[27]), "=r"(u[28]),
+          "=r"(u[29]), "=r"(u[30]), "=r"(u[31])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&r)[32]) {
+    const uint32_t* u = reinterpret_cast<const uint32_t*>(r);
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(u[0]), "r"(u[1]), "r"(u[2]), "r"(u[3]), "r"(u[4]), "r"(u[5]), "r"(u[6]), "r"(u[7]), "r"(u[8]),
+        "r"(u[9]), "r"(u[10]), "r"(u[11]), "r"(u[12]), "r"(u[13]), "r"(u[14]), "r"(u[15]), "r"(u[16]),
+        "r"(u[17]), "r"(u[18]), "r"(u[19]), "r"(u[20]), "r"(u[21]), "r"(u[22]), "r"(u[23]), "r"(u[24]),
+        "r"(u[25]), "r"(u[26]), "r"(u[27]), "r"(u[28]), "r"(u[29]), "r"(u[30]), "r"(u[31])
+        : "memory");
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle, version 1 (sm_100):
+// start address >> 4 [0,14), leading byte offset >> 4 [16,30), stride byte
+// offset >> 4 [32,46), version [46,48), layout type [61,64) = 2 (128B swizzle).
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor, kind::f16 with fp32 accumulate: D format [4,6) = 1,
+// A/B format [7,10)/[10,13) (0 f16, 1 bf16), B major [16] (1 = MN-major),
+// N >> 3 [17,23), M >> 4 [24,29).
+__host__ __device__ constexpr uint32_t idesc_f16(int dt, int m, int n, int b_mn) {
+    return (1u << 4) | ((uint32_t)dt << 7) | ((uint32_t)dt << 10) | ((uint32_t)b_mn << 16) |
+           ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, const PoolView& pv, int code,
+                                        int* failed) {
+    if (mbar_wait_bounded(bar, parity, kTcWaitLimit)) return true;
+    if (atomicCAS(pv.status, 0, KV_ERR_TIMEOUT) == 0) {
+        pv.status[1] = blockIdx.x;
+        pv.status[2] = code;
+    }
+    *reinterpret_cast<volatile int*>(failed) = 1;
+    return false;
+}
+
+// Swizzled byte offset of 16-byte chunk c (0..7) of row r in a 128-byte-row region.
+__device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+template <int DT>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+    if (DT == 0) {
+        __half2 h = __floats2half2_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+}  // namespace
+
+// Partial row ((qhead * n + s) * nsplit + sp), kTcPartFloats floats, holds
+// o[128] (normalised), then m (base 2) and l.
+template <int DT>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    prefill_tc_kernel(PoolView pv, int layer, int seq, int pos0, int n, const float* __restrict__ q,
+                      float* __restrict__ out, float* __restrict__ part, int nsplit, int tiles_per_split) {
+    extern __shared__ uint8_t smem_raw[];
+    TcSmem& sm = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int G = pv.group, Tc = kTcRows / G;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int h = blockIdx.y, sp = blockIdx.z;
+    const int s0 = blockIdx.x * Tc;
+    const int s_last = min(n, s0 + Tc) - 1;
+    const int ntiles = (pos0 + s_last) / kBlockTokens + 1;
+    const int t_begin = sp * tiles_per_split;  // a multiple of 4
+    const int t_end = min(ntiles, t_begin + tiles_per_split);
+    const int nst = t_end > t_begin ? (t_end - t_begin + 3) / 4 : 0;
+    const int kv_lim = min(t_end * kBlockTokens, pos0 + s_last + 1);  // keys >= kv_lim never count
+
+    if (tid == 0) {
+        for (int i = 0; i < kTcKvStages; ++i) {
+            mbar_init(&sm.full[i], 1);
+            mbar_init(&sm.empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) mbar_init(&sm.s_full[i], 1);
+        mbar_init(&sm.p_ready, 128);
+        mbar_init(&sm.o_done, 1);
+        mbar_init(&sm.q_ready, 128);
+        mbar_init(&sm.mma_done, 1);
+        sm.failed = 0;
+    }
+    fence_mbar_init();
+    if (warp == 5) {
+        tmem_alloc(&sm.tmem_base, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = sm.tmem_base;
+
+    if (warp == 4) {
+        // ---------------------------------------------------------- producer
+        if (lane == 0) {
+            const uint64_t policy = policy_evict_first();
+            const int* trow = pv.table + (size_t)seq * pv.max_blocks_per_seq;
+            int issued = 0;
+            for (int j = 0; j < nst; ++j) {
+                const int b = j % kTcKvStages;
+                if (j >= kTcKvStages && !tc_wait(&sm.empty[b], ((j / kTcKvStages) - 1) & 1, pv, 700, &sm.failed))
+                    break;
+                if (*reinterpret_cast<volatile int*>(&sm.failed)) break;
+                int tiles = 0;
+                for (int u = 0; u < 4; ++u) tiles += (t_begin + 4 * j + u < t_end);
+                mbar_arrive_expect_tx(&sm.full[b], (uint32_t)tiles * 2u * kTileBytes);
+                for (int u = 0; u < tiles; ++u) {
+                    const int t = t_begin + 4 * j + u;
+                    int blk = (t < pv.max_blocks_per_seq) ? trow[t] : -1;
+                    if (blk < 0 || blk >= pv.num_blocks) {
+                        if (atomicCAS(pv.status, 0, 5) == 0) {
+                            pv.status[1] = t;
+                            pv.status[2] = 701;
+                        }
+                        blk = 0;  // stay inside the pool; the status voids the outputs
+                    }
+                    const size_t off = (size_t)layer * pv.layer_bytes + ((size_t)blk * pv.kv_heads + h) * kTileBytes;
+                    bulk_g2s_hint(sm.k[b][0] + u * 2048, pv.k + off, 2048, &sm.full[b], policy);
+                    bulk_g2s_hint(sm.k[b][1] + u * 2048, pv.k + off + 2048, 2048, &sm.full[b], policy);
+                    bulk_g2s_hint(sm.v[b][u], pv.v + off, kTileBytes, &sm.full[b], policy);
+                }
+                ++issued;
+            }
+            // Drain: the stages issued last must land before the CTA exits.
+            for (int j = issued > kTcKvStages ? issued - kTcKvStages : 0; j < issued; ++j)
+                mbar_wait_bounded(&sm.full[j % kTcKvStages], (j / kTcKvStages) & 1, kTcWaitLimit);
+        }
+    } else if (warp == 5) {
+        // ------------------------------------------------------------- MMA
+        if (lane == 0) {
+            const uint32_t id_qk = idesc_f16(DT, kTcRows, kTcStageKeys, 0);
+            const uint32_t id_pv = idesc_f16(DT, kTcRows, kHeadDim, 1);
+            const uint32_t q0 = smem_u32(sm.q[0][0]);
+            const uint32_t p0 = smem_u32(sm.p[0]);
+            bool ok = tc_wait(&sm.q_ready, 0, pv, 710, &sm.failed);
+            auto issue_qk = [&](int j) {
+                const uint32_t kb = smem_u32(sm.k[j % kTcKvStages][0]);
+                const uint32_t d = tmem + (uint32_t)((j & 1) * kTcStageKeys);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint32_t koff = (uint32_t)((kk >> 2) * (kTcStageKeys * 128) + (kk & 3) * 32);
+                    const uint64_t bd = sdesc(kb + koff, 16, 1024);
+#pragma unroll
+                    for (int hl = 0; hl < 2; ++hl) {
+                        const uint32_t qoff = (uint32_t)(hl * 2 * kTcRows * 128 + (kk >> 2) * (kTcRows * 128) + (kk & 3) * 32);
+                        tc_mma(d, sdesc(q0 + qoff, 16, 1024), bd, id_qk, (kk | hl) != 0);
+                    }
+                }
+                tc_commit(&sm.s_full[j & 1]);
+            };
+            auto issue_pv = [&](int j) {
+                const int b = j % kTcKvStages;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const uint64_t bd = sdesc(smem_u32(sm.v[b][u]), 2048, 1024);
+#pragma unroll
+                    for (int hl = 0; hl < 2; ++hl)
+                        tc_mma(tmem + 128u, sdesc(p0 + (uint32_t)(hl * kTcRows * 128 + u * 32), 16, 1024), bd,
+                               id_pv, (j | u | hl) != 0);
+                }
+                tc_commit(&sm.o_done);
+                tc_commit(&sm.empty[b]);
+            };
+            // Issue whichever group is ready: S of stage q (its K/V landed and
+            // its score buffer was read) or P*V of stage p (its P written).
+            int qk = 0, pvn = 0;
+            long long since = clock64();
+            while (ok && pvn < nst) {
+                bool progressed = false;
+                if (qk < nst && qk <= pvn + 1 &&
+                    mbar_test_wait(&sm.full[qk % kTcKvStages], (qk / kTcKvStages) & 1)) {
+                    tc_fence_after();
+                    issue_qk(qk);
+                    ++qk;
+                    progressed = true;
+                }
+                if (pvn < qk && mbar_test_wait(&sm.p_ready, pvn & 1)) {
+                    tc_fence_after();
+                    issue_pv(pvn);
+                    ++pvn;
+                    progressed = true;
+                }
+                if (progressed) {
+                    since = clock64();
+                } else if (*reinterpret_cast<volatile int*>(&sm.failed)) {
+                    ok = false;
+                } else if (clock64() - since > kTcWaitLimit) {
+                    if (atomicCAS(pv.status, 0, KV_ERR_TIMEOUT) == 0) {
+                        pv.status[1] = blockIdx.x;
+                        pv.status[2] = 711;
+                    }
+                    *reinterpret_cast<volatile int*>(&sm.failed) = 1;
+                    ok = false;
+                }
+            }
+            // every MMA issued above has completed once this arrives
+            tc_commit(&sm.mma_done);
+            mbar_wait_bounded(&sm.mma_done, 0, kTcWaitLimit);
+        }
+    } else {
+        // ------------------------------------------------------------ rows
+        const int r = tid;  // 0..127: tensor-memory lane and CTA row
+        const int tok = r / G, g = r % G;
+        const int s = s0 + tok;
+        const bool live = tok < Tc && s < n;
+        const int qhead = h * G + g;
+        const int prow = pos0 + s;  // keys <= prow count for this row
+        // q row: rotate (non-fused, host cos/sin), scale, split into hi + lo
+        {
+            const float qscale = 0.08838834764831845f * 1.4426950408889634f;  // 1/sqrt(128) * log2(e)
+            const float* qr = q + (size_t)(live ? s : 0) * (pv.q_heads * kHeadDim) + (size_t)qhead * kHeadDim;
+            const float* cs = reinterpret_cast<const float*>(pv.rope + (size_t)(live ? prow : 0) * (kHeadDim / 2));
+#pragma unroll 1
+            for (int c = 0; c < 8; ++c) {  // dims 8c..8c+7 and their partners 64+8c..
+                float lo[8], hi[8];
+#pragma unroll
+                for (int e = 0; e < 8; e += 2) {
+                    const int i = 8 * c + e;
+                    float l0 = 0.f, h0 = 0.f, l1 = 0.f, h1 = 0.f;
+                    if (live) {
+                        const float2 a = *reinterpret_cast<const float2*>(qr + i);
+                        const float2 bb = *reinterpret_cast<const float2*>(qr + i + 64);
+                        const float4 t = *reinterpret_cast<const float4*>(cs + 2 * i);
+                        rope_pair(a.x, bb.x, t.x, t.y, l0, h0);
+                        rope_pair(a.y, bb.y, t.z, t.w, l1, h1);
+                    }
+                    lo[e] = l0 * qscale;
+                    lo[e + 1] = l1 * qscale;
+                    hi[e] = h0 * qscale;
+                    hi[e + 1] = h1 * qscale;
+                }
+                uint32_t wh[2][4], wl[2][4];  // [dims half][pairs]
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    split_pair<DT>(lo[2 * e], lo[2 * e + 1], wh[0][e], wl[0][e]);
+                    split_pair<DT>(hi[2 * e], hi[2 * e + 1], wh[1][e], wl[1][e]);
+                }
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    *reinterpret_cast<uint4*>(sm.q[0][half] + swz(r, c)) =
+                        make_uint4(wh[half][0], wh[half][1], wh[half][2], wh[half][3]);
+                    *reinterpret_cast<uint4*>(sm.q[1][half] + swz(r, c)) =
+                        make_uint4(wl[half][0], wl[half][1], wl[half][2], wl[half][3]);
+                }
+            }
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive(&sm.q_ready);
+
+        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nst; ++j) {
+            if (!__all_sync(0xffffffffu, tc_wait(&sm.s_full[j & 1], (j >> 1) & 1, pv, 720, &sm.failed))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float sc[64];
+            {
+                float a[32], bq[32];
+                tmem_ld32(tmem + lane_base + (uint32_t)((j & 1) * kTcStageKeys), a);
+                tmem_ld32(tmem + lane_base + (uint32_t)((j & 1) * kTcStageKeys + 32), bq);
+                tc_wait_ld();
+#pragma unroll
+                for (int c = 0; c < 32; ++c) {
+                    sc[c] = a[c];
+                    sc[32 + c] = bq[c];
+                }
+            }
+            const int kbase = (t_begin + 4 * j) * kBlockTokens;
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int c = 0; c < 64; ++c) {
+                const int key = kbase + c;
+                if (key > prow || key >= kv_lim) sc[c] = -INFINITY;
+                mx4[c & 3] = fmaxf(mx4[c & 3], sc[c]);
+            }
+            const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+            // Lazy rescale: the reference max m moves only when a score
+            // exceeds it by more than kTcRescale (base 2), so weights stay
+            // <= 2^kTcRescale and the output row in tensor memory is rescaled
+            // rarely; l and O always share the same reference, so the result
+            // is the same softmax.
+            float alpha = 1.f;
+            if (mx > m + kTcRescale || m == -INFINITY) {
+                const float mn = fmaxf(m, mx);
+                const float mu = (mn == -INFINITY) ? 0.f : mn;
+                alpha = fast_exp2(m - mu);  // 0 while m is -inf
+                m = mn;
+            }
+            const float mu = (m == -INFINITY) ? 0.f : m;
+            float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int c = 0; c < 64; ++c) {
+                sc[c] = fast_exp2(sc[c] - mu);
+                sum4[c & 3] += sc[c];
+            }
+            l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
+            // The last stage: V rows of keys >= kv_lim may hold anything
+            // (stale smem, rows past the sequence); zero them so masked
+            // weights (exactly 0) stay 0.
+            if (j == nst - 1) {
+                for (int x = r; x < kTcStageKeys * 16; x += 128) {  // (key row, 16-byte chunk)
+                    const int kr = x >> 4, ch = x & 15;
+                    if (kbase + kr >= kv_lim) {
+                        const int u = kr >> 4, t = kr & 15;
+                        *reinterpret_cast<uint4*>(sm.v[j % kTcKvStages][u] + ((ch >> 3) * 16 + t) * 128 + (ch & 7) * 16) =
+                            make_uint4(0u, 0u, 0u, 0u);
+                    }
+                }
+            }
+            // Previous P*V done: P may be overwritten and O rescaled.
+            if (j >= 1) {
+                if (!__all_sync(0xffffffffu, tc_wait(&sm.o_done, (j - 1) & 1, pv, 721, &sm.failed))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, alpha != 1.f)) {  // rare after the first stages
+#pragma unroll 1
+                    for (int c4 = 0; c4 < 4; ++c4) {
+                        float o[32];
+                        tmem_ld32(tmem + lane_base + 128u + (uint32_t)(32 * c4), o);
+                        tc_wait_ld();
+#pragma unroll
+                        for (int c = 0; c < 32; ++c) o[c] *= alpha;
+                        tmem_st32(tmem + lane_base + 128u + (uint32_t)(32 * c4), o);
+                    }
+                    tc_wait_st();
+                }
+            }
+            // P (hi + lo) as the A operand: row r, 64 keys = 8 chunks of 8
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                uint32_t ph[4], pl[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) split_pair<DT>(sc[8 * c + 2 * e], sc[8 * c + 2 * e + 1], ph[e], pl[e]);
+                *reinterpret_cast<uint4*>(sm.p[0] + swz(r, c)) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+                *reinterpret_cast<uint4*>(sm.p[1] + swz(r, c)) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_fence_before();
+            mbar_arrive(&sm.p_ready);
+        }
+        // ---- the output row ----
+        if (ok && nst > 0 && __all_sync(0xffffffffu, tc_wait(&sm.o_done, (nst - 1) & 1, pv, 722, &sm.failed))) {
+            tc_fence_after();
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            float* dst = nullptr;
+            if (live) {
+                if (nsplit == 1) {
+                    dst = out + (size_t)s * (pv.q_heads * kHeadDim) + (size_t)qhead * kHeadDim;
+                } else {
+                    float* prow_p = part + (((size_t)qhead * n + s) * nsplit + sp) * kTcPartFloats;
+                    prow_p[kHeadDim] = m;
+                    prow_p[kHeadDim + 1] = l;
+                    dst = prow_p;
+                }
+            }
+#pragma unroll 1
+            for (int c4 = 0; c4 < 4; ++c4) {
+                float o[32];
+                tmem_ld32(tmem + lane_base + 128u + (uint32_t)(32 * c4), o);
+                tc_wait_ld();
+                if (dst) {
+#pragma unroll
+                    for (int c = 0; c < 32; c += 4)
+                        *reinterpret_cast<float4*>(dst + 32 * c4 + c) =
+                            make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
+                }
+            }
+        } else if (live && nsplit > 1) {
+            // no keys in this split (or a failure): an empty partial
+            float* prow_p = part + (((size_t)qhead * n + s) * nsplit + sp) * kTcPartFloats;
+            prow_p[kHeadDim] = -INFINITY;
+            prow_p[kHeadDim + 1] = 0.f;
+        } else if (live && nst == 0) {
+            float* dst = out + (size_t)s * (pv.q_heads * kHeadDim) + (size_t)qhead * kHeadDim;
+            for (int c = 0; c < kHeadDim; ++c) dst[c] = 0.f;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// Merge of the key splits: one CTA per (query, 4 query heads), one thread per
+// (head, dim).
+__global__ void __launch_bounds__(4 * kHeadDim)
+    prefill_tc_merge_kernel(int q_heads, int n, const float* __restrict__ part, float* __restrict__ out,
+                            int nsplit) {
+    const int s = blockIdx.x, qhead = blockIdx.y * 4 + threadIdx.y, d = threadIdx.x;
+    if (qhead >= q_heads) return;
+    float M = -INFINITY, L = 0.f, A = 0.f;
+    for (int sp = 0; sp < nsplit; ++sp) {
+        const float* pr = part + (((size_t)qhead * n + s) * nsplit + sp) * kTcPartFloats;
+        const float lc = __ldcg(pr + kHeadDim + 1);
+        if (!(lc > 0.f)) continue;
+        const float mc = __ldcg(pr + kHeadDim);
+        const float Mn = fmaxf(M, mc);
+        const float a = fast_exp2(M - Mn), e = lc * fast_exp2(mc - Mn);
+        A = A * a + e * __ldcg(pr + d);
+        L = L * a + e;
+        M = Mn;
+    }
+    out[(size_t)s * q_heads * kHeadDim + (size_t)qhead * kHeadDim + d] = L > 0.f ? A / L : 0.f;
+}
+
+size_t prefill_tc_smem_bytes() { return sizeof(TcSmem) + 1024; }
+
+int prefill_tc_tokens_per_cta(int group) { return kTcRows / group; }
+size_t prefill_tc_part_floats(int q_heads, int n, int nsplit) {
+    return (size_t)q_heads * n * nsplit * kTcPartFloats;
+}
+
+cudaError_t launch_prefill_tc(const PoolView& pv, int layer, int seq, int pos0, int n, const float* q,
+                              float* out, float* part, int nsplit, int tiles_per_split, cudaStream_t st) {
+    const int Tc = kTcRows / pv.group;
+    const int smem = (int)prefill_tc_smem_bytes();
+    const dim3 grid((unsigned)((n + Tc - 1) / Tc), (unsigned)pv.kv_heads, (unsigned)nsplit);
+    cudaError_t e;
+    if (pv.dtype == 0) {
+        e = cudaFuncSetAttribute(prefill_tc_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        prefill_tc_kernel<0><<<grid, kTcThreads, smem, st>>>(pv, layer, seq, pos0, n, q, out, part, nsplit,
+                                                             tiles_per_split);
+    } else {
+        e = cudaFuncSetAttribute(prefill_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        prefill_tc_kernel<1><<<grid, kTcThreads, smem, st>>>(pv, layer, seq, pos0, n, q, out, part, nsplit,
+                                                             tiles_per_split);
+    }
+    e = counted(cudaGetLastError());
+    if (e != cudaSuccess || nsplit == 1) return e;
+    prefill_tc_merge_kernel<<<dim3((unsigned)n, (unsigned)((pv.q_heads + 3) / 4)), dim3(kHeadDim, 4), 0, st>>>(
+        pv.q_heads, n, part, out, nsplit);
+    return counted(cudaGetLastError());
+}
+
+}  // namespace kvattn

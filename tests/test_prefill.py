@@ -21,7 +21,7 @@ def rel_err(gpu, ref):
     return float((np.abs(g - r).max(axis=1) / den).max())
 
 
-def run_case(kv, orc, L0, chunks, dtype, layers=1, qh=12, kvh=2, seed=0):
+def run_case(kv, orc, L0, chunks, dtype, layers=1, qh=12, kvh=2, seed=0, kernel="tc"):
     rng = np.random.default_rng(seed)
     kvd, hid = kvh * HD, qh * HD
     total = L0 + sum(chunks)
@@ -48,7 +48,7 @@ def run_case(kv, orc, L0, chunks, dtype, layers=1, qh=12, kvh=2, seed=0):
             v = rng.standard_normal((n, kvd)).astype(np.float32)
             out = torch.empty((n, hid), device="cuda")
             P.append_chunk(y, s, pos, torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda())
-            P.prefill(y, s, pos, torch.from_numpy(q).cuda(), out)
+            P.prefill(y, s, pos, torch.from_numpy(q).cuda(), out, kernel=kernel)
             kc, vc = caches[y]
             ref, _, _ = orc.layer_step(q, k, v, kc, vc, pos, qh, kvh, HD, 1e6, dtype)
             worst = max(worst, rel_err(out.cpu().numpy(), ref))
@@ -62,35 +62,42 @@ def run_case(kv, orc, L0, chunks, dtype, layers=1, qh=12, kvh=2, seed=0):
     return worst
 
 
+KERNELS = ["tc", "mma"]  # tcgen05 (attn_prefill) and the mma.sync baseline (attn_prefill_mma)
+
+
 @pytest.mark.gpu
+@pytest.mark.parametrize("kernel", KERNELS)
 @pytest.mark.parametrize("dtype", [0, 1], ids=["f16", "bf16"])
-def test_prefill_ragged_chunks(kv, orc, dtype):
+def test_prefill_ragged_chunks(kv, orc, dtype, kernel):
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     # first chunk at position 0, then ragged sizes and offsets off the block grid
-    assert run_case(kv, orc, 0, [1, 15, 16, 17, 100], dtype, layers=2, seed=dtype) <= TOL
+    assert run_case(kv, orc, 0, [1, 15, 16, 17, 100], dtype, layers=2, seed=dtype, kernel=kernel) <= TOL
 
 
 @pytest.mark.gpu
-def test_prefill_512_chunks_after_context(kv, orc):
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_prefill_512_chunks_after_context(kv, orc, kernel):
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
-    assert run_case(kv, orc, 1003, [512, 512], 1, seed=3) <= TOL
+    assert run_case(kv, orc, 1003, [512, 512], 1, seed=3, kernel=kernel) <= TOL
 
 
 @pytest.mark.gpu
-def test_prefill_long_context_many_splits(kv, orc):
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_prefill_long_context_many_splits(kv, orc, kernel):
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
-    assert run_case(kv, orc, 6000, [64, 33], 0, seed=4) <= TOL
+    assert run_case(kv, orc, 6000, [64, 33], 0, seed=4, kernel=kernel) <= TOL
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("qh,kvh", [(16, 2), (4, 4), (8, 1)])
-def test_prefill_group_sizes(kv, orc, qh, kvh):
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("qh,kvh", [(16, 2), (4, 4), (8, 1), (6, 1), (10, 2)])
+def test_prefill_group_sizes(kv, orc, qh, kvh, kernel):
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
-    assert run_case(kv, orc, 300, [40], 1, qh=qh, kvh=kvh, seed=qh) <= TOL
+    assert run_case(kv, orc, 300, [40], 1, qh=qh, kvh=kvh, seed=qh, kernel=kernel) <= TOL
 
 
 def test_prefill_rejects_bad_calls():
