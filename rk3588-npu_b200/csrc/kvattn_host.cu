@@ -749,14 +749,15 @@ int attn_prefill(kvp_pool* p, int layer, int seq, int pos0, int n, const float* 
     const int max_tiles = (pos0 + n - 1) / kBlockTokens + 1;
     const long ctas = (long)nq * p->kv_heads;
     // One CTA per SM is resident: pick the split count that minimises
-    // waves x (tiles per CTA + a fixed cost per CTA of ~8 tiles) + a merge
-    // cost per split, with at least one 64-key stage per split.
+    // waves x (tiles per CTA + a fixed cost per CTA of ~16 tiles: q setup and
+    // the first copies) + a merge cost per split, with at least one 64-key
+    // stage per split.
     const int max_split = std::max(1, std::min(64, max_tiles / 4));
     int nsplit = 1;
     double best = 1e30;
     for (int ns = 1; ns <= max_split; ++ns) {
         const long waves = (ctas * ns + p->num_sms - 1) / p->num_sms;
-        const double cost = (double)waves * ((double)max_tiles / ns + 8.0) + 0.25 * ns;
+        const double cost = (double)waves * ((double)max_tiles / ns + 16.0) + 0.25 * ns;
         if (cost < best - 1e-9) {
             best = cost;
             nsplit = ns;

@@ -151,14 +151,21 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, const Po
 // Swizzled byte offset of 16-byte chunk c (0..7) of row r in a 128-byte-row region.
 __device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
+// P split into hi + lo 16-bit halves.  For bf16 with integer ops only: hi =
+// the upper 16 bits (truncation, remainder below 2^-7 |p|, exact in fp32),
+// lo = the upper 16 bits of that remainder, so |hi + lo - p| < 2^-14 |p|.
+// For f16 the rounding converter is used.
 template <int DT>
-__device__ __forceinline__ uint32_t pack2(float a, float b) {
-    if (DT == 0) {
-        __half2 h = __floats2half2_rn(a, b);
-        return *reinterpret_cast<uint32_t*>(&h);
+__device__ __forceinline__ void split_p(float a, float b, uint32_t& hi, uint32_t& lo) {
+    if (DT == 1) {
+        const uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
+        hi = __byte_perm(ua, ub, 0x7632);
+        const float ra = a - __uint_as_float(ua & 0xFFFF0000u);
+        const float rb = b - __uint_as_float(ub & 0xFFFF0000u);
+        lo = __byte_perm(__float_as_uint(ra), __float_as_uint(rb), 0x7632);
+    } else {
+        split_pair<DT>(a, b, hi, lo);
     }
-    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
 }
 
 }  // namespace
@@ -206,39 +213,47 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     if (warp == 4) {
         // ---------------------------------------------------------- producer
-        if (lane == 0) {
-            const uint64_t policy = policy_evict_first();
-            const int* trow = pv.table + (size_t)seq * pv.max_blocks_per_seq;
-            int issued = 0;
-            for (int j = 0; j < nst; ++j) {
-                const int b = j % kTcKvStages;
-                if (j >= kTcKvStages && !tc_wait(&sm.empty[b], ((j / kTcKvStages) - 1) & 1, pv, 700, &sm.failed))
-                    break;
-                if (*reinterpret_cast<volatile int*>(&sm.failed)) break;
-                int tiles = 0;
-                for (int u = 0; u < 4; ++u) tiles += (t_begin + 4 * j + u < t_end);
-                mbar_arrive_expect_tx(&sm.full[b], (uint32_t)tiles * 2u * kTileBytes);
-                for (int u = 0; u < tiles; ++u) {
-                    const int t = t_begin + 4 * j + u;
-                    int blk = (t < pv.max_blocks_per_seq) ? trow[t] : -1;
-                    if (blk < 0 || blk >= pv.num_blocks) {
-                        if (atomicCAS(pv.status, 0, 5) == 0) {
-                            pv.status[1] = t;
-                            pv.status[2] = 701;
-                        }
-                        blk = 0;  // stay inside the pool; the status voids the outputs
-                    }
-                    const size_t off = (size_t)layer * pv.layer_bytes + ((size_t)blk * pv.kv_heads + h) * kTileBytes;
-                    bulk_g2s_hint(sm.k[b][0] + u * 2048, pv.k + off, 2048, &sm.full[b], policy);
-                    bulk_g2s_hint(sm.k[b][1] + u * 2048, pv.k + off + 2048, 2048, &sm.full[b], policy);
-                    bulk_g2s_hint(sm.v[b][u], pv.v + off, kTileBytes, &sm.full[b], policy);
-                }
-                ++issued;
+        // Lane 0 waits for the stage and arms its barrier; lanes 0-3 then
+        // issue one tile each (its block id, two K halves, the V tile).
+        const uint64_t policy = policy_evict_first();
+        const int* trow = pv.table + (size_t)seq * pv.max_blocks_per_seq;
+        int issued = 0;
+        for (int j = 0; j < nst; ++j) {
+            const int b = j % kTcKvStages;
+            int tiles = 0;
+            for (int u = 0; u < 4; ++u) tiles += (t_begin + 4 * j + u < t_end);
+            int go = 1;
+            if (lane == 0) {
+                if (j >= kTcKvStages &&
+                    !tc_wait(&sm.empty[b], ((j / kTcKvStages) - 1) & 1, pv, 700, &sm.failed))
+                    go = 0;
+                if (*reinterpret_cast<volatile int*>(&sm.failed)) go = 0;
+                if (go) mbar_arrive_expect_tx(&sm.full[b], (uint32_t)tiles * 2u * kTileBytes);
             }
-            // Drain: the stages issued last must land before the CTA exits.
+            go = __shfl_sync(0xffffffffu, go, 0);
+            if (!go) break;
+            if (lane < tiles) {
+                const int t = t_begin + 4 * j + lane;
+                int blk = (t < pv.max_blocks_per_seq) ? trow[t] : -1;
+                if (blk < 0 || blk >= pv.num_blocks) {
+                    if (atomicCAS(pv.status, 0, 5) == 0) {
+                        pv.status[1] = t;
+                        pv.status[2] = 701;
+                    }
+                    blk = 0;  // stay inside the pool; the status voids the outputs
+                }
+                const size_t off = (size_t)layer * pv.layer_bytes + ((size_t)blk * pv.kv_heads + h) * kTileBytes;
+                bulk_g2s_hint(sm.k[b][0] + lane * 2048, pv.k + off, 2048, &sm.full[b], policy);
+                bulk_g2s_hint(sm.k[b][1] + lane * 2048, pv.k + off + 2048, 2048, &sm.full[b], policy);
+                bulk_g2s_hint(sm.v[b][lane], pv.v + off, kTileBytes, &sm.full[b], policy);
+            }
+            __syncwarp();
+            ++issued;
+        }
+        // Drain: the stages issued last must land before the CTA exits.
+        if (lane == 0)
             for (int j = issued > kTcKvStages ? issued - kTcKvStages : 0; j < issued; ++j)
                 mbar_wait_bounded(&sm.full[j % kTcKvStages], (j / kTcKvStages) & 1, kTcWaitLimit);
-        }
     } else if (warp == 5) {
         // ------------------------------------------------------------- MMA
         if (lane == 0) {
@@ -319,42 +334,57 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const bool live = tok < Tc && s < n;
         const int qhead = h * G + g;
         const int prow = pos0 + s;  // keys <= prow count for this row
-        // q row: rotate (non-fused, host cos/sin), scale, split into hi + lo
+        // q rows: warp w prepares rows 32w..32w+31 one row at a time, lane l
+        // holding dims 4l..4l+3 (one coalesced 512-byte load per row); the
+        // NeoX partner of dim d < 64 is d + 64, i.e. lane l ^ 16.  Rotate
+        // (non-fused, host cos/sin), scale, split into hi + lo 16-bit halves
+        // and store into the swizzled K-major rows.
         {
             const float qscale = 0.08838834764831845f * 1.4426950408889634f;  // 1/sqrt(128) * log2(e)
-            const float* qr = q + (size_t)(live ? s : 0) * (pv.q_heads * kHeadDim) + (size_t)qhead * kHeadDim;
-            const float* cs = reinterpret_cast<const float*>(pv.rope + (size_t)(live ? prow : 0) * (kHeadDim / 2));
+            const int half = lane >> 4, c = (lane & 15) >> 1;  // dims 4l..: half, 16-byte chunk
+            const int ip = 4 * (lane & 15);                   // rotation pair index of dim 4l
+            // 8 rows per batch: all their loads are issued before any is used.
 #pragma unroll 1
-            for (int c = 0; c < 8; ++c) {  // dims 8c..8c+7 and their partners 64+8c..
-                float lo[8], hi[8];
+            for (int i0 = 0; i0 < 32; i0 += 8) {
+                float4 xs[8], c0s[8], c1s[8];
 #pragma unroll
-                for (int e = 0; e < 8; e += 2) {
-                    const int i = 8 * c + e;
-                    float l0 = 0.f, h0 = 0.f, l1 = 0.f, h1 = 0.f;
-                    if (live) {
-                        const float2 a = *reinterpret_cast<const float2*>(qr + i);
-                        const float2 bb = *reinterpret_cast<const float2*>(qr + i + 64);
-                        const float4 t = *reinterpret_cast<const float4*>(cs + 2 * i);
-                        rope_pair(a.x, bb.x, t.x, t.y, l0, h0);
-                        rope_pair(a.y, bb.y, t.z, t.w, l1, h1);
+                for (int u = 0; u < 8; ++u) {
+                    const int rr = warp * 32 + i0 + u;
+                    const int tk = rr / G, gg = rr % G, ss = s0 + tk;
+                    xs[u] = c0s[u] = c1s[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (tk < Tc && ss < n) {  // the same for the whole warp
+                        xs[u] = __ldg(reinterpret_cast<const float4*>(q + (size_t)ss * (pv.q_heads * kHeadDim) +
+                                                                      (size_t)(h * G + gg) * kHeadDim + 4 * lane));
+                        const float* cs = reinterpret_cast<const float*>(pv.rope + (size_t)(pos0 + ss) * (kHeadDim / 2));
+                        c0s[u] = __ldg(reinterpret_cast<const float4*>(cs + 2 * ip));      // pairs ip, ip+1
+                        c1s[u] = __ldg(reinterpret_cast<const float4*>(cs + 2 * ip + 4));  // pairs ip+2, ip+3
                     }
-                    lo[e] = l0 * qscale;
-                    lo[e + 1] = l1 * qscale;
-                    hi[e] = h0 * qscale;
-                    hi[e + 1] = h1 * qscale;
-                }
-                uint32_t wh[2][4], wl[2][4];  // [dims half][pairs]
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    split_pair<DT>(lo[2 * e], lo[2 * e + 1], wh[0][e], wl[0][e]);
-                    split_pair<DT>(hi[2 * e], hi[2 * e + 1], wh[1][e], wl[1][e]);
                 }
 #pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    *reinterpret_cast<uint4*>(sm.q[0][half] + swz(r, c)) =
-                        make_uint4(wh[half][0], wh[half][1], wh[half][2], wh[half][3]);
-                    *reinterpret_cast<uint4*>(sm.q[1][half] + swz(r, c)) =
-                        make_uint4(wl[half][0], wl[half][1], wl[half][2], wl[half][3]);
+                for (int u = 0; u < 8; ++u) {
+                    const int rr = warp * 32 + i0 + u;
+                    const float4 x = xs[u], c0 = c0s[u], c1 = c1s[u];
+                    float y[4];
+                    y[0] = __shfl_xor_sync(0xffffffffu, x.x, 16);
+                    y[1] = __shfl_xor_sync(0xffffffffu, x.y, 16);
+                    y[2] = __shfl_xor_sync(0xffffffffu, x.z, 16);
+                    y[3] = __shfl_xor_sync(0xffffffffu, x.w, 16);
+                    const float xv[4] = {x.x, x.y, x.z, x.w};
+                    const float cc[4] = {c0.x, c0.z, c1.x, c1.z}, sn[4] = {c0.y, c0.w, c1.y, c1.w};
+                    float o[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        float r0, r1;  // (first half, second half) of the rotated pair
+                        if (half == 0) rope_pair(xv[e], y[e], cc[e], sn[e], r0, r1);
+                        else rope_pair(y[e], xv[e], cc[e], sn[e], r0, r1);
+                        o[e] = (half == 0 ? r0 : r1) * qscale;
+                    }
+                    uint32_t wh[2], wl[2];
+                    split_pair<DT>(o[0], o[1], wh[0], wl[0]);
+                    split_pair<DT>(o[2], o[3], wh[1], wl[1]);
+                    const uint32_t off = swz(rr, c) + (uint32_t)((lane & 1) * 8);
+                    *reinterpret_cast<uint2*>(sm.q[0][half] + off) = make_uint2(wh[0], wh[1]);
+                    *reinterpret_cast<uint2*>(sm.q[1][half] + off) = make_uint2(wl[0], wl[1]);
                 }
             }
         }
@@ -449,7 +479,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int c = 0; c < 8; ++c) {
                 uint32_t ph[4], pl[4];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) split_pair<DT>(sc[8 * c + 2 * e], sc[8 * c + 2 * e + 1], ph[e], pl[e]);
+                for (int e = 0; e < 4; ++e) split_p<DT>(sc[8 * c + 2 * e], sc[8 * c + 2 * e + 1], ph[e], pl[e]);
                 *reinterpret_cast<uint4*>(sm.p[0] + swz(r, c)) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
                 *reinterpret_cast<uint4*>(sm.p[1] + swz(r, c)) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
             }
