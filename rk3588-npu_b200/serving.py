@@ -11,7 +11,9 @@ box keeps that per-sequence contract and adds three things:
               (Scheduler, the kvs_* C ABI);
   prefill     up to `prefill_slots` admitted requests append one chunk of
               their prompt per step (kv_append_chunk: RoPE + encode + store,
-              every layer), the length advancing after the last layer;
+              every layer) and, when the caller passes the chunk's queries,
+              attend it causally over the cache (attn_prefill, tcgen05), the
+              length advancing after the last layer;
   decode      every request whose prompt is in the cache advances one token
               per step (one plan, one fused append + attention launch per
               layer, one commit); a request that generated its budget frees
@@ -109,8 +111,10 @@ class Server:
         decode_io(layer, reqs) -> (q [n, hidden], k [n, kv_dim], v [n, kv_dim],
             out [n, hidden]) device fp32 for this rank's decoding requests
             (in the order given);
-        prefill_kv(layer, req, pos0, n) -> (k [n, kv_dim], v [n, kv_dim])
-            device fp32 for one prompt chunk.
+        prefill_kv(layer, req, pos0, n) -> (k [n, kv_dim], v [n, kv_dim]) device
+            fp32 for one prompt chunk, or (k, v, q [n, hidden], out [n, hidden])
+            to also run the chunk's causal attention (attn_prefill) after its
+            append.
         Returns the step's global counts (every rank returns the same)."""
         self.admit()
         dec = self.local_decode()
@@ -126,8 +130,10 @@ class Server:
                     q, k, v, out = decode_io(layer, dec)
                     self.pool.decode_layer(layer, q, k, v, out)
                 for r, c in local_chunks:
-                    k, v = prefill_kv(layer, r, r.filled, c)
-                    self.pool.append_chunk(layer, r.seq, r.filled, k, v)
+                    io = prefill_kv(layer, r, r.filled, c)
+                    self.pool.append_chunk(layer, r.seq, r.filled, io[0], io[1])
+                    if len(io) == 4:
+                        self.pool.prefill(layer, r.seq, r.filled, io[2], io[3])
         if dec:
             self.pool.commit()
         # ---- bookkeeping, identical on every rank ----

@@ -1,7 +1,8 @@
 """Continuous batching (serving.Server): placement, chunked prefill, decode,
 completion.  Host logic on CPU with two gloo ranks and bookkeeping-only
-pools; on the GPU, every decode output against the oracle and every cached
-row bit-exact through admissions, completions and block reuse."""
+pools; on the GPU, every decode output and every prefill chunk's attention
+against the oracle and every cached row bit-exact through admissions,
+completions and block reuse."""
 from __future__ import annotations
 
 import os
@@ -154,16 +155,21 @@ def test_serving_gpu_matches_oracle_with_block_reuse():
         state[layer] = (reqs, qh, kh, vh, out)
         return (torch.from_numpy(qh).cuda(), torch.from_numpy(kh).cuda(), torch.from_numpy(vh).cuda(), out)
 
+    prefill_checks = []
+
     def prefill_kv(layer, req, pos0, n):
+        """The chunk's k/v and q; the oracle appends and attends the same
+        chunk (op_attention with seq = n) on the mirror."""
         if req.rid not in mirror:
             new_mirror(req)
+        qh = rng.standard_normal((n, hid)).astype(np.float32)
         kh = rng.standard_normal((n, kvd)).astype(np.float32)
         vh = rng.standard_normal((n, kvd)).astype(np.float32)
         kc, vc = mirror[req.rid][layer]
-        orc.lib().orc_rope_append(np.zeros((n, hid), np.float32).reshape(-1), kh.copy().reshape(-1),
-                                  vh.reshape(-1), kc.reshape(-1), vc.reshape(-1), n, pos0, 12, 2, 128,
-                                  1e6, dtype)
-        return torch.from_numpy(kh).cuda(), torch.from_numpy(vh).cuda()
+        ref, _, _ = orc.layer_step(qh, kh, vh, kc, vc, pos0, dtype=dtype)
+        out = torch.empty((n, hid), device="cuda")
+        prefill_checks.append((out, ref))
+        return (torch.from_numpy(kh).cuda(), torch.from_numpy(vh).cuda(), torch.from_numpy(qh).cuda(), out)
 
     reused = False
     for step in range(200):
@@ -171,8 +177,13 @@ def test_serving_gpu_matches_oracle_with_block_reuse():
             break
         before = {r.rid: r.length for r in srv.decoding}
         state.clear()
+        prefill_checks.clear()
         srv.step(decode_io, prefill_kv)
         reused = reused or bool(srv.finished and (srv.prefilling or srv.decoding))
+        for out, ref in prefill_checks:  # chunk attention against the oracle
+            g = out.cpu().numpy().reshape(-1, 128).astype(np.float64)
+            rr = ref.reshape(-1, 128).astype(np.float64)
+            worst = max(worst, float((np.abs(g - rr).max(1) / np.abs(rr).max(1)).max()))
         for layer, (reqs, qh, kh, vh, out) in state.items():
             got = out.cpu().numpy()
             for i, r in enumerate(reqs):
