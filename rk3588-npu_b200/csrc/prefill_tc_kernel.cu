@@ -7,21 +7,26 @@
 //
 // One CTA = one KV head h, Tc = 128 / G query tokens x the G query heads of the
 // group = up to 128 rows (row r = token r / G, head r % G), one key split.
-//   warps 0-3  rows: thread r owns tensor-memory lane r = row r.  They rotate,
+//   warps 0-7  rows: warps w and w+4 own tensor-memory lanes 32(w%4).. (rows),
+//              each half of the row's columns.  They rotate,
 //              scale and split their q row into 16-bit hi + lo halves in shared
 //              memory (K-major, 128-byte swizzle), then per key stage of 64
 //              keys read the row's scores from tensor memory, apply the causal
 //              mask, run the online softmax, rescale the output row in tensor
-//              memory when the row maximum moved, and write P (hi + lo) back to
-//              shared memory as the next MMA's A operand;
-//   warp 4     producer: bulk async copies (TMA engine, into this CTA only) of
+//              memory when the row maximum moved, and write P (hi + lo) back
+//              over the stage's score columns in tensor memory, where the
+//              P*V MMA reads it as its A operand;
+//   warp 8     producer: bulk async copies (TMA engine, into this CTA only) of
 //              the stage's four (block, head) tiles -- each K tile as two
 //              2 KiB halves into two 64-row K-major regions, each V tile whole;
-//   warp 5     allocates 256 tensor-memory columns (two 64-column score
-//              buffers, a 128-column output) and one elected lane issues the
-//              MMAs:  S = Qhi K^T + Qlo K^T  (M 128, N 64, K 16 x 8 x 2),
-//                     O += Phi V + Plo V    (M 128, N 128, K 16 x 4 x 2; the
-//              pool's V tile is an MN-major operand as it lies), committing
+//   warp 9     allocates 512 tensor-memory columns (two 64-column score
+//              buffers, a 128-column output, 128 columns of Q hi + lo) and one
+//              elected lane issues the MMAs:
+//                     S = Qhi K^T + Qlo K^T  (M 128, N 64, K 16 x 8 x 2; Q from
+//              tensor memory, K from shared memory),
+//                     O += Phi V + Plo V    (M 128, N 128, K 16 x 4 x 2; P from
+//              tensor memory, the pool's V tile an MN-major operand as it
+//              lies), committing
 //              each group to an mbarrier.  The next stage's S is computed while
 //              the rows run the softmax of this one (double-buffered S); the
 //              issuing lane polls both conditions and issues whichever group is
@@ -42,9 +47,11 @@ namespace {
 
 constexpr int kTcRows = 128;                 // MMA M: rows per CTA
 constexpr int kTcStageKeys = 64;             // keys per stage = 4 tiles
-constexpr int kTcThreads = 6 * 32;
-constexpr int kTcKvStages = 3;               // K/V stages in flight
-constexpr uint32_t kTmemCols = 256;          // S0 [0,64) S1 [64,128) O [128,256)
+constexpr int kTcRowWarps = 8;               // two softmax warps per row quarter
+constexpr int kTcThreads = (kTcRowWarps + 2) * 32;
+constexpr int kTcKvStages = 4;               // K/V stages in flight
+constexpr uint32_t kTmemCols = 512;          // S0 [0,64) S1 [64,128) O [128,256) Qhi [256,320) Qlo [320,384)
+constexpr uint32_t kTmemQ = 256;             // first column of Q (hi, then lo)
 constexpr long long kTcWaitLimit = 4000000000LL;
 constexpr int kTcPartFloats = kHeadDim + 4;  // 16-byte aligned rows
 constexpr float kTcRescale = 8.f;            // lazy-rescale threshold (log2 units)
@@ -54,8 +61,10 @@ struct TcSmem {
     uint8_t q[2][2][kTcRows * 128];         // [hi/lo][dims 0-63 / 64-127][row][128 B]
     uint8_t k[kTcKvStages][2][kTcStageKeys * 128];  // [stage][dims half][key][128 B]
     uint8_t v[kTcKvStages][4][kTileBytes];          // [stage][tile] pool tile layout
-    uint8_t p[2][kTcRows * 128];                    // [hi/lo][row][64 keys x 2 B]
     uint64_t full[kTcKvStages], empty[kTcKvStages], s_full[2], p_ready, o_done, q_ready, mma_done;
+    float xmax[2][2][kTcRows];  // [stage parity][column half][row]: the pair's row maxima
+    float xsum[2][kTcRows];     // [column half][row]: the pair's row sums
+    int xbad[2][2][4];          // [stage parity][column half][row quarter]: a wait gave up
     uint32_t tmem_base;
     int failed;
 };
@@ -85,6 +94,16 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
         " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem desc]: A (M rows x K 16-bit values) read from
+// tensor memory, lane = row, two K values per 32-bit column.
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 // Arrive once on `bar` when every MMA this thread issued so far has completed.
@@ -119,6 +138,16 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&r)[32]) 
         "r"(u[9]), "r"(u[10]), "r"(u[11]), "r"(u[12]), "r"(u[13]), "r"(u[14]), "r"(u[15]), "r"(u[16]),
         "r"(u[17]), "r"(u[18]), "r"(u[19]), "r"(u[20]), "r"(u[21]), "r"(u[22]), "r"(u[23]), "r"(u[24]),
         "r"(u[25]), "r"(u[26]), "r"(u[27]), "r"(u[28]), "r"(u[29]), "r"(u[30]), "r"(u[31])
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&r)[16]) {
+    const uint32_t* u = reinterpret_cast<const uint32_t*>(r);
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(u[0]), "r"(u[1]), "r"(u[2]), "r"(u[3]), "r"(u[4]), "r"(u[5]), "r"(u[6]), "r"(u[7]), "r"(u[8]),
+        "r"(u[9]), "r"(u[10]), "r"(u[11]), "r"(u[12]), "r"(u[13]), "r"(u[14]), "r"(u[15])
         : "memory");
 }
 
@@ -195,14 +224,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_init(&sm.empty[i], 1);
         }
         for (int i = 0; i < 2; ++i) mbar_init(&sm.s_full[i], 1);
-        mbar_init(&sm.p_ready, 128);
+        mbar_init(&sm.p_ready, kTcRowWarps * 32);
         mbar_init(&sm.o_done, 1);
-        mbar_init(&sm.q_ready, 128);
+        mbar_init(&sm.q_ready, kTcRowWarps * 32);
         mbar_init(&sm.mma_done, 1);
         sm.failed = 0;
     }
     fence_mbar_init();
-    if (warp == 5) {
+    if (warp == kTcRowWarps + 1) {
         tmem_alloc(&sm.tmem_base, kTmemCols);
         tmem_relinquish();
     }
@@ -211,7 +240,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
 
-    if (warp == 4) {
+    if (warp == kTcRowWarps) {
         // ---------------------------------------------------------- producer
         // Lane 0 waits for the stage and arms its barrier; lanes 0-3 then
         // issue one tile each (its block id, two K halves, the V tile).
@@ -254,14 +283,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (lane == 0)
             for (int j = issued > kTcKvStages ? issued - kTcKvStages : 0; j < issued; ++j)
                 mbar_wait_bounded(&sm.full[j % kTcKvStages], (j / kTcKvStages) & 1, kTcWaitLimit);
-    } else if (warp == 5) {
+    } else if (warp == kTcRowWarps + 1) {
         // ------------------------------------------------------------- MMA
         if (lane == 0) {
             const uint32_t id_qk = idesc_f16(DT, kTcRows, kTcStageKeys, 0);
             const uint32_t id_pv = idesc_f16(DT, kTcRows, kHeadDim, 1);
-            const uint32_t q0 = smem_u32(sm.q[0][0]);
-            const uint32_t p0 = smem_u32(sm.p[0]);
             bool ok = tc_wait(&sm.q_ready, 0, pv, 710, &sm.failed);
+            // Q (hi, lo) is read from tensor memory: dims 16kk.. are columns
+            // 8kk.. of each 64-column block.
             auto issue_qk = [&](int j) {
                 const uint32_t kb = smem_u32(sm.k[j % kTcKvStages][0]);
                 const uint32_t d = tmem + (uint32_t)((j & 1) * kTcStageKeys);
@@ -270,10 +299,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     const uint32_t koff = (uint32_t)((kk >> 2) * (kTcStageKeys * 128) + (kk & 3) * 32);
                     const uint64_t bd = sdesc(kb + koff, 16, 1024);
 #pragma unroll
-                    for (int hl = 0; hl < 2; ++hl) {
-                        const uint32_t qoff = (uint32_t)(hl * 2 * kTcRows * 128 + (kk >> 2) * (kTcRows * 128) + (kk & 3) * 32);
-                        tc_mma(d, sdesc(q0 + qoff, 16, 1024), bd, id_qk, (kk | hl) != 0);
-                    }
+                    for (int hl = 0; hl < 2; ++hl)
+                        tc_mma_ts(d, tmem + kTmemQ + (uint32_t)(hl * 64 + kk * 8), bd, id_qk, (kk | hl) != 0);
                 }
                 tc_commit(&sm.s_full[j & 1]);
             };
@@ -283,9 +310,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int u = 0; u < 4; ++u) {
                     const uint64_t bd = sdesc(smem_u32(sm.v[b][u]), 2048, 1024);
 #pragma unroll
-                    for (int hl = 0; hl < 2; ++hl)
-                        tc_mma(tmem + 128u, sdesc(p0 + (uint32_t)(hl * kTcRows * 128 + u * 32), 16, 1024), bd,
-                               id_pv, (j | u | hl) != 0);
+                    for (int hl = 0; hl < 2; ++hl)  // P of stage j sits in its score columns
+                        tc_mma_ts(tmem + 128u, tmem + (uint32_t)((j & 1) * kTcStageKeys + hl * 32 + u * 8), bd,
+                                  id_pv, (j | u | hl) != 0);
                 }
                 tc_commit(&sm.o_done);
                 tc_commit(&sm.empty[b]);
@@ -328,13 +355,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
     } else {
         // ------------------------------------------------------------ rows
-        const int r = tid;  // 0..127: tensor-memory lane and CTA row
+        // Warps w and w + 4 share tensor-memory lanes 32(w%4).. (the CTA rows
+        // 32(w%4)..+31): warp w < 4 takes score columns 0-31 and output
+        // columns 0-63 of those rows, warp w + 4 the other halves; the pair
+        // exchanges its row maxima (and at the end its row sums) through
+        // shared memory at its own named barrier.
+        const int quarter = warp & 3, ch = warp >> 2;
+        const int r = quarter * 32 + lane;  // tensor-memory lane and CTA row
+        const int tr = warp * 32 + lane;    // 0..255
         const int tok = r / G, g = r % G;
         const int s = s0 + tok;
         const bool live = tok < Tc && s < n;
         const int qhead = h * G + g;
         const int prow = pos0 + s;  // keys <= prow count for this row
-        // q rows: warp w prepares rows 32w..32w+31 one row at a time, lane l
+        const int bar_id = 1 + quarter;
+        // q rows: warp w prepares rows 16w..16w+15 one row at a time, lane l
         // holding dims 4l..4l+3 (one coalesced 512-byte load per row); the
         // NeoX partner of dim d < 64 is d + 64, i.e. lane l ^ 16.  Rotate
         // (non-fused, host cos/sin), scale, split into hi + lo 16-bit halves
@@ -345,11 +380,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int ip = 4 * (lane & 15);                   // rotation pair index of dim 4l
             // 8 rows per batch: all their loads are issued before any is used.
 #pragma unroll 1
-            for (int i0 = 0; i0 < 32; i0 += 8) {
+            for (int i0 = 0; i0 < 16; i0 += 8) {
                 float4 xs[8], c0s[8], c1s[8];
 #pragma unroll
                 for (int u = 0; u < 8; ++u) {
-                    const int rr = warp * 32 + i0 + u;
+                    const int rr = warp * 16 + i0 + u;
                     const int tk = rr / G, gg = rr % G, ss = s0 + tk;
                     xs[u] = c0s[u] = c1s[u] = make_float4(0.f, 0.f, 0.f, 0.f);
                     if (tk < Tc && ss < n) {  // the same for the whole warp
@@ -362,7 +397,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
 #pragma unroll
                 for (int u = 0; u < 8; ++u) {
-                    const int rr = warp * 32 + i0 + u;
+                    const int rr = warp * 16 + i0 + u;
                     const float4 x = xs[u], c0 = c0s[u], c1 = c1s[u];
                     float y[4];
                     y[0] = __shfl_xor_sync(0xffffffffu, x.x, 16);
@@ -388,44 +423,70 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             }
         }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        // Each row into its tensor-memory lane, the QK MMA's A operand:
+        // warp ch = 0 copies the row's hi half, ch = 1 its lo half (64
+        // columns, two dims per column), unswizzling the staged rows.
+        named_bar_sync(5, kTcRowWarps * 32);  // every row staged
+        const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+#pragma unroll 1
+        for (int c2 = 0; c2 < 2; ++c2) {  // dims 64c2..64c2+63 = columns 32c2..
+            float w[32];
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) {
+                const uint4 v4 = *reinterpret_cast<const uint4*>(sm.q[ch][c2] + swz(r, cc));
+                w[4 * cc + 0] = __uint_as_float(v4.x);
+                w[4 * cc + 1] = __uint_as_float(v4.y);
+                w[4 * cc + 2] = __uint_as_float(v4.z);
+                w[4 * cc + 3] = __uint_as_float(v4.w);
+            }
+            tmem_st32(tmem + lane_base + kTmemQ + (uint32_t)(ch * 64 + c2 * 32), w);
+        }
+        tc_wait_st();
+        tc_fence_before();
         mbar_arrive(&sm.q_ready);
 
-        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-        float m = -INFINITY, l = 0.f;
+        float m = -INFINITY, lh = 0.f;  // lh: this half's share of the row sum
         bool ok = true;
+        bool bad = false;  // a bounded wait of this warp gave up (acted on with the partner)
         for (int j = 0; j < nst; ++j) {
-            if (!__all_sync(0xffffffffu, tc_wait(&sm.s_full[j & 1], (j >> 1) & 1, pv, 720, &sm.failed))) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            float sc[64];
-            {
-                float a[32], bq[32];
-                tmem_ld32(tmem + lane_base + (uint32_t)((j & 1) * kTcStageKeys), a);
-                tmem_ld32(tmem + lane_base + (uint32_t)((j & 1) * kTcStageKeys + 32), bq);
+            // Both warps of a pair meet at their named barrier exactly once
+            // per stage and leave the loop together: a failed wait is
+            // published next to the row maxima and acted on after the barrier.
+            bad = bad || !__all_sync(0xffffffffu, tc_wait(&sm.s_full[j & 1], (j >> 1) & 1, pv, 720, &sm.failed));
+            float sc[32];
+            float mx = -INFINITY;
+            const int kbase = (t_begin + 4 * j) * kBlockTokens + ch * 32;
+            if (!bad) {
+                tc_fence_after();
+                tmem_ld32(tmem + lane_base + (uint32_t)((j & 1) * kTcStageKeys + ch * 32), sc);
                 tc_wait_ld();
+                float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
                 for (int c = 0; c < 32; ++c) {
-                    sc[c] = a[c];
-                    sc[32 + c] = bq[c];
+                    const int key = kbase + c;
+                    if (key > prow || key >= kv_lim) sc[c] = -INFINITY;
+                    mx4[c & 3] = fmaxf(mx4[c & 3], sc[c]);
                 }
+                mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
             }
-            const int kbase = (t_begin + 4 * j) * kBlockTokens;
-            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-            for (int c = 0; c < 64; ++c) {
-                const int key = kbase + c;
-                if (key > prow || key >= kv_lim) sc[c] = -INFINITY;
-                mx4[c & 3] = fmaxf(mx4[c & 3], sc[c]);
+            // exchange with the partner warp; the barrier also orders both
+            // warps' score reads before either writes P over those columns
+            sm.xmax[j & 1][ch][r] = mx;
+            if (lane == 0) sm.xbad[j & 1][ch][quarter] = bad ? 1 : 0;
+            tc_fence_before();
+            named_bar_sync(bar_id, 64);
+            tc_fence_after();
+            if (bad || sm.xbad[j & 1][ch ^ 1][quarter]) {
+                ok = false;
+                *reinterpret_cast<volatile int*>(&sm.failed) = 1;
+                break;
             }
-            const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+            mx = fmaxf(mx, sm.xmax[j & 1][ch ^ 1][r]);
             // Lazy rescale: the reference max m moves only when a score
             // exceeds it by more than kTcRescale (base 2), so weights stay
             // <= 2^kTcRescale and the output row in tensor memory is rescaled
-            // rarely; l and O always share the same reference, so the result
-            // is the same softmax.
+            // rarely; the sums and O always share the same reference, so the
+            // result is the same softmax.  Both warps of a row decide alike.
             float alpha = 1.f;
             if (mx > m + kTcRescale || m == -INFINITY) {
                 const float mn = fmaxf(m, mx);
@@ -436,97 +497,112 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const float mu = (m == -INFINITY) ? 0.f : m;
             float sum4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int c = 0; c < 64; ++c) {
+            for (int c = 0; c < 32; ++c) {
                 sc[c] = fast_exp2(sc[c] - mu);
                 sum4[c & 3] += sc[c];
             }
-            l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
+            lh = lh * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
             // The last stage: V rows of keys >= kv_lim may hold anything
             // (stale smem, rows past the sequence); zero them so masked
             // weights (exactly 0) stay 0.
             if (j == nst - 1) {
-                for (int x = r; x < kTcStageKeys * 16; x += 128) {  // (key row, 16-byte chunk)
-                    const int kr = x >> 4, ch = x & 15;
-                    if (kbase + kr >= kv_lim) {
+                const int kb0 = (t_begin + 4 * j) * kBlockTokens;
+                for (int x = tr; x < kTcStageKeys * 16; x += 256) {  // (key row, 16-byte chunk)
+                    const int kr = x >> 4, cq = x & 15;
+                    if (kb0 + kr >= kv_lim) {
                         const int u = kr >> 4, t = kr & 15;
-                        *reinterpret_cast<uint4*>(sm.v[j % kTcKvStages][u] + ((ch >> 3) * 16 + t) * 128 + (ch & 7) * 16) =
+                        *reinterpret_cast<uint4*>(sm.v[j % kTcKvStages][u] + ((cq >> 3) * 16 + t) * 128 + (cq & 7) * 16) =
                             make_uint4(0u, 0u, 0u, 0u);
                     }
                 }
             }
-            // Previous P*V done: P may be overwritten and O rescaled.
-            if (j >= 1) {
-                if (!__all_sync(0xffffffffu, tc_wait(&sm.o_done, (j - 1) & 1, pv, 721, &sm.failed))) {
-                    ok = false;
-                    break;
+            // P (hi + lo) over this stage's score columns: the A operand of
+            // P*V (hi of the 64 keys in columns 0-31, lo in 32-63, two keys
+            // per column; this warp's 32 keys are columns 16ch.. of each).
+            {
+                float ph[16], pl[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    uint32_t hh, ll;
+                    split_p<DT>(sc[2 * e], sc[2 * e + 1], hh, ll);
+                    ph[e] = __uint_as_float(hh);
+                    pl[e] = __uint_as_float(ll);
                 }
+                const uint32_t sbuf = tmem + lane_base + (uint32_t)((j & 1) * kTcStageKeys + ch * 16);
+                tmem_st16(sbuf, ph);
+                tmem_st16(sbuf + 32u, pl);
+            }
+            // The output row is rescaled only when its reference max moved
+            // (rare after the first stages); then the previous P*V must be done.
+            if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.f) &&
+                !(bad = !__all_sync(0xffffffffu, tc_wait(&sm.o_done, (j - 1) & 1, pv, 721, &sm.failed)))) {
                 tc_fence_after();
-                if (__any_sync(0xffffffffu, alpha != 1.f)) {  // rare after the first stages
 #pragma unroll 1
-                    for (int c4 = 0; c4 < 4; ++c4) {
-                        float o[32];
-                        tmem_ld32(tmem + lane_base + 128u + (uint32_t)(32 * c4), o);
-                        tc_wait_ld();
+                for (int c2 = 0; c2 < 2; ++c2) {
+                    float o[32];
+                    const uint32_t oc = tmem + lane_base + 128u + (uint32_t)(ch * 64 + 32 * c2);
+                    tmem_ld32(oc, o);
+                    tc_wait_ld();
 #pragma unroll
-                        for (int c = 0; c < 32; ++c) o[c] *= alpha;
-                        tmem_st32(tmem + lane_base + 128u + (uint32_t)(32 * c4), o);
-                    }
-                    tc_wait_st();
+                    for (int c = 0; c < 32; ++c) o[c] *= alpha;
+                    tmem_st32(oc, o);
                 }
             }
-            // P (hi + lo) as the A operand: row r, 64 keys = 8 chunks of 8
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                uint32_t ph[4], pl[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) split_p<DT>(sc[8 * c + 2 * e], sc[8 * c + 2 * e + 1], ph[e], pl[e]);
-                *reinterpret_cast<uint4*>(sm.p[0] + swz(r, c)) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
-                *reinterpret_cast<uint4*>(sm.p[1] + swz(r, c)) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
-            }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_wait_st();
+            if (j == nst - 1) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // zeroed V rows
             tc_fence_before();
             mbar_arrive(&sm.p_ready);
         }
-        // ---- the output row ----
-        if (ok && nst > 0 && __all_sync(0xffffffffu, tc_wait(&sm.o_done, (nst - 1) & 1, pv, 722, &sm.failed))) {
+        ok = ok && !bad;
+        // ---- the output row: this warp's 64 columns ----
+        const bool fin = ok && nst > 0 &&
+                         __all_sync(0xffffffffu, tc_wait(&sm.o_done, (nst - 1) & 1, pv, 722, &sm.failed));
+        sm.xsum[ch][r] = lh;
+        named_bar_sync(bar_id, 64);
+        const float l = lh + sm.xsum[ch ^ 1][r];
+        if (fin) {
             tc_fence_after();
             const float inv = l > 0.f ? 1.f / l : 0.f;
             float* dst = nullptr;
             if (live) {
                 if (nsplit == 1) {
-                    dst = out + (size_t)s * (pv.q_heads * kHeadDim) + (size_t)qhead * kHeadDim;
+                    dst = out + (size_t)s * (pv.q_heads * kHeadDim) + (size_t)qhead * kHeadDim + ch * 64;
                 } else {
                     float* prow_p = part + (((size_t)qhead * n + s) * nsplit + sp) * kTcPartFloats;
-                    prow_p[kHeadDim] = m;
-                    prow_p[kHeadDim + 1] = l;
-                    dst = prow_p;
+                    if (ch == 0) {
+                        prow_p[kHeadDim] = m;
+                        prow_p[kHeadDim + 1] = l;
+                    }
+                    dst = prow_p + ch * 64;
                 }
             }
 #pragma unroll 1
-            for (int c4 = 0; c4 < 4; ++c4) {
+            for (int c2 = 0; c2 < 2; ++c2) {
                 float o[32];
-                tmem_ld32(tmem + lane_base + 128u + (uint32_t)(32 * c4), o);
+                tmem_ld32(tmem + lane_base + 128u + (uint32_t)(ch * 64 + 32 * c2), o);
                 tc_wait_ld();
                 if (dst) {
 #pragma unroll
                     for (int c = 0; c < 32; c += 4)
-                        *reinterpret_cast<float4*>(dst + 32 * c4 + c) =
+                        *reinterpret_cast<float4*>(dst + 32 * c2 + c) =
                             make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
                 }
             }
         } else if (live && nsplit > 1) {
             // no keys in this split (or a failure): an empty partial
-            float* prow_p = part + (((size_t)qhead * n + s) * nsplit + sp) * kTcPartFloats;
-            prow_p[kHeadDim] = -INFINITY;
-            prow_p[kHeadDim + 1] = 0.f;
+            if (ch == 0) {
+                float* prow_p = part + (((size_t)qhead * n + s) * nsplit + sp) * kTcPartFloats;
+                prow_p[kHeadDim] = -INFINITY;
+                prow_p[kHeadDim + 1] = 0.f;
+            }
         } else if (live && nst == 0) {
-            float* dst = out + (size_t)s * (pv.q_heads * kHeadDim) + (size_t)qhead * kHeadDim;
-            for (int c = 0; c < kHeadDim; ++c) dst[c] = 0.f;
+            float* dst = out + (size_t)s * (pv.q_heads * kHeadDim) + (size_t)qhead * kHeadDim + ch * 64;
+            for (int c = 0; c < 64; ++c) dst[c] = 0.f;
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == kTcRowWarps + 1) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
