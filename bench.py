@@ -113,6 +113,14 @@ def make_workload(name: str) -> Workload:
             "positions) in every one of 28 layers, bf16 KV",
             "synthetic (seeded N(0,1) K/V/q; prompts seed 4)",
             None)
+    if name == "model1":
+        return Workload(
+            "model1", 1, 28, 0, None, None, False,
+            "Qwen2-1.5B greedy decode on one GPU: 28 layers, hidden 1536, 12 q / 2 kv heads x 128, "
+            "SwiGLU 8960, vocab 151936 (tied lm_head), fp16 weights and KV cache; prompt of 128 ids "
+            "uniform in [0,151936) (seed 0), then one greedy token per step",
+            "synthetic (random-init N(0,0.02) weights from seed 0, RMSNorm weights 1; prompt seed 0)",
+            None)
     if name == "serve":
         return Workload(
             "serve", 128, 28, 1, [L for L, _ in serve_stream()[0]], None, False,
@@ -132,7 +140,7 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload",
-                    choices=["batch32", "paged28", "paged1", "long1", "long4", "serve", "prefill"],
+                    choices=["batch32", "paged28", "paged1", "long1", "long4", "serve", "prefill", "model1"],
                     default="batch32")
     ap.add_argument("--transport", choices=["nccl", "p2p"], default="nccl",
                     help="long workloads: merge of the per-GPU states by NCCL all-gather + combine "
@@ -943,6 +951,195 @@ def cpu_baseline_prefill(pos0, ch, layers, seconds):
                       f"layers; fp16 caches (the reference's only cache type)"}
 
 
+def _qwen2():
+    load_pkg()
+    import importlib
+    return importlib.import_module("rk3588_npu_b200.qwen2")
+
+
+def run_model(args, rank, world, local):
+    """Qwen2-1.5B greedy decode through the device model (qw2_forward, one
+    token per step).  Every GPU runs its own replica of the model and its own
+    request (replicas only: no collective).  value: device time (CUDA events
+    on the model's stream around each step); e2e: the same calls timed on the
+    host clock (host token id in, host argmax out, the call's one sync)."""
+    import torch
+    kv = load_pkg()
+    kv.load()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    q2 = _qwen2()
+    wl = make_workload("model1")
+    K, W = args.steps, args.warmup
+    M = q2.Model(local)
+    t0 = time.perf_counter()
+    M.load_synthetic(seed=0)
+    load_s = time.perf_counter() - t0
+    stream = torch.cuda.current_stream()
+    kv.call("qw2_set_stream", M.h, stream.cuda_stream)
+    prompt = q2.synth_prompt(128, q2.QWEN2_1_5B["vocab"], seed=0).tolist()
+    assert len(prompt) + K + W <= q2.QWEN2_1_5B["max_position"], "steps + warmup must fit 512 positions"
+    _, nxt = M.forward(prompt)
+    for _ in range(W):
+        _, nxt = M.forward([nxt])
+    sampler = ClockSampler(range(local, local + 1)) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(args.settle)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    kc0 = kv.kernel_count()
+    pos0 = M.cur_pos()
+    t_host = time.perf_counter()
+    for i in range(K):
+        ev[i][0].record(stream)
+        _, nxt = M.forward([nxt])
+        ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    host_s = time.perf_counter() - t_host
+    kernels = kv.kernel_count() - kc0
+    step_ms = sum(a.elapsed_time(b) for a, b in ev)
+    clocks = sampler.stop() if sampler else None
+    times = torch.tensor([step_ms, host_s], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    step_ms, host_s = times[0].item(), times[1].item()
+    if rank == 0:
+        wbytes = M.weight_bytes()
+        # KV read of every layer at this step's length + the appended row
+        kv_bytes = 28 * 2 * 2 * 128 * 2 * (pos0 + K / 2 + 1)
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+            os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+        peak = float(peaks.get("hbm_gbs", 6650.0))
+        achieved = (wbytes + kv_bytes) / (step_ms / K * 1e-3) / 1e9
+        line = {
+            "metric": "Qwen2-1.5B greedy decode tokens/s and achieved HBM GB/s (weights + KV per token)",
+            "value": round(world * K / (step_ms * 1e-3), 2), "unit": "tokens/s", "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": round(step_ms / K, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": wl.data,
+            "config": {"workload": wl.desc, "name": wl.name, "prompt": 128, "positions_timed": [pos0, pos0 + K],
+                       "parallelism": "replicas only (one model and one request per GPU)",
+                       "l2": "inputs larger than L2 (3.09 GB of weights per step, no flush)",
+                       "weights_load_s": round(load_s, 1)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
+                         "note": "whole decode step (all launches); algorithmic bytes = fp16 weights "
+                                 f"({wbytes} B: 28 layers of projections + the tied lm_head) + KV rows read"},
+            "e2e": {"value": round(world * K / host_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4,
+                    "d2h_bytes_per_step": 4 + 4 * 32,
+                    "note": "qw2_forward from a host token id to the host argmax (and the pool's status "
+                            "words), host clock"},
+            "gpu_launches": int(kernels),
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_model(q2, max(1, int(args.cpu_seconds // 3)))
+        print(json.dumps(line), flush=True)
+    M.close()
+    if dist:
+        dist.destroy_process_group()
+
+
+def _ref_model(q2, tmpdir):
+    """The reference's Qwen2Model compiled from its sources (oracle/_ref),
+    loaded from an F16 safetensors file of the same seeded weights."""
+    import ctypes as C
+    so = os.path.join(ROOT, "oracle", "_ref", "libqwen2ref.so")
+    if not os.path.exists(so):
+        return None, None
+    R = C.CDLL(so)
+    R.ref_qwen2_load.restype = C.c_void_p
+    R.ref_qwen2_load.argtypes = [C.c_char_p]
+    R.ref_qwen2_forward.argtypes = [C.c_void_p, C.POINTER(C.c_int), C.c_int, C.c_void_p, C.c_int]
+    R.ref_greedy_sample.argtypes = [C.c_void_p, C.c_int]
+    R.ref_qwen2_free.argtypes = [C.c_void_p]
+    os.makedirs(tmpdir, exist_ok=True)
+    path = os.path.join(tmpdir, "model.safetensors")
+    cfg = q2.QWEN2_1_5B
+    q2.write_safetensors(path, q2.tensor_specs(cfg), q2.synth_weights(cfg, seed=0), dtype="F16")
+    R.ref_set_threads(os.cpu_count() or 1)
+    m = R.ref_qwen2_load(tmpdir.encode())
+    return R, m
+
+
+def _ref_decode(R, m, q2, ids):
+    import ctypes as C
+    V = q2.QWEN2_1_5B["vocab"]
+    logits = np.empty(V, np.float32)
+    a = (C.c_int * len(ids))(*ids)
+    R.ref_qwen2_forward(m, a, len(ids), logits.ctypes.data_as(C.c_void_p), V)
+    return R.ref_greedy_sample(logits.ctypes.data_as(C.c_void_p), V)
+
+
+def cpu_baseline_model(q2, tokens):
+    """The reference's own model (Qwen2Model::forward, CPU stand-in linears on
+    every host thread) decoding `tokens` greedy tokens from position 0."""
+    import shutil
+    tmp = "/tmp/qwen2_bench_ref"
+    R, m = _ref_model(q2, tmp)
+    if not m:
+        shutil.rmtree(tmp, ignore_errors=True)
+        return {"value": None, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "unavailable",
+                "sample": "oracle/_ref/libqwen2ref.so was not built"}
+    nxt = 0
+    t0 = time.perf_counter()
+    for _ in range(tokens):
+        nxt = _ref_decode(R, m, q2, [nxt])
+    dt = time.perf_counter() - t0
+    R.ref_qwen2_free(m)
+    shutil.rmtree(tmp, ignore_errors=True)
+    return {"value": round(tokens / dt, 3), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "reference",
+            "sample": f"{tokens} greedy decode tokens at positions 0..{tokens - 1} of the same seeded model "
+                      f"({dt:.1f} s), Qwen2Model::forward compiled from the reference sources with a CPU "
+                      f"fp16 linear stand-in on {os.cpu_count()} host threads"}
+
+
+def run_reference_model(args, world):
+    """Reference arm of the model workload: Qwen2Model::forward of the
+    reference (oracle/_ref), one greedy token per step, all host threads."""
+    q2 = _qwen2()
+    import shutil
+    tmp = "/tmp/qwen2_bench_ref"
+    R, m = _ref_model(q2, tmp)
+    wl = make_workload("model1")
+    if not m:
+        shutil.rmtree(tmp, ignore_errors=True)
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libqwen2ref.so was not built"}))
+        return
+    K, W = args.steps, args.warmup
+    nxt = 0
+    total = 0.0
+    for i in range(W + K):
+        t0 = time.perf_counter()
+        nxt = _ref_decode(R, m, q2, [nxt])
+        if i >= W:
+            total += time.perf_counter() - t0
+    R.ref_qwen2_free(m)
+    shutil.rmtree(tmp, ignore_errors=True)
+    value = round(K / total, 3)
+    cores = os.cpu_count()
+    sample = (f"{K} greedy decode tokens after {W} untimed, positions 0..{K + W - 1}, Qwen2Model::forward "
+              f"compiled from the reference sources with a CPU fp16 linear stand-in on {cores} host threads")
+    print(json.dumps({
+        "impl": "reference", "metric": "Qwen2-1.5B greedy decode tokens/s and achieved HBM GB/s (weights + KV per token)",
+        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": round(total / K * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": wl.data,
+        "config": {"workload": wl.desc, "name": wl.name},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "reference", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+        flush=True)
+
+
 # ------------------------------------------------------- CPU (reference) path
 def _oracle():
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -1075,6 +1272,9 @@ def run_reference(args, rank, world):
     if args.workload == "prefill":
         run_reference_prefill(args, world)
         return
+    if args.workload == "model1":
+        run_reference_model(args, world)
+        return
     wl = make_workload(args.workload)
     threads = max(1, min(os.cpu_count() or 1, wl.batch))
     kind, fn = cpu_step_fn(orc, threads)
@@ -1125,6 +1325,8 @@ def main():
         run_serve(args, rank, world, local)
     elif args.workload == "prefill":
         run_prefill(args, rank, world, local)
+    elif args.workload == "model1":
+        run_model(args, rank, world, local)
     else:
         run_ours(args, rank, world, local)
 

@@ -191,6 +191,51 @@ int xchg_prepare(::kvx_exch* x, int device, int rows, int* status, float* out, X
                  float** m, float** l, float** o);
 void xchg_commit(::kvx_exch* x);
 
+// ---- Qwen2 forward kernels (model_kernels.cu) ----
+// One projection y = epilogue(x W^T): W fp16 [N][K], x [M][K]: in = 0 fp16
+// bits, 1 fp32 rounded through fp16, 2 fp32 rows RMSNorm'd with norm_w / eps
+// and rounded through fp16.  Modes: 0 QKV (fp16-rounded + bias,
+// rows n < n0 to out0 [M][n0], then n1 rows to out1 [M][n1], the rest to out2),
+// 1 residual (resid [M][N] += rounded), 2 gate/up (w = gate, w2 = up; out16
+// [M][N] = fp16(silu(g) * u)), 3 logits (logits [M][N] = rounded).
+struct GemvArgs {
+    const uint16_t* w = nullptr;
+    const uint16_t* w2 = nullptr;
+    int N = 0, K = 0, M = 0, ks = 1;
+    const void* x = nullptr;
+    const float* bias = nullptr;
+    float* out0 = nullptr;
+    float* out1 = nullptr;
+    float* out2 = nullptr;
+    int n0 = 0, n1 = 0;
+    float* resid = nullptr;
+    uint16_t* out16 = nullptr;
+    float* logits = nullptr;
+    const float* norm_w = nullptr;
+    float eps = 0.f;
+};
+cudaError_t launch_gemv(int mode, int in, GemvArgs a, cudaStream_t st);
+int gemv_split(int K);
+cudaError_t launch_rmsnorm_f16(const float* x, const float* w, uint16_t* y, int rows, int H, float eps,
+                               cudaStream_t st);
+cudaError_t launch_embed(const int* ids, int n, const uint16_t* table, float* hidden, int H, cudaStream_t st);
+cudaError_t launch_argmax(const float* v, int n, unsigned long long* best, cudaStream_t st);
+cudaError_t launch_weight_to_f16(const void* src, int dtype, uint16_t* dst, size_t n, cudaStream_t st);
+
+// Sets a device for the scope of a call and restores the caller's.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int dev) {
+        if (dev < 0) return;  // host-only object: no device calls
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
 // Sets the calling thread's kv_last_error() message; returns `status`.
 int set_error(int status, const char* msg);
 

@@ -1,0 +1,391 @@
+// model_kernels.cu -- the non-attention kernels of the Qwen2 forward
+// (qwen2_model.cpp:131-274) on sm_100a: embedding lookup, RMSNorm, the
+// projections as HBM-streaming GEMVs with fused epilogues, greedy argmax, and
+// the load-time weight conversion.
+//
+// Projection contract (the reference's ILinearOp, op_linear.h, as the device
+// model computes it): input rows are fp16 values (the truncating f32_to_f16 of
+// half.h), weights fp16 [N][K] (the file's [out][in] layout), products exact
+// in fp32 (11-bit x 11-bit significands), fp32 accumulation, result truncated
+// to fp16 and widened back, then the fp32 epilogue of the call site.
+//
+// An RMSNorm feeding a projection is fused into it: every CTA first computes
+// 1/rms of its input rows (a few KB read from L2) and applies the norm while
+// loading the input.
+//
+// GEMV layout: `ks` warps share one output row, each summing every ks-th
+// 16-byte chunk (8 weights) of it, 8 chunks per lane in flight; 8 warps per
+// CTA, so 8/ks rows per row group; a grid of (SMs x resident CTAs) walks the
+// row groups.  A CTA processes up to MR input rows at once, reading each
+// weight chunk once for all of them.  Weights stream through with no L1
+// allocation; the input rows are staged once per CTA in shared memory as
+// fp16 codes (the norm and the rounding applied there, not per weight).
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <float.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "device_common.cuh"
+#include "kvattn_internal.h"
+
+namespace kvattn {
+
+namespace {
+
+constexpr int kGemvWarps = 8;
+
+// fp16 -> fp32 exactly as worker/include/core/half.h:34-43 (its exponent-0
+// branch included).
+__device__ __forceinline__ float dec_f16_ref(uint32_t h) {
+    const uint32_t sign = (h & 0x8000u) << 16, e = (h >> 10) & 0x1Fu, mant = h & 0x3FFu;
+    uint32_t x;
+    if (e == 0) x = sign | (mant << 13);
+    else if (e == 31) x = sign | 0x7F800000u | (mant << 13);
+    else x = sign | ((e + 112u) << 23) | (mant << 13);
+    return __uint_as_float(x);
+}
+
+// Round an fp32 value through the reference's fp16 (f16_to_f32(f32_to_f16(x))).
+__device__ __forceinline__ float f16_round(float x) { return dec_f16_ref(enc_f16_trunc(x)); }
+
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+// The fp16 value a projection sees for input element k of row m (IN: 0 fp16
+// bits as given; 1 fp32 rounded through fp16; 2 RMSNorm of an fp32 row,
+// (x * inv) * w (op_rmsnorm.cpp:17-18), rounded through fp16), as the bits
+// of the reference's truncating f32_to_f16.  These codes are never fp16
+// subnormals, so the hardware conversion back to fp32 is the reference's.
+template <int IN>
+__device__ __forceinline__ uint16_t input_code(const GemvArgs& a, int m, int k, float inv) {
+    if (IN == 0) return static_cast<const uint16_t*>(a.x)[(size_t)m * a.K + k];
+    float v = static_cast<const float*>(a.x)[(size_t)m * a.K + k];
+    if (IN == 2) v = __fmul_rn(__fmul_rn(v, inv), a.norm_w[k]);
+    return enc_f16_trunc(v);
+}
+
+// 8 fp16 weights against 8 fp16 inputs (both as 16-byte chunks), fp32 FMAs;
+// every product is exact in fp32.
+__device__ __forceinline__ float dot8h(const uint4& w, const uint4& x, float acc) {
+    const __half2* wh = reinterpret_cast<const __half2*>(&w);
+    const __half2* xh = reinterpret_cast<const __half2*>(&x);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float2 fw = __half22float2(wh[j]), fx = __half22float2(xh[j]);
+        acc = fmaf(fw.x, fx.x, acc);
+        acc = fmaf(fw.y, fx.y, acc);
+    }
+    return acc;
+}
+
+// 1 / rms of an fp32 row of H values (op_rmsnorm.cpp:12-15) by a 256-thread
+// block: thread-strided sums of the rounded squares, warp tree, warps in
+// order.  Every caller (the standalone kernel and the fused projections)
+// runs this same order, so all of them get the same value.
+__device__ __forceinline__ float block_inv_rms(const float* __restrict__ xr, int H, float eps, float* part) {
+    float s = 0.f;
+    for (int i = threadIdx.x; i < H; i += 256) s = __fadd_rn(s, __fmul_rn(xr[i], xr[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+    __syncthreads();
+    float t = 0.f;
+    for (int i = 0; i < 8; ++i) t += part[i];
+    __syncthreads();  // part is reused by the next row
+    const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)H), eps));
+    return __fdiv_rn(1.0f, rms);
+}
+
+}  // namespace
+
+constexpr int kGemvUnroll = 8;  // 16-byte weight chunks in flight per lane
+
+// MODE: 0 QKV (+bias, split into q / k / v), 1 residual add, 2 gate/up +
+// SiLU product (fp16 out), 3 logits.  NW = 2 for gate/up (two weight rows per
+// output), else 1.  Dynamic shared memory: the MR input rows as fp16 codes
+// [MR][K].  The CTA walks row groups blockIdx.x, +gridDim.x, ...; its first
+// weight loads are issued before the input rows are staged.
+template <int MODE, int IN, int MR>
+__global__ void __launch_bounds__(kGemvWarps * 32)
+    gemv_kernel(GemvArgs a) {
+    constexpr int NW = MODE == 2 ? 2 : 1;
+    extern __shared__ uint4 gemv_smem[];
+    uint16_t* xs = reinterpret_cast<uint16_t*>(gemv_smem);
+    __shared__ float red[kGemvWarps][NW * MR];
+    __shared__ float s_part[8];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ks = a.ks, rows_per_cta = kGemvWarps / ks, sub = warp / ks, part = warp % ks;
+    const int m0 = blockIdx.y * MR;
+    const int K = a.K, nch = K >> 3, step = 32 * ks;
+    const int ngroups = (a.N + rows_per_cta - 1) / rows_per_cta;
+    const uint16_t* w2 = NW == 2 ? a.w2 : a.w;
+
+    uint4 wv[NW][kGemvUnroll];
+    auto load_batch = [&](int n, int base) {
+#pragma unroll
+        for (int u = 0; u < kGemvUnroll; ++u) {
+            const int c = base + u * step;
+            if (n < a.N && c < nch) {
+                wv[0][u] = ld_stream16(reinterpret_cast<const uint4*>(a.w + (size_t)n * K) + c);
+                if (NW == 2) wv[NW - 1][u] = ld_stream16(reinterpret_cast<const uint4*>(w2 + (size_t)n * K) + c);
+            }
+        }
+    };
+    int rg = blockIdx.x;
+    bool loaded = false;
+    if (rg < ngroups) {
+        load_batch(rg * rows_per_cta + sub, part * 32 + lane);
+        loaded = true;
+    }
+    // stage the input rows (RMSNorm and fp16 rounding applied once per CTA)
+#pragma unroll 1
+    for (int m = 0; m < MR; ++m) {
+        const int row = m0 + m;
+        if (row >= a.M) break;  // uniform across the CTA
+        const float inv = IN == 2 ? block_inv_rms(static_cast<const float*>(a.x) + (size_t)row * K, K, a.eps, s_part)
+                                  : 1.f;
+        for (int k = threadIdx.x; k < K; k += kGemvWarps * 32) xs[m * K + k] = input_code<IN>(a, row, k, inv);
+    }
+    __syncthreads();
+
+#pragma unroll 1
+    for (; rg < ngroups; rg += gridDim.x) {
+        const int n = rg * rows_per_cta + sub;
+        float acc[NW][MR];
+#pragma unroll
+        for (int t = 0; t < NW; ++t)
+#pragma unroll
+            for (int m = 0; m < MR; ++m) acc[t][m] = 0.f;
+#pragma unroll 1
+        for (int base = part * 32 + lane; base < nch; base += kGemvUnroll * step) {
+            if (!loaded) load_batch(n, base);
+            loaded = false;
+#pragma unroll
+            for (int u = 0; u < kGemvUnroll; ++u) {
+                const int c = base + u * step;
+                if (n < a.N && c < nch) {
+#pragma unroll
+                    for (int m = 0; m < MR; ++m) {
+                        if (m0 + m < a.M) {
+                            const uint4 x8 = *reinterpret_cast<const uint4*>(xs + m * K + c * 8);
+#pragma unroll
+                            for (int t = 0; t < NW; ++t) acc[t][m] = dot8h(wv[t][u], x8, acc[t][m]);
+                        }
+                    }
+                }
+            }
+        }
+        loaded = false;
+#pragma unroll
+        for (int t = 0; t < NW; ++t)
+#pragma unroll
+            for (int m = 0; m < MR; ++m) {
+                float v = acc[t][m];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                acc[t][m] = v;
+            }
+        if (ks > 1) {
+            if (lane == 0) {
+#pragma unroll
+                for (int t = 0; t < NW; ++t)
+#pragma unroll
+                    for (int m = 0; m < MR; ++m) red[warp][t * MR + m] = acc[t][m];
+            }
+            __syncthreads();
+            if (part == 0) {
+#pragma unroll
+                for (int t = 0; t < NW; ++t)
+#pragma unroll
+                    for (int m = 0; m < MR; ++m) {
+                        float v = red[warp][t * MR + m];
+                        for (int p = 1; p < ks; ++p) v += red[warp + p][t * MR + m];
+                        acc[t][m] = v;
+                    }
+            }
+        }
+        if (part == 0 && n < a.N) {
+            // lane m finishes input row m0 + m
+#pragma unroll
+            for (int m = 0; m < MR; ++m) {
+                const int row = m0 + m;
+                if (lane != m || row >= a.M) continue;
+                const float r = f16_round(acc[0][m]);
+                if (MODE == 0) {
+                    const float v = __fadd_rn(r, a.bias[n]);  // op_vec_add_bias (op_elementwise.cpp:8-11)
+                    if (n < a.n0) a.out0[(size_t)row * a.n0 + n] = v;
+                    else if (n < a.n0 + a.n1) a.out1[(size_t)row * a.n1 + (n - a.n0)] = v;
+                    else a.out2[(size_t)row * (a.N - a.n0 - a.n1) + (n - a.n0 - a.n1)] = v;
+                } else if (MODE == 1) {
+                    float* h = a.resid + (size_t)row * a.N + n;  // op_vec_add (op_elementwise.cpp:3-5)
+                    *h = __fadd_rn(*h, r);
+                } else if (MODE == 2) {
+                    // op_silu (op_silu.cpp:4-7), then gate *= up, then f32_to_f16
+                    const float g = r, u = f16_round(acc[NW - 1][m]);
+                    const float sg = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+                    a.out16[(size_t)row * a.N + n] = enc_f16_trunc(__fmul_rn(sg, u));
+                } else {
+                    a.logits[(size_t)row * a.N + n] = r;
+                }
+            }
+        }
+        if (ks > 1) __syncthreads();  // red is reused by the next row group
+    }
+}
+
+// RMSNorm (op_rmsnorm.cpp:4-20) of row blockIdx.x, output rounded to fp16 (the
+// f32_to_f16 before every projection).  Per-term products rounded like the
+// reference's loop; the sum is a tree.
+__global__ void __launch_bounds__(256)
+    rmsnorm_f16_kernel(const float* __restrict__ x, const float* __restrict__ w, uint16_t* __restrict__ y, int H,
+                       float eps) {
+    __shared__ float part[8];
+    const float* xr = x + (size_t)blockIdx.x * H;
+    uint16_t* yr = y + (size_t)blockIdx.x * H;
+    const float inv = block_inv_rms(xr, H, eps, part);
+    for (int i = threadIdx.x; i < H; i += blockDim.x) yr[i] = enc_f16_trunc(__fmul_rn(__fmul_rn(xr[i], inv), w[i]));
+}
+
+// op_embedding_lookup (op_embedding.cpp:4-12): row ids[blockIdx.x] of the table.
+__global__ void __launch_bounds__(256)
+    embed_kernel(const int* __restrict__ ids, const uint16_t* __restrict__ table, float* __restrict__ hidden,
+                 int H) {
+    const size_t id = (size_t)ids[blockIdx.x];
+    for (int d = threadIdx.x; d < H; d += blockDim.x)
+        hidden[(size_t)blockIdx.x * H + d] = dec_f16_ref(table[id * H + d]);
+}
+
+// op_greedy_sample (op_sampling.cpp:4-11): the first index of the largest
+// value above -FLT_MAX (index 0 if none).  Packed key: order-preserving bits
+// of the value, then the complement of the index, so the maximum key is the
+// largest value at its lowest index; NaN never counts.
+__global__ void __launch_bounds__(256)
+    argmax_kernel(const float* __restrict__ v, int n, unsigned long long* __restrict__ best) {
+    unsigned long long k = 0;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const float f = v[i];
+        if (f > -FLT_MAX) {
+            const uint32_t u = __float_as_uint(f);
+            const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+            const unsigned long long key = ((unsigned long long)ord << 32) | (0xFFFFFFFFu - (uint32_t)i);
+            k = key > k ? key : k;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long t = __shfl_xor_sync(0xffffffffu, k, o);
+        k = t > k ? t : k;
+    }
+    if ((threadIdx.x & 31) == 0 && k) atomicMax(best, k);
+}
+
+// Load-time conversion of a matrix to the stored fp16 (weight_loader.cpp:184-194):
+// F16 as is (subnormals to signed zero), BF16 via f32 to fp16 (bf16_to_f16),
+// F32 by the truncating f32_to_f16.
+__global__ void __launch_bounds__(256)
+    weight_to_f16_kernel(const void* __restrict__ src, int dtype, uint16_t* __restrict__ dst, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        uint16_t h;
+        if (dtype == 0) {
+            h = static_cast<const uint16_t*>(src)[i];
+            if ((h & 0x7C00u) == 0) h &= 0x8000u;
+        } else if (dtype == 1) {
+            h = enc_f16_trunc(__uint_as_float((uint32_t)static_cast<const uint16_t*>(src)[i] << 16));
+        } else {
+            h = enc_f16_trunc(static_cast<const float*>(src)[i]);
+        }
+        dst[i] = h;
+    }
+}
+
+int gemv_split(int K) {
+    int ks = 1;
+    while (ks < kGemvWarps && K / (ks * 2) >= 1536) ks *= 2;
+    return ks;
+}
+
+template <int MODE, int IN, int MR>
+static cudaError_t launch_gemv_mr(const GemvArgs& a, cudaStream_t st) {
+    static int max_smem_set = 0;     // dynamic shared memory attribute granted so far
+    static int ctas_per_sm[64] = {};  // occupancy by (smem / 4 KiB) bucket
+    static int sms = 0;
+    const int smem = MR * a.K * 2;
+    cudaError_t e;
+    if (smem > max_smem_set && smem > 48 * 1024) {
+        e = cudaFuncSetAttribute(gemv_kernel<MODE, IN, MR>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        max_smem_set = smem;
+    }
+    if (!sms) {
+        int dev = 0;
+        if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+        if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    }
+    const int bucket = smem >> 12 < 64 ? smem >> 12 : 63;
+    if (!ctas_per_sm[bucket]) {
+        int n = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_kernel<MODE, IN, MR>, kGemvWarps * 32,
+                                                          (size_t)smem);
+        if (e != cudaSuccess) return e;
+        ctas_per_sm[bucket] = n > 0 ? n : 1;
+    }
+    const int rows_per_cta = kGemvWarps / a.ks;
+    const int groups = (a.N + rows_per_cta - 1) / rows_per_cta;
+    const int ylen = (a.M + MR - 1) / MR;
+    int gx = sms * ctas_per_sm[bucket] / ylen;
+    gx = gx < 1 ? 1 : gx > groups ? groups : gx;
+    gemv_kernel<MODE, IN, MR><<<dim3((unsigned)gx, (unsigned)ylen), kGemvWarps * 32, smem, st>>>(a);
+    return counted(cudaGetLastError());
+}
+
+template <int MODE, int IN>
+static cudaError_t launch_gemv_t(const GemvArgs& a, cudaStream_t st) {
+    return a.M == 1 ? launch_gemv_mr<MODE, IN, 1>(a, st) : launch_gemv_mr<MODE, IN, 8>(a, st);
+}
+
+cudaError_t launch_gemv(int mode, int in, GemvArgs a, cudaStream_t st) {
+    if (a.K % 8 != 0 || a.N <= 0 || a.M <= 0) return cudaErrorInvalidValue;
+    a.ks = gemv_split(a.K);
+    switch (mode * 4 + in) {
+        case 0 * 4 + 2: return launch_gemv_t<0, 2>(a, st);  // RMSNorm -> QKV
+        case 1 * 4 + 0: return launch_gemv_t<1, 0>(a, st);  // down + residual
+        case 1 * 4 + 1: return launch_gemv_t<1, 1>(a, st);  // O (fp32 attention) + residual
+        case 2 * 4 + 2: return launch_gemv_t<2, 2>(a, st);  // RMSNorm -> gate/up
+        case 3 * 4 + 2: return launch_gemv_t<3, 2>(a, st);  // final RMSNorm -> lm_head
+        case 0 * 4 + 0: return launch_gemv_t<0, 0>(a, st);
+        case 2 * 4 + 0: return launch_gemv_t<2, 0>(a, st);
+        case 3 * 4 + 0: return launch_gemv_t<3, 0>(a, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_rmsnorm_f16(const float* x, const float* w, uint16_t* y, int rows, int H, float eps,
+                               cudaStream_t st) {
+    rmsnorm_f16_kernel<<<rows, 256, 0, st>>>(x, w, y, H, eps);
+    return counted(cudaGetLastError());
+}
+
+cudaError_t launch_embed(const int* ids, int n, const uint16_t* table, float* hidden, int H, cudaStream_t st) {
+    embed_kernel<<<n, 256, 0, st>>>(ids, table, hidden, H);
+    return counted(cudaGetLastError());
+}
+
+cudaError_t launch_argmax(const float* v, int n, unsigned long long* best, cudaStream_t st) {
+    cudaError_t e = cudaMemsetAsync(best, 0, sizeof(unsigned long long), st);
+    if (e != cudaSuccess) return e;
+    argmax_kernel<<<296, 256, 0, st>>>(v, n, best);
+    return counted(cudaGetLastError());
+}
+
+cudaError_t launch_weight_to_f16(const void* src, int dtype, uint16_t* dst, size_t n, cudaStream_t st) {
+    weight_to_f16_kernel<<<592, 256, 0, st>>>(src, dtype, dst, n);
+    return counted(cudaGetLastError());
+}
+
+}  // namespace kvattn
