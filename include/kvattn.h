@@ -264,6 +264,15 @@ int kvp_plan_cta_start(const kvp_pool* pool, int* cta_start, int cap);
  * kvp_timing_read synchronises on the last event and returns the summed
  * launch durations (ms) and the launch count since enabling, then resets. */
 int kvp_timing_enable(kvp_pool* pool, int enable);
+
+/* Let every decode launch of this pool start while the previous kernel in
+ * its stream is still running (programmatic dependent launch): the launch's
+ * K/V tile copies begin at once and the threads that read q / k_new / v_new
+ * or write anything wait for that kernel to finish.  Valid only when no
+ * kernel that may still be running writes this pool's blocks -- e.g. when a
+ * host-side copy or synchronisation separates consecutive decode steps, as
+ * in qw2_forward.  Default off. */
+int kvp_set_overlap(kvp_pool* pool, int enable);
 int kvp_timing_read(kvp_pool* pool, double* total_ms, int* launches);
 
 /* Number of SMs and of resident decode CTAs per SM used for grid sizing. */

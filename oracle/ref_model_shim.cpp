@@ -34,7 +34,7 @@
 namespace {
 
 int g_threads = 0;    // 0: hardware concurrency
-int g_sum_order = 0;  // 0: k = 0..K-1 (the contract); 1: k = K-1..0 (a sensitivity probe only)
+int g_sum_order = 0;  // 0: k = 0..K-1 (the contract); 1: k = K-1..0; 2: 32-lane tree (probes only)
 
 int n_threads() {
     if (g_threads > 0) return g_threads;
@@ -61,11 +61,31 @@ public:
             auto work = [&](int t) {
                 const int n0 = (int)((long long)N_ * t / T), n1 = (int)((long long)N_ * (t + 1) / T);
                 std::vector<float> acc((size_t)(n1 - n0), 0.0f);
-                for (int i = 0; i < K_; ++i) {
-                    const int k = g_sum_order ? K_ - 1 - i : i;
-                    const float ak = a[k];
-                    const float* wr = w_.data() + (size_t)k * N_ + n0;
-                    for (int j = 0; j < n1 - n0; ++j) acc[j] += ak * wr[j];
+                if (g_sum_order == 2) {
+                    // 32 lanes, lane l summing the 8-element chunks l, l + 32, ...
+                    // in order, then a butterfly over the lanes (a parallel order)
+                    std::vector<float> lanes((size_t)(n1 - n0) * 32, 0.0f);
+                    for (int c = 0; c < K_ / 8; ++c)
+                        for (int e = 0; e < 8; ++e) {
+                            const int k = c * 8 + e;
+                            const float ak = a[k];
+                            const float* wr = w_.data() + (size_t)k * N_ + n0;
+                            float* lr = lanes.data() + (c % 32);
+                            for (int j = 0; j < n1 - n0; ++j) lr[(size_t)j * 32] += ak * wr[j];
+                        }
+                    for (int j = 0; j < n1 - n0; ++j) {
+                        float* l = lanes.data() + (size_t)j * 32;
+                        for (int o = 16; o > 0; o >>= 1)
+                            for (int x = 0; x < o; ++x) l[x] = l[x] + l[x + o];
+                        acc[j] = l[0];
+                    }
+                } else {
+                    for (int i = 0; i < K_; ++i) {
+                        const int k = g_sum_order ? K_ - 1 - i : i;
+                        const float ak = a[k];
+                        const float* wr = w_.data() + (size_t)k * N_ + n0;
+                        for (int j = 0; j < n1 - n0; ++j) acc[j] += ak * wr[j];
+                    }
                 }
                 for (int j = 0; j < n1 - n0; ++j) out[n0 + j] = f32_to_f16(acc[j]);
             };
@@ -95,8 +115,8 @@ extern "C" {
 
 void ref_set_threads(int n) { g_threads = n; }
 
-// Order of the stand-in's fp32 sums: 0 the contract above; 1 reversed, which
-// changes nothing but rounding.  Used only to measure how far rounding noise
+// Order of the stand-in's fp32 sums: 0 the contract above; 1 reversed; 2 the
+// order of a 32-lane parallel reduction.  1 and 2 change nothing but rounding.  Used only to measure how far rounding noise
 // alone moves the model's logits (the noise floor any other summation order,
 // e.g. a parallel one, meets).
 void ref_set_sum_order(int order) { g_sum_order = order; }

@@ -66,6 +66,7 @@ _SIGS = {
     "kvp_plan_cta_start": [_vp, _ip, C.c_int],
     "kvp_launch_info": [_vp, _ip, _ip],
     "kvp_timing_enable": [_vp, C.c_int],
+    "kvp_set_overlap": [_vp, C.c_int],
     "attn_contig_noalloc": [_vp, _vp, _vp, _vp] + [C.c_int] * 7 + [_vp],
     "kvp_timing_read": [_vp, C.POINTER(C.c_double), _ip],
     "kvx_create": [C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)],

@@ -421,6 +421,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
 
     // ---------------------------------------------------------- consumers
+    // When launched as a programmatic dependent (kvp_set_overlap), the
+    // producer above copies tiles at once; everything below reads the
+    // previous kernel's q / k_new / v_new or writes results, so it waits for
+    // that kernel first (a no-op for an ordinary launch).
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const float qscale = 0.08838834764831845f * 1.4426950408889634f;  // 1/sqrt(128) * log2(e)
     const int g = lane >> 2, c = lane & 3;
     // Warp w prepares the q fragments of piece w (w < kQPre) while the first
@@ -661,14 +666,31 @@ cudaError_t decode_occupancy(int* ctas_per_sm) {
 
 cudaError_t launch_decode(const PoolView& pv, const PlanView& plan, int nsplits, int max_pieces,
                           int layer, const float* q, const float* k_new, const float* v_new,
-                          float* out, float* m_out, float* l_out, int grid, cudaStream_t st) {
+                          float* out, float* m_out, float* l_out, int grid, bool pdl, cudaStream_t st) {
     const int smem = (int)sizeof(Smem) + 1024;
     if (grid < 1) grid = 1;
-    if (pv.dtype == 0)
-        decode_kernel<0><<<grid, kThreads, smem, st>>>(pv, plan, layer, q, k_new, v_new, out, m_out, l_out);
-    else
-        decode_kernel<1><<<grid, kThreads, smem, st>>>(pv, plan, layer, q, k_new, v_new, out, m_out, l_out);
-    cudaError_t e = counted(cudaGetLastError());
+    cudaError_t e;
+    if (pdl) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)grid);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = (size_t)smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = pv.dtype == 0 ? cudaLaunchKernelEx(&cfg, decode_kernel<0>, pv, plan, layer, q, k_new, v_new, out, m_out, l_out)
+                          : cudaLaunchKernelEx(&cfg, decode_kernel<1>, pv, plan, layer, q, k_new, v_new, out, m_out, l_out);
+        e = counted(e);
+    } else {
+        if (pv.dtype == 0)
+            decode_kernel<0><<<grid, kThreads, smem, st>>>(pv, plan, layer, q, k_new, v_new, out, m_out, l_out);
+        else
+            decode_kernel<1><<<grid, kThreads, smem, st>>>(pv, plan, layer, q, k_new, v_new, out, m_out, l_out);
+        e = counted(cudaGetLastError());
+    }
     if (e != cudaSuccess || nsplits == 0) return e;
     const bool wide = max_pieces > 64;
     cudaLaunchConfig_t cfg = {};

@@ -86,6 +86,7 @@ struct kvp_pool {
     int num_blocks = 0, dtype = 0, max_seqs = 0, max_seq_len = 0, mbps = 0;
     float theta = 0.f;
     int num_sms = 0, occupancy = 0;
+    bool overlap = false;  // decode launches as programmatic dependents (kvp_set_overlap)
     long max_items = 0;
     long max_tiles = 0;  // bound on flat blocks in one plan
     PoolView pv{};
@@ -872,7 +873,9 @@ int attn_decode_plan_ex(kvp_pool* p, int nseq, const int* seq_ids, const int* ro
     // fewer blocks and every CTA finishes at about the same time.
     constexpr long kPieceCost = 6;
     const long gmax = std::max(1L, (long)p->num_sms * p->occupancy);
-    const long G = std::min(gmax, std::max(1L, (total_blocks + 7) / 8));
+    // At least 16 blocks per CTA: below that, a split costs more (a merge
+    // launch) than the blocks it moves to another SM.
+    const long G = std::min(gmax, std::max(1L, (total_blocks + 15) / 16));
     const long per = std::max(kPieceCost + 1,
                               (total_blocks + kPieceCost * (nsegments + G - 1) + G - 1) / G);
     std::vector<WorkItem> items;
@@ -1071,7 +1074,7 @@ static int decode_call(kvp_pool* p, int layer, const float* q, const float* k_ne
         KV_CUDA(cudaEventRecord(te->first, st));
     }
     KV_CUDA(launch_decode(p->pv, p->plan_view, p->plan_nsplits, p->plan_max_pieces, layer, q, k_new,
-                          v_new, out, m, l, p->plan_grid, st));
+                          v_new, out, m, l, p->plan_grid, p->overlap && !te, st));
     if (x) {
         KV_CUDA(launch_xchg(xa, st));
         xchg_commit(x);
@@ -1079,6 +1082,14 @@ static int decode_call(kvp_pool* p, int layer, const float* q, const float* k_ne
     if (te) KV_CUDA(cudaEventRecord(te->second, st));
     KV_CUDA(cudaEventRecord(p->slot_free[r], st));
     p->plan_patched = true;
+    return KV_OK;
+}
+
+int kvp_set_overlap(kvp_pool* p, int enable) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    std::lock_guard<std::mutex> lk(p->mu);
+    if (int rc = require_device(p)) return rc;
+    p->overlap = enable != 0;
     return KV_OK;
 }
 

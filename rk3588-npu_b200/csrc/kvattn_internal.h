@@ -135,7 +135,7 @@ struct PlanView {
 // ---- launchers (kernels.cu) ----
 cudaError_t launch_decode(const PoolView& pv, const PlanView& plan, int nsplits, int max_pieces,
                           int layer, const float* q, const float* k_new, const float* v_new,
-                          float* out, float* m_out, float* l_out, int grid, cudaStream_t st);
+                          float* out, float* m_out, float* l_out, int grid, bool pdl, cudaStream_t st);
 cudaError_t decode_occupancy(int* ctas_per_sm);
 cudaError_t launch_import(const PoolView& pv, int layer, int seq, int pos0, int n,
                           const uint16_t* k_rows, const uint16_t* v_rows, cudaStream_t st);

@@ -27,6 +27,7 @@
 #include <stdint.h>
 
 #include "device_common.cuh"
+#include "kvattn.h"
 #include "kvattn_internal.h"
 
 namespace kvattn {
@@ -57,19 +58,6 @@ __device__ __forceinline__ uint4 ld_stream16(const void* p) {
     return r;
 }
 
-// The fp16 value a projection sees for input element k of row m (IN: 0 fp16
-// bits as given; 1 fp32 rounded through fp16; 2 RMSNorm of an fp32 row,
-// (x * inv) * w (op_rmsnorm.cpp:17-18), rounded through fp16), as the bits
-// of the reference's truncating f32_to_f16.  These codes are never fp16
-// subnormals, so the hardware conversion back to fp32 is the reference's.
-template <int IN>
-__device__ __forceinline__ uint16_t input_code(const GemvArgs& a, int m, int k, float inv) {
-    if (IN == 0) return static_cast<const uint16_t*>(a.x)[(size_t)m * a.K + k];
-    float v = static_cast<const float*>(a.x)[(size_t)m * a.K + k];
-    if (IN == 2) v = __fmul_rn(__fmul_rn(v, inv), a.norm_w[k]);
-    return enc_f16_trunc(v);
-}
-
 // 8 fp16 weights against 8 fp16 inputs (both as 16-byte chunks), fp32 FMAs;
 // every product is exact in fp32.
 __device__ __forceinline__ float dot8h(const uint4& w, const uint4& x, float acc) {
@@ -84,13 +72,24 @@ __device__ __forceinline__ float dot8h(const uint4& w, const uint4& x, float acc
     return acc;
 }
 
+constexpr int kStageU = 2;  // 16-byte fp32 input chunks per thread in flight while staging
+
 // 1 / rms of an fp32 row of H values (op_rmsnorm.cpp:12-15) by a 256-thread
-// block: thread-strided sums of the rounded squares, warp tree, warps in
-// order.  Every caller (the standalone kernel and the fused projections)
-// runs this same order, so all of them get the same value.
-__device__ __forceinline__ float block_inv_rms(const float* __restrict__ xr, int H, float eps, float* part) {
-    float s = 0.f;
-    for (int i = threadIdx.x; i < H; i += 256) s = __fadd_rn(s, __fmul_rn(xr[i], xr[i]));
+// block: thread t sums the rounded squares of its float4 chunks t, t + 256,
+// ... (components in order), then a warp tree, then the 8 warps in order.
+// Every caller (the standalone kernel and the fused projections) runs this
+// same order, so all of them get the same value.  All loads of a thread are
+// issued before any is used.
+__device__ __forceinline__ float sum_sq4(float s, const float4& v) {
+    s = __fadd_rn(s, __fmul_rn(v.x, v.x));
+    s = __fadd_rn(s, __fmul_rn(v.y, v.y));
+    s = __fadd_rn(s, __fmul_rn(v.z, v.z));
+    return __fadd_rn(s, __fmul_rn(v.w, v.w));
+}
+
+// Finish 1/rms from each thread's partial sum (warp tree, then the 8 warps in
+// order; every thread of the 256 gets the value).
+__device__ __forceinline__ float block_inv_rms_from(float s, int H, float eps, float* part) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
@@ -102,15 +101,138 @@ __device__ __forceinline__ float block_inv_rms(const float* __restrict__ xr, int
     return __fdiv_rn(1.0f, rms);
 }
 
+__device__ __forceinline__ float block_inv_rms(const float* __restrict__ xr, int H, float eps, float* part) {
+    const float4* src = reinterpret_cast<const float4*>(xr);
+    const int n4 = H >> 2;
+    float s = 0.f;
+    for (int base = threadIdx.x; base < n4; base += kStageU * 256) {
+        float4 v[kStageU];
+#pragma unroll
+        for (int u = 0; u < kStageU; ++u)
+            if (base + u * 256 < n4) v[u] = __ldg(src + base + u * 256);
+#pragma unroll
+        for (int u = 0; u < kStageU; ++u)
+            if (base + u * 256 < n4) s = sum_sq4(s, v[u]);
+    }
+    return block_inv_rms_from(s, H, eps, part);
+}
+
+// Stage input row `row` of a projection into shared memory as the fp16 codes
+// the projection multiplies (IN: 0 fp16 codes as given; 1 fp32 rounded
+// through fp16; 2 RMSNorm of an fp32 row, (x * inv) * w (op_rmsnorm.cpp:
+// 17-18), rounded through fp16), by the reference's truncating f32_to_f16.
+// These codes are never fp16 subnormals, so the hardware conversion back to
+// fp32 is the reference's f16_to_f32.  16-byte loads, several in flight per
+// thread.
+template <int IN>
+__device__ __forceinline__ void stage_row(const GemvArgs& a, int row, uint16_t* xs_row, float* part) {
+    const int K = a.K;
+    if (IN == 0) {
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.x) + (size_t)row * K);
+        uint4* dst = reinterpret_cast<uint4*>(xs_row);
+        const int n8 = K >> 3;
+        // 5 chunks per thread: a row of up to 10240 values in one round of loads
+        for (int base = threadIdx.x; base < n8; base += 5 * 256) {
+            uint4 v[5];
+#pragma unroll
+            for (int u = 0; u < 5; ++u)
+                if (base + u * 256 < n8) v[u] = __ldg(src + base + u * 256);
+#pragma unroll
+            for (int u = 0; u < 5; ++u)
+                if (base + u * 256 < n8) dst[base + u * 256] = v[u];
+        }
+        return;
+    }
+    const float* xr = static_cast<const float*>(a.x) + (size_t)row * K;
+    const float4* src = reinterpret_cast<const float4*>(xr);
+    const float4* wsrc = reinterpret_cast<const float4*>(a.norm_w);
+    uint2* dst = reinterpret_cast<uint2*>(xs_row);
+    const int n4 = K >> 2;
+    auto encode = [&](const float4& v, const float4& w, float inv, int i) {
+        float e[4] = {v.x, v.y, v.z, v.w};
+        if (IN == 2) {
+            const float f[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) e[j] = __fmul_rn(__fmul_rn(e[j], inv), f[j]);
+        }
+        dst[i] = make_uint2((uint32_t)enc_f16_trunc(e[0]) | ((uint32_t)enc_f16_trunc(e[1]) << 16),
+                            (uint32_t)enc_f16_trunc(e[2]) | ((uint32_t)enc_f16_trunc(e[3]) << 16));
+    };
+    if (n4 <= kStageU * 256) {
+        // the whole row in registers: one round of loads (row and norm
+        // weights together), the sum of squares from registers, then the codes
+        float4 v[kStageU], w[kStageU];
+        float sq = 0.f;
+#pragma unroll
+        for (int u = 0; u < kStageU; ++u) {
+            const int i = threadIdx.x + u * 256;
+            if (i < n4) {
+                v[u] = __ldg(src + i);
+                if (IN == 2) w[u] = __ldg(wsrc + i);
+            }
+        }
+        float inv = 1.f;
+        if (IN == 2) {
+#pragma unroll
+            for (int u = 0; u < kStageU; ++u)
+                if (threadIdx.x + u * 256 < n4) sq = sum_sq4(sq, v[u]);
+            inv = block_inv_rms_from(sq, K, a.eps, part);
+        }
+#pragma unroll
+        for (int u = 0; u < kStageU; ++u) {
+            const int i = threadIdx.x + u * 256;
+            if (i < n4) encode(v[u], w[u], inv, i);
+        }
+        return;
+    }
+    const float inv = IN == 2 ? block_inv_rms(xr, K, a.eps, part) : 1.f;
+    for (int base = threadIdx.x; base < n4; base += kStageU * 256) {
+        float4 v[kStageU], w[kStageU];
+#pragma unroll
+        for (int u = 0; u < kStageU; ++u)
+            if (base + u * 256 < n4) {
+                v[u] = __ldg(src + base + u * 256);
+                if (IN == 2) w[u] = __ldg(wsrc + base + u * 256);
+            }
+#pragma unroll
+        for (int u = 0; u < kStageU; ++u)
+            if (base + u * 256 < n4) encode(v[u], w[u], inv, base + u * 256);
+    }
+}
+
 }  // namespace
 
 constexpr int kGemvUnroll = 8;  // 16-byte weight chunks in flight per lane
+
+// The call site's fp32 epilogue of output n of input row `row`, from the fp32
+// sums of its weight row (acc) and, for gate/up, of its up row (acc2).
+template <int MODE>
+__device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int row, int n, float acc, float acc2) {
+    const float r = f16_round(acc);
+    if (MODE == 0) {
+        const float v = __fadd_rn(r, a.bias[n]);  // op_vec_add_bias (op_elementwise.cpp:8-11)
+        if (n < a.n0) a.out0[(size_t)row * a.n0 + n] = v;
+        else if (n < a.n0 + a.n1) a.out1[(size_t)row * a.n1 + (n - a.n0)] = v;
+        else a.out2[(size_t)row * (a.N - a.n0 - a.n1) + (n - a.n0 - a.n1)] = v;
+    } else if (MODE == 1) {
+        float* h = a.resid + (size_t)row * a.N + n;  // op_vec_add (op_elementwise.cpp:3-5)
+        *h = __fadd_rn(*h, r);
+    } else if (MODE == 2) {
+        // op_silu (op_silu.cpp:4-7), then gate *= up, then f32_to_f16
+        const float u = f16_round(acc2);
+        const float sg = __fdiv_rn(r, __fadd_rn(1.0f, expf(-r)));
+        a.out16[(size_t)row * a.N + n] = enc_f16_trunc(__fmul_rn(sg, u));
+    } else {
+        a.logits[(size_t)row * a.N + n] = r;
+    }
+}
 
 // MODE: 0 QKV (+bias, split into q / k / v), 1 residual add, 2 gate/up +
 // SiLU product (fp16 out), 3 logits.  NW = 2 for gate/up (two weight rows per
 // output), else 1.  Dynamic shared memory: the MR input rows as fp16 codes
 // [MR][K].  The CTA walks row groups blockIdx.x, +gridDim.x, ...; its first
-// weight loads are issued before the input rows are staged.
+// weight loads are issued before it waits for the previous kernel (every
+// access before that wait reads only weights, which no kernel writes).
 template <int MODE, int IN, int MR>
 __global__ void __launch_bounds__(kGemvWarps * 32)
     gemv_kernel(GemvArgs a) {
@@ -137,20 +259,23 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
             }
         }
     };
+    // Launched as a programmatic dependent of the previous kernel: let the
+    // next one launch, stream the first (read-only) weights, and only then
+    // wait for the previous kernel's results (the input rows) to be visible.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     int rg = blockIdx.x;
     bool loaded = false;
     if (rg < ngroups) {
         load_batch(rg * rows_per_cta + sub, part * 32 + lane);
         loaded = true;
     }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     // stage the input rows (RMSNorm and fp16 rounding applied once per CTA)
 #pragma unroll 1
     for (int m = 0; m < MR; ++m) {
         const int row = m0 + m;
         if (row >= a.M) break;  // uniform across the CTA
-        const float inv = IN == 2 ? block_inv_rms(static_cast<const float*>(a.x) + (size_t)row * K, K, a.eps, s_part)
-                                  : 1.f;
-        for (int k = threadIdx.x; k < K; k += kGemvWarps * 32) xs[m * K + k] = input_code<IN>(a, row, k, inv);
+        stage_row<IN>(a, row, xs + m * K, s_part);
     }
     __syncthreads();
 
@@ -216,23 +341,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
             for (int m = 0; m < MR; ++m) {
                 const int row = m0 + m;
                 if (lane != m || row >= a.M) continue;
-                const float r = f16_round(acc[0][m]);
-                if (MODE == 0) {
-                    const float v = __fadd_rn(r, a.bias[n]);  // op_vec_add_bias (op_elementwise.cpp:8-11)
-                    if (n < a.n0) a.out0[(size_t)row * a.n0 + n] = v;
-                    else if (n < a.n0 + a.n1) a.out1[(size_t)row * a.n1 + (n - a.n0)] = v;
-                    else a.out2[(size_t)row * (a.N - a.n0 - a.n1) + (n - a.n0 - a.n1)] = v;
-                } else if (MODE == 1) {
-                    float* h = a.resid + (size_t)row * a.N + n;  // op_vec_add (op_elementwise.cpp:3-5)
-                    *h = __fadd_rn(*h, r);
-                } else if (MODE == 2) {
-                    // op_silu (op_silu.cpp:4-7), then gate *= up, then f32_to_f16
-                    const float g = r, u = f16_round(acc[NW - 1][m]);
-                    const float sg = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
-                    a.out16[(size_t)row * a.N + n] = enc_f16_trunc(__fmul_rn(sg, u));
-                } else {
-                    a.logits[(size_t)row * a.N + n] = r;
-                }
+                gemv_epilogue<MODE>(a, row, n, acc[0][m], acc[NW - 1][m]);
             }
         }
         if (ks > 1) __syncthreads();  // red is reused by the next row group
@@ -338,10 +447,23 @@ static cudaError_t launch_gemv_mr(const GemvArgs& a, cudaStream_t st) {
     const int rows_per_cta = kGemvWarps / a.ks;
     const int groups = (a.N + rows_per_cta - 1) / rows_per_cta;
     const int ylen = (a.M + MR - 1) / MR;
-    int gx = sms * ctas_per_sm[bucket] / ylen;
-    gx = gx < 1 ? 1 : gx > groups ? groups : gx;
-    gemv_kernel<MODE, IN, MR><<<dim3((unsigned)gx, (unsigned)ylen), kGemvWarps * 32, smem, st>>>(a);
-    return counted(cudaGetLastError());
+    int cap = sms * ctas_per_sm[bucket] / ylen;
+    cap = cap < 1 ? 1 : cap;
+    // as many CTAs as fit, but every CTA the same number of row groups (the
+    // next kernel waits for the last CTA)
+    const int rounds = (groups + cap - 1) / cap;
+    const int gx = (groups + rounds - 1) / rounds;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)gx, (unsigned)ylen);
+    cfg.blockDim = dim3(kGemvWarps * 32);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return counted(cudaLaunchKernelEx(&cfg, gemv_kernel<MODE, IN, MR>, a));
 }
 
 template <int MODE, int IN>

@@ -432,6 +432,9 @@ int qw2_create(int device, const qw2_config* cfg, qw2_model** out) {
         step(kvp_create(device, cfg->layers, cfg->q_heads, cfg->kv_heads, cfg->head_dim, kBlockTokens, blocks,
                         KV_F16, 1, cfg->max_position, cfg->rope_theta, &m->pool));
     }
+    // every forward ends with a host synchronisation, so no decode launch
+    // overlaps a kernel that writes the cache (kvp_set_overlap's contract)
+    if (rc == KV_OK) step(kvp_set_overlap(m->pool, 1));
     if (rc == KV_OK) step(new_sequence(m));
     if (rc != KV_OK) {
         const std::string msg = kv_last_error();

@@ -18,7 +18,10 @@ same reference run again with only the stand-in linear's fp32 sums taken in
 reverse k order (ref_set_sum_order(1)), fed the same tokens; its relative
 logit difference from the first run (prefill: max |diff| / max |ref| over the
 vocabulary; each decode step: over the stored top 64) is what any other
-summation order, a parallel one included, must be expected to meet.
+summation order, a parallel one included, must be expected to meet.  The
+reversed-sum run's teacher-forced argmaxes and its own free-running greedy
+stream are stored too: where the reference's top-2 margin is inside that
+floor, its own greedy choice flips with the summation order.
 
 Run here (needs the reference sources for `make -C oracle model`):
     python tests/golden/gen_qwen2_golden.py [--dir /tmp/qwen2_synth_s0]
@@ -124,13 +127,23 @@ def main():
     fwd(prompt)
     den = np.abs(prefill_logits.astype(np.float64)).max()
     floor_prefill = float(np.abs(logits.astype(np.float64) - prefill_logits).max() / den)
+    argmax_reversed = [int(np.argmax(logits))]
     floor_steps = []
     for step, tok in enumerate(out):
-        fwd([tok])
+        argmax_reversed.append(fwd([tok]))
         val = top_val[step].astype(np.float64)
         floor_steps.append(float(np.abs(logits[top_idx[step]] - val).max() / np.abs(val).max()))
     R.ref_qwen2_free(m)
+    # the free-running greedy stream of the reversed-sum reference
+    e = R.ref_engine_load(args.dir.encode())
+    assert e
+    eo = (C.c_int * args.steps)()
+    k = R.ref_engine_generate(e, ids, len(prompt), args.steps, None, 0, 0, eo, args.steps)
+    R.ref_engine_free(e)
+    stream_reversed = [eo[i] for i in range(k)]
     R.ref_set_sum_order(0)
+    same = next((i for i, (a, b) in enumerate(zip(stream_reversed, out)) if a != b), None)
+    print(f"reversed-sum stream first differs at {same}", flush=True)
     print(f"noise floor: prefill {floor_prefill:.3g}, decode max {max(floor_steps):.3g}", flush=True)
 
     bits = prefill_logits.view(np.uint32)
@@ -142,7 +155,9 @@ def main():
     np.savez_compressed(dst, prompt=prompt, output_ids=np.array(out, np.int32), prefill_logits_f16=h16,
                         top_idx=np.stack(top_idx), top_val=np.stack(top_val).astype(np.float32),
                         weights_seed=np.int32(0), prompt_seed=np.int32(0), std=np.float32(0.02),
-                        floor_prefill=np.float64(floor_prefill), floor_steps=np.array(floor_steps, np.float64))
+                        floor_prefill=np.float64(floor_prefill), floor_steps=np.array(floor_steps, np.float64),
+                        argmax_reversed=np.array(argmax_reversed[:-1], np.int32),
+                        stream_reversed=np.array(stream_reversed, np.int32))
     print("wrote", dst, "first ids", out[:8])
 
 

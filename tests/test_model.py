@@ -4,12 +4,18 @@ Oracle: tests/golden/qwen2_greedy.npz, made by tests/golden/gen_qwen2_golden.py
 from the reference's Qwen2Model + LLMEngine (worker/src/model/qwen2_model.cpp,
 worker/src/api/llm_engine.cpp) compiled unmodified with a CPU stand-in for the
 NPU linear (oracle/ref_model_shim.cpp), on the seeded N(0, 0.02) weights and
-128-id prompt of the Qwen2-1.5B config.  The bar: the greedy token stream
-identical; logits within 1e-3 relative (max |diff| / max |ref|) or, where it
-is larger, twice the model's own rounding-noise floor stored in the fixture:
+128-id prompt of the Qwen2-1.5B config.
+
+The bar is the reference's own rounding-noise floor, stored in the fixture:
 the reference run against itself with only its fp32 sums reordered differs
-by 2.7e-3 on the prompt's logits (up to 2.4e-3 on decode steps), so 1e-3 is
-out of reach of any other summation order for this random-weight model.
+by 2.7e-3 on the prompt's logits (up to 2.5e-3 on decode steps).  So:
+  * logits within 1e-3 relative (max |diff| / max |ref|) or, where larger,
+    twice that floor;
+  * every greedy choice equal to the reference's, except at a step whose
+    top-2 margin is itself inside twice the floor (there the reference's own
+    choice flips with the summation order: a 1-ulp fp16 tie at step 28 of
+    this stream); at such a step the choice must be one of the reference's
+    near-top tokens, and a free-running stream may first differ only there.
 
 Reduced configs check the loader (safetensors parsing and the F32 / BF16 /
 F16 conversions of weight_loader.cpp:164-235) and the error behaviour.
@@ -49,6 +55,30 @@ def f16_bits_to_f32(h: np.ndarray) -> np.ndarray:
 def logit_tol(floor: float) -> float:
     """1e-3, or twice the reference's own rounding-noise floor where that is larger."""
     return max(TOL, 2.0 * float(floor))
+
+
+def margins(g):
+    """Relative top-2 margin of the reference's logits before each emitted id
+    (index 0: the prompt's logits; i >= 1: decode step i - 1) and the noise
+    floor at the same point."""
+    pre = np.sort(f16_bits_to_f32(g["prefill_logits_f16"]).astype(np.float64))[::-1]
+    tv = g["top_val"].astype(np.float64)
+    m = np.concatenate([[(pre[0] - pre[1]) / np.abs(pre).max()], (tv[:, 0] - tv[:, 1]) / np.abs(tv).max(axis=1)])
+    floor = np.concatenate([[g["floor_prefill"]], g["floor_steps"]])
+    return m, floor
+
+
+def near_top(g, i):
+    """Ids the reference ranks within twice the noise floor of its top choice
+    before emitted id i."""
+    m, floor = margins(g)
+    if i == 0:
+        v = f16_bits_to_f32(g["prefill_logits_f16"]).astype(np.float64)
+        band = 2 * floor[0] * np.abs(v).max()
+        return set(np.nonzero(v >= v.max() - band)[0].tolist())
+    v, idx = g["top_val"][i - 1].astype(np.float64), g["top_idx"][i - 1]
+    band = 2 * floor[i] * np.abs(v).max()
+    return set(idx[v >= v[0] - band].tolist())
 
 
 def rel(a, ref):
@@ -120,8 +150,16 @@ def test_greedy_stream_matches_reference_engine(full_model):
     g = dict(np.load(GOLD))
     full_model.reset()
     ids = full_model.generate(g["prompt"].tolist(), 128, stop_tokens=(), repetition_window=0)
-    assert ids == g["output_ids"].tolist()
-    assert full_model.cur_pos() == 128 + 128  # the prompt, then one forward per emitted id
+    ref = g["output_ids"].tolist()
+    assert len(ids) == 128 and full_model.cur_pos() == 128 + 128  # the prompt, then one forward per id
+    first = next((i for i, (a, b) in enumerate(zip(ids, ref)) if a != b), None)
+    if first is not None:
+        m, floor = margins(g)
+        # only where the reference's own choice is inside its rounding noise
+        assert m[first] <= 2 * floor[first], (first, m[first], floor[first])
+        assert ids[first] in near_top(g, first)
+        print(f"stream identical for {first} ids; id {first} is a near-tie "
+              f"(reference margin {m[first]:.2e} vs noise floor {floor[first]:.2e})")
 
 
 @pytest.mark.gpu
@@ -131,14 +169,21 @@ def test_prefill_and_decode_logits_match_reference(full_model):
     logits, am = full_model.forward(g["prompt"].tolist())
     ref = f16_bits_to_f32(g["prefill_logits_f16"]).astype(np.float64)
     assert rel(logits, ref) <= logit_tol(g["floor_prefill"])
-    assert am == int(g["output_ids"][0]) == int(np.argmax(logits))
+    m, floor = margins(g)
+    out = g["output_ids"].tolist()
+    choices = [am]
     worst = 0.0
-    for s, tok in enumerate(g["output_ids"].tolist()):
+    for s, tok in enumerate(out):
         logits, am = full_model.forward([tok])
         idx, val = g["top_idx"][s], g["top_val"][s].astype(np.float64)
         worst = max(worst, float(np.abs(logits[idx] - val).max() / np.abs(val).max()))
-        assert am == int(idx[0])
+        choices.append(am)
     assert worst <= logit_tol(np.max(g["floor_steps"]))
+    # teacher-forced greedy choices: equal to the reference's except at near-ties
+    for i, c in enumerate(choices[:128]):
+        if c != out[i]:
+            assert m[i] <= 2 * floor[i] and c in near_top(g, i), (i, c, out[i], m[i], floor[i])
+    assert sum(c != o for c, o in zip(choices, out)) <= int((m <= 2 * floor).sum())
     assert full_model.cur_pos() == 256
 
 
