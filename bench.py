@@ -140,13 +140,16 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload",
-                    choices=["batch32", "paged28", "paged1", "long1", "long4", "serve", "prefill", "model1"],
+                    choices=["batch32", "paged28", "paged1", "long1", "long4", "serve", "prefill", "model1",
+                             "model_batch"],
                     default="batch32")
     ap.add_argument("--transport", choices=["nccl", "p2p"], default="nccl",
                     help="long workloads: merge of the per-GPU states by NCCL all-gather + combine "
                          "launch, or by the fused peer-memory exchange kernel")
     ap.add_argument("--prefill-kernel", choices=["tc", "mma"], default="tc",
                     help="prefill workload: the tcgen05 kernel (attn_prefill) or the mma.sync baseline")
+    ap.add_argument("--sessions", type=int, default=8,
+                    help="model_batch workload: concurrent sessions decoding together")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--settle", type=float, default=1.0,
@@ -1049,6 +1052,101 @@ def run_model(args, rank, world, local):
         dist.destroy_process_group()
 
 
+def run_model_batch(args, rank, world, local):
+    """Qwen2-1.5B greedy decode of `--sessions` concurrent sessions through
+    the batching engine (qw2_generate_batch): every engine step is one
+    forward over all sessions (one weight pass of the projections for up to
+    8 rows, one planned decode-attention launch).  Each session first
+    prefills its own 128-id prompt; the timed call then generates K ids per
+    session (K + 1 forwards).  value: device events around that call; e2e:
+    the host clock around it (host ids in and out)."""
+    import torch
+    kv = load_pkg()
+    kv.load()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    q2 = _qwen2()
+    B, K, W = args.sessions, args.steps, args.warmup
+    M = q2.Model(local, max_sessions=B)
+    M.load_synthetic(seed=0)
+    stream = torch.cuda.current_stream()
+    kv.call("qw2_set_stream", M.h, stream.cuda_stream)
+    sessions = [0] + [M.create_session() for _ in range(B - 1)]
+    prompts = [q2.synth_prompt(128, q2.QWEN2_1_5B["vocab"], seed=s).tolist() for s in range(B)]
+    assert 128 + W + K + 2 <= q2.QWEN2_1_5B["max_position"], "steps + warmup must fit 512 positions"
+    M.generate_batch([dict(session=s, input_ids=p, max_new_tokens=0) for s, p in zip(sessions, prompts)])
+    last = [p[-1] for p in prompts]
+    if W:
+        out = M.generate_batch([dict(session=s, input_ids=[t], max_new_tokens=W) for s, t in zip(sessions, last)])
+        last = [ids[-1] for ids, _ in out]
+    sampler = ClockSampler(range(local, local + 1)) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(args.settle)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    kc0 = kv.kernel_count()
+    pos0 = M.session_len(0)
+    t0 = time.perf_counter()
+    e0.record(stream)
+    out = M.generate_batch([dict(session=s, input_ids=[t], max_new_tokens=K) for s, t in zip(sessions, last)])
+    e1.record(stream)
+    torch.cuda.synchronize()
+    host_s = time.perf_counter() - t0
+    kernels = kv.kernel_count() - kc0
+    dev_ms = e0.elapsed_time(e1)
+    clocks = sampler.stop() if sampler else None
+    tokens = sum(len(ids) for ids, _ in out)
+    assert tokens == B * K and all(r["status"] == 0 for _, r in out)
+    times = torch.tensor([dev_ms, host_s], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    dev_ms, host_s = times[0].item(), times[1].item()
+    if rank == 0:
+        wbytes = M.weight_bytes()
+        steps = K + 1
+        passes = -(-B // 8)  # the projections read their weights once per 8 rows
+        kv_bytes = B * 28 * 2 * 2 * 128 * 2 * (pos0 + K / 2 + 1)
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+            os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+        peak = float(peaks.get("hbm_gbs", 6650.0))
+        achieved = (passes * wbytes + kv_bytes) / (dev_ms / steps * 1e-3) / 1e9
+        line = {
+            "metric": "Qwen2-1.5B greedy decode tokens/s, concurrent sessions through the batching engine",
+            "value": round(world * tokens / (dev_ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": round(dev_ms / steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (random-init N(0,0.02) weights from seed 0, RMSNorm weights 1; prompts seeds 0..B-1)",
+            "config": {"workload": f"Qwen2-1.5B greedy decode of {B} sessions at once on one GPU (each after its "
+                                   "own 128-id prompt), one engine step = one forward over all sessions",
+                       "name": "model_batch", "sessions": B, "positions_timed": [pos0, pos0 + K + 1],
+                       "parallelism": "replicas only (one model per GPU)",
+                       "l2": "inputs larger than L2 (3.09 GB of weights per pass, no flush)"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
+                         "note": f"whole engine step; algorithmic bytes = {passes} pass(es) over the fp16 "
+                                 f"weights ({wbytes} B each) + the KV rows of {B} sessions"},
+            "e2e": {"value": round(world * tokens / host_s, 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 8 * B + 4 * 32,
+                    "note": "qw2_generate_batch from host ids to host ids, host clock"},
+            "gpu_launches": int(kernels),
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    M.close()
+    if dist:
+        dist.destroy_process_group()
+
+
 def _ref_model(q2, tmpdir):
     """The reference's Qwen2Model compiled from its sources (oracle/_ref),
     loaded from an F16 safetensors file of the same seeded weights."""
@@ -1067,7 +1165,16 @@ def _ref_model(q2, tmpdir):
     cfg = q2.QWEN2_1_5B
     q2.write_safetensors(path, q2.tensor_specs(cfg), q2.synth_weights(cfg, seed=0), dtype="F16")
     R.ref_set_threads(os.cpu_count() or 1)
-    m = R.ref_qwen2_load(tmpdir.encode())
+    # the reference's loader reports progress on stdout (qwen2_model.cpp:53-117):
+    # send it to stderr so this process's stdout stays one JSON line
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        m = R.ref_qwen2_load(tmpdir.encode())
+    finally:
+        os.dup2(saved, 1)
+        os.close(saved)
     return R, m
 
 
@@ -1272,7 +1379,7 @@ def run_reference(args, rank, world):
     if args.workload == "prefill":
         run_reference_prefill(args, world)
         return
-    if args.workload == "model1":
+    if args.workload in ("model1", "model_batch"):
         run_reference_model(args, world)
         return
     wl = make_workload(args.workload)
@@ -1327,6 +1434,8 @@ def main():
         run_prefill(args, rank, world, local)
     elif args.workload == "model1":
         run_model(args, rank, world, local)
+    elif args.workload == "model_batch":
+        run_model_batch(args, rank, world, local)
     else:
         run_ours(args, rank, world, local)
 

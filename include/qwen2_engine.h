@@ -33,7 +33,7 @@ extern "C" {
 typedef struct qw2_model qw2_model;
 
 /* Qwen2Config (model_config.h:8-23).  Constraints here: head_dim 128,
- * hidden == q_heads * head_dim, hidden and intermediate multiples of 8,
+ * hidden == q_heads * head_dim, hidden and intermediate multiples of 32,
  * q_heads / kv_heads <= 8. */
 typedef struct qw2_config {
     int hidden;        /* 1536 */
@@ -105,8 +105,81 @@ int qw2_forward(qw2_model* m, const int* tokens, int n, float* logits_host, int*
 int qw2_generate(qw2_model* m, const int* prompt, int n_prompt, int max_new, const int* stop_tokens,
                  int n_stop, int repetition_window, int* out_ids, int cap, int* n_out);
 
-/* The model's KV pool (sequence 0), for inspection with kvp_gather etc. */
+/* The model's KV pool, for inspection with kvp_gather etc.; qw2_session_seq
+ * gives a session's sequence id in it. */
 int qw2_kv_pool(qw2_model* m, kvp_pool** pool);
+
+/* ------------------------------------------------------------ sessions
+ * The reference plans multi-session, batch and async interfaces on top of
+ * LLMEngine (docs/api_requirements.md:90-151: create_session /
+ * destroy_session / session_exists, generate_session, generate_batch,
+ * generate_async + cancel_generation).  Here a session is one sequence of
+ * the model's paged KV pool; qw2_create's model has one session (id 0, the
+ * one qw2_forward / qw2_generate / qw2_reset use), qw2_create_sessions's has
+ * up to max_sessions, all sharing the weights. */
+int qw2_create_sessions(int device, const qw2_config* cfg, int max_sessions, qw2_model** out);
+int qw2_session_create(qw2_model* m, int* session);
+int qw2_session_destroy(qw2_model* m, int session);
+int qw2_session_exists(const qw2_model* m, int session, int* exists);
+int qw2_session_len(const qw2_model* m, int session, int* len);
+int qw2_session_seq(const qw2_model* m, int session, int* seq_id);
+/* Qwen2Model::forward on one session (its cache continues). */
+int qw2_forward_session(qw2_model* m, int session, const int* tokens, int n, float* logits_host, int* argmax);
+
+/* GenerationConfig (worker/include/api/generation_config.h:9-25) and
+ * GenerationResult (generation_config.h:28-36). */
+typedef struct qw2_gen_config {
+    int max_new_tokens;
+    int repetition_window;  /* 0 disables */
+    const int* stop_tokens;
+    int n_stop;
+} qw2_gen_config;
+
+typedef struct qw2_result {
+    int n_out;           /* generated ids (the first out_cap are stored) */
+    int prefill_tokens;
+    int decode_tokens;
+    float prefill_ms;    /* host clock; in a batch the forwards are shared */
+    float decode_ms;
+    int hit_stop;
+    int hit_repetition;
+    int cancelled;
+    int status;          /* KV_OK, or the status that ended the request */
+} qw2_result;
+
+/* TokenCallback (llm_engine.h): called after the forward of each generated
+ * id, with its decode step and the step's host time. */
+typedef void (*qw2_token_cb)(void* user, int session, int step, int id, float elapsed_ms);
+
+typedef struct qw2_request {
+    int session;
+    const int* input_ids;
+    int n_input;
+    qw2_gen_config cfg;
+    int* out_ids;        /* generate_batch: where the generated ids go */
+    int out_cap;
+    qw2_token_cb on_token;
+    void* user;
+} qw2_request;
+
+/* generate_session: LLMEngine::generate's loop on a session whose cache holds
+ * the earlier turns (the input is appended at the session's position). */
+int qw2_generate_session(qw2_model* m, int session, const int* input_ids, int n_input, const qw2_gen_config* cfg,
+                         int* out_ids, int out_cap, qw2_result* result);
+/* generate_batch: every request at once (distinct sessions).  Each engine
+ * step runs one forward over all of them: one-token rows of the decoding
+ * requests share every projection and one planned decode-attention launch;
+ * prompts are appended in chunks of up to 256 tokens beside them. */
+int qw2_generate_batch(qw2_model* m, int n_requests, const qw2_request* requests, qw2_result* results);
+/* generate_async: queue a request (input and stop ids are copied) and return
+ * at once; a worker thread runs every queued request, batched as above.
+ * qw2_wait blocks up to timeout_ms (< 0: no limit) for job `job`: KV_OK with
+ * its ids and result when it finished (the job is then retired),
+ * KV_ERR_TIMEOUT if still running.  qw2_cancel ends the session's queued or
+ * running request at the next step (result.cancelled = 1). */
+int qw2_submit(qw2_model* m, const qw2_request* request, int* job);
+int qw2_wait(qw2_model* m, int job, int timeout_ms, int* out_ids, int out_cap, qw2_result* result);
+int qw2_cancel(qw2_model* m, int session);
 
 /* Bytes of weights one decode step reads (all projections + lm_head). */
 int qw2_weight_bytes(const qw2_model* m, long long* bytes);

@@ -4,7 +4,8 @@ Usage: python rk3588-npu_b200/build.py [--force]
 
 Sources: csrc/*.cu (kernels + host runtime + C ABI) and csrc/*.cpp (host-only
 C ABI parts, compiled through nvcc's host compiler).  Output:
-lib/libkvattn.so next to this file.  cudart is linked statically, so the
+lib/libkvattn.so next to this file, and bin/qwen2_chat (frontend/qwen2_chat.cpp,
+the line-protocol front end of the device model, linked against it).  cudart is linked statically, so the
 library needs only the CUDA driver at run time; streams and device pointers
 from any other runtime in the process (e.g. torch's) are interchangeable
 with it because they are driver objects.
@@ -20,6 +21,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIBDIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIBDIR, "libkvattn.so")
+CHAT_SRC = os.path.join(HERE, "frontend", "qwen2_chat.cpp")
+CHAT = os.path.join(HERE, "bin", "qwen2_chat")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
 NVCC = os.environ.get("NVCC", "nvcc")
@@ -38,10 +41,10 @@ def _deps() -> list[str]:
 
 
 def up_to_date() -> bool:
-    if not os.path.exists(LIB):
+    if not os.path.exists(LIB) or not os.path.exists(CHAT):
         return False
-    t = os.path.getmtime(LIB)
-    return all(os.path.getmtime(d) <= t for d in _deps())
+    t = min(os.path.getmtime(LIB), os.path.getmtime(CHAT))
+    return all(os.path.getmtime(d) <= t for d in _deps() + [CHAT_SRC])
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
@@ -64,6 +67,13 @@ def build(force: bool = False, verbose: bool = False) -> str:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)
     os.replace(tmp, LIB)
+    os.makedirs(os.path.dirname(CHAT), exist_ok=True)
+    cmd = [os.environ.get("CXX", "g++"), "-O2", "-std=c++17", f"-I{INCLUDE}", CHAT_SRC, "-o", CHAT + ".tmp",
+           f"-L{LIBDIR}", "-lkvattn", "-Wl,-rpath,$ORIGIN/../lib"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    os.replace(CHAT + ".tmp", CHAT)
     return LIB
 
 

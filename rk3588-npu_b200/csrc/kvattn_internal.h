@@ -219,7 +219,8 @@ int gemv_split(int K);
 cudaError_t launch_rmsnorm_f16(const float* x, const float* w, uint16_t* y, int rows, int H, float eps,
                                cudaStream_t st);
 cudaError_t launch_embed(const int* ids, int n, const uint16_t* table, float* hidden, int H, cudaStream_t st);
-cudaError_t launch_argmax(const float* v, int n, unsigned long long* best, cudaStream_t st);
+cudaError_t launch_argmax(const float* v, int n, int rows, unsigned long long* best, cudaStream_t st);
+cudaError_t launch_gather_rows(const float* src, const int* idx, int rows, float* dst, int H, cudaStream_t st);
 cudaError_t launch_weight_to_f16(const void* src, int dtype, uint16_t* dst, size_t n, cudaStream_t st);
 
 // Sets a device for the scope of a call and restores the caller's.

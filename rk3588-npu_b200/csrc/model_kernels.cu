@@ -200,6 +200,71 @@ __device__ __forceinline__ void stage_row(const GemvArgs& a, int row, uint16_t* 
     }
 }
 
+// The same codes as stage_row, one row staged by one warp (used when a CTA
+// stages several rows): lane l takes the 16-byte chunks l, l + 32, ...; the
+// RMSNorm sum is lane-sequential then a warp tree, with no CTA barrier.
+template <int IN>
+__device__ __forceinline__ void stage_row_warp(const GemvArgs& a, int row, uint16_t* xs_row) {
+    const int K = a.K, lane = threadIdx.x & 31;
+    if (IN == 0) {
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.x) + (size_t)row * K);
+        uint4* dst = reinterpret_cast<uint4*>(xs_row);
+        const int n8 = K >> 3;
+        for (int base = lane; base < n8; base += 8 * 32) {
+            uint4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (base + u * 32 < n8) v[u] = __ldg(src + base + u * 32);
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (base + u * 32 < n8) dst[base + u * 32] = v[u];
+        }
+        return;
+    }
+    const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + (size_t)row * K);
+    const float4* wsrc = reinterpret_cast<const float4*>(a.norm_w);
+    uint2* dst = reinterpret_cast<uint2*>(xs_row);
+    const int n4 = K >> 2;
+    float inv = 1.f;
+    if (IN == 2) {
+        float s = 0.f;
+        for (int base = lane; base < n4; base += 8 * 32) {
+            float4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (base + u * 32 < n4) v[u] = __ldg(src + base + u * 32);
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (base + u * 32 < n4) s = sum_sq4(s, v[u]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)K), a.eps));
+        inv = __fdiv_rn(1.0f, rms);
+    }
+    for (int base = lane; base < n4; base += 4 * 32) {
+        float4 v[4], w[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (base + u * 32 < n4) {
+                v[u] = __ldg(src + base + u * 32);
+                if (IN == 2) w[u] = __ldg(wsrc + base + u * 32);
+            }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (base + u * 32 < n4) {
+                float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+                if (IN == 2) {
+                    const float f[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) e[j] = __fmul_rn(__fmul_rn(e[j], inv), f[j]);
+                }
+                dst[base + u * 32] = make_uint2((uint32_t)enc_f16_trunc(e[0]) | ((uint32_t)enc_f16_trunc(e[1]) << 16),
+                                                (uint32_t)enc_f16_trunc(e[2]) | ((uint32_t)enc_f16_trunc(e[3]) << 16));
+            }
+    }
+}
+
 }  // namespace
 
 constexpr int kGemvUnroll = 8;  // 16-byte weight chunks in flight per lane
@@ -270,12 +335,13 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
         loaded = true;
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    // stage the input rows (RMSNorm and fp16 rounding applied once per CTA)
-#pragma unroll 1
-    for (int m = 0; m < MR; ++m) {
-        const int row = m0 + m;
-        if (row >= a.M) break;  // uniform across the CTA
-        stage_row<IN>(a, row, xs + m * K, s_part);
+    // stage the input rows (RMSNorm and fp16 rounding applied once per CTA):
+    // one row with the whole CTA, several rows one per warp, all at once
+    if (MR == 1) {
+        if (m0 < a.M) stage_row<IN>(a, m0, xs, s_part);
+    } else {
+        for (int m = warp; m < MR; m += kGemvWarps)
+            if (m0 + m < a.M) stage_row_warp<IN>(a, m0 + m, xs + m * K);
     }
     __syncthreads();
 
@@ -348,6 +414,142 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Several input rows (2..32: a decode step of several sessions) on the tensor
+// cores: y^T = W x^T as mma.sync m16n8k16 tiles, W the A operand (16 weight
+// rows x 16 k), the staged input rows the B operand (16 k x 8 rows), fp32
+// accumulators.  Products of fp16 values are exact, sums fp32: the contract
+// of the one-row kernel, in another order.
+//
+// The k order inside each 32-wide span is permuted consistently for A and B
+// so that both operands come from plain 16-byte loads: lane (g, c) loads
+// weights [row g][8c, 8c+8) and [row g+8][8c, 8c+8) of the span and input
+// [row g][8c, 8c+8) from shared memory; step 0 of the span multiplies the
+// pairs (8c, 8c+1) and (8c+2, 8c+3) (in the fragment slots of logical k
+// 2c.. and 2c+8..), step 1 the pairs (8c+4, 8c+5) and (8c+6, 8c+7).  Every
+// physical k of the span is used exactly once.
+//
+// Warp w: weight rows tile w / kMmaKs (16 rows), k spans w % kMmaKs, +kMmaKs,
+// ...; 8 warps = 16 * 8 / kMmaKs rows per row group.  Input rows are staged
+// with a padded stride (K + 8 halves) so that the 8 rows of a B load sit in
+// different banks.
+constexpr int kMmaKs = 8;      // warps per 16-row tile (k split)
+constexpr int kMmaPad = 8;     // halves of padding per staged row
+constexpr int kMmaU = 8;       // k spans per warp in flight
+
+template <int MODE, int IN, int NT>
+__global__ void __launch_bounds__(kGemvWarps * 32)
+    gemv_mma_kernel(GemvArgs a) {
+    constexpr int NW = MODE == 2 ? 2 : 1;
+    constexpr int MR = NT * 8;
+    extern __shared__ uint4 gemv_smem[];
+    uint16_t* xs = reinterpret_cast<uint16_t*>(gemv_smem);  // [MR][K + kMmaPad]
+    __shared__ float red[kGemvWarps][NW * NT * 4][32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+    const int tiles_per_cta = kGemvWarps / kMmaKs, sub = warp / kMmaKs, part = warp % kMmaKs;
+    const int m0 = blockIdx.y * MR;
+    const int K = a.K, spans = K >> 5, ldx = K + kMmaPad;
+    const int ngroups = (a.N + 16 * tiles_per_cta - 1) / (16 * tiles_per_cta);
+    const uint16_t* wmat[2] = {a.w, NW == 2 ? a.w2 : a.w};
+
+    uint4 wa[NW][kMmaU], wb[NW][kMmaU];
+    auto load_batch = [&](int n0, int base) {
+#pragma unroll
+        for (int u = 0; u < kMmaU; ++u) {
+            const int sp = base + u * kMmaKs;
+#pragma unroll
+            for (int q = 0; q < NW; ++q) {
+                wa[q][u] = make_uint4(0u, 0u, 0u, 0u);
+                wb[q][u] = make_uint4(0u, 0u, 0u, 0u);
+                if (sp < spans) {
+                    const uint16_t* base_q = wmat[q] + (size_t)sp * 32 + 8 * c;
+                    if (n0 + g < a.N) wa[q][u] = ld_stream16(base_q + (size_t)(n0 + g) * K);
+                    if (n0 + g + 8 < a.N) wb[q][u] = ld_stream16(base_q + (size_t)(n0 + g + 8) * K);
+                }
+            }
+        }
+    };
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    int rg = blockIdx.x;
+    bool loaded = false;
+    if (rg < ngroups) {
+        load_batch((rg * tiles_per_cta + sub) * 16, part);
+        loaded = true;
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // stage the input rows, one per warp (rows past M as zeros)
+    for (int m = warp; m < MR; m += kGemvWarps) {
+        if (m0 + m < a.M) {
+            stage_row_warp<IN>(a, m0 + m, xs + (size_t)m * ldx);
+        } else {
+            uint4* z = reinterpret_cast<uint4*>(xs + (size_t)m * ldx);
+            for (int i = lane; i < (K >> 3); i += 32) z[i] = make_uint4(0u, 0u, 0u, 0u);
+        }
+    }
+    __syncthreads();
+
+#pragma unroll 1
+    for (; rg < ngroups; rg += gridDim.x) {
+        const int n0 = (rg * tiles_per_cta + sub) * 16;
+        float d[NW][NT][4];
+#pragma unroll
+        for (int q = 0; q < NW; ++q)
+#pragma unroll
+            for (int t = 0; t < NT; ++t) d[q][t][0] = d[q][t][1] = d[q][t][2] = d[q][t][3] = 0.f;
+#pragma unroll 1
+        for (int base = part; base < spans; base += kMmaU * kMmaKs) {
+            if (!loaded) load_batch(n0, base);
+            loaded = false;
+#pragma unroll
+            for (int u = 0; u < kMmaU; ++u) {
+                const int sp = base + u * kMmaKs;
+                if (sp < spans) {
+#pragma unroll
+                    for (int t = 0; t < NT; ++t) {
+                        const uint4 xb = *reinterpret_cast<const uint4*>(xs + (size_t)(t * 8 + g) * ldx + sp * 32 + 8 * c);
+#pragma unroll
+                        for (int q = 0; q < NW; ++q) {
+                            mma16816<0>(d[q][t], wa[q][u].x, wb[q][u].x, wa[q][u].y, wb[q][u].y, xb.x, xb.y);
+                            mma16816<0>(d[q][t], wa[q][u].z, wb[q][u].z, wa[q][u].w, wb[q][u].w, xb.z, xb.w);
+                        }
+                    }
+                }
+            }
+        }
+        loaded = false;
+        // the kMmaKs partial tiles of the same 16 rows, summed in order
+        if (part != 0) {
+#pragma unroll
+            for (int q = 0; q < NW; ++q)
+#pragma unroll
+                for (int t = 0; t < NT; ++t)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) red[warp][(q * NT + t) * 4 + i][lane] = d[q][t][i];
+        }
+        __syncthreads();
+        if (part == 0) {
+#pragma unroll
+            for (int q = 0; q < NW; ++q)
+#pragma unroll
+                for (int t = 0; t < NT; ++t)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        float v = d[q][t][i];
+                        for (int p2 = 1; p2 < kMmaKs; ++p2) v += red[warp + p2][(q * NT + t) * 4 + i][lane];
+                        d[q][t][i] = v;
+                    }
+#pragma unroll
+            for (int t = 0; t < NT; ++t)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int n = n0 + g + (i >= 2 ? 8 : 0), row = m0 + t * 8 + 2 * c + (i & 1);
+                    if (n < a.N && row < a.M) gemv_epilogue<MODE>(a, row, n, d[0][t][i], d[NW - 1][t][i]);
+                }
+        }
+        __syncthreads();  // red is reused by the next row group
+    }
+}
+
 // RMSNorm (op_rmsnorm.cpp:4-20) of row blockIdx.x, output rounded to fp16 (the
 // f32_to_f16 before every projection).  Per-term products rounded like the
 // reference's loop; the sum is a tree.
@@ -370,12 +572,14 @@ __global__ void __launch_bounds__(256)
         hidden[(size_t)blockIdx.x * H + d] = dec_f16_ref(table[id * H + d]);
 }
 
-// op_greedy_sample (op_sampling.cpp:4-11): the first index of the largest
-// value above -FLT_MAX (index 0 if none).  Packed key: order-preserving bits
+// op_greedy_sample (op_sampling.cpp:4-11) of each row: the first index of
+// the largest value above -FLT_MAX (index 0 if none).  Packed key: order-preserving bits
 // of the value, then the complement of the index, so the maximum key is the
 // largest value at its lowest index; NaN never counts.
 __global__ void __launch_bounds__(256)
     argmax_kernel(const float* __restrict__ v, int n, unsigned long long* __restrict__ best) {
+    v += (size_t)blockIdx.y * n;  // row blockIdx.y
+    best += blockIdx.y;
     unsigned long long k = 0;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const float f = v[i];
@@ -426,7 +630,7 @@ static cudaError_t launch_gemv_mr(const GemvArgs& a, cudaStream_t st) {
     static int sms = 0;
     const int smem = MR * a.K * 2;
     cudaError_t e;
-    if (smem > max_smem_set && smem > 48 * 1024) {
+    if (smem > max_smem_set) {
         e = cudaFuncSetAttribute(gemv_kernel<MODE, IN, MR>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         max_smem_set = smem;
@@ -466,13 +670,76 @@ static cudaError_t launch_gemv_mr(const GemvArgs& a, cudaStream_t st) {
     return counted(cudaLaunchKernelEx(&cfg, gemv_kernel<MODE, IN, MR>, a));
 }
 
+template <int MODE, int IN, int NT>
+static cudaError_t launch_gemv_mma_nt(const GemvArgs& a, cudaStream_t st) {
+    static int max_smem_set = 0;
+    static int ctas_per_sm[64] = {};
+    static int sms = 0;
+    const int smem = NT * 8 * (a.K + kMmaPad) * 2;
+    cudaError_t e;
+    if (smem > max_smem_set) {  // static (the reduction buffer) + dynamic may pass 48 KB at any size
+        e = cudaFuncSetAttribute(gemv_mma_kernel<MODE, IN, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        max_smem_set = smem;
+    }
+    if (!sms) {
+        int dev = 0;
+        if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+        if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    }
+    const int bucket = smem >> 12 < 64 ? smem >> 12 : 63;
+    if (!ctas_per_sm[bucket]) {
+        int n = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_mma_kernel<MODE, IN, NT>, kGemvWarps * 32,
+                                                          (size_t)smem);
+        if (e != cudaSuccess) return e;
+        ctas_per_sm[bucket] = n > 0 ? n : 1;
+    }
+    const int rows_per_group = 16 * (kGemvWarps / kMmaKs);
+    const int groups = (a.N + rows_per_group - 1) / rows_per_group;
+    const int ylen = (a.M + NT * 8 - 1) / (NT * 8);
+    int cap = sms * ctas_per_sm[bucket] / ylen;
+    cap = cap < 1 ? 1 : cap;
+    const int rounds = (groups + cap - 1) / cap;
+    const int gx = (groups + rounds - 1) / rounds;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)gx, (unsigned)ylen);
+    cfg.blockDim = dim3(kGemvWarps * 32);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return counted(cudaLaunchKernelEx(&cfg, gemv_mma_kernel<MODE, IN, NT>, a));
+}
+
+// Rows of one pass: up to 32 while their staged copies fit beside the rest
+// (K = 1536: 32 rows, 98 KB; K = 8960: 8 rows, 143 KB); more rows take more
+// passes over the weights.
+template <int MODE, int IN>
+static cudaError_t launch_gemv_mma(const GemvArgs& a, cudaStream_t st) {
+    const int fit = (200 * 1024) / (8 * (a.K + kMmaPad) * 2);  // n8 tiles whose rows fit
+    const int need = (a.M + 7) / 8;
+    const int nt = need < fit ? need : fit;
+    if (nt >= 4) return launch_gemv_mma_nt<MODE, IN, 4>(a, st);
+    if (nt >= 2) return launch_gemv_mma_nt<MODE, IN, 2>(a, st);
+    return launch_gemv_mma_nt<MODE, IN, 1>(a, st);
+}
+
+// One row: the CUDA-core kernel (HBM-bound at 2 B per weight).  Several rows
+// (sessions decoding together, prompt chunks): the tensor-core kernel, in
+// passes of up to 32 rows.
 template <int MODE, int IN>
 static cudaError_t launch_gemv_t(const GemvArgs& a, cudaStream_t st) {
-    return a.M == 1 ? launch_gemv_mr<MODE, IN, 1>(a, st) : launch_gemv_mr<MODE, IN, 8>(a, st);
+    if (a.M == 1) return launch_gemv_mr<MODE, IN, 1>(a, st);
+    return launch_gemv_mma<MODE, IN>(a, st);
 }
 
 cudaError_t launch_gemv(int mode, int in, GemvArgs a, cudaStream_t st) {
     if (a.K % 8 != 0 || a.N <= 0 || a.M <= 0) return cudaErrorInvalidValue;
+    if (a.M > 1 && a.K % 32 != 0) return cudaErrorInvalidValue;  // the tensor-core path walks 32-wide k spans
     a.ks = gemv_split(a.K);
     switch (mode * 4 + in) {
         case 0 * 4 + 2: return launch_gemv_t<0, 2>(a, st);  // RMSNorm -> QKV
@@ -498,10 +765,24 @@ cudaError_t launch_embed(const int* ids, int n, const uint16_t* table, float* hi
     return counted(cudaGetLastError());
 }
 
-cudaError_t launch_argmax(const float* v, int n, unsigned long long* best, cudaStream_t st) {
-    cudaError_t e = cudaMemsetAsync(best, 0, sizeof(unsigned long long), st);
+cudaError_t launch_argmax(const float* v, int n, int rows, unsigned long long* best, cudaStream_t st) {
+    cudaError_t e = cudaMemsetAsync(best, 0, sizeof(unsigned long long) * rows, st);
     if (e != cudaSuccess) return e;
-    argmax_kernel<<<296, 256, 0, st>>>(v, n, best);
+    const int gx = rows >= 296 ? 1 : 296 / rows;
+    argmax_kernel<<<dim3((unsigned)gx, (unsigned)rows), 256, 0, st>>>(v, n, best);
+    return counted(cudaGetLastError());
+}
+
+// dst[i] = src row idx[i] (H floats), one CTA per row.
+__global__ void __launch_bounds__(256)
+    gather_rows_kernel(const float* __restrict__ src, const int* __restrict__ idx, float* __restrict__ dst, int H) {
+    const float* s = src + (size_t)idx[blockIdx.x] * H;
+    float* d = dst + (size_t)blockIdx.x * H;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) d[i] = s[i];
+}
+
+cudaError_t launch_gather_rows(const float* src, const int* idx, int rows, float* dst, int H, cudaStream_t st) {
+    gather_rows_kernel<<<rows, 256, 0, st>>>(src, idx, dst, H);
     return counted(cudaGetLastError());
 }
 

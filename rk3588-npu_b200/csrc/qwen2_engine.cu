@@ -20,7 +20,15 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <atomic>
+#include <chrono>
+#include <condition_variable>
+#include <deque>
+#include <map>
+#include <memory>
+#include <mutex>
 #include <string>
+#include <thread>
 #include <unordered_map>
 #include <vector>
 
@@ -76,6 +84,33 @@ constexpr size_t kStagingBytes = 64u << 20;
 
 }  // namespace
 
+namespace {
+
+// One generation request moving through LLMEngine::generate's loop
+// (llm_engine.cpp:66-98) one engine step at a time.
+struct Job {
+    int id = 0;
+    int session = 0;
+    std::vector<int> input;       // ids still to append (prefill)
+    int n_input = 0;
+    int max_new = 0;
+    int rep_window = 0;
+    std::vector<int> stops;
+    qw2_token_cb cb = nullptr;
+    void* user = nullptr;
+    std::vector<int> out;
+    int next = 0;                 // greedy choice of the last forward
+    int step = 0;                 // decode step (loop counter of the reference)
+    bool prefilled = false;
+    bool decoding = false;        // `next` is pushed and waits for its forward
+    bool done = false;
+    std::atomic<bool> cancel{false};  // set by qw2_cancel from another thread
+    qw2_result res{};
+    std::chrono::steady_clock::time_point t0, t_prefill, t_step;
+};
+
+}  // namespace
+
 struct qw2_model {
     int device = 0;
     qw2_config c{};
@@ -83,7 +118,21 @@ struct qw2_model {
     cudaStream_t st = nullptr;
     bool own_stream = false;
     kvp_pool* pool = nullptr;
-    int seq = -1;
+    int max_sessions = 1;
+    int rows_cap = 0;              // rows of one forward (activation buffers)
+    std::vector<int> session_seq;  // session -> pool sequence id, -1 = free
+    std::vector<char> session_busy;  // an async request runs on it
+
+    // async engine
+    std::mutex mu;                 // one model operation at a time
+    std::mutex qmu;                // the queue and the finished jobs
+    std::condition_variable qcv;
+    std::deque<std::shared_ptr<Job>> queue;
+    std::map<int, std::shared_ptr<Job>> finished;
+    std::map<int, std::shared_ptr<Job>> running;
+    std::thread worker;
+    bool stop_worker = false;
+    int next_job = 1;
 
     struct Layer {
         float* ln1 = nullptr;
@@ -108,9 +157,10 @@ struct qw2_model {
     float* v = nullptr;       // [R][kvd]
     float* attn = nullptr;    // [R][H]
     uint16_t* h16 = nullptr;  // [R][IS]
-    float* logits = nullptr;  // [V]
-    int* ids = nullptr;       // [R]
-    unsigned long long* best = nullptr;
+    float* logits = nullptr;  // [S][V]: one row per session of a forward
+    float* last = nullptr;    // [S][H]: the last hidden row of each session
+    int* ids = nullptr;       // [R + S]: token ids, then the last-row index of each session
+    unsigned long long* best = nullptr;  // [S]
     void* staging = nullptr;
 
     std::vector<void*> allocs;
@@ -142,7 +192,8 @@ int check_cfg(const qw2_config* c) {
     if (c->hidden != c->q_heads * c->head_dim) return qfail(KV_ERR_INVAL, "hidden != q_heads * head_dim");
     if (c->q_heads % c->kv_heads || c->q_heads / c->kv_heads > kMaxGroup)
         return qfail(KV_ERR_INVAL, "q_heads / kv_heads must be an integer <= %d", kMaxGroup);
-    if (c->hidden % 8 || c->intermediate % 8) return qfail(KV_ERR_INVAL, "hidden and intermediate must be multiples of 8");
+    if (c->hidden % 32 || c->intermediate % 32)
+        return qfail(KV_ERR_INVAL, "hidden and intermediate must be multiples of 32");
     return KV_OK;
 }
 
@@ -202,10 +253,6 @@ int resolve(qw2_model* m, const char* name, Target* t) {
     return qfail(KV_ERR_INVAL, "unknown tensor name '%s'", name);
 }
 
-int new_sequence(qw2_model* m) {
-    QW_OK(kvp_seq_alloc(m->pool, &m->seq));
-    return KV_OK;
-}
 
 // ---- a minimal reader of the safetensors header (a JSON object) ----
 struct JsonTensor {
@@ -351,6 +398,368 @@ bool detect_repetition(const std::vector<int>& ids, int window) {
 
 }  // namespace
 
+namespace {
+
+int session_check(const qw2_model* m, int session) {
+    if (session < 0 || session >= m->max_sessions || m->session_seq[session] < 0)
+        return qfail(KV_ERR_BADSEQ, "no session %d", session);
+    return KV_OK;
+}
+
+// n tokens of one session, at its current position.
+struct Group {
+    int session = 0;
+    const int* tokens = nullptr;
+    int n = 0;
+    float* logits_host = nullptr;  // [vocab] or NULL
+    int argmax = 0;
+};
+
+// Qwen2Model::forward (qwen2_model.cpp:131-274) over several sessions at
+// once.  Rows: the one-token groups first (in the given order: one planned
+// decode-attention launch covers them), then every longer group (appended
+// as a chunk and attended with the prefill kernel).  The projections run
+// once over all rows; lm_head and the argmax over each group's last row.
+int forward_groups(qw2_model* m, std::vector<Group>& gs) {
+    const qw2_config& c = m->c;
+    const int G = (int)gs.size();
+    if (G == 0) return qfail(KV_ERR_INVAL, "forward of no tokens");
+    if (G > m->max_sessions) return qfail(KV_ERR_INVAL, "%d groups > %d sessions", G, m->max_sessions);
+    QW_OK(qw2_ready(m));
+    std::vector<int> order;  // decode groups first
+    for (int pass = 0; pass < 2; ++pass)
+        for (int g = 0; g < G; ++g)
+            if ((gs[g].n == 1) == (pass == 0)) order.push_back(g);
+    std::vector<int> pos(G), seq(G), off(G);
+    std::vector<char> seen(m->max_sessions, 0);
+    int rows = 0, nD = 0;
+    for (int g : order) {
+        Group& gr = gs[g];
+        QW_OK(session_check(m, gr.session));
+        if (seen[gr.session]) return qfail(KV_ERR_INVAL, "session %d twice in one forward", gr.session);
+        seen[gr.session] = 1;
+        if (gr.n <= 0 || !gr.tokens) return qfail(KV_ERR_INVAL, "forward of %d tokens", gr.n);
+        for (int i = 0; i < gr.n; ++i)
+            if (gr.tokens[i] < 0 || gr.tokens[i] >= c.vocab)
+                return qfail(KV_ERR_RANGE, "token id %d outside [0, %d)", gr.tokens[i], c.vocab);
+        seq[g] = m->session_seq[gr.session];
+        QW_OK(kvp_seq_len(m->pool, seq[g], &pos[g]));
+        if (pos[g] + gr.n > c.max_position)
+            return qfail(KV_ERR_RANGE, "positions %d..%d pass max_position %d", pos[g], pos[g] + gr.n - 1,
+                         c.max_position);
+        off[g] = rows;
+        rows += gr.n;
+        nD += gr.n == 1;
+    }
+    if (rows > m->rows_cap) return qfail(KV_ERR_RANGE, "%d rows in one forward > %d", rows, m->rows_cap);
+    DeviceGuard dg(m->device);
+    cudaStream_t st = m->st;
+    const int H = c.hidden, kvd = m->kvd, IS = c.intermediate;
+
+    // token ids, then the index of each group's last row (in `order`)
+    std::vector<int> host(rows + G);
+    for (int g : order) memcpy(host.data() + off[g], gs[g].tokens, sizeof(int) * gs[g].n);
+    for (int i = 0; i < G; ++i) host[rows + i] = off[order[i]] + gs[order[i]].n - 1;
+    QW_CUDA(cudaMemcpyAsync(m->ids, host.data(), sizeof(int) * host.size(), cudaMemcpyHostToDevice, st));
+    QW_CUDA(launch_embed(m->ids, rows, m->embed, m->hidden, H, st));
+    if (nD) {
+        std::vector<int> dseq;
+        for (int i = 0; i < nD; ++i) dseq.push_back(seq[order[i]]);
+        QW_OK(attn_decode_plan(m->pool, nD, dseq.data(), st));
+    }
+    for (int i = nD; i < G; ++i) QW_OK(kvp_seq_reserve(m->pool, seq[order[i]], pos[order[i]] + gs[order[i]].n));
+
+    for (int li = 0; li < c.layers; ++li) {
+        const qw2_model::Layer& Ly = m->L[li];
+        // 1-2: input RMSNorm fused into the Q/K/V projections (+ biases)
+        GemvArgs a;
+        a.w = Ly.wqkv;
+        a.N = H + 2 * kvd;
+        a.K = H;
+        a.M = rows;
+        a.x = m->hidden;
+        a.norm_w = Ly.ln1;
+        a.eps = c.rms_eps;
+        a.bias = Ly.bqkv;
+        a.out0 = m->q;
+        a.out1 = m->k;
+        a.out2 = m->v;
+        a.n0 = H;
+        a.n1 = kvd;
+        QW_CUDA(launch_gemv(0, 2, a, st));
+        // 3-5: RoPE, KV append, attention
+        if (nD) QW_OK(attn_decode_append(m->pool, li, m->q, m->k, m->v, m->attn, st));
+        for (int i = nD; i < G; ++i) {
+            const int g = order[i], o = off[g];
+            QW_OK(kv_append_chunk(m->pool, li, seq[g], pos[g], gs[g].n, m->k + (size_t)o * kvd,
+                                  m->v + (size_t)o * kvd, st));
+            QW_OK(attn_prefill(m->pool, li, seq[g], pos[g], gs[g].n, m->q + (size_t)o * H, m->attn + (size_t)o * H,
+                               st));
+        }
+        // 6-7: O projection + residual
+        GemvArgs o;
+        o.w = Ly.wo;
+        o.N = H;
+        o.K = H;
+        o.M = rows;
+        o.x = m->attn;
+        o.resid = m->hidden;
+        QW_CUDA(launch_gemv(1, 1, o, st));
+        // 8-10: post-attention RMSNorm fused into gate/up (+ SiLU product), down + residual
+        GemvArgs gu;
+        gu.w = Ly.wg;
+        gu.w2 = Ly.wu;
+        gu.N = IS;
+        gu.K = H;
+        gu.M = rows;
+        gu.x = m->hidden;
+        gu.norm_w = Ly.ln2;
+        gu.eps = c.rms_eps;
+        gu.out16 = m->h16;
+        QW_CUDA(launch_gemv(2, 2, gu, st));
+        GemvArgs d;
+        d.w = Ly.wd;
+        d.N = H;
+        d.K = IS;
+        d.M = rows;
+        d.x = m->h16;
+        d.resid = m->hidden;
+        QW_CUDA(launch_gemv(1, 0, d, st));
+    }
+    if (nD) QW_OK(attn_decode_commit(m->pool));
+    for (int i = nD; i < G; ++i) QW_OK(kvp_seq_set_len(m->pool, seq[order[i]], pos[order[i]] + gs[order[i]].n));
+
+    // final RMSNorm of each group's last token fused into lm_head (tied embedding), argmax
+    const float* last = m->hidden;
+    if (!(G == rows)) {  // one-token groups only: the last rows are rows 0..G-1 already
+        QW_CUDA(launch_gather_rows(m->hidden, m->ids + rows, G, m->last, H, st));
+        last = m->last;
+    }
+    GemvArgs lm;
+    lm.w = m->embed;
+    lm.N = c.vocab;
+    lm.K = H;
+    lm.M = G;
+    lm.x = last;
+    lm.norm_w = m->norm;
+    lm.eps = c.rms_eps;
+    lm.logits = m->logits;
+    QW_CUDA(launch_gemv(3, 2, lm, st));
+    QW_CUDA(launch_argmax(m->logits, c.vocab, G, m->best, st));
+    std::vector<unsigned long long> keys(G);
+    QW_CUDA(cudaMemcpyAsync(keys.data(), m->best, sizeof(unsigned long long) * G, cudaMemcpyDeviceToHost, st));
+    for (int i = 0; i < G; ++i)
+        if (gs[order[i]].logits_host)
+            QW_CUDA(cudaMemcpyAsync(gs[order[i]].logits_host, m->logits + (size_t)i * c.vocab,
+                                    sizeof(float) * (size_t)c.vocab, cudaMemcpyDeviceToHost, st));
+    int status = 0;
+    QW_OK(kvp_device_status(m->pool, st, &status));  // synchronises the stream
+    if (status != 0) return status;
+    for (int i = 0; i < G; ++i) {
+        const unsigned long long key = keys[i];
+        gs[order[i]].argmax = key ? (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFu)) : 0;
+    }
+    return KV_OK;
+}
+
+using Clock = std::chrono::steady_clock;
+
+float ms_since(Clock::time_point t) {
+    return std::chrono::duration<float, std::milli>(Clock::now() - t).count();
+}
+
+void job_finish(Job& j, int status) {
+    j.done = true;
+    j.res.status = status;
+    j.res.n_out = (int)j.out.size();
+    j.res.decode_tokens = (int)j.out.size();
+    if (j.prefilled) j.res.decode_ms = ms_since(j.t_prefill);
+}
+
+// The loop head of llm_engine.cpp:76-90 once `next` holds the greedy choice
+// of the job's last forward: stop at max_new or a stop token (not emitted),
+// emit `next`, stop on a repetition (emitted, never forwarded), else its
+// forward is due.
+void job_advance(Job& j) {
+    if (j.step >= j.max_new) {
+        job_finish(j, KV_OK);
+        return;
+    }
+    for (int s : j.stops)
+        if (s == j.next) {
+            j.res.hit_stop = 1;
+            job_finish(j, KV_OK);
+            return;
+        }
+    j.out.push_back(j.next);
+    if (j.rep_window > 0 && detect_repetition(j.out, j.rep_window)) {
+        j.res.hit_repetition = 1;
+        job_finish(j, KV_OK);
+        return;
+    }
+    j.decoding = true;
+    j.t_step = Clock::now();
+}
+
+constexpr int kPrefillChunk = 256;  // prompt tokens of one request appended per engine step
+
+// One engine step over the live jobs: every decoding job forwards its pushed
+// id, every prefilling job appends its next prompt chunk (as rows allow),
+// all in one forward_groups.  Returns the forward's status (a failure ends
+// every job of the step).
+int engine_step(qw2_model* m, std::vector<Job*>& jobs) {
+    std::vector<Group> gs;
+    std::vector<Job*> gj;
+    int rows = 0;
+    for (Job* j : jobs) {
+        if (j->done) continue;
+        if (j->cancel) {  // cancel_generation: ends at this step boundary
+            j->res.cancelled = 1;
+            job_finish(*j, KV_OK);
+            continue;
+        }
+        if (j->prefilled && j->decoding) {
+            Group g;
+            g.session = j->session;
+            g.tokens = &j->out.back();
+            g.n = 1;
+            gs.push_back(g);
+            gj.push_back(j);
+            ++rows;
+        }
+    }
+    for (Job* j : jobs) {
+        if (j->done || j->prefilled) continue;
+        int n = std::min((int)j->input.size(), std::min(kPrefillChunk, m->c.max_position));
+        n = std::min(n, m->rows_cap - rows);
+        if (n <= 0) continue;
+        Group g;
+        g.session = j->session;
+        g.tokens = j->input.data();
+        g.n = n;
+        gs.push_back(g);
+        gj.push_back(j);
+        rows += n;
+    }
+    if (gs.empty()) return KV_OK;
+    const int rc = forward_groups(m, gs);
+    if (rc != KV_OK) {
+        for (Job* j : gj) job_finish(*j, rc);
+        return rc;
+    }
+    for (size_t i = 0; i < gs.size(); ++i) {
+        Job& j = *gj[i];
+        j.next = gs[i].argmax;
+        if (!j.prefilled) {
+            j.input.erase(j.input.begin(), j.input.begin() + gs[i].n);
+            if (!j.input.empty()) continue;
+            j.prefilled = true;
+            j.t_prefill = Clock::now();
+            j.res.prefill_ms = ms_since(j.t0);
+            j.res.prefill_tokens = j.n_input;
+        } else {
+            j.decoding = false;
+            if (j.cb) j.cb(j.user, j.session, j.step, j.out.back(), ms_since(j.t_step));
+            ++j.step;
+        }
+        job_advance(j);
+    }
+    return KV_OK;
+}
+
+std::shared_ptr<Job> make_job(const qw2_request& r) {
+    auto j = std::make_shared<Job>();
+    j->session = r.session;
+    j->input.assign(r.input_ids, r.input_ids + r.n_input);
+    j->n_input = r.n_input;
+    j->max_new = r.cfg.max_new_tokens;
+    j->rep_window = r.cfg.repetition_window;
+    if (r.cfg.n_stop > 0) j->stops.assign(r.cfg.stop_tokens, r.cfg.stop_tokens + r.cfg.n_stop);
+    j->cb = r.on_token;
+    j->user = r.user;
+    j->t0 = Clock::now();
+    return j;
+}
+
+int check_request(const qw2_model* m, const qw2_request& r) {
+    QW_OK(session_check(m, r.session));
+    if (r.n_input < 0 || (r.n_input > 0 && !r.input_ids) || (r.cfg.n_stop > 0 && !r.cfg.stop_tokens) ||
+        r.cfg.n_stop < 0 || (r.out_cap > 0 && !r.out_ids))
+        return qfail(KV_ERR_INVAL, "malformed request for session %d", r.session);
+    return KV_OK;
+}
+
+// Run jobs to completion on the calling thread (the model lock held).
+int run_jobs(qw2_model* m, std::vector<Job*>& jobs) {
+    for (Job* j : jobs)
+        if (j->n_input == 0) job_finish(*j, KV_OK);  // llm_engine.cpp:59: nothing to do
+    for (;;) {
+        bool live = false;
+        for (Job* j : jobs) live = live || !j->done;
+        if (!live) return KV_OK;
+        const int rc = engine_step(m, jobs);
+        if (rc != KV_OK) {
+            for (Job* j : jobs)
+                if (!j->done) job_finish(*j, rc);
+            return rc;
+        }
+    }
+}
+
+void worker_loop(qw2_model* m) {
+    std::vector<std::shared_ptr<Job>> active;
+    for (;;) {
+        {
+            std::unique_lock<std::mutex> lk(m->qmu);
+            m->qcv.wait(lk, [&] { return m->stop_worker || !m->queue.empty() || !active.empty(); });
+            if (m->stop_worker) {
+                for (auto& j : active) {
+                    job_finish(*j, KV_ERR_STATE);
+                    m->finished[j->id] = j;
+                }
+                for (auto& j : m->queue) {
+                    job_finish(*j, KV_ERR_STATE);
+                    m->finished[j->id] = j;
+                }
+                m->queue.clear();
+                m->qcv.notify_all();
+                return;
+            }
+            while (!m->queue.empty()) {
+                active.push_back(m->queue.front());
+                m->queue.pop_front();
+            }
+        }
+        std::vector<Job*> raw;
+        for (auto& j : active) {
+            if (j->n_input == 0 && !j->done) job_finish(*j, KV_OK);
+            raw.push_back(j.get());
+        }
+        {
+            std::lock_guard<std::mutex> mk(m->mu);
+            const int rc = engine_step(m, raw);
+            if (rc != KV_OK)
+                for (Job* j : raw)
+                    if (!j->done) job_finish(*j, rc);
+        }
+        std::lock_guard<std::mutex> lk(m->qmu);
+        std::vector<std::shared_ptr<Job>> still;
+        for (auto& j : active) {
+            if (j->done) {
+                m->running.erase(j->id);
+                m->session_busy[j->session] = 0;
+                m->finished[j->id] = j;
+            } else {
+                still.push_back(j);
+            }
+        }
+        active.swap(still);
+        m->qcv.notify_all();
+    }
+}
+
+}  // namespace
+
 extern "C" {
 
 int qw2_config_default(qw2_config* c) {
@@ -371,6 +780,12 @@ int qw2_config_default(qw2_config* c) {
 
 int qw2_destroy(qw2_model* m) {
     if (!m) return KV_OK;
+    {
+        std::lock_guard<std::mutex> lk(m->qmu);
+        m->stop_worker = true;
+    }
+    m->qcv.notify_all();
+    if (m->worker.joinable()) m->worker.join();
     DeviceGuard g(m->device);
     if (m->st) cudaStreamSynchronize(m->st);
     if (m->pool) kvp_destroy(m->pool);
@@ -380,10 +795,11 @@ int qw2_destroy(qw2_model* m) {
     return KV_OK;
 }
 
-int qw2_create(int device, const qw2_config* cfg, qw2_model** out) {
+int qw2_create_sessions(int device, const qw2_config* cfg, int max_sessions, qw2_model** out) {
     if (!out) return qfail(KV_ERR_INVAL, "NULL out");
     *out = nullptr;
     QW_OK(check_cfg(cfg));
+    if (max_sessions < 1 || max_sessions > 1024) return qfail(KV_ERR_INVAL, "max_sessions %d outside [1, 1024]", max_sessions);
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
         return qfail(KV_ERR_INVAL, "no CUDA device %d", device);
@@ -393,7 +809,12 @@ int qw2_create(int device, const qw2_config* cfg, qw2_model** out) {
     m->device = device;
     m->c = *cfg;
     m->kvd = cfg->kv_heads * cfg->head_dim;
-    const size_t H = cfg->hidden, kvd = m->kvd, IS = cfg->intermediate, V = cfg->vocab, R = cfg->max_position;
+    m->max_sessions = max_sessions;
+    m->rows_cap = cfg->max_position + max_sessions;
+    m->session_seq.assign(max_sessions, -1);
+    m->session_busy.assign(max_sessions, 0);
+    const size_t H = cfg->hidden, kvd = m->kvd, IS = cfg->intermediate, V = cfg->vocab, R = m->rows_cap,
+                 S = max_sessions;
     int rc = KV_OK;
     auto step = [&](int s) {
         if (rc == KV_OK) rc = s;
@@ -417,9 +838,10 @@ int qw2_create(int device, const qw2_config* cfg, qw2_model** out) {
     step(m->alloc_n(&m->v, R * kvd));
     step(m->alloc_n(&m->attn, R * H));
     step(m->alloc_n(&m->h16, R * IS));
-    step(m->alloc_n(&m->logits, V));
-    step(m->alloc_n(&m->ids, R));
-    step(m->alloc_n(&m->best, 1));
+    step(m->alloc_n(&m->logits, S * V));
+    step(m->alloc_n(&m->last, S * H));
+    step(m->alloc_n(&m->ids, R + S));
+    step(m->alloc_n(&m->best, S));
     step(m->alloc(&m->staging, kStagingBytes));
     if (rc == KV_OK) {
         if (cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking) != cudaSuccess)
@@ -428,14 +850,14 @@ int qw2_create(int device, const qw2_config* cfg, qw2_model** out) {
             m->own_stream = true;
     }
     if (rc == KV_OK) {
-        const int blocks = (cfg->max_position + kBlockTokens - 1) / kBlockTokens;
+        const int blocks = max_sessions * ((cfg->max_position + kBlockTokens - 1) / kBlockTokens);
         step(kvp_create(device, cfg->layers, cfg->q_heads, cfg->kv_heads, cfg->head_dim, kBlockTokens, blocks,
-                        KV_F16, 1, cfg->max_position, cfg->rope_theta, &m->pool));
+                        KV_F16, max_sessions, cfg->max_position, cfg->rope_theta, &m->pool));
     }
     // every forward ends with a host synchronisation, so no decode launch
     // overlaps a kernel that writes the cache (kvp_set_overlap's contract)
     if (rc == KV_OK) step(kvp_set_overlap(m->pool, 1));
-    if (rc == KV_OK) step(new_sequence(m));
+    if (rc == KV_OK) step(kvp_seq_alloc(m->pool, &m->session_seq[0]));  // session 0
     if (rc != KV_OK) {
         const std::string msg = kv_last_error();
         qw2_destroy(m);
@@ -443,6 +865,10 @@ int qw2_create(int device, const qw2_config* cfg, qw2_model** out) {
     }
     *out = m;
     return KV_OK;
+}
+
+int qw2_create(int device, const qw2_config* cfg, qw2_model** out) {
+    return qw2_create_sessions(device, cfg, 1, out);
 }
 
 int qw2_set_stream(qw2_model* m, void* stream) {
@@ -459,6 +885,7 @@ int qw2_set_tensor(qw2_model* m, const char* name, int dtype, const int64_t* sha
     if (!m || !name || !shape || !host) return qfail(KV_ERR_INVAL, "NULL argument");
     if (dtype != QW2_F16 && dtype != QW2_BF16 && dtype != QW2_F32)
         return qfail(KV_ERR_INVAL, "tensor '%s': unsupported dtype %d", name, dtype);
+    std::lock_guard<std::mutex> lk(m->mu);
     Target t;
     QW_OK(resolve(m, name, &t));
     const bool shape_ok = t.matrix ? (ndim == 2 && shape[0] == t.rows && shape[1] == t.cols)
@@ -562,142 +989,189 @@ int qw2_ready(qw2_model* m) {
 
 int qw2_reset(qw2_model* m) {
     if (!m) return qfail(KV_ERR_INVAL, "NULL model");
+    std::lock_guard<std::mutex> lk(m->mu);
+    if (m->session_busy[0]) return qfail(KV_ERR_STATE, "session 0 has a running request");
     DeviceGuard g(m->device);
-    QW_OK(kvp_reset(m->pool, m->st));
-    QW_OK(new_sequence(m));
+    bool others = false;
+    for (int s = 1; s < m->max_sessions; ++s) others = others || m->session_seq[s] >= 0;
+    if (!others) {
+        // Qwen2Model::reset_kv_cache: the whole cache zeroed (kv_cache.cpp:12-16)
+        QW_OK(kvp_reset(m->pool, m->st));
+    } else {
+        QW_OK(kvp_seq_free(m->pool, m->session_seq[0]));  // other sessions keep their blocks
+    }
+    QW_OK(kvp_seq_alloc(m->pool, &m->session_seq[0]));
     QW_CUDA(cudaStreamSynchronize(m->st));
     return KV_OK;
 }
 
-int qw2_cur_pos(const qw2_model* m, int* pos) {
-    if (!m || !pos) return qfail(KV_ERR_INVAL, "NULL argument");
-    return kvp_seq_len(m->pool, m->seq, pos);
+int qw2_cur_pos(const qw2_model* m, int* pos) { return qw2_session_len(m, 0, pos); }
+
+int qw2_session_create(qw2_model* m, int* session) {
+    if (!m || !session) return qfail(KV_ERR_INVAL, "NULL argument");
+    std::lock_guard<std::mutex> lk(m->mu);
+    for (int s = 0; s < m->max_sessions; ++s)
+        if (m->session_seq[s] < 0) {
+            QW_OK(kvp_seq_alloc(m->pool, &m->session_seq[s]));
+            *session = s;
+            return KV_OK;
+        }
+    return qfail(KV_ERR_OOM, "all %d sessions in use", m->max_sessions);
+}
+
+int qw2_session_destroy(qw2_model* m, int session) {
+    if (!m) return qfail(KV_ERR_INVAL, "NULL model");
+    std::lock_guard<std::mutex> lk(m->mu);
+    QW_OK(session_check(m, session));
+    {
+        std::lock_guard<std::mutex> qk(m->qmu);
+        if (m->session_busy[session]) return qfail(KV_ERR_STATE, "session %d has a running request", session);
+    }
+    QW_OK(kvp_seq_free(m->pool, m->session_seq[session]));
+    m->session_seq[session] = -1;
+    return KV_OK;
+}
+
+int qw2_session_exists(const qw2_model* m, int session, int* exists) {
+    if (!m || !exists) return qfail(KV_ERR_INVAL, "NULL argument");
+    *exists = session >= 0 && session < m->max_sessions && m->session_seq[session] >= 0;
+    return KV_OK;
+}
+
+int qw2_session_len(const qw2_model* m, int session, int* len) {
+    if (!m || !len) return qfail(KV_ERR_INVAL, "NULL argument");
+    QW_OK(session_check(m, session));
+    return kvp_seq_len(m->pool, m->session_seq[session], len);
+}
+
+int qw2_session_seq(const qw2_model* m, int session, int* seq_id) {
+    if (!m || !seq_id) return qfail(KV_ERR_INVAL, "NULL argument");
+    QW_OK(session_check(m, session));
+    *seq_id = m->session_seq[session];
+    return KV_OK;
+}
+
+int qw2_forward_session(qw2_model* m, int session, const int* tokens, int n, float* logits_host, int* argmax) {
+    if (!m || !tokens) return qfail(KV_ERR_INVAL, "NULL argument");
+    std::lock_guard<std::mutex> lk(m->mu);
+    QW_OK(session_check(m, session));
+    {
+        std::lock_guard<std::mutex> qk(m->qmu);
+        if (m->session_busy[session]) return qfail(KV_ERR_STATE, "session %d has a running request", session);
+    }
+    std::vector<Group> gs(1);
+    gs[0].session = session;
+    gs[0].tokens = tokens;
+    gs[0].n = n;
+    gs[0].logits_host = logits_host;
+    QW_OK(forward_groups(m, gs));
+    if (argmax) *argmax = gs[0].argmax;
+    return KV_OK;
 }
 
 int qw2_forward(qw2_model* m, const int* tokens, int n, float* logits_host, int* argmax) {
-    if (!m || !tokens) return qfail(KV_ERR_INVAL, "NULL argument");
-    if (n <= 0) return qfail(KV_ERR_INVAL, "forward of %d tokens", n);
-    QW_OK(qw2_ready(m));
-    const qw2_config& c = m->c;
-    for (int i = 0; i < n; ++i)
-        if (tokens[i] < 0 || tokens[i] >= c.vocab) return qfail(KV_ERR_RANGE, "token id %d outside [0, %d)", tokens[i], c.vocab);
-    int pos = 0;
-    QW_OK(kvp_seq_len(m->pool, m->seq, &pos));
-    if (pos + n > c.max_position)
-        return qfail(KV_ERR_RANGE, "positions %d..%d pass max_position %d", pos, pos + n - 1, c.max_position);
-    DeviceGuard g(m->device);
-    cudaStream_t st = m->st;
-    const int H = c.hidden, kvd = m->kvd, IS = c.intermediate;
+    return qw2_forward_session(m, 0, tokens, n, logits_host, argmax);
+}
 
-    QW_CUDA(cudaMemcpyAsync(m->ids, tokens, sizeof(int) * n, cudaMemcpyHostToDevice, st));
-    QW_CUDA(launch_embed(m->ids, n, m->embed, m->hidden, H, st));
-    if (n == 1) QW_OK(attn_decode_plan(m->pool, 1, &m->seq, st));
-    else QW_OK(kvp_seq_reserve(m->pool, m->seq, pos + n));
-
-    for (int li = 0; li < c.layers; ++li) {
-        const qw2_model::Layer& Ly = m->L[li];
-        // 1-2: input RMSNorm fused into the Q/K/V projections (+ biases)
-        GemvArgs a;
-        a.w = Ly.wqkv;
-        a.N = H + 2 * kvd;
-        a.K = H;
-        a.M = n;
-        a.x = m->hidden;
-        a.norm_w = Ly.ln1;
-        a.eps = c.rms_eps;
-        a.bias = Ly.bqkv;
-        a.out0 = m->q;
-        a.out1 = m->k;
-        a.out2 = m->v;
-        a.n0 = H;
-        a.n1 = kvd;
-        QW_CUDA(launch_gemv(0, 2, a, st));
-        // 3-5: RoPE, KV append, attention
-        if (n == 1) {
-            QW_OK(attn_decode_append(m->pool, li, m->q, m->k, m->v, m->attn, st));
-        } else {
-            QW_OK(kv_append_chunk(m->pool, li, m->seq, pos, n, m->k, m->v, st));
-            QW_OK(attn_prefill(m->pool, li, m->seq, pos, n, m->q, m->attn, st));
-        }
-        // 6-7: O projection + residual
-        GemvArgs o;
-        o.w = Ly.wo;
-        o.N = H;
-        o.K = H;
-        o.M = n;
-        o.x = m->attn;
-        o.resid = m->hidden;
-        QW_CUDA(launch_gemv(1, 1, o, st));
-        // 8-10: post-attention RMSNorm fused into gate/up (+ SiLU product), down + residual
-        GemvArgs gu;
-        gu.w = Ly.wg;
-        gu.w2 = Ly.wu;
-        gu.N = IS;
-        gu.K = H;
-        gu.M = n;
-        gu.x = m->hidden;
-        gu.norm_w = Ly.ln2;
-        gu.eps = c.rms_eps;
-        gu.out16 = m->h16;
-        QW_CUDA(launch_gemv(2, 2, gu, st));
-        GemvArgs d;
-        d.w = Ly.wd;
-        d.N = H;
-        d.K = IS;
-        d.M = n;
-        d.x = m->h16;
-        d.resid = m->hidden;
-        QW_CUDA(launch_gemv(1, 0, d, st));
+int qw2_generate_batch(qw2_model* m, int n_requests, const qw2_request* requests, qw2_result* results) {
+    if (!m || n_requests < 0 || (n_requests > 0 && (!requests || !results)))
+        return qfail(KV_ERR_INVAL, "NULL argument");
+    std::lock_guard<std::mutex> lk(m->mu);
+    std::vector<char> seen(m->max_sessions, 0);
+    for (int i = 0; i < n_requests; ++i) {
+        QW_OK(check_request(m, requests[i]));
+        if (seen[requests[i].session]) return qfail(KV_ERR_INVAL, "session %d twice in one batch", requests[i].session);
+        seen[requests[i].session] = 1;
+        std::lock_guard<std::mutex> qk(m->qmu);
+        if (m->session_busy[requests[i].session])
+            return qfail(KV_ERR_STATE, "session %d has a running request", requests[i].session);
     }
-    if (n == 1) QW_OK(attn_decode_commit(m->pool));
-    else QW_OK(kvp_seq_set_len(m->pool, m->seq, pos + n));
+    std::vector<std::shared_ptr<Job>> jobs;
+    std::vector<Job*> raw;
+    for (int i = 0; i < n_requests; ++i) {
+        jobs.push_back(make_job(requests[i]));
+        raw.push_back(jobs.back().get());
+    }
+    const int rc = run_jobs(m, raw);
+    for (int i = 0; i < n_requests; ++i) {
+        const Job& j = *jobs[i];
+        results[i] = j.res;
+        for (int k = 0; k < (int)j.out.size() && k < requests[i].out_cap; ++k) requests[i].out_ids[k] = j.out[k];
+    }
+    return rc;
+}
 
-    // final RMSNorm of the last token fused into lm_head (tied embedding), argmax
-    GemvArgs lm;
-    lm.w = m->embed;
-    lm.N = c.vocab;
-    lm.K = H;
-    lm.M = 1;
-    lm.x = m->hidden + (size_t)(n - 1) * H;
-    lm.norm_w = m->norm;
-    lm.eps = c.rms_eps;
-    lm.logits = m->logits;
-    QW_CUDA(launch_gemv(3, 2, lm, st));
-    QW_CUDA(launch_argmax(m->logits, c.vocab, m->best, st));
-    unsigned long long key = 0;
-    QW_CUDA(cudaMemcpyAsync(&key, m->best, sizeof key, cudaMemcpyDeviceToHost, st));
-    if (logits_host)
-        QW_CUDA(cudaMemcpyAsync(logits_host, m->logits, sizeof(float) * (size_t)c.vocab, cudaMemcpyDeviceToHost, st));
-    int status = 0;
-    QW_OK(kvp_device_status(m->pool, st, &status));  // synchronises the stream
-    if (status != 0) return status;
-    if (argmax) *argmax = key ? (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFu)) : 0;
-    return KV_OK;
+int qw2_generate_session(qw2_model* m, int session, const int* input_ids, int n_input, const qw2_gen_config* cfg,
+                         int* out_ids, int out_cap, qw2_result* result) {
+    if (!m || !cfg || !result) return qfail(KV_ERR_INVAL, "NULL argument");
+    qw2_request r{};
+    r.session = session;
+    r.input_ids = input_ids;
+    r.n_input = n_input;
+    r.cfg = *cfg;
+    r.out_ids = out_ids;
+    r.out_cap = out_cap;
+    return qw2_generate_batch(m, 1, &r, result);
 }
 
 int qw2_generate(qw2_model* m, const int* prompt, int n_prompt, int max_new, const int* stop_tokens, int n_stop,
                  int repetition_window, int* out_ids, int cap, int* n_out) {
-    if (!m || !n_out || (n_stop > 0 && !stop_tokens) || (cap > 0 && !out_ids))
-        return qfail(KV_ERR_INVAL, "NULL argument");
+    if (!m || !n_out) return qfail(KV_ERR_INVAL, "NULL argument");
     *n_out = 0;
     if (n_prompt <= 0 || !prompt) return KV_OK;  // llm_engine.cpp:59
-    auto is_stop = [&](int id) {
-        for (int i = 0; i < n_stop; ++i)
-            if (stop_tokens[i] == id) return true;
-        return false;
-    };
-    int next = 0;
-    QW_OK(qw2_forward(m, prompt, n_prompt, nullptr, &next));
-    std::vector<int> out;
-    for (int step = 0; step < max_new; ++step) {
-        if (is_stop(next)) break;
-        out.push_back(next);
-        if (repetition_window > 0 && detect_repetition(out, repetition_window)) break;
-        const int id = next;
-        QW_OK(qw2_forward(m, &id, 1, nullptr, &next));
+    qw2_gen_config cfg{max_new, repetition_window, stop_tokens, n_stop};
+    qw2_result res{};
+    QW_OK(qw2_generate_session(m, 0, prompt, n_prompt, &cfg, out_ids, cap, &res));
+    *n_out = res.n_out;
+    return res.status;
+}
+
+int qw2_submit(qw2_model* m, const qw2_request* request, int* job) {
+    if (!m || !request || !job) return qfail(KV_ERR_INVAL, "NULL argument");
+    QW_OK(check_request(m, *request));
+    auto j = make_job(*request);
+    {
+        std::lock_guard<std::mutex> lk(m->qmu);
+        if (m->stop_worker) return qfail(KV_ERR_STATE, "model is being destroyed");
+        if (m->session_busy[request->session])
+            return qfail(KV_ERR_STATE, "session %d has a running request", request->session);
+        m->session_busy[request->session] = 1;
+        j->id = m->next_job++;
+        m->running[j->id] = j;
+        m->queue.push_back(j);
+        if (!m->worker.joinable()) m->worker = std::thread(worker_loop, m);
     }
-    for (size_t i = 0; i < out.size() && (int)i < cap; ++i) out_ids[i] = out[i];
-    *n_out = (int)out.size();
+    m->qcv.notify_all();
+    *job = j->id;
+    return KV_OK;
+}
+
+int qw2_wait(qw2_model* m, int job, int timeout_ms, int* out_ids, int out_cap, qw2_result* result) {
+    if (!m || !result || (out_cap > 0 && !out_ids)) return qfail(KV_ERR_INVAL, "NULL argument");
+    std::unique_lock<std::mutex> lk(m->qmu);
+    auto ready = [&] { return m->finished.count(job) > 0; };
+    if (!ready() && !m->running.count(job)) return qfail(KV_ERR_INVAL, "no job %d", job);
+    if (timeout_ms < 0) m->qcv.wait(lk, ready);
+    else if (!m->qcv.wait_for(lk, std::chrono::milliseconds(timeout_ms), ready))
+        return qfail(KV_ERR_TIMEOUT, "job %d still running", job);
+    std::shared_ptr<Job> j = m->finished[job];
+    m->finished.erase(job);
+    *result = j->res;
+    for (int k = 0; k < (int)j->out.size() && k < out_cap; ++k) out_ids[k] = j->out[k];
+    return KV_OK;
+}
+
+int qw2_cancel(qw2_model* m, int session) {
+    if (!m) return qfail(KV_ERR_INVAL, "NULL model");
+    std::lock_guard<std::mutex> lk(m->qmu);
+    bool any = false;
+    for (auto& kv : m->running)
+        if (kv.second->session == session) {
+            kv.second->cancel = true;
+            any = true;
+        }
+    if (!any) return qfail(KV_ERR_BADSEQ, "no request running on session %d", session);
+    m->qcv.notify_all();
     return KV_OK;
 }
 

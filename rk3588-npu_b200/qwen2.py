@@ -114,8 +114,44 @@ def write_safetensors(path: str, specs, tensors, dtype: str = "F32") -> None:
             f.write(f32_to_f16_trunc(a).tobytes() if dt == "F16" else np.ascontiguousarray(a, np.float32).tobytes())
 
 
+class Qw2GenConfig(C.Structure):
+    _fields_ = [("max_new_tokens", C.c_int), ("repetition_window", C.c_int), ("stop_tokens", C.POINTER(C.c_int)),
+                ("n_stop", C.c_int)]
+
+
+class Qw2Result(C.Structure):
+    _fields_ = [("n_out", C.c_int), ("prefill_tokens", C.c_int), ("decode_tokens", C.c_int),
+                ("prefill_ms", C.c_float), ("decode_ms", C.c_float), ("hit_stop", C.c_int),
+                ("hit_repetition", C.c_int), ("cancelled", C.c_int), ("status", C.c_int)]
+
+    def as_dict(self) -> dict:
+        return {f: getattr(self, f) for f, _ in self._fields_}
+
+
+TOKEN_CB = C.CFUNCTYPE(None, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_float)
+
+
+class Qw2Request(C.Structure):
+    _fields_ = [("session", C.c_int), ("input_ids", C.POINTER(C.c_int)), ("n_input", C.c_int),
+                ("cfg", Qw2GenConfig), ("out_ids", C.POINTER(C.c_int)), ("out_cap", C.c_int),
+                ("on_token", TOKEN_CB), ("user", C.c_void_p)]
+
+
 _SIGS = {
     "qw2_config_default": [C.POINTER(Qw2Config)],
+    "qw2_create_sessions": [C.c_int, C.POINTER(Qw2Config), C.c_int, C.POINTER(C.c_void_p)],
+    "qw2_session_create": [C.c_void_p, C.POINTER(C.c_int)],
+    "qw2_session_destroy": [C.c_void_p, C.c_int],
+    "qw2_session_exists": [C.c_void_p, C.c_int, C.POINTER(C.c_int)],
+    "qw2_session_len": [C.c_void_p, C.c_int, C.POINTER(C.c_int)],
+    "qw2_session_seq": [C.c_void_p, C.c_int, C.POINTER(C.c_int)],
+    "qw2_forward_session": [C.c_void_p, C.c_int, C.POINTER(C.c_int), C.c_int, C.c_void_p, C.POINTER(C.c_int)],
+    "qw2_generate_session": [C.c_void_p, C.c_int, C.POINTER(C.c_int), C.c_int, C.POINTER(Qw2GenConfig),
+                             C.POINTER(C.c_int), C.c_int, C.POINTER(Qw2Result)],
+    "qw2_generate_batch": [C.c_void_p, C.c_int, C.POINTER(Qw2Request), C.POINTER(Qw2Result)],
+    "qw2_submit": [C.c_void_p, C.POINTER(Qw2Request), C.POINTER(C.c_int)],
+    "qw2_wait": [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_int), C.c_int, C.POINTER(Qw2Result)],
+    "qw2_cancel": [C.c_void_p, C.c_int],
     "qw2_create": [C.c_int, C.POINTER(Qw2Config), C.POINTER(C.c_void_p)],
     "qw2_destroy": [C.c_void_p],
     "qw2_set_tensor": [C.c_void_p, C.c_char_p, C.c_int, C.POINTER(C.c_longlong), C.c_int, C.c_void_p],
@@ -149,15 +185,17 @@ def _ints(xs):
 
 
 class Model:
-    """Qwen2Model + LLMEngine on one GPU (weights, KV pool and scratch on the device)."""
+    """Qwen2Model + LLMEngine on one GPU (weights, KV pool and scratch on the
+    device), with up to `max_sessions` sessions sharing the weights."""
 
-    def __init__(self, device: int = 0, cfg: dict = QWEN2_1_5B):
+    def __init__(self, device: int = 0, cfg: dict = QWEN2_1_5B, max_sessions: int = 1):
         self.L = _lib()
         c = Qw2Config(**cfg)
         h = C.c_void_p()
-        _check(self.L.qw2_create(device, C.byref(c), C.byref(h)), "qw2_create")
+        _check(self.L.qw2_create_sessions(device, C.byref(c), max_sessions, C.byref(h)), "qw2_create_sessions")
         self.h = h
         self.cfg = dict(cfg)
+        self._keep = {}  # ctypes objects an async job still points at
 
     def close(self) -> None:
         if self.h:
@@ -217,6 +255,85 @@ class Model:
         _check(self.L.qw2_generate(self.h, ids, len(prompt), max_new, stops, len(stop_tokens), repetition_window,
                                    out, max_new, C.byref(n)), "qw2_generate")
         return [out[i] for i in range(n.value)]
+
+    # ---------------------------------------------------------- sessions
+    def create_session(self) -> int:
+        sid = C.c_int()
+        _check(self.L.qw2_session_create(self.h, C.byref(sid)), "qw2_session_create")
+        return sid.value
+
+    def destroy_session(self, session: int) -> None:
+        _check(self.L.qw2_session_destroy(self.h, session), "qw2_session_destroy")
+
+    def session_exists(self, session: int) -> bool:
+        e = C.c_int()
+        _check(self.L.qw2_session_exists(self.h, session, C.byref(e)), "qw2_session_exists")
+        return bool(e.value)
+
+    def session_len(self, session: int) -> int:
+        n = C.c_int()
+        _check(self.L.qw2_session_len(self.h, session, C.byref(n)), "qw2_session_len")
+        return n.value
+
+    def forward_session(self, session: int, tokens) -> tuple[np.ndarray, int]:
+        ids = _ints(tokens)
+        logits = np.empty(self.cfg["vocab"], np.float32)
+        am = C.c_int()
+        _check(self.L.qw2_forward_session(self.h, session, ids, len(tokens), logits.ctypes.data_as(C.c_void_p),
+                                          C.byref(am)), "qw2_forward_session")
+        return logits, am.value
+
+    def _request(self, session, input_ids, max_new_tokens, stop_tokens=(), repetition_window=0, on_token=None,
+                 out_cap=None):
+        ids = _ints(input_ids)
+        stops = _ints(stop_tokens)
+        cap = max_new_tokens if out_cap is None else out_cap
+        out = (C.c_int * max(1, cap))()
+        cb = TOKEN_CB(lambda user, s, step, tok, ms: on_token(s, step, tok, ms)) if on_token else TOKEN_CB()
+        r = Qw2Request(session, ids, len(input_ids), Qw2GenConfig(max_new_tokens, repetition_window, stops,
+                                                                  len(stop_tokens)), out, cap, cb, None)
+        return r, (ids, stops, out, cb)
+
+    def generate_session(self, session: int, input_ids, max_new_tokens: int, stop_tokens=(),
+                         repetition_window: int = 0):
+        """generate_session: (generated ids, result dict); the session keeps its cache."""
+        r, keep = self._request(session, input_ids, max_new_tokens, stop_tokens, repetition_window)
+        res = Qw2Result()
+        _check(self.L.qw2_generate_session(self.h, session, r.input_ids, r.n_input, C.byref(r.cfg), r.out_ids,
+                                           r.out_cap, C.byref(res)), "qw2_generate_session")
+        return [keep[2][i] for i in range(min(res.n_out, r.out_cap))], res.as_dict()
+
+    def generate_batch(self, requests):
+        """generate_batch: requests are dicts (session, input_ids, max_new_tokens,
+        stop_tokens=(), repetition_window=0, on_token=None); returns a list of
+        (ids, result dict)."""
+        built = [self._request(q["session"], q["input_ids"], q["max_new_tokens"], q.get("stop_tokens", ()),
+                               q.get("repetition_window", 0), q.get("on_token")) for q in requests]
+        arr = (Qw2Request * max(1, len(built)))(*[b[0] for b in built])
+        res = (Qw2Result * max(1, len(built)))()
+        _check(self.L.qw2_generate_batch(self.h, len(built), arr, res), "qw2_generate_batch")
+        return [([b[1][2][i] for i in range(min(res[k].n_out, b[0].out_cap))], res[k].as_dict())
+                for k, b in enumerate(built)]
+
+    def submit(self, session: int, input_ids, max_new_tokens: int, stop_tokens=(), repetition_window: int = 0,
+               on_token=None) -> int:
+        """generate_async: returns a job id at once (a worker thread runs it)."""
+        r, keep = self._request(session, input_ids, max_new_tokens, stop_tokens, repetition_window, on_token)
+        job = C.c_int()
+        _check(self.L.qw2_submit(self.h, C.byref(r), C.byref(job)), "qw2_submit")
+        self._keep[job.value] = (keep, max_new_tokens)
+        return job.value
+
+    def wait(self, job: int, timeout_ms: int = -1):
+        cap = self._keep.get(job, (None, 1))[1]
+        out = (C.c_int * max(1, cap))()
+        res = Qw2Result()
+        _check(self.L.qw2_wait(self.h, job, timeout_ms, out, cap, C.byref(res)), "qw2_wait")
+        self._keep.pop(job, None)
+        return [out[i] for i in range(min(res.n_out, cap))], res.as_dict()
+
+    def cancel(self, session: int) -> None:
+        _check(self.L.qw2_cancel(self.h, session), "qw2_cancel")
 
     def weight_bytes(self) -> int:
         b = C.c_longlong()
