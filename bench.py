@@ -57,7 +57,7 @@ class Workload:
 
     @property
     def dtype_name(self) -> str:
-        return "f16" if self.dtype == 0 else "bf16"
+        return ("f16", "bf16", "int8")[self.dtype]
 
 
 def uniform_lengths(n=32, seed=1) -> list[int]:
@@ -148,6 +148,9 @@ def parse_args():
                          "launch, or by the fused peer-memory exchange kernel")
     ap.add_argument("--prefill-kernel", choices=["tc", "mma"], default="tc",
                     help="prefill workload: the tcgen05 kernel (attn_prefill) or the mma.sync baseline")
+    ap.add_argument("--kv-dtype", choices=["native", "int8"], default="native",
+                    help="batch32 / paged28 / paged1: keep the workload's cache type, or an INT8 cache "
+                         "(per-row scales) with the same contexts")
     ap.add_argument("--sessions", type=int, default=8,
                     help="model_batch workload: concurrent sessions decoding together")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -176,14 +179,16 @@ def dist_env():
     return rank, world, local
 
 
-def step_bytes(kv_lens) -> float:
+def step_bytes(kv_lens, dtype: int = 0) -> float:
     """Algorithmic HBM bytes of one decode launch.  Per sequence attending T
     tokens: the K and V rows of the T-1 cached tokens (2 KV heads x 128 dims
-    x 2 B x 2 = 1024 B per token), the appended 1024 B row, fp32 q/k/v in and
-    fp32 out (4 x (1536 + 256 + 256 + 1536) B), and 4 B per block-table entry."""
+    x 2 B x 2 = 1024 B per token; INT8: 2 x (128 codes + a 4-byte scale) x 2
+    = 528 B), the appended row, fp32 q/k/v in and fp32 out
+    (4 x (1536 + 256 + 256 + 1536) B), and 4 B per block-table entry."""
+    row = 528.0 if dtype == 2 else 1024.0
     tot = 0.0
     for T in kv_lens:
-        tot += 1024.0 * (T - 1) + 1024.0 + 4.0 * -(-T // 16) + 4.0 * (HID + 2 * KVD + HID)
+        tot += row * (T - 1) + row + 4.0 * -(-T // 16) + 4.0 * (HID + 2 * KVD + HID)
     return tot
 
 
@@ -273,6 +278,8 @@ def peak_hbm():
 def ncu_traffic(profile: str):
     """Per-launch DRAM bytes of the decode kernel from the committed ncu
     summary of the workload (line `traffic_bytes_per_launch:`)."""
+    if not profile:
+        return None
     path = os.path.join(ROOT, "profiles", profile)
     try:
         for line in open(path):
@@ -309,6 +316,18 @@ def setup_pool(kv, torch, dev, wl: Workload, steps_total: int, seed: int):
     g = torch.Generator(device="cuda").manual_seed(seed)
     total = sum(wl.lens)
     for layer in range(wl.layers):
+        if wl.dtype == 2:  # INT8: seeded codes and per-row scales
+            kc = torch.randint(-127, 128, (total, KVD), generator=g, device="cuda", dtype=torch.int8)
+            vc = torch.randint(-127, 128, (total, KVD), generator=g, device="cuda", dtype=torch.int8)
+            ks = torch.rand((total, NKV), generator=g, device="cuda") * 0.03 + 0.001
+            vs = torch.rand((total, NKV), generator=g, device="cuda") * 0.03 + 0.001
+            o = 0
+            for s, L in zip(ids, wl.lens):
+                if L:
+                    P.import_i8(layer, s, 0, kc[o:o + L], vc[o:o + L], ks[o:o + L], vs[o:o + L])
+                o += L
+            del kc, vc, ks, vs
+            continue
         k_all = encode_device(torch.randn((total, KVD), generator=g, device="cuda"), wl.dtype)
         v_all = encode_device(torch.randn((total, KVD), generator=g, device="cuda"), wl.dtype)
         o = 0
@@ -334,6 +353,11 @@ def run_ours(args, rank, world, local):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     wl = make_workload(args.workload)
+    if args.kv_dtype == "int8":
+        wl.dtype = 2
+        wl.desc += "; INT8 KV cache (per (token, KV head) row fp32 scale, codes in [-127, 127])"
+        wl.data = wl.data.replace("K/V", "INT8 K/V codes and scales")
+        wl.profile = None
     B, NL, lens = wl.batch, wl.layers, wl.lens
     K, W = args.steps, args.warmup
     P, ids = setup_pool(kv, torch, local, wl, K + W + 10, seed=1 + rank)
@@ -457,7 +481,7 @@ def run_ours(args, rank, world, local):
     step_ms, kern_ms, e2e_ms = times.tolist()
     # decode kernel per layer (+ its split combine), counted by the library
     if rank == 0:
-        alg = sum(step_bytes(kl) for kl in kv_lens_per_step) / K  # per launch
+        alg = sum(step_bytes(kl, wl.dtype) for kl in kv_lens_per_step) / K  # per launch
         peak, peak_kind = peak_hbm()
         achieved = alg / (kern_ms / (K * NL) * 1e-3) / 1e9
         line = {

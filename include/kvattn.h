@@ -52,7 +52,13 @@ enum kv_status {
     KV_ERR_TIMEOUT = 7  /* a device-side bounded wait gave up (see kvp_device_status) */
 };
 
-enum kv_dtype { KV_F16 = 0, KV_BF16 = 1 };
+/* KV cache element types.  KV_I8: the INT8 compression the reference plans
+ * (docs/work_division.md:72): per (token, KV head) row of 128 values one fp32
+ * scale = max|x| / 127 and codes round-half-away(x / scale) in [-127, 127];
+ * attention reads code * scale.  INT8 pools serve the decode path
+ * (attn_decode_*, kv_append_chunk, kvp_import_i8 / kvp_gather_i8); the
+ * prefill attention and the 16-bit import / gather reject them. */
+enum kv_dtype { KV_F16 = 0, KV_BF16 = 1, KV_I8 = 2 };
 
 /* Pass as `device` to kvp_create for a bookkeeping-only pool: allocator,
  * block tables and decode planning run on the host with no device memory
@@ -129,6 +135,13 @@ int kvp_import(kvp_pool* pool, int layer, int seq_id, int pos0, int n, const voi
  * [len][num_kv_heads*128] (what k_ptr(layer)/v_ptr(layer) would hold). */
 int kvp_gather(kvp_pool* pool, int layer, int seq_id, void* k_rows, void* v_rows,
                void* stream);
+
+/* INT8 pools: the same, with codes [n][num_kv_heads*128] int8 (16-byte
+ * aligned) and scales [n][num_kv_heads] fp32 for K and for V. */
+int kvp_import_i8(kvp_pool* pool, int layer, int seq_id, int pos0, int n, const void* k_codes,
+                  const void* v_codes, const float* k_scales, const float* v_scales, void* stream);
+int kvp_gather_i8(kvp_pool* pool, int layer, int seq_id, void* k_codes, void* v_codes, float* k_scales,
+                  float* v_scales, void* stream);
 
 /* Prefill append: RoPE (positions pos0..pos0+n-1) and encode n new tokens'
  * k/v [n][num_kv_heads*128] fp32 into the sequence's blocks, as

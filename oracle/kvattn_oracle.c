@@ -11,6 +11,8 @@
  *   - row softmax                          worker/src/ops/op_softmax.cpp:6-16
  *   - causal GQA attention                 worker/src/ops/op_attention.cpp:9-56
  *   - KV append loop at the call site      worker/src/model/qwen2_model.cpp:180-206
+ *   - INT8 KV (planned by the reference, docs/work_division.md:72): the
+ *     scheme the device implements, restated (orc_quantize_i8 ...)
  *
  * The loops keep the reference's accumulation order exactly, so with
  * `-O2 -ffp-contract=off` on x86-64 this file reproduces the reference
@@ -242,4 +244,96 @@ void orc_lse_combine(const float* m, const float* l, const float* o, int G, int 
             out[(long)r * dim + d] = (float)(L > 0 ? acc / L : 0.0);
         }
     }
+}
+
+/* ---- INT8 KV cache ----
+ * The reference plans an FP16 -> INT8 KV compression to cut memory traffic
+ * (docs/work_division.md:72, docs/worker_arch.md:330: a QuantizedKVCache
+ * behind the same interface) but ships no implementation, so this restates
+ * the scheme the device implements:
+ *   one fp32 scale per (token, KV head) row of head_dim values,
+ *   scale = max|x| / 127, code = round-half-away(x / scale) clamped to
+ *   [-127, 127] (0 for an all-zero row or a NaN element),
+ *   dequantised value = code * scale.
+ * K is quantised after RoPE, like the 16-bit append.  Every operation is
+ * exactly rounded (fabsf, fmaxf, division, roundf), so the device's codes and
+ * scales are reproducible bit for bit. */
+void orc_quantize_i8(const float* x, int n, int8_t* q, float* scale) {
+    float amax = 0.0f;
+    for (int i = 0; i < n; ++i) amax = fmaxf(amax, fabsf(x[i]));
+    const float s = amax / 127.0f;
+    *scale = s;
+    for (int i = 0; i < n; ++i) {
+        float r = (s > 0.0f) ? roundf(x[i] / s) : 0.0f;
+        if (r != r) r = 0.0f;
+        if (r > 127.0f) r = 127.0f;
+        if (r < -127.0f) r = -127.0f;
+        q[i] = (int8_t)r;
+    }
+}
+
+/* op_attention (op_attention.cpp:9-56) over INT8 caches: the same loops with
+ * every cached value dequantised as code * scale.  kq/vq [T][kv_dim] codes,
+ * ks/vs [T][n_kv_heads] scales. */
+int orc_attention_i8(const float* q, const int8_t* kq, const float* ks, const int8_t* vq,
+                     const float* vs, float* out, int seq, int total_len, int n_heads,
+                     int n_kv_heads, int head_dim, int pos_base) {
+    const int hidden = n_heads * head_dim;
+    const int kv_dim = n_kv_heads * head_dim;
+    const float scale = 1.0f / sqrtf((float)head_dim);
+    memset(out, 0, sizeof(float) * (size_t)seq * hidden);
+    float* scores = (float*)malloc(sizeof(float) * ((size_t)seq * total_len + 1));
+    if (!scores) return -1;
+    for (int h = 0; h < n_heads; ++h) {
+        int kv_h = h / (n_heads / n_kv_heads);
+        for (int sq = 0; sq < seq; ++sq) {
+            int abs_sq = pos_base + sq;
+            for (int sk = 0; sk < total_len; ++sk) {
+                if (sk > abs_sq) {
+                    scores[(long)sq * total_len + sk] = -1e9f;
+                    continue;
+                }
+                float dot = 0.0f;
+                const float* qh = q + (long)sq * hidden + h * head_dim;
+                const int8_t* kh = kq + (long)sk * kv_dim + kv_h * head_dim;
+                const float kscale = ks[(long)sk * n_kv_heads + kv_h];
+                for (int d = 0; d < head_dim; ++d) dot += qh[d] * ((float)kh[d] * kscale);
+                scores[(long)sq * total_len + sk] = dot * scale;
+            }
+        }
+        orc_softmax(scores, seq, total_len);
+        for (int sq = 0; sq < seq; ++sq) {
+            float* out_row = out + (long)sq * hidden + h * head_dim;
+            for (int sk = 0; sk < total_len; ++sk) {
+                const int8_t* vh = vq + (long)sk * kv_dim + kv_h * head_dim;
+                const float vscale = vs[(long)sk * n_kv_heads + kv_h];
+                float w = scores[(long)sq * total_len + sk];
+                for (int d = 0; d < head_dim; ++d) out_row[d] += w * ((float)vh[d] * vscale);
+            }
+        }
+    }
+    free(scores);
+    return 0;
+}
+
+/* One layer step over INT8 caches: RoPE at pos+s, quantise and append every
+ * (token, KV head) row, attend over pos+seq. */
+int orc_layer_step_i8(float* q, float* k, const float* v, int8_t* kq, float* ks, int8_t* vq,
+                      float* vs, float* out, int seq, int pos, int n_heads, int n_kv_heads,
+                      int head_dim, float theta) {
+    const int hidden = n_heads * head_dim;
+    const int kv_dim = n_kv_heads * head_dim;
+    for (int s = 0; s < seq; ++s)
+        orc_rope(q + (long)s * hidden, k + (long)s * kv_dim, n_heads, n_kv_heads, head_dim,
+                 pos + s, theta);
+    for (int s = 0; s < seq; ++s)
+        for (int hh = 0; hh < n_kv_heads; ++hh) {
+            const long row = (long)(pos + s);
+            orc_quantize_i8(k + (long)s * kv_dim + hh * head_dim, head_dim,
+                            kq + row * kv_dim + hh * head_dim, ks + row * n_kv_heads + hh);
+            orc_quantize_i8(v + (long)s * kv_dim + hh * head_dim, head_dim,
+                            vq + row * kv_dim + hh * head_dim, vs + row * n_kv_heads + hh);
+        }
+    return orc_attention_i8(q, kq, ks, vq, vs, out, seq, pos + seq, n_heads, n_kv_heads,
+                            head_dim, pos);
 }

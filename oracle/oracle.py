@@ -27,6 +27,7 @@ F16, BF16 = 0, 1
 
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
+_i8p = np.ctypeslib.ndpointer(np.int8, flags="C_CONTIGUOUS")
 
 
 def build(ref: bool = True) -> None:
@@ -69,6 +70,12 @@ def lib() -> C.CDLL:
         L.orc_layer_step.argtypes = [_f32p, _f32p, _f32p, _u16p, _u16p, _f32p] + [C.c_int] * 5 + [
             C.c_float, C.c_int]
         L.orc_lse_combine.argtypes = [_f32p, _f32p, _f32p, C.c_int, C.c_int, C.c_int, _f32p]
+        L.orc_quantize_i8.argtypes = [_f32p, C.c_int, _i8p, _f32p]
+        L.orc_attention_i8.restype = C.c_int
+        L.orc_attention_i8.argtypes = [_f32p, _i8p, _f32p, _i8p, _f32p, _f32p] + [C.c_int] * 6
+        L.orc_layer_step_i8.restype = C.c_int
+        L.orc_layer_step_i8.argtypes = [_f32p, _f32p, _f32p, _i8p, _f32p, _i8p, _f32p, _f32p] + [C.c_int] * 5 + [
+            C.c_float]
         _lib = L
     return _lib
 
@@ -164,6 +171,36 @@ def layer_step(q, k, v, k_cache, v_cache, pos, n_heads=12, n_kv_heads=2, head_di
                               n_kv_heads, head_dim, theta, dtype)
     assert rc == 0
     return out, q, k
+
+
+def quantize_i8(x):
+    """INT8 KV codes and scales of rows [n, head_dim] (orc_quantize_i8)."""
+    x = np.ascontiguousarray(x, np.float32)
+    rows = x.reshape(-1, x.shape[-1])
+    q = np.empty(rows.shape, np.int8)
+    s = np.empty(rows.shape[0], np.float32)
+    for i in range(rows.shape[0]):
+        lib().orc_quantize_i8(rows[i], rows.shape[1], q[i], s[i:i + 1])
+    return q.reshape(x.shape), s.reshape(x.shape[:-1])
+
+
+def layer_step_i8(q, k, v, kq, ks, vq, vs, pos, n_heads=12, n_kv_heads=2, head_dim=128, theta=1e6):
+    """RoPE + INT8 append + attention of one layer over INT8 caches.
+
+    kq/vq [capacity, kv_dim] int8 and ks/vs [capacity, n_kv_heads] float32,
+    modified in place.  Returns out [seq, hidden]."""
+    q = np.array(q, np.float32, order="C")
+    k = np.array(k, np.float32, order="C")
+    v = np.ascontiguousarray(v, np.float32)
+    seq = q.shape[0]
+    out = np.empty((seq, n_heads * head_dim), np.float32)
+    for a in (kq, ks, vq, vs):
+        assert a.flags.c_contiguous
+    rc = lib().orc_layer_step_i8(q.reshape(-1), k.reshape(-1), v.reshape(-1), kq.reshape(-1), ks.reshape(-1),
+                                 vq.reshape(-1), vs.reshape(-1), out.reshape(-1), seq, pos, n_heads, n_kv_heads,
+                                 head_dim, theta)
+    assert rc == 0
+    return out
 
 
 def lse_combine(m, l, o):

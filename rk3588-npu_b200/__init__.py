@@ -21,7 +21,7 @@ LIB_PATH = os.path.join(HERE, "lib", "libkvattn.so")
 
 KV_OK, KV_ERR_INVAL, KV_ERR_OOM, KV_ERR_BADSEQ, KV_ERR_CUDA, KV_ERR_RANGE, KV_ERR_STATE, \
     KV_ERR_TIMEOUT = range(8)
-KV_F16, KV_BF16 = 0, 1
+KV_F16, KV_BF16, KV_I8 = 0, 1, 2
 KVP_HOST_ONLY = -1
 HEAD_DIM = 128
 BLOCK_TOKENS = 16
@@ -51,6 +51,8 @@ _SIGS = {
     "kvp_seq_blocks": [_vp, C.c_int, _ip, C.c_int, _ip],
     "kvp_import": [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp],
     "kvp_gather": [_vp, C.c_int, C.c_int, _vp, _vp, _vp],
+    "kvp_import_i8": [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp, _vp, _vp],
+    "kvp_gather_i8": [_vp, C.c_int, C.c_int, _vp, _vp, _vp, _vp, _vp],
     "kv_append_chunk": [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp],
     "attn_prefill": [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp],
     "attn_prefill_mma": [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp],
@@ -249,6 +251,24 @@ class Pool:
         v = torch.empty((n, self.kv_dim), dtype=torch.int16, device=dev)
         call("kvp_gather", self.h, layer, seq, _ptr(k), _ptr(v), _stream(stream))
         return k, v
+
+    def import_i8(self, layer, seq, pos0, k_codes, v_codes, k_scales, v_scales, stream=None) -> None:
+        """INT8 pools: codes [n, kv_dim] int8, scales [n, kv_heads] fp32 (device tensors)."""
+        n = k_codes.shape[0]
+        call("kvp_import_i8", self.h, layer, seq, pos0, n, _ptr(k_codes), _ptr(v_codes), _ptr(k_scales),
+             _ptr(v_scales), _stream(stream))
+
+    def gather_i8(self, layer, seq, stream=None):
+        """INT8 pools: (k_codes, v_codes, k_scales, v_scales) of positions [0, len)."""
+        import torch
+        n = self.cur_pos(seq)
+        dev = torch.device("cuda", self.device)
+        kc = torch.empty((n, self.kv_dim), dtype=torch.int8, device=dev)
+        vc = torch.empty((n, self.kv_dim), dtype=torch.int8, device=dev)
+        ks = torch.empty((n, self.kv_dim // HEAD_DIM), dtype=torch.float32, device=dev)
+        vs = torch.empty((n, self.kv_dim // HEAD_DIM), dtype=torch.float32, device=dev)
+        call("kvp_gather_i8", self.h, layer, seq, _ptr(kc), _ptr(vc), _ptr(ks), _ptr(vs), _stream(stream))
+        return kc, vc, ks, vs
 
     def append_chunk(self, layer, seq, pos0, k, v, stream=None) -> None:
         n = k.shape[0]

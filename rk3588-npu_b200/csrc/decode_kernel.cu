@@ -53,13 +53,36 @@ constexpr int kConsumerWarps = 4;
 static_assert(kStages % kConsumerWarps == 0, "each ring stage must belong to one consumer warp");
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kStageBytes = 2 * kTileBytes;  // K tile then V tile
+
+// Shared-memory shapes per cache type.  16-bit caches: a ring stage holds the
+// K and V tiles as they lie in HBM (the swizzled mma layout).  INT8 caches: a
+// stage holds the two compact tiles (codes + scales); each consumer warp
+// expands the block it owns into its own 16-bit tile pair (`scratch`).
+template <int DT>
+struct StageCfg {
+    static constexpr int tile = kTileBytes;
+    static constexpr int stage = 2 * kTileBytes;
+    static constexpr int scratch = 16;  // unused
+};
+template <>
+struct StageCfg<2> {
+    static constexpr int tile = kTileBytesI8;
+    static constexpr int stage = 2 * kTileBytesI8;
+    static constexpr int scratch = 2 * kTileBytes;
+};
+// The tensor-core operand type: fp16 for fp16 and int8 caches (int8 codes are
+// exact in fp16), bf16 for bf16 caches.
+template <int DT>
+__host__ __device__ constexpr int mma_type() { return DT == 1 ? 1 : 0; }
 constexpr int kMergeStride = 132;            // floats per (warp, head) row, padded
 constexpr long long kWaitLimit = 4000000000LL;  // SM clocks (~2 s) before a wait gives up
 constexpr int kQPre = 4;                     // pieces whose q fragments are prepared up front
 constexpr int kEarlyLanes = 2;               // ring stages issued before the plan header load
 
+template <int DT>
 struct Smem {
-    alignas(1024) uint8_t stage[kStages][kStageBytes];
+    alignas(1024) uint8_t stage[kStages][StageCfg<DT>::stage];
+    alignas(1024) uint8_t scratch[kConsumerWarps][StageCfg<DT>::scratch];
     float merge_o[kConsumerWarps][kMaxGroup][kMergeStride];
     float merge_m[kConsumerWarps][kMaxGroup];
     float merge_l[kConsumerWarps][kMaxGroup];
@@ -86,7 +109,8 @@ __device__ __forceinline__ void report(const PoolView& pv, int code, int item, i
 }
 
 // A bounded wait gave up: record where (status[3..16]) for the host to read.
-__device__ __forceinline__ void flag_timeout(const PoolView& pv, Smem& sm, int item, int role,
+template <class SmemT>
+__device__ __forceinline__ void flag_timeout(const PoolView& pv, SmemT& sm, int item, int role,
                                              uint32_t k) {
     if (atomicCAS(pv.status, 0, 7 /* KV_ERR_TIMEOUT */) == 0) {
         const int s = k % kStages;
@@ -152,8 +176,8 @@ __device__ __forceinline__ void load_q_frags(const PoolView& pv, const float* q,
             float lo0, hi0, lo1, hi1;
             rope_pair(a.x, b.x, t.x, t.y, lo0, hi0);
             rope_pair(a.y, b.y, t.z, t.w, lo1, hi1);
-            split_pair<DT>(lo0 * qscale, lo1 * qscale, qh[kk][r], ql[kk][r]);
-            split_pair<DT>(hi0 * qscale, hi1 * qscale, qh[kk + 4][r], ql[kk + 4][r]);
+            split_pair<mma_type<DT>()>(lo0 * qscale, lo1 * qscale, qh[kk][r], ql[kk][r]);
+            split_pair<mma_type<DT>()>(hi0 * qscale, hi1 * qscale, qh[kk + 4][r], ql[kk + 4][r]);
         }
     }
 }
@@ -194,13 +218,78 @@ __device__ __forceinline__ void write_new_row(const PoolView& pv, int layer, int
     *reinterpret_cast<uint32_t*>(sV + o_hi) = vhi;
 }
 
+// INT8 cache: the new token's k (rotated) and v rows quantised by the warp
+// (quant_row_warp), codes and scales stored to the pool tile (the append)
+// and the codes, as fp16, into the warp's expanded tiles; ks / vs receive the
+// row's scales.
+__device__ __forceinline__ void write_new_row_i8(const PoolView& pv, int layer, int blk, int head, int t,
+                                                 const float* k_new, const float* v_new, int row, int rope_pos,
+                                                 uint8_t* sK, uint8_t* sV, int lane, float& ks, float& vs) {
+    const size_t kvw = (size_t)pv.kv_heads * kHeadDim;
+    const float* kr = k_new + (size_t)row * kvw + (size_t)head * kHeadDim;
+    const float* vr = v_new + (size_t)row * kvw + (size_t)head * kHeadDim;
+    const float* cs = reinterpret_cast<const float*>(pv.rope + (size_t)rope_pos * (kHeadDim / 2));
+    const int i = 2 * lane;  // dims i, i+1 and their partners i+64, i+65
+    const float2 a = *reinterpret_cast<const float2*>(kr + i);
+    const float2 b = *reinterpret_cast<const float2*>(kr + i + 64);
+    const float4 cc = *reinterpret_cast<const float4*>(cs + 2 * i);
+    float kx[4], vx[4];
+    rope_pair(a.x, b.x, cc.x, cc.y, kx[0], kx[2]);
+    rope_pair(a.y, b.y, cc.z, cc.w, kx[1], kx[3]);
+    const float2 va = *reinterpret_cast<const float2*>(vr + i);
+    const float2 vb = *reinterpret_cast<const float2*>(vr + i + 64);
+    vx[0] = va.x;
+    vx[1] = va.y;
+    vx[2] = vb.x;
+    vx[3] = vb.y;
+    int8_t kc[4], vc[4];
+    ks = quant_row_warp(kx, kc);
+    vs = quant_row_warp(vx, vc);
+    const size_t tile = (size_t)layer * pv.layer_bytes + ((size_t)blk * pv.kv_heads + head) * kTileBytesI8;
+    uint8_t* kt = pv.k + tile;
+    uint8_t* vt = pv.v + tile;
+    *reinterpret_cast<char2*>(kt + t * kHeadDim + i) = make_char2(kc[0], kc[1]);
+    *reinterpret_cast<char2*>(kt + t * kHeadDim + i + 64) = make_char2(kc[2], kc[3]);
+    *reinterpret_cast<char2*>(vt + t * kHeadDim + i) = make_char2(vc[0], vc[1]);
+    *reinterpret_cast<char2*>(vt + t * kHeadDim + i + 64) = make_char2(vc[2], vc[3]);
+    if (lane == 0) {
+        reinterpret_cast<float*>(kt + kBlockTokens * kHeadDim)[t] = ks;
+        reinterpret_cast<float*>(vt + kBlockTokens * kHeadDim)[t] = vs;
+    }
+    *reinterpret_cast<uint32_t*>(sK + tile_offset(t, i)) = codes_to_half2(kc[0], kc[1]);
+    *reinterpret_cast<uint32_t*>(sK + tile_offset(t, i + 64)) = codes_to_half2(kc[2], kc[3]);
+    *reinterpret_cast<uint32_t*>(sV + tile_offset(t, i)) = codes_to_half2(vc[0], vc[1]);
+    *reinterpret_cast<uint32_t*>(sV + tile_offset(t, i + 64)) = codes_to_half2(vc[2], vc[3]);
+}
+
+// INT8 cache: expand a staged compact tile (codes row-major + scales) into
+// the 16-bit swizzled layout the mma path reads; lane l converts 16-byte
+// output chunks l, l+32, ... (row x / 16, 8 dims x % 16).
+__device__ __forceinline__ void expand_tile_i8(const uint8_t* src, uint8_t* dst, int lane) {
+#pragma unroll 4
+    for (int x = lane; x < kBlockTokens * 16; x += 32) {
+        const int t = x >> 4, ch = x & 15;
+        const uint2 raw = *reinterpret_cast<const uint2*>(src + t * kHeadDim + ch * 8);
+        const int8_t* c = reinterpret_cast<const int8_t*>(&raw);
+        *reinterpret_cast<uint4*>(dst + tile_offset(t, ch * 8)) =
+            make_uint4(codes_to_half2(c[0], c[1]), codes_to_half2(c[2], c[3]), codes_to_half2(c[4], c[5]),
+                       codes_to_half2(c[6], c[7]));
+    }
+}
+
 // One 16-token block: scores, online softmax update, P*V accumulate.
 // `valid` tokens (rows 0..valid-1) take part; the rest are masked.
+// For an INT8 cache (DT 2) the staged tiles hold the codes; ks / vs are the
+// K / V scales of token rows g and g + 8: the scores are scaled by ks and the
+// softmax weights by vs on their way into P*V (the sums keep the unscaled
+// weights), which is attention over code * scale exactly up to fp32 rounding.
 template <int DT>
 __device__ __forceinline__ void consume_block(uint32_t sK, uint32_t sV, int valid, int lane,
                                               const uint32_t (&qh)[8][2],
                                               const uint32_t (&ql)[8][2], float (&m2)[2],
-                                              float (&lsum)[2], float (&o)[8][4]) {
+                                              float (&lsum)[2], float (&o)[8][4], const float (&ks)[2],
+                                              const float (&vs_in)[2]) {
+    const float vs[2] = {DT == 2 ? vs_in[0] : 1.f, DT == 2 ? vs_in[1] : 1.f};
     const int g = lane >> 2;
     const int mi = lane >> 3, r = lane & 7;
     // ---- S^T[16 tokens][8 heads] = K[16][128] * Qs^T ----
@@ -215,13 +304,19 @@ __device__ __forceinline__ void consume_block(uint32_t sK, uint32_t sV, int vali
             const uint32_t addr = rowb + (uint32_t)(cidx >> 3) * 2048u + (uint32_t)(((cidx & 7) ^ r) << 4);
             uint32_t a0, a1, a2, a3;
             ldsm_x4(addr, a0, a1, a2, a3);
-            mma16816<DT>(sa[kk & 1], a0, a1, a2, a3, qh[kk][0], qh[kk][1]);
-            mma16816<DT>(sb[kk & 1], a0, a1, a2, a3, ql[kk][0], ql[kk][1]);
+            mma16816<mma_type<DT>()>(sa[kk & 1], a0, a1, a2, a3, qh[kk][0], qh[kk][1]);
+            mma16816<mma_type<DT>()>(sb[kk & 1], a0, a1, a2, a3, ql[kk][0], ql[kk][1]);
         }
     }
     float s[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) s[e] = (sa[0][e] + sa[1][e]) + (sb[0][e] + sb[1][e]);
+    if (DT == 2) {
+        s[0] *= ks[0];
+        s[1] *= ks[0];
+        s[2] *= ks[1];
+        s[3] *= ks[1];
+    }
     if (g >= valid) s[0] = s[1] = -INFINITY;
     if (g + 8 >= valid) s[2] = s[3] = -INFINITY;
     // ---- online softmax, per head column (2c, 2c+1) ----
@@ -250,8 +345,8 @@ __device__ __forceinline__ void consume_block(uint32_t sK, uint32_t sV, int vali
     }
     // ---- P^T as B fragments (k = tokens, n = heads) ----
     uint32_t h01, l01, h23, l23;
-    split_pair<DT>(p0, p1, h01, l01);
-    split_pair<DT>(p2, p3, h23, l23);
+    split_pair<mma_type<DT>()>(p0 * vs[0], p1 * vs[0], h01, l01);
+    split_pair<mma_type<DT>()>(p2 * vs[1], p3 * vs[1], h23, l23);
     const uint32_t bh0 = movmatrix_t(h01), bh1 = movmatrix_t(h23);
     const uint32_t bl0 = movmatrix_t(l01), bl1 = movmatrix_t(l23);
     // ---- O^T[128 dims][8 heads] += V^T * P^T ----
@@ -264,8 +359,8 @@ __device__ __forceinline__ void consume_block(uint32_t sK, uint32_t sV, int vali
             const uint32_t addr = rowb + (uint32_t)(cidx >> 3) * 2048u + (uint32_t)(((cidx & 7) ^ r) << 4);
             uint32_t a0, a1, a2, a3;
             ldsm_x4_t(addr, a0, a1, a2, a3);
-            mma16816<DT>(o[mt], a0, a1, a2, a3, bh0, bh1);
-            mma16816<DT>(o[mt], a0, a1, a2, a3, bl0, bl1);
+            mma16816<mma_type<DT>()>(o[mt], a0, a1, a2, a3, bh0, bh1);
+            mma16816<mma_type<DT>()>(o[mt], a0, a1, a2, a3, bl0, bl1);
         }
     }
 }
@@ -278,7 +373,8 @@ __global__ void __launch_bounds__(kThreads, 2)
                   const float* __restrict__ k_new, const float* __restrict__ v_new,
                   float* __restrict__ out, float* __restrict__ m_out, float* __restrict__ l_out) {
     extern __shared__ uint8_t smem_raw[];
-    Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Smem<DT>& sm = *reinterpret_cast<Smem<DT>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    constexpr int TB = StageCfg<DT>::tile;  // bytes of one K or V tile in HBM and in a stage
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // The combine kernel may be scheduled now; it waits for this grid.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -299,10 +395,10 @@ __global__ void __launch_bounds__(kThreads, 2)
             report(pv, 5, blockIdx.x, 200 + f);  // never read outside the pool
             mbar_arrive(&sm.full[s]);
         } else {
-            const size_t off = (size_t)layer * pv.layer_bytes + (size_t)tile * kTileBytes;
-            mbar_arrive_expect_tx(&sm.full[s], kStageBytes);
-            bulk_g2s_hint(sm.stage[s], pv.k + off, kTileBytes, &sm.full[s], policy);
-            bulk_g2s_hint(sm.stage[s] + kTileBytes, pv.v + off, kTileBytes, &sm.full[s], policy);
+            const size_t off = (size_t)layer * pv.layer_bytes + (size_t)tile * TB;
+            mbar_arrive_expect_tx(&sm.full[s], 2 * TB);
+            bulk_g2s_hint(sm.stage[s], pv.k + off, TB, &sm.full[s], policy);
+            bulk_g2s_hint(sm.stage[s] + TB, pv.v + off, TB, &sm.full[s], policy);
         }
     };
     // Only the first kEarlyLanes stages go out here: their tiles then sit at
@@ -477,14 +573,55 @@ __global__ void __launch_bounds__(kThreads, 2)
                 dead = true;
             }
             if (dead) continue;
-            uint8_t* sK = sm.stage[s];
-            uint8_t* sV = sm.stage[s] + kTileBytes;
             const int idx = wi.b0 + b;
             const int valid = min(kBlockTokens, wi.kv_len - idx * kBlockTokens);
             const bool newblk = wi.append && idx == last_blk;
-            if (newblk)
-                write_new_row<DT>(pv, layer, wi.new_block, wi.head, valid - 1, k_new, v_new, wi.slot,
-                                  wi.rope_pos, sK, sV, lane);
+            uint8_t* sK;
+            uint8_t* sV;
+            float ks[2] = {1.f, 1.f}, vs[2] = {1.f, 1.f};  // INT8: scales of token rows g, g + 8
+            if (DT == 2) {
+                // Expand the compact tiles into this warp's 16-bit pair, keep
+                // the scales of rows g and g + 8, and free the stage at once.
+                sK = sm.scratch[warp];
+                sV = sK + kTileBytes;
+                const uint8_t* qK = sm.stage[s];
+                const uint8_t* qV = qK + TB;
+                __syncwarp();  // this warp's previous block has been read
+                expand_tile_i8(qK, sK, lane);
+                expand_tile_i8(qV, sV, lane);
+                const float* kss = reinterpret_cast<const float*>(qK + kBlockTokens * kHeadDim);
+                const float* vss = reinterpret_cast<const float*>(qV + kBlockTokens * kHeadDim);
+                ks[0] = kss[g];
+                ks[1] = kss[g + 8];
+                vs[0] = vss[g];
+                vs[1] = vss[g + 8];
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&sm.empty[s]);
+                    *reinterpret_cast<volatile int*>(&sm.cons_done[warp]) = (int)k + 1;
+                }
+            } else {
+                sK = sm.stage[s];
+                sV = sm.stage[s] + kTileBytes;
+            }
+            if (newblk) {
+                if (DT == 2) {
+                    float nks, nvs;
+                    write_new_row_i8(pv, layer, wi.new_block, wi.head, valid - 1, k_new, v_new, wi.slot, wi.rope_pos,
+                                     sK, sV, lane, nks, nvs);
+                    if (g == valid - 1) {
+                        ks[0] = nks;
+                        vs[0] = nvs;
+                    }
+                    if (g + 8 == valid - 1) {
+                        ks[1] = nks;
+                        vs[1] = nvs;
+                    }
+                } else {
+                    write_new_row<DT>(pv, layer, wi.new_block, wi.head, valid - 1, k_new, v_new, wi.slot,
+                                      wi.rope_pos, sK, sV, lane);
+                }
+            }
             if (valid < kBlockTokens) {
                 // Rows past the end may hold anything (stale tiles, inf):
                 // zero them in V so masked weights (exactly 0) stay 0.
@@ -493,16 +630,22 @@ __global__ void __launch_bounds__(kThreads, 2)
                     *reinterpret_cast<uint4*>(sV + ((ch >> 3) * 16 + t) * 128 + (ch & 7) * 16) =
                         make_uint4(0u, 0u, 0u, 0u);
                 }
+                if (DT == 2) {  // and their scales (stale words may be inf or NaN)
+                    if (g >= valid) vs[0] = 0.f;
+                    if (g + 8 >= valid) vs[1] = 0.f;
+                }
             }
             __syncwarp();
-            consume_block<DT>(smem_u32(sK), smem_u32(sV), valid, lane, qh, ql, m2, lsum, o);
-            // Generic-proxy writes to the tile must be ordered before the
-            // next bulk copy (async proxy) overwrites it.
-            if (valid < kBlockTokens || newblk) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&sm.empty[s]);
-                *reinterpret_cast<volatile int*>(&sm.cons_done[warp]) = (int)k + 1;
+            consume_block<DT>(smem_u32(sK), smem_u32(sV), valid, lane, qh, ql, m2, lsum, o, ks, vs);
+            if (DT != 2) {
+                // Generic-proxy writes to the tile must be ordered before the
+                // next bulk copy (async proxy) overwrites it.
+                if (valid < kBlockTokens || newblk) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&sm.empty[s]);
+                    *reinterpret_cast<volatile int*>(&sm.cons_done[warp]) = (int)k + 1;
+                }
             }
         }
 
@@ -655,56 +798,55 @@ __global__ void __launch_bounds__(kCombineWarps * 32)
     }
 }
 
-cudaError_t decode_occupancy(int* ctas_per_sm) {
-    const int smem = (int)sizeof(Smem) + 1024;
-    cudaError_t e = cudaFuncSetAttribute(decode_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+template <int DT>
+static cudaError_t decode_occupancy_t(int* ctas_per_sm) {
+    const int smem = (int)sizeof(Smem<DT>) + 1024;
+    cudaError_t e = cudaFuncSetAttribute(decode_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, decode_kernel<0>, kThreads, smem);
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, decode_kernel<DT>, kThreads, smem);
+}
+
+cudaError_t decode_occupancy(int dtype, int* ctas_per_sm) {
+    return dtype == 0 ? decode_occupancy_t<0>(ctas_per_sm)
+                      : dtype == 1 ? decode_occupancy_t<1>(ctas_per_sm) : decode_occupancy_t<2>(ctas_per_sm);
 }
 
 cudaError_t launch_decode(const PoolView& pv, const PlanView& plan, int nsplits, int max_pieces,
                           int layer, const float* q, const float* k_new, const float* v_new,
                           float* out, float* m_out, float* l_out, int grid, bool pdl, cudaStream_t st) {
-    const int smem = (int)sizeof(Smem) + 1024;
     if (grid < 1) grid = 1;
-    cudaError_t e;
-    if (pdl) {
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)grid);
-        cfg.blockDim = dim3(kThreads);
-        cfg.dynamicSmemBytes = (size_t)smem;
-        cfg.stream = st;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        e = pv.dtype == 0 ? cudaLaunchKernelEx(&cfg, decode_kernel<0>, pv, plan, layer, q, k_new, v_new, out, m_out, l_out)
-                          : cudaLaunchKernelEx(&cfg, decode_kernel<1>, pv, plan, layer, q, k_new, v_new, out, m_out, l_out);
-        e = counted(e);
-    } else {
-        if (pv.dtype == 0)
-            decode_kernel<0><<<grid, kThreads, smem, st>>>(pv, plan, layer, q, k_new, v_new, out, m_out, l_out);
-        else
-            decode_kernel<1><<<grid, kThreads, smem, st>>>(pv, plan, layer, q, k_new, v_new, out, m_out, l_out);
-        e = counted(cudaGetLastError());
-    }
-    if (e != cudaSuccess || nsplits == 0) return e;
-    const bool wide = max_pieces > 64;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(nsplits * pv.group));
-    cfg.blockDim = dim3((wide ? 16 : 4) * 32);
-    cfg.dynamicSmemBytes = 0;
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kThreads);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (wide) return counted(cudaLaunchKernelEx(&cfg, combine_kernel<16>, pv, plan, nsplits, out, m_out, l_out));
-    return counted(cudaLaunchKernelEx(&cfg, combine_kernel<4>, pv, plan, nsplits, out, m_out, l_out));
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaError_t e;
+    if (pv.dtype == 0) {
+        cfg.dynamicSmemBytes = sizeof(Smem<0>) + 1024;
+        e = cudaLaunchKernelEx(&cfg, decode_kernel<0>, pv, plan, layer, q, k_new, v_new, out, m_out, l_out);
+    } else if (pv.dtype == 1) {
+        cfg.dynamicSmemBytes = sizeof(Smem<1>) + 1024;
+        e = cudaLaunchKernelEx(&cfg, decode_kernel<1>, pv, plan, layer, q, k_new, v_new, out, m_out, l_out);
+    } else {
+        cfg.dynamicSmemBytes = sizeof(Smem<2>) + 1024;
+        e = cudaLaunchKernelEx(&cfg, decode_kernel<2>, pv, plan, layer, q, k_new, v_new, out, m_out, l_out);
+    }
+    e = counted(e);
+    if (e != cudaSuccess || nsplits == 0) return e;
+    const bool wide = max_pieces > 64;
+    cudaLaunchConfig_t ccfg = {};
+    ccfg.gridDim = dim3((unsigned)(nsplits * pv.group));
+    ccfg.blockDim = dim3((wide ? 16 : 4) * 32);
+    ccfg.dynamicSmemBytes = 0;
+    ccfg.stream = st;
+    ccfg.attrs = attr;  // programmatic dependent of the decode grid
+    ccfg.numAttrs = 1;
+    if (wide) return counted(cudaLaunchKernelEx(&ccfg, combine_kernel<16>, pv, plan, nsplits, out, m_out, l_out));
+    return counted(cudaLaunchKernelEx(&ccfg, combine_kernel<4>, pv, plan, nsplits, out, m_out, l_out));
 }
 
 }  // namespace kvattn

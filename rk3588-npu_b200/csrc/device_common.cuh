@@ -32,6 +32,32 @@ __device__ __forceinline__ uint16_t enc_trunc(float f) {
     return DT == 0 ? enc_f16_trunc(f) : enc_bf16_trunc(f);
 }
 
+// INT8 KV: quantise one 128-value row held by a warp, lane l holding dims
+// 2l, 2l+1, 2l+64, 2l+65 in x[0..3]: scale = max|x| / 127, code =
+// round-half-away(x / scale) clamped to [-127, 127] (0 for an all-zero row or
+// a NaN).  Every step is exactly rounded (the max in any order is exact), so
+// the codes and the scale equal a sequential CPU restatement bit for bit.
+__device__ __forceinline__ float quant_row_warp(const float (&x)[4], int8_t (&code)[4]) {
+    float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float s = __fdiv_rn(amax, 127.0f);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        float r = s > 0.0f ? roundf(__fdiv_rn(x[j], s)) : 0.0f;
+        if (r != r) r = 0.0f;
+        r = fminf(fmaxf(r, -127.0f), 127.0f);
+        code[j] = (int8_t)(int)r;
+    }
+    return s;
+}
+
+// Two int8 codes as one fp16 pair (exact: |code| <= 127).
+__device__ __forceinline__ uint32_t codes_to_half2(int8_t a, int8_t b) {
+    const __half2 h = __floats2half2_rn((float)a, (float)b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 // Decoders for the gather-free paths (prefill checks etc.).
 __device__ __forceinline__ float dec_bf16(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
 

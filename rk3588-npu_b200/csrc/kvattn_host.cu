@@ -324,7 +324,8 @@ int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, in
         return fail(KV_ERR_INVAL, "sizes must be positive");
     if (num_q_heads % num_kv_heads != 0 || num_q_heads / num_kv_heads > kMaxGroup)
         return fail(KV_ERR_INVAL, "num_q_heads/num_kv_heads must be an integer <= %d", kMaxGroup);
-    if (dtype != KV_F16 && dtype != KV_BF16) return fail(KV_ERR_INVAL, "dtype must be KV_F16 or KV_BF16");
+    if (dtype != KV_F16 && dtype != KV_BF16 && dtype != KV_I8)
+        return fail(KV_ERR_INVAL, "dtype must be KV_F16, KV_BF16 or KV_I8");
     if (!(rope_theta > 0.f)) return fail(KV_ERR_INVAL, "rope_theta must be > 0");
     const bool host_only = (device == KVP_HOST_ONLY);
     if (!host_only) {
@@ -390,11 +391,12 @@ int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, in
         return KV_OK;
     }
     KV_CUDA_B(cudaDeviceGetAttribute(&p->num_sms, cudaDevAttrMultiProcessorCount, device));
-    KV_CUDA_B(decode_occupancy(&p->occupancy));
+    KV_CUDA_B(decode_occupancy(dtype, &p->occupancy));
     if (p->occupancy < 1) p->occupancy = 1;
     p->max_items = 2L * max_seqs * num_kv_heads + (long)p->num_sms * p->occupancy + 64;
 
-    const size_t layer_bytes = (size_t)num_blocks * num_kv_heads * kTileBytes;
+    const int tile_bytes = dtype == KV_I8 ? kTileBytesI8 : kTileBytes;
+    const size_t layer_bytes = (size_t)num_blocks * num_kv_heads * tile_bytes;
     KV_CUDA_B(cudaMalloc(&p->d_k, layer_bytes * num_layers));
     KV_CUDA_B(cudaMalloc(&p->d_v, layer_bytes * num_layers));
     KV_CUDA_B(cudaMemset(p->d_k, 0, layer_bytes * num_layers));
@@ -444,6 +446,7 @@ int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, in
     pv.max_items = (int)p->max_items;
     pv.dtype = dtype;
     pv.layer_bytes = layer_bytes;
+    pv.tile_bytes = tile_bytes;
     *out = p;
     return KV_OK;
 }
@@ -631,6 +634,7 @@ int kvp_import(kvp_pool* p, int layer, int seq, int pos0, int n, const void* k_r
     if (n < 0 || pos0 < 0) return fail(KV_ERR_INVAL, "negative position/count");
     if ((long)pos0 + n > (long)p->seqs[seq].blocks.size() * kBlockTokens)
         return fail(KV_ERR_RANGE, "positions [%d, %d) exceed reserved blocks", pos0, pos0 + n);
+    if (p->dtype == KV_I8) return fail(KV_ERR_INVAL, "INT8 pool: use kvp_import_i8");
     if (n == 0) return KV_OK;
     if (!k_rows || !v_rows || ((uintptr_t)k_rows & 15) || ((uintptr_t)v_rows & 15))
         return fail(KV_ERR_INVAL, "row pointers must be non-NULL and 16-byte aligned");
@@ -642,6 +646,32 @@ int kvp_import(kvp_pool* p, int layer, int seq, int pos0, int n, const void* k_r
     return KV_OK;
 }
 
+int kvp_import_i8(kvp_pool* p, int layer, int seq, int pos0, int n, const void* k_codes, const void* v_codes,
+                  const float* k_scales, const float* v_scales, void* stream) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    std::lock_guard<std::mutex> lk(p->mu);
+    int rc = check_seq(p, seq);
+    if (rc) return rc;
+    rc = require_device(p);
+    if (rc) return rc;
+    if (p->dtype != KV_I8) return fail(KV_ERR_INVAL, "not an INT8 pool");
+    if (layer < 0 || layer >= p->layers) return fail(KV_ERR_INVAL, "layer %d out of range", layer);
+    if (n < 0 || pos0 < 0) return fail(KV_ERR_INVAL, "negative position/count");
+    if ((long)pos0 + n > (long)p->seqs[seq].blocks.size() * kBlockTokens)
+        return fail(KV_ERR_RANGE, "positions [%d, %d) exceed reserved blocks", pos0, pos0 + n);
+    if (n == 0) return KV_OK;
+    if (!k_codes || !v_codes || !k_scales || !v_scales || ((uintptr_t)k_codes & 15) || ((uintptr_t)v_codes & 15) ||
+        ((uintptr_t)k_scales & 3) || ((uintptr_t)v_scales & 3))
+        return fail(KV_ERR_INVAL, "code pointers must be 16-byte aligned, scale pointers 4-byte aligned");
+    DeviceGuard dg(p->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    rc = sync_table(p, st);
+    if (rc) return rc;
+    KV_CUDA(launch_import_i8(p->pv, layer, seq, pos0, n, (const int8_t*)k_codes, (const int8_t*)v_codes, k_scales,
+                             v_scales, st));
+    return KV_OK;
+}
+
 int kvp_gather(kvp_pool* p, int layer, int seq, void* k_rows, void* v_rows, void* stream) {
     if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
     std::lock_guard<std::mutex> lk(p->mu);
@@ -650,6 +680,7 @@ int kvp_gather(kvp_pool* p, int layer, int seq, void* k_rows, void* v_rows, void
     rc = require_device(p);
     if (rc) return rc;
     if (layer < 0 || layer >= p->layers) return fail(KV_ERR_INVAL, "layer %d out of range", layer);
+    if (p->dtype == KV_I8) return fail(KV_ERR_INVAL, "INT8 pool: use kvp_gather_i8");
     const int len = p->seqs[seq].len;
     if (len == 0) return KV_OK;
     if (!k_rows || !v_rows || ((uintptr_t)k_rows & 15) || ((uintptr_t)v_rows & 15))
@@ -659,6 +690,29 @@ int kvp_gather(kvp_pool* p, int layer, int seq, void* k_rows, void* v_rows, void
     rc = sync_table(p, st);
     if (rc) return rc;
     KV_CUDA(launch_gather(p->pv, layer, seq, len, (uint16_t*)k_rows, (uint16_t*)v_rows, st));
+    return KV_OK;
+}
+
+int kvp_gather_i8(kvp_pool* p, int layer, int seq, void* k_codes, void* v_codes, float* k_scales, float* v_scales,
+                  void* stream) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    std::lock_guard<std::mutex> lk(p->mu);
+    int rc = check_seq(p, seq);
+    if (rc) return rc;
+    rc = require_device(p);
+    if (rc) return rc;
+    if (p->dtype != KV_I8) return fail(KV_ERR_INVAL, "not an INT8 pool");
+    if (layer < 0 || layer >= p->layers) return fail(KV_ERR_INVAL, "layer %d out of range", layer);
+    const int len = p->seqs[seq].len;
+    if (len == 0) return KV_OK;
+    if (!k_codes || !v_codes || !k_scales || !v_scales || ((uintptr_t)k_codes & 15) || ((uintptr_t)v_codes & 15) ||
+        ((uintptr_t)k_scales & 3) || ((uintptr_t)v_scales & 3))
+        return fail(KV_ERR_INVAL, "code pointers must be 16-byte aligned, scale pointers 4-byte aligned");
+    DeviceGuard dg(p->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    rc = sync_table(p, st);
+    if (rc) return rc;
+    KV_CUDA(launch_gather_i8(p->pv, layer, seq, len, (int8_t*)k_codes, (int8_t*)v_codes, k_scales, v_scales, st));
     return KV_OK;
 }
 
@@ -707,6 +761,7 @@ int prefill_checks(kvp_pool* p, int layer, int seq, int pos0, int n, const float
     if (rc) return rc;
     rc = require_device(p);
     if (rc) return rc;
+    if (p->dtype == KV_I8) return fail(KV_ERR_INVAL, "prefill attention reads 16-bit caches; INT8 pools decode only");
     if (layer < 0 || layer >= p->layers) return fail(KV_ERR_INVAL, "layer %d out of range", layer);
     if (n < 0 || pos0 < 0) return fail(KV_ERR_INVAL, "negative position/count");
     if ((long)pos0 + n > p->max_seq_len)

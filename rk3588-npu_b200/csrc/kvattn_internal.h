@@ -11,6 +11,9 @@ namespace kvattn {
 constexpr int kHeadDim = 128;          // dims per head (the only supported value)
 constexpr int kBlockTokens = 16;       // token rows per block
 constexpr int kTileBytes = kBlockTokens * kHeadDim * 2;  // one (block, kv head) tile: 4 KiB
+// INT8 pools: a (block, kv head) tile is 16 rows x 128 int8 codes (row t at
+// byte 128 t, dim d at byte d) followed by the 16 rows' fp32 scales.
+constexpr int kTileBytesI8 = kBlockTokens * kHeadDim + kBlockTokens * 4;  // 2112 bytes
 constexpr int kMaxGroup = 8;           // query heads per KV head handled by one MMA tile
 constexpr int kPartialFloats = kMaxGroup * (kHeadDim + 2);  // m[8], l[8], o[8][128]
 constexpr int kMaxCtaItems = 64;       // pieces per decode CTA (the planner never assigns more)
@@ -117,8 +120,9 @@ struct PoolView {
     int max_seq_len;
     int max_seqs;
     int max_items;
-    int dtype;               // 0 f16, 1 bf16
-    size_t layer_bytes;      // num_blocks * kv_heads * kTileBytes
+    int dtype;               // 0 f16, 1 bf16, 2 int8 codes + per-row fp32 scales
+    int tile_bytes;          // kTileBytes, or kTileBytesI8 for int8
+    size_t layer_bytes;      // num_blocks * kv_heads * tile_bytes
 };
 
 // Plan as the decode kernel sees it (device pointers into one upload).
@@ -136,13 +140,17 @@ struct PlanView {
 cudaError_t launch_decode(const PoolView& pv, const PlanView& plan, int nsplits, int max_pieces,
                           int layer, const float* q, const float* k_new, const float* v_new,
                           float* out, float* m_out, float* l_out, int grid, bool pdl, cudaStream_t st);
-cudaError_t decode_occupancy(int* ctas_per_sm);
+cudaError_t decode_occupancy(int dtype, int* ctas_per_sm);
 cudaError_t launch_import(const PoolView& pv, int layer, int seq, int pos0, int n,
                           const uint16_t* k_rows, const uint16_t* v_rows, cudaStream_t st);
 cudaError_t launch_gather(const PoolView& pv, int layer, int seq, int len, uint16_t* k_rows,
                           uint16_t* v_rows, cudaStream_t st);
 cudaError_t launch_append_chunk(const PoolView& pv, int layer, int seq, int pos0, int n,
                                 const float* k, const float* v, cudaStream_t st);
+cudaError_t launch_import_i8(const PoolView& pv, int layer, int seq, int pos0, int n, const int8_t* k_codes,
+                             const int8_t* v_codes, const float* k_scales, const float* v_scales, cudaStream_t st);
+cudaError_t launch_gather_i8(const PoolView& pv, int layer, int seq, int len, int8_t* k_codes, int8_t* v_codes,
+                             float* k_scales, float* v_scales, cudaStream_t st);
 cudaError_t launch_patch(const PoolView& pv, const TablePatch* patches, int npatch,
                          cudaStream_t st);
 cudaError_t launch_prefill(const PoolView& pv, int layer, int seq, int pos0, int n, const float* q,

@@ -16,7 +16,7 @@ namespace kvattn {
 namespace {
 
 __device__ __forceinline__ size_t tile_base(const PoolView& pv, int layer, int blk, int head) {
-    return (size_t)layer * pv.layer_bytes + ((size_t)blk * pv.kv_heads + head) * kTileBytes;
+    return (size_t)layer * pv.layer_bytes + ((size_t)blk * pv.kv_heads + head) * pv.tile_bytes;
 }
 
 // Chunk `ch` (0..15, 8 dims each) of token row t inside a tile.
@@ -101,6 +101,102 @@ __global__ void append_chunk_kernel(PoolView pv, int layer, int seq, int pos0, i
     }
 }
 
+// The same append into an INT8 pool: the rotated k row and the v row of each
+// (token, kv head) quantised by its warp (quant_row_warp), codes and scale
+// written to the tile.
+__global__ void append_chunk_i8_kernel(PoolView pv, int layer, int seq, int pos0, int n,
+                                       const float* __restrict__ k, const float* __restrict__ v) {
+    const int lane = threadIdx.x & 31;
+    const long nwarps = (long)n * pv.kv_heads;
+    const int* trow = pv.table + (size_t)seq * pv.max_blocks_per_seq;
+    const size_t kvw = (size_t)pv.kv_heads * kHeadDim;
+    for (long w = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5; w < nwarps;
+         w += ((long)gridDim.x * blockDim.x) >> 5) {
+        const int h = (int)(w % pv.kv_heads);
+        const int r = (int)(w / pv.kv_heads);
+        const int p = pos0 + r;
+        const float* kr = k + (size_t)r * kvw + (size_t)h * kHeadDim;
+        const float* vr = v + (size_t)r * kvw + (size_t)h * kHeadDim;
+        const float* cs = reinterpret_cast<const float*>(pv.rope + (size_t)p * (kHeadDim / 2));
+        const int i = 2 * lane;
+        float2 a = *reinterpret_cast<const float2*>(kr + i);
+        float2 b = *reinterpret_cast<const float2*>(kr + i + 64);
+        float4 cc = *reinterpret_cast<const float4*>(cs + 2 * i);
+        float kx[4], vx[4];
+        rope_pair(a.x, b.x, cc.x, cc.y, kx[0], kx[2]);
+        rope_pair(a.y, b.y, cc.z, cc.w, kx[1], kx[3]);
+        const float2 va = *reinterpret_cast<const float2*>(vr + i);
+        const float2 vb = *reinterpret_cast<const float2*>(vr + i + 64);
+        vx[0] = va.x;
+        vx[1] = va.y;
+        vx[2] = vb.x;
+        vx[3] = vb.y;
+        int8_t kc[4], vc[4];
+        const float ks = quant_row_warp(kx, kc), vs = quant_row_warp(vx, vc);
+        const int blk = trow[p / kBlockTokens];
+        const int t = p % kBlockTokens;
+        const size_t tb = tile_base(pv, layer, blk, h);
+        uint8_t* kt = pv.k + tb;
+        uint8_t* vt = pv.v + tb;
+        *reinterpret_cast<char2*>(kt + t * kHeadDim + i) = make_char2(kc[0], kc[1]);
+        *reinterpret_cast<char2*>(kt + t * kHeadDim + i + 64) = make_char2(kc[2], kc[3]);
+        *reinterpret_cast<char2*>(vt + t * kHeadDim + i) = make_char2(vc[0], vc[1]);
+        *reinterpret_cast<char2*>(vt + t * kHeadDim + i + 64) = make_char2(vc[2], vc[3]);
+        if (lane == 0) {
+            reinterpret_cast<float*>(kt + kBlockTokens * kHeadDim)[t] = ks;
+            reinterpret_cast<float*>(vt + kBlockTokens * kHeadDim)[t] = vs;
+        }
+    }
+}
+
+// INT8 rows <-> tiles: codes [n][kv_heads * 128], scales [n][kv_heads]; one
+// thread per (row, kv head, K|V, 16-byte chunk of 8 chunks) plus the scale.
+__global__ void import_i8_kernel(PoolView pv, int layer, int seq, int pos0, int n, const uint4* __restrict__ kc,
+                                 const uint4* __restrict__ vc, const float* __restrict__ ks,
+                                 const float* __restrict__ vs) {
+    const long total = (long)n * pv.kv_heads * 9 * 2;
+    const int* trow = pv.table + (size_t)seq * pv.max_blocks_per_seq;
+    for (long x = blockIdx.x * (long)blockDim.x + threadIdx.x; x < total; x += (long)gridDim.x * blockDim.x) {
+        const int ch = (int)(x % 9);
+        long rest = x / 9;
+        const int h = (int)(rest % pv.kv_heads);
+        rest /= pv.kv_heads;
+        const int isv = (int)(rest & 1);
+        const int r = (int)(rest >> 1);
+        const int p = pos0 + r;
+        const int blk = trow[p / kBlockTokens];
+        const int t = p % kBlockTokens;
+        uint8_t* tile = (isv ? pv.v : pv.k) + tile_base(pv, layer, blk, h);
+        if (ch < 8) {
+            *reinterpret_cast<uint4*>(tile + t * kHeadDim + ch * 16) = (isv ? vc : kc)[((size_t)r * pv.kv_heads + h) * 8 + ch];
+        } else {
+            reinterpret_cast<float*>(tile + kBlockTokens * kHeadDim)[t] = (isv ? vs : ks)[(size_t)r * pv.kv_heads + h];
+        }
+    }
+}
+
+__global__ void gather_i8_kernel(PoolView pv, int layer, int seq, int len, uint4* __restrict__ kc,
+                                 uint4* __restrict__ vc, float* __restrict__ ks, float* __restrict__ vs) {
+    const long total = (long)len * pv.kv_heads * 9 * 2;
+    const int* trow = pv.table + (size_t)seq * pv.max_blocks_per_seq;
+    for (long x = blockIdx.x * (long)blockDim.x + threadIdx.x; x < total; x += (long)gridDim.x * blockDim.x) {
+        const int ch = (int)(x % 9);
+        long rest = x / 9;
+        const int h = (int)(rest % pv.kv_heads);
+        rest /= pv.kv_heads;
+        const int isv = (int)(rest & 1);
+        const int p = (int)(rest >> 1);
+        const int blk = trow[p / kBlockTokens];
+        const int t = p % kBlockTokens;
+        const uint8_t* tile = (isv ? pv.v : pv.k) + tile_base(pv, layer, blk, h);
+        if (ch < 8) {
+            (isv ? vc : kc)[((size_t)p * pv.kv_heads + h) * 8 + ch] = *reinterpret_cast<const uint4*>(tile + t * kHeadDim + ch * 16);
+        } else {
+            (isv ? vs : ks)[(size_t)p * pv.kv_heads + h] = reinterpret_cast<const float*>(tile + kBlockTokens * kHeadDim)[t];
+        }
+    }
+}
+
 __global__ void patch_kernel(PoolView pv, const TablePatch* __restrict__ patches, int npatch) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < npatch; i += gridDim.x * blockDim.x) {
         const TablePatch p = patches[i];
@@ -176,8 +272,29 @@ cudaError_t launch_append_chunk(const PoolView& pv, int layer, int seq, int pos0
     const int grid = grid_for(work, 256);
     if (pv.dtype == 0)
         append_chunk_kernel<0><<<grid, 256, 0, st>>>(pv, layer, seq, pos0, n, k, v);
-    else
+    else if (pv.dtype == 1)
         append_chunk_kernel<1><<<grid, 256, 0, st>>>(pv, layer, seq, pos0, n, k, v);
+    else
+        append_chunk_i8_kernel<<<grid, 256, 0, st>>>(pv, layer, seq, pos0, n, k, v);
+    return counted(cudaGetLastError());
+}
+
+cudaError_t launch_import_i8(const PoolView& pv, int layer, int seq, int pos0, int n, const int8_t* k_codes,
+                             const int8_t* v_codes, const float* k_scales, const float* v_scales, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    const long work = (long)n * pv.kv_heads * 18;
+    import_i8_kernel<<<grid_for(work, 256), 256, 0, st>>>(pv, layer, seq, pos0, n,
+                                                          reinterpret_cast<const uint4*>(k_codes),
+                                                          reinterpret_cast<const uint4*>(v_codes), k_scales, v_scales);
+    return counted(cudaGetLastError());
+}
+
+cudaError_t launch_gather_i8(const PoolView& pv, int layer, int seq, int len, int8_t* k_codes, int8_t* v_codes,
+                             float* k_scales, float* v_scales, cudaStream_t st) {
+    if (len <= 0) return cudaSuccess;
+    const long work = (long)len * pv.kv_heads * 18;
+    gather_i8_kernel<<<grid_for(work, 256), 256, 0, st>>>(pv, layer, seq, len, reinterpret_cast<uint4*>(k_codes),
+                                                          reinterpret_cast<uint4*>(v_codes), k_scales, v_scales);
     return counted(cudaGetLastError());
 }
 

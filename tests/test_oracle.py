@@ -126,3 +126,51 @@ def test_restatement_equals_reference_live(orc):
         assert np.array_equal(kc, kc2) and np.array_equal(vc, vc2)
         assert np.array_equal(bits(q1), bits(q2))
         assert np.array_equal(bits(o1), bits(o2))
+
+
+def test_int8_quantiser_properties(orc):
+    """orc_quantize_i8: scale = max|x| / 127, codes round-half-away(x / scale)
+    in [-127, 127], every element within half a step of its dequantised
+    value; an all-zero row has scale 0 and zero codes."""
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((64, 128)).astype(np.float32) * rng.uniform(0.01, 100, (64, 1)).astype(np.float32)
+    x[3] = 0.0
+    x[5, 7] = -x[5].__abs__().max() * 2  # a negative extreme
+    q, s = orc.quantize_i8(x)
+    assert q.dtype == np.int8 and s.shape == (64,)
+    amax = np.abs(x).max(axis=1)
+    assert np.array_equal(s, (amax / np.float32(127)).astype(np.float32))
+    assert s[3] == 0 and not q[3].any()
+    nz = s > 0
+    assert (np.abs(q[nz]).max(axis=1) == 127).all()
+    err = np.abs(q.astype(np.float32) * s[:, None] - x)
+    assert (err <= s[:, None] * 0.5 * (1 + 1e-6) + 1e-30).all()
+    # exact halves round away from zero: 2.5 steps -> 3, -2.5 -> -3
+    row = np.zeros((1, 128), np.float32)
+    row[0, 0], row[0, 1], row[0, 2] = 127.0, 2.5, -2.5
+    q1, s1 = orc.quantize_i8(row)
+    assert s1[0] == 1.0 and q1[0, 0] == 127 and q1[0, 1] == 3 and q1[0, 2] == -3
+
+
+def test_int8_attention_close_to_fp32(orc):
+    """The INT8 layer step against the same step on unquantised fp32 caches:
+    quantisation error only (informational bound, per-row scales)."""
+    rng = np.random.default_rng(6)
+    T, kvd, hid = 200, 256, 1536
+    k = rng.standard_normal((T, kvd)).astype(np.float32)
+    v = rng.standard_normal((T, kvd)).astype(np.float32)
+    kq = np.zeros((T + 1, kvd), np.int8)
+    vq = np.zeros((T + 1, kvd), np.int8)
+    ks = np.zeros((T + 1, 2), np.float32)
+    vs = np.zeros((T + 1, 2), np.float32)
+    for t in range(T):
+        for h in range(2):
+            kq[t, h * 128:(h + 1) * 128], ks[t, h] = [a[0] for a in orc.quantize_i8(k[t:t + 1, h * 128:(h + 1) * 128])]
+            vq[t, h * 128:(h + 1) * 128], vs[t, h] = [a[0] for a in orc.quantize_i8(v[t:t + 1, h * 128:(h + 1) * 128])]
+    q = rng.standard_normal((1, hid)).astype(np.float32)
+    kn = rng.standard_normal((1, kvd)).astype(np.float32)
+    vn = rng.standard_normal((1, kvd)).astype(np.float32)
+    out = orc.layer_step_i8(q, kn, vn, kq, ks, vq, vs, T)
+    assert np.isfinite(out).all() and np.abs(out).max() > 0
+    # the appended row is the quantised RoPE'd k / plain v
+    assert np.abs(vq[T].astype(np.float32) * np.repeat(vs[T], 128) - vn[0]).max() <= vs[T].max() * 0.5001
