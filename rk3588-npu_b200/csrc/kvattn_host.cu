@@ -792,9 +792,10 @@ int attn_prefill(kvp_pool* p, int layer, int seq, int pos0, int n, const float* 
     const long ctas = (long)nq * p->kv_heads;
     // One CTA per SM is resident: pick the split count that minimises
     // waves x (tiles per CTA + a fixed cost per CTA of ~16 tiles: q setup and
-    // the first copies) + a merge cost per split, with at least one 64-key
+    // the first copies) + a merge cost per split, with at least one key
     // stage per split.
-    const int max_split = std::max(1, std::min(64, max_tiles / 4));
+    const int stage_tiles = prefill_tc_stage_tiles();
+    const int max_split = std::max(1, std::min(64, max_tiles / stage_tiles));
     int nsplit = 1;
     double best = 1e30;
     for (int ns = 1; ns <= max_split; ++ns) {
@@ -806,7 +807,7 @@ int attn_prefill(kvp_pool* p, int layer, int seq, int pos0, int n, const float* 
         }
     }
     int tps = (max_tiles + nsplit - 1) / nsplit;
-    tps = (tps + 3) / 4 * 4;  // whole 64-key stages
+    tps = (tps + stage_tiles - 1) / stage_tiles * stage_tiles;  // whole key stages
     nsplit = (max_tiles + tps - 1) / tps;
     if (nsplit > 1) {
         rc = prefill_part_reserve(p, prefill_tc_part_floats(p->q_heads, n, nsplit), st);

@@ -158,6 +158,7 @@ cudaError_t launch_prefill(const PoolView& pv, int layer, int seq, int pos0, int
 cudaError_t launch_prefill_tc(const PoolView& pv, int layer, int seq, int pos0, int n, const float* q,
                               float* out, float* part, int nsplit, int tiles_per_split, cudaStream_t st);
 int prefill_tc_tokens_per_cta(int group);
+int prefill_tc_stage_tiles();  // key tiles per stage of the tcgen05 prefill (a split is a whole number of them)
 size_t prefill_tc_part_floats(int q_heads, int n, int nsplit);
 cudaError_t launch_combine(int G, int rows, int dim, const float* m, const float* l,
                            const float* o, size_t gstride_ml, size_t gstride_o, float* out,

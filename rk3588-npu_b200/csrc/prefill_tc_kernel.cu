@@ -10,21 +10,21 @@
 //   warps 0-7  rows: warps w and w+4 own tensor-memory lanes 32(w%4).. (rows),
 //              each half of the row's columns.  They rotate,
 //              scale and split their q row into 16-bit hi + lo halves in shared
-//              memory (K-major, 128-byte swizzle), then per key stage of 64
+//              memory (K-major, 128-byte swizzle), then per key stage of 128
 //              keys read the row's scores from tensor memory, apply the causal
 //              mask, run the online softmax, rescale the output row in tensor
 //              memory when the row maximum moved, and write P (hi + lo) back
 //              over the stage's score columns in tensor memory, where the
 //              P*V MMA reads it as its A operand;
 //   warp 8     producer: bulk async copies (TMA engine, into this CTA only) of
-//              the stage's four (block, head) tiles -- each K tile as two
+//              the stage's eight (block, head) tiles -- each K tile as two
 //              2 KiB halves into two 64-row K-major regions, each V tile whole;
-//   warp 9     allocates 512 tensor-memory columns (two 64-column score
+//   warp 9     allocates 512 tensor-memory columns (two 128-column score
 //              buffers, a 128-column output, 128 columns of Q hi + lo) and one
 //              elected lane issues the MMAs:
-//                     S = Qhi K^T + Qlo K^T  (M 128, N 64, K 16 x 8 x 2; Q from
+//                     S = Qhi K^T + Qlo K^T  (M 128, N 128, K 16 x 8 x 2; Q from
 //              tensor memory, K from shared memory),
-//                     O += Phi V + Plo V    (M 128, N 128, K 16 x 4 x 2; P from
+//                     O += Phi V + Plo V    (M 128, N 128, K 16 x 8 x 2; P from
 //              tensor memory, the pool's V tile an MN-major operand as it
 //              lies), committing
 //              each group to an mbarrier.  The next stage's S is computed while
@@ -46,12 +46,14 @@ namespace kvattn {
 namespace {
 
 constexpr int kTcRows = 128;                 // MMA M: rows per CTA
-constexpr int kTcStageKeys = 64;             // keys per stage = 4 tiles
+constexpr int kTcStageKeys = 128;            // keys per stage = 8 tiles
+constexpr int kTcStageTiles = kTcStageKeys / kBlockTokens;
 constexpr int kTcRowWarps = 8;               // two softmax warps per row quarter
 constexpr int kTcThreads = (kTcRowWarps + 2) * 32;
-constexpr int kTcKvStages = 4;               // K/V stages in flight
-constexpr uint32_t kTmemCols = 512;          // S0 [0,64) S1 [64,128) O [128,256) Qhi [256,320) Qlo [320,384)
-constexpr uint32_t kTmemQ = 256;             // first column of Q (hi, then lo)
+constexpr int kTcKvStages = 2;               // K/V stages in flight (64 KB each)
+constexpr uint32_t kTmemCols = 512;          // S0 [0,128) S1 [128,256) O [256,384) Qhi [384,448) Qlo [448,512)
+constexpr uint32_t kTmemO = 256;             // first column of the output accumulator
+constexpr uint32_t kTmemQ = 384;             // first column of Q (hi, then lo)
 constexpr long long kTcWaitLimit = 4000000000LL;
 constexpr int kTcPartFloats = kHeadDim + 4;  // 16-byte aligned rows
 constexpr float kTcRescale = 8.f;            // lazy-rescale threshold (log2 units)
@@ -60,7 +62,7 @@ constexpr float kTcRescale = 8.f;            // lazy-rescale threshold (log2 uni
 struct TcSmem {
     uint8_t q[2][2][kTcRows * 128];         // [hi/lo][dims 0-63 / 64-127][row][128 B]
     uint8_t k[kTcKvStages][2][kTcStageKeys * 128];  // [stage][dims half][key][128 B]
-    uint8_t v[kTcKvStages][4][kTileBytes];          // [stage][tile] pool tile layout
+    uint8_t v[kTcKvStages][kTcStageTiles][kTileBytes];  // [stage][tile] pool tile layout
     uint64_t full[kTcKvStages], empty[kTcKvStages], s_full[2], p_ready, o_done, q_ready, mma_done;
     float xmax[2][2][kTcRows];  // [stage parity][column half][row]: the pair's row maxima
     float xsum[2][kTcRows];     // [column half][row]: the pair's row sums
@@ -213,9 +215,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int s0 = blockIdx.x * Tc;
     const int s_last = min(n, s0 + Tc) - 1;
     const int ntiles = (pos0 + s_last) / kBlockTokens + 1;
-    const int t_begin = sp * tiles_per_split;  // a multiple of 4
+    const int t_begin = sp * tiles_per_split;  // a multiple of kTcStageTiles
     const int t_end = min(ntiles, t_begin + tiles_per_split);
-    const int nst = t_end > t_begin ? (t_end - t_begin + 3) / 4 : 0;
+    const int nst = t_end > t_begin ? (t_end - t_begin + kTcStageTiles - 1) / kTcStageTiles : 0;
     const int kv_lim = min(t_end * kBlockTokens, pos0 + s_last + 1);  // keys >= kv_lim never count
 
     if (tid == 0) {
@@ -242,7 +244,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     if (warp == kTcRowWarps) {
         // ---------------------------------------------------------- producer
-        // Lane 0 waits for the stage and arms its barrier; lanes 0-3 then
+        // Lane 0 waits for the stage and arms its barrier; lanes 0-7 then
         // issue one tile each (its block id, two K halves, the V tile).
         const uint64_t policy = policy_evict_first();
         const int* trow = pv.table + (size_t)seq * pv.max_blocks_per_seq;
@@ -250,7 +252,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int j = 0; j < nst; ++j) {
             const int b = j % kTcKvStages;
             int tiles = 0;
-            for (int u = 0; u < 4; ++u) tiles += (t_begin + 4 * j + u < t_end);
+            for (int u = 0; u < kTcStageTiles; ++u) tiles += (t_begin + kTcStageTiles * j + u < t_end);
             int go = 1;
             if (lane == 0) {
                 if (j >= kTcKvStages &&
@@ -262,7 +264,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             go = __shfl_sync(0xffffffffu, go, 0);
             if (!go) break;
             if (lane < tiles) {
-                const int t = t_begin + 4 * j + lane;
+                const int t = t_begin + kTcStageTiles * j + lane;
                 int blk = (t < pv.max_blocks_per_seq) ? trow[t] : -1;
                 if (blk < 0 || blk >= pv.num_blocks) {
                     if (atomicCAS(pv.status, 0, 5) == 0) {
@@ -293,7 +295,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             // 8kk.. of each 64-column block.
             auto issue_qk = [&](int j) {
                 const uint32_t kb = smem_u32(sm.k[j % kTcKvStages][0]);
-                const uint32_t d = tmem + (uint32_t)((j & 1) * kTcStageKeys);
+                const uint32_t d = tmem + (uint32_t)((j & 1) * kTcStageKeys);  // S: one column per key
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     const uint32_t koff = (uint32_t)((kk >> 2) * (kTcStageKeys * 128) + (kk & 3) * 32);
@@ -307,11 +309,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             auto issue_pv = [&](int j) {
                 const int b = j % kTcKvStages;
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
+                for (int u = 0; u < kTcStageTiles; ++u) {
                     const uint64_t bd = sdesc(smem_u32(sm.v[b][u]), 2048, 1024);
 #pragma unroll
-                    for (int hl = 0; hl < 2; ++hl)  // P of stage j sits in its score columns
-                        tc_mma_ts(tmem + 128u, tmem + (uint32_t)((j & 1) * kTcStageKeys + hl * 32 + u * 8), bd,
+                    for (int hl = 0; hl < 2; ++hl)  // P of stage j sits in its score columns (hi, then lo)
+                        tc_mma_ts(tmem + kTmemO,
+                                  tmem + (uint32_t)((j & 1) * kTcStageKeys + hl * (kTcStageKeys / 2) + u * 8), bd,
                                   id_pv, (j | u | hl) != 0);
                 }
                 tc_commit(&sm.o_done);
@@ -453,16 +456,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             // per stage and leave the loop together: a failed wait is
             // published next to the row maxima and acted on after the barrier.
             bad = bad || !__all_sync(0xffffffffu, tc_wait(&sm.s_full[j & 1], (j >> 1) & 1, pv, 720, &sm.failed));
-            float sc[32];
+            constexpr int kHalf = kTcStageKeys / 2;  // this warp's keys of the stage
+            float sc[kHalf];
             float mx = -INFINITY;
-            const int kbase = (t_begin + 4 * j) * kBlockTokens + ch * 32;
+            const int kbase = (t_begin + kTcStageTiles * j) * kBlockTokens + ch * kHalf;
             if (!bad) {
                 tc_fence_after();
-                tmem_ld32(tmem + lane_base + (uint32_t)((j & 1) * kTcStageKeys + ch * 32), sc);
+                const uint32_t scol = tmem + lane_base + (uint32_t)((j & 1) * kTcStageKeys + ch * kHalf);
+                tmem_ld32(scol, *reinterpret_cast<float(*)[32]>(sc));
+                tmem_ld32(scol + 32u, *reinterpret_cast<float(*)[32]>(sc + 32));
                 tc_wait_ld();
                 float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-                for (int c = 0; c < 32; ++c) {
+                for (int c = 0; c < kHalf; ++c) {
                     const int key = kbase + c;
                     if (key > prow || key >= kv_lim) sc[c] = -INFINITY;
                     mx4[c & 3] = fmaxf(mx4[c & 3], sc[c]);
@@ -497,7 +503,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const float mu = (m == -INFINITY) ? 0.f : m;
             float sum4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int c = 0; c < 32; ++c) {
+            for (int c = 0; c < kHalf; ++c) {
                 sc[c] = fast_exp2(sc[c] - mu);
                 sum4[c & 3] += sc[c];
             }
@@ -506,7 +512,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             // (stale smem, rows past the sequence); zero them so masked
             // weights (exactly 0) stay 0.
             if (j == nst - 1) {
-                const int kb0 = (t_begin + 4 * j) * kBlockTokens;
+                const int kb0 = (t_begin + kTcStageTiles * j) * kBlockTokens;
                 for (int x = tr; x < kTcStageKeys * 16; x += 256) {  // (key row, 16-byte chunk)
                     const int kr = x >> 4, cq = x & 15;
                     if (kb0 + kr >= kv_lim) {
@@ -517,20 +523,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             }
             // P (hi + lo) over this stage's score columns: the A operand of
-            // P*V (hi of the 64 keys in columns 0-31, lo in 32-63, two keys
-            // per column; this warp's 32 keys are columns 16ch.. of each).
+            // P*V (hi of the 128 keys in columns 0-63, lo in 64-127, two keys
+            // per column; this warp's 64 keys are columns 32ch.. of each).
             {
-                float ph[16], pl[16];
+                float ph[32], pl[32];
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
+                for (int e = 0; e < 32; ++e) {
                     uint32_t hh, ll;
                     split_p<DT>(sc[2 * e], sc[2 * e + 1], hh, ll);
                     ph[e] = __uint_as_float(hh);
                     pl[e] = __uint_as_float(ll);
                 }
-                const uint32_t sbuf = tmem + lane_base + (uint32_t)((j & 1) * kTcStageKeys + ch * 16);
-                tmem_st16(sbuf, ph);
-                tmem_st16(sbuf + 32u, pl);
+                const uint32_t sbuf = tmem + lane_base + (uint32_t)((j & 1) * kTcStageKeys + ch * 32);
+                tmem_st32(sbuf, ph);
+                tmem_st32(sbuf + (uint32_t)(kTcStageKeys / 2), pl);
             }
             // The output row is rescaled only when its reference max moved
             // (rare after the first stages); then the previous P*V must be done.
@@ -540,7 +546,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll 1
                 for (int c2 = 0; c2 < 2; ++c2) {
                     float o[32];
-                    const uint32_t oc = tmem + lane_base + 128u + (uint32_t)(ch * 64 + 32 * c2);
+                    const uint32_t oc = tmem + lane_base + kTmemO + (uint32_t)(ch * 64 + 32 * c2);
                     tmem_ld32(oc, o);
                     tc_wait_ld();
 #pragma unroll
@@ -579,7 +585,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll 1
             for (int c2 = 0; c2 < 2; ++c2) {
                 float o[32];
-                tmem_ld32(tmem + lane_base + 128u + (uint32_t)(ch * 64 + 32 * c2), o);
+                tmem_ld32(tmem + lane_base + kTmemO + (uint32_t)(ch * 64 + 32 * c2), o);
                 tc_wait_ld();
                 if (dst) {
 #pragma unroll
@@ -633,6 +639,7 @@ __global__ void __launch_bounds__(4 * kHeadDim)
 size_t prefill_tc_smem_bytes() { return sizeof(TcSmem) + 1024; }
 
 int prefill_tc_tokens_per_cta(int group) { return kTcRows / group; }
+int prefill_tc_stage_tiles() { return kTcStageTiles; }
 size_t prefill_tc_part_floats(int q_heads, int n, int nsplit) {
     return (size_t)q_heads * n * nsplit * kTcPartFloats;
 }
