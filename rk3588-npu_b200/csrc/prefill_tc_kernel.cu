@@ -341,15 +341,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
                 if (progressed) {
                     since = clock64();
-                } else if (*reinterpret_cast<volatile int*>(&sm.failed)) {
-                    ok = false;
-                } else if (clock64() - since > kTcWaitLimit) {
-                    if (atomicCAS(pv.status, 0, KV_ERR_TIMEOUT) == 0) {
-                        pv.status[1] = blockIdx.x;
-                        pv.status[2] = 711;
+                } else {
+                    __nanosleep(32);  // leave the issue slots to the row warps
+                    if (*reinterpret_cast<volatile int*>(&sm.failed)) {
+                        ok = false;
+                    } else if (clock64() - since > kTcWaitLimit) {
+                        if (atomicCAS(pv.status, 0, KV_ERR_TIMEOUT) == 0) {
+                            pv.status[1] = blockIdx.x;
+                            pv.status[2] = 711;
+                        }
+                        *reinterpret_cast<volatile int*>(&sm.failed) = 1;
+                        ok = false;
                     }
-                    *reinterpret_cast<volatile int*>(&sm.failed) = 1;
-                    ok = false;
                 }
             }
             // every MMA issued above has completed once this arrives
@@ -467,11 +470,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 tmem_ld32(scol + 32u, *reinterpret_cast<float(*)[32]>(sc + 32));
                 tc_wait_ld();
                 float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                if (kbase + kHalf - 1 <= prow && kbase + kHalf <= kv_lim) {
+                    // every key of this warp's half is visible to the row
 #pragma unroll
-                for (int c = 0; c < kHalf; ++c) {
-                    const int key = kbase + c;
-                    if (key > prow || key >= kv_lim) sc[c] = -INFINITY;
-                    mx4[c & 3] = fmaxf(mx4[c & 3], sc[c]);
+                    for (int c = 0; c < kHalf; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], sc[c]);
+                } else {
+#pragma unroll
+                    for (int c = 0; c < kHalf; ++c) {
+                        const int key = kbase + c;
+                        if (key > prow || key >= kv_lim) sc[c] = -INFINITY;
+                        mx4[c & 3] = fmaxf(mx4[c & 3], sc[c]);
+                    }
                 }
                 mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
             }
