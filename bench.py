@@ -146,8 +146,10 @@ def parse_args():
     ap.add_argument("--transport", choices=["nccl", "p2p"], default="nccl",
                     help="long workloads: merge of the per-GPU states by NCCL all-gather + combine "
                          "launch, or by the fused peer-memory exchange kernel")
-    ap.add_argument("--prefill-kernel", choices=["tc", "mma"], default="tc",
-                    help="prefill workload: the tcgen05 kernel (attn_prefill) or the mma.sync baseline")
+    ap.add_argument("--prefill-kernel", choices=["tc", "tc1", "mma"], default="tc",
+                    help="prefill workload: the tcgen05 kernel over all requests per launch "
+                         "(kv_append_chunk_batch + attn_prefill_batch), the tcgen05 kernel one request per "
+                         "call (tc1), or the mma.sync baseline (one request per call)")
     ap.add_argument("--kv-dtype", choices=["native", "int8"], default="native",
                     help="batch32 / paged28 / paged1: keep the workload's cache type, or an INT8 cache "
                          "(per-row scales) with the same contexts")
@@ -871,13 +873,16 @@ def run_prefill(args, rank, world, local):
                 P.import_rows(y, s, 0, k, v)
     for s, p0 in zip(ids, pos0):
         P.set_cur_pos(s, p0)
-    qb = torch.randn((NL, CH, HID), generator=g, device="cuda")
-    kb = torch.randn((NL, CH, KVD), generator=g, device="cuda")
-    vb = torch.randn((NL, CH, KVD), generator=g, device="cuda")
-    ob = torch.empty((CH, HID), device="cuda")
+    # every request's chunk rows, concatenated (as a batched projection writes them)
+    R = wl.batch * CH
+    qb = torch.randn((NL, R, HID), generator=g, device="cuda")
+    kb = torch.randn((NL, R, KVD), generator=g, device="cuda")
+    vb = torch.randn((NL, R, KVD), generator=g, device="cuda")
+    ob = torch.empty((R, HID), device="cuda")
     L = kv._lib
     st = torch.cuda.current_stream().cuda_stream
-    prefill_fn = L.attn_prefill if args.prefill_kernel == "tc" else L.attn_prefill_mma
+    prefill_fn = L.attn_prefill_mma if args.prefill_kernel == "mma" else L.attn_prefill
+    ids_c, pos_c, ns_c = kv._ints(ids), kv._ints(pos0), kv._ints([CH] * len(ids))
 
     def chk(rc, fn):
         if rc != 0:
@@ -885,10 +890,17 @@ def run_prefill(args, rank, world, local):
 
     def step():
         for y in range(NL):
-            for s, p0 in zip(ids, pos0):
-                chk(L.kv_append_chunk(P.h, y, s, p0, CH, kb[y].data_ptr(), vb[y].data_ptr(), st),
+            if args.prefill_kernel == "tc":  # all requests' chunks in shared launches
+                chk(L.kv_append_chunk_batch(P.h, y, len(ids), ids_c, pos_c, ns_c, kb[y].data_ptr(),
+                                            vb[y].data_ptr(), st), "kv_append_chunk_batch")
+                chk(L.attn_prefill_batch(P.h, y, len(ids), ids_c, pos_c, ns_c, qb[y].data_ptr(), ob.data_ptr(),
+                                         st), "attn_prefill_batch")
+                continue
+            for i, (s, p0) in enumerate(zip(ids, pos0)):  # one call per request
+                r = i * CH
+                chk(L.kv_append_chunk(P.h, y, s, p0, CH, kb[y, r].data_ptr(), vb[y, r].data_ptr(), st),
                     "kv_append_chunk")
-                chk(prefill_fn(P.h, y, s, p0, CH, qb[y].data_ptr(), ob.data_ptr(), st), "attn_prefill")
+                chk(prefill_fn(P.h, y, s, p0, CH, qb[y, r].data_ptr(), ob[r].data_ptr(), st), "attn_prefill")
 
     # real (not doubled by the hi/lo split) FLOPs: QK^T and PV, 2 * 128 each per (query, key, head)
     flops = NL * sum(sum(4.0 * HD * NQ * (p0 + i + 1) for i in range(CH)) for p0 in pos0)
@@ -929,7 +941,8 @@ def run_prefill(args, rank, world, local):
             "ms_per_step": round(step_ms / K, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": wl.dtype_name, "data": wl.data,
             "config": {"workload": wl.desc, "name": wl.name, "chunk": CH, "layers": NL,
-                       "kernel": "tcgen05" if args.prefill_kernel == "tc" else "mma.sync",
+                       "kernel": {"tc": "tcgen05, all requests per launch", "tc1": "tcgen05, one launch per request",
+                                  "mma": "mma.sync, one launch per request"}[args.prefill_kernel],
                        "contexts_before_chunk": pos0, "l2": "inputs larger than L2 (no flush)"},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": None,

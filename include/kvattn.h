@@ -160,6 +160,19 @@ int kv_append_chunk(kvp_pool* pool, int layer, int seq_id, int pos0, int n, cons
  * 5th-generation tensor cores (tcgen05 MMA with accumulators in tensor memory). */
 int attn_prefill(kvp_pool* pool, int layer, int seq_id, int pos0, int n, const float* q,
                  float* out, void* stream);
+/* Several prompt chunks at once (chunked prefill of a continuous-batching
+ * step): chunk i appends / attends n[i] tokens at positions pos0[i].. of
+ * sequence seq_ids[i] (distinct sequences); its rows are rows
+ * [n[0] + ... + n[i-1], ... + n[i]) of k / v / q / out, laid out as in the
+ * single-chunk calls.  Same results as one call per chunk; the chunks share
+ * launches (up to 32 chunks per launch), with the key splits of the
+ * attention planned over all of them.  Replaces the per-request loop around
+ * the append (qwen2_model.cpp:180-200) and op_attention (op_attention.cpp:
+ * 9-56) when several requests prefill in one step. */
+int kv_append_chunk_batch(kvp_pool* pool, int layer, int nreq, const int* seq_ids, const int* pos0,
+                          const int* n, const float* k, const float* v, void* stream);
+int attn_prefill_batch(kvp_pool* pool, int layer, int nreq, const int* seq_ids, const int* pos0,
+                       const int* n, const float* q, float* out, void* stream);
 /* The same computation on the legacy mma.sync tensor path (the baseline
  * attn_prefill's tcgen05 kernel is measured against). */
 int attn_prefill_mma(kvp_pool* pool, int layer, int seq_id, int pos0, int n, const float* q,

@@ -56,6 +56,8 @@ _SIGS = {
     "kv_append_chunk": [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp],
     "attn_prefill": [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp],
     "attn_prefill_mma": [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp],
+    "kv_append_chunk_batch": [_vp, C.c_int, C.c_int, _vp, _vp, _vp, _vp, _vp, _vp],
+    "attn_prefill_batch": [_vp, C.c_int, C.c_int, _vp, _vp, _vp, _vp, _vp, _vp],
     "attn_decode_plan": [_vp, C.c_int, _ip, _vp],
     "attn_decode_plan_ex": [_vp, C.c_int, _ip, _ip, _ip, _vp],
     "attn_decode_append": [_vp, C.c_int, _vp, _vp, _vp, _vp, _vp],
@@ -282,6 +284,21 @@ class Pool:
         n = q.shape[0]
         fn = "attn_prefill" if kernel == "tc" else "attn_prefill_mma"
         call(fn, self.h, layer, seq, pos0, n, _ptr(q), _ptr(out), _stream(stream))
+
+    def append_chunk_batch(self, layer, seqs, pos0s, k, v, ns=None, stream=None) -> None:
+        """Chunks of several sequences in one call: chunk i is ns[i] rows of
+        k / v [sum(ns), kv_dim] (in order) at positions pos0s[i].. of seqs[i]."""
+        ns = list(ns) if ns is not None else [k.shape[0]]
+        assert len(seqs) == len(pos0s) == len(ns) and sum(ns) == k.shape[0]
+        call("kv_append_chunk_batch", self.h, layer, len(seqs), _ints(seqs), _ints(pos0s), _ints(ns), _ptr(k),
+             _ptr(v), _stream(stream))
+
+    def prefill_batch(self, layer, seqs, pos0s, ns, q, out, stream=None) -> None:
+        """Causal attention of several chunks (rows concatenated in q / out, in
+        order) in shared tcgen05 launches."""
+        assert len(seqs) == len(pos0s) == len(ns) and sum(ns) == q.shape[0]
+        call("attn_prefill_batch", self.h, layer, len(seqs), _ints(seqs), _ints(pos0s), _ints(ns), _ptr(q),
+             _ptr(out), _stream(stream))
 
     # ---- decode ----
     def plan(self, seq_ids, rope_pos=None, append=None, stream=None) -> None:

@@ -52,7 +52,6 @@ constexpr int kConsumerWarps = 4;
 // owned by another warp, had not landed; the parity test then passed early.)
 static_assert(kStages % kConsumerWarps == 0, "each ring stage must belong to one consumer warp");
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kStageBytes = 2 * kTileBytes;  // K tile then V tile
 
 // Shared-memory shapes per cache type.  16-bit caches: a ring stage holds the
 // K and V tiles as they lie in HBM (the swizzled mma layout).  INT8 caches: a

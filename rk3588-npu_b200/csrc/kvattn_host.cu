@@ -716,29 +716,78 @@ int kvp_gather_i8(kvp_pool* p, int layer, int seq, void* k_codes, void* v_codes,
     return KV_OK;
 }
 
-int kv_append_chunk(kvp_pool* p, int layer, int seq, int pos0, int n, const float* k,
-                    const float* v, void* stream) {
-    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
-    std::lock_guard<std::mutex> lk(p->mu);
+namespace {
+
+// One prompt chunk's checks, shared by the append and attention entry
+// points (in the order the single-chunk calls report them).
+int chunk_check(kvp_pool* p, int layer, int seq, int pos0, int n, bool first) {
     int rc = check_seq(p, seq);
     if (rc) return rc;
-    rc = require_device(p);
-    if (rc) return rc;
+    if (first && (rc = require_device(p))) return rc;
     if (layer < 0 || layer >= p->layers) return fail(KV_ERR_INVAL, "layer %d out of range", layer);
     if (n < 0 || pos0 < 0) return fail(KV_ERR_INVAL, "negative position/count");
     if ((long)pos0 + n > p->max_seq_len)
         return fail(KV_ERR_RANGE, "position %ld beyond max_seq_len %d", (long)pos0 + n - 1, p->max_seq_len);
     if ((long)pos0 + n > (long)p->seqs[seq].blocks.size() * kBlockTokens)
         return fail(KV_ERR_RANGE, "positions [%d, %d) exceed reserved blocks", pos0, pos0 + n);
-    if (n == 0) return KV_OK;
+    return KV_OK;
+}
+
+// Every chunk of a batch (distinct sequences); *rows = the rows of all chunks.
+int batch_check(kvp_pool* p, int layer, int nreq, const int* seqs, const int* pos0, const int* ns, long* rows) {
+    if (nreq < 0 || (nreq > 0 && (!seqs || !pos0 || !ns))) return fail(KV_ERR_INVAL, "bad chunk list");
+    if (nreq == 0) {
+        int rc = require_device(p);
+        if (rc) return rc;
+    }
+    long total = 0;
+    for (int i = 0; i < nreq; ++i) {
+        int rc = chunk_check(p, layer, seqs[i], pos0[i], ns[i], i == 0);
+        if (rc) return rc;
+        for (int j = 0; j < i; ++j)
+            if (seqs[j] == seqs[i]) return fail(KV_ERR_INVAL, "sequence %d appears twice in one batch", seqs[i]);
+        total += ns[i];
+    }
+    *rows = total;
+    return KV_OK;
+}
+
+}  // namespace
+
+int kv_append_chunk_batch(kvp_pool* p, int layer, int nreq, const int* seqs, const int* pos0, const int* ns,
+                          const float* k, const float* v, void* stream) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    std::lock_guard<std::mutex> lk(p->mu);
+    long rows = 0;
+    int rc = batch_check(p, layer, nreq, seqs, pos0, ns, &rows);
+    if (rc || rows == 0) return rc;
     if (!k || !v || ((uintptr_t)k & 7) || ((uintptr_t)v & 7))
         return fail(KV_ERR_INVAL, "k/v must be non-NULL and 8-byte aligned");
     DeviceGuard dg(p->device);
     cudaStream_t st = (cudaStream_t)stream;
     rc = sync_table(p, st);
     if (rc) return rc;
-    KV_CUDA(launch_append_chunk(p->pv, layer, seq, pos0, n, k, v, st));
+    const size_t kvw = (size_t)p->kv_heads * kHeadDim;
+    long row = 0;
+    for (int b0 = 0; b0 < nreq; b0 += kMaxChunkBatch) {
+        ChunkBatch cb{};
+        const long base = row;
+        for (int i = b0; i < std::min(nreq, b0 + kMaxChunkBatch); ++i) {
+            cb.seq[cb.nreq] = seqs[i];
+            cb.pos0[cb.nreq] = pos0[i];
+            cb.row0[cb.nreq] = (int)(row - base);
+            ++cb.nreq;
+            row += ns[i];
+        }
+        cb.row0[cb.nreq] = (int)(row - base);
+        KV_CUDA(launch_append_batch(p->pv, layer, cb, k + base * kvw, v + base * kvw, st));
+    }
     return KV_OK;
+}
+
+int kv_append_chunk(kvp_pool* p, int layer, int seq, int pos0, int n, const float* k,
+                    const float* v, void* stream) {
+    return kv_append_chunk_batch(p, layer, 1, &seq, &pos0, &n, k, v, stream);
 }
 
 namespace {
@@ -754,67 +803,153 @@ int prefill_part_reserve(kvp_pool* p, size_t need, cudaStream_t st) {
     return KV_OK;
 }
 
-// Shared checks of the prefill entry points; on success the table is on the device.
+// Shared checks of the single-chunk mma.sync entry point; on success the
+// table is on the device.
 int prefill_checks(kvp_pool* p, int layer, int seq, int pos0, int n, const float* q, float* out,
                    cudaStream_t st) {
-    int rc = check_seq(p, seq);
-    if (rc) return rc;
-    rc = require_device(p);
+    int rc = chunk_check(p, layer, seq, pos0, n, true);
     if (rc) return rc;
     if (p->dtype == KV_I8) return fail(KV_ERR_INVAL, "prefill attention reads 16-bit caches; INT8 pools decode only");
-    if (layer < 0 || layer >= p->layers) return fail(KV_ERR_INVAL, "layer %d out of range", layer);
-    if (n < 0 || pos0 < 0) return fail(KV_ERR_INVAL, "negative position/count");
-    if ((long)pos0 + n > p->max_seq_len)
-        return fail(KV_ERR_RANGE, "position %ld beyond max_seq_len %d", (long)pos0 + n - 1, p->max_seq_len);
-    if ((long)pos0 + n > (long)p->seqs[seq].blocks.size() * kBlockTokens)
-        return fail(KV_ERR_RANGE, "positions [%d, %d) exceed reserved blocks", pos0, pos0 + n);
     if (n == 0) return KV_OK;
     if (!q || !out || ((uintptr_t)q & 15) || ((uintptr_t)out & 15))
         return fail(KV_ERR_INVAL, "q and out must be 16-byte aligned");
     return sync_table(p, st);
 }
 
-}  // namespace
+// Key splits of the chunks of one tcgen05 launch.  Every CTA is resident
+// alone on its SM and costs (its key tiles + kFixedTiles), the fixed part
+// being the q setup, the first copies and the epilogue (measured ~7.7 us, ~2
+// key stages).  For a target of X tiles per CTA (whole stages) chunk i gets
+// nsplit_i = ceil(T_i / X) splits; the X kept minimises the makespan
+// estimate max(W / SMs, w_max) (+ half a CTA when the grid exceeds one
+// wave) plus the merge cost, W being the summed CTA costs.  CTAs are then
+// listed longest first.
+constexpr double kFixedTiles = 16.0;
 
-// Tensor-core (tcgen05) version: 128 (token, head) rows per CTA, key splits
-// of whole 64-key stages, about one CTA per SM.
-int attn_prefill(kvp_pool* p, int layer, int seq, int pos0, int n, const float* q, float* out,
-                 void* stream) {
-    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
-    std::lock_guard<std::mutex> lk(p->mu);
-    DeviceGuard dg(p->device);
-    cudaStream_t st = (cudaStream_t)stream;
-    int rc = prefill_checks(p, layer, seq, pos0, n, q, out, st);
-    if (rc || n == 0) return rc;
-    const int tc = prefill_tc_tokens_per_cta(p->q_heads / p->kv_heads);
-    const int nq = (n + tc - 1) / tc;
-    const int max_tiles = (pos0 + n - 1) / kBlockTokens + 1;
-    const long ctas = (long)nq * p->kv_heads;
-    // One CTA per SM is resident: pick the split count that minimises
-    // waves x (tiles per CTA + a fixed cost per CTA of ~16 tiles: q setup and
-    // the first copies) + a merge cost per split, with at least one key
-    // stage per split.
-    const int stage_tiles = prefill_tc_stage_tiles();
-    const int max_split = std::max(1, std::min(64, max_tiles / stage_tiles));
-    int nsplit = 1;
-    double best = 1e30;
-    for (int ns = 1; ns <= max_split; ++ns) {
-        const long waves = (ctas * ns + p->num_sms - 1) / p->num_sms;
-        const double cost = (double)waves * ((double)max_tiles / ns + 16.0) + 0.25 * ns;
+struct ChunkPlan {
+    int seq, pos0, n, row0, nq, ctas_per_split, T, nsplit, tps;
+};
+
+void plan_splits(std::vector<ChunkPlan>& cs, int num_sms, int q_heads) {
+    const int st = prefill_tc_stage_tiles();
+    int tmax = 0;
+    for (const ChunkPlan& c : cs) tmax = std::max(tmax, c.T);
+    double best = 1e300;
+    int best_x = tmax;
+    for (int x = st; x < tmax + st; x += st) {
+        double W = 0.0, wmax = 0.0, merge = 0.0;
+        long N = 0;
+        for (const ChunkPlan& c : cs) {
+            int ns = std::min(64, std::max(1, (c.T + x - 1) / x));
+            int tps = ((c.T + ns - 1) / ns + st - 1) / st * st;
+            ns = (c.T + tps - 1) / tps;
+            const double w = tps + kFixedTiles;
+            W += (double)c.ctas_per_split * ns * w;
+            N += (long)c.ctas_per_split * ns;
+            wmax = std::max(wmax, w);
+            // partials written and read back (~2.3 MB per tile-time), plus a launch
+            if (ns > 1) merge += 8.0 + 2.0 * (double)c.n * q_heads * ns * 528.0 / 2.3e6;
+        }
+        const double cost = (N <= num_sms ? wmax : std::max(W / num_sms, wmax) + 0.5 * wmax) + merge;
         if (cost < best - 1e-9) {
             best = cost;
-            nsplit = ns;
+            best_x = x;
         }
     }
-    int tps = (max_tiles + nsplit - 1) / nsplit;
-    tps = (tps + stage_tiles - 1) / stage_tiles * stage_tiles;  // whole key stages
-    nsplit = (max_tiles + tps - 1) / tps;
-    if (nsplit > 1) {
-        rc = prefill_part_reserve(p, prefill_tc_part_floats(p->q_heads, n, nsplit), st);
+    for (ChunkPlan& c : cs) {
+        int ns = std::min(64, std::max(1, (c.T + best_x - 1) / best_x));
+        c.tps = ((c.T + ns - 1) / ns + st - 1) / st * st;
+        c.nsplit = (c.T + c.tps - 1) / c.tps;
+    }
+}
+
+// One tcgen05 launch (+ merge) over chunks [b0, b1) of a checked batch whose
+// rows start at row `base`.
+int prefill_tc_launch(kvp_pool* p, int layer, const int* seqs, const int* pos0, const int* ns, int b0, int b1,
+                      long base, const float* q, float* out, cudaStream_t st) {
+    const int tc = prefill_tc_tokens_per_cta(p->q_heads / p->kv_heads);
+    std::vector<ChunkPlan> cs;
+    long row = 0;
+    for (int i = b0; i < b1; ++i) {
+        if (ns[i] > 0) {
+            ChunkPlan c{};
+            c.seq = seqs[i];
+            c.pos0 = pos0[i];
+            c.n = ns[i];
+            c.row0 = (int)row;
+            c.nq = (ns[i] + tc - 1) / tc;
+            c.ctas_per_split = c.nq * p->kv_heads;
+            c.T = (pos0[i] + ns[i] - 1) / kBlockTokens + 1;
+            cs.push_back(c);
+        }
+        row += ns[i];
+    }
+    if (cs.empty()) return KV_OK;
+    plan_splits(cs, p->num_sms, p->q_heads);
+    std::stable_sort(cs.begin(), cs.end(), [](const ChunkPlan& a, const ChunkPlan& b) { return a.tps > b.tps; });
+    TcBatch tb{};
+    int ctas = 0, mrows = 0;
+    long long partf = 0;
+    for (const ChunkPlan& c : cs) {
+        TcReq& r = tb.r[tb.nreq++];
+        r.seq = c.seq;
+        r.pos0 = c.pos0;
+        r.n = c.n;
+        r.row0 = c.row0;
+        r.nq = c.nq;
+        r.nsplit = c.nsplit;
+        r.tps = c.tps;
+        r.cta0 = ctas;
+        r.mrow0 = mrows;
+        r.part0 = partf;
+        ctas += c.ctas_per_split * c.nsplit;
+        if (c.nsplit > 1) {
+            mrows += c.n;
+            partf += (long long)prefill_tc_part_floats(p->q_heads, c.n, c.nsplit);
+        }
+    }
+    if (partf > 0) {
+        int rc = prefill_part_reserve(p, (size_t)partf, st);
         if (rc) return rc;
     }
-    KV_CUDA(launch_prefill_tc(p->pv, layer, seq, pos0, n, q, out, p->d_prefill_part, nsplit, tps, st));
+    const size_t qw = (size_t)p->q_heads * kHeadDim;
+    KV_CUDA(launch_prefill_tc(p->pv, layer, tb, ctas, mrows, q + base * qw, out + base * qw, p->d_prefill_part,
+                              st));
     return KV_OK;
+}
+
+}  // namespace
+
+// Tensor-core (tcgen05) version over several chunks: one launch (plus one
+// merge launch when a chunk is split) per kMaxChunkBatch chunks.
+int attn_prefill_batch(kvp_pool* p, int layer, int nreq, const int* seqs, const int* pos0, const int* ns,
+                       const float* q, float* out, void* stream) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    std::lock_guard<std::mutex> lk(p->mu);
+    long rows = 0;
+    int rc = batch_check(p, layer, nreq, seqs, pos0, ns, &rows);
+    if (rc) return rc;
+    if (p->dtype == KV_I8) return fail(KV_ERR_INVAL, "prefill attention reads 16-bit caches; INT8 pools decode only");
+    if (rows == 0) return KV_OK;
+    if (!q || !out || ((uintptr_t)q & 15) || ((uintptr_t)out & 15))
+        return fail(KV_ERR_INVAL, "q and out must be 16-byte aligned");
+    DeviceGuard dg(p->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    rc = sync_table(p, st);
+    if (rc) return rc;
+    long base = 0;
+    for (int b0 = 0; b0 < nreq; b0 += kMaxChunkBatch) {
+        const int b1 = std::min(nreq, b0 + kMaxChunkBatch);
+        rc = prefill_tc_launch(p, layer, seqs, pos0, ns, b0, b1, base, q, out, st);
+        if (rc) return rc;
+        for (int i = b0; i < b1; ++i) base += ns[i];
+    }
+    return KV_OK;
+}
+
+int attn_prefill(kvp_pool* p, int layer, int seq, int pos0, int n, const float* q, float* out,
+                 void* stream) {
+    return attn_prefill_batch(p, layer, 1, &seq, &pos0, &n, q, out, stream);
 }
 
 // The same on mma.sync (the baseline the tensor-core version is measured against).

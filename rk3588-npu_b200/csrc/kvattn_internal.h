@@ -145,8 +145,18 @@ cudaError_t launch_import(const PoolView& pv, int layer, int seq, int pos0, int 
                           const uint16_t* k_rows, const uint16_t* v_rows, cudaStream_t st);
 cudaError_t launch_gather(const PoolView& pv, int layer, int seq, int len, uint16_t* k_rows,
                           uint16_t* v_rows, cudaStream_t st);
-cudaError_t launch_append_chunk(const PoolView& pv, int layer, int seq, int pos0, int n,
-                                const float* k, const float* v, cudaStream_t st);
+// Prompt chunks of several sequences in one launch: chunk i is rows
+// [row0[i], row0[i+1]) of the concatenated k / v (or q / out) rows, at
+// positions pos0[i].. of sequence seq[i].  Passed by value (kernel parameter).
+constexpr int kMaxChunkBatch = 32;
+struct ChunkBatch {
+    int nreq;
+    int seq[kMaxChunkBatch];
+    int pos0[kMaxChunkBatch];
+    int row0[kMaxChunkBatch + 1];
+};
+cudaError_t launch_append_batch(const PoolView& pv, int layer, const ChunkBatch& cb, const float* k,
+                                const float* v, cudaStream_t st);
 cudaError_t launch_import_i8(const PoolView& pv, int layer, int seq, int pos0, int n, const int8_t* k_codes,
                              const int8_t* v_codes, const float* k_scales, const float* v_scales, cudaStream_t st);
 cudaError_t launch_gather_i8(const PoolView& pv, int layer, int seq, int len, int8_t* k_codes, int8_t* v_codes,
@@ -155,8 +165,22 @@ cudaError_t launch_patch(const PoolView& pv, const TablePatch* patches, int npat
                          cudaStream_t st);
 cudaError_t launch_prefill(const PoolView& pv, int layer, int seq, int pos0, int n, const float* q,
                            float* out, float* part, int nsplit, int tiles_per_split, cudaStream_t st);
-cudaError_t launch_prefill_tc(const PoolView& pv, int layer, int seq, int pos0, int n, const float* q,
-                              float* out, float* part, int nsplit, int tiles_per_split, cudaStream_t st);
+// One chunk of a tcgen05 prefill launch: its CTAs are [cta0, cta0 + nq *
+// kv_heads * nsplit) (token group fastest, then KV head, then key split);
+// with nsplit > 1 its partials start at part0 floats and its merge rows at
+// mrow0 (both running totals over the chunks before it).
+struct TcReq {
+    int seq, pos0, n, row0;
+    int nq, nsplit, tps, cta0;
+    int mrow0, pad;
+    long long part0;
+};
+struct TcBatch {
+    int nreq, pad;
+    TcReq r[kMaxChunkBatch];  // in launch order (cta0 ascending)
+};
+cudaError_t launch_prefill_tc(const PoolView& pv, int layer, const TcBatch& b, int total_ctas, int merge_rows,
+                              const float* q, float* out, float* part, cudaStream_t st);
 int prefill_tc_tokens_per_cta(int group);
 int prefill_tc_stage_tiles();  // key tiles per stage of the tcgen05 prefill (a split is a whole number of them)
 size_t prefill_tc_part_floats(int q_heads, int n, int nsplit);

@@ -64,20 +64,29 @@ __global__ void gather_kernel(PoolView pv, int layer, int seq, int len, uint4* _
     }
 }
 
-// Prefill append (qwen2_model.cpp:180-200 for seq = n): one warp per
-// (token, kv head); lane l rotates dims 2l, 2l+1 with partners +64.
+// Chunk of concatenated row r and its position.
+__device__ __forceinline__ int chunk_of(const ChunkBatch& cb, int r, int& p) {
+    int i = 0;
+    while (i + 1 < cb.nreq && r >= cb.row0[i + 1]) ++i;
+    p = cb.pos0[i] + (r - cb.row0[i]);
+    return i;
+}
+
+// Prefill append (qwen2_model.cpp:180-200 for seq = n) of every chunk of the
+// batch: one warp per (row, kv head); lane l rotates dims 2l, 2l+1 with
+// partners +64.
 template <int DT>
-__global__ void append_chunk_kernel(PoolView pv, int layer, int seq, int pos0, int n,
+__global__ void append_chunk_kernel(PoolView pv, int layer, const __grid_constant__ ChunkBatch cb,
                                     const float* __restrict__ k, const float* __restrict__ v) {
     const int lane = threadIdx.x & 31;
-    const long nwarps = (long)n * pv.kv_heads;
-    const int* trow = pv.table + (size_t)seq * pv.max_blocks_per_seq;
+    const long nwarps = (long)cb.row0[cb.nreq] * pv.kv_heads;
     const size_t kvw = (size_t)pv.kv_heads * kHeadDim;
     for (long w = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5; w < nwarps;
          w += ((long)gridDim.x * blockDim.x) >> 5) {
         const int h = (int)(w % pv.kv_heads);
         const int r = (int)(w / pv.kv_heads);
-        const int p = pos0 + r;
+        int p;
+        const int* trow = pv.table + (size_t)cb.seq[chunk_of(cb, r, p)] * pv.max_blocks_per_seq;
         const float* kr = k + (size_t)r * kvw + (size_t)h * kHeadDim;
         const float* vr = v + (size_t)r * kvw + (size_t)h * kHeadDim;
         const float* cs = reinterpret_cast<const float*>(pv.rope + (size_t)p * (kHeadDim / 2));
@@ -104,17 +113,17 @@ __global__ void append_chunk_kernel(PoolView pv, int layer, int seq, int pos0, i
 // The same append into an INT8 pool: the rotated k row and the v row of each
 // (token, kv head) quantised by its warp (quant_row_warp), codes and scale
 // written to the tile.
-__global__ void append_chunk_i8_kernel(PoolView pv, int layer, int seq, int pos0, int n,
+__global__ void append_chunk_i8_kernel(PoolView pv, int layer, const __grid_constant__ ChunkBatch cb,
                                        const float* __restrict__ k, const float* __restrict__ v) {
     const int lane = threadIdx.x & 31;
-    const long nwarps = (long)n * pv.kv_heads;
-    const int* trow = pv.table + (size_t)seq * pv.max_blocks_per_seq;
+    const long nwarps = (long)cb.row0[cb.nreq] * pv.kv_heads;
     const size_t kvw = (size_t)pv.kv_heads * kHeadDim;
     for (long w = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5; w < nwarps;
          w += ((long)gridDim.x * blockDim.x) >> 5) {
         const int h = (int)(w % pv.kv_heads);
         const int r = (int)(w / pv.kv_heads);
-        const int p = pos0 + r;
+        int p;
+        const int* trow = pv.table + (size_t)cb.seq[chunk_of(cb, r, p)] * pv.max_blocks_per_seq;
         const float* kr = k + (size_t)r * kvw + (size_t)h * kHeadDim;
         const float* vr = v + (size_t)r * kvw + (size_t)h * kHeadDim;
         const float* cs = reinterpret_cast<const float*>(pv.rope + (size_t)p * (kHeadDim / 2));
@@ -265,17 +274,18 @@ cudaError_t launch_gather(const PoolView& pv, int layer, int seq, int len, uint1
     return counted(cudaGetLastError());
 }
 
-cudaError_t launch_append_chunk(const PoolView& pv, int layer, int seq, int pos0, int n,
-                                const float* k, const float* v, cudaStream_t st) {
-    if (n <= 0) return cudaSuccess;
-    const long work = (long)n * pv.kv_heads * 32;
+cudaError_t launch_append_batch(const PoolView& pv, int layer, const ChunkBatch& cb, const float* k,
+                                const float* v, cudaStream_t st) {
+    const long rows = cb.nreq > 0 ? cb.row0[cb.nreq] : 0;
+    if (rows <= 0) return cudaSuccess;
+    const long work = rows * pv.kv_heads * 32;
     const int grid = grid_for(work, 256);
     if (pv.dtype == 0)
-        append_chunk_kernel<0><<<grid, 256, 0, st>>>(pv, layer, seq, pos0, n, k, v);
+        append_chunk_kernel<0><<<grid, 256, 0, st>>>(pv, layer, cb, k, v);
     else if (pv.dtype == 1)
-        append_chunk_kernel<1><<<grid, 256, 0, st>>>(pv, layer, seq, pos0, n, k, v);
+        append_chunk_kernel<1><<<grid, 256, 0, st>>>(pv, layer, cb, k, v);
     else
-        append_chunk_i8_kernel<<<grid, 256, 0, st>>>(pv, layer, seq, pos0, n, k, v);
+        append_chunk_i8_kernel<<<grid, 256, 0, st>>>(pv, layer, cb, k, v);
     return counted(cudaGetLastError());
 }
 

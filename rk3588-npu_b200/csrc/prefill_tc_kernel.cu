@@ -5,8 +5,11 @@
 // worker/src/ops/op_attention.cpp:9-56, causal, GQA; q rotated here at
 // pos0 + s): query s attends to positions [0, pos0 + s] of the pool.
 //
-// One CTA = one KV head h, Tc = 128 / G query tokens x the G query heads of the
-// group = up to 128 rows (row r = token r / G, head r % G), one key split.
+// One launch covers the prompt chunks of up to kMaxChunkBatch sequences (their
+// rows concatenated in q and out); the host lists each chunk's CTAs, longest
+// first.  One CTA = one chunk, one KV head h, Tc = 128 / G query tokens x the
+// G query heads of the group = up to 128 rows (row r = token r / G, head
+// r % G), one key split.
 //   warps 0-7  rows: warps w and w+4 own tensor-memory lanes 32(w%4).. (rows),
 //              each half of the row's columns.  They rotate,
 //              scale and split their q row into 16-bit hi + lo halves in shared
@@ -89,15 +92,6 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
-// D[tmem] (+)= A[smem desc] * B[smem desc]
-__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                       uint32_t accumulate) {
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
 // D[tmem] (+)= A[tmem] * B[smem desc]: A (M rows x K 16-bit values) read from
 // tensor memory, lane = row, two K values per 32-bit column.
 __device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
@@ -140,16 +134,6 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&r)[32]) 
         "r"(u[9]), "r"(u[10]), "r"(u[11]), "r"(u[12]), "r"(u[13]), "r"(u[14]), "r"(u[15]), "r"(u[16]),
         "r"(u[17]), "r"(u[18]), "r"(u[19]), "r"(u[20]), "r"(u[21]), "r"(u[22]), "r"(u[23]), "r"(u[24]),
         "r"(u[25]), "r"(u[26]), "r"(u[27]), "r"(u[28]), "r"(u[29]), "r"(u[30]), "r"(u[31])
-        : "memory");
-}
-
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&r)[16]) {
-    const uint32_t* u = reinterpret_cast<const uint32_t*>(r);
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
-            taddr),
-        "r"(u[0]), "r"(u[1]), "r"(u[2]), "r"(u[3]), "r"(u[4]), "r"(u[5]), "r"(u[6]), "r"(u[7]), "r"(u[8]),
-        "r"(u[9]), "r"(u[10]), "r"(u[11]), "r"(u[12]), "r"(u[13]), "r"(u[14]), "r"(u[15])
         : "memory");
 }
 
@@ -201,18 +185,31 @@ __device__ __forceinline__ void split_p(float a, float b, uint32_t& hi, uint32_t
 
 }  // namespace
 
-// Partial row ((qhead * n + s) * nsplit + sp), kTcPartFloats floats, holds
-// o[128] (normalised), then m (base 2) and l.
+// The chunk of CTA `cta` (chunks in cta0 order).
+__device__ __forceinline__ int tc_chunk_of(const TcBatch& b, int cta) {
+    int i = 0;
+    while (i + 1 < b.nreq && cta >= b.r[i + 1].cta0) ++i;
+    return i;
+}
+
+// A chunk's partial row ((qhead * n + s) * nsplit + sp), kTcPartFloats
+// floats from its part0, holds o[128] (normalised), then m (base 2) and l.
 template <int DT>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    prefill_tc_kernel(PoolView pv, int layer, int seq, int pos0, int n, const float* __restrict__ q,
-                      float* __restrict__ out, float* __restrict__ part, int nsplit, int tiles_per_split) {
+    prefill_tc_kernel(PoolView pv, int layer, const __grid_constant__ TcBatch b, const float* __restrict__ q,
+                      float* __restrict__ out, float* __restrict__ part) {
     extern __shared__ uint8_t smem_raw[];
     TcSmem& sm = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int G = pv.group, Tc = kTcRows / G;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int h = blockIdx.y, sp = blockIdx.z;
-    const int s0 = blockIdx.x * Tc;
+    const TcReq& R = b.r[tc_chunk_of(b, (int)blockIdx.x)];
+    const int seq = R.seq, pos0 = R.pos0, n = R.n, nsplit = R.nsplit, tiles_per_split = R.tps;
+    const int local = (int)blockIdx.x - R.cta0;
+    const int h = (local / R.nq) % pv.kv_heads, sp = local / (R.nq * pv.kv_heads);
+    const int s0 = (local % R.nq) * Tc;
+    q += (size_t)R.row0 * (pv.q_heads * kHeadDim);
+    out += (size_t)R.row0 * (pv.q_heads * kHeadDim);
+    part += R.part0;
     const int s_last = min(n, s0 + Tc) - 1;
     const int ntiles = (pos0 + s_last) / kBlockTokens + 1;
     const int t_begin = sp * tiles_per_split;  // a multiple of kTcStageTiles
@@ -623,13 +620,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
 }
 
-// Merge of the key splits: one CTA per (query, 4 query heads), one thread per
-// (head, dim).
+// Merge of the key splits: one CTA per (query of a split chunk, 4 query
+// heads), one thread per (head, dim).  Merge row x belongs to the last chunk
+// whose mrow0 <= x (chunks without splits add no rows).
 __global__ void __launch_bounds__(4 * kHeadDim)
-    prefill_tc_merge_kernel(int q_heads, int n, const float* __restrict__ part, float* __restrict__ out,
-                            int nsplit) {
-    const int s = blockIdx.x, qhead = blockIdx.y * 4 + threadIdx.y, d = threadIdx.x;
+    prefill_tc_merge_kernel(int q_heads, const __grid_constant__ TcBatch b, const float* __restrict__ part,
+                            float* __restrict__ out) {
+    const int x = blockIdx.x, qhead = blockIdx.y * 4 + threadIdx.y, d = threadIdx.x;
     if (qhead >= q_heads) return;
+    int i = 0;
+    while (i + 1 < b.nreq && x >= b.r[i + 1].mrow0) ++i;
+    const TcReq& R = b.r[i];
+    const int n = R.n, nsplit = R.nsplit, s = x - R.mrow0;
+    part += R.part0;
+    out += (size_t)R.row0 * q_heads * kHeadDim;
     float M = -INFINITY, L = 0.f, A = 0.f;
     for (int sp = 0; sp < nsplit; ++sp) {
         const float* pr = part + (((size_t)qhead * n + s) * nsplit + sp) * kTcPartFloats;
@@ -653,27 +657,24 @@ size_t prefill_tc_part_floats(int q_heads, int n, int nsplit) {
     return (size_t)q_heads * n * nsplit * kTcPartFloats;
 }
 
-cudaError_t launch_prefill_tc(const PoolView& pv, int layer, int seq, int pos0, int n, const float* q,
-                              float* out, float* part, int nsplit, int tiles_per_split, cudaStream_t st) {
-    const int Tc = kTcRows / pv.group;
+cudaError_t launch_prefill_tc(const PoolView& pv, int layer, const TcBatch& b, int total_ctas, int merge_rows,
+                              const float* q, float* out, float* part, cudaStream_t st) {
+    if (total_ctas <= 0) return cudaSuccess;
     const int smem = (int)prefill_tc_smem_bytes();
-    const dim3 grid((unsigned)((n + Tc - 1) / Tc), (unsigned)pv.kv_heads, (unsigned)nsplit);
     cudaError_t e;
     if (pv.dtype == 0) {
         e = cudaFuncSetAttribute(prefill_tc_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        prefill_tc_kernel<0><<<grid, kTcThreads, smem, st>>>(pv, layer, seq, pos0, n, q, out, part, nsplit,
-                                                             tiles_per_split);
+        prefill_tc_kernel<0><<<total_ctas, kTcThreads, smem, st>>>(pv, layer, b, q, out, part);
     } else {
         e = cudaFuncSetAttribute(prefill_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        prefill_tc_kernel<1><<<grid, kTcThreads, smem, st>>>(pv, layer, seq, pos0, n, q, out, part, nsplit,
-                                                             tiles_per_split);
+        prefill_tc_kernel<1><<<total_ctas, kTcThreads, smem, st>>>(pv, layer, b, q, out, part);
     }
     e = counted(cudaGetLastError());
-    if (e != cudaSuccess || nsplit == 1) return e;
-    prefill_tc_merge_kernel<<<dim3((unsigned)n, (unsigned)((pv.q_heads + 3) / 4)), dim3(kHeadDim, 4), 0, st>>>(
-        pv.q_heads, n, part, out, nsplit);
+    if (e != cudaSuccess || merge_rows == 0) return e;
+    prefill_tc_merge_kernel<<<dim3((unsigned)merge_rows, (unsigned)((pv.q_heads + 3) / 4)), dim3(kHeadDim, 4), 0,
+                              st>>>(pv.q_heads, b, part, out);
     return counted(cudaGetLastError());
 }
 

@@ -468,6 +468,15 @@ int forward_groups(qw2_model* m, std::vector<Group>& gs) {
         QW_OK(attn_decode_plan(m->pool, nD, dseq.data(), st));
     }
     for (int i = nD; i < G; ++i) QW_OK(kvp_seq_reserve(m->pool, seq[order[i]], pos[order[i]] + gs[order[i]].n));
+    // the prompt chunks: consecutive rows from off[order[nD]], appended and
+    // attended together (shared launches)
+    std::vector<int> cseq, cpos, cn;
+    for (int i = nD; i < G; ++i) {
+        cseq.push_back(seq[order[i]]);
+        cpos.push_back(pos[order[i]]);
+        cn.push_back(gs[order[i]].n);
+    }
+    const size_t crow = nD < G ? (size_t)off[order[nD]] : 0;
 
     for (int li = 0; li < c.layers; ++li) {
         const qw2_model::Layer& Ly = m->L[li];
@@ -489,12 +498,12 @@ int forward_groups(qw2_model* m, std::vector<Group>& gs) {
         QW_CUDA(launch_gemv(0, 2, a, st));
         // 3-5: RoPE, KV append, attention
         if (nD) QW_OK(attn_decode_append(m->pool, li, m->q, m->k, m->v, m->attn, st));
-        for (int i = nD; i < G; ++i) {
-            const int g = order[i], o = off[g];
-            QW_OK(kv_append_chunk(m->pool, li, seq[g], pos[g], gs[g].n, m->k + (size_t)o * kvd,
-                                  m->v + (size_t)o * kvd, st));
-            QW_OK(attn_prefill(m->pool, li, seq[g], pos[g], gs[g].n, m->q + (size_t)o * H, m->attn + (size_t)o * H,
-                               st));
+        if (nD < G) {
+            const int nc = G - nD;
+            QW_OK(kv_append_chunk_batch(m->pool, li, nc, cseq.data(), cpos.data(), cn.data(), m->k + crow * kvd,
+                                        m->v + crow * kvd, st));
+            QW_OK(attn_prefill_batch(m->pool, li, nc, cseq.data(), cpos.data(), cn.data(), m->q + crow * H,
+                                     m->attn + crow * H, st));
         }
         // 6-7: O projection + residual
         GemvArgs o;

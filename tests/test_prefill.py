@@ -111,3 +111,97 @@ def test_prefill_rejects_bad_calls():
     with pytest.raises(kv.KVError) as e:
         kv.call("attn_prefill", P.h, 0, s + 1, 0, 4, 16, 16, None)
     assert e.value.status == kv.KV_ERR_BADSEQ
+
+
+def run_batch(kv, orc, ctx, chunks, dtype, seed, qh=12, kvh=2):
+    """Every sequence i holds ctx[i] imported tokens, then one batched append +
+    attention of chunks[i] tokens per sequence; each against the oracle."""
+    rng = np.random.default_rng(seed)
+    kvd, hid = kvh * HD, qh * HD
+    nseq = len(ctx)
+    nb = sum(-(-(c + n) // 16) for c, n in zip(ctx, chunks)) + 8
+    P = kv.Pool(0, 1, nb, num_q_heads=qh, num_kv_heads=kvh, dtype=dtype, max_seqs=nseq,
+                max_seq_len=max(c + n for c, n in zip(ctx, chunks)) + 16)
+    ids, caches = [], []
+    for c, n in zip(ctx, chunks):
+        s = P.seq_alloc()
+        P.reserve(s, c + n)
+        kc = np.zeros((c + n, kvd), np.uint16)
+        vc = np.zeros((c + n, kvd), np.uint16)
+        if c:
+            kc[:c] = orc.encode(rng.standard_normal((c, kvd)).astype(np.float32), dtype)
+            vc[:c] = orc.encode(rng.standard_normal((c, kvd)).astype(np.float32), dtype)
+            P.import_rows(0, s, 0, torch.from_numpy(kc[:c].view(np.int16)).cuda(),
+                          torch.from_numpy(vc[:c].view(np.int16)).cuda())
+        P.set_cur_pos(s, c)
+        ids.append(s)
+        caches.append((kc, vc))
+    R = sum(chunks)
+    q = rng.standard_normal((R, hid)).astype(np.float32)
+    k = rng.standard_normal((R, kvd)).astype(np.float32)
+    v = rng.standard_normal((R, kvd)).astype(np.float32)
+    out = torch.full((R, hid), float("nan"), device="cuda")
+    P.append_chunk_batch(0, ids, ctx, torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda(), ns=chunks)
+    P.prefill_batch(0, ids, ctx, chunks, torch.from_numpy(q).cuda(), out)
+    got = out.cpu().numpy()
+    worst, r0 = 0.0, 0
+    for i, (c, n) in enumerate(zip(ctx, chunks)):
+        kc, vc = caches[i]
+        if n:
+            ref, _, _ = orc.layer_step(q[r0:r0 + n], k[r0:r0 + n], v[r0:r0 + n], kc, vc, c, qh, kvh, HD, 1e6, dtype)
+            worst = max(worst, rel_err(got[r0:r0 + n], ref))
+        P.set_cur_pos(ids[i], c + n)
+        kd, vd = P.gather(0, ids[i])
+        assert np.array_equal(kd.cpu().numpy().view(np.uint16), kc[:c + n])
+        assert np.array_equal(vd.cpu().numpy().view(np.uint16), vc[:c + n])
+        r0 += n
+    assert P.device_status() == 0
+    P.close()
+    return worst
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [0, 1], ids=["f16", "bf16"])
+def test_prefill_batch_mixed_chunks(kv, orc, dtype):
+    """One launch over ragged chunks and contexts: a chunk at position 0, a
+    one-token chunk, an empty chunk, 512-token chunks after long contexts
+    (split and unsplit in the same launch)."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    ctx = [0, 37, 2000, 5000, 16, 700, 3000]
+    chunks = [100, 1, 512, 512, 0, 33, 512]
+    assert run_batch(kv, orc, ctx, chunks, dtype, seed=10 + dtype) <= TOL
+
+
+@pytest.mark.gpu
+def test_prefill_batch_more_chunks_than_one_launch(kv, orc):
+    """40 chunks: two launches of at most 32 chunks each."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    rng = np.random.default_rng(12)
+    ctx = [int(x) for x in rng.integers(0, 300, 40)]
+    chunks = [int(x) for x in rng.integers(1, 40, 40)]
+    assert run_batch(kv, orc, ctx, chunks, 1, seed=12) <= TOL
+
+
+def test_prefill_batch_rejects_bad_calls():
+    kv = load_pkg()
+    P = kv.Pool(kv.KVP_HOST_ONLY, 1, 8, max_seqs=2, max_seq_len=128)
+    a, b = P.seq_alloc(), P.seq_alloc()
+    P.reserve(a, 32)
+    P.reserve(b, 32)
+    ints = kv._ints
+    for fn in ("attn_prefill_batch", "kv_append_chunk_batch"):
+        with pytest.raises(kv.KVError) as e:  # no device storage
+            kv.call(fn, P.h, 0, 2, ints([a, b]), ints([0, 0]), ints([4, 4]), 16, 16, None)
+        assert e.value.status == kv.KV_ERR_STATE
+        with pytest.raises(kv.KVError) as e:  # a dead sequence
+            kv.call(fn, P.h, 0, 2, ints([b + 1, a]), ints([0, 0]), ints([4, 4]), 16, 16, None)
+        assert e.value.status == kv.KV_ERR_BADSEQ
+        with pytest.raises(kv.KVError) as e:  # the same sequence twice
+            kv.call(fn, P.h, 0, 2, ints([a, a]), ints([0, 4]), ints([4, 4]), 16, 16, None)
+        assert e.value.status in (kv.KV_ERR_STATE, kv.KV_ERR_INVAL)
+        with pytest.raises(kv.KVError) as e:  # past the reserved blocks
+            kv.call(fn, P.h, 0, 1, ints([b]), ints([30]), ints([4]), 16, 16, None)
+        assert e.value.status in (kv.KV_ERR_STATE, kv.KV_ERR_RANGE)
+    P.close()
