@@ -742,14 +742,16 @@ def run_serve(args, rank, world, local):
     kb = torch.randn((NL, maxrows, KVD), generator=gq, device="cuda")
     vb = torch.randn((NL, maxrows, KVD), generator=gq, device="cuda")
     ob = torch.empty((NL, maxrows, HID), device="cuda")
-    kp = torch.randn((NL, 512, KVD), generator=gq, device="cuda")
-    vp = torch.randn((NL, 512, KVD), generator=gq, device="cuda")
+    # prompt-chunk rows of all prefilling requests (8 slots x 512), concatenated
+    kp = torch.randn((NL, 8 * 512, KVD), generator=gq, device="cuda")
+    vp = torch.randn((NL, 8 * 512, KVD), generator=gq, device="cuda")
 
     def decode_io(layer, reqs):
         n = len(reqs)
         return qb[layer, :n], kb[layer, :n], vb[layer, :n], ob[layer, :n]
 
-    def prefill_kv(layer, req, pos0, n):
+    def prefill_kv(layer, chunks):  # every local chunk at once (kv_append_chunk_batch)
+        n = sum(c for _, _, c in chunks)
         return kp[layer, :n], vp[layer, :n]
 
     torch.cuda.synchronize()
@@ -757,17 +759,17 @@ def run_serve(args, rank, world, local):
     if sampler:
         sampler.start()
     for _ in range(W):
-        srv.step(decode_io, prefill_kv)
+        srv.step(decode_io, prefill_batch_io=prefill_kv)
     # ~settle seconds more of untimed steps (the same count on every rank)
     torch.cuda.synchronize()
     t0 = time.time()
-    srv.step(decode_io, prefill_kv)
+    srv.step(decode_io, prefill_batch_io=prefill_kv)
     torch.cuda.synchronize()
     n_settle = torch.tensor([int(args.settle / max(time.time() - t0, 1e-4))], device="cuda")
     if dist:
         dist.all_reduce(n_settle, op=dist.ReduceOp.MIN)
     for _ in range(int(n_settle.item())):
-        srv.step(decode_io, prefill_kv)
+        srv.step(decode_io, prefill_batch_io=prefill_kv)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     alg = 0.0
     dec_tokens = pre_tokens = completed = 0
@@ -781,7 +783,7 @@ def run_serve(args, rank, world, local):
         alg += NL * step_bytes([r.length + 1 for r in mine]) if mine else 0.0
         e0, e1 = ev[i]
         e0.record()
-        c = srv.step(decode_io, prefill_kv)
+        c = srv.step(decode_io, prefill_batch_io=prefill_kv)
         e1.record()
         dec_tokens += c["decode_tokens"]
         pre_tokens += c["prefill_tokens"]

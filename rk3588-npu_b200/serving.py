@@ -105,7 +105,7 @@ class Server:
     def local_decode(self) -> list[Request]:
         return [r for r in self.decoding if r.gpu == self.rank]
 
-    def step(self, decode_io=None, prefill_kv=None) -> dict:
+    def step(self, decode_io=None, prefill_kv=None, prefill_batch_io=None) -> dict:
         """One engine step on this rank.
 
         decode_io(layer, reqs) -> (q [n, hidden], k [n, kv_dim], v [n, kv_dim],
@@ -114,7 +114,12 @@ class Server:
         prefill_kv(layer, req, pos0, n) -> (k [n, kv_dim], v [n, kv_dim]) device
             fp32 for one prompt chunk, or (k, v, q [n, hidden], out [n, hidden])
             to also run the chunk's causal attention (attn_prefill) after its
-            append.
+            append;
+        prefill_batch_io(layer, chunks) -> the same for all of this rank's
+            chunks [(req, pos0, n), ...] at once, rows concatenated in that
+            order: appended (and attended) with kv_append_chunk_batch /
+            attn_prefill_batch in shared launches.  Used instead of prefill_kv
+            when given.
         Returns the step's global counts (every rank returns the same)."""
         self.admit()
         dec = self.local_decode()
@@ -129,6 +134,15 @@ class Server:
                 if dec:
                     q, k, v, out = decode_io(layer, dec)
                     self.pool.decode_layer(layer, q, k, v, out)
+                if prefill_batch_io is not None and local_chunks:
+                    seqs = [r.seq for r, _ in local_chunks]
+                    pos0 = [r.filled for r, _ in local_chunks]
+                    ns = [c for _, c in local_chunks]
+                    io = prefill_batch_io(layer, [(r, r.filled, c) for r, c in local_chunks])
+                    self.pool.append_chunk_batch(layer, seqs, pos0, io[0], io[1], ns=ns)
+                    if len(io) == 4:
+                        self.pool.prefill_batch(layer, seqs, pos0, ns, io[2], io[3])
+                    continue
                 for r, c in local_chunks:
                     io = prefill_kv(layer, r, r.filled, c)
                     self.pool.append_chunk(layer, r.seq, r.filled, io[0], io[1])

@@ -108,7 +108,11 @@ def test_admission_waits_for_room():
 
 # ------------------------------------------------------------------- GPU
 @pytest.mark.gpu
-def test_serving_gpu_matches_oracle_with_block_reuse():
+@pytest.mark.parametrize("batched", [False, True], ids=["per_request", "batched_prefill"])
+def test_serving_gpu_matches_oracle_with_block_reuse(batched):
+    """batched: the step's prompt chunks go through kv_append_chunk_batch +
+    attn_prefill_batch (Server.step's prefill_batch_io) instead of one call
+    per request."""
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     import sys
@@ -171,6 +175,18 @@ def test_serving_gpu_matches_oracle_with_block_reuse():
         prefill_checks.append((out, ref))
         return (torch.from_numpy(kh).cuda(), torch.from_numpy(vh).cuda(), torch.from_numpy(qh).cuda(), out)
 
+    def prefill_batch_io(layer, chunks):
+        """All chunks' rows concatenated; each chunk's slice of the shared
+        output is checked against its oracle step."""
+        parts = [prefill_kv(layer, r, p0, n) for r, p0, n in chunks]
+        out = torch.empty((sum(n for _, _, n in chunks), hid), device="cuda")
+        first, o = len(prefill_checks) - len(chunks), 0
+        for i, (_, _, n) in enumerate(chunks):
+            prefill_checks[first + i] = (out[o:o + n], prefill_checks[first + i][1])
+            o += n
+        return (torch.cat([p[0] for p in parts]), torch.cat([p[1] for p in parts]),
+                torch.cat([p[2] for p in parts]), out)
+
     reused = False
     for step in range(200):
         if not (srv.queue or srv.prefilling or srv.decoding):
@@ -178,7 +194,10 @@ def test_serving_gpu_matches_oracle_with_block_reuse():
         before = {r.rid: r.length for r in srv.decoding}
         state.clear()
         prefill_checks.clear()
-        srv.step(decode_io, prefill_kv)
+        if batched:
+            srv.step(decode_io, prefill_batch_io=prefill_batch_io)
+        else:
+            srv.step(decode_io, prefill_kv)
         reused = reused or bool(srv.finished and (srv.prefilling or srv.decoding))
         for out, ref in prefill_checks:  # chunk attention against the oracle
             g = out.cpu().numpy().reshape(-1, 128).astype(np.float64)
