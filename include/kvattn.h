@@ -56,8 +56,9 @@ enum kv_status {
  * (docs/work_division.md:72): per (token, KV head) row of 128 values one fp32
  * scale = max|x| / 127 and codes round-half-away(x / scale) in [-127, 127];
  * attention reads code * scale.  INT8 pools serve the decode path
- * (attn_decode_*, kv_append_chunk, kvp_import_i8 / kvp_gather_i8); the
- * prefill attention and the 16-bit import / gather reject them. */
+ * (attn_decode_*), the prompt path (kv_append_chunk(_batch), and
+ * attn_prefill(_batch) / attn_prefill_mma on the mma.sync prefill kernel)
+ * and kvp_import_i8 / kvp_gather_i8; the 16-bit import / gather reject them. */
 enum kv_dtype { KV_F16 = 0, KV_BF16 = 1, KV_I8 = 2 };
 
 /* Pass as `device` to kvp_create for a bookkeeping-only pool: allocator,

@@ -809,11 +809,30 @@ int prefill_checks(kvp_pool* p, int layer, int seq, int pos0, int n, const float
                    cudaStream_t st) {
     int rc = chunk_check(p, layer, seq, pos0, n, true);
     if (rc) return rc;
-    if (p->dtype == KV_I8) return fail(KV_ERR_INVAL, "prefill attention reads 16-bit caches; INT8 pools decode only");
     if (n == 0) return KV_OK;
     if (!q || !out || ((uintptr_t)q & 15) || ((uintptr_t)out & 15))
         return fail(KV_ERR_INVAL, "q and out must be 16-byte aligned");
     return sync_table(p, st);
+}
+
+// One chunk on the mma.sync kernel (checked, table on the device): key
+// splits for about two CTAs per SM, at least 16 tiles (256 keys) per split.
+int prefill_mma_launch(kvp_pool* p, int layer, int seq, int pos0, int n, const float* q, float* out,
+                       cudaStream_t st) {
+    if (n == 0) return KV_OK;
+    const int nqb = (n + 15) / 16;
+    const int max_tiles = (pos0 + n - 1) / kBlockTokens + 1;
+    const long ctas = (long)nqb * p->kv_heads;
+    int nsplit = (int)std::min<long>((2L * p->num_sms + ctas - 1) / ctas, (max_tiles + 15) / 16);
+    nsplit = std::max(nsplit, 1);
+    const int tps = (max_tiles + nsplit - 1) / nsplit;
+    nsplit = (max_tiles + tps - 1) / tps;
+    if (nsplit > 1) {
+        int rc = prefill_part_reserve(p, (size_t)p->q_heads * nqb * 16 * nsplit * (2 + kHeadDim), st);
+        if (rc) return rc;
+    }
+    KV_CUDA(launch_prefill(p->pv, layer, seq, pos0, n, q, out, p->d_prefill_part, nsplit, tps, st));
+    return KV_OK;
 }
 
 // Key splits of the chunks of one tcgen05 launch.  Every CTA is resident
@@ -921,7 +940,9 @@ int prefill_tc_launch(kvp_pool* p, int layer, const int* seqs, const int* pos0, 
 }  // namespace
 
 // Tensor-core (tcgen05) version over several chunks: one launch (plus one
-// merge launch when a chunk is split) per kMaxChunkBatch chunks.
+// merge launch when a chunk is split) per kMaxChunkBatch chunks.  An INT8
+// pool runs each chunk on the mma.sync kernel (codes expanded to fp16 in
+// shared memory, scales applied to scores and weights).
 int attn_prefill_batch(kvp_pool* p, int layer, int nreq, const int* seqs, const int* pos0, const int* ns,
                        const float* q, float* out, void* stream) {
     if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
@@ -929,7 +950,6 @@ int attn_prefill_batch(kvp_pool* p, int layer, int nreq, const int* seqs, const 
     long rows = 0;
     int rc = batch_check(p, layer, nreq, seqs, pos0, ns, &rows);
     if (rc) return rc;
-    if (p->dtype == KV_I8) return fail(KV_ERR_INVAL, "prefill attention reads 16-bit caches; INT8 pools decode only");
     if (rows == 0) return KV_OK;
     if (!q || !out || ((uintptr_t)q & 15) || ((uintptr_t)out & 15))
         return fail(KV_ERR_INVAL, "q and out must be 16-byte aligned");
@@ -938,6 +958,15 @@ int attn_prefill_batch(kvp_pool* p, int layer, int nreq, const int* seqs, const 
     rc = sync_table(p, st);
     if (rc) return rc;
     long base = 0;
+    if (p->dtype == KV_I8) {
+        const size_t qw = (size_t)p->q_heads * kHeadDim;
+        for (int i = 0; i < nreq; ++i) {
+            rc = prefill_mma_launch(p, layer, seqs[i], pos0[i], ns[i], q + base * qw, out + base * qw, st);
+            if (rc) return rc;
+            base += ns[i];
+        }
+        return KV_OK;
+    }
     for (int b0 = 0; b0 < nreq; b0 += kMaxChunkBatch) {
         const int b1 = std::min(nreq, b0 + kMaxChunkBatch);
         rc = prefill_tc_launch(p, layer, seqs, pos0, ns, b0, b1, base, q, out, st);
@@ -961,21 +990,7 @@ int attn_prefill_mma(kvp_pool* p, int layer, int seq, int pos0, int n, const flo
     cudaStream_t st = (cudaStream_t)stream;
     int rc = prefill_checks(p, layer, seq, pos0, n, q, out, st);
     if (rc || n == 0) return rc;
-    // Key splits: enough CTAs for two per SM, at least 16 tiles (256 keys)
-    // per split.
-    const int nqb = (n + 15) / 16;
-    const int max_tiles = (pos0 + n - 1) / kBlockTokens + 1;
-    const long ctas = (long)nqb * p->kv_heads;
-    int nsplit = (int)std::min<long>((2L * p->num_sms + ctas - 1) / ctas, (max_tiles + 15) / 16);
-    nsplit = std::max(nsplit, 1);
-    const int tps = (max_tiles + nsplit - 1) / nsplit;
-    nsplit = (max_tiles + tps - 1) / tps;
-    if (nsplit > 1) {
-        rc = prefill_part_reserve(p, (size_t)p->q_heads * nqb * 16 * nsplit * (2 + kHeadDim), st);
-        if (rc) return rc;
-    }
-    KV_CUDA(launch_prefill(p->pv, layer, seq, pos0, n, q, out, p->d_prefill_part, nsplit, tps, st));
-    return KV_OK;
+    return prefill_mma_launch(p, layer, seq, pos0, n, q, out, st);
 }
 
 int attn_decode_plan_ex(kvp_pool* p, int nseq, const int* seq_ids, const int* rope_pos,

@@ -22,6 +22,14 @@
 // A split of the key range writes partial (m, l, o) per (query, head); a
 // merge kernel combines the splits.  Tensor-core bound for long contexts;
 // this mma.sync version is the baseline for a tcgen05 one.
+//
+// INT8 caches (DT 2): the producer copies the two compact tiles (codes +
+// per-row scales); the consumer warps expand them together into one 16-bit
+// tile pair per ring stage (codes are exact in fp16), each warp its share,
+// and meet at a named barrier.  Scores are multiplied by the key's K scale
+// and the softmax weights by the key's V scale on their way into P*V (the
+// row sums keep the unscaled weights): attention over code * scale, as the
+// decode kernel computes it.
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -38,8 +46,12 @@ constexpr int kPStages = 4;                   // ring stages (K + V tile each)
 constexpr int kPStageBytes = 2 * kTileBytes;
 constexpr long long kPWaitLimit = 4000000000LL;  // SM clocks before a wait gives up
 
+template <int DT>
 struct PrefillSmem {
+    static constexpr int kWide = DT == 2 ? kPStages : 1;  // expanded stages (INT8 only)
     alignas(1024) uint8_t stage[kPStages][kPStageBytes];
+    alignas(1024) uint8_t wide[kWide][DT == 2 ? kPStageBytes : 16];
+    float scales[kWide][2][kBlockTokens];  // INT8: K and V scales of the stage's 16 keys
     uint64_t full[kPStages];
     uint64_t empty[kPStages];
 };
@@ -95,8 +107,11 @@ template <int DT>
 __global__ void __launch_bounds__(9 * 32, 1)
     prefill_kernel(PoolView pv, int layer, int seq, int pos0, int n, const float* __restrict__ q,
                    float* __restrict__ out, float* __restrict__ part, int nsplit, int tiles_per_split) {
+    constexpr int MT = DT == 1 ? 1 : 0;  // operand type: bf16 for bf16 caches, else fp16
+    constexpr int TB = DT == 2 ? kTileBytesI8 : kTileBytes;  // bytes of one K or V tile in HBM
     extern __shared__ uint8_t smem_raw[];
-    PrefillSmem& sm = *reinterpret_cast<PrefillSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    PrefillSmem<DT>& sm =
+        *reinterpret_cast<PrefillSmem<DT>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int G = pv.group;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int qb = blockIdx.x, h = blockIdx.y, sp = blockIdx.z;
@@ -137,10 +152,10 @@ __global__ void __launch_bounds__(9 * 32, 1)
                     }
                     mbar_arrive(&sm.full[s]);  // nothing loaded: the outputs are void, the status says so
                 } else {
-                    const size_t off = (size_t)layer * pv.layer_bytes + ((size_t)blk * pv.kv_heads + h) * kTileBytes;
-                    mbar_arrive_expect_tx(&sm.full[s], kPStageBytes);
-                    bulk_g2s_hint(sm.stage[s], pv.k + off, kTileBytes, &sm.full[s], policy);
-                    bulk_g2s_hint(sm.stage[s] + kTileBytes, pv.v + off, kTileBytes, &sm.full[s], policy);
+                    const size_t off = (size_t)layer * pv.layer_bytes + ((size_t)blk * pv.kv_heads + h) * TB;
+                    mbar_arrive_expect_tx(&sm.full[s], 2 * TB);
+                    bulk_g2s_hint(sm.stage[s], pv.k + off, TB, &sm.full[s], policy);
+                    bulk_g2s_hint(sm.stage[s] + TB, pv.v + off, TB, &sm.full[s], policy);
                 }
                 ++issued;
             }
@@ -157,7 +172,7 @@ __global__ void __launch_bounds__(9 * 32, 1)
     const int r = lane >> 2, c = lane & 3;
     const float qscale = 0.08838834764831845f * 1.4426950408889634f;  // 1/sqrt(128) * log2(e)
     uint32_t qh[8][4], ql[8][4];
-    load_q_rows<DT>(pv, q, s0, n, pos0, qhead, qscale, lane, qh, ql);
+    load_q_rows<MT>(pv, q, s0, n, pos0, qhead, qscale, lane, qh, ql);
     const int p0 = pos0 + s0 + r, p1 = p0 + 8;                // absolute positions of rows r, r+8
     float m2[2] = {-INFINITY, -INFINITY}, lsum[2] = {0.f, 0.f};
     float o[16][4];
@@ -165,17 +180,51 @@ __global__ void __launch_bounds__(9 * 32, 1)
     for (int nt = 0; nt < 16; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
     const int mi = lane >> 3, rr = lane & 7;
 
+    bool dead = false;  // INT8: a wait gave up; the warp keeps meeting the others at the barrier
     for (int t = t_begin; t < t_end; ++t) {
         const int k = t - t_begin, s = k % kPStages;
-        if (!mbar_wait_bounded(&sm.full[s], (k / kPStages) & 1, kPWaitLimit)) {
+        if (!dead && !mbar_wait_bounded(&sm.full[s], (k / kPStages) & 1, kPWaitLimit)) {
             if (atomicCAS(pv.status, 0, KV_ERR_TIMEOUT) == 0) {
                 pv.status[1] = qb;
                 pv.status[2] = 602;
             }
-            break;
+            if (DT != 2) break;
+            dead = true;
         }
-        const uint32_t sK = smem_u32(sm.stage[s]);
-        const uint32_t sV = sK + kTileBytes;
+        uint32_t sK = smem_u32(sm.stage[s]);
+        uint32_t sV = sK + kTileBytes;
+        float ksc[2][2] = {{1.f, 1.f}, {1.f, 1.f}}, vsc[2][2] = {{1.f, 1.f}, {1.f, 1.f}};  // keys 8j + 2c + e
+        if constexpr (DT == 2) {
+            // this warp's share of the two compact tiles into the stage's 16-bit pair
+            const uint8_t* cK = sm.stage[s];
+            uint8_t* wK = sm.wide[s];
+            if (!dead) {
+                for (int x = g * 32 + lane; x < 2 * kBlockTokens * 16; x += G * 32) {
+                    const int which = x >> 8, y = x & 255, tt = y >> 4, ch = y & 15;
+                    const uint2 raw = *reinterpret_cast<const uint2*>(cK + which * TB + tt * kHeadDim + ch * 8);
+                    const int8_t* cc = reinterpret_cast<const int8_t*>(&raw);
+                    *reinterpret_cast<uint4*>(wK + which * kTileBytes + tile_offset(tt, ch * 8)) =
+                        make_uint4(codes_to_half2(cc[0], cc[1]), codes_to_half2(cc[2], cc[3]),
+                                   codes_to_half2(cc[4], cc[5]), codes_to_half2(cc[6], cc[7]));
+                }
+                if (g == 0)  // lanes 0-15 the K scales, 16-31 the V scales
+                    sm.scales[s][lane >> 4][lane & 15] =
+                        reinterpret_cast<const float*>(cK + (lane >> 4) * TB + kBlockTokens * kHeadDim)[lane & 15];
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.empty[s]);  // the compact stage is no longer read
+            named_bar_sync(1, G * 32);                  // every share expanded
+            if (dead) continue;
+            sK = smem_u32(wK);
+            sV = sK + kTileBytes;
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    ksc[j][e] = sm.scales[s][0][8 * j + 2 * c + e];
+                    vsc[j][e] = sm.scales[s][1][8 * j + 2 * c + e];
+                }
+        }
         // ---- S[16 q][16 keys] = Q K^T ----
         float sc[2][4] = {};
         {
@@ -187,10 +236,19 @@ __global__ void __launch_bounds__(9 * 32, 1)
                 const uint32_t addr = rowb + (uint32_t)(cidx >> 3) * 2048u + (uint32_t)(((cidx & 7) ^ rr) << 4);
                 uint32_t b00, b01, b10, b11;
                 ldsm_x4(addr, b00, b01, b10, b11);
-                mma_a4<DT>(sc[0], qh[kk], b00, b01);
-                mma_a4<DT>(sc[1], qh[kk], b10, b11);
-                mma_a4<DT>(sc[0], ql[kk], b00, b01);
-                mma_a4<DT>(sc[1], ql[kk], b10, b11);
+                mma_a4<MT>(sc[0], qh[kk], b00, b01);
+                mma_a4<MT>(sc[1], qh[kk], b10, b11);
+                mma_a4<MT>(sc[0], ql[kk], b00, b01);
+                mma_a4<MT>(sc[1], ql[kk], b10, b11);
+            }
+        }
+        if constexpr (DT == 2) {  // scores of codes times the key's K scale
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                sc[j][0] *= ksc[j][0];
+                sc[j][1] *= ksc[j][1];
+                sc[j][2] *= ksc[j][0];
+                sc[j][3] *= ksc[j][1];
             }
         }
         // causal mask (and keys past the context of the last query)
@@ -235,11 +293,20 @@ __global__ void __launch_bounds__(9 * 32, 1)
         }
         // P as the A operand: regs (row r, keys 2c..), (row r+8, keys 2c..),
         // (row r, keys 8+2c..), (row r+8, keys 8+2c..)
+        if constexpr (DT == 2) {  // weights times the key's V scale (masked keys stay exactly 0)
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                pv_[j][0] = pv_[j][0] > 0.f ? pv_[j][0] * vsc[j][0] : 0.f;
+                pv_[j][1] = pv_[j][1] > 0.f ? pv_[j][1] * vsc[j][1] : 0.f;
+                pv_[j][2] = pv_[j][2] > 0.f ? pv_[j][2] * vsc[j][0] : 0.f;
+                pv_[j][3] = pv_[j][3] > 0.f ? pv_[j][3] * vsc[j][1] : 0.f;
+            }
+        }
         uint32_t ph[4], pl[4];
-        split_pair<DT>(pv_[0][0], pv_[0][1], ph[0], pl[0]);
-        split_pair<DT>(pv_[0][2], pv_[0][3], ph[1], pl[1]);
-        split_pair<DT>(pv_[1][0], pv_[1][1], ph[2], pl[2]);
-        split_pair<DT>(pv_[1][2], pv_[1][3], ph[3], pl[3]);
+        split_pair<MT>(pv_[0][0], pv_[0][1], ph[0], pl[0]);
+        split_pair<MT>(pv_[0][2], pv_[0][3], ph[1], pl[1]);
+        split_pair<MT>(pv_[1][0], pv_[1][1], ph[2], pl[2]);
+        split_pair<MT>(pv_[1][2], pv_[1][3], ph[3], pl[3]);
         // ---- O[16 q][128] += P V ----
         {
             const int key = (mi & 1) * 8 + rr;
@@ -250,14 +317,14 @@ __global__ void __launch_bounds__(9 * 32, 1)
                 const uint32_t addr = rowb + (uint32_t)(cidx >> 3) * 2048u + (uint32_t)(((cidx & 7) ^ rr) << 4);
                 uint32_t b0a, b1a, b0b, b1b;  // dims 16m..16m+7 (a) and 16m+8.. (b)
                 ldsm_x4_t(addr, b0a, b1a, b0b, b1b);
-                mma_a4<DT>(o[2 * m], ph, b0a, b1a);
-                mma_a4<DT>(o[2 * m + 1], ph, b0b, b1b);
-                mma_a4<DT>(o[2 * m], pl, b0a, b1a);
-                mma_a4<DT>(o[2 * m + 1], pl, b0b, b1b);
+                mma_a4<MT>(o[2 * m], ph, b0a, b1a);
+                mma_a4<MT>(o[2 * m + 1], ph, b0b, b1b);
+                mma_a4<MT>(o[2 * m], pl, b0a, b1a);
+                mma_a4<MT>(o[2 * m + 1], pl, b0b, b1b);
             }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.empty[s]);
+        if (DT != 2 && lane == 0) mbar_arrive(&sm.empty[s]);
     }
 
     // ---- row sums across the quad, then outputs or partials ----
@@ -317,21 +384,26 @@ __global__ void __launch_bounds__(kHeadDim)
     out[(size_t)s * pv.q_heads * kHeadDim + (size_t)qhead * kHeadDim + d] = L > 0.f ? A / L : 0.f;
 }
 
-size_t prefill_smem_bytes() { return sizeof(PrefillSmem) + 1024; }
 
 cudaError_t launch_prefill(const PoolView& pv, int layer, int seq, int pos0, int n, const float* q,
                            float* out, float* part, int nsplit, int tiles_per_split, cudaStream_t st) {
     const int nqb = (n + 15) / 16;
-    const int smem = (int)prefill_smem_bytes();
     const dim3 grid((unsigned)nqb, (unsigned)pv.kv_heads, (unsigned)nsplit);
     const int threads = (pv.group + 1) * 32;
     if (pv.dtype == 0) {
+        const int smem = (int)sizeof(PrefillSmem<0>) + 1024;
         cudaFuncSetAttribute(prefill_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         prefill_kernel<0><<<grid, threads, smem, st>>>(pv, layer, seq, pos0, n, q, out, part, nsplit,
                                                        tiles_per_split);
-    } else {
+    } else if (pv.dtype == 1) {
+        const int smem = (int)sizeof(PrefillSmem<1>) + 1024;
         cudaFuncSetAttribute(prefill_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         prefill_kernel<1><<<grid, threads, smem, st>>>(pv, layer, seq, pos0, n, q, out, part, nsplit,
+                                                       tiles_per_split);
+    } else {
+        const int smem = (int)sizeof(PrefillSmem<2>) + 1024;
+        cudaFuncSetAttribute(prefill_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        prefill_kernel<2><<<grid, threads, smem, st>>>(pv, layer, seq, pos0, n, q, out, part, nsplit,
                                                        tiles_per_split);
     }
     cudaError_t e = counted(cudaGetLastError());
