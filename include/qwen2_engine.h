@@ -118,6 +118,14 @@ int qw2_kv_pool(qw2_model* m, kvp_pool** pool);
  * one qw2_forward / qw2_generate / qw2_reset use), qw2_create_sessions's has
  * up to max_sessions, all sharing the weights. */
 int qw2_create_sessions(int device, const qw2_config* cfg, int max_sessions, qw2_model** out);
+/* The same with the KV cache in another element type: KV_F16 (the
+ * reference's KVCache, what qw2_create_sessions uses), KV_BF16, or KV_I8 --
+ * the INT8 compression the reference plans (docs/work_division.md:72; the
+ * scheme of kvattn.h), a quarter of the fp16 cache's bytes per token plus
+ * one fp32 scale per (token, KV head) row.  The prompt and decode paths are
+ * the same calls; only the cache changes, so the logits move by the
+ * quantisation error. */
+int qw2_create_kv(int device, const qw2_config* cfg, int max_sessions, int kv_dtype, qw2_model** out);
 int qw2_session_create(qw2_model* m, int* session);
 int qw2_session_destroy(qw2_model* m, int session);
 int qw2_session_exists(const qw2_model* m, int session, int* exists);

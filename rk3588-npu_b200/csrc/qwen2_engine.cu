@@ -804,10 +804,12 @@ int qw2_destroy(qw2_model* m) {
     return KV_OK;
 }
 
-int qw2_create_sessions(int device, const qw2_config* cfg, int max_sessions, qw2_model** out) {
+int qw2_create_kv(int device, const qw2_config* cfg, int max_sessions, int kv_dtype, qw2_model** out) {
     if (!out) return qfail(KV_ERR_INVAL, "NULL out");
     *out = nullptr;
     QW_OK(check_cfg(cfg));
+    if (kv_dtype != KV_F16 && kv_dtype != KV_BF16 && kv_dtype != KV_I8)
+        return qfail(KV_ERR_INVAL, "KV cache type %d is not KV_F16, KV_BF16 or KV_I8", kv_dtype);
     if (max_sessions < 1 || max_sessions > 1024) return qfail(KV_ERR_INVAL, "max_sessions %d outside [1, 1024]", max_sessions);
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
@@ -861,7 +863,7 @@ int qw2_create_sessions(int device, const qw2_config* cfg, int max_sessions, qw2
     if (rc == KV_OK) {
         const int blocks = max_sessions * ((cfg->max_position + kBlockTokens - 1) / kBlockTokens);
         step(kvp_create(device, cfg->layers, cfg->q_heads, cfg->kv_heads, cfg->head_dim, kBlockTokens, blocks,
-                        KV_F16, max_sessions, cfg->max_position, cfg->rope_theta, &m->pool));
+                        kv_dtype, max_sessions, cfg->max_position, cfg->rope_theta, &m->pool));
     }
     // every forward ends with a host synchronisation, so no decode launch
     // overlaps a kernel that writes the cache (kvp_set_overlap's contract)
@@ -874,6 +876,10 @@ int qw2_create_sessions(int device, const qw2_config* cfg, int max_sessions, qw2
     }
     *out = m;
     return KV_OK;
+}
+
+int qw2_create_sessions(int device, const qw2_config* cfg, int max_sessions, qw2_model** out) {
+    return qw2_create_kv(device, cfg, max_sessions, KV_F16, out);
 }
 
 int qw2_create(int device, const qw2_config* cfg, qw2_model** out) {

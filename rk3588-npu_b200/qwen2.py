@@ -140,6 +140,7 @@ class Qw2Request(C.Structure):
 _SIGS = {
     "qw2_config_default": [C.POINTER(Qw2Config)],
     "qw2_create_sessions": [C.c_int, C.POINTER(Qw2Config), C.c_int, C.POINTER(C.c_void_p)],
+    "qw2_create_kv": [C.c_int, C.POINTER(Qw2Config), C.c_int, C.c_int, C.POINTER(C.c_void_p)],
     "qw2_session_create": [C.c_void_p, C.POINTER(C.c_int)],
     "qw2_session_destroy": [C.c_void_p, C.c_int],
     "qw2_session_exists": [C.c_void_p, C.c_int, C.POINTER(C.c_int)],
@@ -186,13 +187,15 @@ def _ints(xs):
 
 class Model:
     """Qwen2Model + LLMEngine on one GPU (weights, KV pool and scratch on the
-    device), with up to `max_sessions` sessions sharing the weights."""
+    device), with up to `max_sessions` sessions sharing the weights.
+    kv_dtype: the KV cache's element type (0 fp16 as in the reference, 1
+    bf16, 2 INT8 codes + per-row scales)."""
 
-    def __init__(self, device: int = 0, cfg: dict = QWEN2_1_5B, max_sessions: int = 1):
+    def __init__(self, device: int = 0, cfg: dict = QWEN2_1_5B, max_sessions: int = 1, kv_dtype: int = 0):
         self.L = _lib()
         c = Qw2Config(**cfg)
         h = C.c_void_p()
-        _check(self.L.qw2_create_sessions(device, C.byref(c), max_sessions, C.byref(h)), "qw2_create_sessions")
+        _check(self.L.qw2_create_kv(device, C.byref(c), max_sessions, kv_dtype, C.byref(h)), "qw2_create_kv")
         self.h = h
         self.cfg = dict(cfg)
         self._keep = {}  # ctypes objects an async job still points at

@@ -175,3 +175,29 @@ def test_async_submit_wait_and_cancel(model):
     M.forward_session(sessions[0], [1])  # the session is free again
     for s in sessions:
         M.destroy_session(s)
+
+
+@pytest.mark.gpu
+def test_int8_kv_model_tracks_fp16_cache():
+    """The model with an INT8 KV cache (qw2_create_kv, KV_I8): the same prompt
+    (one chunk) and teacher-forced decode steps as the fp16-cache model; the
+    logits differ only by the cache's quantisation error (not at all would
+    mean the INT8 path did not run)."""
+    need_gpu()
+    m = q2()
+    models = [m.Model(0, SMALL, kv_dtype=dt) for dt in (0, 2)]
+    for M in models:
+        for name, a in m.synth_weights(SMALL, seed=21):
+            M.set_tensor(name, a)
+    p = prompt(40, 12)
+    follow = prompt(8, 13)
+    worst, moved = 0.0, False
+    for toks in [p] + [[t] for t in follow]:
+        (l16, _), (l8, _) = [M.forward_session(0, toks) for M in models]
+        d = float(np.abs(l8 - l16).max() / np.abs(l16).max())
+        worst = max(worst, d)
+        moved = moved or d > 0.0
+    assert moved and worst <= 5e-2, worst
+    for M in models:
+        assert M.session_len(0) == 48
+        M.close()
