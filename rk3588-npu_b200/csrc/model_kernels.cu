@@ -298,7 +298,9 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int row, int n,
 // [MR][K].  The CTA walks row groups blockIdx.x, +gridDim.x, ...; its first
 // weight loads are issued before it waits for the previous kernel (every
 // access before that wait reads only weights, which no kernel writes).
-template <int MODE, int IN, int MR>
+// U: 16-byte weight chunks in flight per lane (kGemvUnroll, or more when one
+// batch of that depth would not cover a warp's share of the row).
+template <int MODE, int IN, int MR, int U>
 __global__ void __launch_bounds__(kGemvWarps * 32)
     gemv_kernel(GemvArgs a) {
     constexpr int NW = MODE == 2 ? 2 : 1;
@@ -313,10 +315,10 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
     const int ngroups = (a.N + rows_per_cta - 1) / rows_per_cta;
     const uint16_t* w2 = NW == 2 ? a.w2 : a.w;
 
-    uint4 wv[NW][kGemvUnroll];
+    uint4 wv[NW][U];
     auto load_batch = [&](int n, int base) {
 #pragma unroll
-        for (int u = 0; u < kGemvUnroll; ++u) {
+        for (int u = 0; u < U; ++u) {
             const int c = base + u * step;
             if (n < a.N && c < nch) {
                 wv[0][u] = ld_stream16(reinterpret_cast<const uint4*>(a.w + (size_t)n * K) + c);
@@ -354,11 +356,11 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
 #pragma unroll
             for (int m = 0; m < MR; ++m) acc[t][m] = 0.f;
 #pragma unroll 1
-        for (int base = part * 32 + lane; base < nch; base += kGemvUnroll * step) {
+        for (int base = part * 32 + lane; base < nch; base += U * step) {
             if (!loaded) load_batch(n, base);
             loaded = false;
 #pragma unroll
-            for (int u = 0; u < kGemvUnroll; ++u) {
+            for (int u = 0; u < U; ++u) {
                 const int c = base + u * step;
                 if (n < a.N && c < nch) {
 #pragma unroll
@@ -623,7 +625,7 @@ int gemv_split(int K) {
     return ks;
 }
 
-template <int MODE, int IN, int MR>
+template <int MODE, int IN, int MR, int U>
 static cudaError_t launch_gemv_mr(const GemvArgs& a, cudaStream_t st) {
     static int max_smem_set = 0;     // dynamic shared memory attribute granted so far
     static int ctas_per_sm[64] = {};  // occupancy by (smem / 4 KiB) bucket
@@ -631,7 +633,7 @@ static cudaError_t launch_gemv_mr(const GemvArgs& a, cudaStream_t st) {
     const int smem = MR * a.K * 2;
     cudaError_t e;
     if (smem > max_smem_set) {
-        e = cudaFuncSetAttribute(gemv_kernel<MODE, IN, MR>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        e = cudaFuncSetAttribute(gemv_kernel<MODE, IN, MR, U>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         max_smem_set = smem;
     }
@@ -643,7 +645,7 @@ static cudaError_t launch_gemv_mr(const GemvArgs& a, cudaStream_t st) {
     const int bucket = smem >> 12 < 64 ? smem >> 12 : 63;
     if (!ctas_per_sm[bucket]) {
         int n = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_kernel<MODE, IN, MR>, kGemvWarps * 32,
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_kernel<MODE, IN, MR, U>, kGemvWarps * 32,
                                                           (size_t)smem);
         if (e != cudaSuccess) return e;
         ctas_per_sm[bucket] = n > 0 ? n : 1;
@@ -667,7 +669,7 @@ static cudaError_t launch_gemv_mr(const GemvArgs& a, cudaStream_t st) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return counted(cudaLaunchKernelEx(&cfg, gemv_kernel<MODE, IN, MR>, a));
+    return counted(cudaLaunchKernelEx(&cfg, gemv_kernel<MODE, IN, MR, U>, a));
 }
 
 template <int MODE, int IN, int NT>
@@ -733,7 +735,14 @@ static cudaError_t launch_gemv_mma(const GemvArgs& a, cudaStream_t st) {
 // passes of up to 32 rows.
 template <int MODE, int IN>
 static cudaError_t launch_gemv_t(const GemvArgs& a, cudaStream_t st) {
-    if (a.M == 1) return launch_gemv_mr<MODE, IN, 1>(a, st);
+    if (a.M == 1) {
+        // one batch of loads per row part when 9 chunks per lane cover it
+        // (the 8960-wide down projection: 1120 chunks over 4 x 32 lanes;
+        // 9 keeps three CTAs per SM resident, 12 would leave two)
+        const int per_lane = ((a.K >> 3) + 32 * a.ks - 1) / (32 * a.ks);
+        if (per_lane == kGemvUnroll + 1) return launch_gemv_mr<MODE, IN, 1, kGemvUnroll + 1>(a, st);
+        return launch_gemv_mr<MODE, IN, 1, kGemvUnroll>(a, st);
+    }
     return launch_gemv_mma<MODE, IN>(a, st);
 }
 
