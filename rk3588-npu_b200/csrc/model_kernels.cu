@@ -26,6 +26,8 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "device_common.cuh"
 #include "kvattn.h"
 #include "kvattn_internal.h"
@@ -625,35 +627,57 @@ int gemv_split(int K) {
     return ks;
 }
 
+// Launch facts of one kernel, per device (a process may drive several GPUs,
+// from several threads): the dynamic shared memory granted so far, the SM
+// count, and the resident CTAs per SM by 4 KiB shared-memory bucket.
+// Concurrent first calls may query twice; every value written is the same.
+struct LaunchCache {
+    static constexpr int kDevices = 64;
+    std::atomic<int> smem_set[kDevices];
+    std::atomic<int> sms[kDevices];
+    std::atomic<int> ctas[kDevices][64];
+
+    cudaError_t get(const void* fn, int smem, int* sms_out, int* ctas_out) {
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        if (dev < 0 || dev >= kDevices) return cudaErrorInvalidDevice;
+        if (smem > smem_set[dev].load()) {
+            e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (e != cudaSuccess) return e;
+            int cur = smem_set[dev].load();
+            while (cur < smem && !smem_set[dev].compare_exchange_weak(cur, smem)) {
+            }
+        }
+        if (!sms[dev].load()) {
+            int n = 0;
+            if ((e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+            sms[dev].store(n);
+        }
+        const int bucket = smem >> 12 < 64 ? smem >> 12 : 63;
+        if (!ctas[dev][bucket].load()) {
+            int n = 0;
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, kGemvWarps * 32, (size_t)smem);
+            if (e != cudaSuccess) return e;
+            ctas[dev][bucket].store(n > 0 ? n : 1);
+        }
+        *sms_out = sms[dev].load();
+        *ctas_out = ctas[dev][bucket].load();
+        return cudaSuccess;
+    }
+};
+
 template <int MODE, int IN, int MR, int U>
 static cudaError_t launch_gemv_mr(const GemvArgs& a, cudaStream_t st) {
-    static int max_smem_set = 0;     // dynamic shared memory attribute granted so far
-    static int ctas_per_sm[64] = {};  // occupancy by (smem / 4 KiB) bucket
-    static int sms = 0;
+    static LaunchCache cache;
     const int smem = MR * a.K * 2;
-    cudaError_t e;
-    if (smem > max_smem_set) {
-        e = cudaFuncSetAttribute(gemv_kernel<MODE, IN, MR, U>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        max_smem_set = smem;
-    }
-    if (!sms) {
-        int dev = 0;
-        if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-        if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-    }
-    const int bucket = smem >> 12 < 64 ? smem >> 12 : 63;
-    if (!ctas_per_sm[bucket]) {
-        int n = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_kernel<MODE, IN, MR, U>, kGemvWarps * 32,
-                                                          (size_t)smem);
-        if (e != cudaSuccess) return e;
-        ctas_per_sm[bucket] = n > 0 ? n : 1;
-    }
+    int sms = 0, ctas = 0;
+    cudaError_t e = cache.get(reinterpret_cast<const void*>(gemv_kernel<MODE, IN, MR, U>), smem, &sms, &ctas);
+    if (e != cudaSuccess) return e;
     const int rows_per_cta = kGemvWarps / a.ks;
     const int groups = (a.N + rows_per_cta - 1) / rows_per_cta;
     const int ylen = (a.M + MR - 1) / MR;
-    int cap = sms * ctas_per_sm[bucket] / ylen;
+    int cap = sms * ctas / ylen;
     cap = cap < 1 ? 1 : cap;
     // as many CTAs as fit, but every CTA the same number of row groups (the
     // next kernel waits for the last CTA)
@@ -674,33 +698,15 @@ static cudaError_t launch_gemv_mr(const GemvArgs& a, cudaStream_t st) {
 
 template <int MODE, int IN, int NT>
 static cudaError_t launch_gemv_mma_nt(const GemvArgs& a, cudaStream_t st) {
-    static int max_smem_set = 0;
-    static int ctas_per_sm[64] = {};
-    static int sms = 0;
+    static LaunchCache cache;  // static (the reduction buffer) + dynamic may pass 48 KB at any size
     const int smem = NT * 8 * (a.K + kMmaPad) * 2;
-    cudaError_t e;
-    if (smem > max_smem_set) {  // static (the reduction buffer) + dynamic may pass 48 KB at any size
-        e = cudaFuncSetAttribute(gemv_mma_kernel<MODE, IN, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        max_smem_set = smem;
-    }
-    if (!sms) {
-        int dev = 0;
-        if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-        if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-    }
-    const int bucket = smem >> 12 < 64 ? smem >> 12 : 63;
-    if (!ctas_per_sm[bucket]) {
-        int n = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_mma_kernel<MODE, IN, NT>, kGemvWarps * 32,
-                                                          (size_t)smem);
-        if (e != cudaSuccess) return e;
-        ctas_per_sm[bucket] = n > 0 ? n : 1;
-    }
+    int sms = 0, ctas = 0;
+    cudaError_t e = cache.get(reinterpret_cast<const void*>(gemv_mma_kernel<MODE, IN, NT>), smem, &sms, &ctas);
+    if (e != cudaSuccess) return e;
     const int rows_per_group = 16 * (kGemvWarps / kMmaKs);
     const int groups = (a.N + rows_per_group - 1) / rows_per_group;
     const int ylen = (a.M + NT * 8 - 1) / (NT * 8);
-    int cap = sms * ctas_per_sm[bucket] / ylen;
+    int cap = sms * ctas / ylen;
     cap = cap < 1 ? 1 : cap;
     const int rounds = (groups + cap - 1) / cap;
     const int gx = (groups + rounds - 1) / rounds;
