@@ -174,3 +174,53 @@ def test_int8_attention_close_to_fp32(orc):
     assert np.isfinite(out).all() and np.abs(out).max() > 0
     # the appended row is the quantised RoPE'd k / plain v
     assert np.abs(vq[T].astype(np.float32) * np.repeat(vs[T], 128) - vn[0]).max() <= vs[T].max() * 0.5001
+
+
+def test_int8_prefill_step_matches_numpy(orc):
+    """The INT8 layer step with a multi-token chunk (seq = n, the prefill
+    attention's checker) against an independent float64 numpy computation:
+    NeoX RoPE at positions pos..pos+n-1, causal GQA attention over the
+    dequantised caches (the context's codes and the chunk's appended codes);
+    the appended k / v rows decode to the rotated k and to v within half a
+    quantisation step."""
+    rng = np.random.default_rng(8)
+    C, n, qh, kvh, hd = 150, 37, 12, 2, 128
+    kvd, hid, G = kvh * hd, qh * hd, qh // kvh
+    kq = np.zeros((C + n, kvd), np.int8)
+    vq = np.zeros((C + n, kvd), np.int8)
+    ks = np.zeros((C + n, kvh), np.float32)
+    vs = np.zeros((C + n, kvh), np.float32)
+    kq[:C] = rng.integers(-127, 128, (C, kvd))
+    vq[:C] = rng.integers(-127, 128, (C, kvd))
+    ks[:C] = rng.uniform(0.001, 0.05, (C, kvh))
+    vs[:C] = rng.uniform(0.001, 0.05, (C, kvh))
+    q = rng.standard_normal((n, hid)).astype(np.float32)
+    k = rng.standard_normal((n, kvd)).astype(np.float32)
+    v = rng.standard_normal((n, kvd)).astype(np.float32)
+    out = orc.layer_step_i8(q, k, v, kq, ks, vq, vs, C)
+
+    def rope(x, heads):  # NeoX pairs (i, i + 64), theta 1e6, float64
+        x = x.astype(np.float64).reshape(n, heads, hd)
+        pos = np.arange(C, C + n, dtype=np.float64)[:, None]
+        ang = pos * (1e6 ** (-np.arange(64, dtype=np.float64) * 2 / hd))[None, :]
+        c, s = np.cos(ang)[:, None, :], np.sin(ang)[:, None, :]
+        a, b = x[..., :64], x[..., 64:]
+        return np.concatenate([a * c - b * s, b * c + a * s], axis=-1)
+
+    qr, kr = rope(q, qh), rope(k, kvh)
+    kd = kq.astype(np.float64).reshape(C + n, kvh, hd) * ks[..., None]
+    vd = vq.astype(np.float64).reshape(C + n, kvh, hd) * vs[..., None]
+    # the chunk's appended rows (the oracle rotates in fp32: ~3e-5 from float64)
+    step_k = ks[C:, :, None] * 0.5 * (1 + 1e-5) + 1e-4
+    assert (np.abs(kd[C:] - kr) <= step_k).all()
+    assert (np.abs(vd[C:] - v.astype(np.float64).reshape(n, kvh, hd)) <= vs[C:, :, None] * 0.5 * (1 + 1e-5) + 1e-7).all()
+    ref = np.zeros((n, qh, hd))
+    for h in range(qh):
+        kh, vh = kd[:, h // G], vd[:, h // G]
+        sc = qr[:, h] @ kh.T / np.sqrt(hd)
+        sc[np.arange(C + n)[None, :] > (C + np.arange(n))[:, None]] = -np.inf
+        p = np.exp(sc - sc.max(axis=1, keepdims=True))
+        ref[:, h] = (p / p.sum(axis=1, keepdims=True)) @ vh
+    got = out.reshape(n, qh, hd).astype(np.float64)
+    rel = (np.abs(got - ref).max(axis=2) / np.abs(ref).max(axis=2)).max()
+    assert rel <= 5e-4, rel  # fp32 vs float64; a wrong mask, group or scale is O(1)
