@@ -183,8 +183,11 @@ int attn_prefill_mma(kvp_pool* pool, int layer, int seq_id, int pos0, int n, con
 
 /* Plan one decode step for nseq sequences (host ids).  For each sequence:
  * position p = its length; one block is reserved for p+1 if needed (all or
- * nothing); the split-KV work list is built and uploaded on `stream`.
- * The plan stays valid for every layer until the next plan or commit. */
+ * nothing); the split-KV work partition is built on the host and passed to
+ * every layer's launch as kernel parameters (nothing is uploaded; block-table
+ * entries queued by reserve / set_blocks are applied on `stream`).  The plan
+ * stays valid for every layer until the next plan or commit.  A plan of more
+ * than 256 sequences runs as one launch per 256 sequences per layer. */
 int attn_decode_plan(kvp_pool* pool, int nseq, const int* seq_ids, void* stream);
 
 /* The same with per-sequence control, for a sequence whose positions are
@@ -258,14 +261,18 @@ int attn_combine_lse_packed(int G, int rows, int dim, const float* packed, float
  * decode loop that may not call into the allocator).  It creates no pool and
  * calls no cudaMalloc/cudaFree: split-KV partial states go to a fixed
  * file-scope device array of 4 MiB that every GPU loading this library holds
- * until the process exits.  No counterpart in the reference; it has
- * op_attention's semantics (worker/src/ops/op_attention.cpp:9-56) on device
- * pointers: q [seq][n_heads*128] fp32 already rotated, contiguous caches
- * [total_len][n_kv_heads*128] of `dtype`, causal mask from pos_base, out
- * [seq][n_heads*128] fp32.  Limit: seq * n_kv_heads <= 1008 (else
- * KV_ERR_RANGE).  The first call on a device looks up the array's device
- * address (cudaGetSymbolAddress) with that device current, so make that first
- * call before any stream capture.  All calls share the array: calls that
+ * until the process exits.  No counterpart in the reference.  The math: for
+ * query row s (absolute position pos_base + s) and query head h of KV group
+ * g = h / (n_heads / n_kv_heads), out[s][h] = softmax(q[s][h] . K_g^T /
+ * sqrt(128)) V_g over keys 0 .. min(pos_base + s, total_len - 1), with
+ * q [seq][n_heads*128] fp32 already rotated, contiguous caches
+ * [total_len][n_kv_heads*128] of `dtype` (KV_F16 or KV_BF16) and out
+ * [seq][n_heads*128] fp32, all device pointers; q and the caches 16-byte
+ * aligned.  Limit: seq * n_kv_heads <= 1008 (else KV_ERR_RANGE).  The first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress)
+ * with that device current, so make that first call before any stream
+ * capture; the address is kept for the process, so the entry point is not
+ * for use across cudaDeviceReset.  All calls share the array: calls that
  * overlap on the GPU (concurrent streams) race and must be serialised by the
  * caller; nothing in it needs clearing, every value read is written first
  * in the same call. */
@@ -292,13 +299,18 @@ int kvp_plan_cta_start(const kvp_pool* pool, int* cta_start, int cap);
  * launch durations (ms) and the launch count since enabling, then resets. */
 int kvp_timing_enable(kvp_pool* pool, int enable);
 
-/* Let every decode launch of this pool start while the previous kernel in
- * its stream is still running (programmatic dependent launch): the launch's
- * K/V tile copies begin at once and the threads that read q / k_new / v_new
- * or write anything wait for that kernel to finish.  Valid only when no
- * kernel that may still be running writes this pool's blocks -- e.g. when a
- * host-side copy or synchronisation separates consecutive decode steps, as
- * in qw2_forward.  Default off. */
+/* With overlap enabled, every decode launch on a created stream (not the
+ * legacy default stream) is a programmatic dependent launch: its CTAs start
+ * while the previous kernel in the stream finishes and copy their first K/V
+ * tiles then, while everything that reads other state that kernel may write
+ * (q / k_new / v_new) or writes anything waits for it inside the kernel.
+ * Valid when that kernel writes
+ * none of this pool's blocks or block-table entries -- or is itself a decode
+ * launch (or merge) of this pool: the rows and table entries the previous
+ * decode launch of the pool appended are read only after it.  The library
+ * turns the early copies off by itself for the first decode launch after any
+ * other of its calls that writes the pool (import, prompt append, reset,
+ * reserve / set_blocks).  Default off. */
 int kvp_set_overlap(kvp_pool* pool, int enable);
 int kvp_timing_read(kvp_pool* pool, double* total_ms, int* launches);
 

@@ -342,6 +342,12 @@ class Pool:
     def timing(self, enable: bool) -> None:
         call("kvp_timing_enable", self.h, int(enable))
 
+    def set_overlap(self, enable: bool) -> None:
+        """kvp_set_overlap: decode launches may copy their first tiles while
+        the previous kernel in the stream finishes (that kernel must not
+        write this pool, other than as one of this pool's decode launches)."""
+        call("kvp_set_overlap", self.h, int(enable))
+
     def timing_read(self):
         """(summed decode-launch milliseconds, launches) since timing(True)."""
         ms, n = C.c_double(), C.c_int()

@@ -76,7 +76,18 @@ __host__ __device__ constexpr int mma_type() { return DT == 1 ? 1 : 0; }
 constexpr int kMergeStride = 132;            // floats per (warp, head) row, padded
 constexpr long long kWaitLimit = 4000000000LL;  // SM clocks (~2 s) before a wait gives up
 constexpr int kQPre = 4;                     // pieces whose q fragments are prepared up front
-constexpr int kEarlyLanes = 2;               // ring stages issued before the plan header load
+
+// One piece of a CTA's range: blocks [b0, b1) of segment (slot, head).  A
+// split piece (its segment has blocks in other CTAs too) writes its partial
+// state to partials[part]; any other piece writes the output rows directly.
+struct Piece {
+    int slot;
+    int head;
+    int b0;
+    int b1;
+    int split;
+    int part;
+};
 
 template <int DT>
 struct Smem {
@@ -85,9 +96,9 @@ struct Smem {
     float merge_o[kConsumerWarps][kMaxGroup][kMergeStride];
     float merge_m[kConsumerWarps][kMaxGroup];
     float merge_l[kConsumerWarps][kMaxGroup];
-    WorkItem items[kMaxCtaItems];     // this CTA's pieces
+    Piece items[kMaxCtaItems];        // this CTA's pieces
     int cum[kMaxCtaItems + 1];        // flat block offset of each piece
-    int ok[kMaxCtaItems];             // piece passed the checks
+    int ok[kMaxCtaItems];             // piece's slot passed the checks
     // q fragments (hi, lo) of the first kQPre pieces, as each lane holds them
     uint32_t qfrag[kQPre][2][8][2][32];
     uint64_t full[kStages];
@@ -132,19 +143,64 @@ __device__ __forceinline__ void flag_timeout(const PoolView& pv, SmemT& sm, int 
     sm.failed = 1;
 }
 
-// Every index a piece leads to, checked before any access (the plan comes
-// from the host planner; a bad piece is reported and skipped).
-__device__ __forceinline__ int item_check(const PoolView& pv, const PlanHeader& hdr,
-                                          const WorkItem& w) {
-    if (w.slot < 0 || w.slot >= hdr.nslots) return 1;
-    if (w.head < 0 || w.head >= pv.kv_heads) return 2;
-    if (w.seq < 0 || w.seq >= pv.max_seqs) return 3;
-    if (w.kv_len < 0 || w.kv_len > pv.max_blocks_per_seq * kBlockTokens) return 4;
-    if (w.rope_pos < 0 || w.rope_pos >= pv.max_seq_len) return 5;
-    if (w.append && (w.kv_len < 1 || w.new_block < 0 || w.new_block >= pv.num_blocks)) return 6;
-    if (w.b0 < 0 || w.b1 < w.b0 || w.b1 > (w.kv_len + kBlockTokens - 1) / kBlockTokens) return 7;
-    if (w.seg_first < 0 || w.seg_n < 1 || w.seg_first + w.seg_n > pv.max_items) return 8;
+// Slot fields checked before any access they lead to (the plan comes from the
+// host planner; a slot that fails is reported and its pieces are skipped).
+__device__ __forceinline__ int slot_check(const PoolView& pv, const DecodeSlot& s) {
+    if (s.seq < 0 || s.seq >= pv.max_seqs) return 3;
+    if (s.kv_len < 0 || s.kv_len > pv.max_blocks_per_seq * kBlockTokens) return 4;
+    if (s.rope_pos < 0 || s.rope_pos >= pv.max_seq_len) return 5;
+    if (s.new_block >= 0 && (s.kv_len < 1 || s.new_block >= pv.num_blocks)) return 6;
     return 0;
+}
+
+__host__ __device__ __forceinline__ int nblocks_of(int kv_len) { return (kv_len + kBlockTokens - 1) / kBlockTokens; }
+
+// Position of flat block f (< a.total) of a launch: slot i, KV head h, block
+// b of nb.  slot_f0 is non-decreasing; the largest i with slot_f0[i] <= f is
+// a slot with blocks (an empty slot shares its offset with the next one).
+template <int S>
+__device__ __forceinline__ void locate(const DecodeArgs<S>& a, int kvh, int f, int& i, int& h, int& b, int& nb) {
+    int lo = 0, hi = a.nslots - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (a.slot_f0[mid] <= f) lo = mid;
+        else hi = mid - 1;
+    }
+    i = lo;
+    nb = nblocks_of(a.slot[i].kv_len);
+    const int r = f - a.slot_f0[i];
+    h = nb > 0 ? r / nb : 0;
+    b = r - h * nb;
+}
+
+// Step a position `k` flat blocks forward (never past the launch's blocks).
+template <int S>
+__device__ __forceinline__ void advance(const DecodeArgs<S>& a, int kvh, int k, int& i, int& h, int& b, int& nb) {
+    b += k;
+    while (b >= nb && i < a.nslots) {
+        b -= nb;
+        if (++h == kvh) {
+            h = 0;
+            do {
+                ++i;
+            } while (i < a.nslots && a.slot[i].kv_len == 0);
+            nb = i < a.nslots ? nblocks_of(a.slot[i].kv_len) : 1;
+        }
+    }
+}
+
+// Tile id (block * kv_heads + head) of block b of a slot's segment, or -1
+// for a block that holds only the new token (nothing to load).  The new
+// token's block comes from the plan, every other from the block table.
+__device__ __forceinline__ int tile_of(const PoolView& pv, const DecodeSlot& s, int h, int b) {
+    int blk;
+    if (s.new_block >= 0 && b == (s.kv_len - 1) / kBlockTokens) {
+        if (s.kv_len - b * kBlockTokens == 1) return -1;
+        blk = s.new_block;
+    } else {
+        blk = __ldcg(pv.table + (size_t)s.seq * pv.max_blocks_per_seq + b);
+    }
+    return blk * pv.kv_heads + h;
 }
 
 // Rotated, pre-scaled q of query head (head*group + g) as mma B fragments.
@@ -366,26 +422,32 @@ __device__ __forceinline__ void consume_block(uint32_t sK, uint32_t sV, int vali
 
 }  // namespace
 
-template <int DT>
+
+template <int DT, int S>
 __global__ void __launch_bounds__(kThreads, 2)
-    decode_kernel(PoolView pv, PlanView plan, int layer, const float* __restrict__ q,
-                  const float* __restrict__ k_new, const float* __restrict__ v_new,
-                  float* __restrict__ out, float* __restrict__ m_out, float* __restrict__ l_out) {
+    decode_kernel(PoolView pv, const __grid_constant__ DecodeArgs<S> a, const float* __restrict__ q,
+                  const float* __restrict__ k_new, const float* __restrict__ v_new, float* __restrict__ out,
+                  float* __restrict__ m_out, float* __restrict__ l_out) {
     extern __shared__ uint8_t smem_raw[];
     Smem<DT>& sm = *reinterpret_cast<Smem<DT>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     constexpr int TB = StageCfg<DT>::tile;  // bytes of one K or V tile in HBM and in a stage
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // The combine kernel may be scheduled now; it waits for this grid.
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    // Round 0 first: producer lane l initialises its own stage's barriers and
-    // issues flat block l straight from this CTA's descriptor, which needs no
-    // other load, so the first copies leave after one round trip.  A tile id
-    // is range-checked before any copy; the descriptor itself is validated
-    // below, and a lane that issued round 0 always drains it.
-    const CtaDesc* cdp = plan.cta + blockIdx.x;
+    const int layer = a.layer;
+    const int kvh = pv.kv_heads;
+    const bool early = (a.flags & kDecEarly) != 0;
+    // This CTA's flat range, from the kernel parameters (checked; a bad range
+    // is reported once the previous kernel has finished, and no work runs).
+    int f0 = 0, f1 = 0;
+    const bool range_ok = a.nslots >= 0 && a.nslots <= S && a.grid <= kMaxGrid && (int)blockIdx.x < a.grid &&
+                          a.total >= 0 && (a.nslots > 0 || a.total == 0) && a.slot_f0[a.nslots] == a.total;
+    if (range_ok) {
+        f0 = a.cta_f0[blockIdx.x];
+        f1 = a.cta_f0[blockIdx.x + 1];
+        if (f0 < 0 || f1 < f0 || f1 > a.total) f0 = f1 = 0;
+    }
     const bool prod_lane = warp == kConsumerWarps && lane < kStages;
     const uint64_t policy = policy_evict_first();
-    const long ntile_ids = (long)pv.num_blocks * pv.kv_heads;
+    const long ntile_ids = (long)pv.num_blocks * kvh;
     // One ring round of producer lane `s` for flat block f with tile id `tile`.
     auto issue = [&](int s, int f, int tile) {
         if (tile == -1) {
@@ -400,109 +462,109 @@ __global__ void __launch_bounds__(kThreads, 2)
             bulk_g2s_hint(sm.stage[s] + TB, pv.v + off, TB, &sm.full[s], policy);
         }
     };
-    // Only the first kEarlyLanes stages go out here: their tiles then sit at
-    // the front of the DRAM queue and arrive early; the other lanes issue
-    // their first round from the producer loop a little later.
+    // Producer lane l owns ring stage l and flat blocks f0 + l, f0 + l + 8, ...
+    int pf = f0 + (prod_lane ? lane : 0);
+    int pi = 0, ph = 0, pb = 0, pnb = 1;
     bool issued0 = false;
-    int tile0 = -2;
     if (prod_lane) {
-        const int nf0 = cdp->nf;
-        tile0 = cdp->first[lane];
         mbar_init(&sm.full[lane], 1);
         mbar_init(&sm.empty[lane], 1);
         fence_mbar_init();
-        if (lane < kEarlyLanes && lane < nf0) {  // round 0: the stage is free
-            issue(lane, lane, tile0);
-            issued0 = true;
+        if (pf < f1) {
+            locate(a, kvh, pf, pi, ph, pb, pnb);
+            // Round 0 before the previous kernel has finished (kDecEarly): a
+            // block that kernel may still write (the row the previous decode
+            // launch appended) is read only after it.
+            const DecodeSlot& sl = a.slot[pi];
+            if (early && a.defer_blk[pi] != pb && slot_check(pv, sl) == 0) {
+                issue(lane, pf, tile_of(pv, sl, ph, pb));
+                issued0 = true;
+            }
         }
-    }
-    const PlanHeader hdr = *plan.hdr;
-
-    // Block-table entries allocated by this step's plan.  No launch reads an
-    // entry it patches: the block of a new token is taken from its piece.
-    for (int i = blockIdx.x * kThreads + tid; i < hdr.npatch; i += gridDim.x * kThreads) {
-        const TablePatch p = plan.patches[i];
-        if (p.seq < 0 || p.seq >= pv.max_seqs || p.idx < 0 || p.idx >= pv.max_blocks_per_seq ||
-            p.block < 0 || p.block >= pv.num_blocks) {
-            report(pv, 5, -1, i);
-            continue;
-        }
-        pv.table[(size_t)p.seq * pv.max_blocks_per_seq + p.idx] = p.block;
-    }
-
-    // This CTA's descriptor, checked against the plan before its pieces and
-    // tiles are used; the other threads load and check the pieces.
-    const CtaDesc cd = *cdp;
-    int n = cd.n, nf = cd.nf;
-    if (n < 0 || n > kMaxCtaItems || cd.i0 < 0 || cd.i0 + n > hdr.nitems || nf < 0 || cd.f0 < 0 ||
-        cd.f0 + nf > hdr.ntiles) {
-        if (tid == 0) report(pv, 5, cd.i0, 300);
-        n = 0;
-        nf = 0;
-    }
-    const int i0 = cd.i0;
-    int tile_next = (prod_lane && lane + kStages < nf) ? plan.tiles[cd.f0 + lane + kStages] : -1;
-    for (int j = tid; j < n; j += kThreads) {
-        WorkItem w = plan.items[i0 + j];
-        const int bad = item_check(pv, hdr, w);
-        if (bad) {
-            report(pv, 5, i0 + j, bad);
-            w.b0 = w.b1 = 0;
-        }
-        sm.items[j] = w;
-        sm.ok[j] = !bad;
     }
     if (tid == 0) {
+        // This CTA's pieces (kernel parameters only).
+        int n = 0, f = f0;
+        if (f < f1) {
+            int i, h, b, nb;
+            locate(a, kvh, f, i, h, b, nb);
+            while (f < f1 && n < kMaxCtaItems && i < a.nslots) {
+                const int seg_end = a.slot_f0[i] + (h + 1) * nb;
+                const int e = min(seg_end, f1);
+                Piece& pc = sm.items[n];
+                pc.slot = i;
+                pc.head = h;
+                pc.b0 = b;
+                pc.b1 = b + (e - f);
+                pc.split = (b > 0 || e < seg_end) ? 1 : 0;
+                pc.part = 2 * (int)blockIdx.x + (n == 0 ? 0 : 1);
+                sm.ok[n] = slot_check(pv, a.slot[i]) == 0 && nb > 0;
+                ++n;
+                advance(a, kvh, e - f, i, h, b, nb);
+                f = e;
+            }
+            if (f < f1) n = -1;  // more pieces than a CTA holds: reported below, nothing runs
+        }
+        sm.nitems = n;
         sm.failed = 0;
         sm.prod_issued = 0;
         for (int w = 0; w < kConsumerWarps; ++w) sm.cons_done[w] = 0;
     }
     __syncthreads();
+    int n = sm.nitems;
+    if (n < 0) n = 0;
     if (tid == 0) {
         sm.cum[0] = 0;
         for (int j = 0; j < n; ++j) sm.cum[j + 1] = sm.cum[j] + (sm.items[j].b1 - sm.items[j].b0);
-        // The tile list and the pieces must describe the same blocks; if not,
-        // no consumer runs (the producer still drains what it issued).
-        sm.nitems = (sm.cum[n] == nf) ? n : 0;
-        if (sm.cum[n] != nf) report(pv, 5, i0, 301);
     }
     __syncthreads();
-    n = sm.nitems;
     const int total = sm.cum[n];
+    const int nf = (total == f1 - f0) ? total : 0;  // blocks the producer streams
 
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------ producer
-        // Lane l < kStages owns ring stage l and issues flat blocks l, l +
-        // kStages, ...  Each lane refills its stage as soon as that stage is
-        // released -- the lanes poll their own barriers without blocking and
-        // never wait for one another -- so a slow stage does not hold back
-        // the other seven.  Each lane fetches the tile id of its next round
-        // one round ahead.
+        // Everything below reads state the previous kernel may write (the
+        // block table, deferred blocks): wait for it, then let the next
+        // kernel launch (it can overlap only this one).
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
         if (lane < kStages) {
             const int s = lane;
-            // Lanes below kEarlyLanes issued round 0 above; the others start
-            // with it (their stage is free: a fresh barrier passes the
-            // parity-1 test at once).
-            uint32_t rounds = issued0 ? 1u : 0u;
-            int f = issued0 ? lane + kStages : lane;  // this lane's next flat block
-            int cur = issued0 ? tile_next : tile0;    // its tile id
-            int nxt = issued0 ? ((f + kStages < total) ? plan.tiles[cd.f0 + f + kStages] : -1) : tile_next;
+            const bool live0 = pf < f1 && pf - f0 < nf;
+            uint32_t rounds = issued0 ? 1u : 0u;  // rounds issued (all drained before the exit)
+            if (live0 && !issued0) {
+                const DecodeSlot& sl = a.slot[pi];
+                issue(s, pf, slot_check(pv, sl) == 0 ? tile_of(pv, sl, ph, pb) : -2);
+                rounds = 1;
+            }
+            // Lane s refills its stage as soon as the consumer releases it,
+            // polling without blocking; the next round's tile id is fetched
+            // one round ahead.
+            int f = pf + kStages;
+            if (live0) advance(a, kvh, kStages, pi, ph, pb, pnb);
+            auto next_tile = [&]() -> int {
+                const DecodeSlot& sl = a.slot[pi];
+                return slot_check(pv, sl) == 0 ? tile_of(pv, sl, ph, pb) : -2;
+            };
+            int cur = (live0 && f - f0 < nf) ? next_tile() : -1;
             bool stopped = false;
             long long since = clock64();
             for (;;) {
-                const bool has = !stopped && f < total;
+                const bool has = live0 && !stopped && f - f0 < nf;
                 if (!__any_sync(0xffu, has)) break;
-                bool ready = has && mbar_test_wait(&sm.empty[s], (rounds & 1) ^ 1);
+                const bool ready = has && mbar_test_wait(&sm.empty[s], (rounds & 1) ^ 1);
                 if (ready) {
                     issue(s, f, cur);
                     ++rounds;
-                    atomicMax(&sm.prod_issued, f + 1);
+                    atomicMax(&sm.prod_issued, f - f0 + 1);
                     f += kStages;
-                    cur = nxt;
-                    if (f + kStages < total) nxt = plan.tiles[cd.f0 + f + kStages];  // in flight
+                    if (f - f0 < nf) {
+                        advance(a, kvh, kStages, pi, ph, pb, pnb);
+                        cur = next_tile();  // in flight while the stage drains
+                    }
                     since = clock64();
                 } else if (has && clock64() - since > kWaitLimit) {
-                    flag_timeout(pv, sm, i0, 0, (uint32_t)f);
+                    flag_timeout(pv, sm, blockIdx.x, 0, (uint32_t)(f - f0));
                     stopped = true;
                 }
                 if (!__any_sync(0xffu, ready)) __nanosleep(32);
@@ -516,19 +578,46 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
 
     // ---------------------------------------------------------- consumers
-    // When launched as a programmatic dependent (kvp_set_overlap), the
-    // producer above copies tiles at once; everything below reads the
-    // previous kernel's q / k_new / v_new or writes results, so it waits for
-    // that kernel first (a no-op for an ordinary launch).
+    // q / k_new / v_new come from the previous kernel and every write below
+    // may race with it: wait for it to finish first.
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (tid == 0) {
+        if (!range_ok) report(pv, 5, blockIdx.x, 300);
+        else if (sm.nitems < 0) report(pv, 5, blockIdx.x, 302);
+        else if (nf != f1 - f0) report(pv, 5, blockIdx.x, 301);
+    }
+    if (blockIdx.x == 0 && range_ok) {
+        // Rows of slots with nothing to attend are zero (m = -inf, l = 0),
+        // and the first launch of a plan enters its new blocks in the table.
+        for (int i = tid; i < a.nslots; i += kConsumerWarps * 32) {
+            const DecodeSlot sl = a.slot[i];
+            if (slot_check(pv, sl) != 0) {
+                report(pv, 5, i, 303);
+                continue;
+            }
+            if ((a.flags & kDecPatch) && sl.new_block >= 0)
+                pv.table[(size_t)sl.seq * pv.max_blocks_per_seq + (sl.kv_len - 1) / kBlockTokens] = sl.new_block;
+            if (sl.kv_len == 0) {
+                const int row = (a.row0 + i) * pv.q_heads;
+                for (int x = 0; x < pv.q_heads * kHeadDim; ++x) out[(size_t)row * kHeadDim + x] = 0.f;
+                if (m_out != nullptr)
+                    for (int hq = 0; hq < pv.q_heads; ++hq) {
+                        m_out[row + hq] = -INFINITY;
+                        l_out[row + hq] = 0.f;
+                    }
+            }
+        }
+    }
+    if (nf == 0) n = 0;
     const float qscale = 0.08838834764831845f * 1.4426950408889634f;  // 1/sqrt(128) * log2(e)
     const int g = lane >> 2, c = lane & 3;
     // Warp w prepares the q fragments of piece w (w < kQPre) while the first
     // copies are in flight, so piece switches read them from shared memory.
     if (warp < n && warp < kQPre && sm.ok[warp]) {
-        const WorkItem& w = sm.items[warp];
+        const Piece& w = sm.items[warp];
         uint32_t qh[8][2], ql[8][2];
-        load_q_frags<DT>(pv, q, w.slot, w.head, w.rope_pos, qscale, lane, qh, ql);
+        load_q_frags<DT>(pv, q, a.row0 + w.slot, w.head, a.slot[w.slot].rope_pos, qscale, lane, qh, ql);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
 #pragma unroll
@@ -540,11 +629,33 @@ __global__ void __launch_bounds__(kThreads, 2)
     named_bar_sync(1, kConsumerWarps * 32);
     bool dead = false;
     for (int j = 0; j < n; ++j) {
-        if (!sm.ok[j]) continue;  // rejected by the checks above
-        const WorkItem wi = sm.items[j];
+        const Piece wi = sm.items[j];
         const int nb = wi.b1 - wi.b0;
         const int fbase = sm.cum[j];
-        const int last_blk = (wi.kv_len - 1) / kBlockTokens;
+        if (!sm.ok[j]) {
+            // A rejected slot: still release the stages its blocks occupy so
+            // the producer's ring keeps moving (it loaded nothing for them).
+            for (int b = (warp - fbase % kConsumerWarps + kConsumerWarps) % kConsumerWarps; b < nb;
+                 b += kConsumerWarps) {
+                const uint32_t k = (uint32_t)(fbase + b);
+                const int s = k % kStages;
+                if (!dead && !mbar_wait_bounded(&sm.full[s], (k / kStages) & 1, kWaitLimit)) {
+                    flag_timeout(pv, sm, blockIdx.x, 1, k);
+                    dead = true;
+                }
+                if (dead) continue;
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&sm.empty[s]);
+                    *reinterpret_cast<volatile int*>(&sm.cons_done[warp]) = (int)k + 1;
+                }
+            }
+            continue;
+        }
+        const DecodeSlot sl = a.slot[wi.slot];
+        const int row = a.row0 + wi.slot;
+        const bool append = sl.new_block >= 0;
+        const int last_blk = (sl.kv_len - 1) / kBlockTokens;
 
         uint32_t qh[8][2], ql[8][2];
         if (j < kQPre) {
@@ -556,7 +667,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                     ql[kk][r] = sm.qfrag[j][1][kk][r][lane];
                 }
         } else {
-            load_q_frags<DT>(pv, q, wi.slot, wi.head, wi.rope_pos, qscale, lane, qh, ql);
+            load_q_frags<DT>(pv, q, row, wi.head, sl.rope_pos, qscale, lane, qh, ql);
         }
         float m2[2] = {-INFINITY, -INFINITY}, lsum[2] = {0.f, 0.f};
         float o[8][4];
@@ -568,13 +679,13 @@ __global__ void __launch_bounds__(kThreads, 2)
             const uint32_t k = (uint32_t)(fbase + b);  // k % kConsumerWarps == warp
             const int s = k % kStages;
             if (!dead && !mbar_wait_bounded(&sm.full[s], (k / kStages) & 1, kWaitLimit)) {
-                flag_timeout(pv, sm, i0 + j, 1, k);
+                flag_timeout(pv, sm, blockIdx.x, 1, k);
                 dead = true;
             }
             if (dead) continue;
             const int idx = wi.b0 + b;
-            const int valid = min(kBlockTokens, wi.kv_len - idx * kBlockTokens);
-            const bool newblk = wi.append && idx == last_blk;
+            const int valid = min(kBlockTokens, sl.kv_len - idx * kBlockTokens);
+            const bool newblk = append && idx == last_blk;
             uint8_t* sK;
             uint8_t* sV;
             float ks[2] = {1.f, 1.f}, vs[2] = {1.f, 1.f};  // INT8: scales of token rows g, g + 8
@@ -606,7 +717,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             if (newblk) {
                 if (DT == 2) {
                     float nks, nvs;
-                    write_new_row_i8(pv, layer, wi.new_block, wi.head, valid - 1, k_new, v_new, wi.slot, wi.rope_pos,
+                    write_new_row_i8(pv, layer, sl.new_block, wi.head, valid - 1, k_new, v_new, row, sl.rope_pos,
                                      sK, sV, lane, nks, nvs);
                     if (g == valid - 1) {
                         ks[0] = nks;
@@ -617,8 +728,8 @@ __global__ void __launch_bounds__(kThreads, 2)
                         vs[1] = nvs;
                     }
                 } else {
-                    write_new_row<DT>(pv, layer, wi.new_block, wi.head, valid - 1, k_new, v_new, wi.slot,
-                                      wi.rope_pos, sK, sV, lane);
+                    write_new_row<DT>(pv, layer, sl.new_block, wi.head, valid - 1, k_new, v_new, row, sl.rope_pos,
+                                      sK, sV, lane);
                 }
             }
             if (valid < kBlockTokens) {
@@ -671,8 +782,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         named_bar_sync(1, kConsumerWarps * 32);
 
         const int d = tid;  // 0..127: one output dim per thread
-        const int qrow = wi.slot * pv.q_heads + wi.head * pv.group;
-        float* part = pv.partials + (size_t)(i0 + j) * kPartialFloats;
+        const int qrow = row * pv.q_heads + wi.head * pv.group;
+        float* part = pv.partials + (size_t)wi.part * kPartialFloats;
         for (int h = 0; h < pv.group; ++h) {
             float M = -INFINITY;
 #pragma unroll
@@ -686,7 +797,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                 O += sm.merge_o[w][h][d] * e;
             }
             const float on = L > 0.f ? O / L : 0.f;
-            if (wi.seg_n == 1) {
+            if (!wi.split) {
                 out[(size_t)(qrow + h) * kHeadDim + d] = on;
                 if (m_out != nullptr && d == 0) {
                     m_out[qrow + h] = M * 0.6931471805599453f;
@@ -705,9 +816,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 
 // Merge of the pieces of every split segment, one CTA per (segment, query
 // head).  Launched right behind the decode grid with programmatic dependent
-// launch: its CTAs become resident early (a 4-warp one fits beside two decode
-// CTAs on an SM), read their segment descriptor -- the plan was uploaded
-// before the decode grid started -- and block in griddepcontrol.wait until
+// launch: its CTAs become resident while the decode grid runs, read their
+// segment from the kernel parameters and block in griddepcontrol.wait until
 // the decode grid has completed and its partial stores are visible.  Warp w
 // takes pieces w, w+W, ... eight at a time (all their loads issued together;
 // lane l holds dims 4l..4l+3), merging with an online log-sum-exp; the W
@@ -716,40 +826,45 @@ __global__ void __launch_bounds__(kThreads, 2)
 // more than 64 pieces (a few very long contexts over the whole GPU).
 template <int kCombineWarps>
 __global__ void __launch_bounds__(kCombineWarps * 32)
-    combine_kernel(PoolView pv, PlanView plan, int nsplits, float* __restrict__ out,
+    combine_kernel(PoolView pv, const __grid_constant__ CombineArgs cargs, float* __restrict__ out,
                    float* __restrict__ m_out, float* __restrict__ l_out) {
     static_assert(kCombineWarps * 32 >= kHeadDim, "the final merge maps one thread to each dim");
-    // A kernel launched behind this one with programmatic dependent launch
-    // (the cross-GPU exchange) may be scheduled now; it waits for this grid.
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     __shared__ float s_m[kCombineWarps], s_l[kCombineWarps];
     __shared__ __align__(16) float s_o[kCombineWarps][kHeadDim];
     const int G = pv.group;
     const int si = blockIdx.x / G, h = blockIdx.x % G;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    SplitSeg sg = {};
-    bool ok = si < nsplits;
+    bool ok = si < cargs.nsegs && si < kMaxGrid;
+    int slot = 0, head = 0, first = 0, np = 0;
     if (ok) {
-        sg = plan.splits[si];
-        if (sg.slot < 0 || sg.slot >= plan.hdr->nslots || sg.head < 0 || sg.head >= pv.kv_heads ||
-            sg.seg_first < 0 || sg.seg_n < 1 || sg.seg_first + sg.seg_n > pv.max_items) {
+        const int2 sg = cargs.seg[si];
+        slot = sg.x & 0xffff;
+        head = sg.x >> 16;
+        first = sg.y & 0xffff;
+        np = sg.y >> 16;
+        if (head >= pv.kv_heads || np < 1 || (first >> 1) + np > kMaxGrid) {
             if (threadIdx.x == 0) report(pv, 5, si, 400);
             ok = false;
         }
     }
+    // The next decode launch may start now: it overlaps this merge and the
+    // end of the decode grid (which completes before this kernel can), and
+    // it waits for this kernel before it reads or writes anything shared.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
     if (!ok) return;
-    const float* p0 = pv.partials + (size_t)sg.seg_first * kPartialFloats;
+    const int g0 = first >> 1;
     float M = -INFINITY, L = 0.f;
     float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int c0 = warp; c0 < sg.seg_n; c0 += 8 * kCombineWarps) {
+    for (int c0 = warp; c0 < np; c0 += 8 * kCombineWarps) {
         float mm[8], ll[8];
         float4 oo[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
             const int pc = c0 + u * kCombineWarps;
-            const bool live = pc < sg.seg_n;
-            const float* pp = p0 + (size_t)pc * kPartialFloats;
+            const bool live = pc < np;
+            const int pidx = pc == 0 ? first : 2 * (g0 + pc);
+            const float* pp = pv.partials + (size_t)(live ? pidx : 0) * kPartialFloats;
             mm[u] = live ? __ldcg(pp + h) : 0.f;
             ll[u] = live ? __ldcg(pp + kMaxGroup + h) : 0.f;
             oo[u] = live ? __ldcg(reinterpret_cast<const float4*>(pp + 2 * kMaxGroup + h * kHeadDim) + lane)
@@ -789,7 +904,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32)
         Lt += s_l[w] * f;
         At += s_o[w][d] * f;
     }
-    const int row = sg.slot * pv.q_heads + sg.head * G + h;
+    const int row = (cargs.row0 + slot) * pv.q_heads + head * G + h;
     out[(size_t)row * kHeadDim + d] = Lt > 0.f ? At / Lt : 0.f;
     if (m_out != nullptr && d == 0) {
         m_out[row] = Mt * 0.6931471805599453f;
@@ -800,22 +915,31 @@ __global__ void __launch_bounds__(kCombineWarps * 32)
 template <int DT>
 static cudaError_t decode_occupancy_t(int* ctas_per_sm) {
     const int smem = (int)sizeof(Smem<DT>) + 1024;
-    cudaError_t e = cudaFuncSetAttribute(decode_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(decode_kernel<DT, kSlotsSmall>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, decode_kernel<DT>, kThreads, smem);
+    e = cudaFuncSetAttribute(decode_kernel<DT, kSlotsLarge>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, decode_kernel<DT, kSlotsSmall>, kThreads, smem);
 }
 
 cudaError_t decode_occupancy(int dtype, int* ctas_per_sm) {
+    // The combine kernel runs beside two decode CTAs on an SM (resident
+    // while the decode grid streams): give it the decode kernel's
+    // shared-memory carveout, or the SM could not host both.
+    cudaError_t e = cudaFuncSetAttribute(combine_kernel<4>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(combine_kernel<16>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return e;
     return dtype == 0 ? decode_occupancy_t<0>(ctas_per_sm)
                       : dtype == 1 ? decode_occupancy_t<1>(ctas_per_sm) : decode_occupancy_t<2>(ctas_per_sm);
 }
 
-cudaError_t launch_decode(const PoolView& pv, const PlanView& plan, int nsplits, int max_pieces,
-                          int layer, const float* q, const float* k_new, const float* v_new,
-                          float* out, float* m_out, float* l_out, int grid, bool pdl, cudaStream_t st) {
-    if (grid < 1) grid = 1;
+template <int S>
+cudaError_t launch_decode(const PoolView& pv, const DecodeArgs<S>& a, const CombineArgs& c, int max_pieces,
+                          const float* q, const float* k_new, const float* v_new, float* out, float* m_out,
+                          float* l_out, bool pdl, cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)grid);
+    cfg.gridDim = dim3((unsigned)(a.grid < 1 ? 1 : a.grid));
     cfg.blockDim = dim3(kThreads);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -826,26 +950,33 @@ cudaError_t launch_decode(const PoolView& pv, const PlanView& plan, int nsplits,
     cudaError_t e;
     if (pv.dtype == 0) {
         cfg.dynamicSmemBytes = sizeof(Smem<0>) + 1024;
-        e = cudaLaunchKernelEx(&cfg, decode_kernel<0>, pv, plan, layer, q, k_new, v_new, out, m_out, l_out);
+        e = cudaLaunchKernelEx(&cfg, decode_kernel<0, S>, pv, a, q, k_new, v_new, out, m_out, l_out);
     } else if (pv.dtype == 1) {
         cfg.dynamicSmemBytes = sizeof(Smem<1>) + 1024;
-        e = cudaLaunchKernelEx(&cfg, decode_kernel<1>, pv, plan, layer, q, k_new, v_new, out, m_out, l_out);
+        e = cudaLaunchKernelEx(&cfg, decode_kernel<1, S>, pv, a, q, k_new, v_new, out, m_out, l_out);
     } else {
         cfg.dynamicSmemBytes = sizeof(Smem<2>) + 1024;
-        e = cudaLaunchKernelEx(&cfg, decode_kernel<2>, pv, plan, layer, q, k_new, v_new, out, m_out, l_out);
+        e = cudaLaunchKernelEx(&cfg, decode_kernel<2, S>, pv, a, q, k_new, v_new, out, m_out, l_out);
     }
     e = counted(e);
-    if (e != cudaSuccess || nsplits == 0) return e;
-    const bool wide = max_pieces > 64;
+    if (e != cudaSuccess || c.nsegs == 0) return e;
+    const int warps = max_pieces > 64 ? 16 : 4;
     cudaLaunchConfig_t ccfg = {};
-    ccfg.gridDim = dim3((unsigned)(nsplits * pv.group));
-    ccfg.blockDim = dim3((wide ? 16 : 4) * 32);
+    ccfg.gridDim = dim3((unsigned)(c.nsegs * pv.group));
+    ccfg.blockDim = dim3(warps * 32);
     ccfg.dynamicSmemBytes = 0;
     ccfg.stream = st;
     ccfg.attrs = attr;  // programmatic dependent of the decode grid
     ccfg.numAttrs = 1;
-    if (wide) return counted(cudaLaunchKernelEx(&ccfg, combine_kernel<16>, pv, plan, nsplits, out, m_out, l_out));
-    return counted(cudaLaunchKernelEx(&ccfg, combine_kernel<4>, pv, plan, nsplits, out, m_out, l_out));
+    if (warps == 16) return counted(cudaLaunchKernelEx(&ccfg, combine_kernel<16>, pv, c, out, m_out, l_out));
+    return counted(cudaLaunchKernelEx(&ccfg, combine_kernel<4>, pv, c, out, m_out, l_out));
 }
+
+template cudaError_t launch_decode<kSlotsSmall>(const PoolView&, const DecodeArgs<kSlotsSmall>&, const CombineArgs&,
+                                                int, const float*, const float*, const float*, float*, float*,
+                                                float*, bool, cudaStream_t);
+template cudaError_t launch_decode<kSlotsLarge>(const PoolView&, const DecodeArgs<kSlotsLarge>&, const CombineArgs&,
+                                                int, const float*, const float*, const float*, float*, float*,
+                                                float*, bool, cudaStream_t);
 
 }  // namespace kvattn

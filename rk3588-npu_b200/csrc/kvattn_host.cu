@@ -67,12 +67,22 @@ int cuda_fail(cudaError_t e, const char* what) {
         if (e_ != cudaSuccess) return cuda_fail(e_, #call); \
     } while (0)
 
-constexpr int kRing = 4;  // plan upload buffers in flight
-
 struct Seq {
     bool live = false;
     int len = 0;
     std::vector<int> blocks;
+    long long app_serial = -1;  // decode launch that last appended to this sequence
+    int app_pos = -1;           // the position it wrote
+};
+
+// One decode launch's share of a plan (at most kSlotsLarge sequences): the
+// kernel parameters of its launches.
+struct SubPlan {
+    int row0 = 0, nslots = 0, grid = 0, total = 0, max_pieces = 0;
+    std::vector<DecodeSlot> slots;
+    std::vector<int> slot_f0;            // nslots + 1
+    std::vector<int> cta_f0;             // grid + 1
+    std::vector<int2> comb;              // split segments (CombineArgs::seg)
 };
 
 }  // namespace
@@ -86,9 +96,7 @@ struct kvp_pool {
     int num_blocks = 0, dtype = 0, max_seqs = 0, max_seq_len = 0, mbps = 0;
     float theta = 0.f;
     int num_sms = 0, occupancy = 0;
-    bool overlap = false;  // decode launches as programmatic dependents (kvp_set_overlap)
-    long max_items = 0;
-    long max_tiles = 0;  // bound on flat blocks in one plan
+    bool overlap = false;  // decode launches may copy their first tiles early (kvp_set_overlap)
     PoolView pv{};
 
     // device allocations
@@ -96,7 +104,6 @@ struct kvp_pool {
     void* d_v = nullptr;
     float2* d_rope = nullptr;
     int* d_table = nullptr;
-    int* d_counters = nullptr;
     float* d_partials = nullptr;
     int* d_status = nullptr;
     float* d_prefill_part = nullptr;  // key-split partials of attn_prefill (grown on demand)
@@ -114,25 +121,24 @@ struct kvp_pool {
     size_t pending_cap = 0;
     cudaEvent_t pending_evt = nullptr;
 
-    // plan ring
-    size_t plan_bytes = 0;
-    uint8_t* h_plan[kRing] = {};
-    uint8_t* d_plan[kRing] = {};
-    cudaEvent_t copy_done[kRing] = {};  // upload of ring slot r finished (copy stream)
-    cudaEvent_t slot_free[kRing] = {};  // last launch reading ring slot r finished
-    cudaStream_t copy_stream = nullptr; // non-blocking: plan uploads overlap running kernels
-    int ring_next = 0;
-
     // active plan
     bool plan_active = false;
-    bool plan_patched = false;
-    int plan_slot_ring = 0;
-    int plan_nslots = 0, plan_nitems = 0, plan_npatch = 0, plan_grid = 0, plan_nsplits = 0;
-    int plan_max_pieces = 0;  // most pieces of one split segment
-    PlanView plan_view{};
+    bool plan_patched = false;           // its new blocks are in the device table (or queued)
+    std::vector<SubPlan> subs;
+    std::vector<TablePatch> plan_patches;  // the plan's new blocks
     std::vector<int> plan_seqs;
     std::vector<int> plan_append;
+    std::vector<DecodeSlot> plan_slots;
+    std::vector<unsigned> seen;   // duplicate check of a plan's ids (stamp per plan)
+    unsigned seen_stamp = 0;
     cudaStream_t plan_stream = nullptr;
+
+    // What the previous decode launch may still be writing when the next one
+    // starts early (see decode_call).
+    long long launch_serial = 0;  // decode launches made
+    int last_layer = -1;          // layer of the previous decode launch
+    bool last_patched = false;    // the previous decode launch wrote table entries
+    bool dirty = true;            // another pool-writing kernel ran since the previous decode launch
 
     // launch timing (kvp_timing_enable)
     bool timing = false;
@@ -214,22 +220,24 @@ int flush_pending(kvp_pool* p, cudaStream_t st) {
     KV_CUDA(cudaEventRecord(p->pending_evt, st));
     KV_CUDA(launch_patch(p->pv, p->d_pending, (int)n, st));
     p->pending.clear();
+    p->dirty = true;
     return KV_OK;
+}
+
+// A plan whose new blocks no decode launch has entered in the device table
+// yet (it may never get one): queue them like reserved blocks.
+void queue_plan_patches(kvp_pool* p) {
+    if (p->plan_active && !p->plan_patched) {
+        p->pending.insert(p->pending.end(), p->plan_patches.begin(), p->plan_patches.end());
+        p->plan_patched = true;
+    }
 }
 
 // Make the device block table current: queued patches and, if no layer call
 // applied them yet, the active plan's new-block patches.
 int sync_table(kvp_pool* p, cudaStream_t st) {
-    int rc = flush_pending(p, st);
-    if (rc != KV_OK) return rc;
-    if (p->plan_active && !p->plan_patched && p->plan_npatch > 0) {
-        const int r = p->plan_slot_ring;
-        KV_CUDA(cudaStreamWaitEvent(st, p->copy_done[r], 0));
-        KV_CUDA(launch_patch(p->pv, p->plan_view.patches, p->plan_npatch, st));
-        KV_CUDA(cudaEventRecord(p->slot_free[r], st));
-        p->plan_patched = true;
-    }
-    return KV_OK;
+    queue_plan_patches(p);
+    return flush_pending(p, st);
 }
 
 int require_device(const kvp_pool* p) {
@@ -243,45 +251,17 @@ int check_seq(const kvp_pool* p, int seq) {
     return KV_OK;
 }
 
-// Byte layout of one packed plan: header, slots, items, patches, CTA
-// descriptors, tile list.
-struct PlanLayout {
-    size_t slots, items, patches, cta, tiles, splits, bytes;
-};
-
-size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
-
-PlanLayout plan_layout(int nslots, long nitems, int npatch, long grid, long ntiles, long nsplits) {
-    PlanLayout L;
-    L.slots = align16(sizeof(PlanHeader));
-    L.items = align16(L.slots + (size_t)nslots * sizeof(DecodeSlot));
-    L.patches = align16(L.items + (size_t)nitems * sizeof(WorkItem));
-    L.cta = align16(L.patches + (size_t)npatch * sizeof(TablePatch));
-    L.tiles = align16(L.cta + (size_t)grid * sizeof(CtaDesc));
-    L.splits = align16(L.tiles + (size_t)ntiles * sizeof(int));
-    L.bytes = align16(L.splits + (size_t)nsplits * sizeof(SplitSeg));
-    return L;
-}
-
 void free_device(kvp_pool* p) {
     cudaFree(p->d_k);
     cudaFree(p->d_v);
     cudaFree(p->d_rope);
     cudaFree(p->d_table);
-    cudaFree(p->d_counters);
     cudaFree(p->d_partials);
     cudaFree(p->d_prefill_part);
     cudaFree(p->d_status);
     cudaFree(p->d_pending);
     cudaFreeHost(p->h_pending);
     if (p->pending_evt) cudaEventDestroy(p->pending_evt);
-    for (int i = 0; i < kRing; ++i) {
-        cudaFree(p->d_plan[i]);
-        cudaFreeHost(p->h_plan[i]);
-        if (p->copy_done[i]) cudaEventDestroy(p->copy_done[i]);
-        if (p->slot_free[i]) cudaEventDestroy(p->slot_free[i]);
-    }
-    if (p->copy_stream) cudaStreamDestroy(p->copy_stream);
     for (auto& e : p->tev) {
         cudaEventDestroy(e.first);
         cudaEventDestroy(e.second);
@@ -353,9 +333,6 @@ int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, in
     p->theta = rope_theta;
     p->seqs.resize(max_seqs);
     p->reset_free_list();
-    // Pieces: every CTA boundary splits at most one segment, so items <=
-    // segments + CTAs; CTAs <= grid + segments / kMaxCtaItems (item cap).
-    p->max_items = 2L * max_seqs * num_kv_heads + 148L * 4 + 64;
 
     auto bail = [&](cudaError_t e, const char* what) {
         free_device(p);
@@ -369,17 +346,10 @@ int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, in
     } while (0)
 
     if (host_only) {
-        // Bookkeeping only: plans are built for a nominal 148-SM part and kept on the host.
+        // Bookkeeping only: plans are built for a nominal 148-SM part (two
+        // decode CTAs per SM) and kept on the host.
         p->num_sms = 148;
-        p->occupancy = 3;
-        p->max_tiles = ((long)num_blocks + max_seqs) * num_kv_heads;
-        p->plan_bytes = plan_layout(max_seqs, p->max_items, max_seqs, p->max_items, p->max_tiles,
-                                 (long)max_seqs * num_kv_heads).bytes;
-        p->h_plan[0] = (uint8_t*)malloc(p->plan_bytes);
-        if (!p->h_plan[0]) {
-            delete p;
-            return fail(KV_ERR_INVAL, "host allocation of %zu bytes failed", p->plan_bytes);
-        }
+        p->occupancy = 2;
         p->pv.num_blocks = num_blocks;
         p->pv.kv_heads = num_kv_heads;
         p->pv.q_heads = num_q_heads;
@@ -393,7 +363,6 @@ int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, in
     KV_CUDA_B(cudaDeviceGetAttribute(&p->num_sms, cudaDevAttrMultiProcessorCount, device));
     KV_CUDA_B(decode_occupancy(dtype, &p->occupancy));
     if (p->occupancy < 1) p->occupancy = 1;
-    p->max_items = 2L * max_seqs * num_kv_heads + (long)p->num_sms * p->occupancy + 64;
 
     const int tile_bytes = dtype == KV_I8 ? kTileBytesI8 : kTileBytes;
     const size_t layer_bytes = (size_t)num_blocks * num_kv_heads * tile_bytes;
@@ -409,23 +378,10 @@ int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, in
 
     KV_CUDA_B(cudaMalloc((void**)&p->d_table, (size_t)max_seqs * p->mbps * sizeof(int)));
     KV_CUDA_B(cudaMemset(p->d_table, 0, (size_t)max_seqs * p->mbps * sizeof(int)));
-    KV_CUDA_B(cudaMalloc((void**)&p->d_counters, (size_t)max_seqs * num_kv_heads * sizeof(int)));
-    KV_CUDA_B(cudaMemset(p->d_counters, 0, (size_t)max_seqs * num_kv_heads * sizeof(int)));
-    KV_CUDA_B(cudaMalloc((void**)&p->d_partials, (size_t)p->max_items * kPartialFloats * sizeof(float)));
+    KV_CUDA_B(cudaMalloc((void**)&p->d_partials, (size_t)2 * kMaxGrid * kPartialFloats * sizeof(float)));
     KV_CUDA_B(cudaMalloc((void**)&p->d_status, 32 * sizeof(int)));
     KV_CUDA_B(cudaMemset(p->d_status, 0, 32 * sizeof(int)));
     KV_CUDA_B(cudaEventCreateWithFlags(&p->pending_evt, cudaEventDisableTiming));
-
-    p->max_tiles = ((long)num_blocks + max_seqs) * num_kv_heads;
-    p->plan_bytes = plan_layout(max_seqs, p->max_items, max_seqs, p->max_items, p->max_tiles,
-                                 (long)max_seqs * num_kv_heads).bytes;
-    KV_CUDA_B(cudaStreamCreateWithFlags(&p->copy_stream, cudaStreamNonBlocking));
-    for (int i = 0; i < kRing; ++i) {
-        KV_CUDA_B(cudaMallocHost((void**)&p->h_plan[i], p->plan_bytes));
-        KV_CUDA_B(cudaMalloc((void**)&p->d_plan[i], p->plan_bytes));
-        KV_CUDA_B(cudaEventCreateWithFlags(&p->copy_done[i], cudaEventDisableTiming));
-        KV_CUDA_B(cudaEventCreateWithFlags(&p->slot_free[i], cudaEventDisableTiming));
-    }
 #undef KV_CUDA_B
 
     PoolView& pv = p->pv;
@@ -433,7 +389,6 @@ int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, in
     pv.v = (uint8_t*)p->d_v;
     pv.rope = p->d_rope;
     pv.table = p->d_table;
-    pv.counters = p->d_counters;
     pv.partials = p->d_partials;
     pv.status = p->d_status;
     pv.num_blocks = num_blocks;
@@ -443,7 +398,6 @@ int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, in
     pv.max_blocks_per_seq = p->mbps;
     pv.max_seq_len = max_seq_len;
     pv.max_seqs = max_seqs;
-    pv.max_items = (int)p->max_items;
     pv.dtype = dtype;
     pv.layer_bytes = layer_bytes;
     pv.tile_bytes = tile_bytes;
@@ -454,7 +408,6 @@ int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, in
 int kvp_destroy(kvp_pool* p) {
     if (!p) return KV_OK;
     if (p->host_only) {
-        free(p->h_plan[0]);
         delete p;
         return KV_OK;
     }
@@ -481,6 +434,7 @@ int kvp_reset(kvp_pool* p, void* stream) {
     p->reset_free_list();
     p->pending.clear();
     p->plan_active = false;
+    p->dirty = true;
     return KV_OK;
 }
 
@@ -643,6 +597,7 @@ int kvp_import(kvp_pool* p, int layer, int seq, int pos0, int n, const void* k_r
     rc = sync_table(p, st);
     if (rc) return rc;
     KV_CUDA(launch_import(p->pv, layer, seq, pos0, n, (const uint16_t*)k_rows, (const uint16_t*)v_rows, st));
+    p->dirty = true;
     return KV_OK;
 }
 
@@ -669,6 +624,7 @@ int kvp_import_i8(kvp_pool* p, int layer, int seq, int pos0, int n, const void* 
     if (rc) return rc;
     KV_CUDA(launch_import_i8(p->pv, layer, seq, pos0, n, (const int8_t*)k_codes, (const int8_t*)v_codes, k_scales,
                              v_scales, st));
+    p->dirty = true;
     return KV_OK;
 }
 
@@ -782,6 +738,7 @@ int kv_append_chunk_batch(kvp_pool* p, int layer, int nreq, const int* seqs, con
         cb.row0[cb.nreq] = (int)(row - base);
         KV_CUDA(launch_append_batch(p->pv, layer, cb, k + base * kvw, v + base * kvw, st));
     }
+    p->dirty = true;
     return KV_OK;
 }
 
@@ -993,6 +950,126 @@ int attn_prefill_mma(kvp_pool* p, int layer, int seq, int pos0, int n, const flo
     return prefill_mma_launch(p, layer, seq, pos0, n, q, out, st);
 }
 
+}  // extern "C"
+
+namespace {
+
+// Work partition of one sub-plan whose slots are filled: every CTA gets one
+// contiguous run of the flat (slot, KV head, block) sequence of about equal
+// cost, a piece costing its blocks plus kPieceCost block-equivalents (warp
+// merge, q reload, partial write), so CTAs holding two pieces take fewer
+// blocks and every CTA finishes at about the same time.  A segment crossing
+// a CTA boundary becomes pieces merged by the combine kernel.
+void partition(const kvp_pool* p, SubPlan& sp) {
+    const int kvh = p->kv_heads;
+    const int n = sp.nslots;
+    sp.slot_f0.resize(n + 1);
+    long T = 0;
+    int nseg = 0;
+    for (int i = 0; i < n; ++i) {
+        sp.slot_f0[i] = (int)T;
+        const int nb = (sp.slots[i].kv_len + kBlockTokens - 1) / kBlockTokens;
+        T += (long)kvh * nb;
+        if (nb) nseg += kvh;
+    }
+    sp.slot_f0[n] = (int)T;
+    sp.total = (int)T;
+    constexpr long kPieceCost = 6;
+    const long gmax = std::max(1L, std::min<long>(kMaxGrid, (long)p->num_sms * p->occupancy));
+    // At least 16 blocks per CTA: below that, a split costs more (a merge)
+    // than the blocks it moves to another SM.
+    const long G = std::min(gmax, std::max(1L, (T + 15) / 16));
+    long per = std::max(kPieceCost + 1, (T + kPieceCost * (nseg + G - 1) + G - 1) / G);
+    for (;;) {
+        sp.cta_f0.resize(1);
+        sp.cta_f0[0] = 0;
+        sp.comb.clear();
+        sp.max_pieces = 0;
+        long fill = 0;
+        int cta_items = 0;
+        for (int i = 0; i < n; ++i) {
+            const int nb = (sp.slots[i].kv_len + kBlockTokens - 1) / kBlockTokens;
+            for (int h = 0; nb > 0 && h < kvh; ++h) {
+                const long F = sp.slot_f0[i] + (long)h * nb;
+                int b = 0, pieces = 0, first = 0;
+                while (b < nb) {
+                    if (cta_items > 0 && (fill + kPieceCost >= per || cta_items == kMaxCtaItems)) {
+                        sp.cta_f0.push_back((int)(F + b));
+                        fill = 0;
+                        cta_items = 0;
+                    }
+                    // A split segment's first piece is its CTA's first (partial
+                    // 2g) or last (2g + 1) piece; every later one is a first.
+                    if (pieces == 0) first = 2 * ((int)sp.cta_f0.size() - 1) + (cta_items == 0 ? 0 : 1);
+                    fill += kPieceCost;
+                    const int take = (int)std::min<long>(nb - b, std::max(1L, per - fill));
+                    b += take;
+                    fill += take;
+                    ++cta_items;
+                    ++pieces;
+                }
+                if (pieces > 1) {
+                    sp.comb.push_back(make_int2(i | (h << 16), first | (pieces << 16)));
+                    sp.max_pieces = std::max(sp.max_pieces, pieces);
+                }
+            }
+        }
+        sp.cta_f0.push_back((int)T);
+        if ((int)sp.cta_f0.size() - 1 <= kMaxGrid) break;
+        per += per / 4 + 1;  // too many CTAs (the piece cap): coarser runs
+    }
+    sp.grid = (int)sp.cta_f0.size() - 1;
+}
+
+// The pieces of CTA g of a sub-plan, derived from its flat range exactly as
+// the kernel derives them: (plan row, head, b0, b1) for each.
+template <class F>
+void cta_pieces(const kvp_pool* p, const SubPlan& sp, int g, F&& emit) {
+    const int kvh = p->kv_heads;
+    int f = sp.cta_f0[g];
+    const int f1 = sp.cta_f0[g + 1];
+    int i = 0;
+    while (f < f1) {
+        while (i + 1 <= sp.nslots - 1 && sp.slot_f0[i + 1] <= f) ++i;
+        const int nb = (sp.slots[i].kv_len + kBlockTokens - 1) / kBlockTokens;
+        const int r = f - sp.slot_f0[i];
+        const int h = r / nb, b = r - h * nb;
+        const int e = std::min(sp.slot_f0[i] + (h + 1) * nb, f1);
+        emit(sp.row0 + i, h, b, b + (e - f));
+        f = e;
+        (void)kvh;
+    }
+}
+
+template <int S>
+void fill_args(const kvp_pool* p, const SubPlan& sp, int layer, int flags, DecodeArgs<S>& a) {
+    a.nslots = sp.nslots;
+    a.grid = sp.grid;
+    a.layer = layer;
+    a.flags = flags;
+    a.total = sp.total;
+    a.row0 = sp.row0;
+    a.pad[0] = a.pad[1] = 0;
+    for (int i = 0; i < sp.nslots; ++i) {
+        const DecodeSlot& sl = sp.slots[i];
+        a.slot[i] = sl;
+        a.slot_f0[i] = sp.slot_f0[i];
+        // A row the previous decode launch of this pool appended (to the
+        // same layer, or with a table entry it wrote) is read only after
+        // that launch finishes.
+        const Seq& sq = p->seqs[sl.seq];
+        const bool prev = sq.app_serial >= 0 && sq.app_serial == p->launch_serial - 1 &&
+                          (p->last_layer == layer || p->last_patched);
+        a.defer_blk[i] = prev ? sq.app_pos / kBlockTokens : -1;
+    }
+    a.slot_f0[sp.nslots] = sp.total;
+    for (int g = 0; g <= sp.grid; ++g) a.cta_f0[g] = sp.cta_f0[g];
+}
+
+}  // namespace
+
+extern "C" {
+
 int attn_decode_plan_ex(kvp_pool* p, int nseq, const int* seq_ids, const int* rope_pos,
                         const int* append, void* stream) {
     if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
@@ -1003,14 +1080,17 @@ int attn_decode_plan_ex(kvp_pool* p, int nseq, const int* seq_ids, const int* ro
     cudaStream_t st = (cudaStream_t)stream;
 
     // ---- validate everything before changing anything ----
-    std::vector<char> seen(p->max_seqs, 0);
+    if (p->seen.size() != (size_t)p->max_seqs || ++p->seen_stamp == 0) {
+        p->seen.assign(p->max_seqs, 0u);
+        p->seen_stamp = 1;
+    }
     int new_blocks = 0;
     for (int i = 0; i < nseq; ++i) {
         const int sid = seq_ids[i];
         int rc = check_seq(p, sid);
         if (rc) return rc;
-        if (seen[sid]) return fail(KV_ERR_INVAL, "sequence %d listed twice", sid);
-        seen[sid] = 1;
+        if (p->seen[sid] == p->seen_stamp) return fail(KV_ERR_INVAL, "sequence %d listed twice", sid);
+        p->seen[sid] = p->seen_stamp;
         const Seq& s = p->seqs[sid];
         const int app = append ? (append[i] != 0) : 1;
         const int rp = rope_pos ? rope_pos[i] : s.len;
@@ -1025,189 +1105,49 @@ int attn_decode_plan_ex(kvp_pool* p, int nseq, const int* seq_ids, const int* ro
         return fail(KV_ERR_OOM, "decode step needs %d new blocks, %zu free", new_blocks, p->free_.size());
 
     // A plan that never reached a layer call still owes its table entries.
-    if (p->plan_active && !p->plan_patched && p->plan_npatch > 0 && !p->host_only) {
-        const int r0 = p->plan_slot_ring;
-        KV_CUDA(cudaStreamWaitEvent(st, p->copy_done[r0], 0));
-        KV_CUDA(launch_patch(p->pv, p->plan_view.patches, p->plan_npatch, st));
-        KV_CUDA(cudaEventRecord(p->slot_free[r0], st));
-        p->plan_patched = true;
-    }
+    queue_plan_patches(p);
     int rc = flush_pending(p, st);
     if (rc) return rc;
 
     // ---- slots (and the blocks new tokens start) ----
-    const int r = p->host_only ? 0 : p->ring_next;
-    p->ring_next = (r + 1) % kRing;
-    if (!p->host_only) KV_CUDA(cudaEventSynchronize(p->copy_done[r]));  // host buffer reusable
-    uint8_t* h = p->h_plan[r];
-    std::vector<DecodeSlot> slots(nseq);
-    std::vector<TablePatch> patches;
+    std::vector<DecodeSlot>& slots = p->plan_slots;
+    slots.resize(nseq);
+    p->plan_patches.clear();
     p->plan_seqs.assign(seq_ids, seq_ids + nseq);
     p->plan_append.resize(nseq);
-    long total_blocks = 0;
-    int nsegments = 0;
     for (int i = 0; i < nseq; ++i) {
         const int sid = seq_ids[i];
         Seq& s = p->seqs[sid];
         const int app = append ? (append[i] != 0) : 1;
         DecodeSlot& sl = slots[i];
-        sl = DecodeSlot{};
         sl.seq = sid;
         sl.kv_len = s.len + app;
         sl.rope_pos = rope_pos ? rope_pos[i] : s.len;
-        sl.append = app;
         sl.new_block = -1;
         if (app) {
             const int idx = s.len / kBlockTokens;
             if (idx >= (int)s.blocks.size()) {
                 const int b = p->pop_block();
                 s.blocks.push_back(b);
-                patches.push_back(TablePatch{sid, idx, b, 0});
+                p->plan_patches.push_back(TablePatch{sid, idx, b, 0});
             }
             sl.new_block = s.blocks[idx];
         }
         p->plan_append[i] = app;
-        total_blocks += (long)p->kv_heads * ((sl.kv_len + kBlockTokens - 1) / kBlockTokens);
-        nsegments += p->kv_heads;
     }
-
-    // ---- pieces: each CTA gets one contiguous, equal run of the flattened
-    // (slot, kv head, block) sequence; a segment crossing a CTA boundary is
-    // cut into pieces whose partial results are merged on the device ----
-    // Cost model: a piece costs its blocks plus kPieceCost block-equivalents
-    // (warp merge, q reload, partial write), so CTAs holding two pieces take
-    // fewer blocks and every CTA finishes at about the same time.
-    constexpr long kPieceCost = 6;
-    const long gmax = std::max(1L, (long)p->num_sms * p->occupancy);
-    // At least 16 blocks per CTA: below that, a split costs more (a merge
-    // launch) than the blocks it moves to another SM.
-    const long G = std::min(gmax, std::max(1L, (total_blocks + 15) / 16));
-    const long per = std::max(kPieceCost + 1,
-                              (total_blocks + kPieceCost * (nsegments + G - 1) + G - 1) / G);
-    std::vector<WorkItem> items;
-    std::vector<int> cta_start(1, 0);
-    long fill = 0;
-    int cta_items = 0;
-    auto piece = [&](int i, int hd, int b0, int b1, int seg_first) {
-        const DecodeSlot& sl = slots[i];
-        return WorkItem{i, hd, b0, b1, seg_first, 1, sl.seq, sl.kv_len, sl.rope_pos, sl.append,
-                        sl.new_block, 0};
-    };
-    auto close_cta = [&]() {
-        cta_start.push_back((int)items.size());
-        fill = 0;
-        cta_items = 0;
-    };
-    for (int i = 0; i < nseq; ++i) {
-        const int nblk = (slots[i].kv_len + kBlockTokens - 1) / kBlockTokens;
-        for (int hd = 0; hd < p->kv_heads; ++hd) {
-            const int seg_first = (int)items.size();
-            if (nblk == 0) {  // nothing to attend: one empty piece still writes the (zero) result
-                if (fill + kPieceCost > per || cta_items == kMaxCtaItems) close_cta();
-                items.push_back(piece(i, hd, 0, 0, seg_first));
-                fill += kPieceCost;
-                ++cta_items;
-                continue;
-            }
-            int b = 0;
-            while (b < nblk) {
-                if (fill + kPieceCost >= per || cta_items == kMaxCtaItems) close_cta();
-                fill += kPieceCost;
-                const int take = (int)std::min<long>(nblk - b, per - fill);
-                items.push_back(piece(i, hd, b, b + take, seg_first));
-                b += take;
-                fill += take;
-                ++cta_items;
-            }
-            const int seg_n = (int)items.size() - seg_first;
-            for (int x = seg_first; x < (int)items.size(); ++x) items[x].seg_n = seg_n;
-        }
+    // ---- one launch per kSlotsLarge sequences, each partitioned on its own ----
+    // (the sub-plans' buffers are reused from plan to plan)
+    p->subs.resize((nseq + kSlotsLarge - 1) / kSlotsLarge);
+    for (size_t k = 0; k < p->subs.size(); ++k) {
+        SubPlan& sp = p->subs[k];
+        sp.row0 = (int)k * kSlotsLarge;
+        sp.nslots = std::min(kSlotsLarge, nseq - sp.row0);
+        sp.slots.assign(slots.begin() + sp.row0, slots.begin() + sp.row0 + sp.nslots);
+        partition(p, sp);
     }
-    close_cta();
-    const int grid = (int)cta_start.size() - 1;
-    if ((long)items.size() > p->max_items || grid > p->max_items)
-        return fail(KV_ERR_STATE, "work list overflow (%zu items, %d CTAs)", items.size(), grid);
-
-    // ---- per-CTA descriptors and the flat tile list (the host owns the
-    // block tables, so the kernel needs no table reads to start copying) ----
-    std::vector<CtaDesc> ctas(grid);
-    std::vector<int> tiles;
-    tiles.reserve((size_t)total_blocks);
-    for (int gi = 0; gi < grid; ++gi) {
-        ctas[gi] = CtaDesc{cta_start[gi], cta_start[gi + 1] - cta_start[gi], (int)tiles.size(), 0,
-                           {-2, -2, -2, -2, -2, -2, -2, -2}};
-        for (int x = cta_start[gi]; x < cta_start[gi + 1]; ++x) {
-            const WorkItem& w = items[x];
-            const Seq& sq = p->seqs[w.seq];
-            const int last = (w.kv_len - 1) / kBlockTokens;
-            for (int b = w.b0; b < w.b1; ++b) {
-                const bool newblk = w.append && b == last;
-                const int valid = std::min(kBlockTokens, w.kv_len - b * kBlockTokens);
-                const int blk = newblk ? w.new_block : sq.blocks[b];
-                tiles.push_back(newblk && valid == 1 ? -1 : blk * p->kv_heads + w.head);
-            }
-        }
-        ctas[gi].nf = (int)tiles.size() - ctas[gi].f0;
-        for (int x = 0; x < 8 && x < ctas[gi].nf; ++x) ctas[gi].first[x] = tiles[ctas[gi].f0 + x];
-    }
-    if ((long)tiles.size() > p->max_tiles)
-        return fail(KV_ERR_STATE, "tile list overflow (%zu > %ld)", tiles.size(), p->max_tiles);
-    std::vector<SplitSeg> splits;
-    for (size_t x = 0; x < items.size(); ++x)
-        if (items[x].seg_n > 1 && (int)x == items[x].seg_first)
-            splits.push_back(SplitSeg{items[x].slot, items[x].head, items[x].seg_first, items[x].seg_n});
-
-    // ---- pack and upload once, on the copy stream ----
-    const PlanLayout L = plan_layout(nseq, (long)items.size(), (int)patches.size(), grid, (long)tiles.size(),
-                                     (long)splits.size());
-    PlanHeader* hdr = (PlanHeader*)h;
-    hdr->nslots = nseq;
-    hdr->nitems = (int)items.size();
-    hdr->npatch = (int)patches.size();
-    hdr->grid = grid;
-    hdr->off_slots = (int)L.slots;
-    hdr->off_items = (int)L.items;
-    hdr->off_patches = (int)L.patches;
-    hdr->off_cta = (int)L.cta;
-    hdr->off_tiles = (int)L.tiles;
-    hdr->ntiles = (int)tiles.size();
-    hdr->off_splits = (int)L.splits;
-    hdr->nsplits = (int)splits.size();
-    memcpy(h + L.slots, slots.data(), slots.size() * sizeof(DecodeSlot));
-    memcpy(h + L.items, items.data(), items.size() * sizeof(WorkItem));
-    if (!patches.empty()) memcpy(h + L.patches, patches.data(), patches.size() * sizeof(TablePatch));
-    memcpy(h + L.cta, ctas.data(), ctas.size() * sizeof(CtaDesc));
-    if (!tiles.empty()) memcpy(h + L.tiles, tiles.data(), tiles.size() * sizeof(int));
-    if (!splits.empty()) memcpy(h + L.splits, splits.data(), splits.size() * sizeof(SplitSeg));
-
     p->plan_active = true;
-    p->plan_patched = patches.empty();
-    p->plan_slot_ring = r;
-    p->plan_nslots = nseq;
-    p->plan_nitems = (int)items.size();
-    p->plan_npatch = (int)patches.size();
-    p->plan_grid = grid;
-    const uint8_t* base = p->host_only ? h : p->d_plan[r];
-    p->plan_view.hdr = (const PlanHeader*)base;
-    p->plan_view.slots = (const DecodeSlot*)(base + L.slots);
-    p->plan_view.items = (const WorkItem*)(base + L.items);
-    p->plan_view.patches = (const TablePatch*)(base + L.patches);
-    p->plan_view.cta = (const CtaDesc*)(base + L.cta);
-    p->plan_view.tiles = (const int*)(base + L.tiles);
-    p->plan_view.splits = (const SplitSeg*)(base + L.splits);
-    p->plan_nsplits = (int)splits.size();
-    p->plan_max_pieces = 0;
-    for (const SplitSeg& sg : splits) p->plan_max_pieces = std::max(p->plan_max_pieces, sg.seg_n);
+    p->plan_patched = p->plan_patches.empty() || p->host_only;
     p->plan_stream = st;
-    if (p->host_only) {
-        p->plan_patched = true;
-        return KV_OK;
-    }
-    // The previous launches that read ring slot r must be done before the
-    // copy overwrites it; the copy itself overlaps whatever runs now.
-    KV_CUDA(cudaStreamWaitEvent(p->copy_stream, p->slot_free[r], 0));
-    KV_CUDA(cudaMemcpyAsync(p->d_plan[r], h, L.bytes, cudaMemcpyHostToDevice, p->copy_stream));
-    KV_CUDA(cudaEventRecord(p->copy_done[r], p->copy_stream));
     return KV_OK;
 }
 
@@ -1215,30 +1155,36 @@ int kvp_plan_info(const kvp_pool* p, int* nitems, int* grid, int* npatch, int* i
                   int* item_head, int* item_b0, int* item_b1, int cap) {
     if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
     if (!p->plan_active) return fail(KV_ERR_STATE, "no active decode plan");
-    const uint8_t* h = p->h_plan[p->plan_slot_ring];
-    const PlanHeader* hdr = (const PlanHeader*)h;
-    const WorkItem* items = (const WorkItem*)(h + hdr->off_items);
-    if (nitems) *nitems = hdr->nitems;
-    if (grid) *grid = hdr->grid;
-    if (npatch) *npatch = hdr->npatch;
-    const int n = std::min(cap, hdr->nitems);
-    for (int i = 0; i < n; ++i) {
-        if (item_slot) item_slot[i] = items[i].slot;
-        if (item_head) item_head[i] = items[i].head;
-        if (item_b0) item_b0[i] = items[i].b0;
-        if (item_b1) item_b1[i] = items[i].b1;
+    int n = 0, gtot = 0;
+    for (const SubPlan& sp : p->subs) {
+        for (int g = 0; g < sp.grid; ++g)
+            cta_pieces(p, sp, g, [&](int slot, int h, int b0, int b1) {
+                if (n < cap) {
+                    if (item_slot) item_slot[n] = slot;
+                    if (item_head) item_head[n] = h;
+                    if (item_b0) item_b0[n] = b0;
+                    if (item_b1) item_b1[n] = b1;
+                }
+                ++n;
+            });
+        gtot += sp.grid;
     }
+    if (nitems) *nitems = n;
+    if (grid) *grid = gtot;
+    if (npatch) *npatch = (int)p->plan_patches.size();
     return KV_OK;
 }
 
 int kvp_plan_cta_start(const kvp_pool* p, int* cta_start, int cap) {
     if (!p || !cta_start) return fail(KV_ERR_INVAL, "NULL argument");
     if (!p->plan_active) return fail(KV_ERR_STATE, "no active decode plan");
-    const uint8_t* h = p->h_plan[p->plan_slot_ring];
-    const PlanHeader* hdr = (const PlanHeader*)h;
-    const CtaDesc* cs = (const CtaDesc*)(h + hdr->off_cta);
-    const int n = std::min(cap, hdr->grid + 1);
-    for (int i = 0; i < n; ++i) cta_start[i] = i < hdr->grid ? cs[i].i0 : hdr->nitems;
+    int k = 0, n = 0;
+    for (const SubPlan& sp : p->subs)
+        for (int g = 0; g < sp.grid; ++g, ++k) {
+            if (k < cap) cta_start[k] = n;
+            cta_pieces(p, sp, g, [&](int, int, int, int) { ++n; });
+        }
+    if (k < cap) cta_start[k] = n;
     return KV_OK;
 }
 
@@ -1260,34 +1206,64 @@ static int decode_call(kvp_pool* p, int layer, const float* q, const float* k_ne
     XchgArgs xa;
     if (x) {
         // the local states go to this rank's slot of the exchange area
-        if (int rc = xchg_prepare(x, p->device, p->plan_nslots * p->q_heads, p->pv.status, x_out, &xa,
+        if (int rc = xchg_prepare(x, p->device, (int)p->plan_seqs.size() * p->q_heads, p->pv.status, x_out, &xa,
                                   &m, &l, &out))
             return rc;
     }
     DeviceGuard dg(p->device);
     cudaStream_t st = (cudaStream_t)stream;
-    const int r = p->plan_slot_ring;
-    KV_CUDA(cudaStreamWaitEvent(st, p->copy_done[r], 0));
-    std::pair<cudaEvent_t, cudaEvent_t>* te = nullptr;
-    if (p->timing) {
-        if (p->tev_used == p->tev.size()) {
-            cudaEvent_t a, b;
-            KV_CUDA(cudaEventCreate(&a));
-            KV_CUDA(cudaEventCreate(&b));
-            p->tev.emplace_back(a, b);
+    // With kvp_set_overlap, programmatic dependent launches: the decode grid
+    // starts while the previous kernel in the stream finishes and copies its
+    // first tiles then.  Only on a created stream (the legacy default stream
+    // keeps ordinary launches), and not while timing: events between
+    // launches would serialise them anyway.
+    const bool pdl = p->overlap && !p->timing && st != nullptr && st != cudaStreamLegacy;
+    for (const SubPlan& sp : p->subs) {
+        int flags = 0;
+        if (pdl && !p->dirty) flags |= kDecEarly;
+        if (!p->plan_patched) flags |= kDecPatch;
+        std::pair<cudaEvent_t, cudaEvent_t>* te = nullptr;
+        if (p->timing) {
+            if (p->tev_used == p->tev.size()) {
+                cudaEvent_t a, b;
+                KV_CUDA(cudaEventCreate(&a));
+                KV_CUDA(cudaEventCreate(&b));
+                p->tev.emplace_back(a, b);
+            }
+            te = &p->tev[p->tev_used++];
+            KV_CUDA(cudaEventRecord(te->first, st));
         }
-        te = &p->tev[p->tev_used++];
-        KV_CUDA(cudaEventRecord(te->first, st));
+        CombineArgs ca;
+        ca.nsegs = (int)sp.comb.size();
+        ca.row0 = sp.row0;
+        ca.pad[0] = ca.pad[1] = 0;
+        for (size_t i = 0; i < sp.comb.size(); ++i) ca.seg[i] = sp.comb[i];
+        if (sp.nslots <= kSlotsSmall) {
+            DecodeArgs<kSlotsSmall> a;
+            fill_args(p, sp, layer, flags, a);
+            KV_CUDA(launch_decode(p->pv, a, ca, sp.max_pieces, q, k_new, v_new, out, m, l, pdl, st));
+        } else {
+            static thread_local DecodeArgs<kSlotsLarge> a;  // 7 KB: kept off the stack
+            fill_args(p, sp, layer, flags, a);
+            KV_CUDA(launch_decode(p->pv, a, ca, sp.max_pieces, q, k_new, v_new, out, m, l, pdl, st));
+        }
+        if (te) KV_CUDA(cudaEventRecord(te->second, st));
+        for (const DecodeSlot& sl : sp.slots)
+            if (sl.new_block >= 0) {
+                Seq& sq = p->seqs[sl.seq];
+                sq.app_serial = p->launch_serial;
+                sq.app_pos = sl.kv_len - 1;
+            }
+        p->last_layer = layer;
+        p->last_patched = (flags & kDecPatch) != 0;
+        p->launch_serial++;
+        p->dirty = false;
     }
-    KV_CUDA(launch_decode(p->pv, p->plan_view, p->plan_nsplits, p->plan_max_pieces, layer, q, k_new,
-                          v_new, out, m, l, p->plan_grid, p->overlap && !te, st));
+    p->plan_patched = true;
     if (x) {
         KV_CUDA(launch_xchg(xa, st));
         xchg_commit(x);
     }
-    if (te) KV_CUDA(cudaEventRecord(te->second, st));
-    KV_CUDA(cudaEventRecord(p->slot_free[r], st));
-    p->plan_patched = true;
     return KV_OK;
 }
 
@@ -1348,13 +1324,9 @@ int attn_decode_commit(kvp_pool* p) {
     if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
     std::lock_guard<std::mutex> lk(p->mu);
     if (!p->plan_active) return fail(KV_ERR_STATE, "no active decode plan");
-    if (!p->plan_patched && p->plan_npatch > 0 && !p->host_only) {
-        DeviceGuard dg(p->device);
-        const int r = p->plan_slot_ring;
-        KV_CUDA(cudaStreamWaitEvent(p->plan_stream, p->copy_done[r], 0));
-        KV_CUDA(launch_patch(p->pv, p->plan_view.patches, p->plan_npatch, p->plan_stream));
-        KV_CUDA(cudaEventRecord(p->slot_free[r], p->plan_stream));
-    }
+    // New blocks of a plan that no layer call entered in the table are
+    // queued; the next call that touches the device applies them.
+    queue_plan_patches(p);
     for (size_t i = 0; i < p->plan_seqs.size(); ++i)
         if (p->plan_append[i]) p->seqs[p->plan_seqs[i]].len += 1;
     p->plan_active = false;

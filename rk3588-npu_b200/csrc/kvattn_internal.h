@@ -27,36 +27,6 @@ __host__ __device__ inline uint32_t tile_offset(int t, int d) {
     return (uint32_t)(((d >> 6) * 16 + t) * 128 + ((((d >> 3) & 7) ^ (t & 7)) << 4) + (d & 7) * 2);
 }
 
-// One batch row of a decode plan.
-struct DecodeSlot {
-    int seq;        // row of the block table
-    int kv_len;     // tokens attended (including the new one when append)
-    int rope_pos;   // position used to rotate q and the new k
-    int append;     // 1: write the new token at local slot kv_len-1
-    int new_block;  // block id holding slot kv_len-1 when append (else -1)
-    int pad[3];
-};
-
-// One piece of work: blocks [b0, b1) of the segment (slot, kv head).  A
-// segment (all blocks of one sequence for one KV head) is cut into seg_n
-// consecutive pieces starting at item index seg_first; each CTA owns a
-// contiguous run of items, so pieces of one segment sit in different CTAs.
-// The slot's fields are repeated here so a CTA needs one load per piece.
-struct WorkItem {
-    int slot;
-    int head;
-    int b0;
-    int b1;
-    int seg_first;
-    int seg_n;
-    int seq;        // = slots[slot].seq
-    int kv_len;     // = slots[slot].kv_len
-    int rope_pos;   // = slots[slot].rope_pos
-    int append;     // = slots[slot].append
-    int new_block;  // = slots[slot].new_block
-    int pad;
-};
-
 // A block-table entry to write before use: table[seq][idx] = block.
 struct TablePatch {
     int seq;
@@ -65,42 +35,56 @@ struct TablePatch {
     int pad;
 };
 
-// Per-CTA descriptor: pieces [i0, i0 + n) and flat blocks [f0, f0 + nf) of
-// the plan's tile list.
-struct CtaDesc {
-    int i0;
-    int n;
-    int f0;
-    int nf;
-    int first[8];  // tiles[f0 .. f0+7] (or -2 past nf): the first ring round needs no second load
+// ---- decode plans (kernel parameters) ---------------------------------
+// A decode step is passed to its launches by value: the host owns the block
+// tables and lengths, so it builds the work partition in O(sequences + CTAs)
+// and no plan is uploaded.  Work is the flat sequence of 16-token blocks of
+// every segment (slot i, KV head h), slot-major: segment (i, h) is blocks
+// [slot_f0[i] + h * nb_i, slot_f0[i] + (h + 1) * nb_i) with nb_i =
+// ceil(kv_len_i / 16).  CTA g owns flat blocks [cta_f0[g], cta_f0[g + 1]);
+// its pieces are the maximal runs of one segment inside that range.  Only a
+// CTA's first and last piece can be part of a segment that other CTAs share
+// (a split segment); their partial states go to partials[2g] (first piece)
+// and partials[2g + 1] (last piece), merged by the combine kernel launched
+// right behind the decode grid.
+constexpr int kMaxGrid = 320;       // decode CTAs per launch (B200: 148 SMs x 2 resident)
+constexpr int kSlotsSmall = 64;     // slot capacities of the two kernel-parameter layouts
+constexpr int kSlotsLarge = 256;    // (a step with more sequences runs as several launches)
+
+struct DecodeSlot {
+    int seq;        // row of the block table
+    int kv_len;     // tokens attended (including the new one when it appends)
+    int rope_pos;   // position used to rotate q and the new k
+    int new_block;  // block holding slot kv_len-1 when the launch appends; -1: attend only
 };
 
-// The plan is one contiguous upload: header, slots, items, patches, one
-// CtaDesc per CTA, and the tile list: for every flat block of every CTA (in
-// CTA order) the tile index block * kv_heads + head to copy, or -1 for a
-// block that holds only the new token (nothing to load).
-// A segment cut into several pieces: its partial states are merged by the
-// combine kernel into the outputs of (slot, head).
-struct SplitSeg {
-    int slot;
-    int head;
-    int seg_first;
-    int seg_n;
-};
+// Flags of a decode launch.
+constexpr int kDecEarly = 1;  // copy the first ring round before the previous kernel finishes
+constexpr int kDecPatch = 2;  // write table[seq][(kv_len-1)/16] = new_block for appending slots
 
-struct PlanHeader {
+template <int S>
+struct DecodeArgs {
     int nslots;
-    int nitems;
-    int npatch;
     int grid;
-    int off_slots;    // byte offsets from the header
-    int off_items;
-    int off_patches;
-    int off_cta;
-    int off_tiles;
-    int ntiles;
-    int off_splits;
-    int nsplits;
+    int layer;
+    int flags;
+    int total;                  // flat blocks of the launch
+    int row0;                   // row of slot 0 in q / k_new / v_new / out / m / l
+    int pad[2];
+    int slot_f0[S + 1];         // flat offset of slot i's first segment; slot_f0[nslots] = total
+    DecodeSlot slot[S];
+    int defer_blk[S];           // block of slot i the previous decode launch may still write (-1: none)
+    int cta_f0[kMaxGrid + 1];   // flat range of every CTA
+};
+
+// A split segment, for the combine kernel: x = slot | head << 16, y =
+// first_part | npieces << 16.  Its pieces' partial states are at
+// first_part, then 2 * (first_part / 2 + u) for u = 1 .. npieces - 1.
+struct CombineArgs {
+    int nsegs;
+    int row0;
+    int pad[2];
+    int2 seg[kMaxGrid];
 };
 
 // Device view of the pool handed to kernels by value.
@@ -109,8 +93,7 @@ struct PoolView {
     uint8_t* v;
     const float2* rope;      // [max_seq_len][kHeadDim/2] (cos, sin)
     int* table;              // [max_seqs][max_blocks_per_seq]
-    int* counters;           // [max_seqs][kv_heads] arrival counters (kept at 0 between launches)
-    float* partials;         // [max_items][kPartialFloats]
+    float* partials;         // [2 * kMaxGrid][kPartialFloats]: split-piece states of a decode launch
     int* status;             // device status: [0] code, [1] item index, [2] detail
     int num_blocks;
     int kv_heads;
@@ -119,27 +102,20 @@ struct PoolView {
     int max_blocks_per_seq;
     int max_seq_len;
     int max_seqs;
-    int max_items;
     int dtype;               // 0 f16, 1 bf16, 2 int8 codes + per-row fp32 scales
     int tile_bytes;          // kTileBytes, or kTileBytesI8 for int8
     size_t layer_bytes;      // num_blocks * kv_heads * tile_bytes
 };
 
-// Plan as the decode kernel sees it (device pointers into one upload).
-struct PlanView {
-    const PlanHeader* hdr;
-    const DecodeSlot* slots;
-    const WorkItem* items;
-    const TablePatch* patches;
-    const CtaDesc* cta;
-    const int* tiles;
-    const SplitSeg* splits;
-};
-
 // ---- launchers (kernels.cu) ----
-cudaError_t launch_decode(const PoolView& pv, const PlanView& plan, int nsplits, int max_pieces,
-                          int layer, const float* q, const float* k_new, const float* v_new,
-                          float* out, float* m_out, float* l_out, int grid, bool pdl, cudaStream_t st);
+// One decode launch (and, when the plan splits segments, its combine launch
+// right behind it).  pdl: launch as a programmatic dependent of the previous
+// kernel in the stream (every read of state that kernel may write waits for
+// it inside the kernel).
+template <int S>
+cudaError_t launch_decode(const PoolView& pv, const DecodeArgs<S>& a, const CombineArgs& c, int max_pieces,
+                          const float* q, const float* k_new, const float* v_new, float* out, float* m_out,
+                          float* l_out, bool pdl, cudaStream_t st);
 cudaError_t decode_occupancy(int dtype, int* ctas_per_sm);
 cudaError_t launch_import(const PoolView& pv, int layer, int seq, int pos0, int n,
                           const uint16_t* k_rows, const uint16_t* v_rows, cudaStream_t st);

@@ -10,11 +10,17 @@
 // file-scope __device__ array of fixed size (kScratchFloats floats, 4 MiB),
 // which every GPU that loads this library holds until the process exits.
 //
-// Semantics are those of op_attention (worker/src/ops/op_attention.cpp:9-56)
-// on device pointers: q [seq][n_heads*128] fp32 (already rotated), caches
-// [total_len][n_kv_heads*128] 16-bit (fp16 or bf16), causal mask from
-// pos_base, out [seq][n_heads*128] fp32.  Two launches: partials per
-// (query row, KV head, split) into the scratch array, then their merge.
+// The math: for query row s (at absolute position pos_base + s) and query
+// head h of KV group g, out = softmax(q_s,h . K_g^T / sqrt(128)) V_g over keys
+// 0 .. pos_base + s (causal), with q [seq][n_heads*128] fp32 (already
+// rotated), caches [total_len][n_kv_heads*128] 16-bit (fp16 or bf16) and out
+// [seq][n_heads*128] fp32, all device pointers (q and the caches 16-byte
+// aligned).  Two launches: partials per (query row, KV head, split) into the
+// scratch array, then their merge.
+//
+// The device address of the array is looked up once per device and kept
+// for the life of the process; it belongs to that device's primary
+// context, so the entry point is not for use across cudaDeviceReset.
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -38,71 +44,106 @@ constexpr int kWarps = 4;
 static __device__ __align__(256) float g_scratch[kScratchFloats];
 
 // One partial: m[8], l[8], o[8][128] (kPartialFloats floats), base-2 logits.
-__device__ __forceinline__ float load16(const uint16_t* p, int dt) {
-    return dt == 0 ? __half2float(*reinterpret_cast<const __half*>(p)) : dec_bf16(*p);
+
+// Eight 16-bit cache values (one 16-byte load) as floats.
+__device__ __forceinline__ void load8(const uint16_t* p, int dt, float (&f)[8]) {
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p));
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if (dt == 0) {
+            const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+            f[2 * i] = t.x;
+            f[2 * i + 1] = t.y;
+        } else {
+            f[2 * i] = __uint_as_float(w[i] << 16);
+            f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+        }
+    }
 }
 
-// grid (nsplit, n_kv_heads, seq), 128 threads; lane l of each warp owns dims
-// 4l..4l+3; warps take keys w, w+4, ... of the split; states merged at the end.
+// grid (nsplit, n_kv_heads, seq), 128 threads.  Each half-warp is a key
+// stream: warp w takes key pairs t0 + 2w + 8j, its halves one key each, and
+// lane i of a half holds dims 8i..8i+7, so a key's K and V rows arrive as
+// one 16-byte load per lane; the eight streams' states are merged in shared
+// memory.
 __global__ void __launch_bounds__(kWarps * 32)
     contig_partial_kernel(const float* __restrict__ q, const uint16_t* __restrict__ kc,
                           const uint16_t* __restrict__ vc, float* __restrict__ scratch, int seq,
                           int total_len, int n_heads, int n_kv_heads, int pos_base, int nsplit,
                           int split_tokens, int dt) {
+    constexpr int kStreams = kWarps * 2;
     const int split = blockIdx.x, kvh = blockIdx.y, sq = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int stream = warp * 2 + (lane >> 4), li = lane & 15;
     const int group = n_heads / n_kv_heads;
     const int kv_dim = n_kv_heads * kHeadDim;
     const int lim = min(total_len, pos_base + sq + 1);  // keys 0..abs position (causal)
     const int t0 = split * split_tokens, t1 = min(lim, t0 + split_tokens);
     const float scale = 0.08838834764831845f * 1.4426950408889634f;  // 1/sqrt(128) * log2(e)
-    __shared__ float sm_o[kWarps][kMaxGroup][kHeadDim];
-    __shared__ float sm_m[kWarps][kMaxGroup], sm_l[kWarps][kMaxGroup];
+    __shared__ float sm_o[kStreams][kMaxGroup][kHeadDim];
+    __shared__ float sm_m[kStreams][kMaxGroup], sm_l[kStreams][kMaxGroup];
 
-    float qv[kMaxGroup][4], o[kMaxGroup][4], m[kMaxGroup], l[kMaxGroup];
+    float qv[kMaxGroup][8], o[kMaxGroup][8], m[kMaxGroup], l[kMaxGroup];
 #pragma unroll
     for (int h = 0; h < kMaxGroup; ++h) {
         m[h] = -INFINITY;
         l[h] = 0.f;
+        const float4* qr = reinterpret_cast<const float4*>(q + (size_t)sq * n_heads * kHeadDim +
+                                                           (size_t)(kvh * group + h) * kHeadDim + 8 * li);
+        const float4 a = h < group ? qr[0] : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 b = h < group ? qr[1] : make_float4(0.f, 0.f, 0.f, 0.f);
+        qv[h][0] = a.x * scale;
+        qv[h][1] = a.y * scale;
+        qv[h][2] = a.z * scale;
+        qv[h][3] = a.w * scale;
+        qv[h][4] = b.x * scale;
+        qv[h][5] = b.y * scale;
+        qv[h][6] = b.z * scale;
+        qv[h][7] = b.w * scale;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            o[h][e] = 0.f;
-            qv[h][e] = h < group ? q[(size_t)sq * n_heads * kHeadDim + (size_t)(kvh * group + h) * kHeadDim +
-                                     4 * lane + e] * scale
-                                 : 0.f;
-        }
+        for (int e = 0; e < 8; ++e) o[h][e] = 0.f;
     }
-    for (int t = t0 + warp; t < t1; t += kWarps) {
-        const uint16_t* kr = kc + (size_t)t * kv_dim + (size_t)kvh * kHeadDim + 4 * lane;
-        const uint16_t* vr = vc + (size_t)t * kv_dim + (size_t)kvh * kHeadDim + 4 * lane;
-        float kf[4], vf[4];
+    // Both halves of a warp run the same iterations (the half-warp sums
+    // shuffle with the whole warp's mask); a half whose key is past the
+    // split's end loads nothing and keeps its state.
+    for (int tp = t0 + 2 * warp; tp < t1; tp += kStreams) {
+        const int t = tp + (lane >> 4);
+        const bool valid = t < t1;
+        float kf[8], vf[8];
+        if (valid) {
+            const size_t off = (size_t)t * kv_dim + (size_t)kvh * kHeadDim + 8 * li;
+            load8(kc + off, dt, kf);
+            load8(vc + off, dt, vf);
+        } else {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            kf[e] = load16(kr + e, dt);
-            vf[e] = load16(vr + e, dt);
+            for (int e = 0; e < 8; ++e) kf[e] = vf[e] = 0.f;
         }
 #pragma unroll
         for (int h = 0; h < kMaxGroup; ++h) {
             if (h >= group) break;
-            float s = qv[h][0] * kf[0] + qv[h][1] * kf[1] + qv[h][2] * kf[2] + qv[h][3] * kf[3];
+            float s = 0.f;
 #pragma unroll
-            for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+            for (int e = 0; e < 8; ++e) s += qv[h][e] * kf[e];
+#pragma unroll
+            for (int off2 = 8; off2; off2 >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off2);  // within the half-warp
+            if (!valid) continue;
             const float mn = fmaxf(m[h], s);
             const float a = fast_exp2(m[h] - mn);  // 0 while m is -inf
             const float p = fast_exp2(s - mn);
             l[h] = l[h] * a + p;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) o[h][e] = o[h][e] * a + p * vf[e];
+            for (int e = 0; e < 8; ++e) o[h][e] = o[h][e] * a + p * vf[e];
             m[h] = mn;
         }
     }
 #pragma unroll
     for (int h = 0; h < kMaxGroup; ++h) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) sm_o[warp][h][4 * lane + e] = o[h][e];
-        if (lane == 0) {
-            sm_m[warp][h] = m[h];
-            sm_l[warp][h] = l[h];
+        for (int e = 0; e < 8; ++e) sm_o[stream][h][8 * li + e] = o[h][e];
+        if (li == 0) {
+            sm_m[stream][h] = m[h];
+            sm_l[stream][h] = l[h];
         }
     }
     __syncthreads();
@@ -110,10 +151,10 @@ __global__ void __launch_bounds__(kWarps * 32)
     float* part = scratch + ((size_t)(sq * n_kv_heads + kvh) * nsplit + split) * kPartialFloats;
     for (int h = 0; h < group; ++h) {
         float M = -INFINITY;
-        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, sm_m[w][h]);
+        for (int w = 0; w < kStreams; ++w) M = fmaxf(M, sm_m[w][h]);
         const float Mu = M == -INFINITY ? 0.f : M;
         float L = 0.f, O = 0.f;
-        for (int w = 0; w < kWarps; ++w) {
+        for (int w = 0; w < kStreams; ++w) {
             const float e = fast_exp2(sm_m[w][h] - Mu);
             L += sm_l[w][h] * e;
             O += sm_o[w][h][d] * e;
@@ -162,6 +203,7 @@ extern "C" int attn_contig_noalloc(const float* q, const void* k_cache, const vo
                                    float* out, int seq, int total_len, int n_heads, int n_kv_heads,
                                    int head_dim, int pos_base, int dtype, void* stream) {
     if (!q || !k_cache || !v_cache || !out) return KV_ERR_INVAL;
+    if (((uintptr_t)q | (uintptr_t)k_cache | (uintptr_t)v_cache) & 15) return KV_ERR_INVAL;
     if (head_dim != kHeadDim || seq < 1 || total_len < 1 || pos_base < 0 || n_kv_heads < 1 ||
         n_heads < n_kv_heads || n_heads % n_kv_heads != 0 || n_heads / n_kv_heads > kMaxGroup ||
         (dtype != KV_F16 && dtype != KV_BF16))
