@@ -250,6 +250,28 @@ int kvx_destroy(kvx_exch* x);
 int attn_decode_append_xgpu(kvp_pool* pool, int layer, const float* q, const float* k_new,
                             const float* v_new, float* out, kvx_exch* x, void* stream);
 
+/* ---- Split-KV across GPUs over NCCL -----------------------------------------
+ * No counterpart in the reference.  One communicator per rank (one process
+ * per GPU): rank 0 makes a unique id with kvn_unique_id and passes its
+ * KVN_UNIQUE_ID_BYTES bytes to the other ranks by any means (its own RPC, a
+ * file, a framework's broadcast); then every rank calls kvn_create with its
+ * rank (a collective: it returns once all ranks joined), for up to max_rows
+ * (sequence x query head) rows.  attn_decode_append_nccl then runs one layer
+ * of a sequence-split step on `stream`: the local decode over this rank's
+ * slice of the planned sequences (as attn_decode_append_partial), an NCCL
+ * all-gather of every rank's packed (m, l, o) states, and their log-sum-exp
+ * merge into out [rows][128] -- one host call per layer.  Every rank must
+ * make the same sequence of calls.  NCCL is loaded at run time (the copy
+ * already in the process if there is one, else libnccl.so.2): KV_ERR_STATE
+ * if none is found.  Destroy after the last call of every rank. */
+typedef struct kvn_comm kvn_comm;
+#define KVN_UNIQUE_ID_BYTES 128
+int kvn_unique_id(void* id);
+int kvn_create(int device, int rank, int world, const void* id, int max_rows, kvn_comm** out);
+int kvn_destroy(kvn_comm* c);
+int attn_decode_append_nccl(kvp_pool* pool, int layer, const float* q, const float* k_new,
+                            const float* v_new, float* out, kvn_comm* c, void* stream);
+
 /* The same merge over the packed buffer an all-gather of per-rank states
  * yields: packed [G][rows*(2+dim)], rank g's part laid out as
  * [m rows][l rows][o rows x dim].  No reference counterpart. */

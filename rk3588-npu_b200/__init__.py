@@ -26,6 +26,7 @@ KVP_HOST_ONLY = -1
 HEAD_DIM = 128
 BLOCK_TOKENS = 16
 KVX_HANDLE_BYTES = 64
+KVN_UNIQUE_ID_BYTES = 128
 
 _vp = C.c_void_p
 _ip = C.POINTER(C.c_int)
@@ -78,6 +79,10 @@ _SIGS = {
     "kvx_open": [_vp, C.c_int, _vp],
     "kvx_destroy": [_vp],
     "attn_decode_append_xgpu": [_vp, C.c_int, _vp, _vp, _vp, _vp, _vp, _vp],
+    "kvn_unique_id": [_vp],
+    "kvn_create": [C.c_int, C.c_int, C.c_int, _vp, C.c_int, C.POINTER(_vp)],
+    "kvn_destroy": [_vp],
+    "attn_decode_append_nccl": [_vp, C.c_int, _vp, _vp, _vp, _vp, _vp, _vp],
     "kvs_create": [C.c_int, C.c_int, C.POINTER(C.c_longlong), C.POINTER(_vp)],
     "kvs_destroy": [_vp],
     "kvs_place": [_vp, C.c_longlong, C.c_int, _ip],

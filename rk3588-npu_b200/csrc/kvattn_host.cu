@@ -1194,7 +1194,7 @@ int attn_decode_plan(kvp_pool* p, int nseq, const int* seq_ids, void* stream) {
 
 static int decode_call(kvp_pool* p, int layer, const float* q, const float* k_new, const float* v_new,
                        float* out, float* m, float* l, void* stream, kvx_exch* x = nullptr,
-                       float* x_out = nullptr) {
+                       float* x_out = nullptr, kvn_comm* nc = nullptr) {
     if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
     std::lock_guard<std::mutex> lk(p->mu);
     if (!p->plan_active) return fail(KV_ERR_STATE, "no active decode plan");
@@ -1204,11 +1204,14 @@ static int decode_call(kvp_pool* p, int layer, const float* q, const float* k_ne
     if (((uintptr_t)q | (uintptr_t)k_new | (uintptr_t)v_new) & 7)
         return fail(KV_ERR_INVAL, "q/k_new/v_new must be 8-byte aligned");
     XchgArgs xa;
+    const int rows = (int)p->plan_seqs.size() * p->q_heads;
     if (x) {
         // the local states go to this rank's slot of the exchange area
-        if (int rc = xchg_prepare(x, p->device, (int)p->plan_seqs.size() * p->q_heads, p->pv.status, x_out, &xa,
-                                  &m, &l, &out))
-            return rc;
+        if (int rc = xchg_prepare(x, p->device, rows, p->pv.status, x_out, &xa, &m, &l, &out)) return rc;
+    }
+    if (nc) {
+        // the local states go to the communicator's send buffer
+        if (int rc = nccl_prepare(nc, p->device, rows, &m, &l, &out)) return rc;
     }
     DeviceGuard dg(p->device);
     cudaStream_t st = (cudaStream_t)stream;
@@ -1264,6 +1267,7 @@ static int decode_call(kvp_pool* p, int layer, const float* q, const float* k_ne
         KV_CUDA(launch_xchg(xa, st));
         xchg_commit(x);
     }
+    if (nc) return nccl_gather_combine(nc, rows, x_out, st);
     return KV_OK;
 }
 
@@ -1318,6 +1322,13 @@ int attn_decode_append_xgpu(kvp_pool* p, int layer, const float* q, const float*
     if (!x || !out) return fail(KV_ERR_INVAL, "NULL argument");
     float* dummy = out;  // replaced by the exchange slot inside decode_call
     return decode_call(p, layer, q, k_new, v_new, dummy, dummy, dummy, stream, x, out);
+}
+
+int attn_decode_append_nccl(kvp_pool* p, int layer, const float* q, const float* k_new, const float* v_new,
+                            float* out, kvn_comm* c, void* stream) {
+    if (!c || !out) return fail(KV_ERR_INVAL, "NULL argument");
+    float* dummy = out;  // replaced by the communicator's send buffer inside decode_call
+    return decode_call(p, layer, q, k_new, v_new, dummy, dummy, dummy, stream, nullptr, out, c);
 }
 
 int attn_decode_commit(kvp_pool* p) {

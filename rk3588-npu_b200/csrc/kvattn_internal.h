@@ -5,6 +5,7 @@
 #include <stdint.h>
 
 struct kvx_exch;  // split-KV exchange object of the C ABI (xgpu_exchange.cu)
+struct kvn_comm;  // split-KV NCCL communicator of the C ABI (nccl_split.cu)
 
 namespace kvattn {
 
@@ -199,6 +200,12 @@ cudaError_t launch_xchg(const XchgArgs& a, cudaStream_t st);
 int xchg_prepare(::kvx_exch* x, int device, int rows, int* status, float* out, XchgArgs* a,
                  float** m, float** l, float** o);
 void xchg_commit(::kvx_exch* x);
+
+// ---- split-KV merge over an NCCL all-gather (nccl_split.cu) ----
+// Point m / l / o at this rank's packed state buffer of the communicator.
+int nccl_prepare(::kvn_comm* c, int device, int rows, float** m, float** l, float** o);
+// All-gather every rank's packed states on `st` and merge them into out.
+int nccl_gather_combine(::kvn_comm* c, int rows, float* out, cudaStream_t st);
 
 // ---- Qwen2 forward kernels (model_kernels.cu) ----
 // One projection y = epilogue(x W^T): W fp16 [N][K], x [M][K]: in = 0 fp16

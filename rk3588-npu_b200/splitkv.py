@@ -5,17 +5,25 @@ each sequence's positions in its own pool (rank r: positions [lo_r, hi_r) of
 the initial context; new tokens are appended on the last rank).  One decode
 step per layer:
 
-  1. each rank attends over its slice (attn_decode_append_partial), the last
-     rank also appending the new token: per (sequence, query head) a partial
-     state (m, l, o) -- max of the scaled scores, sum of exp, normalised o;
-  2. one all-gather of the packed states (NCCL over NVLink on GPUs);
-  3. attn_combine_lse_packed merges the gathered states into the output.
+  1. each rank attends over its slice, the last rank also appending the new
+     token: per (sequence, query head) a partial state (m, l, o) -- max of
+     the scaled scores, sum of exp, normalised o;
+  2. one all-gather of the packed states;
+  3. their log-sum-exp merge into the output.
 
-With transport="p2p" steps 2-3 run inside the library instead
-(attn_decode_append_xgpu): right behind the local decode, an exchange kernel
-pushes the states into every peer's area over NVLink (CUDA IPC mappings set
-up once, the handles passed through torch.distributed), waits for the peers'
-states of the same call and merges -- one host call per layer.
+transport="nccl" (the default): all three in one library call per layer,
+attn_decode_append_nccl -- the local decode, ncclAllGather over NVLink on the
+library's NCCL communicator (kvn_create; the unique id passed through
+torch.distributed), and the merge kernel, all on the caller's stream.
+
+transport="p2p": attn_decode_append_xgpu -- right behind the local decode, an
+exchange kernel pushes the states into every peer's area over NVLink (CUDA
+IPC mappings set up once, the handles passed through torch.distributed),
+waits for the peers' states of the same call and merges.
+
+transport="collective": attn_decode_append_partial, then torch.distributed's
+all-gather and attn_combine_lse_packed -- for process groups whose backend is
+not NCCL (two ranks sharing one GPU over gloo in the tests).
 
 The reference has no split-KV; the merge restates the log-sum-exp identity
 the oracle checks (oracle/kvattn_oracle.c: orc_lse_combine).
@@ -27,7 +35,7 @@ import torch.distributed as dist
 
 import ctypes as C
 
-from . import Pool, call, _ptr, _stream, _vp, HEAD_DIM, KVX_HANDLE_BYTES
+from . import Pool, call, _ptr, _stream, _vp, HEAD_DIM, KVX_HANDLE_BYTES, KVN_UNIQUE_ID_BYTES
 
 
 def slice_bounds(length: int, rank: int, world: int) -> tuple[int, int]:
@@ -44,10 +52,11 @@ class SplitKV:
 
     def __init__(self, pool: Pool, lengths, rank: int, world: int, group=None,
                  transport: str = "nccl"):
-        assert transport in ("nccl", "p2p")
+        assert transport in ("nccl", "p2p", "collective")
         self.pool, self.rank, self.world, self.group = pool, rank, world, group
         self.transport = transport
         self._x = None
+        self._n = None
         self.lengths = [int(x) for x in lengths]
         self.initial = list(self.lengths)
         self.ids = []
@@ -61,6 +70,20 @@ class SplitKV:
         self._buf = None
         if transport == "p2p" and world > 1 and pool.device >= 0:
             self._open_exchange()
+        if transport == "nccl" and world > 1 and pool.device >= 0:
+            self._open_nccl()
+
+    def _open_nccl(self) -> None:
+        """The library's NCCL communicator (a collective: every rank joins)."""
+        uid = (C.c_char * KVN_UNIQUE_ID_BYTES)()
+        if self.rank == 0:
+            call("kvn_unique_id", uid)
+        obj = [bytes(uid)]
+        dist.broadcast_object_list(obj, src=0, group=self.group)
+        c = _vp()
+        call("kvn_create", self.pool.device, self.rank, self.world,
+             C.create_string_buffer(obj[0], KVN_UNIQUE_ID_BYTES), self.rows, C.byref(c))
+        self._n = c
 
     def _open_exchange(self) -> None:
         x = _vp()
@@ -76,12 +99,18 @@ class SplitKV:
         dist.barrier(group=self.group)
 
     def close(self) -> None:
-        """Release the exchange (every rank, after its last layer call)."""
+        """Release the exchange / communicator (every rank, after its last
+        layer call)."""
         if self._x is not None:
             torch.cuda.synchronize(self.pool.device)
             dist.barrier(group=self.group)
             call("kvx_destroy", self._x)
             self._x = None
+        if self._n is not None:
+            torch.cuda.synchronize(self.pool.device)
+            dist.barrier(group=self.group)
+            call("kvn_destroy", self._n)
+            self._n = None
 
     @property
     def is_last(self) -> bool:
@@ -107,7 +136,7 @@ class SplitKV:
         rope = list(self.lengths)
         append = [1 if self.is_last else 0] * len(self.ids)
         self.pool.plan(self.ids, rope_pos=rope, append=append, stream=stream)
-        if self._buf is None and self.pool.device >= 0 and self._x is None:  # host-only pools never run
+        if self._buf is None and self.pool.device >= 0 and self.transport == "collective":  # host-only pools never run
             dev = torch.device("cuda", self.pool.device)
             n = self.rows * (2 + HEAD_DIM)
             self._buf = torch.empty(n, device=dev)
@@ -122,6 +151,10 @@ class SplitKV:
         if self._x is not None:
             call("attn_decode_append_xgpu", self.pool.h, layer, _ptr(q), _ptr(k_new), _ptr(v_new),
                  _ptr(out), self._x, _stream(stream))
+            return
+        if self._n is not None:
+            call("attn_decode_append_nccl", self.pool.h, layer, _ptr(q), _ptr(k_new), _ptr(v_new),
+                 _ptr(out), self._n, _stream(stream))
             return
         R = self.rows
         buf = self._buf

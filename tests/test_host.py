@@ -274,3 +274,19 @@ def test_device_calls_refused_on_host_only_pool(kv):
     with pytest.raises(kv.KVError) as e:
         kv.call("attn_decode_append", P.h, 0, 8, 8, 8, 8, None)  # pointers are never touched
     assert e.value.status in (kv.KV_ERR_STATE, kv.KV_ERR_INVAL)
+
+
+def test_nccl_unique_id_and_argument_checks(kv):
+    """The NCCL communicator's set-up calls that need no GPU: a unique id
+    (NCCL loaded at run time) and the argument checks of kvn_create."""
+    import ctypes as C
+    L = kv.load()
+    uid = (C.c_char * kv.KVN_UNIQUE_ID_BYTES)()
+    if L.kvn_unique_id(uid) != kv.KV_OK:
+        pytest.skip("NCCL not loadable here: " + L.kv_last_error().decode())
+    assert any(bytes(uid))
+    c = kv._vp()
+    assert L.kvn_create(0, 2, 2, uid, 10, C.byref(c)) == kv.KV_ERR_INVAL   # rank outside the world
+    assert L.kvn_create(0, 0, 1, uid, 0, C.byref(c)) == kv.KV_ERR_INVAL    # no rows
+    assert L.kvn_create(0, 0, 1, None, 10, C.byref(c)) == kv.KV_ERR_INVAL  # no id
+    assert L.kvn_destroy(None) == kv.KV_OK

@@ -90,7 +90,9 @@ def _gpu_worker(rank, world, port, q):
         full_k = [orc.encode(rng.standard_normal((L + 4, 256)).astype(np.float32), dtype) for L in lens]
         full_v = [orc.encode(rng.standard_normal((L + 4, 256)).astype(np.float32), dtype) for L in lens]
         P = kv.Pool(0, 1, 600, dtype=dtype, max_seqs=4, max_seq_len=4096)
-        S = sk_mod.SplitKV(P, lens, rank, world)
+        # two ranks on one GPU: NCCL needs one GPU per rank, so the states
+        # go through torch.distributed's gloo all-gather
+        S = sk_mod.SplitKV(P, lens, rank, world, transport="collective")
         S.reserve(4)
         for i, (lo, hi) in enumerate(S.bounds):
             k = torch.from_numpy(full_k[i][lo:hi].view(np.int16)).cuda()
@@ -138,7 +140,7 @@ def test_splitkv_two_ranks_one_gpu_matches_unsplit():
         assert worst <= 1e-3, (rank, worst)
 
 
-def _p2p_worker(rank, world, port, q):
+def _p2p_worker(rank, world, port, q, transport="p2p"):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
@@ -155,7 +157,7 @@ def _p2p_worker(rank, world, port, q):
         full_k = [orc.encode(rng.standard_normal((L + 8, 256)).astype(np.float32), dtype) for L in lens]
         full_v = [orc.encode(rng.standard_normal((L + 8, 256)).astype(np.float32), dtype) for L in lens]
         P = kv.Pool(rank, 2, 600, dtype=dtype, max_seqs=4, max_seq_len=4096)
-        S = sk_mod.SplitKV(P, lens, rank, world, transport="p2p")
+        S = sk_mod.SplitKV(P, lens, rank, world, transport=transport)
         S.reserve(8)
         for layer in range(2):
             for i, (lo, hi) in enumerate(S.bounds):
@@ -207,6 +209,83 @@ def test_splitkv_p2p_exchange_two_gpus_matches_unsplit():
     for rank, worst, status in out:
         assert status == 0
         assert worst <= 1e-3, (rank, worst)
+
+
+@pytest.mark.gpu
+def test_splitkv_nccl_two_gpus_matches_unsplit():
+    """The library's NCCL path (attn_decode_append_nccl: local decode, NCCL
+    all-gather of the packed states, merge) on two GPUs, 2 layers x 3 steps,
+    against the unsplit oracle."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two CUDA devices")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_p2p_worker, args=(r, 2, port, q, "nccl")) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, worst, status in out:
+        assert status == 0
+        assert worst <= 1e-3, (rank, worst)
+
+
+@pytest.mark.gpu
+def test_nccl_call_with_one_rank_equals_local_decode():
+    """A one-rank NCCL communicator (a single-GPU box still runs the NCCL
+    path): the decode states go through the communicator's buffers, a
+    one-rank all-gather and the merge; the output must match the ordinary
+    decode.  A plan with more rows than the communicator holds is refused."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import ctypes as C
+    import sys
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    kv = load_pkg()
+    rng = np.random.default_rng(8)
+    lens = [5, 700, 4000]
+    P = kv.Pool(0, 1, 400, dtype=1, max_seqs=3, max_seq_len=4200)
+    ids = []
+    for L in lens:
+        s = P.seq_alloc()
+        P.reserve(s, L + 4)
+        kc = orc.encode(rng.standard_normal((L, 256)).astype(np.float32), 1)
+        vc = orc.encode(rng.standard_normal((L, 256)).astype(np.float32), 1)
+        P.import_rows(0, s, 0, torch.from_numpy(kc.view(np.int16)).cuda(),
+                      torch.from_numpy(vc.view(np.int16)).cuda())
+        P.set_cur_pos(s, L)
+        ids.append(s)
+    uid = (C.c_char * kv.KVN_UNIQUE_ID_BYTES)()
+    kv.call("kvn_unique_id", uid)
+    c = kv._vp()
+    kv.call("kvn_create", 0, 0, 1, uid, 3 * 12, C.byref(c))
+    q = torch.randn((3, 1536), device="cuda")
+    k = torch.randn((3, 256), device="cuda")
+    v = torch.randn((3, 256), device="cuda")
+    ref = torch.empty((3, 1536), device="cuda")
+    got = torch.empty((3, 1536), device="cuda")
+    P.plan(ids, rope_pos=lens, append=[0, 0, 0])
+    P.decode_layer(0, q, k, v, ref)
+    for _ in range(2):
+        kv.call("attn_decode_append_nccl", P.h, 0, q.data_ptr(), k.data_ptr(), v.data_ptr(), got.data_ptr(), c,
+                None)
+        torch.cuda.synchronize()
+        assert torch.allclose(got, ref, rtol=1e-5, atol=1e-6)
+    kv.call("kvn_destroy", c)
+    # a communicator for one sequence's rows cannot take this 3-sequence plan
+    kv.call("kvn_unique_id", uid)
+    small = kv._vp()
+    kv.call("kvn_create", 0, 0, 1, uid, 12, C.byref(small))
+    rc = kv.load().attn_decode_append_nccl(P.h, 0, q.data_ptr(), k.data_ptr(), v.data_ptr(), got.data_ptr(),
+                                           small, None)
+    assert rc == kv.KV_ERR_RANGE
+    kv.call("kvn_destroy", small)
+    P.commit()
+    assert P.device_status() == 0
 
 
 @pytest.mark.gpu
