@@ -1520,8 +1520,9 @@ def run_reference_prefill(args, world):
     for it in range(W + K):
         qs = [rng.standard_normal((SUB, HID), dtype=np.float32) for _ in pos0]
         ks = [rng.standard_normal((SUB, KVD), dtype=np.float32) for _ in pos0]
+        vs = [rng.standard_normal((SUB, KVD), dtype=np.float32) for _ in pos0]
         t0 = time.perf_counter()
-        list(ex.map(lambda j: orc.ref_layer_step(qs[j], ks[j], ks[j], caches[j][0], caches[j][1], pos0[j]),
+        list(ex.map(lambda j: orc.ref_layer_step(qs[j], ks[j], vs[j], caches[j][0], caches[j][1], pos0[j]),
                     range(len(pos0))))
         dt = time.perf_counter() - t0
         if it >= W:

@@ -21,7 +21,11 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libkvref.so")
-REF_SRC = "/root/reference/worker"
+# Root of the reference checkout (Bobchasm/rk3588-npu): KVATTN_REFERENCE, else
+# the location this build's recipe reads it from.  Only the build of the
+# reference shim needs it; the tests use the prebuilt libraries.
+REF_ROOT = os.environ.get("KVATTN_REFERENCE", "/root/reference")
+REF_SRC = os.path.join(REF_ROOT, "worker")
 
 F16, BF16 = 0, 1
 

@@ -27,6 +27,7 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <mutex>
 
 #include "device_common.cuh"
 #include "kvattn.h"
@@ -629,13 +630,17 @@ int gemv_split(int K) {
 
 // Launch facts of one kernel, per device (a process may drive several GPUs,
 // from several threads): the dynamic shared memory granted so far, the SM
-// count, and the resident CTAs per SM by 4 KiB shared-memory bucket.
-// Concurrent first calls may query twice; every value written is the same.
+// count, and the resident CTAs per SM by 4 KiB shared-memory bucket.  The
+// shared-memory attribute is raised under a per-device lock, so it only
+// grows and never falls below the recorded grant (two first calls with
+// different sizes cannot leave the smaller one set).  Concurrent first
+// calls may query the occupancy twice; every value written is the same.
 struct LaunchCache {
     static constexpr int kDevices = 64;
     std::atomic<int> smem_set[kDevices];
     std::atomic<int> sms[kDevices];
     std::atomic<int> ctas[kDevices][64];
+    std::mutex mu[kDevices];
 
     cudaError_t get(const void* fn, int smem, int* sms_out, int* ctas_out) {
         int dev = 0;
@@ -643,10 +648,11 @@ struct LaunchCache {
         if (e != cudaSuccess) return e;
         if (dev < 0 || dev >= kDevices) return cudaErrorInvalidDevice;
         if (smem > smem_set[dev].load()) {
-            e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-            if (e != cudaSuccess) return e;
-            int cur = smem_set[dev].load();
-            while (cur < smem && !smem_set[dev].compare_exchange_weak(cur, smem)) {
+            std::lock_guard<std::mutex> lk(mu[dev]);
+            if (smem > smem_set[dev].load()) {
+                e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+                if (e != cudaSuccess) return e;
+                smem_set[dev].store(smem);
             }
         }
         if (!sms[dev].load()) {
