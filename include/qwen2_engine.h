@@ -64,6 +64,16 @@ int qw2_destroy(qw2_model* m);
 /* Run on this stream from now on (default: a stream the model created). */
 int qw2_set_stream(qw2_model* m, void* stream);
 
+/* on != 0: every forward from now on repeats the reference's float
+ * operations in the reference's order (Qwen2Model::forward,
+ * qwen2_model.cpp:131-274: RMSNorm, projections and attention with their
+ * sums taken sequentially, softmax and SiLU with exp evaluated in double and
+ * rounded to float once), so logits match the reference's bit for bit
+ * wherever the C library's expf is correctly rounded -- a parity mode, far
+ * slower than the default forward.  Groups of one engine step run one after
+ * another.  Needs the fp16 KV cache; allocates its buffers on first use. */
+int qw2_set_exact(qw2_model* m, int on);
+
 /* One tensor from host memory, named as in the safetensors file
  * (qwen2_model.cpp:72-111: model.embed_tokens.weight, model.layers.<i>.
  * input_layernorm.weight, ...self_attn.{q,k,v}_proj.{weight,bias},

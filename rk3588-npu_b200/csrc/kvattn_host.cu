@@ -173,6 +173,8 @@ struct kvp_pool {
     }
 };
 
+const float2* kvattn::pool_rope_table(const kvp_pool* p) { return p ? p->d_rope : nullptr; }
+
 namespace {
 
 // cos/sin for every (position, pair) with the float libm calls and operation

@@ -20,7 +20,9 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <atomic>
+#include <cmath>
 #include <chrono>
 #include <condition_variable>
 #include <deque>
@@ -118,6 +120,7 @@ struct qw2_model {
     cudaStream_t st = nullptr;
     bool own_stream = false;
     kvp_pool* pool = nullptr;
+    int kv_dtype = KV_F16;
     int max_sessions = 1;
     int rows_cap = 0;              // rows of one forward (activation buffers)
     std::vector<int> session_seq;  // session -> pool sequence id, -1 = free
@@ -162,6 +165,17 @@ struct qw2_model {
     int* ids = nullptr;       // [R + S]: token ids, then the last-row index of each session
     unsigned long long* best = nullptr;  // [S]
     void* staging = nullptr;
+
+    // forward in the reference's operation order (qw2_set_exact): buffers
+    // allocated on first use
+    bool exact = false;
+    uint16_t* ex_x16 = nullptr;    // [R][max(H, IS)] projection inputs
+    uint16_t* ex_qkv16 = nullptr;  // [R][H + 2 kvd]
+    uint16_t* ex_g16 = nullptr;    // [R][IS]
+    uint16_t* ex_u16 = nullptr;    // [R][IS]
+    uint16_t* ex_y16 = nullptr;    // [max(R H, V)] projection outputs
+    uint16_t* ex_kc = nullptr;     // [max_position][kvd] one layer's cache rows
+    uint16_t* ex_vc = nullptr;
 
     std::vector<void*> allocs;
 
@@ -415,12 +429,92 @@ struct Group {
     int argmax = 0;
 };
 
+// Qwen2Model::forward in the reference's operation order (qw2_set_exact):
+// the groups one after another, each with the exact_kernels.cu kernels --
+// RMSNorm, projections, biases, q RoPE, the pool's bit-exact append, the
+// layer's cache rows gathered into the reference layout, attention,
+// residuals, SiLU, lm_head -- then the greedy argmax of its last row.
+int forward_exact(qw2_model* m, std::vector<Group>& gs) {
+    const qw2_config& c = m->c;
+    const int G = (int)gs.size();
+    if (G == 0) return qfail(KV_ERR_INVAL, "forward of no tokens");
+    if (G > m->max_sessions) return qfail(KV_ERR_INVAL, "%d groups > %d sessions", G, m->max_sessions);
+    QW_OK(qw2_ready(m));
+    std::vector<char> seen(m->max_sessions, 0);
+    std::vector<int> pos(G), seq(G);
+    for (int g = 0; g < G; ++g) {
+        const Group& gr = gs[g];
+        QW_OK(session_check(m, gr.session));
+        if (seen[gr.session]) return qfail(KV_ERR_INVAL, "session %d twice in one forward", gr.session);
+        seen[gr.session] = 1;
+        if (gr.n <= 0 || !gr.tokens) return qfail(KV_ERR_INVAL, "forward of %d tokens", gr.n);
+        for (int i = 0; i < gr.n; ++i)
+            if (gr.tokens[i] < 0 || gr.tokens[i] >= c.vocab)
+                return qfail(KV_ERR_RANGE, "token id %d outside [0, %d)", gr.tokens[i], c.vocab);
+        seq[g] = m->session_seq[gr.session];
+        QW_OK(kvp_seq_len(m->pool, seq[g], &pos[g]));
+        if (pos[g] + gr.n > c.max_position)
+            return qfail(KV_ERR_RANGE, "positions %d..%d pass max_position %d", pos[g], pos[g] + gr.n - 1,
+                         c.max_position);
+        if (gr.n > m->rows_cap) return qfail(KV_ERR_RANGE, "%d rows in one forward > %d", gr.n, m->rows_cap);
+    }
+    DeviceGuard dg(m->device);
+    cudaStream_t st = m->st;
+    const int H = c.hidden, kvd = m->kvd, IS = c.intermediate, V = c.vocab;
+    const float scale = 1.0f / std::sqrt((float)c.head_dim);  // op_attention.cpp:20
+    const float2* rope = pool_rope_table(m->pool);
+    for (int g = 0; g < G; ++g) {
+        const Group& gr = gs[g];
+        const int n = gr.n, p0 = pos[g], T = p0 + n;
+        QW_OK(kvp_seq_reserve(m->pool, seq[g], T));
+        QW_OK(kvp_seq_set_len(m->pool, seq[g], T));  // the gathers below read positions [0, T)
+        QW_CUDA(cudaMemcpyAsync(m->ids, gr.tokens, sizeof(int) * n, cudaMemcpyHostToDevice, st));
+        QW_CUDA(launch_embed(m->ids, n, m->embed, m->hidden, H, st));
+        for (int li = 0; li < c.layers; ++li) {
+            const qw2_model::Layer& Ly = m->L[li];
+            QW_CUDA(launch_rmsnorm_exact(m->hidden, Ly.ln1, c.rms_eps, n, H, m->ex_x16, st));
+            QW_CUDA(launch_gemv_exact(m->ex_x16, n, H, Ly.wqkv, H + 2 * kvd, m->ex_qkv16, st));
+            QW_CUDA(launch_qkv_bias_exact(m->ex_qkv16, Ly.bqkv, n, H, kvd, m->q, m->k, m->v, st));
+            QW_CUDA(launch_rope_q_exact(m->q, n, c.q_heads, p0, rope, st));
+            QW_OK(kv_append_chunk(m->pool, li, seq[g], p0, n, m->k, m->v, st));
+            QW_OK(kvp_gather(m->pool, li, seq[g], m->ex_kc, m->ex_vc, st));
+            QW_CUDA(launch_attn_exact(m->q, m->ex_kc, m->ex_vc, m->attn, n, T, c.q_heads, c.kv_heads, p0, scale, st));
+            QW_CUDA(launch_to_f16_exact(m->attn, (long)n * H, m->ex_x16, st));
+            QW_CUDA(launch_gemv_exact(m->ex_x16, n, H, Ly.wo, H, m->ex_y16, st));
+            QW_CUDA(launch_resid_exact(m->hidden, m->ex_y16, (long)n * H, st));
+            QW_CUDA(launch_rmsnorm_exact(m->hidden, Ly.ln2, c.rms_eps, n, H, m->ex_x16, st));
+            QW_CUDA(launch_gemv_exact(m->ex_x16, n, H, Ly.wg, IS, m->ex_g16, st));
+            QW_CUDA(launch_gemv_exact(m->ex_x16, n, H, Ly.wu, IS, m->ex_u16, st));
+            QW_CUDA(launch_silu_mul_exact(m->ex_g16, m->ex_u16, (long)n * IS, m->h16, st));
+            QW_CUDA(launch_gemv_exact(m->h16, n, IS, Ly.wd, H, m->ex_y16, st));
+            QW_CUDA(launch_resid_exact(m->hidden, m->ex_y16, (long)n * H, st));
+        }
+        // final RMSNorm of the last row, lm_head (the tied embedding), argmax
+        QW_CUDA(launch_rmsnorm_exact(m->hidden + (size_t)(n - 1) * H, m->norm, c.rms_eps, 1, H, m->ex_x16, st));
+        QW_CUDA(launch_gemv_exact(m->ex_x16, 1, H, m->embed, V, m->ex_y16, st));
+        float* lg = m->logits + (size_t)g * V;
+        QW_CUDA(launch_f16_to_f32_exact(m->ex_y16, V, lg, st));
+        QW_CUDA(launch_argmax(lg, V, 1, m->best + g, st));
+        if (gr.logits_host)
+            QW_CUDA(cudaMemcpyAsync(gr.logits_host, lg, sizeof(float) * (size_t)V, cudaMemcpyDeviceToHost, st));
+    }
+    std::vector<unsigned long long> keys(G);
+    QW_CUDA(cudaMemcpyAsync(keys.data(), m->best, sizeof(unsigned long long) * G, cudaMemcpyDeviceToHost, st));
+    int status = 0;
+    QW_OK(kvp_device_status(m->pool, st, &status));  // synchronises the stream
+    if (status != 0) return status;
+    for (int g = 0; g < G; ++g)
+        gs[g].argmax = keys[g] ? (int)(0xFFFFFFFFu - (uint32_t)(keys[g] & 0xFFFFFFFFu)) : 0;
+    return KV_OK;
+}
+
 // Qwen2Model::forward (qwen2_model.cpp:131-274) over several sessions at
 // once.  Rows: the one-token groups first (in the given order: one planned
 // decode-attention launch covers them), then every longer group (appended
 // as a chunk and attended with the prefill kernel).  The projections run
 // once over all rows; lm_head and the argmax over each group's last row.
 int forward_groups(qw2_model* m, std::vector<Group>& gs) {
+    if (m->exact) return forward_exact(m, gs);
     const qw2_config& c = m->c;
     const int G = (int)gs.size();
     if (G == 0) return qfail(KV_ERR_INVAL, "forward of no tokens");
@@ -820,6 +914,7 @@ int qw2_create_kv(int device, const qw2_config* cfg, int max_sessions, int kv_dt
     m->device = device;
     m->c = *cfg;
     m->kvd = cfg->kv_heads * cfg->head_dim;
+    m->kv_dtype = kv_dtype;
     m->max_sessions = max_sessions;
     m->rows_cap = cfg->max_position + max_sessions;
     m->session_seq.assign(max_sessions, -1);
@@ -884,6 +979,26 @@ int qw2_create_sessions(int device, const qw2_config* cfg, int max_sessions, qw2
 
 int qw2_create(int device, const qw2_config* cfg, qw2_model** out) {
     return qw2_create_sessions(device, cfg, 1, out);
+}
+
+int qw2_set_exact(qw2_model* m, int on) {
+    if (!m) return qfail(KV_ERR_INVAL, "NULL model");
+    std::lock_guard<std::mutex> lk(m->mu);
+    if (on && m->kv_dtype != KV_F16)
+        return qfail(KV_ERR_INVAL, "the reference-order forward needs the fp16 KV cache (the reference's)");
+    if (on && !m->ex_x16) {
+        DeviceGuard g(m->device);
+        const size_t H = m->c.hidden, kvd = m->kvd, IS = m->c.intermediate, V = m->c.vocab, R = m->rows_cap;
+        QW_OK(m->alloc_n(&m->ex_x16, R * std::max(H, IS)));
+        QW_OK(m->alloc_n(&m->ex_qkv16, R * (H + 2 * kvd)));
+        QW_OK(m->alloc_n(&m->ex_g16, R * IS));
+        QW_OK(m->alloc_n(&m->ex_u16, R * IS));
+        QW_OK(m->alloc_n(&m->ex_y16, std::max(R * H, V)));
+        QW_OK(m->alloc_n(&m->ex_kc, (size_t)m->c.max_position * kvd));
+        QW_OK(m->alloc_n(&m->ex_vc, (size_t)m->c.max_position * kvd));
+    }
+    m->exact = on != 0;
+    return KV_OK;
 }
 
 int qw2_set_stream(qw2_model* m, void* stream) {

@@ -166,6 +166,7 @@ _SIGS = {
     "qw2_kv_pool": [C.c_void_p, C.POINTER(C.c_void_p)],
     "qw2_weight_bytes": [C.c_void_p, C.POINTER(C.c_longlong)],
     "qw2_set_stream": [C.c_void_p, C.c_void_p],
+    "qw2_set_exact": [C.c_void_p, C.c_int],
 }
 
 
@@ -233,6 +234,12 @@ class Model:
 
     def reset(self) -> None:
         _check(self.L.qw2_reset(self.h), "qw2_reset")
+
+    def set_exact(self, on: bool) -> None:
+        """qw2_set_exact: forwards in the reference's operation order (a parity
+        mode whose logits match the reference's bit for bit wherever the C
+        library's expf is correctly rounded; far slower)."""
+        _check(self.L.qw2_set_exact(self.h, int(on)), "qw2_set_exact")
 
     def cur_pos(self) -> int:
         p = C.c_int()

@@ -187,6 +187,57 @@ def test_prefill_and_decode_logits_match_reference(full_model):
     assert full_model.cur_pos() == 256
 
 
+@pytest.fixture(scope="module")
+def exact_model():
+    need_gpu()
+    m = q2()
+    M = m.Model(0)
+    M.load_synthetic(seed=0)
+    M.set_exact(True)
+    yield M
+    M.close()
+
+
+@pytest.mark.gpu
+def test_exact_order_greedy_stream_is_identical(exact_model):
+    """The forward in the reference's operation order (qw2_set_exact): the
+    free-running 128-step greedy stream of LLMEngine::generate equals the
+    reference's, id for id (llm_engine.cpp:76-98, op_sampling.cpp:4-11)."""
+    g = dict(np.load(GOLD))
+    exact_model.reset()
+    ids = exact_model.generate(g["prompt"].tolist(), 128, stop_tokens=(), repetition_window=0)
+    ref = g["output_ids"].tolist()
+    first = next((i for i, (a, b) in enumerate(zip(ids, ref)) if a != b), None)
+    assert first is None and len(ids) == 128, f"stream differs first at id {first}"
+    assert exact_model.cur_pos() == 256
+
+
+@pytest.mark.gpu
+def test_exact_order_logits_match_reference(exact_model):
+    """Teacher-forced: the prompt's logits (all 151936) and every decode
+    step's top-64 logits within 1e-3 of the reference's; in practice
+    bit-identical fp16 values (the count of differing entries is reported and
+    must stay a tiny fraction)."""
+    g = dict(np.load(GOLD))
+    exact_model.reset()
+    logits, am = exact_model.forward(g["prompt"].tolist())
+    ref = f16_bits_to_f32(g["prefill_logits_f16"]).astype(np.float64)
+    assert rel(logits, ref) <= TOL
+    diff = int(np.count_nonzero(logits.astype(np.float64) != ref))
+    worst, ndiff = 0.0, diff
+    for s, tok in enumerate(g["output_ids"].tolist()):
+        logits, am2 = exact_model.forward([tok])
+        idx, val = g["top_idx"][s], g["top_val"][s].astype(np.float64)
+        worst = max(worst, float(np.abs(logits[idx] - val).max() / np.abs(val).max()))
+        ndiff += int(np.count_nonzero(logits[idx].astype(np.float64) != val))
+        if s + 1 < 128:
+            assert am2 == g["output_ids"][s + 1], s
+    assert am == g["output_ids"][0]
+    assert worst <= TOL
+    print(f"exact-order logits: {ndiff} of {151936 + 128 * 64} compared values differ from the reference's")
+    assert ndiff <= 100
+
+
 def small_models(tmp, dtype_name):
     """Two models of the reduced config with the same weights: one from a
     safetensors file of `dtype_name`, one from qw2_set_tensor."""
