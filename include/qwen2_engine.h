@@ -67,11 +67,14 @@ int qw2_set_stream(qw2_model* m, void* stream);
 /* on != 0: every forward from now on repeats the reference's float
  * operations in the reference's order (Qwen2Model::forward,
  * qwen2_model.cpp:131-274: RMSNorm, projections and attention with their
- * sums taken sequentially, softmax and SiLU with exp evaluated in double and
- * rounded to float once), so logits match the reference's bit for bit
- * wherever the C library's expf is correctly rounded -- a parity mode, far
+ * sums taken sequentially, separately rounded products, softmax and SiLU
+ * with the exp of this process's C library), so the logits equal those of
+ * the reference's own loops on this host bit for bit -- a parity mode, far
  * slower than the default forward.  Groups of one engine step run one after
- * another.  Needs the fp16 KV cache; allocates its buffers on first use. */
+ * another.  Needs the fp16 KV cache.  The first call with on != 0 allocates
+ * the mode's buffers and, once per process, finds the float inputs where the
+ * C library's expf is not correctly rounded (a scan of every float with a
+ * finite, nonzero exp on all host threads: seconds). */
 int qw2_set_exact(qw2_model* m, int on);
 
 /* One tensor from host memory, named as in the safetensors file

@@ -24,11 +24,11 @@
 //
 // exp: the reference calls the C library's expf.  Here exp is evaluated in
 // double precision and rounded to float once -- the correctly rounded float
-// exponential.  The C library's expf returns that same value for all but
-// about 0.004 % of float inputs (all with |x| between roughly 2^-17 and
-// 2^-11, where it is off by one unit in the last place), so an fp32 softmax
-// weight or SiLU value can, rarely, differ by one unit; that changes a later
-// fp16 truncation only when it sits on a rounding boundary.
+// exponential -- which is what the C library returns for all but a small
+// set of inputs (0.004 % of the floats on x86-64 glibc 2.39, spread over the
+// whole finite range, each one unit in the last place away).  Those inputs
+// and the library's results come in a table (ExpTab) that the host builds
+// from its own expf; with it, every exp here equals the host's.
 #include <cuda_runtime.h>
 #include <float.h>
 #include <math.h>
@@ -51,7 +51,24 @@ __device__ __forceinline__ float ref_f16(uint32_t h) {
     return __uint_as_float(x);
 }
 
-__device__ __forceinline__ float exp_ref(float x) { return __double2float_rn(exp((double)x)); }
+// exp as the host C library's expf: the correctly rounded value, or the
+// library's own result on the inputs listed in the table.
+__device__ __forceinline__ float exp_ref(float x, const ExpTab& t) {
+    float r = __double2float_rn(exp((double)x));
+    if (t.keys != nullptr) {
+        const uint32_t b = __float_as_uint(x), hb = b >> 16;
+        uint32_t lo = t.bucket[hb];
+        const uint32_t end = t.bucket[hb + 1];
+        uint32_t hi = end;
+        while (lo < hi) {
+            const uint32_t mid = (lo + hi) >> 1;
+            if (t.keys[mid] < b) lo = mid + 1;
+            else hi = mid;
+        }
+        if (lo < end && t.keys[lo] == b) r = __uint_as_float(t.vals[lo]);
+    }
+    return r;
+}
 
 constexpr int kThreadsE = 128;
 
@@ -168,7 +185,8 @@ __global__ void __launch_bounds__(256)
 // key order, output sums in key order (masked keys add 0 * v).
 __global__ void __launch_bounds__(kThreadsE)
     attn_exact_kernel(const float* __restrict__ q, const uint16_t* __restrict__ kc, const uint16_t* __restrict__ vc,
-                      float* __restrict__ out, int total_len, int n_heads, int n_kv_heads, int pos_base, float scale) {
+                      float* __restrict__ out, int total_len, int n_heads, int n_kv_heads, int pos_base, float scale,
+                      ExpTab et) {
     extern __shared__ float sc[];  // [total_len] scores, then weights
     __shared__ float qs[kHeadDim];
     __shared__ float red[kThreadsE / 32];
@@ -199,7 +217,7 @@ __global__ void __launch_bounds__(kThreadsE)
     mx = red[0];
 #pragma unroll
     for (int w = 1; w < kThreadsE / 32; ++w) mx = fmaxf(mx, red[w]);
-    for (int i = tid; i < total_len; i += kThreadsE) sc[i] = exp_ref(__fsub_rn(sc[i], mx));
+    for (int i = tid; i < total_len; i += kThreadsE) sc[i] = exp_ref(__fsub_rn(sc[i], mx), et);
     __syncthreads();
     if (tid == 0) {
         float sum = 0.f;
@@ -232,10 +250,10 @@ __global__ void __launch_bounds__(256)
 // silu(x) = x / (1 + exp(-x)).
 __global__ void __launch_bounds__(256)
     silu_mul_exact_kernel(const uint16_t* __restrict__ g16, const uint16_t* __restrict__ u16, long n,
-                          uint16_t* __restrict__ h16) {
+                          uint16_t* __restrict__ h16, ExpTab et) {
     for (long i = blockIdx.x * 256L + threadIdx.x; i < n; i += gridDim.x * 256L) {
         const float g = ref_f16(g16[i]);
-        const float s = __fdiv_rn(g, __fadd_rn(1.0f, exp_ref(-g)));
+        const float s = __fdiv_rn(g, __fadd_rn(1.0f, exp_ref(-g, et)));
         h16[i] = enc_f16_trunc(__fmul_rn(s, ref_f16(u16[i])));
     }
 }
@@ -279,11 +297,11 @@ cudaError_t launch_rope_q_exact(float* q, int rows, int heads, int pos0, const f
 }
 
 cudaError_t launch_attn_exact(const float* q, const uint16_t* kc, const uint16_t* vc, float* out, int seq, int total_len,
-                              int n_heads, int n_kv_heads, int pos_base, float scale, cudaStream_t st) {
+                              int n_heads, int n_kv_heads, int pos_base, float scale, ExpTab et, cudaStream_t st) {
     const size_t smem = (size_t)total_len * sizeof(float);
     if (smem > 48 * 1024) return cudaErrorInvalidValue;  // up to 12288 keys
     attn_exact_kernel<<<dim3((unsigned)n_heads, (unsigned)seq), kThreadsE, smem, st>>>(q, kc, vc, out, total_len, n_heads,
-                                                                                       n_kv_heads, pos_base, scale);
+                                                                                       n_kv_heads, pos_base, scale, et);
     return counted(cudaGetLastError());
 }
 
@@ -297,8 +315,9 @@ cudaError_t launch_resid_exact(float* hidden, const uint16_t* y16, long n, cudaS
     return counted(cudaGetLastError());
 }
 
-cudaError_t launch_silu_mul_exact(const uint16_t* g16, const uint16_t* u16, long n, uint16_t* h16, cudaStream_t st) {
-    silu_mul_exact_kernel<<<grid_for_e(n), 256, 0, st>>>(g16, u16, n, h16);
+cudaError_t launch_silu_mul_exact(const uint16_t* g16, const uint16_t* u16, long n, uint16_t* h16, ExpTab et,
+                                  cudaStream_t st) {
+    silu_mul_exact_kernel<<<grid_for_e(n), 256, 0, st>>>(g16, u16, n, h16, et);
     return counted(cudaGetLastError());
 }
 

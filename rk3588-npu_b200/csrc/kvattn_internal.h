@@ -241,6 +241,16 @@ cudaError_t launch_gather_rows(const float* src, const int* idx, int rows, float
 cudaError_t launch_weight_to_f16(const void* src, int dtype, uint16_t* dst, size_t n, cudaStream_t st);
 
 // ---- the Qwen2 forward in the reference's operation order (exact_kernels.cu) ----
+// The float inputs where the host C library's expf is not the correctly
+// rounded exponential, with its result: keys (float bits, ascending) and
+// vals of n entries; bucket[b] .. bucket[b + 1] are the entries whose top
+// 16 key bits are b (65537 offsets).  All NULL: the correctly rounded value
+// everywhere.
+struct ExpTab {
+    const uint32_t* keys = nullptr;
+    const uint32_t* vals = nullptr;
+    const uint32_t* bucket = nullptr;
+};
 cudaError_t launch_rmsnorm_exact(const float* x, const float* w, float eps, int rows, int H, uint16_t* y16,
                                  cudaStream_t st);
 cudaError_t launch_gemv_exact(const uint16_t* x16, int M, int K, const uint16_t* W, int N, uint16_t* y16,
@@ -249,10 +259,11 @@ cudaError_t launch_qkv_bias_exact(const uint16_t* qkv16, const float* bias, int 
                                   float* v, cudaStream_t st);
 cudaError_t launch_rope_q_exact(float* q, int rows, int heads, int pos0, const float2* rope, cudaStream_t st);
 cudaError_t launch_attn_exact(const float* q, const uint16_t* kc, const uint16_t* vc, float* out, int seq, int total_len,
-                              int n_heads, int n_kv_heads, int pos_base, float scale, cudaStream_t st);
+                              int n_heads, int n_kv_heads, int pos_base, float scale, ExpTab et, cudaStream_t st);
 cudaError_t launch_to_f16_exact(const float* x, long n, uint16_t* y, cudaStream_t st);
 cudaError_t launch_resid_exact(float* hidden, const uint16_t* y16, long n, cudaStream_t st);
-cudaError_t launch_silu_mul_exact(const uint16_t* g16, const uint16_t* u16, long n, uint16_t* h16, cudaStream_t st);
+cudaError_t launch_silu_mul_exact(const uint16_t* g16, const uint16_t* u16, long n, uint16_t* h16, ExpTab et,
+                                  cudaStream_t st);
 cudaError_t launch_f16_to_f32_exact(const uint16_t* y16, long n, float* y, cudaStream_t st);
 // The pool's device RoPE table [max_seq_len][64] (cos, sin), host-built with
 // the reference's float libm calls.

@@ -176,6 +176,7 @@ struct qw2_model {
     uint16_t* ex_y16 = nullptr;    // [max(R H, V)] projection outputs
     uint16_t* ex_kc = nullptr;     // [max_position][kvd] one layer's cache rows
     uint16_t* ex_vc = nullptr;
+    ExpTab ex_exp;                 // the host expf's deviations from the correctly rounded exp
 
     std::vector<void*> allocs;
 
@@ -429,6 +430,58 @@ struct Group {
     int argmax = 0;
 };
 
+// The float inputs where this process's C library expf (the exp the
+// reference's loops call) differs from the correctly rounded exponential --
+// (float)exp((double)x) -- and its results there, found once per process by
+// evaluating both over every float with a finite, nonzero result
+// (|x| < 104, about 2.2e9 inputs, on all host threads).  Sorted by bits,
+// with an index over the top 16 bits (see ExpTab).
+struct HostExpTable {
+    std::vector<uint32_t> keys, vals, bucket;
+};
+
+const HostExpTable& host_exp_table() {
+    static HostExpTable t;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        // positive inputs [0, 104) then negative ones, as bit ranges
+        const uint32_t kPosEnd = 0x42D00000u, kNegBeg = 0x80000000u, kNegEnd = 0xC2D00000u;
+        const uint64_t total = (uint64_t)kPosEnd + (kNegEnd - kNegBeg);
+        unsigned nt = std::max(1u, std::thread::hardware_concurrency());
+        std::vector<std::vector<std::pair<uint32_t, uint32_t>>> part(nt);
+        std::vector<std::thread> th;
+        for (unsigned w = 0; w < nt; ++w)
+            th.emplace_back([&, w] {
+                const uint64_t a = total * w / nt, b = total * (w + 1) / nt;
+                for (uint64_t i = a; i < b; ++i) {
+                    const uint32_t bits = i < kPosEnd ? (uint32_t)i : (uint32_t)(kNegBeg + (i - kPosEnd));
+                    float x;
+                    memcpy(&x, &bits, 4);
+                    const float lib = std::exp(x), cr = (float)std::exp((double)x);
+                    if (lib != cr) {
+                        uint32_t lb;
+                        memcpy(&lb, &lib, 4);
+                        part[w].emplace_back(bits, lb);
+                    }
+                }
+            });
+        for (auto& x : th) x.join();
+        std::vector<std::pair<uint32_t, uint32_t>> all;
+        for (auto& p : part) all.insert(all.end(), p.begin(), p.end());
+        std::sort(all.begin(), all.end());
+        t.keys.reserve(all.size());
+        t.vals.reserve(all.size());
+        for (auto& kv : all) {
+            t.keys.push_back(kv.first);
+            t.vals.push_back(kv.second);
+        }
+        t.bucket.assign(65537, 0);
+        for (uint32_t k : t.keys) ++t.bucket[(k >> 16) + 1];
+        for (int b = 0; b < 65536; ++b) t.bucket[b + 1] += t.bucket[b];
+    });
+    return t;
+}
+
 // Qwen2Model::forward in the reference's operation order (qw2_set_exact):
 // the groups one after another, each with the exact_kernels.cu kernels --
 // RMSNorm, projections, biases, q RoPE, the pool's bit-exact append, the
@@ -478,14 +531,15 @@ int forward_exact(qw2_model* m, std::vector<Group>& gs) {
             QW_CUDA(launch_rope_q_exact(m->q, n, c.q_heads, p0, rope, st));
             QW_OK(kv_append_chunk(m->pool, li, seq[g], p0, n, m->k, m->v, st));
             QW_OK(kvp_gather(m->pool, li, seq[g], m->ex_kc, m->ex_vc, st));
-            QW_CUDA(launch_attn_exact(m->q, m->ex_kc, m->ex_vc, m->attn, n, T, c.q_heads, c.kv_heads, p0, scale, st));
+            QW_CUDA(launch_attn_exact(m->q, m->ex_kc, m->ex_vc, m->attn, n, T, c.q_heads, c.kv_heads, p0, scale, m->ex_exp,
+                                      st));
             QW_CUDA(launch_to_f16_exact(m->attn, (long)n * H, m->ex_x16, st));
             QW_CUDA(launch_gemv_exact(m->ex_x16, n, H, Ly.wo, H, m->ex_y16, st));
             QW_CUDA(launch_resid_exact(m->hidden, m->ex_y16, (long)n * H, st));
             QW_CUDA(launch_rmsnorm_exact(m->hidden, Ly.ln2, c.rms_eps, n, H, m->ex_x16, st));
             QW_CUDA(launch_gemv_exact(m->ex_x16, n, H, Ly.wg, IS, m->ex_g16, st));
             QW_CUDA(launch_gemv_exact(m->ex_x16, n, H, Ly.wu, IS, m->ex_u16, st));
-            QW_CUDA(launch_silu_mul_exact(m->ex_g16, m->ex_u16, (long)n * IS, m->h16, st));
+            QW_CUDA(launch_silu_mul_exact(m->ex_g16, m->ex_u16, (long)n * IS, m->h16, m->ex_exp, st));
             QW_CUDA(launch_gemv_exact(m->h16, n, IS, Ly.wd, H, m->ex_y16, st));
             QW_CUDA(launch_resid_exact(m->hidden, m->ex_y16, (long)n * H, st));
         }
@@ -996,6 +1050,20 @@ int qw2_set_exact(qw2_model* m, int on) {
         QW_OK(m->alloc_n(&m->ex_y16, std::max(R * H, V)));
         QW_OK(m->alloc_n(&m->ex_kc, (size_t)m->c.max_position * kvd));
         QW_OK(m->alloc_n(&m->ex_vc, (size_t)m->c.max_position * kvd));
+        const HostExpTable& t = host_exp_table();
+        uint32_t *keys = nullptr, *vals = nullptr, *bucket = nullptr;
+        const size_t ne = std::max<size_t>(1, t.keys.size());
+        QW_OK(m->alloc_n(&keys, ne));
+        QW_OK(m->alloc_n(&vals, ne));
+        QW_OK(m->alloc_n(&bucket, t.bucket.size()));
+        if (!t.keys.empty()) {
+            QW_CUDA(cudaMemcpy(keys, t.keys.data(), t.keys.size() * 4, cudaMemcpyHostToDevice));
+            QW_CUDA(cudaMemcpy(vals, t.vals.data(), t.vals.size() * 4, cudaMemcpyHostToDevice));
+        }
+        QW_CUDA(cudaMemcpy(bucket, t.bucket.data(), t.bucket.size() * 4, cudaMemcpyHostToDevice));
+        m->ex_exp.keys = keys;
+        m->ex_exp.vals = vals;
+        m->ex_exp.bucket = bucket;
     }
     m->exact = on != 0;
     return KV_OK;
