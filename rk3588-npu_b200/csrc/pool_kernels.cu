@@ -219,6 +219,9 @@ __global__ void patch_kernel(PoolView pv, const TablePatch* __restrict__ patches
 __global__ void combine_kernel(int G, int rows, int dim, const float* __restrict__ m,
                                const float* __restrict__ l, const float* __restrict__ o,
                                size_t gstride_ml, size_t gstride_o, float* __restrict__ out) {
+    // A decode launch behind this merge may start now: it writes nothing
+    // before this kernel completes.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const long total = (long)rows * dim;
     for (long x = blockIdx.x * (long)blockDim.x + threadIdx.x; x < total; x += (long)gridDim.x * blockDim.x) {
         const int r = (int)(x / dim);

@@ -75,8 +75,12 @@ __device__ __forceinline__ bool wait_word(const uint2* p, unsigned epoch, float&
 
 // One CTA per (sequence, query head) row, one thread per dim.
 __global__ void __launch_bounds__(kHeadDim) xchg_kernel(const __grid_constant__ XchgArgs a) {
-    // The local states come from the decode grid (and its split merge):
-    // wait until they are complete and visible.
+    // The next layer's decode launch may start now (it writes nothing before
+    // this kernel completes, and its early tile copies read another layer):
+    // it overlaps the wait for the peers.  The local states come from the
+    // decode grid (and its split merge): wait until they are complete and
+    // visible.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int r = blockIdx.x, d = threadIdx.x;
     if (r >= a.rows) return;
