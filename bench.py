@@ -153,6 +153,9 @@ def parse_args():
     ap.add_argument("--kv-dtype", choices=["native", "int8"], default="native",
                     help="batch32 / paged28 / paged1: keep the workload's cache type, or an INT8 cache "
                          "(per-row scales) with the same contexts")
+    ap.add_argument("--merge", choices=["grid", "cluster"], default="grid",
+                    help="batch32 / paged28 / paged1: split heads merged by a merge launch behind the decode "
+                         "launch (grid), or inside 8-CTA clusters when the plan balances that way (cluster)")
     ap.add_argument("--sessions", type=int, default=8,
                     help="model_batch workload: concurrent sessions decoding together")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -447,6 +450,10 @@ def run_ours(args, rank, world, local):
     # launch of another group, or a copy: let each launch start its first
     # tile copies while that kernel finishes (the pool's overlap contract).
     P.set_overlap(True)
+    P.set_merge_mode(kv.KVP_MERGE_CLUSTER if args.merge == "cluster" else kv.KVP_MERGE_GRID)
+    P.plan(gids[0], append=[0] * len(gids[0]))  # the plan's shape only: appends nothing
+    merge = "8-CTA clusters" if P.plan_clusters()[0] else "merge launch"
+    P.commit()
     g = torch.Generator(device="cuda").manual_seed(100 + rank)
     nsteps = W + K
     q = torch.randn((nsteps, NL, B, HID), generator=g, device="cuda")
@@ -635,6 +642,7 @@ def run_ours(args, rank, world, local):
                          "traffic": ncu_traffic(wl.profile), "peak_source": peak_kind,
                          "kernel_ms": round(launch_ms, 5), "algorithmic_bytes": round(alg),
                          "timing": "events around the K back-to-back steps; average launch = elapsed / launches",
+                         "split_merge": merge,
                          "isolated": {"kernel_ms": round(iso_launch_ms, 5),
                                       "frac": round(alg / (iso_launch_ms * 1e-3) / 1e9 / peak, 4),
                                       "how": "L2 flushed before each step, events around each decode launch"}},

@@ -339,6 +339,25 @@ int kvp_timing_read(kvp_pool* pool, double* total_ms, int* launches);
 /* Number of SMs and of resident decode CTAs per SM used for grid sizing. */
 int kvp_launch_info(const kvp_pool* pool, int* num_sms, int* ctas_per_sm);
 
+/* How a decode launch merges a sequence's K/V heads split over several CTAs
+ * (long contexts are cut so every SM gets an equal share).  GRID (default):
+ * a merge launch right behind the decode launch (a programmatic dependent
+ * launch, so the next decode launch's first copies overlap it).  CLUSTER:
+ * the planner keeps every split inside a thread-block cluster of 8 CTAs and
+ * merges it there over distributed shared memory -- one launch per layer --
+ * when the cluster packing balances about as well as the grid-wide cut
+ * (else the plan stays GRID).  Measured on B200 for 32 sequences of
+ * U[256,4096] tokens, CLUSTER is slower (19.1-19.9 against 18.6 us per
+ * step): only 33 clusters of 8 fit at once (264 CTAs against 292), and each
+ * next launch can start only in whole free clusters.  Applies to plans made
+ * after the call. */
+#define KVP_MERGE_GRID 0
+#define KVP_MERGE_CLUSTER 1
+int kvp_set_merge_mode(kvp_pool* pool, int mode);
+/* Merge clusters of the active plan's launches (0: every split merged by
+ * the merge launch). */
+int kvp_plan_clusters(const kvp_pool* pool, int* clustered_launches, int* launches);
+
 /* ---- Placement of requests onto GPUs --------------------------------------
  * No counterpart in the reference: its engine runs one sequence on one
  * device (worker/src/engine/llm_engine.cpp:68-98).  A request is placed

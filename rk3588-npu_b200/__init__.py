@@ -23,6 +23,7 @@ KV_OK, KV_ERR_INVAL, KV_ERR_OOM, KV_ERR_BADSEQ, KV_ERR_CUDA, KV_ERR_RANGE, KV_ER
     KV_ERR_TIMEOUT = range(8)
 KV_F16, KV_BF16, KV_I8 = 0, 1, 2
 KVP_HOST_ONLY = -1
+KVP_MERGE_GRID, KVP_MERGE_CLUSTER = 0, 1
 HEAD_DIM = 128
 BLOCK_TOKENS = 16
 KVX_HANDLE_BYTES = 64
@@ -72,6 +73,8 @@ _SIGS = {
     "kvp_launch_info": [_vp, _ip, _ip],
     "kvp_timing_enable": [_vp, C.c_int],
     "kvp_set_overlap": [_vp, C.c_int],
+    "kvp_set_merge_mode": [_vp, C.c_int],
+    "kvp_plan_clusters": [_vp, _ip, _ip],
     "attn_contig_noalloc": [_vp, _vp, _vp, _vp] + [C.c_int] * 7 + [_vp],
     "kvp_timing_read": [_vp, C.POINTER(C.c_double), _ip],
     "kvx_create": [C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)],
@@ -352,6 +355,18 @@ class Pool:
         the previous kernel in the stream finishes (that kernel must not
         write this pool, other than as one of this pool's decode launches)."""
         call("kvp_set_overlap", self.h, int(enable))
+
+    def set_merge_mode(self, mode: int) -> None:
+        """kvp_set_merge_mode: KVP_MERGE_GRID (a merge launch behind the
+        decode launch, the default) or KVP_MERGE_CLUSTER (splits merged inside
+        8-CTA clusters when the packing balances)."""
+        call("kvp_set_merge_mode", self.h, int(mode))
+
+    def plan_clusters(self):
+        """(launches of the active plan merging inside clusters, launches)."""
+        a, b = C.c_int(), C.c_int()
+        call("kvp_plan_clusters", self.h, C.byref(a), C.byref(b))
+        return a.value, b.value
 
     def timing_read(self):
         """(summed decode-launch milliseconds, launches) since timing(True)."""

@@ -22,10 +22,18 @@
 //              (base 2), P^T transposed in registers with movmatrix,
 //              O^T += V^T * P^T (P split hi + lo).
 // At the end of a piece the four warps' states are merged in shared memory.
-// A segment cut into pieces writes per-piece partial (m, l, o); a small
-// combine kernel, launched behind the decode grid with programmatic
-// dependent launch (resident early, released when the grid completes),
-// merges each split segment's pieces with one round of loads.
+// A segment cut into pieces keeps per-piece partial (m, l, o) states, merged
+// in one of two ways the plan chooses:
+//  * a small combine kernel, launched behind the decode grid with
+//    programmatic dependent launch (resident early, released when the grid
+//    completes), merges each split segment's pieces (written to HBM) with
+//    one round of loads;
+//  * when the plan keeps every segment inside a cluster of kClusterCtas
+//    CTAs, the states stay in shared memory: after a cluster barrier the CTA
+//    holding a segment's first block reads the other pieces' states over
+//    distributed shared memory (ld.shared::cluster), writes the merged rows
+//    and releases the cluster with a second barrier, so the step is one
+//    launch.
 //
 // The new token: the consumer that owns the block holding position kv_len-1
 // rotates k (non-fused fp32, cos/sin from the host-built table), encodes k
@@ -85,8 +93,10 @@ struct Piece {
     int head;
     int b0;
     int b1;
-    int split;
-    int part;
+    int split;  // 0 whole segment, 1 merged by the combine kernel, 2 merged in the cluster
+    int part;   // split 1: partials row; split 2: cpart slot (0 first piece, 1 last)
+    int span;   // split 2, first piece of its segment: CTAs after this one holding the rest
+    int pad;
 };
 
 template <int DT>
@@ -96,6 +106,9 @@ struct Smem {
     float merge_o[kConsumerWarps][kMaxGroup][kMergeStride];
     float merge_m[kConsumerWarps][kMaxGroup];
     float merge_l[kConsumerWarps][kMaxGroup];
+    // States of the first and last piece when they are split inside a
+    // cluster: m[8], l[8], o[8][128] (the layout of a partials row).
+    alignas(16) float cpart[2][kPartialFloats];
     Piece items[kMaxCtaItems];        // this CTA's pieces
     int cum[kMaxCtaItems + 1];        // flat block offset of each piece
     int ok[kMaxCtaItems];             // piece's slot passed the checks
@@ -155,38 +168,46 @@ __device__ __forceinline__ int slot_check(const PoolView& pv, const DecodeSlot& 
 
 __host__ __device__ __forceinline__ int nblocks_of(int kv_len) { return (kv_len + kBlockTokens - 1) / kBlockTokens; }
 
-// Position of flat block f (< a.total) of a launch: slot i, KV head h, block
-// b of nb.  slot_f0 is non-decreasing; the largest i with slot_f0[i] <= f is
-// a slot with blocks (an empty slot shares its offset with the next one).
+// Position of flat block f (< a.total) of a launch: segment k (slot i, KV
+// head h), block b of its nb.  seg_f0 is increasing (segments have blocks).
 template <int S>
-__device__ __forceinline__ void locate(const DecodeArgs<S>& a, int kvh, int f, int& i, int& h, int& b, int& nb) {
-    int lo = 0, hi = a.nslots - 1;
+__device__ __forceinline__ void locate(const DecodeArgs<S>& a, int f, int& k, int& i, int& h, int& b, int& nb) {
+    int lo = 0, hi = a.nsegs - 1;
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
-        if (a.slot_f0[mid] <= f) lo = mid;
+        if (a.seg_f0[mid] <= f) lo = mid;
         else hi = mid - 1;
     }
-    i = lo;
-    nb = nblocks_of(a.slot[i].kv_len);
-    const int r = f - a.slot_f0[i];
-    h = nb > 0 ? r / nb : 0;
-    b = r - h * nb;
+    k = lo;
+    i = a.seg[k] & 0xffff;
+    h = a.seg[k] >> 16;
+    b = f - a.seg_f0[k];
+    nb = a.seg_f0[k + 1] - a.seg_f0[k];
 }
 
-// Step a position `k` flat blocks forward (never past the launch's blocks).
+// Step a position `n` flat blocks forward (never past the launch's segments).
 template <int S>
-__device__ __forceinline__ void advance(const DecodeArgs<S>& a, int kvh, int k, int& i, int& h, int& b, int& nb) {
-    b += k;
-    while (b >= nb && i < a.nslots) {
+__device__ __forceinline__ void advance(const DecodeArgs<S>& a, int n, int& k, int& i, int& h, int& b, int& nb) {
+    b += n;
+    while (b >= nb && k < a.nsegs) {
         b -= nb;
-        if (++h == kvh) {
-            h = 0;
-            do {
-                ++i;
-            } while (i < a.nslots && a.slot[i].kv_len == 0);
-            nb = i < a.nslots ? nblocks_of(a.slot[i].kv_len) : 1;
+        if (++k < a.nsegs) {
+            i = a.seg[k] & 0xffff;
+            h = a.seg[k] >> 16;
+            nb = a.seg_f0[k + 1] - a.seg_f0[k];
+        } else {
+            nb = 1;
         }
     }
+}
+
+// Segment (slot i, head h, nb blocks) is usable: it names a slot of the
+// launch (checked before that slot is read) whose fields pass slot_check,
+// a KV head of the pool, and the slot's block count.
+template <int S>
+__device__ __forceinline__ bool seg_ok(const DecodeArgs<S>& a, const PoolView& pv, int i, int h, int nb) {
+    return i < a.nslots && h >= 0 && h < pv.kv_heads && slot_check(pv, a.slot[i]) == 0 && nb == nblocks_of(a.slot[i].kv_len) &&
+           nb > 0;
 }
 
 // Tile id (block * kv_heads + head) of block b of a slot's segment, or -1
@@ -435,11 +456,19 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int layer = a.layer;
     const int kvh = pv.kv_heads;
     const bool early = (a.flags & kDecEarly) != 0;
+    // Merge inside clusters of `C` CTAs (every CTA takes the same branch:
+    // the cluster barriers below are reached by all threads of a cluster).
+    const int C = a.cluster;
+    const bool cmode = C > 1;
+    const int cbase = (int)blockIdx.x - (int)cluster_rank();
+    const bool cluster_ok = !cmode || ((int)cluster_size() == C && a.grid % C == 0);
     // This CTA's flat range, from the kernel parameters (checked; a bad range
     // is reported once the previous kernel has finished, and no work runs).
     int f0 = 0, f1 = 0;
-    const bool range_ok = a.nslots >= 0 && a.nslots <= S && a.grid <= kMaxGrid && (int)blockIdx.x < a.grid &&
-                          a.total >= 0 && (a.nslots > 0 || a.total == 0) && a.slot_f0[a.nslots] == a.total;
+    const bool range_ok = a.nslots >= 0 && a.nslots <= S && a.nsegs >= 0 && a.nsegs <= kSegsPerSlot * S &&
+                          a.grid <= kMaxGrid && (int)blockIdx.x < a.grid && a.total >= 0 &&
+                          (a.nsegs > 0 || a.total == 0) && a.seg_f0[0] == 0 && a.seg_f0[a.nsegs] == a.total &&
+                          cluster_ok;
     if (range_ok) {
         f0 = a.cta_f0[blockIdx.x];
         f1 = a.cta_f0[blockIdx.x + 1];
@@ -464,20 +493,19 @@ __global__ void __launch_bounds__(kThreads, 2)
     };
     // Producer lane l owns ring stage l and flat blocks f0 + l, f0 + l + 8, ...
     int pf = f0 + (prod_lane ? lane : 0);
-    int pi = 0, ph = 0, pb = 0, pnb = 1;
+    int pk = 0, pi = 0, ph = 0, pb = 0, pnb = 1;
     bool issued0 = false;
     if (prod_lane) {
         mbar_init(&sm.full[lane], 1);
         mbar_init(&sm.empty[lane], 1);
         fence_mbar_init();
         if (pf < f1) {
-            locate(a, kvh, pf, pi, ph, pb, pnb);
+            locate(a, pf, pk, pi, ph, pb, pnb);
             // Round 0 before the previous kernel has finished (kDecEarly): a
             // block that kernel may still write (the row the previous decode
             // launch appended) is read only after it.
-            const DecodeSlot& sl = a.slot[pi];
-            if (early && a.defer_blk[pi] != pb && slot_check(pv, sl) == 0) {
-                issue(lane, pf, tile_of(pv, sl, ph, pb));
+            if (early && seg_ok(a, pv, pi, ph, pnb) && a.defer_blk[pi] != pb) {
+                issue(lane, pf, tile_of(pv, a.slot[pi], ph, pb));
                 issued0 = true;
             }
         }
@@ -486,26 +514,43 @@ __global__ void __launch_bounds__(kThreads, 2)
         // This CTA's pieces (kernel parameters only).
         int n = 0, f = f0;
         if (f < f1) {
-            int i, h, b, nb;
-            locate(a, kvh, f, i, h, b, nb);
-            while (f < f1 && n < kMaxCtaItems && i < a.nslots) {
-                const int seg_end = a.slot_f0[i] + (h + 1) * nb;
+            int k, i, h, b, nb;
+            locate(a, f, k, i, h, b, nb);
+            while (f < f1 && n < kMaxCtaItems && k < a.nsegs) {
+                const int seg_end = a.seg_f0[k + 1];
                 const int e = min(seg_end, f1);
                 Piece& pc = sm.items[n];
                 pc.slot = i;
                 pc.head = h;
                 pc.b0 = b;
                 pc.b1 = b + (e - f);
-                pc.split = (b > 0 || e < seg_end) ? 1 : 0;
-                pc.part = 2 * (int)blockIdx.x + (n == 0 ? 0 : 1);
-                sm.ok[n] = slot_check(pv, a.slot[i]) == 0 && nb > 0;
+                pc.split = (b > 0 || e < seg_end) ? (cmode ? 2 : 1) : 0;
+                pc.part = cmode ? (n == 0 ? 0 : 1) : 2 * (int)blockIdx.x + (n == 0 ? 0 : 1);
+                pc.span = 0;
+                if (cmode && b == 0 && e < seg_end) {
+                    // The segment continues in the next CTAs of the cluster
+                    // (each holds it as its first piece); the plan never lets
+                    // it leave the cluster.
+                    int g = (int)blockIdx.x + 1;
+                    while (g < cbase + C && a.cta_f0[g] < seg_end) ++g;
+                    pc.span = g - (int)blockIdx.x - 1;
+                    if (g == cbase + C && a.cta_f0[g] < seg_end) {
+                        n = -2;
+                        break;
+                    }
+                }
+                sm.ok[n] = seg_ok(a, pv, i, h, nb);
                 ++n;
-                advance(a, kvh, e - f, i, h, b, nb);
+                advance(a, e - f, k, i, h, b, nb);
                 f = e;
             }
-            if (f < f1) n = -1;  // more pieces than a CTA holds: reported below, nothing runs
+            if (n >= 0 && f < f1) n = -1;  // more pieces than a CTA holds: reported below, nothing runs
         }
         sm.nitems = n;
+        for (int x = 0; x < 2 * kMaxGroup; ++x) {
+            sm.cpart[x / kMaxGroup][x % kMaxGroup] = -INFINITY;
+            sm.cpart[x / kMaxGroup][kMaxGroup + x % kMaxGroup] = 0.f;  // no weight until written
+        }
         sm.failed = 0;
         sm.prod_issued = 0;
         for (int w = 0; w < kConsumerWarps; ++w) sm.cons_done[w] = 0;
@@ -521,6 +566,71 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int total = sm.cum[n];
     const int nf = (total == f1 - f0) ? total : 0;  // blocks the producer streams
 
+    // Cluster merge, reached by every thread of the CTA (producer lanes too)
+    // after its own work: the CTA holding the first block of a segment split
+    // across the cluster (its last piece, first block 0) merges the states of
+    // the span CTAs after it (their first pieces, cpart[0]) with its own;
+    // the second barrier keeps every CTA's shared memory alive until then.
+    auto cluster_merge = [&]() {
+        if (!cmode) return;
+        cluster_sync();
+        if (warp < kConsumerWarps && n > 0 && nf > 0) {
+            const Piece w = sm.items[n - 1];
+            if (w.split == 2 && w.b0 == 0 && sm.ok[n - 1]) {
+                const uint32_t me = cluster_rank();
+                const int qrow = (a.row0 + w.slot) * pv.q_heads + w.head * pv.group;
+                const float* own = sm.cpart[w.part];
+                const uint32_t peer0 = smem_u32(sm.cpart[0]);
+                for (int x = tid; x < pv.group * 32; x += kConsumerWarps * 32) {
+                    const int h = x >> 5, c4 = x & 31;  // query head h, dims 4 c4 .. 4 c4 + 3
+                    float pm[kClusterCtas], pl[kClusterCtas];
+                    float4 po[kClusterCtas];
+                    pm[0] = own[h];
+                    pl[0] = own[kMaxGroup + h];
+                    po[0] = *reinterpret_cast<const float4*>(own + 2 * kMaxGroup + h * kHeadDim + 4 * c4);
+#pragma unroll
+                    for (int r = 1; r < kClusterCtas; ++r) {
+                        if (r <= w.span) {
+                            const uint32_t base = cluster_map(peer0, me + (uint32_t)r);
+                            pm[r] = ld_cluster_f32(base + 4u * h);
+                            pl[r] = ld_cluster_f32(base + 4u * (kMaxGroup + h));
+                            po[r] = ld_cluster_v4(base + 4u * (2 * kMaxGroup + h * kHeadDim + 4 * c4));
+                        } else {
+                            pm[r] = -INFINITY;
+                            pl[r] = 0.f;
+                            po[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+                    }
+                    float M = -INFINITY, L = 0.f;
+                    float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                    for (int r = 0; r < kClusterCtas; ++r) {
+                        if (!(pl[r] > 0.f)) continue;  // empty piece: no weight
+                        const float Mn = fmaxf(M, pm[r]);
+                        const float al = fast_exp2(M - Mn);  // 0 while M is -inf
+                        const float e = pl[r] * fast_exp2(pm[r] - Mn);
+                        A.x = A.x * al + e * po[r].x;
+                        A.y = A.y * al + e * po[r].y;
+                        A.z = A.z * al + e * po[r].z;
+                        A.w = A.w * al + e * po[r].w;
+                        L = L * al + e;
+                        M = Mn;
+                    }
+                    float* orow = out + (size_t)(qrow + h) * kHeadDim + 4 * c4;
+                    orow[0] = L > 0.f ? A.x / L : 0.f;
+                    orow[1] = L > 0.f ? A.y / L : 0.f;
+                    orow[2] = L > 0.f ? A.z / L : 0.f;
+                    orow[3] = L > 0.f ? A.w / L : 0.f;
+                    if (m_out != nullptr && c4 == 0) {
+                        m_out[qrow + h] = M * 0.6931471805599453f;
+                        l_out[qrow + h] = L;
+                    }
+                }
+            }
+        }
+        cluster_sync();
+    };
+
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------ producer
         // Everything below reads state the previous kernel may write (the
@@ -533,18 +643,16 @@ __global__ void __launch_bounds__(kThreads, 2)
             const bool live0 = pf < f1 && pf - f0 < nf;
             uint32_t rounds = issued0 ? 1u : 0u;  // rounds issued (all drained before the exit)
             if (live0 && !issued0) {
-                const DecodeSlot& sl = a.slot[pi];
-                issue(s, pf, slot_check(pv, sl) == 0 ? tile_of(pv, sl, ph, pb) : -2);
+                issue(s, pf, seg_ok(a, pv, pi, ph, pnb) ? tile_of(pv, a.slot[pi], ph, pb) : -2);
                 rounds = 1;
             }
             // Lane s refills its stage as soon as the consumer releases it,
             // polling without blocking; the next round's tile id is fetched
             // one round ahead.
             int f = pf + kStages;
-            if (live0) advance(a, kvh, kStages, pi, ph, pb, pnb);
+            if (live0) advance(a, kStages, pk, pi, ph, pb, pnb);
             auto next_tile = [&]() -> int {
-                const DecodeSlot& sl = a.slot[pi];
-                return slot_check(pv, sl) == 0 ? tile_of(pv, sl, ph, pb) : -2;
+                return seg_ok(a, pv, pi, ph, pnb) ? tile_of(pv, a.slot[pi], ph, pb) : -2;
             };
             int cur = (live0 && f - f0 < nf) ? next_tile() : -1;
             bool stopped = false;
@@ -559,7 +667,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                     atomicMax(&sm.prod_issued, f - f0 + 1);
                     f += kStages;
                     if (f - f0 < nf) {
-                        advance(a, kvh, kStages, pi, ph, pb, pnb);
+                        advance(a, kStages, pk, pi, ph, pb, pnb);
                         cur = next_tile();  // in flight while the stage drains
                     }
                     since = clock64();
@@ -574,6 +682,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             if (rounds > 0 && !mbar_wait_bounded(&sm.full[s], (rounds - 1) & 1, kWaitLimit))
                 flag_timeout(pv, sm, -2, 2, (uint32_t)(lane + (rounds - 1) * kStages));
         }
+        cluster_merge();
         return;
     }
 
@@ -583,7 +692,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (tid == 0) {
-        if (!range_ok) report(pv, 5, blockIdx.x, 300);
+        if (!range_ok) report(pv, 5, blockIdx.x, cluster_ok ? 300 : 305);
+        else if (sm.nitems == -2) report(pv, 5, blockIdx.x, 304);
         else if (sm.nitems < 0) report(pv, 5, blockIdx.x, 302);
         else if (nf != f1 - f0) report(pv, 5, blockIdx.x, 301);
     }
@@ -783,7 +893,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
         const int d = tid;  // 0..127: one output dim per thread
         const int qrow = row * pv.q_heads + wi.head * pv.group;
-        float* part = pv.partials + (size_t)wi.part * kPartialFloats;
+        float* part = wi.split == 2 ? sm.cpart[wi.part] : pv.partials + (size_t)wi.part * kPartialFloats;
         for (int h = 0; h < pv.group; ++h) {
             float M = -INFINITY;
 #pragma unroll
@@ -812,6 +922,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             }
         }
     }
+    cluster_merge();
 }
 
 // Merge of the pieces of every split segment, one CTA per (segment, query
@@ -912,17 +1023,43 @@ __global__ void __launch_bounds__(kCombineWarps * 32)
     }
 }
 
+// Two CTAs per SM: 228 KB of shared memory per SM, 1 KB of it reserved per CTA.
+static_assert(sizeof(Smem<0>) + 1024 <= 228 * 1024 / 2 - 1024, "two decode CTAs must fit an SM");
+static_assert(sizeof(Smem<1>) + 1024 <= 228 * 1024 / 2 - 1024, "two decode CTAs must fit an SM");
+static_assert(sizeof(Smem<2>) + 1024 <= 228 * 1024 / 2 - 1024, "two decode CTAs must fit an SM");
+
 template <int DT>
-static cudaError_t decode_occupancy_t(int* ctas_per_sm) {
+static cudaError_t decode_occupancy_t(int* ctas_per_sm, int* clusters) {
     const int smem = (int)sizeof(Smem<DT>) + 1024;
     cudaError_t e = cudaFuncSetAttribute(decode_kernel<DT, kSlotsSmall>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(decode_kernel<DT, kSlotsLarge>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, decode_kernel<DT, kSlotsSmall>, kThreads, smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, decode_kernel<DT, kSlotsSmall>, kThreads, smem);
+    if (e != cudaSuccess) return e;
+    // Merge clusters that fit the device at once (GPC boundaries can leave
+    // some CTA slots unused).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kClusterCtas);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kClusterCtas;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    *clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(clusters, decode_kernel<DT, kSlotsSmall>, &cfg);
+    if (e != cudaSuccess) {
+        (void)cudaGetLastError();  // no clusters: grid-wide merges only
+        *clusters = 0;
+    }
+    return cudaSuccess;
 }
 
-cudaError_t decode_occupancy(int dtype, int* ctas_per_sm) {
+cudaError_t decode_occupancy(int dtype, int* ctas_per_sm, int* clusters) {
     // The combine kernel runs beside two decode CTAs on an SM (resident
     // while the decode grid streams): give it the decode kernel's
     // shared-memory carveout, or the SM could not host both.
@@ -930,8 +1067,9 @@ cudaError_t decode_occupancy(int dtype, int* ctas_per_sm) {
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(combine_kernel<16>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
-    return dtype == 0 ? decode_occupancy_t<0>(ctas_per_sm)
-                      : dtype == 1 ? decode_occupancy_t<1>(ctas_per_sm) : decode_occupancy_t<2>(ctas_per_sm);
+    return dtype == 0   ? decode_occupancy_t<0>(ctas_per_sm, clusters)
+           : dtype == 1 ? decode_occupancy_t<1>(ctas_per_sm, clusters)
+                        : decode_occupancy_t<2>(ctas_per_sm, clusters);
 }
 
 template <int S>
@@ -942,11 +1080,19 @@ cudaError_t launch_decode(const PoolView& pv, const DecodeArgs<S>& a, const Comb
     cfg.gridDim = dim3((unsigned)(a.grid < 1 ? 1 : a.grid));
     cfg.blockDim = dim3(kThreads);
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)(a.cluster > 1 ? a.cluster : 1);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cudaLaunchAttribute dattr[2];
+    int nd = 0;
+    if (pdl) dattr[nd++] = attr[0];
+    if (a.cluster > 1) dattr[nd++] = attr[1];
+    cfg.attrs = dattr;
+    cfg.numAttrs = nd;
     cudaError_t e;
     if (pv.dtype == 0) {
         cfg.dynamicSmemBytes = sizeof(Smem<0>) + 1024;

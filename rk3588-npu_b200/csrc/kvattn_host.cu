@@ -79,8 +79,11 @@ struct Seq {
 // kernel parameters of its launches.
 struct SubPlan {
     int row0 = 0, nslots = 0, grid = 0, total = 0, max_pieces = 0;
+    int cluster = 1;                     // 1: grid-wide merge; kClusterCtas: merge inside clusters
     std::vector<DecodeSlot> slots;
-    std::vector<int> slot_f0;            // nslots + 1
+    std::vector<int> seg;                // slot | KV head << 16, in flat order
+    std::vector<int> seg_nb;             // blocks of each segment
+    std::vector<int> seg_f0;             // nsegs + 1
     std::vector<int> cta_f0;             // grid + 1
     std::vector<int2> comb;              // split segments (CombineArgs::seg)
 };
@@ -96,6 +99,8 @@ struct kvp_pool {
     int num_blocks = 0, dtype = 0, max_seqs = 0, max_seq_len = 0, mbps = 0;
     float theta = 0.f;
     int num_sms = 0, occupancy = 0;
+    int clusters = 0;      // merge clusters (kClusterCtas decode CTAs) resident at once; 0: none
+    int merge_mode = KVP_MERGE_GRID;  // kvp_set_merge_mode
     bool overlap = false;  // decode launches may copy their first tiles early (kvp_set_overlap)
     PoolView pv{};
 
@@ -352,6 +357,7 @@ int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, in
         // decode CTAs per SM) and kept on the host.
         p->num_sms = 148;
         p->occupancy = 2;
+        p->clusters = 148 * 2 / kClusterCtas;
         p->pv.num_blocks = num_blocks;
         p->pv.kv_heads = num_kv_heads;
         p->pv.q_heads = num_q_heads;
@@ -363,7 +369,7 @@ int kvp_create(int device, int num_layers, int num_q_heads, int num_kv_heads, in
         return KV_OK;
     }
     KV_CUDA_B(cudaDeviceGetAttribute(&p->num_sms, cudaDevAttrMultiProcessorCount, device));
-    KV_CUDA_B(decode_occupancy(dtype, &p->occupancy));
+    KV_CUDA_B(decode_occupancy(dtype, &p->occupancy, &p->clusters));
     if (p->occupancy < 1) p->occupancy = 1;
 
     const int tile_bytes = dtype == KV_I8 ? kTileBytesI8 : kTileBytes;
@@ -956,27 +962,26 @@ int attn_prefill_mma(kvp_pool* p, int layer, int seq, int pos0, int n, const flo
 
 namespace {
 
-// Work partition of one sub-plan whose slots are filled: every CTA gets one
-// contiguous run of the flat (slot, KV head, block) sequence of about equal
-// cost, a piece costing its blocks plus kPieceCost block-equivalents (warp
-// merge, q reload, partial write), so CTAs holding two pieces take fewer
-// blocks and every CTA finishes at about the same time.  A segment crossing
-// a CTA boundary becomes pieces merged by the combine kernel.
-void partition(const kvp_pool* p, SubPlan& sp) {
-    const int kvh = p->kv_heads;
-    const int n = sp.nslots;
-    sp.slot_f0.resize(n + 1);
+constexpr long kPieceCost = 6;  // block-equivalents a piece costs beyond its blocks
+
+// Work partition of one sub-plan whose slots are filled.  Segments (slot,
+// KV head) with blocks are listed slot-major; every CTA gets one contiguous
+// run of the flat block sequence of about equal cost, a piece costing its
+// blocks plus kPieceCost block-equivalents (warp merge, q reload, partial
+// write), so CTAs holding two pieces take fewer blocks and every CTA
+// finishes at about the same time.  A segment crossing a CTA boundary
+// becomes pieces merged by the combine kernel.  Returns the cost per CTA.
+long partition_grid(const kvp_pool* p, SubPlan& sp) {
+    const int nseg = (int)sp.seg.size();
     long T = 0;
-    int nseg = 0;
-    for (int i = 0; i < n; ++i) {
-        sp.slot_f0[i] = (int)T;
-        const int nb = (sp.slots[i].kv_len + kBlockTokens - 1) / kBlockTokens;
-        T += (long)kvh * nb;
-        if (nb) nseg += kvh;
+    sp.seg_f0.resize(nseg + 1);
+    for (int k = 0; k < nseg; ++k) {
+        sp.seg_f0[k] = (int)T;
+        T += sp.seg_nb[k];
     }
-    sp.slot_f0[n] = (int)T;
+    sp.seg_f0[nseg] = (int)T;
     sp.total = (int)T;
-    constexpr long kPieceCost = 6;
+    sp.cluster = 1;
     const long gmax = std::max(1L, std::min<long>(kMaxGrid, (long)p->num_sms * p->occupancy));
     // At least 16 blocks per CTA: below that, a split costs more (a merge)
     // than the blocks it moves to another SM.
@@ -989,31 +994,29 @@ void partition(const kvp_pool* p, SubPlan& sp) {
         sp.max_pieces = 0;
         long fill = 0;
         int cta_items = 0;
-        for (int i = 0; i < n; ++i) {
-            const int nb = (sp.slots[i].kv_len + kBlockTokens - 1) / kBlockTokens;
-            for (int h = 0; nb > 0 && h < kvh; ++h) {
-                const long F = sp.slot_f0[i] + (long)h * nb;
-                int b = 0, pieces = 0, first = 0;
-                while (b < nb) {
-                    if (cta_items > 0 && (fill + kPieceCost >= per || cta_items == kMaxCtaItems)) {
-                        sp.cta_f0.push_back((int)(F + b));
-                        fill = 0;
-                        cta_items = 0;
-                    }
-                    // A split segment's first piece is its CTA's first (partial
-                    // 2g) or last (2g + 1) piece; every later one is a first.
-                    if (pieces == 0) first = 2 * ((int)sp.cta_f0.size() - 1) + (cta_items == 0 ? 0 : 1);
-                    fill += kPieceCost;
-                    const int take = (int)std::min<long>(nb - b, std::max(1L, per - fill));
-                    b += take;
-                    fill += take;
-                    ++cta_items;
-                    ++pieces;
+        for (int k = 0; k < nseg; ++k) {
+            const int nb = sp.seg_nb[k];
+            const long F = sp.seg_f0[k];
+            int b = 0, pieces = 0, first = 0;
+            while (b < nb) {
+                if (cta_items > 0 && (fill + kPieceCost >= per || cta_items == kMaxCtaItems)) {
+                    sp.cta_f0.push_back((int)(F + b));
+                    fill = 0;
+                    cta_items = 0;
                 }
-                if (pieces > 1) {
-                    sp.comb.push_back(make_int2(i | (h << 16), first | (pieces << 16)));
-                    sp.max_pieces = std::max(sp.max_pieces, pieces);
-                }
+                // A split segment's first piece is its CTA's first (partial
+                // 2g) or last (2g + 1) piece; every later one is a first.
+                if (pieces == 0) first = 2 * ((int)sp.cta_f0.size() - 1) + (cta_items == 0 ? 0 : 1);
+                fill += kPieceCost;
+                const int take = (int)std::min<long>(nb - b, std::max(1L, per - fill));
+                b += take;
+                fill += take;
+                ++cta_items;
+                ++pieces;
+            }
+            if (pieces > 1) {
+                sp.comb.push_back(make_int2(sp.seg[k], first | (pieces << 16)));
+                sp.max_pieces = std::max(sp.max_pieces, pieces);
             }
         }
         sp.cta_f0.push_back((int)T);
@@ -1021,25 +1024,126 @@ void partition(const kvp_pool* p, SubPlan& sp) {
         per += per / 4 + 1;  // too many CTAs (the piece cap): coarser runs
     }
     sp.grid = (int)sp.cta_f0.size() - 1;
+    return per;
+}
+
+// The same step with split segments merged inside thread-block clusters:
+// segments are packed onto K clusters of kClusterCtas CTAs (longest first,
+// each onto the least loaded cluster), so no segment leaves its cluster;
+// each cluster's run is then cut into kClusterCtas equal-cost CTA ranges as
+// above.  Taken when the most loaded cluster's CTAs carry at most about the
+// grid-wide cost per CTA (`per`) plus what the combine launch costs; the plan
+// is left unchanged otherwise.
+bool partition_clusters(const kvp_pool* p, SubPlan& sp, long per) {
+    constexpr int Cn = kClusterCtas;
+    const int nseg = (int)sp.seg.size();
+    const long T = sp.total;
+    const long gmax = std::max(1L, std::min<long>(kMaxGrid, (long)p->num_sms * p->occupancy));
+    const long G = std::min(gmax, std::max(1L, (T + 15) / 16));
+    const int K = (int)std::min<long>({(long)p->clusters, kMaxGrid / Cn, (G + Cn - 1) / Cn, (long)nseg});
+    if (K < 1) return false;
+    std::vector<int> order(nseg);
+    for (int k = 0; k < nseg; ++k) order[k] = k;
+    std::stable_sort(order.begin(), order.end(), [&](int x, int y) { return sp.seg_nb[x] > sp.seg_nb[y]; });
+    std::vector<long> load(K, 0);
+    std::vector<int> owner(nseg);
+    std::vector<int> count(K, 0);
+    for (int k : order) {
+        int j = 0;
+        for (int c = 1; c < K; ++c)
+            if (load[c] < load[j]) j = c;
+        owner[k] = j;
+        load[j] += sp.seg_nb[k] + kPieceCost;
+        ++count[j];
+    }
+    long worst = 0;
+    for (int j = 0; j < K; ++j) worst = std::max(worst, (load[j] + kPieceCost * (Cn - 1) + Cn - 1) / Cn);
+    if (worst > per + per / 10 + 4) return false;
+    // Flat order: cluster by cluster, slot-major inside a cluster.
+    std::vector<int> seg(nseg), nbs(nseg), start(K + 1, 0);
+    for (int j = 0; j < K; ++j) start[j + 1] = start[j] + count[j];
+    std::vector<int> pos(start.begin(), start.end() - 1);
+    for (int k = 0; k < nseg; ++k) {
+        const int at = pos[owner[k]]++;
+        seg[at] = sp.seg[k];
+        nbs[at] = sp.seg_nb[k];
+    }
+    std::vector<int> f0(nseg + 1), cta(1, 0);
+    long F = 0;
+    for (int k = 0; k < nseg; ++k) {
+        f0[k] = (int)F;
+        F += nbs[k];
+    }
+    f0[nseg] = (int)F;
+    for (int j = 0; j < K; ++j) {
+        const long len = (long)f0[start[j + 1]] - f0[start[j]];
+        const long pj = std::max(kPieceCost + 1, (len + kPieceCost * (count[j] + Cn - 1) + Cn - 1) / Cn);
+        int used = 1;  // CTAs of this cluster begun
+        long fill = 0;
+        int cta_items = 0;
+        for (int k = start[j]; k < start[j + 1]; ++k) {
+            int b = 0;
+            while (b < nbs[k]) {
+                if (cta_items > 0 && used < Cn && (fill + kPieceCost >= pj || cta_items == kMaxCtaItems)) {
+                    cta.push_back(f0[k] + b);
+                    ++used;
+                    fill = 0;
+                    cta_items = 0;
+                }
+                if (cta_items == kMaxCtaItems) return false;  // the last CTA would hold too many pieces
+                fill += kPieceCost;
+                const int take = used < Cn ? (int)std::min<long>(nbs[k] - b, std::max(1L, pj - fill)) : nbs[k] - b;
+                b += take;
+                fill += take;
+                ++cta_items;
+            }
+        }
+        // CTAs of the cluster left without blocks get empty ranges; the
+        // cluster's end is the next cluster's first CTA start (or the end).
+        for (; used < Cn; ++used) cta.push_back(f0[start[j + 1]]);
+        cta.push_back(f0[start[j + 1]]);
+    }
+    sp.seg.swap(seg);
+    sp.seg_nb.swap(nbs);
+    sp.seg_f0.swap(f0);
+    sp.cta_f0.swap(cta);
+    sp.grid = K * Cn;
+    sp.cluster = Cn;
+    sp.comb.clear();
+    sp.max_pieces = 0;
+    return true;
+}
+
+void partition(const kvp_pool* p, SubPlan& sp) {
+    const int kvh = p->kv_heads;
+    sp.seg.clear();
+    sp.seg_nb.clear();
+    for (int i = 0; i < sp.nslots; ++i) {
+        const int nb = (sp.slots[i].kv_len + kBlockTokens - 1) / kBlockTokens;
+        for (int h = 0; nb > 0 && h < kvh; ++h) {
+            sp.seg.push_back(i | (h << 16));
+            sp.seg_nb.push_back(nb);
+        }
+    }
+    const long per = partition_grid(p, sp);
+    if (!sp.comb.empty() && p->merge_mode == KVP_MERGE_CLUSTER && p->clusters > 0) partition_clusters(p, sp, per);
 }
 
 // The pieces of CTA g of a sub-plan, derived from its flat range exactly as
 // the kernel derives them: (plan row, head, b0, b1) for each.
 template <class F>
 void cta_pieces(const kvp_pool* p, const SubPlan& sp, int g, F&& emit) {
-    const int kvh = p->kv_heads;
+    (void)p;
     int f = sp.cta_f0[g];
     const int f1 = sp.cta_f0[g + 1];
-    int i = 0;
+    if (f >= f1) return;
+    int k = (int)(std::upper_bound(sp.seg_f0.begin(), sp.seg_f0.end() - 1, f) - sp.seg_f0.begin()) - 1;
     while (f < f1) {
-        while (i + 1 <= sp.nslots - 1 && sp.slot_f0[i + 1] <= f) ++i;
-        const int nb = (sp.slots[i].kv_len + kBlockTokens - 1) / kBlockTokens;
-        const int r = f - sp.slot_f0[i];
-        const int h = r / nb, b = r - h * nb;
-        const int e = std::min(sp.slot_f0[i] + (h + 1) * nb, f1);
-        emit(sp.row0 + i, h, b, b + (e - f));
+        while (k + 1 < (int)sp.seg.size() && sp.seg_f0[k + 1] <= f) ++k;
+        const int b = f - sp.seg_f0[k];
+        const int e = std::min(sp.seg_f0[k + 1], f1);
+        emit(sp.row0 + (sp.seg[k] & 0xffff), sp.seg[k] >> 16, b, b + (e - f));
         f = e;
-        (void)kvh;
     }
 }
 
@@ -1051,11 +1155,16 @@ void fill_args(const kvp_pool* p, const SubPlan& sp, int layer, int flags, Decod
     a.flags = flags;
     a.total = sp.total;
     a.row0 = sp.row0;
-    a.pad[0] = a.pad[1] = 0;
+    a.nsegs = (int)sp.seg.size();
+    a.cluster = sp.cluster;
+    for (int k = 0; k < a.nsegs; ++k) {
+        a.seg_f0[k] = sp.seg_f0[k];
+        a.seg[k] = sp.seg[k];
+    }
+    a.seg_f0[a.nsegs] = sp.total;
     for (int i = 0; i < sp.nslots; ++i) {
         const DecodeSlot& sl = sp.slots[i];
         a.slot[i] = sl;
-        a.slot_f0[i] = sp.slot_f0[i];
         // A row the previous decode launch of this pool appended (to the
         // same layer, or with a table entry it wrote) is read only after
         // that launch finishes.
@@ -1064,7 +1173,6 @@ void fill_args(const kvp_pool* p, const SubPlan& sp, int layer, int flags, Decod
                           (p->last_layer == layer || p->last_patched);
         a.defer_blk[i] = prev ? sq.app_pos / kBlockTokens : -1;
     }
-    a.slot_f0[sp.nslots] = sp.total;
     for (int g = 0; g <= sp.grid; ++g) a.cta_f0[g] = sp.cta_f0[g];
 }
 
@@ -1137,13 +1245,15 @@ int attn_decode_plan_ex(kvp_pool* p, int nseq, const int* seq_ids, const int* ro
         }
         p->plan_append[i] = app;
     }
-    // ---- one launch per kSlotsLarge sequences, each partitioned on its own ----
+    // ---- one launch per kSlotsLarge sequences (fewer with more than
+    // kSegsPerSlot KV heads), each partitioned on its own ----
     // (the sub-plans' buffers are reused from plan to plan)
-    p->subs.resize((nseq + kSlotsLarge - 1) / kSlotsLarge);
+    const int per_launch = std::min(kSlotsLarge, kSegsPerSlot * kSlotsLarge / p->kv_heads);
+    p->subs.resize((nseq + per_launch - 1) / per_launch);
     for (size_t k = 0; k < p->subs.size(); ++k) {
         SubPlan& sp = p->subs[k];
-        sp.row0 = (int)k * kSlotsLarge;
-        sp.nslots = std::min(kSlotsLarge, nseq - sp.row0);
+        sp.row0 = (int)k * per_launch;
+        sp.nslots = std::min(per_launch, nseq - sp.row0);
         sp.slots.assign(slots.begin() + sp.row0, slots.begin() + sp.row0 + sp.nslots);
         partition(p, sp);
     }
@@ -1243,7 +1353,7 @@ static int decode_call(kvp_pool* p, int layer, const float* q, const float* k_ne
         ca.row0 = sp.row0;
         ca.pad[0] = ca.pad[1] = 0;
         for (size_t i = 0; i < sp.comb.size(); ++i) ca.seg[i] = sp.comb[i];
-        if (sp.nslots <= kSlotsSmall) {
+        if (sp.nslots <= kSlotsSmall && (int)sp.seg.size() <= kSegsPerSlot * kSlotsSmall) {
             DecodeArgs<kSlotsSmall> a;
             fill_args(p, sp, layer, flags, a);
             KV_CUDA(launch_decode(p->pv, a, ca, sp.max_pieces, q, k_new, v_new, out, m, l, pdl, st));
@@ -1278,6 +1388,24 @@ int kvp_set_overlap(kvp_pool* p, int enable) {
     std::lock_guard<std::mutex> lk(p->mu);
     if (int rc = require_device(p)) return rc;
     p->overlap = enable != 0;
+    return KV_OK;
+}
+
+int kvp_set_merge_mode(kvp_pool* p, int mode) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    if (mode != KVP_MERGE_GRID && mode != KVP_MERGE_CLUSTER) return fail(KV_ERR_INVAL, "unknown merge mode %d", mode);
+    std::lock_guard<std::mutex> lk(p->mu);
+    p->merge_mode = mode;
+    return KV_OK;
+}
+
+int kvp_plan_clusters(const kvp_pool* p, int* clustered_launches, int* launches) {
+    if (!p) return fail(KV_ERR_INVAL, "pool is NULL");
+    if (!p->plan_active) return fail(KV_ERR_STATE, "no active decode plan");
+    int c = 0;
+    for (const SubPlan& sp : p->subs) c += sp.cluster > 1;
+    if (clustered_launches) *clustered_launches = c;
+    if (launches) *launches = (int)p->subs.size();
     return KV_OK;
 }
 

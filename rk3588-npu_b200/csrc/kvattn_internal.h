@@ -40,18 +40,27 @@ struct TablePatch {
 // ---- decode plans (kernel parameters) ---------------------------------
 // A decode step is passed to its launches by value: the host owns the block
 // tables and lengths, so it builds the work partition in O(sequences + CTAs)
-// and no plan is uploaded.  Work is the flat sequence of 16-token blocks of
-// every segment (slot i, KV head h), slot-major: segment (i, h) is blocks
-// [slot_f0[i] + h * nb_i, slot_f0[i] + (h + 1) * nb_i) with nb_i =
-// ceil(kv_len_i / 16).  CTA g owns flat blocks [cta_f0[g], cta_f0[g + 1]);
-// its pieces are the maximal runs of one segment inside that range.  Only a
-// CTA's first and last piece can be part of a segment that other CTAs share
-// (a split segment); their partial states go to partials[2g] (first piece)
-// and partials[2g + 1] (last piece), merged by the combine kernel launched
-// right behind the decode grid.
+// and no plan is uploaded.  Work is a flat sequence of 16-token blocks made
+// of segments, one per (slot i, KV head h) with blocks: segment k is flat
+// blocks [seg_f0[k], seg_f0[k + 1]), all ceil(kv_len_i / 16) blocks of
+// (seg[k] & 0xffff, seg[k] >> 16).  CTA g owns flat blocks [cta_f0[g],
+// cta_f0[g + 1]); its pieces are the maximal runs of one segment inside that
+// range.  Only a CTA's first and last piece can be part of a segment that
+// other CTAs share (a split segment).  Two ways to merge split segments:
+//  * grid-wide (cluster == 1): the pieces' partial states go to partials[2g]
+//    (first piece) and partials[2g + 1] (last piece), merged by the combine
+//    kernel launched right behind the decode grid;
+//  * in a thread-block cluster (cluster == C > 1): the launch runs in
+//    clusters of C consecutive CTAs and the plan keeps every segment inside
+//    one cluster; a split piece's state stays in its CTA's shared memory and
+//    the CTA holding the segment's first block merges the others' states
+//    over distributed shared memory once the cluster has finished (no
+//    combine launch).
 constexpr int kMaxGrid = 320;       // decode CTAs per launch (B200: 148 SMs x 2 resident)
 constexpr int kSlotsSmall = 64;     // slot capacities of the two kernel-parameter layouts
 constexpr int kSlotsLarge = 256;    // (a step with more sequences runs as several launches)
+constexpr int kSegsPerSlot = 2;     // segment capacity per slot (KV heads beyond 2: fewer slots per launch)
+constexpr int kClusterCtas = 8;     // CTAs of a merge cluster (portable cluster size)
 
 struct DecodeSlot {
     int seq;        // row of the block table
@@ -72,8 +81,10 @@ struct DecodeArgs {
     int flags;
     int total;                  // flat blocks of the launch
     int row0;                   // row of slot 0 in q / k_new / v_new / out / m / l
-    int pad[2];
-    int slot_f0[S + 1];         // flat offset of slot i's first segment; slot_f0[nslots] = total
+    int nsegs;                  // segments (slots with kv_len > 0, times KV heads)
+    int cluster;                // 1: grid-wide merge; kClusterCtas: merge inside clusters
+    int seg_f0[kSegsPerSlot * S + 1];  // flat offset of segment k; seg_f0[nsegs] = total
+    int seg[kSegsPerSlot * S];  // slot | KV head << 16
     DecodeSlot slot[S];
     int defer_blk[S];           // block of slot i the previous decode launch may still write (-1: none)
     int cta_f0[kMaxGrid + 1];   // flat range of every CTA
@@ -118,7 +129,9 @@ template <int S>
 cudaError_t launch_decode(const PoolView& pv, const DecodeArgs<S>& a, const CombineArgs& c, int max_pieces,
                           const float* q, const float* k_new, const float* v_new, float* out, float* m_out,
                           float* l_out, bool pdl, cudaStream_t st);
-cudaError_t decode_occupancy(int dtype, int* ctas_per_sm);
+// ctas_per_sm: resident decode CTAs per SM; clusters: resident merge
+// clusters (kClusterCtas CTAs each) on the device, 0 if none fit.
+cudaError_t decode_occupancy(int dtype, int* ctas_per_sm, int* clusters);
 cudaError_t launch_import(const PoolView& pv, int layer, int seq, int pos0, int n,
                           const uint16_t* k_rows, const uint16_t* v_rows, cudaStream_t st);
 cudaError_t launch_gather(const PoolView& pv, int layer, int seq, int len, uint16_t* k_rows,

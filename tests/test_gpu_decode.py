@@ -161,16 +161,60 @@ def test_decode_long_sequence_many_chunks(kv, orc):
     assert H.P.cur_pos(H.ids[0]) == info_lens[0] + 2
 
 
-def test_decode_config2_shape(kv, orc):
-    """Batch 32, lengths U[256,4096] (seed 1), fp16: 4 steps, every row checked."""
+@pytest.mark.parametrize("mode", ["cluster", "grid"])
+def test_decode_config2_shape(kv, orc, mode):
+    """Batch 32, lengths U[256,4096] (seed 1), fp16: 4 steps, every row checked,
+    split heads merged by the grid-wide merge launch (the default) or inside
+    8-CTA clusters."""
     need_gpu()
     rng = np.random.default_rng(1)
     lens = [int(x) for x in rng.integers(256, 4097, 32)]
     H = Harness(kv, orc, lens, 0, seed=1, extra=8)
+    H.P.set_merge_mode(kv.KVP_MERGE_CLUSTER if mode == "cluster" else kv.KVP_MERGE_GRID)
+    H.P.plan(H.ids, append=[0] * len(H.ids))  # the plan's shape; appends nothing
+    assert H.P.plan_clusters() == ((1, 1) if mode == "cluster" else (0, 1))
+    H.P.commit()
     for _ in range(4):
         assert H.step(check_gather=False) <= TOL
     H.check_cache()
     assert H.P.device_status() == 0
+
+
+@pytest.mark.parametrize("dtype", [0, 1], ids=["f16", "bf16"])
+def test_decode_cluster_and_grid_merges_agree(kv, orc, dtype):
+    """The same step planned both ways (split heads merged inside 8-CTA
+    clusters, or by the merge launch): outputs within 1e-3 of the oracle and
+    (m, l) of the two within rounding, for group sizes 6 and 8.  (INT8 pools:
+    test_int8_kv covers a clustered and a grid-wide plan.)"""
+    need_gpu()
+    for qh, lens in ((12, [3, 100, 513, 1500, 40]), (16, [700, 2100, 64])):
+        res = []
+        for mode in (kv.KVP_MERGE_CLUSTER, kv.KVP_MERGE_GRID):
+            H = Harness(kv, orc, lens, dtype, q_heads=qh, seed=11 + qh, extra=4)
+            H.P.set_merge_mode(mode)
+            B = len(lens)
+            H.P.plan(H.ids)
+            clustered = H.P.plan_clusters()[0]
+            q = H.rng.standard_normal((B, qh * HD)).astype(np.float32)
+            k = H.rng.standard_normal((B, H.kvd)).astype(np.float32)
+            v = H.rng.standard_normal((B, H.kvd)).astype(np.float32)
+            out = torch.empty((B, qh * HD), dtype=torch.float32, device="cuda")
+            m = torch.empty((B * qh,), dtype=torch.float32, device="cuda")
+            l = torch.empty((B * qh,), dtype=torch.float32, device="cuda")
+            H.P.decode_layer(0, to_dev(q), to_dev(k), to_dev(v), out, m, l)
+            H.P.commit()
+            got = out.cpu().numpy()
+            for i in range(B):
+                ref, _, _ = orc.layer_step(q[i:i + 1], k[i:i + 1], v[i:i + 1], H.kc[i][0], H.vc[i][0],
+                                           H.len[i], qh, H.kvh, HD, 1e6, dtype)
+                assert rel_err(got[i], ref[0]) <= TOL, (mode, i)
+            res.append((clustered, got, m.cpu().numpy(), l.cpu().numpy()))
+            assert H.P.device_status() == 0
+        (c0, o0, m0, l0), (c1, o1, m1, l1) = res
+        assert c0 == 1 and c1 == 0
+        assert rel_err(o0, o1) <= TOL
+        assert np.allclose(m0, m1, rtol=1e-5, atol=1e-5)
+        assert np.allclose(l0, l1, rtol=1e-4, atol=0)
 
 
 @pytest.mark.parametrize("dtype", [0, 1], ids=["f16", "bf16"])

@@ -200,6 +200,7 @@ def test_lengths_and_errors(kv):
 
 def test_plan_pieces_cover_every_block_once_balanced(kv):
     P = host_pool(kv, nblocks=40000, max_seqs=40, max_seq_len=32768)
+    P.set_merge_mode(kv.KVP_MERGE_GRID)
     rng = np.random.default_rng(1)
     lens = [0, 1, 15, 16, 17, 255, 256, 257] + list(rng.integers(1, 20000, 24))
     ids = []
@@ -231,6 +232,57 @@ def test_plan_pieces_cover_every_block_once_balanced(kv):
     assert info["npatch"] == sum(1 for L in lens if L % 16 == 0)
     P.commit()
     assert [P.cur_pos(s) for s in ids] == [L + 1 for L in lens]
+
+
+def _plan_costs(info):
+    items, cs = info["items"], info["cta_start"]
+    return [sum(b1 - b0 + 6 for (_, _, b0, b1) in items[cs[g]:cs[g + 1]]) for g in range(info["grid"])]
+
+
+@pytest.mark.parametrize("lens", [
+    [int(x) + 1 for x in np.random.default_rng(1).integers(256, 4097, 32)],   # batch 32, U[256,4096]
+    [3, 100, 513],                                                          # one cluster
+    [int(min(8192, x)) for x in np.random.default_rng(2).lognormal(np.log(2048.0), 0.8, 200)],
+], ids=["batch32", "small", "lognormal200"])
+def test_plan_cluster_merge_keeps_segments_in_clusters(kv, lens):
+    """Merging inside 8-CTA clusters: every (slot, head, block) once, every
+    split segment's pieces in consecutive CTAs of ONE cluster (each later
+    piece its CTA's first), and CTA costs close to the grid-wide cut."""
+    def mk(mode):
+        P = host_pool(kv, nblocks=sum(-(-(L + 1) // 16) for L in lens) + 8, max_seqs=len(lens), max_seq_len=8300)
+        P.set_merge_mode(mode)
+        ids = []
+        for L in lens:
+            s = P.seq_alloc()
+            P.reserve(s, int(L))
+            P.set_cur_pos(s, int(L))
+            ids.append(s)
+        P.plan(ids)
+        return P, P.plan_info()
+    Pg, grid_info = mk(kv.KVP_MERGE_GRID)
+    assert Pg.plan_clusters() == (0, 1)
+    P, info = mk(kv.KVP_MERGE_CLUSTER)
+    assert P.plan_clusters() == (1, 1)
+    items, cs = info["items"], info["cta_start"]
+    assert info["grid"] % 8 == 0 and info["grid"] <= 320
+    cover, where = {}, {}
+    for g in range(info["grid"]):
+        for j, (slot, h, b0, b1) in enumerate(items[cs[g]:cs[g + 1]]):
+            for b in range(b0, b1):
+                assert (slot, h, b) not in cover
+                cover[(slot, h, b)] = 1
+            where.setdefault((slot, h), []).append((g, j, b0, b1))
+    want = {(i, h, b) for i, L in enumerate(lens) for h in range(2) for b in range(-(-(L + 1) // 16))}
+    assert set(cover) == want
+    for pieces in where.values():
+        gs = [g for g, _, _, _ in pieces]
+        assert len({g // 8 for g in gs}) == 1                      # one cluster
+        assert gs == list(range(gs[0], gs[0] + len(gs)))           # consecutive CTAs
+        assert pieces[0][2] == 0 and all(j == 0 for _, j, _, _ in pieces[1:])
+        assert all(pieces[u][3] == pieces[u + 1][2] for u in range(len(pieces) - 1))
+    assert all(cs[g + 1] - cs[g] <= 64 for g in range(info["grid"]))
+    gmax = max(_plan_costs(grid_info))
+    assert max(_plan_costs(info)) <= gmax + gmax // 10 + 4 + 6
 
 
 def test_plan_small_workload_uses_few_ctas(kv):
