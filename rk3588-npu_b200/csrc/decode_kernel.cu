@@ -35,6 +35,12 @@
 //    and releases the cluster with a second barrier, so the step is one
 //    launch.
 //
+// INT8 caches: the ring has 16 stages of compact tiles (codes + row scales,
+// half the bytes of a 16-bit block) and the consumers read the codes in
+// place: ldmatrix on pairs of codes, each pair converted to an exact f16x2 in
+// registers, the scores scaled by the key's K scale and the weights by its V
+// scale (consume_block_i8).
+//
 // The new token: the consumer that owns the block holding position kv_len-1
 // rotates k (non-fused fp32, cos/sin from the host-built table), encodes k
 // and v with the truncating encoders, stores the row to HBM (the append) and
@@ -50,33 +56,37 @@ namespace kvattn {
 
 namespace {
 
-constexpr int kStages = 8;
 constexpr int kConsumerWarps = 4;
-// Stage k of the ring is consumed by warp k % kConsumerWarps.  With kStages a
-// multiple of kConsumerWarps every stage belongs to ONE warp, which consumes
-// its rounds in order; so no waiter is ever more than one phase ahead of a
-// barrier, the condition under which a parity wait is unambiguous.  (With 6
-// stages and 4 warps a warp could wait on round r+1 of a stage whose round r,
-// owned by another warp, had not landed; the parity test then passed early.)
-static_assert(kStages % kConsumerWarps == 0, "each ring stage must belong to one consumer warp");
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 
-// Shared-memory shapes per cache type.  16-bit caches: a ring stage holds the
-// K and V tiles as they lie in HBM (the swizzled mma layout).  INT8 caches: a
-// stage holds the two compact tiles (codes + scales); each consumer warp
-// expands the block it owns into its own 16-bit tile pair (`scratch`).
+// Shared-memory ring per cache type: a stage holds one block's K and V tiles
+// as they lie in HBM -- 16-bit caches the swizzled mma layout (8 KB a
+// stage), INT8 caches the compact tiles (codes in the swizzled i8_offset
+// layout + row scales, 4.1 KB a stage), which the consumers read in place.
+// INT8 stages are half the size, so the ring has twice as many: the bytes
+// in flight per CTA, which bound its streaming rate, stay the same.
+// Stage k of the ring is consumed by warp k % kConsumerWarps.  With the
+// stage count a multiple of kConsumerWarps every stage belongs to ONE warp,
+// which consumes its rounds in order; so no waiter is ever more than one
+// phase ahead of a barrier, the condition under which a parity wait is
+// unambiguous.  (With 6 stages and 4 warps a warp could wait on round r+1 of
+// a stage whose round r, owned by another warp, had not landed; the parity
+// test then passed early.)
 template <int DT>
 struct StageCfg {
     static constexpr int tile = kTileBytes;
     static constexpr int stage = 2 * kTileBytes;
-    static constexpr int scratch = 16;  // unused
+    static constexpr int stages = 8;
 };
 template <>
 struct StageCfg<2> {
     static constexpr int tile = kTileBytesI8;
     static constexpr int stage = 2 * kTileBytesI8;
-    static constexpr int scratch = 2 * kTileBytes;
+    static constexpr int stages = 16;
 };
+static_assert(StageCfg<0>::stages % kConsumerWarps == 0 && StageCfg<2>::stages % kConsumerWarps == 0,
+              "each ring stage must belong to one consumer warp");
+static_assert(StageCfg<2>::stages <= 32, "one producer lane per stage");
 // The tensor-core operand type: fp16 for fp16 and int8 caches (int8 codes are
 // exact in fp16), bf16 for bf16 caches.
 template <int DT>
@@ -101,8 +111,8 @@ struct Piece {
 
 template <int DT>
 struct Smem {
-    alignas(1024) uint8_t stage[kStages][StageCfg<DT>::stage];
-    alignas(1024) uint8_t scratch[kConsumerWarps][StageCfg<DT>::scratch];
+    static constexpr int kS = StageCfg<DT>::stages;
+    alignas(1024) uint8_t stage[kS][StageCfg<DT>::stage];
     float merge_o[kConsumerWarps][kMaxGroup][kMergeStride];
     float merge_m[kConsumerWarps][kMaxGroup];
     float merge_l[kConsumerWarps][kMaxGroup];
@@ -114,8 +124,8 @@ struct Smem {
     int ok[kMaxCtaItems];             // piece's slot passed the checks
     // q fragments (hi, lo) of the first kQPre pieces, as each lane holds them
     uint32_t qfrag[kQPre][2][8][2][32];
-    uint64_t full[kStages];
-    uint64_t empty[kStages];
+    uint64_t full[kS];
+    uint64_t empty[kS];
     int nitems;
     int last_flag;
     int failed;
@@ -136,7 +146,7 @@ template <class SmemT>
 __device__ __forceinline__ void flag_timeout(const PoolView& pv, SmemT& sm, int item, int role,
                                              uint32_t k) {
     if (atomicCAS(pv.status, 0, 7 /* KV_ERR_TIMEOUT */) == 0) {
-        const int s = k % kStages;
+        const int s = k % SmemT::kS;
         const uint64_t f = *reinterpret_cast<volatile uint64_t*>(&sm.full[s]);
         const uint64_t e = *reinterpret_cast<volatile uint64_t*>(&sm.empty[s]);
         pv.status[1] = item;
@@ -144,7 +154,7 @@ __device__ __forceinline__ void flag_timeout(const PoolView& pv, SmemT& sm, int 
         pv.status[3] = blockIdx.x;
         pv.status[4] = threadIdx.x >> 5;
         pv.status[5] = (int)k;
-        pv.status[6] = (int)(k / kStages);
+        pv.status[6] = (int)(k / SmemT::kS);
         pv.status[7] = (int)(uint32_t)f;
         pv.status[8] = (int)(uint32_t)(f >> 32);
         pv.status[9] = (int)(uint32_t)e;
@@ -241,19 +251,47 @@ __device__ __forceinline__ void load_q_frags(const PoolView& pv, const float* q,
     }
     const float* qr = q + (size_t)row * (pv.q_heads * kHeadDim) + (size_t)(head * pv.group + g) * kHeadDim;
     const float* cs = reinterpret_cast<const float*>(pv.rope + (size_t)rope_pos * (kHeadDim / 2));
+    if constexpr (DT == 2) {
+        // INT8 keys are read in place by ldmatrix as pairs of codes: k-step
+        // kk's slots 2c, 2c+1 / 2c+8, 2c+9 hold dims kk*16 + 4c + {0, 1} /
+        // {2, 3} (a permutation of the dot product's terms, the same for
+        // every key row), so this thread's q dims are kk*16 + 4c .. + 3.
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
+        for (int kk = 0; kk < 4; ++kk) {
+            const int i = kk * 16 + 4 * c;  // < 64; partners i + 64 are k-step kk + 4
+            const float2 a01 = *reinterpret_cast<const float2*>(qr + i);  // q rows are 8-byte aligned
+            const float2 a23 = *reinterpret_cast<const float2*>(qr + i + 2);
+            const float2 b01 = *reinterpret_cast<const float2*>(qr + i + 64);
+            const float2 b23 = *reinterpret_cast<const float2*>(qr + i + 66);
+            const float4 a = make_float4(a01.x, a01.y, a23.x, a23.y);
+            const float4 b = make_float4(b01.x, b01.y, b23.x, b23.y);
+            const float4 t0 = *reinterpret_cast<const float4*>(cs + 2 * i);      // c_i, s_i, c_i+1, s_i+1
+            const float4 t1 = *reinterpret_cast<const float4*>(cs + 2 * i + 4);  // c_i+2, s_i+2, ...
+            float lo[4], hi[4];
+            rope_pair(a.x, b.x, t0.x, t0.y, lo[0], hi[0]);
+            rope_pair(a.y, b.y, t0.z, t0.w, lo[1], hi[1]);
+            rope_pair(a.z, b.z, t1.x, t1.y, lo[2], hi[2]);
+            rope_pair(a.w, b.w, t1.z, t1.w, lo[3], hi[3]);
+            split_pair<0>(lo[0] * qscale, lo[1] * qscale, qh[kk][0], ql[kk][0]);
+            split_pair<0>(lo[2] * qscale, lo[3] * qscale, qh[kk][1], ql[kk][1]);
+            split_pair<0>(hi[0] * qscale, hi[1] * qscale, qh[kk + 4][0], ql[kk + 4][0]);
+            split_pair<0>(hi[2] * qscale, hi[3] * qscale, qh[kk + 4][1], ql[kk + 4][1]);
+        }
+    } else {
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            const int i = kk * 16 + r * 8 + 2 * c;  // even, < 64
-            float2 a = *reinterpret_cast<const float2*>(qr + i);
-            float2 b = *reinterpret_cast<const float2*>(qr + i + 64);
-            float4 t = *reinterpret_cast<const float4*>(cs + 2 * i);  // c_i, s_i, c_i+1, s_i+1
-            float lo0, hi0, lo1, hi1;
-            rope_pair(a.x, b.x, t.x, t.y, lo0, hi0);
-            rope_pair(a.y, b.y, t.z, t.w, lo1, hi1);
-            split_pair<mma_type<DT>()>(lo0 * qscale, lo1 * qscale, qh[kk][r], ql[kk][r]);
-            split_pair<mma_type<DT>()>(hi0 * qscale, hi1 * qscale, qh[kk + 4][r], ql[kk + 4][r]);
+        for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const int i = kk * 16 + r * 8 + 2 * c;  // even, < 64
+                float2 a = *reinterpret_cast<const float2*>(qr + i);
+                float2 b = *reinterpret_cast<const float2*>(qr + i + 64);
+                float4 t = *reinterpret_cast<const float4*>(cs + 2 * i);  // c_i, s_i, c_i+1, s_i+1
+                float lo0, hi0, lo1, hi1;
+                rope_pair(a.x, b.x, t.x, t.y, lo0, hi0);
+                rope_pair(a.y, b.y, t.z, t.w, lo1, hi1);
+                split_pair<mma_type<DT>()>(lo0 * qscale, lo1 * qscale, qh[kk][r], ql[kk][r]);
+                split_pair<mma_type<DT>()>(hi0 * qscale, hi1 * qscale, qh[kk + 4][r], ql[kk + 4][r]);
+            }
         }
     }
 }
@@ -296,8 +334,8 @@ __device__ __forceinline__ void write_new_row(const PoolView& pv, int layer, int
 
 // INT8 cache: the new token's k (rotated) and v rows quantised by the warp
 // (quant_row_warp), codes and scales stored to the pool tile (the append)
-// and the codes, as fp16, into the warp's expanded tiles; ks / vs receive the
-// row's scales.
+// and the codes into the staged compact tiles; ks / vs receive the row's
+// scales.
 __device__ __forceinline__ void write_new_row_i8(const PoolView& pv, int layer, int blk, int head, int t,
                                                  const float* k_new, const float* v_new, int row, int rope_pos,
                                                  uint8_t* sK, uint8_t* sV, int lane, float& ks, float& vs) {
@@ -324,33 +362,31 @@ __device__ __forceinline__ void write_new_row_i8(const PoolView& pv, int layer, 
     const size_t tile = (size_t)layer * pv.layer_bytes + ((size_t)blk * pv.kv_heads + head) * kTileBytesI8;
     uint8_t* kt = pv.k + tile;
     uint8_t* vt = pv.v + tile;
-    *reinterpret_cast<char2*>(kt + t * kHeadDim + i) = make_char2(kc[0], kc[1]);
-    *reinterpret_cast<char2*>(kt + t * kHeadDim + i + 64) = make_char2(kc[2], kc[3]);
-    *reinterpret_cast<char2*>(vt + t * kHeadDim + i) = make_char2(vc[0], vc[1]);
-    *reinterpret_cast<char2*>(vt + t * kHeadDim + i + 64) = make_char2(vc[2], vc[3]);
+    const uint32_t o_lo = i8_offset(t, i), o_hi = i8_offset(t, i + 64);
+    *reinterpret_cast<char2*>(kt + o_lo) = make_char2(kc[0], kc[1]);
+    *reinterpret_cast<char2*>(kt + o_hi) = make_char2(kc[2], kc[3]);
+    *reinterpret_cast<char2*>(vt + o_lo) = make_char2(vc[0], vc[1]);
+    *reinterpret_cast<char2*>(vt + o_hi) = make_char2(vc[2], vc[3]);
     if (lane == 0) {
         reinterpret_cast<float*>(kt + kBlockTokens * kHeadDim)[t] = ks;
         reinterpret_cast<float*>(vt + kBlockTokens * kHeadDim)[t] = vs;
     }
-    *reinterpret_cast<uint32_t*>(sK + tile_offset(t, i)) = codes_to_half2(kc[0], kc[1]);
-    *reinterpret_cast<uint32_t*>(sK + tile_offset(t, i + 64)) = codes_to_half2(kc[2], kc[3]);
-    *reinterpret_cast<uint32_t*>(sV + tile_offset(t, i)) = codes_to_half2(vc[0], vc[1]);
-    *reinterpret_cast<uint32_t*>(sV + tile_offset(t, i + 64)) = codes_to_half2(vc[2], vc[3]);
+    *reinterpret_cast<char2*>(sK + o_lo) = make_char2(kc[0], kc[1]);
+    *reinterpret_cast<char2*>(sK + o_hi) = make_char2(kc[2], kc[3]);
+    *reinterpret_cast<char2*>(sV + o_lo) = make_char2(vc[0], vc[1]);
+    *reinterpret_cast<char2*>(sV + o_hi) = make_char2(vc[2], vc[3]);
 }
 
-// INT8 cache: expand a staged compact tile (codes row-major + scales) into
-// the 16-bit swizzled layout the mma path reads; lane l converts 16-byte
-// output chunks l, l+32, ... (row x / 16, 8 dims x % 16).
-__device__ __forceinline__ void expand_tile_i8(const uint8_t* src, uint8_t* dst, int lane) {
-#pragma unroll 4
-    for (int x = lane; x < kBlockTokens * 16; x += 32) {
-        const int t = x >> 4, ch = x & 15;
-        const uint2 raw = *reinterpret_cast<const uint2*>(src + t * kHeadDim + ch * 8);
-        const int8_t* c = reinterpret_cast<const int8_t*>(&raw);
-        *reinterpret_cast<uint4*>(dst + tile_offset(t, ch * 8)) =
-            make_uint4(codes_to_half2(c[0], c[1]), codes_to_half2(c[2], c[3]), codes_to_half2(c[4], c[5]),
-                       codes_to_half2(c[6], c[7]));
-    }
+// Two int8 codes of a 32-bit word, chosen by the byte selector `sel`
+// (0x4140: bytes 0 and 1, 0x4342: 2 and 3, 0x4240: 0 and 2, 0x4341: 1 and 3),
+// as an exact f16x2.  `xf` is the word with every byte's sign bit flipped
+// (code + 128 as an unsigned byte); under the exponent bits 0x64 that byte
+// is the half 1024 + code + 128, and subtracting 1152 (0x6480) leaves code.
+__device__ __forceinline__ uint32_t i8pair_h2(uint32_t xf, uint32_t sel) {
+    const uint32_t w = __byte_perm(xf, 0x64646464u, sel);
+    uint32_t h;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(h) : "r"(w), "r"(0x64806480u));
+    return h;
 }
 
 // One 16-token block: scores, online softmax update, P*V accumulate.
@@ -441,6 +477,117 @@ __device__ __forceinline__ void consume_block(uint32_t sK, uint32_t sV, int vali
     }
 }
 
+// The same for an INT8 block, read in place from the staged compact tiles
+// (codes at i8_offset, ldmatrix on pairs of codes, converted to exact fp16
+// in registers).  Keys: ldmatrix gives thread (g, c) codes 4c..4c+3 of a
+// 16-dim chunk of key rows g and g + 8, the A fragment of one k-step under
+// the dim permutation load_q_frags applies to q.  Values: ldmatrix .trans
+// gives it dims 2g, 2g+1 of keys 2c, 2c+1 (and 2c+8, 2c+9), the V^T A
+// fragment of one 16-dim output tile with rows g -> dim 2g, g + 8 -> dim
+// 2g + 1; o[mt] holds dims mt*16 + 2g (regs 0, 1) and mt*16 + 2g + 1 (regs
+// 2, 3).  Rows past `valid` are masked (their scores -inf, their V scale 0;
+// codes are finite, so their weight 0 contributes exactly 0).
+__device__ __forceinline__ void consume_block_i8(uint32_t sK, uint32_t sV, int valid, int lane,
+                                                 const uint32_t (&qh)[8][2], const uint32_t (&ql)[8][2],
+                                                 float (&m2)[2], float (&lsum)[2], float (&o)[8][4],
+                                                 const float (&ks)[2], const float (&vs)[2]) {
+    const int g = lane >> 2;
+    const int mi = lane >> 3, r = lane & 7;
+    const int t = (mi & 1) * 8 + r;  // key row this lane addresses for ldmatrix
+    // ---- S^T[16 keys][8 heads] = K[16][128] * Qs^T ----
+    float sa[2][4] = {}, sb[2][4] = {};
+    {
+        const uint32_t rowb = sK + (uint32_t)t * 128u;
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            const int chunk = 2 * p + (mi >> 1);
+            uint32_t r0, r1, r2, r3;  // keys g / g+8 of chunk 2p, then of chunk 2p+1
+            ldsm_x4(rowb + (uint32_t)(((chunk ^ t) & 7) << 4), r0, r1, r2, r3);
+            r0 ^= 0x80808080u;
+            r1 ^= 0x80808080u;
+            r2 ^= 0x80808080u;
+            r3 ^= 0x80808080u;
+            {
+                const uint32_t a0 = i8pair_h2(r0, 0x4140), a1 = i8pair_h2(r1, 0x4140);
+                const uint32_t a2 = i8pair_h2(r0, 0x4342), a3 = i8pair_h2(r1, 0x4342);
+                mma16816<0>(sa[0], a0, a1, a2, a3, qh[2 * p][0], qh[2 * p][1]);
+                mma16816<0>(sb[0], a0, a1, a2, a3, ql[2 * p][0], ql[2 * p][1]);
+            }
+            {
+                const uint32_t a0 = i8pair_h2(r2, 0x4140), a1 = i8pair_h2(r3, 0x4140);
+                const uint32_t a2 = i8pair_h2(r2, 0x4342), a3 = i8pair_h2(r3, 0x4342);
+                mma16816<0>(sa[1], a0, a1, a2, a3, qh[2 * p + 1][0], qh[2 * p + 1][1]);
+                mma16816<0>(sb[1], a0, a1, a2, a3, ql[2 * p + 1][0], ql[2 * p + 1][1]);
+            }
+        }
+    }
+    float s[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) s[e] = (sa[0][e] + sa[1][e]) + (sb[0][e] + sb[1][e]);
+    s[0] *= ks[0];
+    s[1] *= ks[0];
+    s[2] *= ks[1];
+    s[3] *= ks[1];
+    if (g >= valid) s[0] = s[1] = -INFINITY;
+    if (g + 8 >= valid) s[2] = s[3] = -INFINITY;
+    // ---- online softmax, per head column (2c, 2c+1) ----
+    float bm0 = fmaxf(s[0], s[2]), bm1 = fmaxf(s[1], s[3]);
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+        bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, off));
+        bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, off));
+    }
+    const float mn0 = fmaxf(m2[0], bm0), mn1 = fmaxf(m2[1], bm1);
+    const float mu0 = (mn0 == -INFINITY) ? 0.f : mn0;
+    const float mu1 = (mn1 == -INFINITY) ? 0.f : mn1;
+    const float al0 = fast_exp2(m2[0] - mu0), al1 = fast_exp2(m2[1] - mu1);
+    m2[0] = mn0;
+    m2[1] = mn1;
+    const float p0 = fast_exp2(s[0] - mu0), p1 = fast_exp2(s[1] - mu1);
+    const float p2 = fast_exp2(s[2] - mu0), p3 = fast_exp2(s[3] - mu1);
+    lsum[0] = lsum[0] * al0 + p0 + p2;
+    lsum[1] = lsum[1] * al1 + p1 + p3;
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+        o[mt][0] *= al0;
+        o[mt][1] *= al1;
+        o[mt][2] *= al0;
+        o[mt][3] *= al1;
+    }
+    // ---- P^T as B fragments (weights times the keys' V scales) ----
+    uint32_t h01, l01, h23, l23;
+    split_pair<0>(p0 * vs[0], p1 * vs[0], h01, l01);
+    split_pair<0>(p2 * vs[1], p3 * vs[1], h23, l23);
+    const uint32_t bh0 = movmatrix_t(h01), bh1 = movmatrix_t(h23);
+    const uint32_t bl0 = movmatrix_t(l01), bl1 = movmatrix_t(l23);
+    // ---- O^T[128 dims][8 heads] += V^T * P^T ----
+    {
+        const uint32_t rowb = sV + (uint32_t)t * 128u;
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            const int chunk = 2 * p + (mi >> 1);
+            uint32_t r0, r1, r2, r3;  // keys 2c.. / 8+2c.. of chunk 2p, then of chunk 2p+1
+            ldsm_x4_t(rowb + (uint32_t)(((chunk ^ t) & 7) << 4), r0, r1, r2, r3);
+            r0 ^= 0x80808080u;
+            r1 ^= 0x80808080u;
+            r2 ^= 0x80808080u;
+            r3 ^= 0x80808080u;
+            {
+                const uint32_t a0 = i8pair_h2(r0, 0x4240), a1 = i8pair_h2(r0, 0x4341);
+                const uint32_t a2 = i8pair_h2(r1, 0x4240), a3 = i8pair_h2(r1, 0x4341);
+                mma16816<0>(o[2 * p], a0, a1, a2, a3, bh0, bh1);
+                mma16816<0>(o[2 * p], a0, a1, a2, a3, bl0, bl1);
+            }
+            {
+                const uint32_t a0 = i8pair_h2(r2, 0x4240), a1 = i8pair_h2(r2, 0x4341);
+                const uint32_t a2 = i8pair_h2(r3, 0x4240), a3 = i8pair_h2(r3, 0x4341);
+                mma16816<0>(o[2 * p + 1], a0, a1, a2, a3, bh0, bh1);
+                mma16816<0>(o[2 * p + 1], a0, a1, a2, a3, bl0, bl1);
+            }
+        }
+    }
+}
+
 }  // namespace
 
 
@@ -474,6 +621,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         f1 = a.cta_f0[blockIdx.x + 1];
         if (f0 < 0 || f1 < f0 || f1 > a.total) f0 = f1 = 0;
     }
+    constexpr int kStages = StageCfg<DT>::stages;  // ring stages (one producer lane each)
+    constexpr unsigned kLaneMask = kStages >= 32 ? 0xffffffffu : ((1u << kStages) - 1u);
     const bool prod_lane = warp == kConsumerWarps && lane < kStages;
     const uint64_t policy = policy_evict_first();
     const long ntile_ids = (long)pv.num_blocks * kvh;
@@ -659,7 +808,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             long long since = clock64();
             for (;;) {
                 const bool has = live0 && !stopped && f - f0 < nf;
-                if (!__any_sync(0xffu, has)) break;
+                if (!__any_sync(kLaneMask, has)) break;
                 const bool ready = has && mbar_test_wait(&sm.empty[s], (rounds & 1) ^ 1);
                 if (ready) {
                     issue(s, f, cur);
@@ -675,7 +824,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                     flag_timeout(pv, sm, blockIdx.x, 0, (uint32_t)(f - f0));
                     stopped = true;
                 }
-                if (!__any_sync(0xffu, ready)) __nanosleep(32);
+                if (!__any_sync(kLaneMask, ready)) __nanosleep(32);
             }
             // Drain, on every path (also after a timeout or a rejected plan):
             // this lane's last issued stage must land before the CTA exits.
@@ -799,30 +948,15 @@ __global__ void __launch_bounds__(kThreads, 2)
             uint8_t* sK;
             uint8_t* sV;
             float ks[2] = {1.f, 1.f}, vs[2] = {1.f, 1.f};  // INT8: scales of token rows g, g + 8
+            sK = sm.stage[s];
+            sV = sm.stage[s] + TB;
             if (DT == 2) {
-                // Expand the compact tiles into this warp's 16-bit pair, keep
-                // the scales of rows g and g + 8, and free the stage at once.
-                sK = sm.scratch[warp];
-                sV = sK + kTileBytes;
-                const uint8_t* qK = sm.stage[s];
-                const uint8_t* qV = qK + TB;
-                __syncwarp();  // this warp's previous block has been read
-                expand_tile_i8(qK, sK, lane);
-                expand_tile_i8(qV, sV, lane);
-                const float* kss = reinterpret_cast<const float*>(qK + kBlockTokens * kHeadDim);
-                const float* vss = reinterpret_cast<const float*>(qV + kBlockTokens * kHeadDim);
+                const float* kss = reinterpret_cast<const float*>(sK + kBlockTokens * kHeadDim);
+                const float* vss = reinterpret_cast<const float*>(sV + kBlockTokens * kHeadDim);
                 ks[0] = kss[g];
                 ks[1] = kss[g + 8];
                 vs[0] = vss[g];
                 vs[1] = vss[g + 8];
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&sm.empty[s]);
-                    *reinterpret_cast<volatile int*>(&sm.cons_done[warp]) = (int)k + 1;
-                }
-            } else {
-                sK = sm.stage[s];
-                sV = sm.stage[s] + kTileBytes;
             }
             if (newblk) {
                 if (DT == 2) {
@@ -842,7 +976,8 @@ __global__ void __launch_bounds__(kThreads, 2)
                                       sK, sV, lane);
                 }
             }
-            if (valid < kBlockTokens) {
+            const bool zeroed = DT != 2 && valid < kBlockTokens;
+            if (zeroed) {
                 // Rows past the end may hold anything (stale tiles, inf):
                 // zero them in V so masked weights (exactly 0) stay 0.
                 for (int x = lane; x < (kBlockTokens - valid) * 16; x += 32) {
@@ -850,22 +985,25 @@ __global__ void __launch_bounds__(kThreads, 2)
                     *reinterpret_cast<uint4*>(sV + ((ch >> 3) * 16 + t) * 128 + (ch & 7) * 16) =
                         make_uint4(0u, 0u, 0u, 0u);
                 }
-                if (DT == 2) {  // and their scales (stale words may be inf or NaN)
-                    if (g >= valid) vs[0] = 0.f;
-                    if (g + 8 >= valid) vs[1] = 0.f;
-                }
+            }
+            if (DT == 2) {
+                // INT8 codes are finite: rows past the end only need a zero
+                // V scale (their stale scale words may be inf or NaN).
+                if (g >= valid) vs[0] = 0.f;
+                if (g + 8 >= valid) vs[1] = 0.f;
             }
             __syncwarp();
-            consume_block<DT>(smem_u32(sK), smem_u32(sV), valid, lane, qh, ql, m2, lsum, o, ks, vs);
-            if (DT != 2) {
-                // Generic-proxy writes to the tile must be ordered before the
-                // next bulk copy (async proxy) overwrites it.
-                if (valid < kBlockTokens || newblk) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&sm.empty[s]);
-                    *reinterpret_cast<volatile int*>(&sm.cons_done[warp]) = (int)k + 1;
-                }
+            if constexpr (DT == 2)
+                consume_block_i8(smem_u32(sK), smem_u32(sV), valid, lane, qh, ql, m2, lsum, o, ks, vs);
+            else
+                consume_block<DT>(smem_u32(sK), smem_u32(sV), valid, lane, qh, ql, m2, lsum, o, ks, vs);
+            // Generic-proxy writes to the tile must be ordered before the
+            // next bulk copy (async proxy) overwrites it.
+            if (zeroed || newblk) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&sm.empty[s]);
+                *reinterpret_cast<volatile int*>(&sm.cons_done[warp]) = (int)k + 1;
             }
         }
 
@@ -882,12 +1020,15 @@ __global__ void __launch_bounds__(kThreads, 2)
             sm.merge_l[warp][2 * c] = lsum[0];
             sm.merge_l[warp][2 * c + 1] = lsum[1];
         }
+        // Output dims of o[mt]'s rows g and g + 8: mt*16 + g and + 8 (16-bit
+        // caches), mt*16 + 2g and + 1 (INT8, consume_block_i8).
+        const int dr0 = DT == 2 ? 2 * g : g, dr1 = DT == 2 ? 2 * g + 1 : g + 8;
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) {
-            sm.merge_o[warp][2 * c][mt * 16 + g] = o[mt][0];
-            sm.merge_o[warp][2 * c + 1][mt * 16 + g] = o[mt][1];
-            sm.merge_o[warp][2 * c][mt * 16 + g + 8] = o[mt][2];
-            sm.merge_o[warp][2 * c + 1][mt * 16 + g + 8] = o[mt][3];
+            sm.merge_o[warp][2 * c][mt * 16 + dr0] = o[mt][0];
+            sm.merge_o[warp][2 * c + 1][mt * 16 + dr0] = o[mt][1];
+            sm.merge_o[warp][2 * c][mt * 16 + dr1] = o[mt][2];
+            sm.merge_o[warp][2 * c + 1][mt * 16 + dr1] = o[mt][3];
         }
         named_bar_sync(1, kConsumerWarps * 32);
 

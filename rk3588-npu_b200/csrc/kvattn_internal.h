@@ -14,7 +14,8 @@ constexpr int kHeadDim = 128;          // dims per head (the only supported valu
 constexpr int kBlockTokens = 16;       // token rows per block
 constexpr int kTileBytes = kBlockTokens * kHeadDim * 2;  // one (block, kv head) tile: 4 KiB
 // INT8 pools: a (block, kv head) tile is 16 rows x 128 int8 codes (row t at
-// byte 128 t, dim d at byte d) followed by the 16 rows' fp32 scales.
+// byte 128 t, its 16-byte chunks swizzled: i8_offset) followed by the 16
+// rows' fp32 scales.
 constexpr int kTileBytesI8 = kBlockTokens * kHeadDim + kBlockTokens * 4;  // 2112 bytes
 constexpr int kMaxGroup = 8;           // query heads per KV head handled by one MMA tile
 constexpr int kPartialFloats = kMaxGroup * (kHeadDim + 2);  // m[8], l[8], o[8][128]
@@ -27,6 +28,15 @@ constexpr int kMaxCtaItems = 64;       // pieces per decode CTA (the planner nev
 // one logical chunk land in 8 different bank groups.
 __host__ __device__ inline uint32_t tile_offset(int t, int d) {
     return (uint32_t)(((d >> 6) * 16 + t) * 128 + ((((d >> 3) & 7) ^ (t & 7)) << 4) + (d & 7) * 2);
+}
+
+// Byte offset of code (token t, dim d) inside an INT8 tile: 16 rows of 128
+// codes, the 16-byte chunk index inside a row XORed with (t & 7) so that one
+// logical chunk of eight consecutive tokens lies in eight different bank
+// groups (ldmatrix reads the codes in place); the 16 fp32 row scales follow
+// the codes (kBlockTokens * kHeadDim bytes in).
+__host__ __device__ inline uint32_t i8_offset(int t, int d) {
+    return (uint32_t)(t * kHeadDim + ((((d >> 4) ^ t) & 7) << 4) + (d & 15));
 }
 
 // A block-table entry to write before use: table[seq][idx] = block.

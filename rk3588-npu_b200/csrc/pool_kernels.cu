@@ -147,10 +147,10 @@ __global__ void append_chunk_i8_kernel(PoolView pv, int layer, const __grid_cons
         const size_t tb = tile_base(pv, layer, blk, h);
         uint8_t* kt = pv.k + tb;
         uint8_t* vt = pv.v + tb;
-        *reinterpret_cast<char2*>(kt + t * kHeadDim + i) = make_char2(kc[0], kc[1]);
-        *reinterpret_cast<char2*>(kt + t * kHeadDim + i + 64) = make_char2(kc[2], kc[3]);
-        *reinterpret_cast<char2*>(vt + t * kHeadDim + i) = make_char2(vc[0], vc[1]);
-        *reinterpret_cast<char2*>(vt + t * kHeadDim + i + 64) = make_char2(vc[2], vc[3]);
+        *reinterpret_cast<char2*>(kt + i8_offset(t, i)) = make_char2(kc[0], kc[1]);
+        *reinterpret_cast<char2*>(kt + i8_offset(t, i + 64)) = make_char2(kc[2], kc[3]);
+        *reinterpret_cast<char2*>(vt + i8_offset(t, i)) = make_char2(vc[0], vc[1]);
+        *reinterpret_cast<char2*>(vt + i8_offset(t, i + 64)) = make_char2(vc[2], vc[3]);
         if (lane == 0) {
             reinterpret_cast<float*>(kt + kBlockTokens * kHeadDim)[t] = ks;
             reinterpret_cast<float*>(vt + kBlockTokens * kHeadDim)[t] = vs;
@@ -177,7 +177,7 @@ __global__ void import_i8_kernel(PoolView pv, int layer, int seq, int pos0, int 
         const int t = p % kBlockTokens;
         uint8_t* tile = (isv ? pv.v : pv.k) + tile_base(pv, layer, blk, h);
         if (ch < 8) {
-            *reinterpret_cast<uint4*>(tile + t * kHeadDim + ch * 16) = (isv ? vc : kc)[((size_t)r * pv.kv_heads + h) * 8 + ch];
+            *reinterpret_cast<uint4*>(tile + i8_offset(t, ch * 16)) = (isv ? vc : kc)[((size_t)r * pv.kv_heads + h) * 8 + ch];
         } else {
             reinterpret_cast<float*>(tile + kBlockTokens * kHeadDim)[t] = (isv ? vs : ks)[(size_t)r * pv.kv_heads + h];
         }
@@ -199,7 +199,7 @@ __global__ void gather_i8_kernel(PoolView pv, int layer, int seq, int len, uint4
         const int t = p % kBlockTokens;
         const uint8_t* tile = (isv ? pv.v : pv.k) + tile_base(pv, layer, blk, h);
         if (ch < 8) {
-            (isv ? vc : kc)[((size_t)p * pv.kv_heads + h) * 8 + ch] = *reinterpret_cast<const uint4*>(tile + t * kHeadDim + ch * 16);
+            (isv ? vc : kc)[((size_t)p * pv.kv_heads + h) * 8 + ch] = *reinterpret_cast<const uint4*>(tile + i8_offset(t, ch * 16));
         } else {
             (isv ? vs : ks)[(size_t)p * pv.kv_heads + h] = reinterpret_cast<const float*>(tile + kBlockTokens * kHeadDim)[t];
         }

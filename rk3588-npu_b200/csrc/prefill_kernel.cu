@@ -201,7 +201,7 @@ __global__ void __launch_bounds__(9 * 32, 1)
             if (!dead) {
                 for (int x = g * 32 + lane; x < 2 * kBlockTokens * 16; x += G * 32) {
                     const int which = x >> 8, y = x & 255, tt = y >> 4, ch = y & 15;
-                    const uint2 raw = *reinterpret_cast<const uint2*>(cK + which * TB + tt * kHeadDim + ch * 8);
+                    const uint2 raw = *reinterpret_cast<const uint2*>(cK + which * TB + i8_offset(tt, ch * 8));
                     const int8_t* cc = reinterpret_cast<const int8_t*>(&raw);
                     *reinterpret_cast<uint4*>(wK + which * kTileBytes + tile_offset(tt, ch * 8)) =
                         make_uint4(codes_to_half2(cc[0], cc[1]), codes_to_half2(cc[2], cc[3]),
