@@ -143,9 +143,9 @@ def parse_args():
                     choices=["batch32", "paged28", "paged1", "long1", "long4", "serve", "prefill", "model1",
                              "model_batch"],
                     default="batch32")
-    ap.add_argument("--transport", choices=["nccl", "p2p"], default="nccl",
-                    help="long workloads: merge of the per-GPU states by NCCL all-gather + combine "
-                         "launch, or by the fused peer-memory exchange kernel")
+    ap.add_argument("--transport", choices=["nccl", "p2p"], default="p2p",
+                    help="long workloads: merge of the per-GPU states by the fused peer-memory exchange "
+                         "kernel (p2p), or by NCCL all-gather + merge launch (nccl)")
     ap.add_argument("--prefill-kernel", choices=["tc", "tc1", "mma"], default="tc",
                     help="prefill workload: the tcgen05 kernel over all requests per launch "
                          "(kv_append_chunk_batch + attn_prefill_batch), the tcgen05 kernel one request per "
@@ -710,14 +710,44 @@ def run_long(args, rank, world, local):
     torch.cuda.set_stream(torch.cuda.Stream())
     P.set_overlap(True)
 
+    # The step through the C ABI with pointers built once (what a C++ worker
+    # does; the SplitKV methods cost more host time per layer than a layer
+    # of a 1/8 slice takes on the GPU).  Same calls as S.begin_step /
+    # S.layer / S.end_step.
+    L = kv._lib
+    h = P.h
+    st = torch.cuda.current_stream().cuda_stream
+    ids_c = kv._ints(S.ids)
+    app_c = kv._ints([1 if S.is_last else 0] * B)
+
+    def chk(rc, fn):
+        if rc != 0:
+            raise kv.KVError(rc, fn, L.kv_last_error().decode())
+
+    in_ptr = [[(q[j, y].data_ptr(), kn[j, y].data_ptr(), vn[j, y].data_ptr()) for y in range(NL)]
+              for j in range(R)]
+    out_ptr = [out[y].data_ptr() for y in range(NL)]
+    if world == 1:
+        def layer_call(y, qa, ka, va):
+            chk(L.attn_decode_append(h, y, qa, ka, va, out_ptr[y], st), "attn_decode_append")
+    elif S._x is not None:
+        def layer_call(y, qa, ka, va):
+            chk(L.attn_decode_append_xgpu(h, y, qa, ka, va, out_ptr[y], S._x, st), "attn_decode_append_xgpu")
+    else:
+        def layer_call(y, qa, ka, va):
+            chk(L.attn_decode_append_nccl(h, y, qa, ka, va, out_ptr[y], S._n, st), "attn_decode_append_nccl")
+
     def step(i, qs=None, ks=None, vs=None):
-        qs = q[i % R] if qs is None else qs
-        ks = kn[i % R] if ks is None else ks
-        vs = vn[i % R] if vs is None else vs
-        S.begin_step()
+        if qs is not None:  # e2e: this step's inputs were just copied in
+            ptrs = [(qs[y].data_ptr(), ks[y].data_ptr(), vs[y].data_ptr()) for y in range(NL)]
+        else:
+            ptrs = in_ptr[i % R]
+        chk(L.attn_decode_plan_ex(h, B, ids_c, kv._ints(S.lengths), app_c, st), "attn_decode_plan_ex")
         for y in range(NL):
-            S.layer(y, qs[y], ks[y], vs[y], out[y])
-        S.end_step()
+            qa, ka, va = ptrs[y]
+            layer_call(y, qa, ka, va)
+        chk(L.attn_decode_commit(h), "attn_decode_commit")
+        S.lengths = [n + 1 for n in S.lengths]
 
     sampler = ClockSampler(range(local, local + 1)) if rank == 0 else None
     if sampler:

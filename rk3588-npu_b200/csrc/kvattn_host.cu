@@ -1353,6 +1353,16 @@ static int decode_call(kvp_pool* p, int layer, const float* q, const float* k_ne
         ca.row0 = sp.row0;
         ca.pad[0] = ca.pad[1] = 0;
         for (size_t i = 0; i < sp.comb.size(); ++i) ca.seg[i] = sp.comb[i];
+        if (x && p->subs.size() == 1 && ca.nsegs > 0 && ca.nsegs <= kMaxXchgSplit) {
+            // The exchange kernel merges the split segments itself (one
+            // launch fewer per layer): hand it the pieces, skip the merge.
+            xa.partials = p->pv.partials;
+            xa.nsplit = ca.nsegs;
+            xa.q_heads = p->q_heads;
+            xa.group = p->q_heads / p->kv_heads;
+            for (int i = 0; i < ca.nsegs; ++i) xa.seg[i] = ca.seg[i];
+            ca.nsegs = 0;
+        }
         if (sp.nslots <= kSlotsSmall && (int)sp.seg.size() <= kSegsPerSlot * kSlotsSmall) {
             DecodeArgs<kSlotsSmall> a;
             fill_args(p, sp, layer, flags, a);

@@ -200,12 +200,20 @@ cudaError_t launch_combine(int G, int rows, int dim, const float* m, const float
 // Layer call e uses inbox buffer e & 1.
 constexpr int kMaxRanks = 8;
 
+constexpr int kMaxXchgSplit = 64;  // split segments whose merge the exchange kernel takes over
 struct XchgArgs {
     float* base[kMaxRanks];  // every rank's area (this rank's is local)
     int world, me, rows, max_rows;
     unsigned epoch;          // >= 1, one more per layer call
     float* out;              // [rows][128]
     int* status;             // the pool's status words
+    // nsplit > 0: the decode launch's split segments (CombineArgs::seg
+    // layout, slot = plan row of the only launch) are merged here from
+    // `partials`, in place of a merge launch; their rows of the local slot
+    // are not written.
+    const float* partials;
+    int nsplit, q_heads, group, pad;
+    int2 seg[kMaxXchgSplit];
 };
 
 __host__ __device__ inline size_t xchg_local_floats(int max_rows) { return (size_t)max_rows * (2 + kHeadDim); }

@@ -73,8 +73,18 @@ __device__ __forceinline__ bool wait_word(const uint2* p, unsigned epoch, float&
     return true;
 }
 
-// One CTA per (sequence, query head) row, one thread per dim.
-__global__ void __launch_bounds__(kHeadDim) xchg_kernel(const __grid_constant__ XchgArgs a) {
+constexpr int kXchgWarps = 16;  // warps of a row's CTA (the first 4 run the exchange)
+
+// One CTA per (sequence, query head) row.  Its local state is either this
+// rank's slot (written by the decode launch) or, for a row of a split
+// segment (nsplit > 0), the merge of the segment's pieces: warp w takes
+// pieces w, w + 16, ... eight at a time (lane l holds dims 4l..4l+3), online
+// log-sum-exp in base 2 as the decode kernel keeps it, then the 16 warps
+// merge in shared memory.  Then thread d < 128 (one per dim) exchanges and
+// merges across ranks.
+__global__ void __launch_bounds__(kXchgWarps * 32) xchg_kernel(const __grid_constant__ XchgArgs a) {
+    __shared__ float s_m[kXchgWarps], s_l[kXchgWarps];
+    __shared__ __align__(16) float s_o[kXchgWarps][kHeadDim];
     // The next layer's decode launch may start now (it writes nothing before
     // this kernel completes, and its early tile copies read another layer):
     // it overlaps the wait for the peers.  The local states come from the
@@ -84,12 +94,88 @@ __global__ void __launch_bounds__(kHeadDim) xchg_kernel(const __grid_constant__ 
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int r = blockIdx.x, d = threadIdx.x;
     if (r >= a.rows) return;
-    const int buf = (int)(a.epoch & 1u);
     const int W = a.world, R = a.max_rows;
     const float* mine = a.base[a.me];
-    const float m0 = __ldcg(mine + r);
-    const float l0 = __ldcg(mine + R + r);
-    const float o0 = __ldcg(mine + 2 * R + (size_t)r * kHeadDim + d);
+    // ---- this rank's state of row r ----
+    int first = 0, np = 0;
+    if (a.nsplit > 0 && a.q_heads > 0 && a.group > 0) {
+        const int key = (r / a.q_heads) | (((r % a.q_heads) / a.group) << 16);
+        for (int k = 0; k < a.nsplit && k < kMaxXchgSplit; ++k)
+            if (a.seg[k].x == key) {
+                first = a.seg[k].y & 0xffff;
+                np = a.seg[k].y >> 16;
+                break;
+            }
+        if (np > 0 && (first >> 1) + np > kMaxGrid) {  // never read past the partials
+            if (d == 0 && atomicCAS(a.status, 0, 5 /* KV_ERR_RANGE */) == 0) {
+                a.status[1] = r;
+                a.status[2] = 510;
+            }
+            np = 0;
+        }
+    }
+    float m0, l0, o0;
+    if (np > 0) {
+        const int warp = d >> 5, lane = d & 31, h = r % a.group, g0 = first >> 1;
+        float M = -INFINITY, L = 0.f;
+        float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int c0 = warp; c0 < np; c0 += 8 * kXchgWarps) {
+            float mm[8], ll[8];
+            float4 oo[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int pc = c0 + u * kXchgWarps;
+                const bool live = pc < np;
+                const int pidx = pc == 0 ? first : 2 * (g0 + pc);
+                const float* pp = a.partials + (size_t)(live ? pidx : 0) * kPartialFloats;
+                mm[u] = live ? __ldcg(pp + h) : 0.f;
+                ll[u] = live ? __ldcg(pp + kMaxGroup + h) : 0.f;
+                oo[u] = live ? __ldcg(reinterpret_cast<const float4*>(pp + 2 * kMaxGroup + h * kHeadDim) + lane)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                if (!(ll[u] > 0.f)) continue;  // empty piece (or past the end): no weight
+                const float Mn = fmaxf(M, mm[u]);
+                const float sa = exp2f(M - Mn);  // 0 while M is -inf
+                const float e = ll[u] * exp2f(mm[u] - Mn);
+                A.x = A.x * sa + e * oo[u].x;
+                A.y = A.y * sa + e * oo[u].y;
+                A.z = A.z * sa + e * oo[u].z;
+                A.w = A.w * sa + e * oo[u].w;
+                L = L * sa + e;
+                M = Mn;
+            }
+        }
+        if (lane == 0) {
+            s_m[warp] = M;
+            s_l[warp] = L;
+        }
+        reinterpret_cast<float4*>(s_o[warp])[lane] = A;
+        __syncthreads();
+        if (d >= kHeadDim) return;
+        float Mt = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kXchgWarps; ++w)
+            if (s_l[w] > 0.f) Mt = fmaxf(Mt, s_m[w]);
+        float Lt = 0.f, At = 0.f;
+#pragma unroll
+        for (int w = 0; w < kXchgWarps; ++w) {
+            if (!(s_l[w] > 0.f)) continue;
+            const float f = exp2f(s_m[w] - Mt);
+            Lt += s_l[w] * f;
+            At += s_o[w][d] * f;
+        }
+        m0 = Mt * 0.6931471805599453f;  // natural-log units, as the decode writes the slot
+        l0 = Lt;
+        o0 = Lt > 0.f ? At / Lt : 0.f;
+    } else {
+        if (d >= kHeadDim) return;
+        m0 = __ldcg(mine + r);
+        l0 = __ldcg(mine + R + r);
+        o0 = __ldcg(mine + 2 * R + (size_t)r * kHeadDim + d);
+    }
+    const int buf = (int)(a.epoch & 1u);
     for (int g = 0; g < W; ++g) {
         if (g == a.me) continue;
         uint2* w = xchg_inbox(a.base[g], W, R, buf, a.me) + (size_t)r * (2 + kHeadDim);
@@ -150,7 +236,7 @@ cudaError_t launch_xchg(const XchgArgs& a, cudaStream_t st) {
     if (a.rows <= 0) return cudaSuccess;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)a.rows);
-    cfg.blockDim = dim3(kHeadDim);
+    cfg.blockDim = dim3(a.nsplit > 0 ? kXchgWarps * 32 : kHeadDim);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
