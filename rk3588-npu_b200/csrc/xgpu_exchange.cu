@@ -12,8 +12,9 @@
 // Per row, thread d (one per dim) writes this rank's value of dim d into
 // every peer's inbox as one 64-bit word {value, epoch of this layer call}
 // with one store over NVLink (the areas are mapped with CUDA IPC); two
-// more words carry m and l.  Readers poll the words of their own inbox until
-// every word carries the current epoch -- a scalar 64-bit access is seen
+// more words carry m and l.  Readers poll the words of their own inbox (all
+// peers' words loaded together in each sweep) until every word carries the
+// current epoch -- a scalar 64-bit access is seen
 // whole, so the value beside a current epoch is current -- and merge.  No fence, flag
 // or barrier sits on the path (the low-latency protocol NCCL calls LL).  No
 // multicast and no bulk copies touch peer memory.
@@ -57,20 +58,6 @@ __device__ __forceinline__ uint2 ld_word(const uint2* p) {
     unsigned long long w;
     asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
     return make_uint2((unsigned)w, (unsigned)(w >> 32));
-}
-
-// Poll one inbox word until it carries `epoch` (bounded); false on timeout.
-__device__ __forceinline__ bool wait_word(const uint2* p, unsigned epoch, float& v) {
-    uint2 w = ld_word(p);
-    if (w.y != epoch) {
-        const long long t0 = clock64();
-        do {
-            if (clock64() - t0 > kXchgWaitLimit) return false;
-            w = ld_word(p);
-        } while (w.y != epoch);
-    }
-    v = __uint_as_float(w.x);
-    return true;
 }
 
 constexpr int kXchgWarps = 16;  // warps of a row's CTA (the first 4 run the exchange)
@@ -183,30 +170,57 @@ __global__ void __launch_bounds__(kXchgWarps * 32) xchg_kernel(const __grid_cons
         if (d == 0) st_word(w, m0, a.epoch);
         if (d == 1) st_word(w + 1, l0, a.epoch);
     }
-    // Merge in rank order (the same arithmetic on every rank), each state
-    // read as it arrives; this rank's own comes from its local area.
-    float M = -INFINITY, L = 0.f, A = 0.f;
+    // Collect every peer's state: each sweep issues the loads of all words
+    // still missing (one round trip for all peers, not one per peer and
+    // word), then keeps those that carry this call's epoch; bounded.
+    float mg[kMaxRanks], lg[kMaxRanks], og[kMaxRanks];
+    unsigned need = 0;
+    for (int g = 0; g < W; ++g)
+        if (g != a.me) need |= 1u << g;
     bool ok = true;
-    for (int g = 0; g < W; ++g) {
-        float mg = m0, lg = l0, og = o0;
-        if (g != a.me) {
+    const long long t0 = clock64();
+    while (need) {
+        uint2 wm[kMaxRanks], wl[kMaxRanks], wo[kMaxRanks];
+#pragma unroll
+        for (int g = 0; g < kMaxRanks; ++g) {
+            if (!((need >> g) & 1u)) continue;
             const uint2* w = xchg_inbox(a.base[a.me], W, R, buf, g) + (size_t)r * (2 + kHeadDim);
-            ok = wait_word(w, a.epoch, mg) && wait_word(w + 1, a.epoch, lg) &&
-                 wait_word(w + 2 + d, a.epoch, og);
-            if (!ok) {
-                if (atomicCAS(a.status, 0, KV_ERR_TIMEOUT) == 0) {
-                    a.status[1] = r;
-                    a.status[2] = 500 + g;
-                    a.status[3] = (int)a.epoch;
-                }
-                break;
+            wm[g] = ld_word(w);
+            wl[g] = ld_word(w + 1);
+            wo[g] = ld_word(w + 2 + d);
+        }
+#pragma unroll
+        for (int g = 0; g < kMaxRanks; ++g) {
+            if (!((need >> g) & 1u)) continue;
+            if (wm[g].y == a.epoch && wl[g].y == a.epoch && wo[g].y == a.epoch) {
+                mg[g] = __uint_as_float(wm[g].x);
+                lg[g] = __uint_as_float(wl[g].x);
+                og[g] = __uint_as_float(wo[g].x);
+                need &= ~(1u << g);
             }
         }
-        if (!(lg > 0.f)) continue;  // an empty slice: no weight
-        const float Mn = fmaxf(M, mg);
+        if (need && clock64() - t0 > kXchgWaitLimit) {
+            ok = false;
+            if (atomicCAS(a.status, 0, KV_ERR_TIMEOUT) == 0) {
+                a.status[1] = r;
+                a.status[2] = 500 + (__ffs(need) - 1);
+                a.status[3] = (int)a.epoch;
+            }
+            break;
+        }
+    }
+    // Merge in rank order (the same arithmetic on every rank); this rank's
+    // own state comes from its local area.
+    float M = -INFINITY, L = 0.f, A = 0.f;
+#pragma unroll
+    for (int g = 0; g < kMaxRanks; ++g) {
+        if (!ok || g >= W) continue;
+        const float m = g == a.me ? m0 : mg[g], l = g == a.me ? l0 : lg[g], o = g == a.me ? o0 : og[g];
+        if (!(l > 0.f)) continue;  // an empty slice: no weight
+        const float Mn = fmaxf(M, m);
         const float sa = expf(M - Mn);  // 0 while M is -inf
-        const float e = lg * expf(mg - Mn);
-        A = A * sa + e * og;
+        const float e = l * expf(m - Mn);
+        A = A * sa + e * o;
         L = L * sa + e;
         M = Mn;
     }
