@@ -67,11 +67,13 @@ def test_int8_append_chunk_bit_exact(kv, orc):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("merge", ["grid", "cluster"])
 @pytest.mark.parametrize("lens,layers,seed", [([0, 1, 15, 16, 17, 33, 300, 1000], 2, 2), ([5000, 40, 2100], 1, 3)])
-def test_int8_decode_matches_oracle(kv, orc, lens, layers, seed):
+def test_int8_decode_matches_oracle(kv, orc, lens, layers, seed, merge):
     """Context imported as codes + scales, then three decode steps (fused
-    RoPE + INT8 append + attention) on a batch with ragged lengths; the long
-    case is cut into pieces merged by the combine kernel."""
+    RoPE + INT8 append + attention) on a batch with ragged lengths; split
+    heads merged by the merge launch, or inside 8-CTA clusters where the
+    planner can keep them there (the first case)."""
     need_gpu()
     qh, kvh = 12, 2
     kvd, hid = kvh * HD, qh * HD
@@ -80,6 +82,7 @@ def test_int8_decode_matches_oracle(kv, orc, lens, layers, seed):
     nb = sum(-(-(L + steps) // 16) for L in lens) + 8
     P = kv.Pool(0, layers, nb, num_q_heads=qh, num_kv_heads=kvh, dtype=kv.KV_I8, max_seqs=len(lens),
                 max_seq_len=max(lens) + 64)
+    P.set_merge_mode(kv.KVP_MERGE_CLUSTER if merge == "cluster" else kv.KVP_MERGE_GRID)
     ids, caches = [], []
     for L in lens:
         s = P.seq_alloc()
@@ -102,8 +105,10 @@ def test_int8_decode_matches_oracle(kv, orc, lens, layers, seed):
         ids.append(s)
         caches.append(per_layer)
     worst = 0.0
+    clustered = 0
     for step in range(steps):
         P.plan(ids)
+        clustered += P.plan_clusters()[0]
         for y in range(layers):
             q = rng.standard_normal((len(lens), hid)).astype(np.float32)
             k = rng.standard_normal((len(lens), kvd)).astype(np.float32)
@@ -117,6 +122,10 @@ def test_int8_decode_matches_oracle(kv, orc, lens, layers, seed):
                 worst = max(worst, rel_err(got[i], ref))
         P.commit()
     assert worst <= TOL, worst
+    if merge == "grid":
+        assert clustered == 0
+    elif seed == 2:  # short contexts: the planner keeps every split inside one cluster
+        assert clustered == steps
     for i, L in enumerate(lens):
         for y in range(layers):
             kc, vc, ks, vs = [t.cpu().numpy() for t in P.gather_i8(y, ids[i])]
