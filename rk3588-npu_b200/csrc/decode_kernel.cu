@@ -116,6 +116,10 @@ struct Smem {
     float merge_o[kConsumerWarps][kMaxGroup][kMergeStride];
     float merge_m[kConsumerWarps][kMaxGroup];
     float merge_l[kConsumerWarps][kMaxGroup];
+    float merge_w[kMaxGroup][kConsumerWarps];  // weight 2^(m_w - M) of warp w's state, per head
+    float merge_inv[kMaxGroup];                // 1 / L per head (0 for an empty head)
+    float merge_M[kMaxGroup];
+    float merge_L[kMaxGroup];
     // States of the first and last piece when they are split inside a
     // cluster: m[8], l[8], o[8][128] (the layout of a partials row).
     alignas(16) float cpart[2][kPartialFloats];
@@ -123,7 +127,11 @@ struct Smem {
     int cum[kMaxCtaItems + 1];        // flat block offset of each piece
     int ok[kMaxCtaItems];             // piece's slot passed the checks
     // q fragments (hi, lo) of the first kQPre pieces, as each lane holds them
-    uint32_t qfrag[kQPre][2][8][2][32];
+    // q fragments (hi, lo) of the pieces in flight, slot j % kQPre for piece
+    // j: [hi/lo][k-step][lane] = the lane's two registers of that k-step.
+    // The consumers read them per block from here rather than holding 32
+    // registers across the block loop.
+    uint2 qfrag[kQPre][2][8][32];
     uint64_t full[kS];
     uint64_t empty[kS];
     int nitems;
@@ -397,8 +405,7 @@ __device__ __forceinline__ uint32_t i8pair_h2(uint32_t xf, uint32_t sel) {
 // weights), which is attention over code * scale exactly up to fp32 rounding.
 template <int DT>
 __device__ __forceinline__ void consume_block(uint32_t sK, uint32_t sV, int valid, int lane,
-                                              const uint32_t (&qh)[8][2],
-                                              const uint32_t (&ql)[8][2], float (&m2)[2],
+                                              const uint2* qf, float (&m2)[2],
                                               float (&lsum)[2], float (&o)[8][4], const float (&ks)[2],
                                               const float (&vs_in)[2]) {
     const float vs[2] = {DT == 2 ? vs_in[0] : 1.f, DT == 2 ? vs_in[1] : 1.f};
@@ -416,8 +423,9 @@ __device__ __forceinline__ void consume_block(uint32_t sK, uint32_t sV, int vali
             const uint32_t addr = rowb + (uint32_t)(cidx >> 3) * 2048u + (uint32_t)(((cidx & 7) ^ r) << 4);
             uint32_t a0, a1, a2, a3;
             ldsm_x4(addr, a0, a1, a2, a3);
-            mma16816<mma_type<DT>()>(sa[kk & 1], a0, a1, a2, a3, qh[kk][0], qh[kk][1]);
-            mma16816<mma_type<DT>()>(sb[kk & 1], a0, a1, a2, a3, ql[kk][0], ql[kk][1]);
+            const uint2 qh = qf[kk * 32], ql = qf[256 + kk * 32];
+            mma16816<mma_type<DT>()>(sa[kk & 1], a0, a1, a2, a3, qh.x, qh.y);
+            mma16816<mma_type<DT>()>(sb[kk & 1], a0, a1, a2, a3, ql.x, ql.y);
         }
     }
     float s[4];
@@ -488,7 +496,7 @@ __device__ __forceinline__ void consume_block(uint32_t sK, uint32_t sV, int vali
 // 2, 3).  Rows past `valid` are masked (their scores -inf, their V scale 0;
 // codes are finite, so their weight 0 contributes exactly 0).
 __device__ __forceinline__ void consume_block_i8(uint32_t sK, uint32_t sV, int valid, int lane,
-                                                 const uint32_t (&qh)[8][2], const uint32_t (&ql)[8][2],
+                                                 const uint2* qf,
                                                  float (&m2)[2], float (&lsum)[2], float (&o)[8][4],
                                                  const float (&ks)[2], const float (&vs)[2]) {
     const int g = lane >> 2;
@@ -510,14 +518,16 @@ __device__ __forceinline__ void consume_block_i8(uint32_t sK, uint32_t sV, int v
             {
                 const uint32_t a0 = i8pair_h2(r0, 0x4140), a1 = i8pair_h2(r1, 0x4140);
                 const uint32_t a2 = i8pair_h2(r0, 0x4342), a3 = i8pair_h2(r1, 0x4342);
-                mma16816<0>(sa[0], a0, a1, a2, a3, qh[2 * p][0], qh[2 * p][1]);
-                mma16816<0>(sb[0], a0, a1, a2, a3, ql[2 * p][0], ql[2 * p][1]);
+                const uint2 qh = qf[(2 * p) * 32], ql = qf[256 + (2 * p) * 32];
+                mma16816<0>(sa[0], a0, a1, a2, a3, qh.x, qh.y);
+                mma16816<0>(sb[0], a0, a1, a2, a3, ql.x, ql.y);
             }
             {
                 const uint32_t a0 = i8pair_h2(r2, 0x4140), a1 = i8pair_h2(r3, 0x4140);
                 const uint32_t a2 = i8pair_h2(r2, 0x4342), a3 = i8pair_h2(r3, 0x4342);
-                mma16816<0>(sa[1], a0, a1, a2, a3, qh[2 * p + 1][0], qh[2 * p + 1][1]);
-                mma16816<0>(sb[1], a0, a1, a2, a3, ql[2 * p + 1][0], ql[2 * p + 1][1]);
+                const uint2 qh = qf[(2 * p + 1) * 32], ql = qf[256 + (2 * p + 1) * 32];
+                mma16816<0>(sa[1], a0, a1, a2, a3, qh.x, qh.y);
+                mma16816<0>(sb[1], a0, a1, a2, a3, ql.x, ql.y);
             }
         }
     }
@@ -878,12 +888,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         uint32_t qh[8][2], ql[8][2];
         load_q_frags<DT>(pv, q, a.row0 + w.slot, w.head, a.slot[w.slot].rope_pos, qscale, lane, qh, ql);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-#pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                sm.qfrag[warp][0][kk][r][lane] = qh[kk][r];
-                sm.qfrag[warp][1][kk][r][lane] = ql[kk][r];
-            }
+        for (int kk = 0; kk < 8; ++kk) {
+            sm.qfrag[warp][0][kk][lane] = make_uint2(qh[kk][0], qh[kk][1]);
+            sm.qfrag[warp][1][kk][lane] = make_uint2(ql[kk][0], ql[kk][1]);
+        }
     }
     named_bar_sync(1, kConsumerWarps * 32);
     bool dead = false;
@@ -916,18 +924,22 @@ __global__ void __launch_bounds__(kThreads, 2)
         const bool append = sl.new_block >= 0;
         const int last_blk = (sl.kv_len - 1) / kBlockTokens;
 
-        uint32_t qh[8][2], ql[8][2];
-        if (j < kQPre) {
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-#pragma unroll
-                for (int r = 0; r < 2; ++r) {
-                    qh[kk][r] = sm.qfrag[j][0][kk][r][lane];
-                    ql[kk][r] = sm.qfrag[j][1][kk][r][lane];
-                }
-        } else {
+        // Piece j's q fragments: prepared up front for j < kQPre, else now
+        // into slot j % kQPre (piece j - kQPre has been merged by every warp:
+        // the merge barriers of the pieces in between have passed).  Every
+        // warp writes the same values and reads back only its own lanes'.
+        const int qslot = j % kQPre;
+        if (j >= kQPre) {
+            uint32_t qh[8][2], ql[8][2];
             load_q_frags<DT>(pv, q, row, wi.head, sl.rope_pos, qscale, lane, qh, ql);
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                sm.qfrag[qslot][0][kk][lane] = make_uint2(qh[kk][0], qh[kk][1]);
+                sm.qfrag[qslot][1][kk][lane] = make_uint2(ql[kk][0], ql[kk][1]);
+            }
+            __syncwarp();
         }
+        const uint2* qf = &sm.qfrag[qslot][0][0][lane];
         float m2[2] = {-INFINITY, -INFINITY}, lsum[2] = {0.f, 0.f};
         float o[8][4];
 #pragma unroll
@@ -994,9 +1006,9 @@ __global__ void __launch_bounds__(kThreads, 2)
             }
             __syncwarp();
             if constexpr (DT == 2)
-                consume_block_i8(smem_u32(sK), smem_u32(sV), valid, lane, qh, ql, m2, lsum, o, ks, vs);
+                consume_block_i8(smem_u32(sK), smem_u32(sV), valid, lane, qf, m2, lsum, o, ks, vs);
             else
-                consume_block<DT>(smem_u32(sK), smem_u32(sV), valid, lane, qh, ql, m2, lsum, o, ks, vs);
+                consume_block<DT>(smem_u32(sK), smem_u32(sV), valid, lane, qf, m2, lsum, o, ks, vs);
             // Generic-proxy writes to the tile must be ordered before the
             // next bulk copy (async proxy) overwrites it.
             if (zeroed || newblk) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -1031,23 +1043,39 @@ __global__ void __launch_bounds__(kThreads, 2)
             sm.merge_o[warp][2 * c + 1][mt * 16 + dr1] = o[mt][3];
         }
         named_bar_sync(1, kConsumerWarps * 32);
+        // The merge weights once per (head, warp) -- thread 4h + w of warp 0
+        // -- instead of by every output dim: M, 2^(m_w - M), L and 1 / L.
+        static_assert(kConsumerWarps == 4 && kMaxGroup * kConsumerWarps <= 32, "one warp computes the weights");
+        if (tid < pv.group * kConsumerWarps) {
+            const int h = tid >> 2, w = tid & 3;
+            const unsigned mask = pv.group * kConsumerWarps >= 32 ? 0xffffffffu
+                                                                  : ((1u << (pv.group * kConsumerWarps)) - 1u);
+            float M = -INFINITY;
+#pragma unroll
+            for (int x = 0; x < kConsumerWarps; ++x) M = fmaxf(M, sm.merge_m[x][h]);
+            const float Mu = (M == -INFINITY) ? 0.f : M;
+            const float e = fast_exp2(sm.merge_m[w][h] - Mu);
+            sm.merge_w[h][w] = e;
+            float L = sm.merge_l[w][h] * e;
+            L += __shfl_xor_sync(mask, L, 1);
+            L += __shfl_xor_sync(mask, L, 2);
+            if (w == 0) {
+                sm.merge_inv[h] = L > 0.f ? __frcp_rn(L) : 0.f;
+                sm.merge_M[h] = M;
+                sm.merge_L[h] = L;
+            }
+        }
+        named_bar_sync(1, kConsumerWarps * 32);
 
         const int d = tid;  // 0..127: one output dim per thread
         const int qrow = row * pv.q_heads + wi.head * pv.group;
         float* part = wi.split == 2 ? sm.cpart[wi.part] : pv.partials + (size_t)wi.part * kPartialFloats;
         for (int h = 0; h < pv.group; ++h) {
-            float M = -INFINITY;
+            float O = 0.f;
 #pragma unroll
-            for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm.merge_m[w][h]);
-            const float Mu = (M == -INFINITY) ? 0.f : M;
-            float L = 0.f, O = 0.f;
-#pragma unroll
-            for (int w = 0; w < kConsumerWarps; ++w) {
-                const float e = fast_exp2(sm.merge_m[w][h] - Mu);
-                L += sm.merge_l[w][h] * e;
-                O += sm.merge_o[w][h][d] * e;
-            }
-            const float on = L > 0.f ? O / L : 0.f;
+            for (int w = 0; w < kConsumerWarps; ++w) O += sm.merge_o[w][h][d] * sm.merge_w[h][w];
+            const float on = O * sm.merge_inv[h];
+            const float M = sm.merge_M[h], L = sm.merge_L[h];
             if (!wi.split) {
                 out[(size_t)(qrow + h) * kHeadDim + d] = on;
                 if (m_out != nullptr && d == 0) {
