@@ -495,6 +495,7 @@ __device__ __forceinline__ void consume_block(uint32_t sK, uint32_t sV, int vali
 // 2g + 1; o[mt] holds dims mt*16 + 2g (regs 0, 1) and mt*16 + 2g + 1 (regs
 // 2, 3).  Rows past `valid` are masked (their scores -inf, their V scale 0;
 // codes are finite, so their weight 0 contributes exactly 0).
+template <int QS, int QLO>
 __device__ __forceinline__ void consume_block_i8(uint32_t sK, uint32_t sV, int valid, int lane,
                                                  const uint2* qf,
                                                  float (&m2)[2], float (&lsum)[2], float (&o)[8][4],
@@ -518,14 +519,14 @@ __device__ __forceinline__ void consume_block_i8(uint32_t sK, uint32_t sV, int v
             {
                 const uint32_t a0 = i8pair_h2(r0, 0x4140), a1 = i8pair_h2(r1, 0x4140);
                 const uint32_t a2 = i8pair_h2(r0, 0x4342), a3 = i8pair_h2(r1, 0x4342);
-                const uint2 qh = qf[(2 * p) * 32], ql = qf[256 + (2 * p) * 32];
+                const uint2 qh = qf[(2 * p) * QS], ql = qf[QLO + (2 * p) * QS];
                 mma16816<0>(sa[0], a0, a1, a2, a3, qh.x, qh.y);
                 mma16816<0>(sb[0], a0, a1, a2, a3, ql.x, ql.y);
             }
             {
                 const uint32_t a0 = i8pair_h2(r2, 0x4140), a1 = i8pair_h2(r3, 0x4140);
                 const uint32_t a2 = i8pair_h2(r2, 0x4342), a3 = i8pair_h2(r3, 0x4342);
-                const uint2 qh = qf[(2 * p + 1) * 32], ql = qf[256 + (2 * p + 1) * 32];
+                const uint2 qh = qf[(2 * p + 1) * QS], ql = qf[QLO + (2 * p + 1) * QS];
                 mma16816<0>(sa[1], a0, a1, a2, a3, qh.x, qh.y);
                 mma16816<0>(sb[1], a0, a1, a2, a3, ql.x, ql.y);
             }
@@ -940,6 +941,17 @@ __global__ void __launch_bounds__(kThreads, 2)
             __syncwarp();
         }
         const uint2* qf = &sm.qfrag[qslot][0][0][lane];
+        // INT8 blocks keep the fragments in registers: their consumers are
+        // bound by instructions, not registers (16 shared loads per block
+        // cost more there than the registers they free).
+        uint2 qreg[16];
+        if (DT == 2) {
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                qreg[kk] = qf[kk * 32];
+                qreg[8 + kk] = qf[256 + kk * 32];
+            }
+        }
         float m2[2] = {-INFINITY, -INFINITY}, lsum[2] = {0.f, 0.f};
         float o[8][4];
 #pragma unroll
@@ -1006,7 +1018,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             }
             __syncwarp();
             if constexpr (DT == 2)
-                consume_block_i8(smem_u32(sK), smem_u32(sV), valid, lane, qf, m2, lsum, o, ks, vs);
+                consume_block_i8<1, 8>(smem_u32(sK), smem_u32(sV), valid, lane, qreg, m2, lsum, o, ks, vs);
             else
                 consume_block<DT>(smem_u32(sK), smem_u32(sV), valid, lane, qf, m2, lsum, o, ks, vs);
             // Generic-proxy writes to the tile must be ordered before the
