@@ -1,5 +1,5 @@
 """Shared test setup: the `gpu` marker, loaders for the product package (its
-directory name has a hyphen, so it is loaded by path) and for the checker."""
+directory name has a hyphen, so it is loaded by path) and for the oracle."""
 from __future__ import annotations
 
 import importlib.util

@@ -1,4 +1,4 @@
-"""Pin the checker: the C restatement (oracle/kvattn_oracle.c) must reproduce
+"""Pin the oracle: the C restatement (oracle/kvattn_oracle.c) must reproduce
 the reference's golden vectors bit-for-bit, and match the reference's own
 compiled functions live where they were built."""
 from __future__ import annotations
@@ -178,7 +178,7 @@ def test_int8_attention_close_to_fp32(orc):
 
 def test_int8_prefill_step_matches_numpy(orc):
     """The INT8 layer step with a multi-token chunk (seq = n, the prefill
-    attention's checker) against an independent float64 numpy computation:
+    attention's oracle) against an independent float64 numpy computation:
     NeoX RoPE at positions pos..pos+n-1, causal GQA attention over the
     dequantised caches (the context's codes and the chunk's appended codes);
     the appended k / v rows decode to the rotated k and to v within half a
