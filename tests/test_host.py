@@ -285,6 +285,22 @@ def test_plan_cluster_merge_keeps_segments_in_clusters(kv, lens):
     assert max(_plan_costs(info)) <= gmax + gmax // 10 + 4 + 6
 
 
+def test_merge_mode_arguments(kv):
+    P = host_pool(kv)
+    with pytest.raises(kv.KVError) as e:
+        P.plan_clusters()  # no active plan
+    assert e.value.status == kv.KV_ERR_STATE
+    with pytest.raises(kv.KVError) as e:
+        P.set_merge_mode(7)
+    assert e.value.status == kv.KV_ERR_INVAL
+    # a plan with no split head stays a single grid-wide launch in either mode
+    a = P.seq_alloc()
+    P.set_merge_mode(kv.KVP_MERGE_CLUSTER)
+    P.plan([a])
+    assert P.plan_clusters() == (0, 1) and P.plan_info()["grid"] == 1
+    P.commit()
+
+
 def test_plan_small_workload_uses_few_ctas(kv):
     P = host_pool(kv, nblocks=64)
     a = P.seq_alloc()
