@@ -962,7 +962,10 @@ int attn_prefill_mma(kvp_pool* p, int layer, int seq, int pos0, int n, const flo
 
 namespace {
 
-constexpr long kPieceCost = 6;  // block-equivalents a piece costs beyond its blocks
+// Block-equivalents a piece costs beyond its blocks (q fragments, the warp
+// merge, the partial write); 8 measured best for 32 sequences of
+// U[256,4096] tokens (6: 18.2, 8-10: 18.0, 12: 18.3, 3: 18.9 us per step).
+constexpr long kPieceCost = 8;
 
 // Work partition of one sub-plan whose slots are filled.  Segments (slot,
 // KV head) with blocks are listed slot-major; every CTA gets one contiguous

@@ -60,6 +60,9 @@ class ModelPool:
             self.seqs[s][0] += 1
 
 
+PIECE_COST = 8  # block-equivalents the planner charges per piece (kPieceCost)
+
+
 def host_pool(kv, nblocks=64, max_seqs=8, max_seq_len=4096, kv_heads=2):
     return kv.Pool(kv.KVP_HOST_ONLY, 1, nblocks, num_q_heads=6 * kv_heads, num_kv_heads=kv_heads,
                    max_seqs=max_seqs, max_seq_len=max_seq_len)
@@ -223,10 +226,10 @@ def test_plan_pieces_cover_every_block_once_balanced(kv):
             cover[(slot, h, b)] = 1
     want = {(i, h, b) for i, L in enumerate(lens) for h in range(2) for b in range(-(-(L + 1) // 16))}
     assert set(cover) == want
-    # balance: with 6 block-equivalents charged per piece, every CTA but the
+    # balance: with PIECE_COST block-equivalents charged per piece, every CTA but the
     # last carries the same cost to within one piece overhead
-    cost = [sum(b1 - b0 + 6 for (_, _, b0, b1) in items[cs[g]:cs[g + 1]]) for g in range(info["grid"])]
-    assert max(cost) - min(cost[:-1]) <= 6
+    cost = [sum(b1 - b0 + PIECE_COST for (_, _, b0, b1) in items[cs[g]:cs[g + 1]]) for g in range(info["grid"])]
+    assert max(cost) - min(cost[:-1]) <= PIECE_COST
     assert all(cs[g + 1] - cs[g] <= 64 for g in range(info["grid"]))
     # one new block for every sequence whose next position starts a block
     assert info["npatch"] == sum(1 for L in lens if L % 16 == 0)
@@ -236,7 +239,7 @@ def test_plan_pieces_cover_every_block_once_balanced(kv):
 
 def _plan_costs(info):
     items, cs = info["items"], info["cta_start"]
-    return [sum(b1 - b0 + 6 for (_, _, b0, b1) in items[cs[g]:cs[g + 1]]) for g in range(info["grid"])]
+    return [sum(b1 - b0 + PIECE_COST for (_, _, b0, b1) in items[cs[g]:cs[g + 1]]) for g in range(info["grid"])]
 
 
 @pytest.mark.parametrize("lens", [
@@ -282,7 +285,7 @@ def test_plan_cluster_merge_keeps_segments_in_clusters(kv, lens):
         assert all(pieces[u][3] == pieces[u + 1][2] for u in range(len(pieces) - 1))
     assert all(cs[g + 1] - cs[g] <= 64 for g in range(info["grid"]))
     gmax = max(_plan_costs(grid_info))
-    assert max(_plan_costs(info)) <= gmax + gmax // 10 + 4 + 6
+    assert max(_plan_costs(info)) <= gmax + gmax // 10 + 4 + PIECE_COST
 
 
 def test_merge_mode_arguments(kv):
